@@ -1,0 +1,325 @@
+"""Python host side of the B200 Breeze-TTS-2 generation library.
+
+`libbreeze.so` (built from `csrc/` by `make`) exports the reference's C ABI
+(sharjeel103/bz-ggml include/breeze/breeze.h); this module binds it with ctypes and mirrors
+the reference's `python/bz_ggml/bindings.py` GeneratorHandle (same method names, argument
+meaning and error behaviour: a failed create/load raises RuntimeError, step calls return
+the C ABI's values). It adds the `bzb_*` extension entry points used by the benchmark and
+the parity tests. There is no CPU fallback: without the built library, or without a CUDA
+device, generator construction fails.
+
+The directory name is not an importable identifier; load it with `load_package()` of the
+repository's `__graft_entry__` or `importlib` under the name `bz_ggml_b200`.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libbreeze.so")
+SYNTH_BIN = os.path.join(HERE, "bin", "breeze-synth")
+
+_c_int_p = ctypes.POINTER(ctypes.c_int)
+_c_uint_p = ctypes.POINTER(ctypes.c_uint)
+_c_float_p = ctypes.POINTER(ctypes.c_float)
+
+# every symbol include/breeze.h and include/bzb_ext.h declare: name -> (restype, argtypes)
+SIGNATURES = {
+    "breeze_init": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_int]),
+    "breeze_free": (None, [ctypes.c_void_p]),
+    "breeze_sample_rate": (ctypes.c_int, [ctypes.c_void_p]),
+    "breeze_generate": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "breeze_generate_wav": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p]),
+    "breeze_last_error": (ctypes.c_char_p, []),
+    "breeze_generator_init": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_int]),
+    "breeze_generator_free": (None, [ctypes.c_void_p]),
+    "breeze_generator_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint, _c_int_p]),
+    "breeze_generator_step_frame": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, _c_int_p]),
+    "breeze_vocoder_init": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_int]),
+    "breeze_vocoder_free": (None, [ctypes.c_void_p]),
+    "breeze_vocoder_create_from_generator": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "breeze_vocoder_session_create": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "breeze_vocoder_session_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_int_p, ctypes.c_int, _c_float_p]),
+    "breeze_vocoder_session_decode_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_int_p, _c_int_p, _c_int_p,
+                                                           _c_int_p, _c_float_p, _c_int_p, _c_int_p]),
+    "breeze_vocoder_session_free": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "breeze_vocoder_stream_decode": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, ctypes.c_int, _c_float_p]),
+    "breeze_vocoder_stream_decode_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_int_p, _c_int_p, _c_int_p,
+                                                          _c_float_p, _c_int_p, _c_int_p]),
+    "breeze_generator_session_create": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p,
+                                                       ctypes.c_float, ctypes.c_uint, _c_int_p]),
+    "breeze_generator_session_create_ext": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p,
+                                                           ctypes.c_char_p, _c_int_p, ctypes.c_int, ctypes.c_float,
+                                                           ctypes.c_uint, ctypes.c_int, _c_int_p, _c_int_p]),
+    "breeze_generator_session_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, _c_int_p]),
+    "breeze_generator_session_free": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "breeze_generator_load_q4_depth": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
+    "breeze_generator_session_set_q4": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "breeze_generator_session_count": (ctypes.c_int, [ctypes.c_void_p]),
+    "breeze_generator_sessions_step_round": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, ctypes.c_int, ctypes.c_uint,
+                                                            _c_int_p, _c_int_p]),
+    "breeze_generator_sessions_step_batched": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, ctypes.c_int, _c_uint_p,
+                                                              _c_int_p, _c_int_p]),
+    "breeze_generator_sessions_step_burst": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, ctypes.c_int, ctypes.c_int,
+                                                            _c_uint_p, _c_int_p, _c_int_p]),
+    "breeze_generator_convert_voice": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, ctypes.c_int, _c_float_p, ctypes.c_int,
+                                                      _c_int_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p,
+                                                      ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_uint,
+                                                      _c_int_p, _c_float_p, ctypes.c_int]),
+    "breeze_generator_encode_audio": (ctypes.c_int, [ctypes.c_void_p, _c_float_p, ctypes.c_int, _c_int_p, _c_int_p]),
+    "breeze_voice_save_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _c_int_p, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_int]),
+    "breeze_voice_load_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p,
+                                              ctypes.c_int, _c_int_p, _c_int_p, _c_int_p, _c_int_p]),
+    "bzb_generator_num_codebooks": (ctypes.c_int, [ctypes.c_void_p]),
+    "bzb_generator_sessions_step_frames": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, ctypes.c_int, ctypes.c_int,
+                                                          _c_uint_p, _c_int_p, _c_int_p]),
+    "bzb_generator_step_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "bzb_generator_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "bzb_generator_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "bzb_generator_weight_bytes_per_step": (ctypes.c_longlong, [ctypes.c_void_p]),
+    "bzb_generator_kv_bytes_per_position": (ctypes.c_longlong, [ctypes.c_void_p]),
+    "bzb_generator_launches_per_step": (ctypes.c_int, [ctypes.c_void_p]),
+    "bzb_generator_profile_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double)]),
+    "bzb_generator_debug_hidden": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_float_p]),
+    "bzb_generator_debug_depth": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_float_p, _c_int_p, _c_int_p,
+                                                 _c_int_p, _c_float_p]),
+    "bzb_generator_debug_gemv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
+                                                _c_float_p, _c_float_p]),
+    "bzb_gguf_inspect": (ctypes.c_int, [ctypes.c_char_p, _c_int_p, _c_int_p, _c_int_p]),
+    "bzb_tokenize": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, _c_int_p, ctypes.c_int]),
+}
+
+
+def build(jobs: int = 8) -> None:
+    """Compile libbreeze.so (sm_100a) and the breeze-synth tool in place."""
+    subprocess.run(["make", "-C", HERE, f"-j{jobs}"], check=True)
+
+
+class BreezeLib:
+    """ctypes binding of libbreeze.so (mirrors bz_ggml.bindings.BreezeLib)."""
+
+    def __init__(self, lib_path: Optional[str] = None):
+        self.lib_path = lib_path or os.environ.get("BREEZE_LIB_PATH") or LIB_PATH
+        if not os.path.exists(self.lib_path):
+            raise FileNotFoundError(f"libbreeze.so not found at {self.lib_path}; run `make -C {HERE}`")
+        self.lib = ctypes.CDLL(self.lib_path, mode=ctypes.RTLD_GLOBAL)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(self.lib, name)
+            fn.restype = res
+            fn.argtypes = args
+
+    def last_error(self) -> str:
+        e = self.lib.breeze_last_error()
+        return e.decode("utf-8", "replace") if e else ""
+
+
+_LIB: Optional[BreezeLib] = None
+
+
+def lib() -> BreezeLib:
+    global _LIB
+    if _LIB is None:
+        _LIB = BreezeLib()
+    return _LIB
+
+
+def _ip(a: np.ndarray):
+    return a.ctypes.data_as(_c_int_p)
+
+
+def _up(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(_c_uint_p)
+
+
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(_c_float_p)
+
+
+class GeneratorHandle:
+    """One generator on one CUDA device (mirrors bz_ggml.bindings.GeneratorHandle)."""
+
+    def __init__(self, model_path: str, cuda_device: int = 0, breeze_lib: Optional[BreezeLib] = None):
+        self.lib = breeze_lib or lib()
+        self.device = cuda_device
+        self.handle = self.lib.lib.breeze_generator_init(model_path.encode("utf-8"), cuda_device)
+        if not self.handle:
+            raise RuntimeError(f"Failed to initialize Generator on CUDA device {cuda_device}: {self.lib.last_error()}")
+        self.nc = self.lib.lib.bzb_generator_num_codebooks(self.handle)
+
+    def close(self):
+        if self.handle:
+            self.lib.lib.breeze_generator_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # --- reference-mirroring API -------------------------------------------------------
+    def session_create(self, session_id: int, text: str, instruction: str = "Speak clearly and naturally.",
+                       cfg_scale: float = 1.0, seed: int = 42, max_new_tokens: int = 0) -> Tuple[int, int]:
+        return self.session_create_ext(session_id, text, instruction, None, None, 0, cfg_scale, seed, max_new_tokens)
+
+    def session_create_ext(self, session_id: int, text: str, instruction: Optional[str] = "Speak clearly and naturally.",
+                           ref_text: Optional[str] = None, ref_codes: Optional[Sequence[int]] = None, ref_frames: int = 0,
+                           cfg_scale: float = 1.0, seed: int = 42, max_new_tokens: int = 0) -> Tuple[int, int]:
+        cb0 = ctypes.c_int()
+        alloc = ctypes.c_int()
+        c_codes = None
+        if ref_codes is not None and ref_frames > 0:
+            arr = np.ascontiguousarray(np.asarray(ref_codes, dtype=np.int32).reshape(-1))
+            c_codes = _ip(arr)
+        res = self.lib.lib.breeze_generator_session_create_ext(
+            self.handle, session_id, text.encode("utf-8"),
+            instruction.encode("utf-8") if instruction else None,
+            ref_text.encode("utf-8") if ref_text else None, c_codes, ref_frames,
+            ctypes.c_float(cfg_scale), ctypes.c_uint(seed & 0xFFFFFFFF), max_new_tokens,
+            ctypes.byref(cb0), ctypes.byref(alloc))
+        if res != 0:
+            raise RuntimeError(f"Session create ext failed (session {session_id}): {self.lib.last_error()}")
+        return cb0.value, alloc.value
+
+    def session_step(self, session_id: int, seed: int) -> Tuple[int, List[int]]:
+        fr = np.zeros(16, np.int32)
+        nxt = self.lib.lib.breeze_generator_session_step(self.handle, session_id, ctypes.c_uint(seed & 0xFFFFFFFF), _ip(fr))
+        return nxt, fr.tolist()
+
+    def session_free(self, session_id: int) -> int:
+        return self.lib.lib.breeze_generator_session_free(self.handle, session_id)
+
+    def active_session_count(self) -> int:
+        return self.lib.lib.breeze_generator_session_count(self.handle)
+
+    def sessions_step_batched(self, session_ids: Sequence[int], seeds: Optional[Sequence[int]] = None):
+        n = len(session_ids)
+        ids = np.asarray(session_ids, np.int32)
+        fr = np.zeros((n, 16), np.int32)
+        nx = np.zeros(n, np.int32)
+        sd = None if seeds is None else np.asarray(seeds, np.uint32)
+        rc = self.lib.lib.breeze_generator_sessions_step_batched(self.handle, _ip(ids), n, _up(sd), _ip(fr), _ip(nx))
+        if rc < 0:
+            raise RuntimeError(f"sessions_step_batched failed: {self.lib.last_error()}")
+        return nx.tolist(), fr.tolist()
+
+    def sessions_step_burst(self, session_ids: Sequence[int], burst_steps: int, seeds: Optional[Sequence[int]] = None):
+        """Returns (next_cb0 per session, frames [session][step][16]) like the reference binding."""
+        n = len(session_ids)
+        ids = np.asarray(session_ids, np.int32)
+        fr = np.zeros((burst_steps, n, 16), np.int32)
+        nx = np.zeros(n, np.int32)
+        sd = None if seeds is None else np.asarray(seeds, np.uint32)
+        rc = self.lib.lib.breeze_generator_sessions_step_burst(self.handle, _ip(ids), n, burst_steps, _up(sd), _ip(fr), _ip(nx))
+        if rc < 0:
+            raise RuntimeError(f"sessions_step_burst failed: {self.lib.last_error()}")
+        return nx.tolist(), fr.transpose(1, 0, 2).tolist()
+
+    # --- extensions ----------------------------------------------------------------------
+    def step_frames(self, session_ids: Sequence[int], burst_steps: int, seeds: Optional[Sequence[int]] = None):
+        """Full-width burst: returns (steps executed, frames [K, n, nc] int32, next_cb0 [n])."""
+        n = len(session_ids)
+        ids = np.ascontiguousarray(np.asarray(session_ids, np.int32))
+        fr = np.zeros((burst_steps, n, self.nc), np.int32)
+        nx = np.zeros(n, np.int32)
+        sd = None if seeds is None else np.ascontiguousarray(np.asarray(seeds, np.uint32))
+        rc = self.lib.lib.bzb_generator_sessions_step_frames(self.handle, _ip(ids), n, burst_steps, _up(sd), _ip(fr), _ip(nx))
+        if rc < 0:
+            raise RuntimeError(f"step_frames failed: {self.lib.last_error()}")
+        return rc, fr, nx
+
+    def step_device(self, burst_steps: int) -> None:
+        if self.lib.lib.bzb_generator_step_device(self.handle, burst_steps) != 0:
+            raise RuntimeError(self.lib.last_error())
+
+    def sync(self) -> None:
+        if self.lib.lib.bzb_generator_sync(self.handle) != 0:
+            raise RuntimeError(self.lib.last_error())
+
+    def stream_ptr(self) -> int:
+        return int(self.lib.lib.bzb_generator_stream(self.handle) or 0)
+
+    def weight_bytes_per_step(self) -> int:
+        return int(self.lib.lib.bzb_generator_weight_bytes_per_step(self.handle))
+
+    def kv_bytes_per_position(self) -> int:
+        return int(self.lib.lib.bzb_generator_kv_bytes_per_position(self.handle))
+
+    def launches_per_step(self) -> int:
+        return int(self.lib.lib.bzb_generator_launches_per_step(self.handle))
+
+    def profile_step(self) -> dict:
+        out = (ctypes.c_double * 5)()
+        if self.lib.lib.bzb_generator_profile_step(self.handle, out) != 0:
+            raise RuntimeError(self.lib.last_error())
+        return dict(step_ms=out[0], gemm_ms=out[1], gemm_launches=int(out[2]), gemm_bytes=out[3])
+
+    def debug_hidden(self, session_id: int, hidden: int) -> np.ndarray:
+        out = np.zeros(hidden, np.float32)
+        if self.lib.lib.bzb_generator_debug_hidden(self.handle, session_id, _fp(out)) != 0:
+            raise RuntimeError(self.lib.last_error())
+        return out
+
+    def debug_depth(self, hidden: np.ndarray, cb0: Sequence[int], vs: int, forced: Optional[np.ndarray] = None):
+        n = hidden.shape[0]
+        h = np.ascontiguousarray(hidden, np.float32)
+        c = np.ascontiguousarray(np.asarray(cb0, np.int32))
+        codes = np.zeros((n, self.nc - 1), np.int32)
+        logits = np.zeros((n, self.nc - 1, vs), np.float32)
+        f = None if forced is None else np.ascontiguousarray(np.asarray(forced, np.int32))
+        rc = self.lib.lib.bzb_generator_debug_depth(self.handle, n, _fp(h), _ip(c), None if f is None else _ip(f),
+                                                    _ip(codes), _fp(logits))
+        if rc != 0:
+            raise RuntimeError(self.lib.last_error())
+        return codes, logits
+
+    def debug_gemv(self, tensor: str, x: np.ndarray, out_dim: int, sub: int = -1) -> np.ndarray:
+        xx = np.ascontiguousarray(x, np.float32)
+        y = np.zeros((xx.shape[0], out_dim), np.float32)
+        if self.lib.lib.bzb_generator_debug_gemv(self.handle, tensor.encode(), sub, xx.shape[0], _fp(xx), _fp(y)) != 0:
+            raise RuntimeError(self.lib.last_error())
+        return y
+
+
+def gguf_inspect(path: str):
+    h, nc, nt = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    if lib().lib.bzb_gguf_inspect(path.encode(), ctypes.byref(h), ctypes.byref(nc), ctypes.byref(nt)) != 0:
+        raise RuntimeError(lib().last_error())
+    return h.value, nc.value, nt.value
+
+
+def tokenize(path: str, text: str, add_bos: bool = True) -> List[int]:
+    buf = np.zeros(1 << 16, np.int32)
+    n = lib().lib.bzb_tokenize(path.encode(), text.encode("utf-8"), 1 if add_bos else 0, _ip(buf), buf.size)
+    if n < 0:
+        raise RuntimeError(lib().last_error())
+    return buf[:n].tolist()
+
+
+def synth_model(out_path: str, preset: str = "full", nc: int = 0, quant: str = "q8_0", seed: int = 0,
+                eos_off: bool = False, max_new_tokens: int = 0, depth_top_k: int = -1) -> str:
+    """Write a seeded random-init Breeze-TTS-2 GGUF (the stand-in for real weights)."""
+    if not os.path.exists(SYNTH_BIN):
+        raise FileNotFoundError(f"{SYNTH_BIN} missing; run `make -C {HERE}`")
+    cmd = [SYNTH_BIN, "--out", out_path, "--preset", preset, "--quant", quant, "--seed", str(seed)]
+    if nc:
+        cmd += ["--nc", str(nc)]
+    if eos_off:
+        cmd += ["--eos-off"]
+    if max_new_tokens:
+        cmd += ["--max-new-tokens", str(max_new_tokens)]
+    if depth_top_k >= 0:
+        cmd += ["--depth-top-k", str(depth_top_k)]
+    subprocess.run(cmd, check=True)
+    return out_path
+
+
+def ids_to_text(ids: Sequence[int]) -> str:
+    """Text whose synthetic-vocabulary tokenisation is exactly `ids` (ids >= 264)."""
+    return "".join(f"<|t{int(i)}|>" for i in ids)

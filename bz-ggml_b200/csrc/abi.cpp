@@ -1,0 +1,514 @@
+// extern "C" surface of libbreeze.so: the reference's breeze.h entry points (same names,
+// arguments, buffer conventions and return codes; see include/breeze.h for the line each
+// one replaces) plus the bzb_* extensions of include/bzb_ext.h. Exceptions never cross the
+// boundary; they become the reference's error returns plus breeze_last_error().
+#include "../../include/bzb_ext.h"
+#include "engine.h"
+
+#include <cerrno>
+#include <climits>
+#include <cstdio>
+#include <cstring>
+#include <filesystem>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+struct breeze_generator {
+    std::unique_ptr<bzb::Engine> eng;
+    int device = 0;
+};
+
+struct breeze_vocoder {
+    int device = 0;
+};
+
+struct breeze_context {
+    breeze_generator * gen = nullptr;
+};
+
+namespace {
+// per-thread last error: the reference keeps one unsynchronised global (src/c_api.cpp:28);
+// each calling thread reads the message of its own last failing call here
+thread_local std::string g_error;
+
+void set_error(const std::string & e) { g_error = e; }
+
+constexpr int kLegacySession = INT_MIN;
+constexpr int kAbiFrameWidth = 16;
+
+int burst_impl(breeze_generator * gen, const int * ids, int n, int K, const unsigned int * seeds, int * out,
+               int width, int * next) {
+    // the engine runs up to 64 steps per graph batch; longer bursts continue with seeds + step
+    std::fill_n(out, (size_t) K * n * width, -1);
+    for (int i = 0; i < n; i++) next[i] = -1;
+    int done = 0;
+    std::vector<int> nx(n);
+    std::vector<unsigned int> sd(n);
+    while (done < K) {
+        const int k = std::min(64, K - done);
+        if (seeds)
+            for (int i = 0; i < n; i++) sd[i] = seeds[i] + (unsigned) done;
+        const bzb::StepResult r = gen->eng->step(ids, n, k, seeds ? sd.data() : nullptr, true,
+                                                 out + (size_t) done * n * width, width, nx.data(), true);
+        // a session stepped in this chunk reports its last cb0 or -1 when it finished; one not
+        // stepped had finished earlier (or never ran) and reports -1 as well
+        if (r.steps_executed > 0)
+            for (int i = 0; i < n; i++) next[i] = nx[i];
+        done += r.steps_executed;
+        if (r.steps_executed < k) break;
+    }
+    return done;
+}
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------------------------------ one-shot
+breeze_context * breeze_init(const char * gguf_path, int use_gpu) {
+    if (!gguf_path) { set_error("null model path"); return nullptr; }
+    if (!use_gpu) { set_error("this library runs on CUDA devices only; use_gpu=0 has no CPU backend here"); return nullptr; }
+    breeze_generator * gen = breeze_generator_init(gguf_path, 0);
+    if (!gen) return nullptr;
+    breeze_context * ctx = new breeze_context();
+    ctx->gen = gen;
+    return ctx;
+}
+
+void breeze_free(breeze_context * ctx) {
+    if (!ctx) return;
+    breeze_generator_free(ctx->gen);
+    delete ctx;
+}
+
+int breeze_sample_rate(breeze_context * ctx) {
+    return (ctx && ctx->gen && ctx->gen->eng) ? ctx->gen->eng->cfg.sample_rate : 0;
+}
+
+int breeze_generate(breeze_context * ctx, const breeze_request * req, breeze_audio_cb cb, void * user) {
+    (void) cb; (void) user;
+    if (!ctx || !req || !req->text) { set_error("null context or request"); return 1; }
+    set_error("breeze_generate streams PCM through the vocoder, which this library does not provide yet");
+    return 1;
+}
+
+int breeze_generate_wav(breeze_context * ctx, const breeze_request * req, const char * out_path) {
+    if (!ctx || !req || !out_path) { set_error("null argument"); return 1; }
+    return breeze_generate(ctx, req, nullptr, nullptr);
+}
+
+const char * breeze_last_error(void) { return g_error.c_str(); }
+
+// ------------------------------------------------------------------------------------ generator
+breeze_generator * breeze_generator_init(const char * gguf_path, int cuda_device) {
+    if (!gguf_path) { set_error("null model path"); return nullptr; }
+    breeze_generator * gen = new breeze_generator();
+    gen->device = cuda_device;
+    try {
+        gen->eng.reset(new bzb::Engine(gguf_path, cuda_device));
+        return gen;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        delete gen;
+        return nullptr;
+    }
+}
+
+void breeze_generator_free(breeze_generator * gen) {
+    if (!gen) return;
+    delete gen;
+}
+
+int breeze_generator_prefill(breeze_generator * gen, const char * text, const char * instruction, unsigned int seed,
+                             int * out_cb0) {
+    if (!gen || !text || !out_cb0) return -1;
+    try {
+        int alloc = 0;
+        gen->eng->session_create(kLegacySession, text, instruction, nullptr, nullptr, 0, 1.0f, seed,
+                                 gen->eng->cfg.max_new_tokens > 0 ? gen->eng->cfg.max_new_tokens : 2048, out_cb0, &alloc);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_step_frame(breeze_generator * gen, int cb0, unsigned int seed, int * out_frame_16) {
+    (void) cb0; (void) seed;
+    if (!gen || !out_frame_16 || !gen->eng->session_active(kLegacySession)) return -1;
+    try {
+        const int sid = kLegacySession;
+        int next = -1;
+        gen->eng->step(&sid, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false);
+        return next;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_session_create_ext(breeze_generator * gen, int session_id, const char * text,
+                                        const char * instruction, const char * ref_text, const int * ref_codes,
+                                        int ref_frames, float cfg_scale, unsigned int seed, int max_new_tokens,
+                                        int * out_cb0, int * out_allocated_tokens) {
+    if (!gen || !text || !out_cb0) return -1;
+    try {
+        gen->eng->session_create(session_id, text, instruction, ref_text, ref_codes, ref_frames, cfg_scale, seed,
+                                 max_new_tokens, out_cb0, out_allocated_tokens);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_session_create(breeze_generator * gen, int session_id, const char * text,
+                                    const char * instruction, float cfg_scale, unsigned int seed, int * out_cb0) {
+    return breeze_generator_session_create_ext(gen, session_id, text, instruction, nullptr, nullptr, 0, cfg_scale,
+                                               seed, 0, out_cb0, nullptr);
+}
+
+int breeze_generator_session_step(breeze_generator * gen, int session_id, unsigned int seed, int * out_frame_16) {
+    (void) seed;
+    if (!gen || !out_frame_16) return -1;
+    if (!gen->eng->session_active(session_id)) return -1;
+    try {
+        int next = -1;
+        gen->eng->step(&session_id, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false);
+        return next;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_session_free(breeze_generator * gen, int session_id) {
+    if (!gen) return -1;
+    try {
+        return gen->eng->session_free(session_id) ? 0 : -1;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_load_q4_depth(breeze_generator * gen, const char * q4_gguf_path) {
+    if (!gen || !q4_gguf_path) return -1;
+    set_error("the Q4_K depth-decoder override is not supported by this library yet");
+    return -1;
+}
+
+int breeze_generator_session_set_q4(breeze_generator * gen, int session_id, int use_q4) {
+    (void) use_q4;
+    if (!gen) return -1;
+    // without a loaded Q4 depth piece the flag resolves to off (src/c_api.cpp:576)
+    return gen->eng->session_exists(session_id) ? 0 : -1;
+}
+
+int breeze_generator_session_count(breeze_generator * gen) { return gen ? gen->eng->session_count() : 0; }
+
+int breeze_generator_sessions_step_round(breeze_generator * gen, const int * session_ids, int num_sessions,
+                                         unsigned int seed, int * out_frames_16, int * out_next_cb0) {
+    if (!gen || !session_ids || num_sessions <= 0 || !out_frames_16 || !out_next_cb0) return 0;
+    int completed = 0;
+    for (int i = 0; i < num_sessions; i++) {
+        const int nb = breeze_generator_session_step(gen, session_ids[i], seed + (unsigned) i, out_frames_16 + (size_t) i * 16);
+        out_next_cb0[i] = nb;
+        if (nb >= 0) completed++;
+    }
+    return completed;
+}
+
+int breeze_generator_sessions_step_batched(breeze_generator * gen, const int * session_ids, int num_sessions,
+                                           const unsigned int * seeds, int * out_frames_16, int * out_next_cb0) {
+    if (!gen || !session_ids || num_sessions <= 0 || !out_frames_16 || !out_next_cb0) return 0;
+    try {
+        const bzb::StepResult r = gen->eng->step(session_ids, num_sessions, 1, seeds, false, out_frames_16,
+                                                 kAbiFrameWidth, out_next_cb0, false);
+        return r.steps_executed == 0 ? 0 : r.still_active;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_sessions_step_burst(breeze_generator * gen, const int * session_ids, int num_sessions,
+                                         int burst_steps, const unsigned int * seeds, int * out_frames_burst,
+                                         int * out_next_cb0) {
+    if (!gen || !session_ids || num_sessions <= 0 || burst_steps <= 0 || !out_frames_burst || !out_next_cb0) return 0;
+    try {
+        return burst_impl(gen, session_ids, num_sessions, burst_steps, seeds, out_frames_burst, kAbiFrameWidth, out_next_cb0);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int breeze_generator_convert_voice(breeze_generator * gen, const int * src_codes, int src_T, const float * ref_audio,
+                                   int ref_audio_len, const int * ref_codes, int ref_frames, const char * ref_text,
+                                   const char * src_text, float cfg_scale, int keep_acoustic, int feed_source,
+                                   unsigned int seed, int * out_codes, float * out_pcm, int max_out_pcm) {
+    (void) ref_audio; (void) ref_audio_len; (void) ref_codes; (void) ref_frames; (void) ref_text; (void) src_text;
+    (void) cfg_scale; (void) keep_acoustic; (void) feed_source; (void) seed; (void) out_codes; (void) out_pcm;
+    (void) max_out_pcm;
+    if (!gen || !src_codes || src_T <= 0) return -1;
+    set_error("voice conversion needs the codec encoder, which this library does not provide yet");
+    return -1;
+}
+
+int breeze_generator_encode_audio(breeze_generator * gen, const float * pcm, int n_samples, int * out_codes,
+                                  int * out_n_frames) {
+    if (!gen || !pcm || n_samples <= 0 || !out_codes || !out_n_frames) return -1;
+    set_error("audio encoding needs the codec encoder, which this library does not provide yet");
+    return -1;
+}
+
+// ------------------------------------------------------------------------------------ vocoder
+breeze_vocoder * breeze_vocoder_init(const char * gguf_path, int cuda_device) {
+    (void) gguf_path; (void) cuda_device;
+    set_error("the streaming vocoder is not provided by this library yet");
+    return nullptr;
+}
+void breeze_vocoder_free(breeze_vocoder * voc) { delete voc; }
+breeze_vocoder * breeze_vocoder_create_from_generator(breeze_generator * gen) {
+    (void) gen;
+    set_error("the streaming vocoder is not provided by this library yet");
+    return nullptr;
+}
+int breeze_vocoder_session_create(breeze_vocoder * voc, int session_id) {
+    (void) session_id;
+    return voc ? 0 : -1;
+}
+int breeze_vocoder_session_decode(breeze_vocoder * voc, int session_id, const int * frames, int n_frames,
+                                  float * out_pcm) {
+    (void) voc; (void) session_id; (void) frames; (void) n_frames; (void) out_pcm;
+    set_error("the streaming vocoder is not provided by this library yet");
+    return 0;
+}
+int breeze_vocoder_session_decode_batch(breeze_vocoder * voc, int batch_size, const int * session_ids,
+                                        const int * flat_tokens, const int * token_offsets,
+                                        const int * n_frames_per_stream, float * flat_pcm, const int * pcm_offsets,
+                                        int * out_n_samples) {
+    (void) voc; (void) batch_size; (void) session_ids; (void) flat_tokens; (void) token_offsets;
+    (void) n_frames_per_stream; (void) flat_pcm; (void) pcm_offsets; (void) out_n_samples;
+    set_error("the streaming vocoder is not provided by this library yet");
+    return 0;
+}
+int breeze_vocoder_session_free(breeze_vocoder * voc, int session_id) {
+    (void) session_id;
+    return voc ? 0 : -1;
+}
+int breeze_vocoder_stream_decode(breeze_vocoder * voc, const int * frames, int n_frames, float * out_pcm) {
+    (void) voc; (void) frames; (void) n_frames; (void) out_pcm;
+    set_error("the streaming vocoder is not provided by this library yet");
+    return 0;
+}
+int breeze_vocoder_stream_decode_batch(breeze_vocoder * voc, int batch_size, const int * flat_tokens,
+                                       const int * token_offsets, const int * n_frames_per_stream, float * flat_pcm,
+                                       const int * pcm_offsets, int * out_n_samples) {
+    (void) voc; (void) batch_size; (void) flat_tokens; (void) token_offsets; (void) n_frames_per_stream;
+    (void) flat_pcm; (void) pcm_offsets; (void) out_n_samples;
+    set_error("the streaming vocoder is not provided by this library yet");
+    return 0;
+}
+
+// ------------------------------------------------------------------------------------ voice files
+// BRZV v1: "BRZV", u32 version, sample_rate, n_codebooks, frames, text_len, text bytes, then
+// frames*n_codebooks little-endian i32 codes (layout of src/voice.cpp:16-69)
+int breeze_voice_save_file(const char * path, const char * name, const char * text, const int * codes, int n_frames,
+                           int n_codebooks, int sample_rate) {
+    if (!path || !name || !text || !codes || n_frames <= 0 || n_codebooks <= 0) return -1;
+    try {
+        std::error_code ec;
+        const std::filesystem::path p(path);
+        if (p.has_parent_path()) std::filesystem::create_directories(p.parent_path(), ec);
+        FILE * f = std::fopen(path, "wb");
+        if (!f) return -1;
+        const uint32_t hdr[5] = { 1u, (uint32_t) (sample_rate > 0 ? sample_rate : 24000), (uint32_t) n_codebooks,
+                                  (uint32_t) n_frames, (uint32_t) std::strlen(text) };
+        bool ok = std::fwrite("BRZV", 1, 4, f) == 4 && std::fwrite(hdr, 4, 5, f) == 5;
+        if (ok && hdr[4]) ok = std::fwrite(text, 1, hdr[4], f) == hdr[4];
+        const size_t n = (size_t) n_frames * n_codebooks;
+        if (ok) ok = std::fwrite(codes, 4, n, f) == n;
+        std::fclose(f);
+        if (!ok) std::filesystem::remove(path, ec);
+        return ok ? 0 : -1;
+    } catch (...) {
+        return -1;
+    }
+}
+
+int breeze_voice_load_file(const char * path, char * out_name, int name_max, char * out_text, int text_max,
+                           int * out_codes, int * out_n_frames, int * out_n_codebooks, int * out_sample_rate) {
+    if (!path || !out_codes || !out_n_frames || !out_n_codebooks) return -1;
+    try {
+        FILE * f = std::fopen(path, "rb");
+        if (!f) return -1;
+        char magic[4];
+        uint32_t hdr[5] = {};
+        bool ok = std::fread(magic, 1, 4, f) == 4 && std::memcmp(magic, "BRZV", 4) == 0 &&
+                  std::fread(hdr, 4, 5, f) == 5 && hdr[0] == 1u;
+        // a corrupt header must not become a giant allocation
+        if (ok) ok = hdr[2] > 0 && hdr[2] <= 64 && hdr[3] > 0 && hdr[3] <= 100000 && hdr[4] <= (1u << 20);
+        std::string text;
+        std::vector<int32_t> codes;
+        if (ok) {
+            text.resize(hdr[4]);
+            if (hdr[4]) ok = std::fread(&text[0], 1, hdr[4], f) == hdr[4];
+        }
+        if (ok) {
+            codes.resize((size_t) hdr[3] * hdr[2]);
+            ok = std::fread(codes.data(), 4, codes.size(), f) == codes.size();
+        }
+        std::fclose(f);
+        if (!ok) return -1;
+        const std::string name = std::filesystem::path(path).stem().string();
+        if (out_name && name_max > 0) {
+            std::strncpy(out_name, name.c_str(), name_max - 1);
+            out_name[name_max - 1] = '\0';
+        }
+        if (out_text && text_max > 0) {
+            std::strncpy(out_text, text.c_str(), text_max - 1);
+            out_text[text_max - 1] = '\0';
+        }
+        *out_n_frames = (int) hdr[3];
+        *out_n_codebooks = (int) hdr[2];
+        if (out_sample_rate) *out_sample_rate = (int) hdr[1];
+        std::memcpy(out_codes, codes.data(), codes.size() * sizeof(int));
+        return (int) codes.size();
+    } catch (...) {
+        return -1;
+    }
+}
+
+// ------------------------------------------------------------------------------------ extensions
+int bzb_generator_num_codebooks(breeze_generator * gen) { return gen ? gen->eng->nc() : 0; }
+
+int bzb_generator_sessions_step_frames(breeze_generator * gen, const int * session_ids, int num_sessions,
+                                       int burst_steps, const unsigned int * seeds, int * out_frames,
+                                       int * out_next_cb0) {
+    if (!gen || !session_ids || num_sessions <= 0 || burst_steps <= 0 || !out_frames || !out_next_cb0) return 0;
+    try {
+        return burst_impl(gen, session_ids, num_sessions, burst_steps, seeds, out_frames, gen->eng->nc(), out_next_cb0);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_generator_step_device(breeze_generator * gen, int burst_steps) {
+    if (!gen || burst_steps <= 0) return -1;
+    try {
+        gen->eng->step_device_only(burst_steps);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_generator_sync(breeze_generator * gen) {
+    if (!gen) return -1;
+    try {
+        gen->eng->sync();
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+void * bzb_generator_stream(breeze_generator * gen) { return gen ? (void *) gen->eng->stream() : nullptr; }
+
+long long bzb_generator_weight_bytes_per_step(breeze_generator * gen) {
+    return gen ? (long long) gen->eng->weight_bytes_per_step() : -1;
+}
+
+long long bzb_generator_kv_bytes_per_position(breeze_generator * gen) {
+    return gen ? (long long) gen->eng->kv_bytes_per_position() : -1;
+}
+
+int bzb_generator_launches_per_step(breeze_generator * gen) { return gen ? gen->eng->launches_per_step() : -1; }
+
+int bzb_generator_profile_step(breeze_generator * gen, double * out5) {
+    if (!gen || !out5) return -1;
+    try {
+        gen->eng->profile_step(out5);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_generator_debug_hidden(breeze_generator * gen, int session_id, float * out) {
+    if (!gen || !out) return -1;
+    try {
+        gen->eng->debug_hidden(session_id, out);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_generator_debug_depth(breeze_generator * gen, int n, const float * hidden, const int * cb0, const int * forced,
+                              int * out_codes, float * out_logits) {
+    if (!gen || !hidden || !cb0 || !out_codes || !out_logits) return -1;
+    try {
+        gen->eng->debug_depth(n, hidden, cb0, forced, out_codes, out_logits);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, const float * x, float * y) {
+    if (!gen || !tensor || rows <= 0 || !x || !y) return -1;
+    try {
+        gen->eng->debug_gemv(tensor, sub, rows, x, y);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_gguf_inspect(const char * gguf_path, int * out_hidden, int * out_num_codebooks, int * out_n_tensors) {
+    if (!gguf_path) return -1;
+    try {
+        bzb::GgufFile g;
+        std::string err;
+        if (!g.open(gguf_path, err)) { set_error(err); return -1; }
+        const bzb::ModelConfig c = bzb::parse_config(g);
+        if (out_hidden) *out_hidden = c.hidden;
+        if (out_num_codebooks) *out_num_codebooks = c.nc;
+        if (out_n_tensors) *out_n_tensors = (int) g.tensors.size();
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_tokenize(const char * gguf_path, const char * text, int add_bos, int * out_ids, int max_ids) {
+    if (!gguf_path || !text || !out_ids || max_ids < 0) return -1;
+    try {
+        bzb::GgufFile g;
+        std::string err;
+        if (!g.open(gguf_path, err)) { set_error(err); return -1; }
+        bzb::Tokenizer t;
+        if (!t.load(g)) { set_error("GGUF has no tokenizer.ggml.tokens"); return -1; }
+        const std::vector<int> ids = t.encode(text, add_bos != 0);
+        const int n = (int) std::min<size_t>(ids.size(), (size_t) max_ids);
+        std::memcpy(out_ids, ids.data(), (size_t) n * sizeof(int));
+        return (int) ids.size();
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+}  // extern "C"

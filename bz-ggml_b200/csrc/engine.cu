@@ -1,0 +1,903 @@
+// Generator engine: loading, the GPU-resident frame step and session prefill.
+//
+// One frame step (reference: src/c_api.cpp:764-949 with src/depth_decoder.cpp:249-365 and
+// src/backbone.cpp:98-179) is captured once per batch bucket as a CUDA graph:
+//   step_init -> depth sub-step 1 (2 tokens/session) -> depth sub-steps 2..nc-1 (argmax and
+//   next-codebook embedding gather on the GPU) -> audio embedding sum -> backbone decode over
+//   the paged KV cache -> Philox top-k sampler with repetition penalty -> frame commit.
+// Session state (positions, sampler streams, penalty histories, last hidden) never leaves the
+// device between steps; the host only uploads the row->slot table and seeds.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <stdexcept>
+
+namespace bzb {
+
+#define CK(x)                                                                                   \
+    do {                                                                                        \
+        cudaError_t e_ = (x);                                                                   \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " (" #x ")"); \
+    } while (0)
+
+namespace {
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+std::vector<float2> rope_table(int max_pos, int hd, float base, float fscale, const std::vector<float> * ff) {
+    // ggml NEOX rope cache: theta_i = p * theta_scale^i by repeated f32 multiplication,
+    // divided by the frequency factor and scaled by freq_scale (ext_factor 0, attn_factor 1)
+    const int half = hd / 2;
+    const float ts = powf(base, -2.0f / (float) hd);
+    std::vector<float2> tab((size_t) max_pos * half);
+    for (int p = 0; p < max_pos; p++) {
+        float theta = (float) p;
+        for (int i = 0; i < half; i++) {
+            float t = ff ? theta / (*ff)[i] : theta;
+            t = fscale * t;
+            tab[(size_t) p * half + i] = make_float2(cosf(t), sinf(t));
+            theta *= ts;
+        }
+    }
+    return tab;
+}
+
+std::vector<float> llama3_freq_factors(const DdConfig & c) {
+    // src/depth_decoder.cpp:10-29
+    const int half = c.hd / 2;
+    std::vector<float> ff(half, 1.0f);
+    const float pi = 3.14159265358979323846f;
+    const float low_wl = (float) c.orig_ctx / c.low;
+    const float high_wl = (float) c.orig_ctx / c.high;
+    for (int i = 0; i < half; i++) {
+        const float freq = std::pow(c.theta, -2.0f * (float) i / (float) c.hd);
+        const float wavelen = 2.0f * pi / freq;
+        if (wavelen > low_wl) ff[i] = c.factor;
+        else if (wavelen < high_wl) ff[i] = 1.0f;
+        else {
+            const float smooth = ((float) c.orig_ctx / wavelen - c.low) / (c.high - c.low);
+            ff[i] = 1.0f / ((1.0f - smooth) / c.factor + smooth);
+        }
+    }
+    return ff;
+}
+
+std::string shape_str(const GgufTensor & t) {
+    std::string s = "[";
+    for (size_t i = 0; i < 3; i++) {
+        if (i) s += ", ";
+        s += i < t.ne.size() ? std::to_string(t.ne[i]) : std::string("1");
+    }
+    return s + "]";
+}
+
+void check_shape(const GgufTensor & t, int64_t n0, int64_t n1, int64_t n2 = -1) {
+    // src/depth_decoder.cpp:31-38: a file built for another codebook or vocab count fails here
+    const int64_t e0 = t.ne.size() > 0 ? t.ne[0] : 1, e1 = t.ne.size() > 1 ? t.ne[1] : 1, e2 = t.ne.size() > 2 ? t.ne[2] : 1;
+    if (e0 == n0 && e1 == n1 && (n2 < 0 || e2 == n2)) return;
+    throw std::runtime_error(t.name + " is " + shape_str(t) + ", expected [" + std::to_string(n0) + ", " +
+                             std::to_string(n1) + ", " + (n2 < 0 ? std::string("any") : std::to_string(n2)) + "]");
+}
+}  // namespace
+
+template <class T> T * Engine::dalloc(size_t n) {
+    void * p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    allocs_.push_back(p);
+    return (T *) p;
+}
+
+const GgufTensor * Engine::need(const std::string & name) {
+    const GgufTensor * t = gg_.find(name);
+    if (!t) throw std::runtime_error("missing tensor: " + name);
+    return t;
+}
+
+QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool interleave_pairs, int row0, int rows) {
+    const int K = (int) parts[0]->ne[0];
+    for (auto * t : parts) {
+        if (t->type != GT_Q8_0) throw std::runtime_error(t->name + ": only Q8_0 linear weights are supported by this engine");
+        if (t->ne[0] != K) throw std::runtime_error(t->name + ": row length differs from its fused partner");
+    }
+    const int KB = K / 32;
+    const size_t row_bytes = (size_t) KB * 34;
+    std::vector<const uint8_t *> src_rows;
+    if (interleave_pairs) {
+        const int F = (int) parts[0]->rows();
+        if (parts.size() != 2 || parts[1]->rows() != F || F % 8) throw std::runtime_error("gate/up pair shapes differ");
+        src_rows.resize((size_t) 2 * F);
+        for (int p = 0; p < 2 * F; p++) {
+            const int tile = p / 16, r = p % 16;
+            const GgufTensor * t = r < 8 ? parts[0] : parts[1];
+            const int src = tile * 8 + (r & 7);
+            src_rows[p] = gg_.data(*t) + (size_t) src * row_bytes;
+        }
+    } else if (rows >= 0) {
+        for (int r = 0; r < rows; r++) src_rows.push_back(gg_.data(*parts[0]) + (size_t) (row0 + r) * row_bytes);
+    } else {
+        for (auto * t : parts)
+            for (int64_t r = 0; r < t->rows(); r++) src_rows.push_back(gg_.data(*t) + (size_t) r * row_bytes);
+    }
+    const int M = (int) src_rows.size();
+    std::vector<uint8_t> raw((size_t) M * row_bytes);
+    for (int r = 0; r < M; r++) std::memcpy(raw.data() + (size_t) r * row_bytes, src_rows[r], row_bytes);
+    uint8_t * raw_dev = nullptr;
+    CK(cudaMalloc(&raw_dev, raw.size()));
+    CK(cudaMemcpyAsync(raw_dev, raw.data(), raw.size(), cudaMemcpyHostToDevice, stream_));
+    QMat q;
+    q.M = M;
+    q.MT = (M + 15) / 16;
+    q.K = K;
+    q.KB = KB;
+    uint4 * qs = dalloc<uint4>((size_t) q.MT * KB * 32);
+    half2 * ds = dalloc<half2>((size_t) q.MT * KB * 8);
+    repack_q8(raw_dev, M, K, qs, ds, stream_);
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaFree(raw_dev));
+    q.qs = qs;
+    q.ds = ds;
+    return q;
+}
+
+QRows Engine::load_qrows(const GgufTensor * t) {
+    if (t->type != GT_Q8_0) throw std::runtime_error(t->name + ": embedding tables must be Q8_0");
+    QRows e;
+    e.K = (int) t->ne[0];
+    e.rows = (int) t->rows();
+    uint8_t * raw_dev = nullptr;
+    CK(cudaMalloc(&raw_dev, t->nbytes));
+    CK(cudaMemcpyAsync(raw_dev, gg_.data(*t), t->nbytes, cudaMemcpyHostToDevice, stream_));
+    int8_t * qs = dalloc<int8_t>((size_t) e.rows * e.K);
+    half * ds = dalloc<half>((size_t) e.rows * (e.K / 32));
+    split_q8_rows(raw_dev, e.rows, e.K, qs, ds, stream_);
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaFree(raw_dev));
+    e.qs = qs;
+    e.ds = ds;
+    return e;
+}
+
+float * Engine::load_f32(const std::string & name, int expect) {
+    const GgufTensor * t = need(name);
+    if (t->type != GT_F32 || t->nelem() != expect)
+        throw std::runtime_error(name + ": expected an F32 vector of " + std::to_string(expect));
+    float * d = dalloc<float>(expect);
+    CK(cudaMemcpyAsync(d, gg_.data(*t), (size_t) expect * 4, cudaMemcpyHostToDevice, stream_));
+    return d;
+}
+
+Engine::Engine(const std::string & path, int dev) : device(dev) {
+    CK(cudaSetDevice(device));
+    CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    init_kernel_attributes();
+    std::string err;
+    if (!gg_.open(path, err)) throw std::runtime_error(err);
+    cfg = parse_config(gg_);
+    if (!tok_.load(gg_)) throw std::runtime_error("GGUF has no tokenizer.ggml.tokens");
+    const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs;
+    if (nc < 2 || nc > 64) throw std::runtime_error("num_codebooks must be in [2, 64]");
+    check_shape(*need("dd.in_proj.weight"), H, cfg.dd.hidden);
+    check_shape(*need("audio_embd.weight"), H, (int64_t) nc * vs);
+    check_shape(*need("dd.codebooks_head.weight"), cfg.dd.hidden, vs, nc - 1);
+
+    // backbone
+    const BbConfig & bb = cfg.bb;
+    for (int l = 0; l < bb.n_layer; l++) {
+        const std::string p = "bb.blk." + std::to_string(l);
+        LayerW w;
+        w.qkv = load_qmat({ need(p + ".attn_q.weight"), need(p + ".attn_k.weight"), need(p + ".attn_v.weight") }, false);
+        w.o = load_qmat({ need(p + ".attn_output.weight") }, false);
+        w.gu = load_qmat({ need(p + ".ffn_gate.weight"), need(p + ".ffn_up.weight") }, true);
+        w.down = load_qmat({ need(p + ".ffn_down.weight") }, false);
+        w.attn_norm = load_f32(p + ".attn_norm.weight", H);
+        w.ffn_norm = load_f32(p + ".ffn_norm.weight", H);
+        w.q_norm = load_f32(p + ".attn_q_norm.weight", bb.hd);
+        w.k_norm = load_f32(p + ".attn_k_norm.weight", bb.hd);
+        if (w.qkv.M != (bb.n_head + 2 * bb.n_kv) * bb.hd || w.qkv.K != H) throw std::runtime_error(p + ": attention shapes do not match the config");
+        bb_.push_back(w);
+    }
+    bb_out_norm_ = load_f32("bb.output_norm.weight", H);
+    lm_head_ = load_qmat({ need("bb.lm_head.weight") }, false);
+    vbb_ = lm_head_.M;
+    if (vbb_ > 4096) throw std::runtime_error("lm_head wider than the sampler's 4096 entries");
+
+    // depth decoder
+    const DdConfig & dd = cfg.dd;
+    dd_in_ = load_qmat({ need("dd.in_proj.weight") }, false);
+    for (int l = 0; l < dd.n_layer; l++) {
+        const std::string p = "dd.blk." + std::to_string(l);
+        LayerW w;
+        w.qkv = load_qmat({ need(p + ".attn_q.weight"), need(p + ".attn_k.weight"), need(p + ".attn_v.weight") }, false);
+        w.o = load_qmat({ need(p + ".attn_output.weight") }, false);
+        w.gu = load_qmat({ need(p + ".ffn_gate.weight"), need(p + ".ffn_up.weight") }, true);
+        w.down = load_qmat({ need(p + ".ffn_down.weight") }, false);
+        w.attn_norm = load_f32(p + ".attn_norm.weight", dd.hidden);
+        w.ffn_norm = load_f32(p + ".ffn_norm.weight", dd.hidden);
+        dd_.push_back(w);
+    }
+    dd_out_norm_ = load_f32("dd.output_norm.weight", dd.hidden);
+    const GgufTensor * head = need("dd.codebooks_head.weight");
+    for (int j = 0; j < nc - 1; j++) dd_head_.push_back(load_qmat({ head }, false, j * vs, vs));
+    audio_embd_ = load_qrows(need("audio_embd.weight"));
+
+    // text encoder (prefill)
+    has_te_ = gg_.find("te.token_embd.weight") != nullptr;
+    if (has_te_) {
+        const TeConfig & te = cfg.te;
+        for (int l = 0; l < te.n_layer; l++) {
+            const std::string p = "te.blk." + std::to_string(l);
+            LayerW w;
+            w.qkv = load_qmat({ need(p + ".attn_q.weight"), need(p + ".attn_k.weight"), need(p + ".attn_v.weight") }, false);
+            w.o = load_qmat({ need(p + ".attn_output.weight") }, false);
+            w.gu = load_qmat({ need(p + ".ffn_gate.weight"), need(p + ".ffn_up.weight") }, true);
+            w.down = load_qmat({ need(p + ".ffn_down.weight") }, false);
+            w.attn_norm = load_f32(p + ".attn_norm.weight", te.hidden);
+            w.ffn_norm = load_f32(p + ".ffn_norm.weight", te.hidden);
+            w.q_norm = load_f32(p + ".attn_q_norm.weight", te.hd);
+            w.k_norm = load_f32(p + ".attn_k_norm.weight", te.hd);
+            w.post_attn = load_f32(p + ".post_attn_norm.weight", te.hidden);
+            w.post_ffn = load_f32(p + ".post_ffn_norm.weight", te.hidden);
+            te_.push_back(w);
+        }
+        te_out_norm_ = load_f32("te.output_norm.weight", te.hidden);
+        te_proj_ = load_qmat({ need("te.proj.weight") }, false);
+        te_embd_ = load_qrows(need("te.token_embd.weight"));
+    }
+    build_rope_tables();
+    alloc_buffers();
+    CK(cudaStreamSynchronize(stream_));
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (auto & kv : graphs_) cudaGraphExecDestroy(kv.second);
+    for (auto & kv : graph_defs_) cudaGraphDestroy(kv.second);
+    for (void * p : prefill_allocs_) cudaFree(p);
+    for (void * p : allocs_) cudaFree(p);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::build_rope_tables() {
+    const int max_ctx = 4096;
+    rope_bb_max_ = max_ctx + 16;
+    auto up = [&](const std::vector<float2> & v) {
+        float2 * d = dalloc<float2>(v.size());
+        CK(cudaMemcpyAsync(d, v.data(), v.size() * sizeof(float2), cudaMemcpyHostToDevice, stream_));
+        CK(cudaStreamSynchronize(stream_));
+        return d;
+    };
+    rope_bb_ = up(rope_table(rope_bb_max_, cfg.bb.hd, cfg.bb.theta, 1.0f, nullptr));
+    const std::vector<float> ff = llama3_freq_factors(cfg.dd);
+    rope_dd_ = up(rope_table(cfg.nc + 2, cfg.dd.hd, cfg.dd.theta, 1.0f, &ff));
+    if (has_te_) {
+        rope_te_max_ = max_ctx;
+        rope_te_full_ = up(rope_table(rope_te_max_, cfg.te.hd, cfg.te.theta_full, cfg.te.fscale_full, nullptr));
+        rope_te_slide_ = up(rope_table(rope_te_max_, cfg.te.hd, cfg.te.theta_sliding, 1.0f, nullptr));
+    }
+}
+
+void Engine::alloc_buffers() {
+    const char * env_r = std::getenv("BZB_MAX_BATCH");
+    rmax_ = env_r ? std::max(8, round_up(std::atoi(env_r), 8)) : 256;
+    kmax_ = 64;
+    max_slots_ = 1024;
+    max_pages_ = 256;  // 4096 positions per session
+    const BbConfig & bb = cfg.bb;
+    const DdConfig & dd = cfg.dd;
+    const int H = cfg.hidden, nc = cfg.nc;
+    const size_t page_elems = (size_t) bb.n_layer * 2 * bb.n_kv * 16 * bb.hd;
+    size_t free_b = 0, total_b = 0;
+    CK(cudaMemGetInfo(&free_b, &total_b));
+    size_t pool_bytes = (size_t) 8 << 30;
+    if (const char * e = std::getenv("BZB_KV_POOL_MB")) pool_bytes = (size_t) std::atoll(e) << 20;
+    pool_bytes = std::min(pool_bytes, free_b / 2);
+    n_pages_ = (int) std::max<size_t>(16, pool_bytes / (page_elems * sizeof(half)));
+    kv_pool_ = dalloc<half>((size_t) n_pages_ * page_elems);
+    free_pages_.clear();
+    for (int p = n_pages_ - 1; p >= 0; p--) free_pages_.push_back(p);
+    page_table_ = dalloc<int>((size_t) max_slots_ * max_pages_);
+    CK(cudaMemsetAsync(page_table_, 0, (size_t) max_slots_ * max_pages_ * sizeof(int), stream_));
+    st_ = dalloc<SessState>(max_slots_);
+    CK(cudaMemsetAsync(st_, 0, (size_t) max_slots_ * sizeof(SessState), stream_));
+    hist_ld_ = round_up(vbb_, 8);
+    hist_ = dalloc<uint16_t>((size_t) max_slots_ * hist_ld_);
+    hid32_ = dalloc<float>((size_t) max_slots_ * H);
+    slots_.assign(max_slots_, SlotHost());
+    free_slots_.clear();
+    for (int s = max_slots_ - 1; s >= 0; s--) free_slots_.push_back(s);
+
+    const int R2 = 2 * rmax_;
+    const int ddq = dd.n_head * dd.hd, ddkv = dd.n_kv * dd.hd;
+    row_slot_ = dalloc<int>(rmax_);
+    row_active_ = dalloc<int>(rmax_);
+    next_ = dalloc<int>(rmax_);
+    seeds_ = dalloc<uint32_t>(rmax_);
+    cur_frames_ = dalloc<int>((size_t) rmax_ * nc);
+    frames_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
+    step_ctr_ = dalloc<int>(1);
+    any_active_ = dalloc<int>(kmax_);
+    slot_scalar_ = dalloc<int>(1);
+    din16_ = dalloc<half>((size_t) R2 * H);
+    dx_ = dalloc<float>((size_t) R2 * dd.hidden);
+    dh16_ = dalloc<half>((size_t) R2 * dd.hidden);
+    dff16_ = dalloc<half>((size_t) R2 * dd.ffn);
+    dqkv_ = dalloc<float>((size_t) R2 * (ddq + 2 * ddkv));
+    datt16_ = dalloc<half>((size_t) R2 * ddq);
+    dkv_ = dalloc<float>((size_t) dd.n_layer * rmax_ * nc * 2 * ddkv);
+    dlog_ = dalloc<float>((size_t) rmax_ * cfg.vs);
+    const int bbq = bb.n_head * bb.hd, bbkv = bb.n_kv * bb.hd;
+    bx_ = dalloc<float>((size_t) rmax_ * H);
+    bh16_ = dalloc<half>((size_t) rmax_ * H);
+    bff16_ = dalloc<half>((size_t) rmax_ * bb.ffn);
+    bqkv_ = dalloc<float>((size_t) rmax_ * (bbq + 2 * bbkv));
+    batt16_ = dalloc<half>((size_t) rmax_ * bbq);
+    blog_ = dalloc<float>((size_t) rmax_ * vbb_);
+    scr_.ws_elems = (size_t) 16 << 20;
+    scr_.ws = dalloc<float4>(scr_.ws_elems);
+    scr_.n_counters = 1 << 16;
+    scr_.counters = dalloc<int>(scr_.n_counters);
+    CK(cudaMemsetAsync(scr_.counters, 0, (size_t) scr_.n_counters * sizeof(int), stream_));
+    CK(cudaMemsetAsync(din16_, 0, (size_t) R2 * H * sizeof(half), stream_));
+    CK(cudaMemsetAsync(dkv_, 0, (size_t) dd.n_layer * rmax_ * nc * 2 * ddkv * sizeof(float), stream_));
+}
+
+void Engine::ensure_prefill_capacity(int T) {
+    if (T <= tmax_) return;
+    CK(cudaStreamSynchronize(stream_));
+    for (void * p : prefill_allocs_) cudaFree(p);
+    prefill_allocs_.clear();
+    tmax_ = round_up(std::max(T, 256), 256);
+    auto pa = [&](size_t bytes) { void * p = nullptr; CK(cudaMalloc(&p, std::max<size_t>(bytes, 16))); prefill_allocs_.push_back(p); return p; };
+    const int H = cfg.hidden;
+    const BbConfig & bb = cfg.bb;
+    const int bbq = bb.n_head * bb.hd, bbkv = bb.n_kv * bb.hd;
+    px_ = (float *) pa((size_t) tmax_ * H * 4);
+    ph16_ = (half *) pa((size_t) tmax_ * H * 2);
+    pff16_ = (half *) pa((size_t) tmax_ * bb.ffn * 2);
+    pqkv_ = (float *) pa((size_t) tmax_ * (bbq + 2 * bbkv) * 4);
+    patt16_ = (half *) pa((size_t) tmax_ * bbq * 2);
+    plog_ = (float *) pa((size_t) vbb_ * 4);
+    ptok_ = (int *) pa((size_t) tmax_ * 4);
+    pframes_ = (int *) pa((size_t) tmax_ * cfg.nc * 4);
+    if (has_te_) {
+        const TeConfig & te = cfg.te;
+        const int teq = te.n_head * te.hd, tekv = te.n_kv * te.hd;
+        tx_ = (float *) pa((size_t) tmax_ * te.hidden * 4);
+        th16_ = (half *) pa((size_t) tmax_ * te.hidden * 2);
+        tff16_ = (half *) pa((size_t) tmax_ * te.ffn * 2);
+        tqkv_ = (float *) pa((size_t) tmax_ * (teq + 2 * tekv) * 4);
+        tatt16_ = (half *) pa((size_t) tmax_ * teq * 2);
+        ttmp_ = (float *) pa((size_t) tmax_ * te.hidden * 4);
+        tk_ = (float *) pa((size_t) tmax_ * tekv * 4);
+        tv_ = (float *) pa((size_t) tmax_ * tekv * 4);
+    }
+}
+
+// ------------------------------------------------------------------------------------ step
+void Engine::gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
+    launches_++;
+    if (!prof_) {
+        launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+        return;
+    }
+    ProfRec r;
+    CK(cudaEventCreate(&r.a));
+    CK(cudaEventCreate(&r.b));
+    const double out_bytes = (double) rows * (out.kind == EPI_STORE || out.kind == EPI_RESID ? w.M * 4.0 : w.M);
+    r.bytes = (double) w.M * w.K / 32.0 * 34.0 + (double) rows * w.K * 2.0 + out_bytes;
+    CK(cudaEventRecord(r.a, stream_));
+    launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+    CK(cudaEventRecord(r.b, stream_));
+    prof_->push_back(r);
+}
+
+void Engine::depth_layer(int l, int rows, int R, int n_new, int start) {
+    const DdConfig & dd = cfg.dd;
+    const LayerW & w = dd_[l];
+    const int D = dd.hidden, q = dd.n_head * dd.hd, kv = dd.n_kv * dd.hd, qkvd = q + 2 * kv;
+    launch_rmsnorm(dx_, D, w.attn_norm, D, dd.eps, dh16_, D, nullptr, 0, 0, rows, nullptr, stream_);
+    gemv(w.qkv, dh16_, D, rows, GemvOut{ EPI_STORE, dqkv_, nullptr, qkvd });
+    AttnDecodeArgs a;
+    a.qkv = dqkv_; a.ldq = qkvd; a.n_head = dd.n_head; a.n_kv = dd.n_kv; a.hd = dd.hd;
+    a.R = R; a.n_new = n_new; a.row_slot = row_slot_; a.row_active = row_active_; a.st = nullptr; a.start = start;
+    a.eps = dd.eps; a.rope = rope_dd_; a.scale = 1.0f / std::sqrt((float) dd.hd);
+    a.kv.flat = dkv_ + (size_t) l * rmax_ * cfg.nc * 2 * kv;
+    a.kv.cap = cfg.nc;
+    a.out = datt16_; a.ldo = q;
+    launch_attn_decode(a, false, stream_);
+    gemv(w.o, datt16_, q, rows, GemvOut{ EPI_RESID, dx_, nullptr, D });
+    launch_rmsnorm(dx_, D, w.ffn_norm, D, dd.eps, dh16_, D, nullptr, 0, 0, rows, nullptr, stream_);
+    gemv(w.gu, dh16_, D, rows, GemvOut{ EPI_SWIGLU, nullptr, dff16_, dd.ffn });
+    gemv(w.down, dff16_, dd.ffn, rows, GemvOut{ EPI_RESID, dx_, nullptr, D });
+}
+
+void Engine::bb_decode_layer(int l, int R) {
+    const BbConfig & bb = cfg.bb;
+    const LayerW & w = bb_[l];
+    const int H = cfg.hidden, q = bb.n_head * bb.hd, kv = bb.n_kv * bb.hd, qkvd = q + 2 * kv;
+    launch_rmsnorm(bx_, H, w.attn_norm, H, bb.eps, bh16_, H, nullptr, 0, 0, R, nullptr, stream_);
+    gemv(w.qkv, bh16_, H, R, GemvOut{ EPI_STORE, bqkv_, nullptr, qkvd });
+    AttnDecodeArgs a;
+    a.qkv = bqkv_; a.ldq = qkvd; a.n_head = bb.n_head; a.n_kv = bb.n_kv; a.hd = bb.hd;
+    a.R = R; a.n_new = 1; a.row_slot = row_slot_; a.row_active = row_active_; a.st = st_;
+    a.q_norm = w.q_norm; a.k_norm = w.k_norm; a.eps = bb.eps; a.rope = rope_bb_;
+    a.scale = 1.0f / std::sqrt((float) bb.hd);
+    a.kv.pool = kv_pool_; a.kv.page_table = page_table_; a.kv.max_pages = max_pages_; a.kv.n_layer = bb.n_layer; a.kv.layer = l;
+    a.out = batt16_; a.ldo = q;
+    launch_attn_decode(a, true, stream_);
+    gemv(w.o, batt16_, q, R, GemvOut{ EPI_RESID, bx_, nullptr, H });
+    launch_rmsnorm(bx_, H, w.ffn_norm, H, bb.eps, bh16_, H, nullptr, 0, 0, R, nullptr, stream_);
+    gemv(w.gu, bh16_, H, R, GemvOut{ EPI_SWIGLU, nullptr, bff16_, bb.ffn });
+    gemv(w.down, bff16_, bb.ffn, R, GemvOut{ EPI_RESID, bx_, nullptr, H });
+}
+
+void Engine::enqueue_step(int R) {
+    const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, D = cfg.dd.hidden;
+    StepArgs sa;
+    sa.R = R; sa.nc = nc; sa.vs = vs; sa.H = H;
+    sa.row_slot = row_slot_; sa.row_active = row_active_; sa.st = st_; sa.hid32 = hid32_; sa.embd = audio_embd_;
+    sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
+    launch_step_init(sa, stream_);
+    // depth sub-step 1: position 0 = backbone hidden, position 1 = cb0 embedding
+    gemv(dd_in_, din16_, H, 2 * R, GemvOut{ EPI_STORE, dx_, nullptr, D });
+    for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, 2 * R, R, 2, 0);
+    launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, R, R, nullptr, stream_);
+    gemv(dd_head_[0], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+    launch_argmax_gather(sa, dlog_, vs, vs, 1, nc > 2 ? 1 : -1, stream_);
+    for (int j = 2; j < nc; j++) {
+        gemv(dd_in_, din16_, H, R, GemvOut{ EPI_STORE, dx_, nullptr, D });
+        for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, R, R, 1, j);
+        launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, 0, R, nullptr, stream_);
+        gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+        launch_argmax_gather(sa, dlog_, vs, vs, j, j + 1 < nc ? j : -1, stream_);
+    }
+    // backbone: one token per session over its own paged cache
+    launch_audio_embed(audio_embd_, cur_frames_, nc, nc, vs, R, bx_, row_active_, stream_);
+    for (int l = 0; l < cfg.bb.n_layer; l++) bb_decode_layer(l, R);
+    launch_rmsnorm(bx_, H, bb_out_norm_, H, cfg.bb.eps, bh16_, H, hid32_, H, 0, R, row_slot_, stream_);
+    gemv(lm_head_, bh16_, H, R, GemvOut{ EPI_STORE, blog_, nullptr, vbb_ });
+    SampleArgs sm;
+    sm.logits = blog_; sm.ld = vbb_; sm.V = vbb_; sm.R = R;
+    sm.row_slot = row_slot_; sm.row_active = row_active_; sm.st = st_; sm.hist = hist_; sm.hist_ld = hist_ld_;
+    // the generator ABI hard-codes the cb0 sampler (src/c_api.cpp:343-351)
+    sm.sup_lo = cfg.cb_size; sm.sup_hi = cfg.vs; sm.eos = cfg.bb_eos;
+    sm.temp = 0.9f; sm.rep = 1.1f; sm.top_p = 1.0f; sm.top_k = 50;
+    sm.seeds = seeds_enabled_ ? seeds_ : nullptr; sm.step_ctr = step_ctr_; sm.next_out = next_;
+    launch_sample(sm, stream_);
+    launch_frames_commit(cur_frames_, frames_all_, R * nc, step_ctr_, stream_);
+}
+
+cudaGraphExec_t Engine::graph_for(int R) {
+    const auto key = std::make_pair(R, seeds_enabled_ ? 1 : 0);
+    auto it = graphs_.find(key);
+    if (it != graphs_.end()) return it->second;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+        enqueue_step(R);
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    CK(cudaStreamEndCapture(stream_, &g));
+    size_t n_nodes = 0;
+    CK(cudaGraphGetNodes(g, nullptr, &n_nodes));
+    graph_nodes_ = (int) n_nodes;
+    cudaGraphExec_t exec = nullptr;
+    CK(cudaGraphInstantiate(&exec, g, 0));
+    graphs_[key] = exec;
+    graph_defs_[key] = g;
+    return exec;
+}
+
+StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
+                        int width, int * next_out, bool fill_inactive) {
+    StepResult res;
+    const int nc = cfg.nc;
+    if (n > rmax_) throw std::runtime_error("batch of " + std::to_string(n) + " sessions exceeds the engine's " + std::to_string(rmax_) + " rows (BZB_MAX_BATCH)");
+    if (K > kmax_) throw std::runtime_error("burst longer than 64 steps");
+    const int R = std::max(8, round_up(n, 8));
+    std::vector<int> rs(R, -1);
+    std::vector<char> used(max_slots_, 0);
+    bool any = false;
+    for (int i = 0; i < n; i++) {
+        auto it = sid_to_slot_.find(sids[i]);
+        if (it == sid_to_slot_.end()) continue;
+        const int s = it->second;
+        if (!slots_[s].active || used[s]) continue;
+        used[s] = 1;
+        rs[i] = s;
+        any = true;
+    }
+    for (int i = 0; i < n; i++) next_out[i] = -1;
+    if (burst && fill_inactive) std::fill_n(frames_out, (size_t) K * n * width, -1);
+    if (!any) return res;
+    seeds_enabled_ = seeds != nullptr;
+    cudaGraphExec_t g = graph_for(R);
+    cur_R_ = R;
+    CK(cudaMemcpyAsync(row_slot_, rs.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    if (seeds) {
+        std::vector<uint32_t> sd(R, 0);
+        for (int i = 0; i < n; i++) sd[i] = seeds[i];
+        CK(cudaMemcpyAsync(seeds_, sd.data(), R * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    }
+    CK(cudaMemsetAsync(step_ctr_, 0, sizeof(int), stream_));
+    CK(cudaMemsetAsync(any_active_, 0, kmax_ * sizeof(int), stream_));
+    CK(cudaMemsetAsync(next_, 0xFF, R * sizeof(int), stream_));
+    for (int k = 0; k < K; k++) CK(cudaGraphLaunch(g, stream_));
+    std::vector<int> fr((size_t) K * R * nc), nx(R), aa(K);
+    CK(cudaMemcpyAsync(fr.data(), frames_all_, fr.size() * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(nx.data(), next_, R * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(aa.data(), any_active_, K * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    for (int k = 0; k < K; k++) res.steps_executed += aa[k] ? 1 : 0;
+    const int wcopy = std::min(width, nc);
+    for (int k = 0; k < K; k++) {
+        for (int i = 0; i < n; i++) {
+            if (rs[i] < 0) continue;
+            const int * src = fr.data() + ((size_t) k * R + i) * nc;
+            if (src[0] < 0 && !burst) continue;
+            int * dst = frames_out + ((size_t) k * n + i) * width;
+            for (int c = 0; c < wcopy; c++) dst[c] = src[c];
+        }
+    }
+    for (int i = 0; i < n; i++) {
+        next_out[i] = rs[i] >= 0 ? nx[i] : -1;
+        if (rs[i] >= 0 && nx[i] < 0) slots_[rs[i]].active = false;
+        if (next_out[i] >= 0) res.still_active++;
+    }
+    return res;
+}
+
+void Engine::step_device_only(int K) {
+    if (cur_R_ == 0) throw std::runtime_error("no batch has been stepped yet");
+    if (K > kmax_) throw std::runtime_error("burst longer than 64 steps");
+    cudaGraphExec_t g = graph_for(cur_R_);
+    CK(cudaMemsetAsync(step_ctr_, 0, sizeof(int), stream_));
+    for (int k = 0; k < K; k++) CK(cudaGraphLaunch(g, stream_));
+}
+
+void Engine::sync() { CK(cudaStreamSynchronize(stream_)); }
+
+bool Engine::session_active(int sid) const {
+    auto it = sid_to_slot_.find(sid);
+    return it != sid_to_slot_.end() && slots_[it->second].active;
+}
+
+// ------------------------------------------------------------------------------------ sessions
+int Engine::acquire_slot(int sid, int n_pages) {
+    if (free_slots_.empty()) throw std::runtime_error("no free session slot");
+    if ((int) free_pages_.size() < n_pages) throw std::runtime_error("KV page pool exhausted");
+    const int slot = free_slots_.back();
+    free_slots_.pop_back();
+    SlotHost & s = slots_[slot];
+    s = SlotHost();
+    s.sid = sid;
+    for (int i = 0; i < n_pages; i++) {
+        s.pages.push_back(free_pages_.back());
+        free_pages_.pop_back();
+    }
+    std::vector<int> row(max_pages_, s.pages.empty() ? 0 : s.pages[0]);
+    for (int i = 0; i < n_pages; i++) row[i] = s.pages[i];
+    CK(cudaMemcpyAsync(page_table_ + (size_t) slot * max_pages_, row.data(), max_pages_ * sizeof(int),
+                       cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    sid_to_slot_[sid] = slot;
+    return slot;
+}
+
+void Engine::release_slot(int slot) {
+    SlotHost & s = slots_[slot];
+    for (int p : s.pages) free_pages_.push_back(p);
+    sid_to_slot_.erase(s.sid);
+    s = SlotHost();
+    free_slots_.push_back(slot);
+}
+
+bool Engine::session_free(int sid) {
+    auto it = sid_to_slot_.find(sid);
+    if (it == sid_to_slot_.end()) return false;
+    CK(cudaStreamSynchronize(stream_));
+    release_slot(it->second);
+    return true;
+}
+
+void Engine::te_forward(const std::vector<int> & tokens, float * out_rows) {
+    if (!has_te_) throw std::runtime_error("GGUF has no text encoder (te.*) tensors");
+    const TeConfig & te = cfg.te;
+    const int T = (int) tokens.size();
+    if (T > rope_te_max_) throw std::runtime_error("text segment longer than 4096 tokens");
+    ensure_prefill_capacity(T);
+    const int D = te.hidden, q = te.n_head * te.hd, kv = te.n_kv * te.hd, qkvd = q + 2 * kv;
+    CK(cudaMemcpyAsync(ptok_, tokens.data(), T * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    launch_embed_rows(te_embd_, ptok_, T, te.embed_scale, tx_, nullptr, D, stream_);
+    for (int l = 0; l < te.n_layer; l++) {
+        const LayerW & w = te_[l];
+        const bool full = l < (int) te.is_full.size() && te.is_full[l] != 0;
+        launch_rmsnorm(tx_, D, w.attn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.qkv, th16_, D, T, GemvOut{ EPI_STORE, tqkv_, nullptr, qkvd });
+        PrefillArgs pa;
+        pa.qkv = tqkv_; pa.ldq = qkvd; pa.T = T; pa.start = 0;
+        pa.n_head = te.n_head; pa.n_kv = te.n_kv; pa.hd = te.hd;
+        pa.q_norm = w.q_norm; pa.k_norm = w.k_norm; pa.eps = te.eps;
+        pa.rope = full ? rope_te_full_ : rope_te_slide_;
+        pa.scale = 1.0f / std::sqrt(te.qpas);
+        pa.flat_k = tk_; pa.flat_v = tv_;
+        pa.window = full ? 0 : te.window;
+        pa.causal = false;
+        pa.out = tatt16_; pa.ldo = q;
+        launch_qk_prep(pa, false, stream_);
+        launch_attn_prefill(pa, false, stream_);
+        gemv(w.o, tatt16_, q, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
+        launch_norm_add(tx_, ttmp_, D, w.post_attn, te.eps, T, stream_);
+        launch_rmsnorm(tx_, D, w.ffn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.gu, th16_, D, T, GemvOut{ EPI_GEGLU, nullptr, tff16_, te.ffn });
+        gemv(w.down, tff16_, te.ffn, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
+        launch_norm_add(tx_, ttmp_, D, w.post_ffn, te.eps, T, stream_);
+    }
+    launch_rmsnorm(tx_, D, te_out_norm_, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+    gemv(te_proj_, th16_, D, T, GemvOut{ EPI_STORE, out_rows, nullptr, cfg.hidden });
+}
+
+void Engine::bb_prefill(int slot, int T) {
+    const BbConfig & bb = cfg.bb;
+    const int H = cfg.hidden, q = bb.n_head * bb.hd, kv = bb.n_kv * bb.hd, qkvd = q + 2 * kv;
+    for (int l = 0; l < bb.n_layer; l++) {
+        const LayerW & w = bb_[l];
+        launch_rmsnorm(px_, H, w.attn_norm, H, bb.eps, ph16_, H, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.qkv, ph16_, H, T, GemvOut{ EPI_STORE, pqkv_, nullptr, qkvd });
+        PrefillArgs pa;
+        pa.qkv = pqkv_; pa.ldq = qkvd; pa.T = T; pa.start = 0;
+        pa.n_head = bb.n_head; pa.n_kv = bb.n_kv; pa.hd = bb.hd;
+        pa.q_norm = w.q_norm; pa.k_norm = w.k_norm; pa.eps = bb.eps; pa.rope = rope_bb_;
+        pa.scale = 1.0f / std::sqrt((float) bb.hd);
+        pa.kv.pool = kv_pool_; pa.kv.n_layer = bb.n_layer; pa.kv.layer = l;
+        pa.page_row = page_table_ + (size_t) slot * max_pages_;
+        pa.causal = true;
+        pa.out = patt16_; pa.ldo = q;
+        launch_qk_prep(pa, true, stream_);
+        launch_attn_prefill(pa, true, stream_);
+        gemv(w.o, patt16_, q, T, GemvOut{ EPI_RESID, px_, nullptr, H });
+        launch_rmsnorm(px_, H, w.ffn_norm, H, bb.eps, ph16_, H, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.gu, ph16_, H, T, GemvOut{ EPI_SWIGLU, nullptr, pff16_, bb.ffn });
+        gemv(w.down, pff16_, bb.ffn, T, GemvOut{ EPI_RESID, px_, nullptr, H });
+    }
+    CK(cudaMemcpyAsync(slot_scalar_, &slot, sizeof(int), cudaMemcpyHostToDevice, stream_));
+    launch_rmsnorm(px_, H, bb_out_norm_, H, bb.eps, ph16_, H, hid32_, H, T - 1, 1, slot_scalar_, stream_);
+    gemv(lm_head_, ph16_, H, 1, GemvOut{ EPI_STORE, plog_, nullptr, vbb_ });
+}
+
+void Engine::session_create(int sid, const std::string & text, const char * instruction, const char * ref_text,
+                            const int * ref_codes, int ref_frames, float cfg_scale, uint32_t seed, int max_new_tokens,
+                            int * out_cb0, int * out_alloc) {
+    const float scale = cfg_scale > 0.0f ? cfg_scale : 1.0f;
+    if (scale != 1.0f) throw std::runtime_error("classifier-free guidance (cfg_scale != 1) is not supported by this engine yet");
+    // output length estimate (src/c_api.cpp:354-364)
+    int est = max_new_tokens;
+    if (est <= 0) {
+        int words = 0;
+        bool in_w = false;
+        for (unsigned char ch : text) {
+            if (std::isspace(ch)) in_w = false;
+            else if (!in_w) { in_w = true; words++; }
+        }
+        est = std::min(1000, (int) std::ceil(words * 1.5f) + 30);
+    }
+    const std::string spk = "[S0]";
+    const std::string ins = instruction ? instruction : "Speak clearly and naturally.";
+    const bool has_ref = ref_codes != nullptr && ref_frames > 0 && ref_text != nullptr && std::strlen(ref_text) > 0;
+    std::vector<std::vector<int>> segs;
+    if (has_ref) segs.push_back(tok_.encode(spk + ref_text, true));
+    segs.push_back(tok_.encode(spk + "<ins_bos>" + ins + "<ins_eos>" + text, true));
+    session_create_tokens(sid, segs, has_ref ? ref_codes : nullptr, has_ref ? ref_frames : 0, seed, est, out_cb0, out_alloc);
+}
+
+void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> & segs, const int * ref_codes,
+                                   int ref_frames, uint32_t seed, int est, int * out_cb0, int * out_alloc) {
+    const int H = cfg.hidden, nc = cfg.nc;
+    // prompt layout (src/c_api.cpp:388-396): [ref text][ref frames][EOS frame] then the tail text
+    int total = 0;
+    for (auto & s : segs) total += (int) s.size();
+    if (ref_codes) total += ref_frames + 1;
+    if (total <= 0) throw std::runtime_error("empty prompt");
+    const int max_available = 2040 - total;
+    if (est > max_available) est = std::max(64, max_available);
+    const int alloc = total + est + 8;
+    const int n_pages = (alloc + 15) / 16;
+    if (n_pages > max_pages_) throw std::runtime_error("prompt plus generation budget exceeds 4096 positions");
+    auto old = sid_to_slot_.find(sid);
+    if (old != sid_to_slot_.end()) {
+        CK(cudaStreamSynchronize(stream_));
+        release_slot(old->second);
+    }
+    const int slot = acquire_slot(sid, n_pages);
+    try {
+        ensure_prefill_capacity(total);
+        int off = 0;
+        auto add_text = [&](const std::vector<int> & toks) {
+            te_forward(toks, px_ + (size_t) off * H);
+            off += (int) toks.size();
+        };
+        auto add_frames = [&](const int * codes, int F) {
+            CK(cudaMemcpyAsync(pframes_, codes, (size_t) F * nc * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            launch_audio_embed(audio_embd_, pframes_, nc, nc, cfg.vs, F, px_ + (size_t) off * H, nullptr, stream_);
+            CK(cudaStreamSynchronize(stream_));
+            off += F;
+        };
+        if (ref_codes) {
+            add_text(segs[0]);
+            add_frames(ref_codes, ref_frames);
+            std::vector<int> eos((size_t) nc, cfg.cb_eos);
+            add_frames(eos.data(), 1);
+            add_text(segs[1]);
+        } else {
+            add_text(segs.back());
+        }
+        bb_prefill(slot, total);
+        SessState s{};
+        s.active = 1;
+        s.pos = total;
+        s.steps = 0;
+        s.max_tokens = est;
+        s.last_cb0 = -1;
+        s.key = seed;
+        s.draw = 0;
+        CK(cudaMemcpyAsync(st_ + slot, &s, sizeof(SessState), cudaMemcpyHostToDevice, stream_));
+        CK(cudaMemsetAsync(hist_ + (size_t) slot * hist_ld_, 0, hist_ld_ * sizeof(uint16_t), stream_));
+        SampleArgs sm;
+        sm.logits = plog_; sm.ld = vbb_; sm.V = vbb_; sm.R = 1;
+        sm.row_slot = slot_scalar_; sm.row_active = nullptr; sm.st = st_; sm.hist = hist_; sm.hist_ld = hist_ld_;
+        sm.sup_lo = cfg.cb_size; sm.sup_hi = cfg.vs; sm.eos = cfg.bb_eos;
+        sm.temp = 0.9f; sm.rep = 1.1f; sm.top_p = 1.0f; sm.top_k = 50;
+        sm.seeds = nullptr; sm.step_ctr = nullptr; sm.next_out = next_; sm.update_hist_first = 1;
+        launch_sample(sm, stream_);
+        int cb0 = -1;
+        CK(cudaMemcpyAsync(&cb0, next_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+        SlotHost & sh = slots_[slot];
+        sh.active = true;
+        sh.max_tokens = est;
+        sh.alloc = alloc;
+        *out_cb0 = cb0;
+        if (out_alloc) *out_alloc = alloc;
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        release_slot(slot);
+        throw;
+    }
+}
+
+// ------------------------------------------------------------------------------------ debug
+void Engine::debug_hidden(int sid, float * out) {
+    auto it = sid_to_slot_.find(sid);
+    if (it == sid_to_slot_.end()) throw std::runtime_error("unknown session");
+    CK(cudaMemcpyAsync(out, hid32_ + (size_t) it->second * cfg.hidden, cfg.hidden * sizeof(float),
+                       cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+}
+
+void Engine::debug_depth(int n, const float * hidden, const int * cb0, const int * forced, int * codes_out,
+                         float * logits_out) {
+    const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, D = cfg.dd.hidden;
+    if (n <= 0 || n > rmax_) throw std::runtime_error("debug_depth: bad row count");
+    const int R = std::max(8, round_up(n, 8));
+    std::vector<int> rs(R, -1), ra(R, 0);
+    for (int i = 0; i < n; i++) { rs[i] = i; ra[i] = 1; }
+    CK(cudaMemcpyAsync(row_slot_, rs.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(row_active_, ra.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    std::vector<half> h16((size_t) 2 * R * H, __float2half(0.0f));
+    for (int i = 0; i < n; i++)
+        for (int d = 0; d < H; d++) h16[(size_t) i * H + d] = __float2half_rn(hidden[(size_t) i * H + d]);
+    CK(cudaMemcpyAsync(din16_, h16.data(), h16.size() * sizeof(half), cudaMemcpyHostToDevice, stream_));
+    std::vector<int> idx(R, 0);
+    for (int i = 0; i < n; i++) idx[i] = cb0[i];
+    ensure_prefill_capacity(R);
+    CK(cudaMemcpyAsync(ptok_, idx.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    launch_embed_rows(audio_embd_, ptok_, n, 1.0f, nullptr, din16_ + (size_t) R * H, H, stream_);
+    StepArgs sa;
+    sa.R = R; sa.nc = nc; sa.vs = vs; sa.H = H;
+    sa.row_slot = row_slot_; sa.row_active = row_active_; sa.st = st_; sa.hid32 = hid32_; sa.embd = audio_embd_;
+    sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
+    std::vector<float> lg((size_t) R * vs);
+    std::vector<int> fr((size_t) R * nc);
+    for (int j = 1; j < nc; j++) {
+        const int rows = j == 1 ? 2 * R : R;
+        gemv(dd_in_, din16_, H, rows, GemvOut{ EPI_STORE, dx_, nullptr, D });
+        for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, rows, R, j == 1 ? 2 : 1, j == 1 ? 0 : j);
+        launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, j == 1 ? R : 0, R, nullptr, stream_);
+        gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+        launch_argmax_gather(sa, dlog_, vs, vs, j, (j + 1 < nc && !forced) ? j : -1, stream_);
+        CK(cudaMemcpyAsync(lg.data(), dlog_, lg.size() * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+        for (int i = 0; i < n; i++)
+            std::memcpy(logits_out + ((size_t) i * (nc - 1) + (j - 1)) * vs, lg.data() + (size_t) i * vs, vs * sizeof(float));
+        if (forced && j + 1 < nc) {
+            for (int i = 0; i < n; i++) idx[i] = j * vs + forced[(size_t) i * (nc - 1) + (j - 1)];
+            CK(cudaMemcpyAsync(ptok_, idx.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            launch_embed_rows(audio_embd_, ptok_, n, 1.0f, nullptr, din16_, H, stream_);
+        }
+    }
+    CK(cudaMemcpyAsync(fr.data(), cur_frames_, fr.size() * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    for (int i = 0; i < n; i++)
+        for (int j = 1; j < nc; j++) codes_out[(size_t) i * (nc - 1) + (j - 1)] = fr[(size_t) i * nc + j];
+}
+
+void Engine::debug_gemv(const char * tensor, int sub, int rows, const float * x, float * y) {
+    const GgufTensor * t = need(tensor);
+    QMat w = sub >= 0 ? load_qmat({ t }, false, (int) (sub * t->ne[1]), (int) t->ne[1]) : load_qmat({ t }, false);
+    const int K = w.K, M = w.M;
+    ensure_prefill_capacity(rows);
+    std::vector<half> xh((size_t) rows * K);
+    for (size_t i = 0; i < xh.size(); i++) xh[i] = __float2half_rn(x[i]);
+    half * xd = nullptr;
+    float * yd = nullptr;
+    CK(cudaMalloc(&xd, xh.size() * sizeof(half)));
+    CK(cudaMalloc(&yd, (size_t) rows * M * sizeof(float)));
+    CK(cudaMemcpyAsync(xd, xh.data(), xh.size() * sizeof(half), cudaMemcpyHostToDevice, stream_));
+    launch_gemv(w, xd, K, rows, GemvOut{ EPI_STORE, yd, nullptr, M }, scr_, stream_);
+    CK(cudaMemcpyAsync(y, yd, (size_t) rows * M * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    cudaFree(xd);
+    cudaFree(yd);
+}
+
+void Engine::profile_step(double * out) {
+    if (cur_R_ == 0) throw std::runtime_error("no batch has been stepped yet");
+    std::vector<ProfRec> recs;
+    cudaEvent_t a, b;
+    CK(cudaEventCreate(&a));
+    CK(cudaEventCreate(&b));
+    CK(cudaMemsetAsync(step_ctr_, 0, sizeof(int), stream_));
+    prof_ = &recs;
+    launches_ = 0;
+    CK(cudaEventRecord(a, stream_));
+    try {
+        enqueue_step(cur_R_);
+    } catch (...) {
+        prof_ = nullptr;
+        throw;
+    }
+    CK(cudaEventRecord(b, stream_));
+    prof_ = nullptr;
+    CK(cudaStreamSynchronize(stream_));
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, a, b));
+    double gms = 0.0, bytes = 0.0;
+    for (auto & r : recs) {
+        float t = 0.0f;
+        CK(cudaEventElapsedTime(&t, r.a, r.b));
+        gms += t;
+        bytes += r.bytes;
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    out[0] = ms;
+    out[1] = gms;
+    out[2] = (double) recs.size();
+    out[3] = bytes;
+    out[4] = (double) launches_;
+}
+
+size_t Engine::weight_bytes_per_step() const {
+    // algorithmic weight bytes of one frame step at Q8_0 (34 bytes per 32 weights): backbone
+    // + lm_head once, depth in_proj + layers + one head per sub-step
+    auto qbytes = [](const QMat & q) { return (size_t) q.M * q.K / 32 * 34; };
+    size_t bb = qbytes(lm_head_);
+    for (const LayerW & w : bb_) bb += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
+    size_t dd = qbytes(dd_in_) + qbytes(dd_head_[0]);
+    for (const LayerW & w : dd_) dd += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
+    return bb + (size_t) (cfg.nc - 1) * dd;
+}
+
+size_t Engine::kv_bytes_per_position() const {
+    return (size_t) cfg.bb.n_layer * 2 * cfg.bb.n_kv * cfg.bb.hd * sizeof(half);
+}
+
+}  // namespace bzb

@@ -1,0 +1,162 @@
+// The B200 generator engine: device-resident weights, a paged KV cache shared by all
+// sessions, device-resident session state and one CUDA-graph frame step per batch bucket.
+#pragma once
+
+#include "host.h"
+#include "kernels.cuh"
+
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace bzb {
+
+struct LayerW {
+    QMat qkv, o, gu, down;
+    float * attn_norm = nullptr, * ffn_norm = nullptr, * q_norm = nullptr, * k_norm = nullptr;
+    float * post_attn = nullptr, * post_ffn = nullptr;
+};
+
+struct SlotHost {
+    int sid = -1;
+    bool active = false;
+    int max_tokens = 0;
+    int alloc = 0;
+    std::vector<int> pages;
+};
+
+struct StepResult {
+    int steps_executed = 0;
+    int still_active = 0;
+};
+
+class Engine {
+public:
+    Engine(const std::string & gguf_path, int device);
+    ~Engine();
+
+    ModelConfig cfg;
+    int device = 0;
+
+    // session life cycle (reference: src/c_api.cpp:325-457, 521-530, 580-582)
+    void session_create(int sid, const std::string & text, const char * instruction, const char * ref_text,
+                        const int * ref_codes, int ref_frames, float cfg_scale, uint32_t seed, int max_new_tokens,
+                        int * out_cb0, int * out_alloc);
+    void session_create_tokens(int sid, const std::vector<std::vector<int>> & text_segments,
+                               const int * ref_codes, int ref_frames, uint32_t seed, int max_tokens,
+                               int * out_cb0, int * out_alloc);
+    bool session_free(int sid);
+    int session_count() const { return (int) sid_to_slot_.size(); }
+    bool session_active(int sid) const;
+    bool session_exists(int sid) const { return sid_to_slot_.count(sid) > 0; }
+
+    // K frame steps over a session list (reference: src/c_api.cpp:601-949). frames_out is
+    // [K][n][width]; rows of sessions not stepped keep their initial contents.
+    StepResult step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
+                    int width, int * next_out, bool fill_inactive);
+
+    // device-resident run of K steps for the current batch (no host copies): timing entry
+    void step_device_only(int K);
+    void sync();
+    cudaStream_t stream() const { return stream_; }
+
+    // debug accessors for parity tests
+    void debug_hidden(int sid, float * out);
+    void debug_depth(int n, const float * hidden, const int * cb0, const int * forced, int * codes_out,
+                     float * logits_out);
+    void debug_gemv(const char * tensor, int sub, int rows, const float * x, float * y);
+    // one eager frame step of the current batch with CUDA events around every dequant-GEMM:
+    // out = {step_ms, gemm_ms, gemm_launches, gemm_algorithmic_bytes, launches}
+    void profile_step(double * out);
+    size_t weight_bytes_per_step() const;
+    size_t kv_bytes_per_position() const;
+
+    int max_rows() const { return rmax_; }
+    int launches_per_step() const { return graph_nodes_; }
+    int nc() const { return cfg.nc; }
+
+private:
+    // loading
+    QMat load_qmat(const std::vector<const GgufTensor *> & parts, bool interleave_pairs, int row0 = 0, int rows = -1);
+    QRows load_qrows(const GgufTensor * t);
+    float * load_f32(const std::string & name, int expect);
+    const GgufTensor * need(const std::string & name);
+    void alloc_buffers();
+    void build_rope_tables();
+
+    // execution
+    void gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out);
+    void enqueue_step(int R);
+    void depth_layer(int l, int rows, int R, int n_new, int start);
+    void bb_decode_layer(int l, int R);
+    void te_forward(const std::vector<int> & tokens, float * out_rows);
+    void bb_prefill(int slot, int T);
+    void ensure_prefill_capacity(int T);
+    cudaGraphExec_t graph_for(int R);
+    int acquire_slot(int sid, int n_pages);
+    void release_slot(int slot);
+
+    GgufFile gg_;
+    Tokenizer tok_;
+    cudaStream_t stream_ = nullptr;
+    std::vector<void *> allocs_;
+    template <class T> T * dalloc(size_t n);
+
+    // weights
+    std::vector<LayerW> bb_, dd_, te_;
+    QMat lm_head_, dd_in_, te_proj_;
+    std::vector<QMat> dd_head_;
+    QRows audio_embd_, te_embd_;
+    float * bb_out_norm_ = nullptr, * dd_out_norm_ = nullptr, * te_out_norm_ = nullptr;
+    float2 * rope_bb_ = nullptr, * rope_dd_ = nullptr, * rope_te_full_ = nullptr, * rope_te_slide_ = nullptr;
+    int rope_bb_max_ = 0, rope_te_max_ = 0;
+    int vbb_ = 0;  // lm_head rows
+    bool has_te_ = false;
+
+    // KV pool and sessions
+    half * kv_pool_ = nullptr;
+    int n_pages_ = 0, max_pages_ = 0, max_slots_ = 0;
+    std::vector<int> free_pages_;
+    int * page_table_ = nullptr;
+    SessState * st_ = nullptr;
+    uint16_t * hist_ = nullptr;
+    int hist_ld_ = 0;
+    float * hid32_ = nullptr;
+    std::vector<SlotHost> slots_;
+    std::vector<int> free_slots_;
+    std::unordered_map<int, int> sid_to_slot_;
+
+    // step buffers
+    int rmax_ = 0, kmax_ = 0;
+    int * row_slot_ = nullptr, * row_active_ = nullptr, * next_ = nullptr, * cur_frames_ = nullptr;
+    int * frames_all_ = nullptr, * step_ctr_ = nullptr, * any_active_ = nullptr, * slot_scalar_ = nullptr;
+    uint32_t * seeds_ = nullptr;
+    half * din16_ = nullptr, * dh16_ = nullptr, * dff16_ = nullptr, * datt16_ = nullptr;
+    float * dx_ = nullptr, * dqkv_ = nullptr, * dkv_ = nullptr, * dlog_ = nullptr;
+    half * bh16_ = nullptr, * bff16_ = nullptr, * batt16_ = nullptr;
+    float * bx_ = nullptr, * bqkv_ = nullptr, * blog_ = nullptr;
+    GemvScratch scr_;
+    bool seeds_enabled_ = false;
+    int cur_R_ = 0;
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs_;
+    std::map<std::pair<int, int>, cudaGraph_t> graph_defs_;
+
+    // prefill buffers (grown on demand)
+    int tmax_ = 0;
+    float * px_ = nullptr, * pqkv_ = nullptr, * plog_ = nullptr, * tx_ = nullptr, * tqkv_ = nullptr;
+    float * ttmp_ = nullptr, * tk_ = nullptr, * tv_ = nullptr;
+    half * ph16_ = nullptr, * pff16_ = nullptr, * patt16_ = nullptr, * th16_ = nullptr, * tff16_ = nullptr,
+         * tatt16_ = nullptr;
+    int * ptok_ = nullptr, * pframes_ = nullptr;
+    std::vector<void *> prefill_allocs_;
+
+    // profiling of one eager step
+    struct ProfRec { cudaEvent_t a, b; double bytes; };
+    std::vector<ProfRec> * prof_ = nullptr;
+    int launches_ = 0;
+    int graph_nodes_ = 0;
+};
+
+}  // namespace bzb

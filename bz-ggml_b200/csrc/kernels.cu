@@ -1,0 +1,983 @@
+// CUDA kernels of the B200 decode engine (sm_100a).
+//
+// Weight contractions are dequant-GEMMs over Q8_0 weights repacked once at load into the
+// mma.m16n8k16 A-fragment order, so each lane streams its weights with one 128-bit load per
+// 16x32 tile and dequantises them in registers; the (few) activation rows are staged once
+// per CTA in shared memory in B-fragment order. Split-K partials are reduced in a fixed order
+// by the last CTA of each output tile, so results do not depend on scheduling.
+#include "kernels.cuh"
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <stdexcept>
+#include <string>
+
+namespace bzb {
+
+#define BZB_CUDA_CHECK(x)                                                                     \
+    do {                                                                                      \
+        cudaError_t e_ = (x);                                                                 \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA: ") + cudaGetErrorString(e_) + " at " #x); \
+    } while (0)
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ uint4 ld_stream(const uint4 * p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void mma16816(float * c, const uint32_t * a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// four int8 (rows g, g, g+8, g+8) -> two half2 scaled by their rows' Q8_0 scales. 0x64XX as
+// f16 is 1024 + XX, so flipping the sign bit and subtracting 1152 recovers the int8 exactly.
+__device__ __forceinline__ void dq_word(uint32_t w, half2 s_g, half2 s_g8, uint32_t & lo, uint32_t & hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    uint32_t l = __byte_perm(u, 0x64646464u, 0x5140u);
+    uint32_t h = __byte_perm(u, 0x64646464u, 0x7362u);
+    const half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    half2 hl = __hmul2(__hsub2(*reinterpret_cast<half2 *>(&l), bias), s_g);
+    half2 hh = __hmul2(__hsub2(*reinterpret_cast<half2 *>(&h), bias), s_g8);
+    lo = *reinterpret_cast<uint32_t *>(&hl);
+    hi = *reinterpret_cast<uint32_t *>(&hh);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    const float c = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(c * x * (1.0f + 0.044715f * x * x)));
+}
+
+// ------------------------------------------------------------------------------------ GEMM
+struct GemvParams {
+    const uint4 * qs;
+    const half2 * ds;
+    int MT, M, KB, kc, splits, MG;
+    const half * x;
+    int ldx, rows;
+    GemvOut out;
+    float4 * ws;
+    int * counters;
+};
+
+constexpr int kGemvThreads = 256;
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
+    extern __shared__ uint4 smem_b[];  // [kc][NT][32]
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mg = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
+    const int kb0 = split * p.kc;
+    const int nkb = min(p.KB, kb0 + p.kc) - kb0;
+    const int mt = mg * 8 + warp;
+    const bool mt_ok = mt < p.MT;
+    const int row0 = chunk * 64;
+    const uint4 * wq = p.qs + ((size_t) mt * p.KB + kb0) * 32 + lane;
+    const half2 * wd = p.ds + ((size_t) mt * p.KB + kb0) * 8 + (lane >> 2);
+
+    uint4 a[8];
+    half2 sc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        if (mt_ok && i < nkb) {
+            a[i] = ld_stream(wq + (size_t) i * 32);
+            sc[i] = wd[(size_t) i * 8];
+        }
+    }
+
+    // stage this CTA's activation rows x[row0 .. row0+8NT) x [kb0*32, (kb0+nkb)*32) in B order
+    const int cpr = nkb * 4;  // 16-byte chunks per row
+    const int total = NT * 8 * cpr;
+    for (int idx = threadIdx.x; idx < total; idx += kGemvThreads) {
+        const int n = idx / cpr, c = idx - n * cpr;
+        const int gr = row0 + n;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (gr < p.rows) v = *reinterpret_cast<const uint4 *>(p.x + (size_t) gr * p.ldx + (size_t) kb0 * 32 + c * 8);
+        const int kb = c >> 2, wsel = c & 3, nt = n >> 3, g = n & 7;
+        uint32_t * base = reinterpret_cast<uint32_t *>(smem_b + (size_t) (kb * NT + nt) * 32);
+        base[(g * 4 + 0) * 4 + wsel] = v.x;
+        base[(g * 4 + 1) * 4 + wsel] = v.y;
+        base[(g * 4 + 2) * 4 + wsel] = v.z;
+        base[(g * 4 + 3) * 4 + wsel] = v.w;
+    }
+    __syncthreads();
+
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+
+    if (mt_ok) {
+        for (int base = 0; base < nkb; base += 8) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int kb = base + i;
+                if (kb < nkb) {
+                    uint32_t A[8];
+                    const half2 sg = __low2half2(sc[i]), sg8 = __high2half2(sc[i]);
+                    dq_word(a[i].x, sg, sg8, A[0], A[1]);
+                    dq_word(a[i].y, sg, sg8, A[2], A[3]);
+                    dq_word(a[i].z, sg, sg8, A[4], A[5]);
+                    dq_word(a[i].w, sg, sg8, A[6], A[7]);
+                    if (kb + 8 < nkb) {
+                        a[i] = ld_stream(wq + (size_t) (kb + 8) * 32);
+                        sc[i] = wd[(size_t) (kb + 8) * 8];
+                    }
+                    const uint4 * bp = smem_b + (size_t) kb * NT * 32 + lane;
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        const uint4 b = bp[nt * 32];
+                        mma16816(acc[nt], A, b.x, b.y);
+                        mma16816(acc[nt], A + 4, b.z, b.w);
+                    }
+                }
+            }
+        }
+    }
+
+    if (p.splits > 1) {
+        if (mt_ok) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+                p.ws[(((size_t) (chunk * p.splits + split) * p.MT + mt) * NT + nt) * 32 + lane] =
+                    make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[chunk * p.MG + mg], 1) == p.splits - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        if (mt_ok) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int sp = 0; sp < p.splits; sp++) {
+                    const float4 v = __ldcg(&p.ws[(((size_t) (chunk * p.splits + sp) * p.MT + mt) * NT + nt) * 32 + lane]);
+                    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+                }
+                acc[nt][0] = s.x; acc[nt][1] = s.y; acc[nt][2] = s.z; acc[nt][3] = s.w;
+            }
+        }
+        if (threadIdx.x == 0) p.counters[chunk * p.MG + mg] = 0;
+    }
+    if (!mt_ok) return;
+
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        const int n0 = row0 + nt * 8 + 2 * t;
+        if (EPI == EPI_STORE || EPI == EPI_RESID) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int m = mt * 16 + g + (e >= 2 ? 8 : 0);
+                const int n = n0 + (e & 1);
+                if (m < p.M && n < p.rows) {
+                    float * dst = p.out.f32 + (size_t) n * p.out.ld + m;
+                    if (EPI == EPI_RESID) *dst += acc[nt][e];
+                    else *dst = acc[nt][e];
+                }
+            }
+        } else {
+            const int j = mt * 8 + g;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int n = n0 + e;
+                if (n < p.rows && j < (p.M >> 1)) {
+                    const float gate = acc[nt][e], up = acc[nt][2 + e];
+                    const float act = EPI == EPI_SWIGLU ? silu_f(gate) : gelu_tanh_f(gate);
+                    p.out.f16[(size_t) n * p.out.ld + j] = __float2half_rn(act * up);
+                }
+            }
+        }
+    }
+}
+
+template <int NT>
+void launch_gemv_nt(const GemvParams & p, dim3 grid, size_t smem, cudaStream_t s) {
+    switch (p.out.kind) {
+        case EPI_STORE: gemv_kernel<NT, EPI_STORE><<<grid, kGemvThreads, smem, s>>>(p); break;
+        case EPI_RESID: gemv_kernel<NT, EPI_RESID><<<grid, kGemvThreads, smem, s>>>(p); break;
+        case EPI_SWIGLU: gemv_kernel<NT, EPI_SWIGLU><<<grid, kGemvThreads, smem, s>>>(p); break;
+        default: gemv_kernel<NT, EPI_GEGLU><<<grid, kGemvThreads, smem, s>>>(p); break;
+    }
+}
+
+template <int NT>
+void set_gemv_attr() {
+    const int mx = 200 * 1024;
+    cudaFuncSetAttribute(gemv_kernel<NT, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(gemv_kernel<NT, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(gemv_kernel<NT, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(gemv_kernel<NT, EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+}
+
+// ------------------------------------------------------------------------------------ repack
+__global__ void repack_q8_kernel(const uint8_t * raw, int M, int KB, uint4 * qs, half2 * ds) {
+    const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int MT = (M + 15) / 16;
+    if (warp_global >= MT * KB) return;
+    const int mt = warp_global / KB, kb = warp_global % KB;
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = mt * 16 + g, r1 = r0 + 8;
+    auto q_at = [&](int r, int k) -> uint32_t {
+        if (r >= M) return 0u;
+        return raw[((size_t) r * KB + kb) * 34 + 2 + k];
+    };
+    uint32_t w[4];
+    for (int hlf = 0; hlf < 2; hlf++) {
+        const int k0 = hlf * 16 + 2 * t;
+        w[hlf * 2 + 0] = q_at(r0, k0) | (q_at(r0, k0 + 1) << 8) | (q_at(r1, k0) << 16) | (q_at(r1, k0 + 1) << 24);
+        w[hlf * 2 + 1] = q_at(r0, k0 + 8) | (q_at(r0, k0 + 9) << 8) | (q_at(r1, k0 + 8) << 16) | (q_at(r1, k0 + 9) << 24);
+    }
+    qs[((size_t) mt * KB + kb) * 32 + lane] = make_uint4(w[0], w[1], w[2], w[3]);
+    if (lane < 8) {
+        auto d_at = [&](int r) -> unsigned short {
+            if (r >= M) return 0;
+            const uint8_t * b = raw + ((size_t) r * KB + kb) * 34;
+            return (unsigned short) (b[0] | (b[1] << 8));
+        };
+        ds[((size_t) mt * KB + kb) * 8 + lane] = __halves2half2(__ushort_as_half(d_at(mt * 16 + lane)),
+                                                               __ushort_as_half(d_at(mt * 16 + lane + 8)));
+    }
+}
+
+__global__ void split_q8_rows_kernel(const uint8_t * raw, long long n_blocks, int8_t * qs, half * ds) {
+    const long long b = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_blocks) return;
+    const uint8_t * src = raw + b * 34;
+    ds[b] = __ushort_as_half((unsigned short) (src[0] | (src[1] << 8)));
+    for (int j = 0; j < 32; j++) qs[b * 32 + j] = (int8_t) src[2 + j];
+}
+
+// ------------------------------------------------------------------------------------ norms
+__device__ float block_sum(float v, float * red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = 0; i < nw; i++) s += red[i];
+    return s;
+}
+
+__global__ void rmsnorm_kernel(const float * x, int ldx, const float * w, int D, float eps, half * o16, int ld16,
+                               float * o32, int ld32, int r0, const int * row_map) {
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    const float * xr = x + (size_t) (r0 + i) * ldx;
+    float ss = 0.0f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) ss += xr[d] * xr[d];
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float) D + eps);
+    const int orow = row_map ? row_map[i] : i;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float y = (xr[d] * scale) * w[d];
+        if (o16) o16[(size_t) i * ld16 + d] = __float2half_rn(y);
+        if (o32 && orow >= 0) o32[(size_t) orow * ld32 + d] = y;
+    }
+}
+
+__global__ void norm_add_kernel(float * x, const float * t, int D, const float * w, float eps) {
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    const float * tr = t + (size_t) r * D;
+    float ss = 0.0f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) ss += tr[d] * tr[d];
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float) D + eps);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) x[(size_t) r * D + d] += (tr[d] * scale) * w[d];
+}
+
+// ------------------------------------------------------------------------------------ embeddings
+__global__ void embed_rows_kernel(QRows e, const int * idx, float scale, float * o32, half * o16, int ld) {
+    const int r = blockIdx.x;
+    int row = idx[r];
+    row = (row < 0 || row >= e.rows) ? 0 : row;
+    const int8_t * q = e.qs + (size_t) row * e.K;
+    const half * d = e.ds + (size_t) row * (e.K / 32);
+    for (int k = threadIdx.x; k < e.K; k += blockDim.x) {
+        const float v = ((float) q[k] * __half2float(d[k >> 5])) * scale;
+        if (o32) o32[(size_t) r * ld + k] = v;
+        if (o16) o16[(size_t) r * ld + k] = __float2half_rn(v);
+    }
+}
+
+__global__ void audio_embed_kernel(QRows e, const int * frames, int ldf, int nc, int vs, float * out,
+                                   const int * row_active) {
+    const int r = blockIdx.x;
+    const bool act = row_active ? row_active[r] != 0 : true;
+    for (int k = threadIdx.x; k < e.K; k += blockDim.x) {
+        float acc = 0.0f;
+        if (act) {
+            for (int cb = 0; cb < nc; cb++) {
+                int code = frames[(size_t) r * ldf + cb];
+                code = (code < 0 || code >= vs) ? 0 : code;
+                const size_t row = (size_t) cb * vs + code;
+                acc += (float) e.qs[row * e.K + k] * __half2float(e.ds[row * (e.K / 32) + (k >> 5)]);
+            }
+        }
+        out[(size_t) r * e.K + k] = acc;
+    }
+}
+
+// ------------------------------------------------------------------------------------ attention
+template <int HD>
+__device__ __forceinline__ void rope_apply(float (&x)[HD / 32], const float2 * cs, int lane) {
+    constexpr int E = HD / 32;
+#pragma unroll
+    for (int j = 0; j < E / 2; j++) {
+        const float2 c = cs[lane + 32 * j];
+        const float x0 = x[j], x1 = x[j + E / 2];
+        x[j] = x0 * c.x - x1 * c.y;
+        x[j + E / 2] = x0 * c.y + x1 * c.x;
+    }
+}
+
+template <int HD>
+__device__ __forceinline__ void head_rmsnorm(float (&x)[HD / 32], const float * w, float eps, int lane) {
+    constexpr int E = HD / 32;
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; e++) ss += x[e] * x[e];
+    ss = warp_sum(ss);
+    const float scale = 1.0f / sqrtf(ss / (float) HD + eps);
+#pragma unroll
+    for (int e = 0; e < E; e++) x[e] = (x[e] * scale) * w[lane + 32 * e];
+}
+
+__device__ __forceinline__ size_t paged_off(const AttnKV & kv, const int * page_row, int p, int kvsel, int h,
+                                            int n_kv, int HD) {
+    const int page = page_row[p >> 4];
+    return ((((size_t) page * kv.n_layer + kv.layer) * 2 + kvsel) * n_kv + h) * 16 * HD + (size_t) (p & 15) * HD;
+}
+
+template <int HD>
+struct DecodeSmem {
+    float k[32][HD + 1];
+    float v[32][HD + 1];
+    float q[8][2][HD];
+};
+
+template <int HD, bool PAGED>
+__global__ void attn_decode_kernel(const AttnDecodeArgs a) {
+    constexpr int E = HD / 32;
+    __shared__ DecodeSmem<HD> sm;
+    const int b = blockIdx.x, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = blockDim.x >> 5;
+    const int slot = a.row_slot ? a.row_slot[b] : b;
+    const bool act = (a.row_active ? a.row_active[b] != 0 : true) && slot >= 0;
+    const int n_new = a.n_new;
+    const int qh = h * G + warp;
+    if (!act) {
+        for (int i = 0; i < n_new; i++)
+            for (int e = 0; e < E; e++)
+                a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(0.0f);
+        return;
+    }
+    const int start = a.st ? a.st[slot].pos : a.start;
+    const int L = start + n_new;
+    const int * page_row = PAGED ? a.kv.page_table + (size_t) slot * a.kv.max_pages : nullptr;
+
+    // 1. normalise, rotate and append the new tokens' keys and values
+    for (int task = warp; task < 2 * n_new; task += G) {
+        const int i = task >> 1;
+        const int isv = task & 1;
+        const int row = b + i * a.R;
+        const float * src = a.qkv + (size_t) row * a.ldq + a.n_head * HD + isv * a.n_kv * HD + h * HD;
+        float x[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
+        if (!isv) {
+            if (a.k_norm) head_rmsnorm<HD>(x, a.k_norm, a.eps, lane);
+            rope_apply<HD>(x, a.rope + (size_t) (start + i) * (HD / 2), lane);
+        }
+        const int p = start + i;
+        if (PAGED) {
+            half * dst = a.kv.pool + paged_off(a.kv, page_row, p, isv, h, a.n_kv, HD);
+#pragma unroll
+            for (int e = 0; e < E; e++) dst[lane + 32 * e] = __float2half_rn(x[e]);
+        } else {
+            float * dst = a.kv.flat + (((size_t) b * a.kv.cap + p) * 2 + isv) * a.n_kv * HD + (size_t) h * HD;
+#pragma unroll
+            for (int e = 0; e < E; e++) dst[lane + 32 * e] = x[e];
+        }
+    }
+    // 2. this warp's query head for each new token
+    for (int i = 0; i < n_new; i++) {
+        const float * src = a.qkv + (size_t) (b + i * a.R) * a.ldq + qh * HD;
+        float x[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
+        if (a.q_norm) head_rmsnorm<HD>(x, a.q_norm, a.eps, lane);
+        rope_apply<HD>(x, a.rope + (size_t) (start + i) * (HD / 2), lane);
+#pragma unroll
+        for (int e = 0; e < E; e++) sm.q[warp][i][lane + 32 * e] = x[e];
+    }
+    float m[2] = { -INFINITY, -INFINITY }, l[2] = { 0.0f, 0.0f };
+    float acc[2][E];
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int e = 0; e < E; e++) acc[i][e] = 0.0f;
+
+    for (int t0 = 0; t0 < L; t0 += 32) {
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < 32 * HD; idx += blockDim.x) {
+            const int j = idx / HD, d = idx - (idx / HD) * HD;
+            const int p = t0 + j;
+            float kv_k = 0.0f, kv_v = 0.0f;
+            if (p < L) {
+                if (PAGED) {
+                    kv_k = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 0, h, a.n_kv, HD) + d]);
+                    kv_v = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 1, h, a.n_kv, HD) + d]);
+                } else {
+                    const float * base = a.kv.flat + ((size_t) b * a.kv.cap + p) * 2 * a.n_kv * HD + (size_t) h * HD + d;
+                    kv_k = base[0];
+                    kv_v = base[(size_t) a.n_kv * HD];
+                }
+            }
+            sm.k[j][d] = kv_k;
+            sm.v[j][d] = kv_v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            if (i >= n_new) break;
+            const int lim = start + i + 1;
+            const int p = t0 + lane;
+            float sc = -INFINITY;
+            if (p < lim) {
+                float dot = 0.0f;
+#pragma unroll 16
+                for (int d = 0; d < HD; d++) dot += sm.q[warp][i][d] * sm.k[lane][d];
+                sc = dot * a.scale;
+            }
+            const float tmax = warp_max(sc);
+            if (tmax == -INFINITY) continue;
+            const float mn = fmaxf(m[i], tmax);
+            const float corr = expf(m[i] - mn);
+            const float pr = p < lim ? expf(sc - mn) : 0.0f;
+            l[i] = l[i] * corr + warp_sum(pr);
+#pragma unroll
+            for (int e = 0; e < E; e++) acc[i][e] *= corr;
+            const int jmax = min(32, lim - t0);
+            for (int j = 0; j < jmax; j++) {
+                const float pj = __shfl_sync(0xffffffffu, pr, j);
+#pragma unroll
+                for (int e = 0; e < E; e++) acc[i][e] += pj * sm.v[j][lane + 32 * e];
+            }
+            m[i] = mn;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        if (i >= n_new) break;
+        const float inv = 1.0f / l[i];
+#pragma unroll
+        for (int e = 0; e < E; e++)
+            a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
+    }
+}
+
+// prefill: normalise/rotate q in place, k likewise, and write k,v to the cache or flat buffers
+template <int HD, bool PAGED>
+__global__ void qk_prep_kernel(const PrefillArgs a) {
+    constexpr int E = HD / 32;
+    const int r = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int p = a.start + r;
+    float * row = a.qkv + (size_t) r * a.ldq;
+    const int tasks = a.n_head + 2 * a.n_kv;
+    for (int task = warp; task < tasks; task += nw) {
+        float x[E];
+        float * src;
+        int kind, h;
+        if (task < a.n_head) { kind = 0; h = task; src = row + h * HD; }
+        else if (task < a.n_head + a.n_kv) { kind = 1; h = task - a.n_head; src = row + (a.n_head + h) * HD; }
+        else { kind = 2; h = task - a.n_head - a.n_kv; src = row + (a.n_head + a.n_kv + h) * HD; }
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
+        if (kind == 0 && a.q_norm) head_rmsnorm<HD>(x, a.q_norm, a.eps, lane);
+        if (kind == 1 && a.k_norm) head_rmsnorm<HD>(x, a.k_norm, a.eps, lane);
+        if (kind < 2) rope_apply<HD>(x, a.rope + (size_t) p * (HD / 2), lane);
+        if (kind == 0) {
+#pragma unroll
+            for (int e = 0; e < E; e++) src[lane + 32 * e] = x[e];
+        } else if (PAGED) {
+            half * dst = a.kv.pool + paged_off(a.kv, a.page_row, p, kind - 1, h, a.n_kv, HD);
+#pragma unroll
+            for (int e = 0; e < E; e++) dst[lane + 32 * e] = __float2half_rn(x[e]);
+        } else {
+            float * dst = (kind == 1 ? a.flat_k : a.flat_v) + ((size_t) r * a.n_kv + h) * HD;
+#pragma unroll
+            for (int e = 0; e < E; e++) dst[lane + 32 * e] = x[e];
+        }
+    }
+}
+
+constexpr int kPrefillQB = 8;
+
+template <int HD, bool PAGED>
+__global__ void attn_prefill_kernel(const PrefillArgs a) {
+    constexpr int E = HD / 32;
+    constexpr int QB = kPrefillQB;
+    extern __shared__ float psm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = blockDim.x >> 5;
+    float * sk = psm;                         // [32][HD+1]
+    float * sv = sk + 32 * (HD + 1);          // [32][HD+1]
+    float * sq = sv + 32 * (HD + 1);          // [G][QB][HD]
+    const int r0 = blockIdx.x * QB, h = blockIdx.y;
+    const int qh = h * G + warp;
+    const int nq = min(QB, a.T - r0);
+    const int left = (a.window + 1) / 2, right = a.window / 2 + 1;
+    int lo[QB], hi[QB];
+    int lo_min = INT_MAX, hi_max = 0;
+    for (int i = 0; i < QB; i++) {
+        const int r = r0 + i;
+        if (i >= nq) { lo[i] = 0; hi[i] = 0; continue; }
+        if (a.causal) { lo[i] = 0; hi[i] = a.start + r + 1; }
+        else if (a.window > 0) { lo[i] = max(0, r - left + 1); hi[i] = min(a.T, r + right); }
+        else { lo[i] = 0; hi[i] = a.T; }
+        lo_min = min(lo_min, lo[i]);
+        hi_max = max(hi_max, hi[i]);
+    }
+    for (int i = 0; i < nq; i++) {
+        const float * src = a.qkv + (size_t) (r0 + i) * a.ldq + qh * HD;
+        for (int e = 0; e < E; e++) sq[((size_t) warp * QB + i) * HD + lane + 32 * e] = src[lane + 32 * e];
+    }
+    float m[QB], l[QB], acc[QB][E];
+#pragma unroll
+    for (int i = 0; i < QB; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) acc[i][e] = 0.0f;
+    }
+    const int t_begin = (lo_min / 32) * 32;
+    for (int t0 = t_begin; t0 < hi_max; t0 += 32) {
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < 32 * HD; idx += blockDim.x) {
+            const int j = idx / HD, d = idx - (idx / HD) * HD;
+            const int p = t0 + j;
+            float vk = 0.0f, vv = 0.0f;
+            if (p < hi_max) {
+                if (PAGED) {
+                    vk = __half2float(a.kv.pool[paged_off(a.kv, a.page_row, p, 0, h, a.n_kv, HD) + d]);
+                    vv = __half2float(a.kv.pool[paged_off(a.kv, a.page_row, p, 1, h, a.n_kv, HD) + d]);
+                } else {
+                    vk = a.flat_k[((size_t) p * a.n_kv + h) * HD + d];
+                    vv = a.flat_v[((size_t) p * a.n_kv + h) * HD + d];
+                }
+            }
+            sk[j * (HD + 1) + d] = vk;
+            sv[j * (HD + 1) + d] = vv;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < QB; i++) {
+            if (i >= nq) continue;
+            const int p = t0 + lane;
+            const bool ok = p >= lo[i] && p < hi[i];
+            float sc = -INFINITY;
+            if (ok) {
+                float dot = 0.0f;
+                const float * q = sq + ((size_t) warp * QB + i) * HD;
+#pragma unroll 16
+                for (int d = 0; d < HD; d++) dot += q[d] * sk[lane * (HD + 1) + d];
+                sc = dot * a.scale;
+            }
+            const float tmax = warp_max(sc);
+            if (tmax == -INFINITY) continue;
+            const float mn = fmaxf(m[i], tmax);
+            const float corr = expf(m[i] - mn);
+            const float pr = ok ? expf(sc - mn) : 0.0f;
+            l[i] = l[i] * corr + warp_sum(pr);
+#pragma unroll
+            for (int e = 0; e < E; e++) acc[i][e] *= corr;
+            for (int j = 0; j < 32; j++) {
+                const float pj = __shfl_sync(0xffffffffu, pr, j);
+                if (pj != 0.0f) {
+#pragma unroll
+                    for (int e = 0; e < E; e++) acc[i][e] += pj * sv[j * (HD + 1) + lane + 32 * e];
+                }
+            }
+            m[i] = mn;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < QB; i++) {
+        if (i >= nq) continue;
+        const float inv = l[i] > 0.0f ? 1.0f / l[i] : 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++)
+            a.out[(size_t) (r0 + i) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
+    }
+}
+
+// ------------------------------------------------------------------------------------ step glue
+__global__ void step_init_kernel(const StepArgs a) {
+    const int r = blockIdx.x;
+    const int slot = a.row_slot[r];
+    const bool act = slot >= 0 && a.st[slot].active != 0;
+    const int k = *a.step_ctr;
+    if (threadIdx.x == 0) {
+        a.row_active[r] = act ? 1 : 0;
+        a.frames[(size_t) r * a.nc] = act ? a.st[slot].last_cb0 : -1;
+        if (act) atomicOr(&a.any_active[k], 1);
+    }
+    const int cb0 = act ? a.st[slot].last_cb0 : 0;
+    const int row = (cb0 < 0 || cb0 >= a.embd.rows) ? 0 : cb0;
+    for (int d = threadIdx.x; d < a.H; d += blockDim.x) {
+        half h0 = __float2half_rn(0.0f), h1 = __float2half_rn(0.0f);
+        if (act) {
+            h0 = __float2half_rn(a.hid32[(size_t) slot * a.H + d]);
+            const float e = (float) a.embd.qs[(size_t) row * a.embd.K + d] * __half2float(a.embd.ds[(size_t) row * (a.embd.K / 32) + (d >> 5)]);
+            h1 = __float2half_rn(e);
+        }
+        a.din16[(size_t) r * a.H + d] = h0;
+        a.din16[(size_t) (a.R + r) * a.H + d] = h1;
+    }
+}
+
+__global__ void argmax_gather_kernel(const StepArgs a, const float * logits, int ld, int V, int col, int gather_cb) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int s_code;
+    const int r = blockIdx.x;
+    if (!a.row_active[r]) {
+        if (threadIdx.x == 0) a.frames[(size_t) r * a.nc + col] = -1;
+        return;
+    }
+    const float * lr = logits + (size_t) r * ld;
+    float best = -INFINITY;
+    int bi = INT_MAX;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = lr[i];
+        if (v > best || (bi == INT_MAX && !(v < best))) { best = v; bi = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = sv[0];
+        int i0 = si[0];
+        for (int w = 1; w < (int) (blockDim.x >> 5); w++)
+            if (sv[w] > b || (sv[w] == b && si[w] < i0)) { b = sv[w]; i0 = si[w]; }
+        if (i0 == INT_MAX) i0 = 0;
+        s_code = i0;
+        a.frames[(size_t) r * a.nc + col] = i0;
+    }
+    __syncthreads();
+    if (gather_cb < 0) return;
+    const size_t row = (size_t) gather_cb * a.vs + s_code;
+    for (int d = threadIdx.x; d < a.H; d += blockDim.x) {
+        const float e = (float) a.embd.qs[row * a.embd.K + d] * __half2float(a.embd.ds[row * (a.embd.K / 32) + (d >> 5)]);
+        a.din16[(size_t) r * a.H + d] = __float2half_rn(e);
+    }
+}
+
+__device__ __forceinline__ unsigned int f2ord(float f) {
+    const unsigned int b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+constexpr int kSortN = 4096;
+
+__global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
+    __shared__ unsigned long long keys[kSortN];
+    __shared__ float lmod[kSortN];
+    const int r = blockIdx.x;
+    const int slot = a.row_slot[r];
+    if (slot < 0) return;
+    if (a.row_active && !a.row_active[r]) return;
+    SessState & s = a.st[slot];
+    if (!s.active) return;
+    const float * lr = a.logits + (size_t) r * a.ld;
+    const uint16_t * hr = a.hist + (size_t) slot * a.hist_ld;
+    for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
+        unsigned long long key = 0ull;
+        if (i < a.V) {
+            float l = lr[i];
+            if (i >= a.sup_lo && i < a.sup_hi) l = -INFINITY;
+            if (a.rep != 1.0f && i < a.hist_ld) {
+                const int c = hr[i];
+                for (int q = 0; q < c; q++) l = l > 0.0f ? l / a.rep : l * a.rep;
+            }
+            lmod[i] = l;
+            key = ((unsigned long long) f2ord(l) << 32) | (unsigned long long) (0xFFFFFFFFu - (unsigned) i);
+        }
+        keys[i] = key;
+    }
+    __syncthreads();
+    // bitonic sort, descending
+    for (int kk = 2; kk <= kSortN; kk <<= 1) {
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long x = keys[i], y = keys[ixj];
+                    const bool desc = (i & kk) == 0;
+                    if (desc ? (x < y) : (x > y)) { keys[i] = y; keys[ixj] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x != 0) return;
+    const int V = a.V;
+    const int keep = (a.top_k > 0 && a.top_k < V) ? a.top_k : V;
+    const float temp = a.temp > 0.0f ? a.temp : 1.0f;
+    auto idx_at = [&](int i) -> int { return (int) (0xFFFFFFFFu - (unsigned) (keys[i] & 0xFFFFFFFFull)); };
+    const float maxl = lmod[idx_at(0)];
+    float sum = 0.0f;
+    for (int i = 0; i < keep; i++) sum += expf((lmod[idx_at(i)] - maxl) / temp);
+    int cut = keep;
+    float total = 1.0f;
+    if (a.top_p < 1.0f) {
+        float cum = 0.0f;
+        for (int i = 0; i < keep; i++) {
+            cum += expf((lmod[idx_at(i)] - maxl) / temp) / sum;
+            if (cum >= a.top_p) { cut = i + 1; break; }
+        }
+        total = 0.0f;
+        for (int i = 0; i < cut; i++) total += expf((lmod[idx_at(i)] - maxl) / temp) / sum;
+    }
+    uint32_t key = s.key, draw = s.draw;
+    if (a.seeds) { key = a.seeds[r] + (uint32_t) (a.step_ctr ? *a.step_ctr : 0); draw = 0; }
+    const uint32_t w = philox_word0(key, draw, 0u);
+    s.key = key;
+    s.draw = draw + 1;
+    const float u = (float) (w >> 8) * (1.0f / 16777216.0f);
+    // cdf over the kept probabilities (renormalised by `total` when top-p cut them)
+    float cdf_last = 0.0f;
+    for (int i = 0; i < cut; i++) {
+        float pi = expf((lmod[idx_at(i)] - maxl) / temp) / sum;
+        if (a.top_p < 1.0f) pi = pi / total;
+        cdf_last += pi;
+    }
+    const float target = u * cdf_last;
+    int pick = idx_at(cut - 1);
+    float cdf = 0.0f;
+    for (int i = 0; i < cut; i++) {
+        float pi = expf((lmod[idx_at(i)] - maxl) / temp) / sum;
+        if (a.top_p < 1.0f) pi = pi / total;
+        cdf += pi;
+        if (target < cdf) { pick = idx_at(i); break; }
+    }
+    uint16_t * hw = a.hist + (size_t) slot * a.hist_ld;
+    if (a.update_hist_first) {
+        if (pick < a.hist_ld) hw[pick] = (uint16_t) min(65535, hw[pick] + 1);
+        s.last_cb0 = pick;
+        a.next_out[r] = pick;
+        return;
+    }
+    s.steps += 1;
+    if (a.advance_pos) s.pos += 1;
+    if (pick == a.eos || s.steps >= s.max_tokens) {
+        s.active = 0;
+        if (a.clamp_on_finish) {
+            s.last_cb0 = -1;
+            s.pos = min(s.pos, s.max_tokens - 1);
+        }
+        a.next_out[r] = -1;
+    } else {
+        if (pick < a.hist_ld) hw[pick] = (uint16_t) min(65535, hw[pick] + 1);
+        s.last_cb0 = pick;
+        a.next_out[r] = pick;
+    }
+}
+
+__global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ctr) {
+    const int k = *ctr;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) all[(size_t) k * n + i] = cur[i];
+    __syncthreads();
+    if (threadIdx.x == 0) *ctr = k + 1;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------ launchers
+void init_kernel_attributes() {
+    set_gemv_attr<1>(); set_gemv_attr<2>(); set_gemv_attr<3>(); set_gemv_attr<4>();
+    set_gemv_attr<5>(); set_gemv_attr<6>(); set_gemv_attr<7>(); set_gemv_attr<8>();
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out,
+                 const GemvScratch & scr, cudaStream_t s) {
+    if (rows <= 0) return;
+    if (ldx % 8 != 0 || w.K % 32 != 0) throw std::runtime_error("gemv: activation stride or K not aligned");
+    const int chunks = (rows + 63) / 64;
+    const int NT = rows >= 64 ? 8 : (rows + 7) / 8;
+    const int MG = (w.MT + 7) / 8;
+    const int target = 2 * 148;
+    int splits = std::max(1, (target + MG * chunks - 1) / (MG * chunks));
+    int kc = (w.KB + splits - 1) / splits;
+    kc = std::max(kc, std::min(4, w.KB));
+    kc = std::min(kc, 16);
+    splits = (w.KB + kc - 1) / kc;
+    while (splits > 1 && (size_t) chunks * splits * w.MT * NT * 32 > scr.ws_elems) {
+        kc *= 2;
+        splits = (w.KB + kc - 1) / kc;
+    }
+    if (splits > 1 && (size_t) chunks * MG > (size_t) scr.n_counters) throw std::runtime_error("gemv: counter scratch too small");
+    if (splits == 1 && kc < w.KB) throw std::runtime_error("gemv: internal tiling error");
+    GemvParams p;
+    p.qs = w.qs; p.ds = w.ds; p.MT = w.MT; p.M = w.M; p.KB = w.KB; p.kc = kc; p.splits = splits; p.MG = MG;
+    p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.ws = scr.ws; p.counters = scr.counters;
+    const size_t smem = (size_t) kc * NT * 32 * sizeof(uint4);
+    if (smem > 200 * 1024) throw std::runtime_error("gemv: shared memory tile too large");
+    dim3 grid(MG, splits, chunks);
+    switch (NT) {
+        case 1: launch_gemv_nt<1>(p, grid, smem, s); break;
+        case 2: launch_gemv_nt<2>(p, grid, smem, s); break;
+        case 3: launch_gemv_nt<3>(p, grid, smem, s); break;
+        case 4: launch_gemv_nt<4>(p, grid, smem, s); break;
+        case 5: launch_gemv_nt<5>(p, grid, smem, s); break;
+        case 6: launch_gemv_nt<6>(p, grid, smem, s); break;
+        case 7: launch_gemv_nt<7>(p, grid, smem, s); break;
+        default: launch_gemv_nt<8>(p, grid, smem, s); break;
+    }
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s) {
+    const int KB = K / 32, MT = (M + 15) / 16;
+    const long long warps = (long long) MT * KB;
+    const int threads = 256;
+    const long long blocks = (warps * 32 + threads - 1) / threads;
+    repack_q8_kernel<<<(unsigned) blocks, threads, 0, s>>>(raw_dev, M, KB, qs, ds);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s) {
+    const long long nb = (long long) rows * (K / 32);
+    split_q8_rows_kernel<<<(unsigned) ((nb + 255) / 256), 256, 0, s>>>(raw_dev, nb, qs, ds);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps, half * out16, int ld16,
+                    float * out32, int ld32, int r0, int n, const int * row_map, cudaStream_t s) {
+    if (n <= 0) return;
+    rmsnorm_kernel<<<n, 256, 0, s>>>(x, ldx, w, D, eps, out16, ld16, out32, ld32, r0, row_map);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_norm_add(float * x, const float * t, int D, const float * w, float eps, int rows, cudaStream_t s) {
+    if (rows <= 0) return;
+    norm_add_kernel<<<rows, 256, 0, s>>>(x, t, D, w, eps);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_embed_rows(const QRows & e, const int * idx, int n, float scale, float * out32, half * out16, int ld,
+                       cudaStream_t s) {
+    if (n <= 0) return;
+    embed_rows_kernel<<<n, 256, 0, s>>>(e, idx, scale, out32, out16, ld);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_audio_embed(const QRows & e, const int * frames, int ld_frames, int nc, int vs, int n, float * out32,
+                        const int * row_active, cudaStream_t s) {
+    if (n <= 0) return;
+    audio_embed_kernel<<<n, 256, 0, s>>>(e, frames, ld_frames, nc, vs, out32, row_active);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s) {
+    const int G = a.n_head / a.n_kv;
+    if (G < 1 || G > 8 || a.n_head % a.n_kv) throw std::runtime_error("attention: unsupported head grouping");
+    if (a.n_new < 1 || a.n_new > 2) throw std::runtime_error("attention: 1 or 2 new tokens per session");
+    dim3 grid(a.R, a.n_kv);
+    const int threads = 32 * G;
+    if (a.hd == 64) {
+        if (paged) attn_decode_kernel<64, true><<<grid, threads, 0, s>>>(a);
+        else attn_decode_kernel<64, false><<<grid, threads, 0, s>>>(a);
+    } else if (a.hd == 128) {
+        if (paged) attn_decode_kernel<128, true><<<grid, threads, 0, s>>>(a);
+        else attn_decode_kernel<128, false><<<grid, threads, 0, s>>>(a);
+    } else throw std::runtime_error("attention: head_dim must be 64 or 128 for decode");
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_qk_prep(const PrefillArgs & a, bool paged, cudaStream_t s) {
+    if (a.T <= 0) return;
+    switch (a.hd) {
+        case 64: if (paged) qk_prep_kernel<64, true><<<a.T, 128, 0, s>>>(a); else qk_prep_kernel<64, false><<<a.T, 128, 0, s>>>(a); break;
+        case 128: if (paged) qk_prep_kernel<128, true><<<a.T, 128, 0, s>>>(a); else qk_prep_kernel<128, false><<<a.T, 128, 0, s>>>(a); break;
+        case 256: if (paged) qk_prep_kernel<256, true><<<a.T, 128, 0, s>>>(a); else qk_prep_kernel<256, false><<<a.T, 128, 0, s>>>(a); break;
+        default: throw std::runtime_error("prefill: head_dim must be 64, 128 or 256");
+    }
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int HD, bool PAGED>
+static void launch_prefill_t(const PrefillArgs & a, int G, cudaStream_t s) {
+    const size_t smem = (size_t) (2 * 32 * (HD + 1) + G * kPrefillQB * HD) * sizeof(float);
+    cudaFuncSetAttribute(attn_prefill_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    dim3 grid((a.T + kPrefillQB - 1) / kPrefillQB, a.n_kv);
+    attn_prefill_kernel<HD, PAGED><<<grid, 32 * G, smem, s>>>(a);
+}
+
+void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s) {
+    if (a.T <= 0) return;
+    const int G = a.n_head / a.n_kv;
+    if (G < 1 || G > 8 || a.n_head % a.n_kv) throw std::runtime_error("prefill attention: unsupported head grouping");
+    switch (a.hd) {
+        case 64: if (paged) launch_prefill_t<64, true>(a, G, s); else launch_prefill_t<64, false>(a, G, s); break;
+        case 128: if (paged) launch_prefill_t<128, true>(a, G, s); else launch_prefill_t<128, false>(a, G, s); break;
+        case 256: if (paged) launch_prefill_t<256, true>(a, G, s); else launch_prefill_t<256, false>(a, G, s); break;
+        default: throw std::runtime_error("prefill attention: head_dim must be 64, 128 or 256");
+    }
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_step_init(const StepArgs & a, cudaStream_t s) {
+    step_init_kernel<<<a.R, 256, 0, s>>>(a);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_argmax_gather(const StepArgs & a, const float * logits, int ld, int V, int col, int gather_cb,
+                          cudaStream_t s) {
+    argmax_gather_kernel<<<a.R, 256, 0, s>>>(a, logits, ld, V, col, gather_cb);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_sample(const SampleArgs & a, cudaStream_t s) {
+    if (a.V > kSortN) throw std::runtime_error("sampler: vocabulary larger than 4096");
+    sample_kernel<<<a.R, 1024, 0, s>>>(a);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s) {
+    frames_commit_kernel<<<1, 256, 0, s>>>(cur, frames_all, n, step_ctr);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace bzb

@@ -1,0 +1,182 @@
+// Device kernels of the B200 decode engine and their host-side launchers.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace bzb {
+
+// Q8_0 weight matrix [M rows, K] repacked for the dequant-GEMM: for each 16-row tile and
+// 32-wide K block, 32 lanes x 16 bytes laid out as the lanes' mma.m16n8k16 A fragments
+// (two k16 halves), plus one half2 (scale of row g, scale of row g+8) per lane group.
+struct QMat {
+    const uint4 * qs = nullptr;    // [MT][KB][32] uint4
+    const half2 * ds = nullptr;    // [MT][KB][8]
+    int M = 0, MT = 0, K = 0, KB = 0;
+};
+
+// Q8_0 rows kept for row gathers (embeddings): int8 values and f16 block scales.
+struct QRows {
+    const int8_t * qs = nullptr;   // [rows][K]
+    const half * ds = nullptr;     // [rows][K/32]
+    int rows = 0, K = 0;
+};
+
+// per-session state resident on the device
+struct SessState {
+    int active;
+    int pos;          // backbone positions already in the KV cache
+    int steps;        // frames generated since creation
+    int max_tokens;
+    int last_cb0;
+    uint32_t key;     // Philox key (the session's current seed)
+    uint32_t draw;    // Philox draw counter under that key
+    int pad;
+};
+
+enum Epilogue { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_GEGLU = 3 };
+
+struct GemvOut {
+    int kind = EPI_STORE;
+    float * f32 = nullptr;   // STORE / RESID target [rows][ld]
+    half * f16 = nullptr;    // SWIGLU / GEGLU target [rows][ld]
+    int ld = 0;
+};
+
+struct GemvScratch {
+    float4 * ws = nullptr;   // split-K partials
+    size_t ws_elems = 0;     // capacity in float4
+    int * counters = nullptr;
+    int n_counters = 0;
+};
+
+// sets the kernels' shared-memory limits; once per device before the first launch or capture
+void init_kernel_attributes();
+
+// y[rows, M] = x16[rows, K] . W^T with the chosen epilogue; rows may exceed 64 (column chunks)
+void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out,
+                 const GemvScratch & scr, cudaStream_t s);
+
+void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s);
+void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s);
+
+// out16[r] = f16(rmsnorm(x[r]) * w) (and out32 when non-null) for rows [r0, r0 + n)
+void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps, half * out16, int ld16,
+                    float * out32, int ld32, int r0, int n, const int * row_map, cudaStream_t s);
+// x[r] += rmsnorm(t[r]) * w  (Gemma post-norms)
+void launch_norm_add(float * x, const float * t, int D, const float * w, float eps, int rows, cudaStream_t s);
+
+// dst[r] = f16/f32 dequantised row idx[r] of an embedding table, scaled
+void launch_embed_rows(const QRows & e, const int * idx, int n, float scale, float * out32, half * out16,
+                       int ld, cudaStream_t s);
+// x[r] = sum over codebooks of audio_embd[frames[r][cb] + cb*vs]
+void launch_audio_embed(const QRows & e, const int * frames, int ld_frames, int nc, int vs, int n,
+                        float * out32, const int * row_active, cudaStream_t s);
+
+struct AttnKV {
+    // paged f16 backbone cache
+    half * pool = nullptr;
+    const int * page_table = nullptr;   // [slot][max_pages]
+    int max_pages = 0, n_layer = 0, layer = 0;
+    // flat f32 cache (depth decoder) [rows][cap][2][n_kv][hd] for this layer
+    float * flat = nullptr;
+    int cap = 0;
+};
+
+struct AttnDecodeArgs {
+    const float * qkv = nullptr;
+    int ldq = 0;
+    int n_head = 0, n_kv = 0, hd = 0;
+    int R = 0;              // sessions (rows per token)
+    int n_new = 1;          // new tokens per session (1 or 2); token i of row b is at b + i*R
+    const int * row_slot = nullptr;   // session slot of each row (paged mode)
+    const int * row_active = nullptr; // 1 when the row is stepped this frame
+    const SessState * st = nullptr;   // start position = st[slot].pos when non-null
+    int start = 0;                    // otherwise this start position
+    const float * q_norm = nullptr, * k_norm = nullptr;
+    float eps = 0;
+    const float2 * rope = nullptr;    // [pos][hd/2] (cos, sin)
+    float scale = 0;
+    AttnKV kv;
+    half * out = nullptr;
+    int ldo = 0;
+};
+void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s);
+
+struct PrefillArgs {
+    float * qkv = nullptr;  // [T][ldq], q normed/roped in place by launch_qk_prep
+    int ldq = 0, T = 0, start = 0;
+    int n_head = 0, n_kv = 0, hd = 0;
+    const float * q_norm = nullptr, * k_norm = nullptr;
+    float eps = 0;
+    const float2 * rope = nullptr;
+    float scale = 0;
+    // paged destination (slot's page row) or flat f32 k/v [T][n_kv][hd]
+    AttnKV kv;
+    const int * page_row = nullptr;
+    float * flat_k = nullptr, * flat_v = nullptr;
+    int window = 0;         // bidirectional window (0 = full) for the text encoder
+    bool causal = true;
+    half * out = nullptr;
+    int ldo = 0;
+};
+void launch_qk_prep(const PrefillArgs & a, bool paged, cudaStream_t s);
+void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s);
+
+struct StepArgs {
+    int R = 0, nc = 0, vs = 0, H = 0;
+    const int * row_slot = nullptr;
+    int * row_active = nullptr;
+    SessState * st = nullptr;
+    const float * hid32 = nullptr;  // [slot][H] last normed backbone hidden
+    QRows embd;
+    half * din16 = nullptr;         // [2R][H]
+    int * frames = nullptr;         // current frame [R][nc]
+    int * step_ctr = nullptr;       // burst step index
+    int * any_active = nullptr;     // [Kmax]
+};
+void launch_step_init(const StepArgs & a, cudaStream_t s);
+// codes[r] = first argmax of logits[r]; frames[..][r][col] = code; when gather_cb >= 0 the
+// next sub-step's input row din16[r] = embedding row (gather_cb*vs + code)
+void launch_argmax_gather(const StepArgs & a, const float * logits, int ld, int V, int col, int gather_cb,
+                          cudaStream_t s);
+
+struct SampleArgs {
+    const float * logits = nullptr;
+    int ld = 0, V = 0, R = 0;
+    const int * row_slot = nullptr;
+    const int * row_active = nullptr;
+    SessState * st = nullptr;
+    uint16_t * hist = nullptr;      // [slot][hist_ld]
+    int hist_ld = 0;
+    int sup_lo = 0, sup_hi = 0, eos = 0;
+    float temp = 0.9f, rep = 1.1f, top_p = 1.0f;
+    int top_k = 50;
+    const uint32_t * seeds = nullptr;   // per-row reseed (key = seeds[r] + step) when non-null
+    const int * step_ctr = nullptr;
+    int * next_out = nullptr;           // [R]
+    int clamp_on_finish = 0;            // burst: last_cb0 = -1 on finish
+    int advance_pos = 1;
+    int update_hist_first = 0;          // prefill: first cb0 is always recorded
+};
+void launch_sample(const SampleArgs & a, cudaStream_t s);
+// copies the current frame into frames_all[step] and advances the burst step counter
+void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s);
+
+// Philox4x32-10 uniform in [0, 1): top 24 bits of the first output word for (key, draw)
+__host__ __device__ inline uint32_t philox_word0(uint32_t key, uint32_t draw_lo, uint32_t draw_hi) {
+    uint32_t c0 = draw_lo, c1 = draw_hi, c2 = 0, c3 = 0, k0 = key, k1 = 0x42524545u;
+    for (int r = 0; r < 10; r++) {
+        const uint64_t p0 = (uint64_t) 0xD2511F53u * c0, p1 = (uint64_t) 0xCD9E8D57u * c2;
+        const uint32_t hi0 = (uint32_t) (p0 >> 32), lo0 = (uint32_t) p0;
+        const uint32_t hi1 = (uint32_t) (p1 >> 32), lo1 = (uint32_t) p1;
+        const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return c0;
+}
+
+}  // namespace bzb

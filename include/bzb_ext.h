@@ -1,0 +1,65 @@
+/*
+ * bzb_ext.h -- entry points of libbreeze.so beyond the reference ABI.
+ *
+ * The reference generator ABI writes 16 codes per frame (src/c_api.cpp:672, 857); models
+ * with more codebooks need the full-width frame, and the measurement and parity harnesses
+ * need device-resident timing and intermediate values. These functions have no counterpart
+ * in the reference; the breeze.h entry points remain the drop-in interface.
+ */
+#ifndef BZB_EXT_H
+#define BZB_EXT_H
+
+#include "breeze.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* number of codebooks per frame of the loaded model (breeze.num_codebooks) */
+BREEZE_API int bzb_generator_num_codebooks(breeze_generator * gen);
+
+/* sessions_step_burst with full-width frames: out_frames is [burst_steps][num_sessions][nc].
+   Same return codes and -1 conventions as breeze_generator_sessions_step_burst. */
+BREEZE_API int bzb_generator_sessions_step_frames(breeze_generator * gen, const int * session_ids,
+                                                  int num_sessions, int burst_steps,
+                                                  const unsigned int * seeds, int * out_frames,
+                                                  int * out_next_cb0);
+
+/* re-runs the last stepped batch K more frames on the device with no host copies (timing);
+   returns 0, or -1 with breeze_last_error() set */
+BREEZE_API int bzb_generator_step_device(breeze_generator * gen, int burst_steps);
+BREEZE_API int bzb_generator_sync(breeze_generator * gen);
+/* the CUDA stream (cudaStream_t) every generator kernel is launched on */
+BREEZE_API void * bzb_generator_stream(breeze_generator * gen);
+
+/* algorithmic bytes of one frame step: Q8_0 weight bytes, and KV bytes per cached position */
+BREEZE_API long long bzb_generator_weight_bytes_per_step(breeze_generator * gen);
+BREEZE_API long long bzb_generator_kv_bytes_per_position(breeze_generator * gen);
+
+/* kernels in one captured frame step (graph nodes of the last captured bucket) */
+BREEZE_API int bzb_generator_launches_per_step(breeze_generator * gen);
+/* one eager frame step of the last batch with CUDA events around every dequant-GEMM launch:
+   out5 = {step_ms, gemm_ms, gemm_launches, gemm_algorithmic_bytes, gemm_launches_counted} */
+BREEZE_API int bzb_generator_profile_step(breeze_generator * gen, double * out5);
+
+/* parity probes: the session's last normed backbone hidden [hidden]; one depth decode of n
+   rows (hidden [n][hidden] f32, cb0 [n]; forced [n][nc-1] replaces each argmax as the next
+   input when non-null) returning codes [n][nc-1] and logits [n][nc-1][audio_vocab]; one
+   dequant-GEMM of a named Q8_0 tensor (slice `sub` of a 3-D tensor, or -1) on x [rows][K] */
+BREEZE_API int bzb_generator_debug_hidden(breeze_generator * gen, int session_id, float * out);
+BREEZE_API int bzb_generator_debug_depth(breeze_generator * gen, int n, const float * hidden, const int * cb0,
+                                         const int * forced, int * out_codes, float * out_logits);
+BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int sub, int rows,
+                                        const float * x, float * y);
+
+/* GGUF inspection without a GPU: 0 and the config values, or -1 with breeze_last_error() */
+BREEZE_API int bzb_gguf_inspect(const char * gguf_path, int * out_hidden, int * out_num_codebooks,
+                                int * out_n_tensors);
+/* tokenizer without a GPU: writes up to max_ids ids, returns the count or -1 */
+BREEZE_API int bzb_tokenize(const char * gguf_path, const char * text, int add_bos, int * out_ids, int max_ids);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,854 @@
+"""CPU oracle for the Breeze-TTS-2 generation path -- TEST INFRASTRUCTURE ONLY.
+
+This module restates, in numpy, what the reference computes on its ggml CPU path for the
+batched decode step and the session prefill that feeds it. Only `tests/`, the package's
+`smoke()` entry and `bench.py`'s CPU-baseline leg may import it, and only as the checker:
+no product code path calls into it.
+
+Parity anchoring: the reference's arithmetic lives in ggml (un-vendored, unpinned: a
+`master` FetchContent in CMakeLists.txt:26-35), and the reference's own tests hold no
+golden logits, tokens or PCM. The dequantisers below are pinned bit-exactly against
+gguf-py 0.19.0 (`gguf.quants`); everything downstream of them is a restatement of the
+reference call sites cited on each function ("parity unpinned" beyond dequantisation).
+
+Two numeric modes for quantised linears (`linear`):
+  * "exact": f32 activations times the dequantised f32 weights (the engine computes this to
+    within f16 activation rounding);
+  * "ggml": activations quantised per 32-block to Q8_0 before an integer dot, the way ggml's
+    CPU backend evaluates a Q8_0 weight (vec_dot_type Q8_0).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass, field
+
+import numpy as np
+
+try:  # gguf-py is the third-party reader used to walk the file; dequantisation is ours
+    import gguf  # type: ignore
+except Exception:  # pragma: no cover
+    gguf = None
+
+_LIBM = ctypes.CDLL("libm.so.6")
+_LIBM.powf.restype = ctypes.c_float
+_LIBM.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+
+F32, F16, Q8_0, Q4_K = 0, 1, 8, 12
+
+
+# ----------------------------------------------------------------------------- dequantisation
+def dequant_q8_0(raw: np.ndarray, n: int) -> np.ndarray:
+    """Q8_0 blocks (f16 d + 32 x int8) -> f32; ggml-quants.c dequantize_row_q8_0 semantics."""
+    b = raw.reshape(-1, 34)
+    d = b[:, :2].copy().view(np.float16).astype(np.float32)
+    q = b[:, 2:].copy().view(np.int8).astype(np.float32)
+    return (q * d).reshape(-1)[:n]
+
+
+def q4k_scale_min(scales: np.ndarray):
+    """6-bit scale/min unpacking of a Q4_K block (ggml get_scale_min_k4)."""
+    s = scales.astype(np.int32)
+    sc = np.empty((s.shape[0], 8), np.int32)
+    mn = np.empty((s.shape[0], 8), np.int32)
+    for j in range(4):
+        sc[:, j] = s[:, j] & 63
+        mn[:, j] = s[:, j + 4] & 63
+    for j in range(4, 8):
+        sc[:, j] = (s[:, j + 4] & 0xF) | ((s[:, j - 4] >> 6) << 4)
+        mn[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+    return sc, mn
+
+
+def dequant_q4_k(raw: np.ndarray, n: int) -> np.ndarray:
+    """Q4_K super-blocks of 256 (d, dmin, 12 packed scale bytes, 128 nibble bytes) -> f32."""
+    b = raw.reshape(-1, 144)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    dmin = b[:, 2:4].copy().view(np.float16).astype(np.float32)
+    sc, mn = q4k_scale_min(b[:, 4:16])
+    qs = b[:, 16:]
+    out = np.empty((b.shape[0], 256), np.float32)
+    for c in range(4):
+        q = qs[:, c * 32:(c + 1) * 32]
+        lo = (q & 0xF).astype(np.float32)
+        hi = (q >> 4).astype(np.float32)
+        d1 = d * sc[:, 2 * c:2 * c + 1].astype(np.float32)
+        m1 = dmin * mn[:, 2 * c:2 * c + 1].astype(np.float32)
+        d2 = d * sc[:, 2 * c + 1:2 * c + 2].astype(np.float32)
+        m2 = dmin * mn[:, 2 * c + 1:2 * c + 2].astype(np.float32)
+        out[:, c * 64:c * 64 + 32] = d1 * lo - m1
+        out[:, c * 64 + 32:c * 64 + 64] = d2 * hi - m2
+    return out.reshape(-1)[:n]
+
+
+def quant_q8_0_rows(x: np.ndarray):
+    """Activation Q8_0 quantisation per 32-block (ggml quantize_row_q8_0 rule): returns int8
+    values and the f16-rounded block scales as f32."""
+    xb = x.astype(np.float32).reshape(x.shape[0], -1, 32)
+    amax = np.abs(xb).max(axis=2, keepdims=True)
+    d = (amax / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        idv = np.where(d == 0, np.float32(0), np.float32(1.0) / d).astype(np.float32)
+    v = (xb * idv).astype(np.float32)
+    a = np.abs(v)
+    fl = np.floor(a)
+    q = (np.sign(v) * (fl + np.floor(2 * (a - fl)))).astype(np.int8)
+    return q, d.astype(np.float16).astype(np.float32)
+
+
+# ----------------------------------------------------------------------------- model file
+@dataclass
+class TensorRec:
+    name: str
+    ne: tuple
+    type: int
+    raw: np.ndarray
+
+
+class GGUFFile:
+    """Reads tensors and KV fields of a GGUF through gguf-py's reader (test infrastructure)."""
+
+    def __init__(self, path: str):
+        if gguf is None:
+            raise RuntimeError("gguf-py is required by the oracle")
+        self.path = path
+        r = gguf.GGUFReader(path)
+        self.fields = {}
+        for k, f in r.fields.items():
+            self.fields[k] = f
+        self.tensors = {}
+        for t in r.tensors:
+            ne = tuple(int(x) for x in t.shape)
+            self.tensors[t.name] = TensorRec(t.name, ne, int(t.tensor_type), np.asarray(t.data).view(np.uint8).reshape(-1))
+        self._cache = {}
+
+    def kv(self, key, default=None):
+        f = self.fields.get(key)
+        if f is None:
+            return default
+        types = [int(x) for x in f.types]
+        if types[0] == 8:  # string
+            return bytes(f.parts[f.data[0]]).decode("utf-8")
+        if types[0] == 9:  # array
+            if len(types) > 1 and types[1] == 8:
+                return [bytes(f.parts[i]).decode("utf-8") for i in f.data]
+            return [int(f.parts[i][0]) for i in f.data]
+        v = f.parts[f.data[0]][0]
+        return float(v) if types[0] in (6, 12) else int(v)
+
+    def has(self, name):
+        return name in self.tensors
+
+    def weight(self, name) -> np.ndarray:
+        """Dequantised f32 tensor shaped [ne_{n-1}, ..., ne_0] (row-major rows of ne0)."""
+        if name in self._cache:
+            return self._cache[name]
+        t = self.tensors[name]
+        n = int(np.prod(t.ne))
+        if t.type == F32:
+            w = t.raw[: n * 4].view(np.float32).copy()
+        elif t.type == F16:
+            w = t.raw[: n * 2].view(np.float16).astype(np.float32)
+        elif t.type == Q8_0:
+            w = dequant_q8_0(t.raw, n)
+        elif t.type == Q4_K:
+            w = dequant_q4_k(t.raw, n)
+        else:
+            raise ValueError(f"unsupported tensor type {t.type} for {name}")
+        w = w.reshape(tuple(reversed(t.ne)))
+        self._cache[name] = w
+        return w
+
+
+# ----------------------------------------------------------------------------- config
+@dataclass
+class Config:
+    """Keys and defaults of src/config.cpp:6-102 (only what the generation path reads)."""
+    hidden: int = 2048
+    nc: int = 16
+    vs: int = 2051
+    cb_size: int = 2048
+    bb_eos: int = 2051
+    cb_eos: int = 0
+    max_new_tokens: int = 750
+    temperature: float = 0.9
+    top_k: int = 50
+    top_p: float = 1.0
+    rep: float = 1.1
+    depth_temperature: float = 0.9
+    depth_top_k: int = 50
+    depth_top_p: float = 1.0
+    te: dict = field(default_factory=dict)
+    bb: dict = field(default_factory=dict)
+    dd: dict = field(default_factory=dict)
+
+
+def parse_config(g: GGUFFile) -> Config:
+    c = Config()
+    c.hidden = g.kv("breeze.hidden_size", 2048)
+    c.nc = g.kv("breeze.num_codebooks", 16)
+    c.vs = g.kv("breeze.audio_vocab_size", 2051)
+    c.cb_size = g.kv("breeze.codec_codebook_size", 2048)
+    c.bb_eos = g.kv("breeze.backbone_eos_token_id", 2051)
+    c.cb_eos = g.kv("breeze.codebook_eos_token_id", 0)
+    c.max_new_tokens = g.kv("breeze.max_new_tokens", 750)
+    c.temperature = g.kv("breeze.temperature", 0.9)
+    c.top_k = g.kv("breeze.top_k", 50)
+    c.top_p = g.kv("breeze.top_p", 1.0)
+    c.rep = g.kv("breeze.repetition_penalty", 1.1)
+    c.depth_temperature = g.kv("breeze.depth_temperature", 0.9)
+    c.depth_top_k = g.kv("breeze.depth_top_k", 50)
+    c.depth_top_p = g.kv("breeze.depth_top_p", 1.0)
+    c.te = dict(hidden=g.kv("breeze.te.hidden_size", 1152), n_layer=g.kv("breeze.te.block_count", 26),
+                n_head=g.kv("breeze.te.head_count", 4), n_kv=g.kv("breeze.te.head_count_kv", 1),
+                hd=g.kv("breeze.te.head_dim", 256), ffn=g.kv("breeze.te.feed_forward_length", 6912),
+                eps=g.kv("breeze.te.rms_eps", 1e-6), theta_full=g.kv("breeze.te.rope_theta_full", 1e6),
+                fscale_full=g.kv("breeze.te.rope_freq_scale_full", 0.125),
+                theta_sliding=g.kv("breeze.te.rope_theta_sliding", 10000.0),
+                window=g.kv("breeze.te.sliding_window", 512),
+                qpas=g.kv("breeze.te.query_pre_attn_scalar", 256.0),
+                embed_scale=g.kv("breeze.te.embed_scale", 1.0),
+                is_full=g.kv("breeze.te.layer_is_full", []) or [])
+    c.bb = dict(hidden=g.kv("breeze.bb.hidden_size", 2048), n_layer=g.kv("breeze.bb.block_count", 28),
+                n_head=g.kv("breeze.bb.head_count", 16), n_kv=g.kv("breeze.bb.head_count_kv", 8),
+                hd=g.kv("breeze.bb.head_dim", 128), ffn=g.kv("breeze.bb.feed_forward_length", 6144),
+                eps=g.kv("breeze.bb.rms_eps", 1e-6), theta=g.kv("breeze.bb.rope_theta", 1e6))
+    c.dd = dict(hidden=g.kv("breeze.dd.hidden_size", 1024), n_layer=g.kv("breeze.dd.block_count", 12),
+                n_head=g.kv("breeze.dd.head_count", 8), n_kv=g.kv("breeze.dd.head_count_kv", 2),
+                hd=g.kv("breeze.dd.head_dim", 128), ffn=g.kv("breeze.dd.feed_forward_length", 8192),
+                eps=g.kv("breeze.dd.rms_eps", 1e-5), theta=g.kv("breeze.dd.rope_theta", 500000.0),
+                factor=g.kv("breeze.dd.rope_factor", 32.0),
+                high=g.kv("breeze.dd.rope_high_freq_factor", 0.0078125),
+                low=g.kv("breeze.dd.rope_low_freq_factor", 0.001953125),
+                orig=g.kv("breeze.dd.rope_orig_ctx", 16))
+    return c
+
+
+# ----------------------------------------------------------------------------- tokenizer
+_META = "▁"
+
+
+class Tokenizer:
+    """SentencePiece-style BPE of src/tokenizer.cpp:19-124 (longest special first, byte
+    fallback, rank-ordered merges)."""
+
+    def __init__(self, g: GGUFFile):
+        self.id_to_token = g.kv("tokenizer.ggml.tokens")
+        types = g.kv("tokenizer.ggml.token_type", []) or []
+        self.token_to_id = {}
+        self.byte_to_id = {}
+        self.specials = {}
+        for i, t in enumerate(self.id_to_token):
+            self.token_to_id[t] = i
+            if len(t) == 6 and t.startswith("<0x") and t.endswith(">"):
+                self.byte_to_id[int(t[3:5], 16)] = i
+            if i < len(types) and types[i] in (3, 4):
+                self.specials[t] = i
+        self.special_lens = sorted({len(s) for s in self.specials}, reverse=True)
+        merges = g.kv("tokenizer.ggml.merges", []) or []
+        self.merge_rank = {m: i for i, m in enumerate(merges)}
+        self.bos = g.kv("tokenizer.ggml.bos_token_id", 2)
+        self.unk = g.kv("tokenizer.ggml.unknown_token_id", 3)
+
+    def _bpe(self, word: str, out: list):
+        syms = []
+        for ch in word:
+            if ch in self.token_to_id:
+                syms.append(ch)
+            else:
+                for b in ch.encode("utf-8"):
+                    syms.append(self.id_to_token[self.byte_to_id[b]] if b in self.byte_to_id else chr(b))
+        while len(syms) > 1:
+            best, best_i = None, -1
+            for i in range(len(syms) - 1):
+                r = self.merge_rank.get(syms[i] + " " + syms[i + 1])
+                if r is not None and (best is None or r < best):
+                    best, best_i = r, i
+            if best_i < 0:
+                break
+            syms[best_i] += syms[best_i + 1]
+            del syms[best_i + 1]
+        for s in syms:
+            if s in self.token_to_id:
+                out.append(self.token_to_id[s])
+            else:
+                for b in s.encode("utf-8"):
+                    out.append(self.byte_to_id.get(b, self.unk))
+
+    def encode(self, text: str, add_bos=True) -> list:
+        out = [self.bos] if add_bos else []
+        normal = []
+        i = 0
+        while i < len(text):
+            hit = None
+            for L in self.special_lens:
+                s = text[i:i + L]
+                if len(s) == L and s in self.specials:
+                    hit = s
+                    break
+            if hit is not None:
+                if normal:
+                    self._bpe("".join(normal).replace(" ", _META), out)
+                    normal = []
+                out.append(self.specials[hit])
+                i += len(hit)
+            else:
+                normal.append(text[i])
+                i += 1
+        if normal:
+            self._bpe("".join(normal).replace(" ", _META), out)
+        return out
+
+
+# ----------------------------------------------------------------------------- primitives
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """ggml_rms_norm (mean of squares in double) followed by ggml_mul with the weight
+    (src/common.cpp:127-129)."""
+    x = x.astype(np.float32)
+    ms = (x.astype(np.float64) ** 2).mean(axis=-1, keepdims=True)
+    scale = (np.float32(1.0) / np.sqrt((ms + eps).astype(np.float32))).astype(np.float32)
+    return ((x * scale).astype(np.float32) * w.astype(np.float32)).astype(np.float32)
+
+
+def linear(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """ggml_mul_mat(w, x) evaluated exactly: f32 activations times the dequantised weight
+    w [out, in] (src/common.cpp:136-138)."""
+    return (x.astype(np.float32) @ w.T).astype(np.float32)
+
+
+def linear_q8(x: np.ndarray, raw: np.ndarray, out_dim: int, in_dim: int, row0: int = 0) -> np.ndarray:
+    """ggml-mode linear on raw Q8_0 weight bytes: activations quantised to Q8_0 per block,
+    integer block dots, f32 accumulation of sumi * (dw * dx) (ggml vec_dot_q8_0_q8_0)."""
+    q, d = quant_q8_0_rows(x.astype(np.float32))
+    nb = in_dim // 32
+    b = raw[row0 * nb * 34:(row0 + out_dim) * nb * 34].reshape(out_dim, nb, 34)
+    wd = b[:, :, :2].copy().view(np.float16).astype(np.float32)[:, :, 0]   # [out, nb]
+    wq = b[:, :, 2:].copy().view(np.int8).astype(np.int32)                  # [out, nb, 32]
+    qi = q.astype(np.int32)
+    out = np.zeros((x.shape[0], out_dim), np.float32)
+    for blk in range(nb):
+        sumi = qi[:, blk, :] @ wq[:, blk, :].T                              # [n, out] exact ints
+        out += sumi.astype(np.float32) * (wd[None, :, blk] * d[:, blk, 0][:, None]).astype(np.float32)
+    return out
+
+
+def silu(x):
+    x = x.astype(np.float32)
+    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def gelu_tanh(x):
+    x = x.astype(np.float32)
+    c = np.float32(math.sqrt(2.0 / math.pi))
+    return (np.float32(0.5) * x * (np.float32(1.0) + np.tanh(c * x * (np.float32(1.0) + np.float32(0.044715) * x * x)))).astype(np.float32)
+
+
+def rope_cos_sin(pos: np.ndarray, n_dims: int, base: float, freq_scale: float = 1.0, ff=None):
+    """ggml rope cache for NEOX mode: theta_i = pos * theta_scale^i built by repeated f32
+    multiplication, theta_scale = powf(base, -2/n_dims), divided by the optional frequency
+    factor and multiplied by freq_scale (ext_factor 0)."""
+    ts = np.float32(_LIBM.powf(ctypes.c_float(base), ctypes.c_float(-2.0 / n_dims)))
+    half = n_dims // 2
+    theta = pos.astype(np.float32).copy()
+    cos = np.empty((pos.shape[0], half), np.float32)
+    sin = np.empty((pos.shape[0], half), np.float32)
+    for i in range(half):
+        t = theta if ff is None else (theta / np.float32(ff[i])).astype(np.float32)
+        t = (np.float32(freq_scale) * t).astype(np.float32)
+        cos[:, i] = np.cos(t)
+        sin[:, i] = np.sin(t)
+        theta = (theta * ts).astype(np.float32)
+    return cos, sin
+
+
+def rope_neox(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """x [T, H, hd]; rotate pairs (i, i + hd/2) with the per-token cos/sin [T, hd/2]."""
+    half = x.shape[-1] // 2
+    x0, x1 = x[..., :half], x[..., half:]
+    c, s = cos[:, None, :], sin[:, None, :]
+    return np.concatenate([x0 * c - x1 * s, x0 * s + x1 * c], axis=-1).astype(np.float32)
+
+
+def llama3_freq_factors(dd: dict) -> np.ndarray:
+    """src/depth_decoder.cpp:10-29."""
+    hd = dd["hd"]
+    half = hd // 2
+    ff = np.ones(half, np.float32)
+    pi = np.float32(3.14159265358979323846)
+    low_wl = np.float32(dd["orig"]) / np.float32(dd["low"])
+    high_wl = np.float32(dd["orig"]) / np.float32(dd["high"])
+    for i in range(half):
+        freq = np.float32(_LIBM.powf(ctypes.c_float(dd["theta"]), ctypes.c_float(np.float32(-2.0 * i) / np.float32(hd))))
+        wavelen = np.float32(2.0) * pi / freq
+        if wavelen > low_wl:
+            ff[i] = dd["factor"]
+        elif wavelen < high_wl:
+            ff[i] = 1.0
+        else:
+            smooth = (np.float32(dd["orig"]) / wavelen - np.float32(dd["low"])) / (np.float32(dd["high"]) - np.float32(dd["low"]))
+            ff[i] = np.float32(1.0) / ((np.float32(1.0) - smooth) / np.float32(dd["factor"]) + smooth)
+    return ff
+
+
+def attention(q, k, v, scale, mask=None):
+    """softmax(K.q * scale + mask) . V with GQA broadcast (src/common.cpp:147-160).
+    q [Tq, H, hd], k/v [Tk, Hkv, hd] -> [Tq, H*hd]."""
+    Tq, H, hd = q.shape
+    Hkv = k.shape[1]
+    g = H // Hkv
+    out = np.empty((Tq, H, hd), np.float32)
+    for h in range(H):
+        kh = k[:, h // g, :]
+        vh = v[:, h // g, :]
+        s = (q[:, h, :] @ kh.T).astype(np.float32) * np.float32(scale)
+        if mask is not None:
+            s = s + mask
+        m = s.max(axis=1, keepdims=True)
+        e = np.exp((s - m).astype(np.float32))
+        p = (e / e.sum(axis=1, keepdims=True, dtype=np.float64)).astype(np.float32)
+        out[:, h, :] = p @ vh
+    return out.reshape(Tq, H * hd)
+
+
+# ----------------------------------------------------------------------------- model
+class Model:
+    def __init__(self, path: str, mode: str = "exact"):
+        self.g = GGUFFile(path)
+        self.cfg = parse_config(self.g)
+        self.tok = Tokenizer(self.g)
+        self.mode = mode
+        self.dd_ff = llama3_freq_factors(self.cfg.dd)
+
+    def w(self, name):
+        return self.g.weight(name)
+
+    def lin(self, x, name, sub: int = -1):
+        """Quantised linear; `sub` selects one [rows, in] slice of a 3-D weight."""
+        w = self.w(name)
+        if sub >= 0:
+            w = w[sub]
+        w = w.reshape(-1, w.shape[-1])
+        if self.mode == "ggml" and self.g.tensors[name].type == Q8_0:
+            return linear_q8(x, self.g.tensors[name].raw, w.shape[0], w.shape[1], max(sub, 0) * w.shape[0])
+        return linear(x, w)
+
+    def embed_rows(self, name, idx) -> np.ndarray:
+        w = self.w(name)
+        return w.reshape(-1, w.shape[-1])[np.asarray(idx, np.int64)].astype(np.float32)
+
+    # ------------------------------------------------------------------ text encoder
+    def text_encoder(self, tokens) -> np.ndarray:
+        """src/text_encoder.cpp:8-72 (Gemma-style bidirectional encoder + projection)."""
+        c = self.cfg.te
+        T = len(tokens)
+        x = self.embed_rows("te.token_embd.weight", tokens) * np.float32(c["embed_scale"])
+        pos = np.arange(T)
+        mfull = np.zeros((T, T), np.float32)
+        mwin = np.zeros((T, T), np.float32)
+        if c["window"] > 0:
+            left, right = (c["window"] + 1) // 2, c["window"] // 2 + 1
+            qi = np.arange(T)[:, None]
+            ki = np.arange(T)[None, :]
+            dist = qi - ki
+            ok = ((dist >= 0) & (dist < left)) | ((dist < 0) & (-dist < right))
+            mwin = np.where(ok, 0.0, -np.inf).astype(np.float32)
+        scale = 1.0 / math.sqrt(c["qpas"])
+        for il in range(c["n_layer"]):
+            p = f"te.blk.{il}"
+            full = il < len(c["is_full"]) and c["is_full"][il] != 0
+            theta = c["theta_full"] if full else c["theta_sliding"]
+            fs = c["fscale_full"] if full else 1.0
+            cos, sin = rope_cos_sin(pos, c["hd"], theta, fs)
+            res = x
+            h = rms_norm(x, self.w(p + ".attn_norm.weight"), c["eps"])
+            q = self.lin(h, p + ".attn_q.weight").reshape(T, c["n_head"], c["hd"])
+            k = self.lin(h, p + ".attn_k.weight").reshape(T, c["n_kv"], c["hd"])
+            v = self.lin(h, p + ".attn_v.weight").reshape(T, c["n_kv"], c["hd"])
+            q = rms_norm(q, self.w(p + ".attn_q_norm.weight"), c["eps"])
+            k = rms_norm(k, self.w(p + ".attn_k_norm.weight"), c["eps"])
+            q = rope_neox(q, cos, sin)
+            k = rope_neox(k, cos, sin)
+            a = attention(q, k, v, scale, mfull if full else mwin)
+            a = self.lin(a, p + ".attn_output.weight")
+            a = rms_norm(a, self.w(p + ".post_attn_norm.weight"), c["eps"])
+            x = (res + a).astype(np.float32)
+            res = x
+            h = rms_norm(x, self.w(p + ".ffn_norm.weight"), c["eps"])
+            gt = gelu_tanh(self.lin(h, p + ".ffn_gate.weight"))
+            up = self.lin(h, p + ".ffn_up.weight")
+            h = self.lin((gt * up).astype(np.float32), p + ".ffn_down.weight")
+            h = rms_norm(h, self.w(p + ".post_ffn_norm.weight"), c["eps"])
+            x = (res + h).astype(np.float32)
+        x = rms_norm(x, self.w("te.output_norm.weight"), c["eps"])
+        return self.lin(x, "te.proj.weight")
+
+    # ------------------------------------------------------------------ audio embedding
+    def audio_embed(self, frames: np.ndarray) -> np.ndarray:
+        """Sum over codebooks of audio_embd rows code + cb*vs (src/backbone.cpp:223-246).
+        frames [F, nc] int -> [F, hidden]."""
+        frames = np.asarray(frames, np.int64)
+        nc, vs = frames.shape[1], self.cfg.vs
+        idx = frames + (np.arange(nc) * vs)[None, :]
+        rows = self.embed_rows("audio_embd.weight", idx.reshape(-1)).reshape(frames.shape[0], nc, -1)
+        acc = np.zeros((frames.shape[0], rows.shape[2]), np.float32)
+        for cb in range(nc):   # ggml_sum_rows accumulates in order
+            acc = (acc + rows[:, cb, :]).astype(np.float32)
+        return acc
+
+    # ------------------------------------------------------------------ backbone
+    def bb_layer_tokens(self, st: "BBState", x: np.ndarray, il: int, pos: np.ndarray):
+        """One pre-norm block over tokens appended at `pos` (src/backbone.cpp:248-276)."""
+        c = self.cfg.bb
+        p = f"bb.blk.{il}"
+        T = x.shape[0]
+        res = x
+        h = rms_norm(x, self.w(p + ".attn_norm.weight"), c["eps"])
+        q = self.lin(h, p + ".attn_q.weight").reshape(T, c["n_head"], c["hd"])
+        k = self.lin(h, p + ".attn_k.weight").reshape(T, c["n_kv"], c["hd"])
+        v = self.lin(h, p + ".attn_v.weight").reshape(T, c["n_kv"], c["hd"])
+        q = rms_norm(q, self.w(p + ".attn_q_norm.weight"), c["eps"])
+        k = rms_norm(k, self.w(p + ".attn_k_norm.weight"), c["eps"])
+        cos, sin = rope_cos_sin(pos, c["hd"], c["theta"])
+        q = rope_neox(q, cos, sin)
+        k = rope_neox(k, cos, sin)
+        st.k[il][pos[0]:pos[0] + T] = k
+        st.v[il][pos[0]:pos[0] + T] = v
+        L = pos[0] + T
+        qi = pos[:, None]
+        ki = np.arange(L)[None, :]
+        mask = np.where(ki <= qi, 0.0, -np.inf).astype(np.float32)
+        a = attention(q, st.k[il][:L], st.v[il][:L], 1.0 / math.sqrt(c["hd"]), mask)
+        x = (res + self.lin(a, p + ".attn_output.weight")).astype(np.float32)
+        res = x
+        h = rms_norm(x, self.w(p + ".ffn_norm.weight"), c["eps"])
+        g = silu(self.lin(h, p + ".ffn_gate.weight"))
+        u = self.lin(h, p + ".ffn_up.weight")
+        return (res + self.lin((g * u).astype(np.float32), p + ".ffn_down.weight")).astype(np.float32)
+
+    def backbone_run(self, st: "BBState", embeds: np.ndarray):
+        """Prefill or single-token run; returns (last normed hidden, logits)
+        (src/backbone.cpp:68-96)."""
+        c = self.cfg.bb
+        T = embeds.shape[0]
+        pos = np.arange(st.pos, st.pos + T)
+        x = embeds.astype(np.float32)
+        for il in range(c["n_layer"]):
+            x = self.bb_layer_tokens(st, x, il, pos)
+        x = rms_norm(x, self.w("bb.output_norm.weight"), c["eps"])
+        last = x[-1:]
+        logits = self.lin(last, "bb.lm_head.weight")
+        st.pos += T
+        return last[0], logits[0]
+
+    def backbone_step_batched(self, states: list, embeds: np.ndarray):
+        """One token per session, each attending to its own cache (src/backbone.cpp:98-179):
+        linears batched over sessions, attention per session over its cache."""
+        c = self.cfg.bb
+        N = embeds.shape[0]
+        x = embeds.astype(np.float32)
+        scale = 1.0 / math.sqrt(c["hd"])
+        pos = np.array([st.pos for st in states])
+        for il in range(c["n_layer"]):
+            p = f"bb.blk.{il}"
+            res = x
+            h = rms_norm(x, self.w(p + ".attn_norm.weight"), c["eps"])
+            q = self.lin(h, p + ".attn_q.weight").reshape(N, c["n_head"], c["hd"])
+            k = self.lin(h, p + ".attn_k.weight").reshape(N, c["n_kv"], c["hd"])
+            v = self.lin(h, p + ".attn_v.weight").reshape(N, c["n_kv"], c["hd"])
+            q = rms_norm(q, self.w(p + ".attn_q_norm.weight"), c["eps"])
+            k = rms_norm(k, self.w(p + ".attn_k_norm.weight"), c["eps"])
+            a = np.empty((N, c["n_head"] * c["hd"]), np.float32)
+            for i, st in enumerate(states):
+                cos, sin = rope_cos_sin(pos[i:i + 1], c["hd"], c["theta"])
+                qi = rope_neox(q[i:i + 1], cos, sin)
+                ki = rope_neox(k[i:i + 1], cos, sin)
+                st.k[il][pos[i]] = ki[0]
+                st.v[il][pos[i]] = v[i]
+                L = pos[i] + 1
+                a[i] = attention(qi, st.k[il][:L], st.v[il][:L], scale)[0]
+            x = (res + self.lin(a, p + ".attn_output.weight")).astype(np.float32)
+            res = x
+            h = rms_norm(x, self.w(p + ".ffn_norm.weight"), c["eps"])
+            g = silu(self.lin(h, p + ".ffn_gate.weight"))
+            u = self.lin(h, p + ".ffn_up.weight")
+            x = (res + self.lin((g * u).astype(np.float32), p + ".ffn_down.weight")).astype(np.float32)
+        x = rms_norm(x, self.w("bb.output_norm.weight"), c["eps"])
+        logits = self.lin(x, "bb.lm_head.weight")
+        for st in states:
+            st.pos += 1
+        return x, logits
+
+    # ------------------------------------------------------------------ depth decoder
+    def depth_logits_chain(self, hiddens: np.ndarray, cb0: np.ndarray, forced=None):
+        """Unified batched depth decode (src/depth_decoder.cpp:249-365): position 0 is the
+        backbone hidden, position 1 the cb0 embedding, then one position per codebook; each
+        sub-step's logits come from head j-1 and its argmax feeds the next embedding.
+        `forced` [N, nc-1] replaces the argmax as the next input (teacher forcing).
+        Returns (codes [N, nc-1], logits [N, nc-1, vs])."""
+        c = self.cfg.dd
+        nc, vs = self.cfg.nc, self.cfg.vs
+        N = hiddens.shape[0]
+        kc = np.zeros((c["n_layer"], N, nc + 1, c["n_kv"], c["hd"]), np.float32)
+        vc = np.zeros_like(kc)
+        codes = np.zeros((N, nc - 1), np.int64)
+        logits_all = np.zeros((N, nc - 1, vs), np.float32)
+        scale = 1.0 / math.sqrt(c["hd"])
+
+        def run_layers(x, start, n_pos):
+            # x [N, n_pos, dd_hidden] for positions start..start+n_pos-1
+            pos = np.arange(start, start + n_pos)
+            cos, sin = rope_cos_sin(pos, c["hd"], c["theta"], 1.0, self.dd_ff)
+            for il in range(c["n_layer"]):
+                p = f"dd.blk.{il}"
+                res = x
+                flat = x.reshape(N * n_pos, -1)
+                h = rms_norm(flat, self.w(p + ".attn_norm.weight"), c["eps"])
+                q = self.lin(h, p + ".attn_q.weight").reshape(N, n_pos, c["n_head"], c["hd"])
+                k = self.lin(h, p + ".attn_k.weight").reshape(N, n_pos, c["n_kv"], c["hd"])
+                v = self.lin(h, p + ".attn_v.weight").reshape(N, n_pos, c["n_kv"], c["hd"])
+                a = np.empty((N, n_pos, c["n_head"] * c["hd"]), np.float32)
+                for s in range(N):
+                    qs_ = rope_neox(q[s], cos, sin)
+                    ks_ = rope_neox(k[s], cos, sin)
+                    kc[il, s, start:start + n_pos] = ks_
+                    vc[il, s, start:start + n_pos] = v[s]
+                    L = start + n_pos
+                    mask = np.where(np.arange(L)[None, :] <= pos[:, None], 0.0, -np.inf).astype(np.float32)
+                    a[s] = attention(qs_, kc[il, s, :L], vc[il, s, :L], scale, mask)
+                o = self.lin(a.reshape(N * n_pos, -1), p + ".attn_output.weight").reshape(x.shape)
+                x = (res + o).astype(np.float32)
+                res = x
+                flat = x.reshape(N * n_pos, -1)
+                h = rms_norm(flat, self.w(p + ".ffn_norm.weight"), c["eps"])
+                gt = silu(self.lin(h, p + ".ffn_gate.weight"))
+                up = self.lin(h, p + ".ffn_up.weight")
+                d = self.lin((gt * up).astype(np.float32), p + ".ffn_down.weight").reshape(x.shape)
+                x = (res + d).astype(np.float32)
+            return x
+
+        e0 = self.embed_rows("audio_embd.weight", cb0)
+        inp = np.stack([hiddens.astype(np.float32), e0], axis=1)       # [N, 2, hidden]
+        x = self.lin(inp.reshape(2 * N, -1), "dd.in_proj.weight").reshape(N, 2, -1)
+        x = run_layers(x, 0, 2)
+        last = rms_norm(x[:, 1], self.w("dd.output_norm.weight"), c["eps"])
+        lg = self.lin(last, "dd.codebooks_head.weight", 0)
+        logits_all[:, 0] = lg
+        codes[:, 0] = np.argmax(lg, axis=1)
+        for j in range(2, nc):
+            prev = codes[:, j - 2] if forced is None else np.asarray(forced)[:, j - 2]
+            e = self.embed_rows("audio_embd.weight", (j - 1) * vs + prev)
+            x = self.lin(e, "dd.in_proj.weight").reshape(N, 1, -1)
+            x = run_layers(x, j, 1)
+            last = rms_norm(x[:, 0], self.w("dd.output_norm.weight"), c["eps"])
+            lg = self.lin(last, "dd.codebooks_head.weight", j - 1)
+            logits_all[:, j - 1] = lg
+            codes[:, j - 1] = np.argmax(lg, axis=1)
+        return codes, logits_all
+
+
+@dataclass
+class BBState:
+    """Per-session backbone KV (f32 like the reference KVCache, common.cpp:48-63)."""
+    k: list
+    v: list
+    pos: int = 0
+
+    @staticmethod
+    def new(m: Model, max_seq: int) -> "BBState":
+        c = m.cfg.bb
+        return BBState([np.zeros((max_seq, c["n_kv"], c["hd"]), np.float32) for _ in range(c["n_layer"])],
+                       [np.zeros((max_seq, c["n_kv"], c["hd"]), np.float32) for _ in range(c["n_layer"])])
+
+
+# ----------------------------------------------------------------------------- sampling
+_PH_M0, _PH_M1 = 0xD2511F53, 0xCD9E8D57
+_PH_W0, _PH_W1 = 0x9E3779B9, 0xBB67AE85
+PHILOX_KEY_HI = 0x42524545
+
+
+def philox4x32_10(ctr, key):
+    """Philox4x32-10 (Salmon et al., SC'11): 10 rounds of the published round function."""
+    c0, c1, c2, c3 = [x & 0xFFFFFFFF for x in ctr]
+    k0, k1 = [x & 0xFFFFFFFF for x in key]
+    for _ in range(10):
+        p0 = _PH_M0 * c0
+        p1 = _PH_M1 * c2
+        hi0, lo0 = p0 >> 32, p0 & 0xFFFFFFFF
+        hi1, lo1 = p1 >> 32, p1 & 0xFFFFFFFF
+        c0, c1, c2, c3 = (hi1 ^ c1 ^ k0) & 0xFFFFFFFF, lo1, (hi0 ^ c3 ^ k1) & 0xFFFFFFFF, lo0
+        k0 = (k0 + _PH_W0) & 0xFFFFFFFF
+        k1 = (k1 + _PH_W1) & 0xFFFFFFFF
+    return c0, c1, c2, c3
+
+
+def philox_uniform(seed: int, draw: int) -> np.float32:
+    """u in [0, 1) from the top 24 bits of the first Philox word for (seed, draw index)."""
+    w = philox4x32_10((draw & 0xFFFFFFFF, (draw >> 32) & 0xFFFFFFFF, 0, 0), (seed & 0xFFFFFFFF, PHILOX_KEY_HI))
+    return np.float32((w[0] >> 8) * (1.0 / 16777216.0))
+
+
+def apply_penalties(logits: np.ndarray, rep: float, hist_counts, suppress_lo: int, suppress_hi: int) -> np.ndarray:
+    """Suppression then repetition penalty, applied once per history occurrence
+    (src/sampling.cpp:13-23)."""
+    l = logits.astype(np.float32).copy()
+    n = l.shape[0]
+    l[max(0, suppress_lo):min(n, suppress_hi)] = -np.inf
+    if hist_counts is not None and rep != 1.0:
+        r = np.float32(rep)
+        for t, cnt in hist_counts.items():
+            if t < 0 or t >= n:
+                continue
+            for _ in range(cnt):
+                l[t] = l[t] / r if l[t] > 0 else l[t] * r
+    return l
+
+
+def sample_philox(logits, temp, top_k, top_p, u: np.float32) -> int:
+    """The engine's sampler: top-k by (logit desc, index asc), softmax at temperature in f32,
+    optional top-p cut (src/sampling.cpp:25-56), then inverse-CDF with a Philox uniform in
+    place of std::discrete_distribution."""
+    n = logits.shape[0]
+    t = np.float32(temp if temp > 0 else 1.0)
+    keep = top_k if 0 < top_k < n else n
+    order = np.lexsort((np.arange(n), -logits.astype(np.float64)))[:keep]
+    maxl = logits[order[0]]
+    p = np.exp(((logits[order] - maxl) / t).astype(np.float32)).astype(np.float32)
+    s = np.float32(0)
+    for v in p:
+        s = np.float32(s + v)
+    probs = (p / s).astype(np.float32)
+    if top_p < 1.0:
+        cum = np.float32(0)
+        cut = keep
+        for i, v in enumerate(probs):
+            cum = np.float32(cum + v)
+            if cum >= np.float32(top_p):
+                cut = i + 1
+                break
+        probs = probs[:cut]
+        order = order[:cut]
+        s2 = np.float32(0)
+        for v in probs:
+            s2 = np.float32(s2 + v)
+        probs = (probs / s2).astype(np.float32)
+    cdf = np.empty_like(probs)
+    acc = np.float32(0)
+    for i, v in enumerate(probs):
+        acc = np.float32(acc + v)
+        cdf[i] = acc
+    r = np.float32(u * cdf[-1])
+    for i in range(len(cdf)):
+        if r < cdf[i]:
+            return int(order[i])
+    return int(order[-1])
+
+
+class PhiloxStream:
+    """Per-session sampler state: seed (key) and draw counter; reseeding resets the counter,
+    mirroring std::mt19937::seed in src/c_api.cpp:343, 631, 816."""
+
+    def __init__(self, seed: int):
+        self.seed(seed)
+
+    def seed(self, s: int):
+        self.key = s & 0xFFFFFFFF
+        self.draw = 0
+
+    def next_uniform(self) -> np.float32:
+        u = philox_uniform(self.key, self.draw)
+        self.draw += 1
+        return u
+
+
+# ----------------------------------------------------------------------------- sessions
+@dataclass
+class Session:
+    sid: int
+    st: BBState
+    hist: dict
+    last_hidden: np.ndarray
+    last_cb0: int
+    rng: PhiloxStream
+    max_tokens: int
+    steps_taken: int = 0
+    active: bool = True
+
+
+class Generator:
+    """Session semantics of the generator C ABI (src/c_api.cpp:325-451, 601-949) with the
+    engine's Philox sampler; CFG (cfg_scale != 1) is not restated."""
+
+    def __init__(self, model: Model):
+        self.m = model
+        self.sessions = {}
+
+    def _sample_cb0(self, sess: Session, logits) -> int:
+        c = self.m.cfg
+        l = apply_penalties(logits, 1.1, sess.hist, c.cb_size, c.vs)
+        return sample_philox(l, 0.9, 50, 1.0, sess.rng.next_uniform())
+
+    def prompt_embeds(self, text, instruction=None, ref_text=None, ref_codes=None):
+        m = self.m
+        ins = instruction if instruction is not None else "Speak clearly and naturally."
+        has_ref = ref_codes is not None and len(ref_codes) > 0 and ref_text
+        embs = []
+        if has_ref:
+            embs.append(m.text_encoder(m.tok.encode("[S0]" + ref_text, True)))
+            embs.append(m.audio_embed(np.asarray(ref_codes).reshape(-1, m.cfg.nc)))
+            embs.append(m.audio_embed(np.full((1, m.cfg.nc), m.cfg.cb_eos)))
+        embs.append(m.text_encoder(m.tok.encode("[S0]<ins_bos>" + ins + "<ins_eos>" + text, True)))
+        return np.concatenate(embs, axis=0)
+
+    def session_create(self, sid, text, instruction=None, ref_text=None, ref_codes=None,
+                       seed=0, max_new_tokens=0, embeds=None):
+        if embeds is None:
+            embeds = self.prompt_embeds(text, instruction, ref_text, ref_codes)
+        est = max_new_tokens
+        if est <= 0:
+            words = len(text.split())
+            est = min(1000, int(math.ceil(words * 1.5)) + 30)
+        total = embeds.shape[0]
+        avail = 2040 - total
+        if est > avail:
+            est = max(64, avail)
+        st = BBState.new(self.m, total + est + 8)
+        h, lg = self.m.backbone_run(st, embeds)
+        sess = Session(sid, st, {}, h, -1, PhiloxStream(seed), est)
+        cb0 = self._sample_cb0(sess, lg)
+        sess.hist[cb0] = sess.hist.get(cb0, 0) + 1
+        sess.last_cb0 = cb0
+        self.sessions[sid] = sess
+        return cb0, total + est + 8
+
+    def step_batched(self, sids, seeds=None, forced_depth=None):
+        """One frame for each active session; returns (frames [N, nc], next_cb0 [N])."""
+        m = self.m
+        nc = m.cfg.nc
+        act = [i for i, s in enumerate(sids) if s in self.sessions and self.sessions[s].active]
+        frames = np.full((len(sids), nc), -1, np.int64)
+        nxt = np.full(len(sids), -1, np.int64)
+        if not act:
+            return frames, nxt
+        ss = [self.sessions[sids[i]] for i in act]
+        if seeds is not None:
+            for i, s in zip(act, ss):
+                s.rng.seed(int(seeds[i]))
+        hid = np.stack([s.last_hidden for s in ss])
+        cb0 = np.array([s.last_cb0 for s in ss])
+        codes, _ = m.depth_logits_chain(hid, cb0, forced_depth)
+        fr = np.concatenate([cb0[:, None], codes], axis=1)
+        ae = m.audio_embed(fr)
+        hs, ls = m.backbone_step_batched([s.st for s in ss], ae)
+        for k, (i, s) in enumerate(zip(act, ss)):
+            frames[i] = fr[k]
+            n = self._sample_cb0(s, ls[k])
+            s.steps_taken += 1
+            if n == m.cfg.bb_eos or s.steps_taken >= s.max_tokens:
+                s.active = False
+            else:
+                s.hist[n] = s.hist.get(n, 0) + 1
+                s.last_cb0 = n
+                s.last_hidden = hs[k]
+                nxt[i] = n
+        return frames, nxt
