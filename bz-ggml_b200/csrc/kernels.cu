@@ -71,7 +71,7 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 struct GemvParams {
     const uint4 * qs;
     const half2 * ds;
-    int MT, M, KB, kc, splits, MG;
+    int MT, M, KB, kper, splits, MG;
     const half * x;
     int ldx, rows;
     GemvOut out;
@@ -80,57 +80,83 @@ struct GemvParams {
 };
 
 constexpr int kGemvThreads = 256;
+constexpr int kSub = 8;        // k32 blocks per staged activation sub-chunk (= weight prefetch depth)
+constexpr int kMaxSplits = 8;
 
+__device__ __forceinline__ uint32_t ldg32(const half * p) { return __ldg(reinterpret_cast<const unsigned int *>(p)); }
+
+// Each CTA owns 8 m16 row tiles (one per warp), one 64-row activation chunk and a K range.
+// Activations for kSub k32 blocks are staged in shared memory in mma B-fragment order, double
+// buffered through registers; weights stream through an 8-deep per-lane register ring that
+// runs across sub-chunk boundaries. Split-K partials (at most kMaxSplits) are reduced in split
+// order by the last CTA of each row group.
 template <int NT, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
-    extern __shared__ uint4 smem_b[];  // [kc][NT][32]
+    extern __shared__ uint4 smem_b[];  // [2][kSub][NT][32]
     __shared__ int s_last;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mg = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
-    const int kb0 = split * p.kc;
-    const int nkb = min(p.KB, kb0 + p.kc) - kb0;
+    const int kb_beg = split * p.kper;
+    const int nkb = min(p.KB, kb_beg + p.kper) - kb_beg;
     const int mt = mg * 8 + warp;
     const bool mt_ok = mt < p.MT;
     const int row0 = chunk * 64;
-    const uint4 * wq = p.qs + ((size_t) mt * p.KB + kb0) * 32 + lane;
-    const half2 * wd = p.ds + ((size_t) mt * p.KB + kb0) * 8 + (lane >> 2);
+    const uint4 * wq = p.qs + ((size_t) mt * p.KB + kb_beg) * 32 + lane;
+    const half2 * wd = p.ds + ((size_t) mt * p.KB + kb_beg) * 8 + (lane >> 2);
 
-    uint4 a[8];
-    half2 sc[8];
+    uint4 a[kSub];
+    half2 sc[kSub];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < kSub; i++) {
         if (mt_ok && i < nkb) {
             a[i] = ld_stream(wq + (size_t) i * 32);
             sc[i] = wd[(size_t) i * 8];
         }
     }
 
-    // stage this CTA's activation rows x[row0 .. row0+8NT) x [kb0*32, (kb0+nkb)*32) in B order
-    const int cpr = nkb * 4;  // 16-byte chunks per row
-    const int total = NT * 8 * cpr;
-    for (int idx = threadIdx.x; idx < total; idx += kGemvThreads) {
-        const int n = idx / cpr, c = idx - n * cpr;
-        const int gr = row0 + n;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (gr < p.rows) v = *reinterpret_cast<const uint4 *>(p.x + (size_t) gr * p.ldx + (size_t) kb0 * 32 + c * 8);
-        const int kb = c >> 2, wsel = c & 3, nt = n >> 3, g = n & 7;
-        uint32_t * base = reinterpret_cast<uint32_t *>(smem_b + (size_t) (kb * NT + nt) * 32);
-        base[(g * 4 + 0) * 4 + wsel] = v.x;
-        base[(g * 4 + 1) * 4 + wsel] = v.y;
-        base[(g * 4 + 2) * 4 + wsel] = v.z;
-        base[(g * 4 + 3) * 4 + wsel] = v.w;
-    }
-    __syncthreads();
+    // this thread's NT staged fragments per sub-chunk: fragment f = tid + 256*r covers
+    // (k block f / (NT*32), row tile (f / 32) % NT, lane f % 32)
+    uint4 st[NT];
+    auto load_stage = [&](int s) {
+        const int kbs = s * kSub;
+#pragma unroll
+        for (int r = 0; r < NT; r++) {
+            const int f = tid + r * kGemvThreads;
+            const int kbl = f / (NT * 32), nt = (f / 32) % NT, L = f & 31;
+            const int n = row0 + nt * 8 + (L >> 2);
+            const int kb = kbs + kbl;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (kb < nkb && n < p.rows) {
+                const half * src = p.x + (size_t) n * p.ldx + (size_t) (kb_beg + kb) * 32 + 2 * (L & 3);
+                v.x = ldg32(src);
+                v.y = ldg32(src + 8);
+                v.z = ldg32(src + 16);
+                v.w = ldg32(src + 24);
+            }
+            st[r] = v;
+        }
+    };
+    auto store_stage = [&](int buf) {
+        uint4 * dst = smem_b + (size_t) buf * kSub * NT * 32;
+#pragma unroll
+        for (int r = 0; r < NT; r++) dst[tid + r * kGemvThreads] = st[r];
+    };
 
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
 
-    if (mt_ok) {
-        for (int base = 0; base < nkb; base += 8) {
+    const int nsubs = (nkb + kSub - 1) / kSub;
+    load_stage(0);
+    store_stage(0);
+    __syncthreads();
+    for (int s = 0; s < nsubs; s++) {
+        if (s + 1 < nsubs) load_stage(s + 1);
+        if (mt_ok) {
+            const uint4 * sbuf = smem_b + (size_t) (s & 1) * kSub * NT * 32 + lane;
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int kb = base + i;
+            for (int i = 0; i < kSub; i++) {
+                const int kb = s * kSub + i;
                 if (kb < nkb) {
                     uint32_t A[8];
                     const half2 sg = __low2half2(sc[i]), sg8 = __high2half2(sc[i]);
@@ -138,47 +164,52 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
                     dq_word(a[i].y, sg, sg8, A[2], A[3]);
                     dq_word(a[i].z, sg, sg8, A[4], A[5]);
                     dq_word(a[i].w, sg, sg8, A[6], A[7]);
-                    if (kb + 8 < nkb) {
-                        a[i] = ld_stream(wq + (size_t) (kb + 8) * 32);
-                        sc[i] = wd[(size_t) (kb + 8) * 8];
+                    if (kb + kSub < nkb) {
+                        a[i] = ld_stream(wq + (size_t) (kb + kSub) * 32);
+                        sc[i] = wd[(size_t) (kb + kSub) * 8];
                     }
-                    const uint4 * bp = smem_b + (size_t) kb * NT * 32 + lane;
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++) {
-                        const uint4 b = bp[nt * 32];
+                        const uint4 b = sbuf[(i * NT + nt) * 32];
                         mma16816(acc[nt], A, b.x, b.y);
                         mma16816(acc[nt], A + 4, b.z, b.w);
                     }
                 }
             }
         }
+        if (s + 1 < nsubs) store_stage((s + 1) & 1);
+        __syncthreads();
     }
 
     if (p.splits > 1) {
         if (mt_ok) {
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
-                p.ws[(((size_t) (chunk * p.splits + split) * p.MT + mt) * NT + nt) * 32 + lane] =
-                    make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+                __stcg(&p.ws[(((size_t) (chunk * p.splits + split) * p.MT + mt) * NT + nt) * 32 + lane],
+                       make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
         }
         __threadfence();
         __syncthreads();
-        if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[chunk * p.MG + mg], 1) == p.splits - 1;
+        if (tid == 0) s_last = atomicAdd(&p.counters[chunk * p.MG + mg], 1) == p.splits - 1;
         __syncthreads();
         if (!s_last) return;
         __threadfence();
         if (mt_ok) {
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int sp = 0; sp < p.splits; sp++) {
-                    const float4 v = __ldcg(&p.ws[(((size_t) (chunk * p.splits + sp) * p.MT + mt) * NT + nt) * 32 + lane]);
-                    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-                }
-                acc[nt][0] = s.x; acc[nt][1] = s.y; acc[nt][2] = s.z; acc[nt][3] = s.w;
+                float4 v[kMaxSplits];
+#pragma unroll
+                for (int sp = 0; sp < kMaxSplits; sp++)
+                    if (sp < p.splits)
+                        v[sp] = __ldcg(&p.ws[(((size_t) (chunk * p.splits + sp) * p.MT + mt) * NT + nt) * 32 + lane]);
+                float4 t = v[0];
+#pragma unroll
+                for (int sp = 1; sp < kMaxSplits; sp++)
+                    if (sp < p.splits) { t.x += v[sp].x; t.y += v[sp].y; t.z += v[sp].z; t.w += v[sp].w; }
+                acc[nt][0] = t.x; acc[nt][1] = t.y; acc[nt][2] = t.z; acc[nt][3] = t.w;
             }
         }
-        if (threadIdx.x == 0) p.counters[chunk * p.MG + mg] = 0;
+        if (tid == 0) p.counters[chunk * p.MG + mg] = 0;
     }
     if (!mt_ok) return;
 
@@ -224,7 +255,7 @@ void launch_gemv_nt(const GemvParams & p, dim3 grid, size_t smem, cudaStream_t s
 
 template <int NT>
 void set_gemv_attr() {
-    const int mx = 200 * 1024;
+    const int mx = 2 * kSub * NT * 32 * (int) sizeof(uint4);
     cudaFuncSetAttribute(gemv_kernel<NT, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     cudaFuncSetAttribute(gemv_kernel<NT, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     cudaFuncSetAttribute(gemv_kernel<NT, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
@@ -286,16 +317,35 @@ __global__ void rmsnorm_kernel(const float * x, int ldx, const float * w, int D,
                                float * o32, int ld32, int r0, const int * row_map) {
     __shared__ float red[32];
     const int i = blockIdx.x;
-    const float * xr = x + (size_t) (r0 + i) * ldx;
+    const float4 * xr = reinterpret_cast<const float4 *>(x + (size_t) (r0 + i) * ldx);
+    const float4 * w4 = reinterpret_cast<const float4 *>(w);
+    const int D4 = D >> 2;
+    float4 v[4];
     float ss = 0.0f;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) ss += xr[d] * xr[d];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int c = threadIdx.x + q * blockDim.x;
+        v[q] = c < D4 ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += v[q].x * v[q].x + v[q].y * v[q].y + v[q].z * v[q].z + v[q].w * v[q].w;
+    }
+    for (int c = threadIdx.x + 4 * blockDim.x; c < D4; c += blockDim.x) {
+        const float4 t = xr[c];
+        ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    }
     ss = block_sum(ss, red);
     const float scale = 1.0f / sqrtf(ss / (float) D + eps);
     const int orow = row_map ? row_map[i] : i;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        const float y = (xr[d] * scale) * w[d];
-        if (o16) o16[(size_t) i * ld16 + d] = __float2half_rn(y);
-        if (o32 && orow >= 0) o32[(size_t) orow * ld32 + d] = y;
+    for (int c = threadIdx.x; c < D4; c += blockDim.x) {
+        const float4 t = xr[c], ww = w4[c];
+        const float4 y = make_float4((t.x * scale) * ww.x, (t.y * scale) * ww.y, (t.z * scale) * ww.z, (t.w * scale) * ww.w);
+        if (o16) {
+            half2 h0 = __floats2half2_rn(y.x, y.y), h1 = __floats2half2_rn(y.z, y.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t *>(&h0);
+            u.y = *reinterpret_cast<uint32_t *>(&h1);
+            *reinterpret_cast<uint2 *>(o16 + (size_t) i * ld16 + 4 * c) = u;
+        }
+        if (o32 && orow >= 0) *reinterpret_cast<float4 *>(o32 + (size_t) orow * ld32 + 4 * c) = y;
     }
 }
 
@@ -373,6 +423,67 @@ __device__ __forceinline__ size_t paged_off(const AttnKV & kv, const int * page_
     return ((((size_t) page * kv.n_layer + kv.layer) * 2 + kvsel) * n_kv + h) * 16 * HD + (size_t) (p & 15) * HD;
 }
 
+// stages positions [t0, t0+32) of one kv head into shared memory as f32 (zeros past `lim`);
+// every 16-byte load of the tile is issued before any conversion or store
+template <int HD, bool PAGED>
+__device__ __forceinline__ void stage_kv_tile(float (*sk)[HD + 1], float (*sv)[HD + 1], const AttnKV & kv,
+                                              const int * page_row, int b, int h, int n_kv, int t0, int lim) {
+    constexpr int VEC = PAGED ? 8 : 4;
+    constexpr int PER_ROW = HD / VEC;
+    constexpr int NV = 32 * PER_ROW;
+    constexpr int MAXV = NV / 32;  // per thread with at least one warp
+    const int nthr = blockDim.x;
+    int pg0 = 0, pg1 = 0;
+    if (PAGED) {
+        pg0 = page_row[t0 >> 4];
+        pg1 = ((t0 >> 4) + 1 < kv.max_pages) ? page_row[(t0 >> 4) + 1] : pg0;
+    }
+    for (int kvsel = 0; kvsel < 2; kvsel++) {
+        uint4 buf[MAXV];
+#pragma unroll
+        for (int i = 0; i < MAXV; i++) {
+            const int v = threadIdx.x + i * nthr;
+            buf[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (v < NV) {
+                const int j = v / PER_ROW, c = v - (v / PER_ROW) * PER_ROW;
+                const int p = t0 + j;
+                if (p < lim) {
+                    if (PAGED) {
+                        const int page = (j < 16) ? pg0 : pg1;
+                        const half * src = kv.pool + ((((size_t) page * kv.n_layer + kv.layer) * 2 + kvsel) * n_kv + h) * 16 * HD +
+                                           (size_t) (p & 15) * HD + c * 8;
+                        buf[i] = *reinterpret_cast<const uint4 *>(src);
+                    } else {
+                        const float * src = kv.flat + (((size_t) b * kv.cap + p) * 2 + kvsel) * n_kv * HD + (size_t) h * HD + c * 4;
+                        buf[i] = *reinterpret_cast<const uint4 *>(src);
+                    }
+                }
+            }
+        }
+        float (*dst)[HD + 1] = kvsel ? sv : sk;
+#pragma unroll
+        for (int i = 0; i < MAXV; i++) {
+            const int v = threadIdx.x + i * nthr;
+            if (v < NV) {
+                const int j = v / PER_ROW, c = v - (v / PER_ROW) * PER_ROW;
+                if (PAGED) {
+                    const half2 * hv = reinterpret_cast<const half2 *>(&buf[i]);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float2 f = __half22float2(hv[q]);
+                        dst[j][c * 8 + 2 * q] = f.x;
+                        dst[j][c * 8 + 2 * q + 1] = f.y;
+                    }
+                } else {
+                    const float * fv = reinterpret_cast<const float *>(&buf[i]);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) dst[j][c * 4 + q] = fv[q];
+                }
+            }
+        }
+    }
+}
+
 template <int HD>
 struct DecodeSmem {
     float k[32][HD + 1];
@@ -444,23 +555,7 @@ __global__ void attn_decode_kernel(const AttnDecodeArgs a) {
 
     for (int t0 = 0; t0 < L; t0 += 32) {
         __syncthreads();
-        for (int idx = threadIdx.x; idx < 32 * HD; idx += blockDim.x) {
-            const int j = idx / HD, d = idx - (idx / HD) * HD;
-            const int p = t0 + j;
-            float kv_k = 0.0f, kv_v = 0.0f;
-            if (p < L) {
-                if (PAGED) {
-                    kv_k = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 0, h, a.n_kv, HD) + d]);
-                    kv_v = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 1, h, a.n_kv, HD) + d]);
-                } else {
-                    const float * base = a.kv.flat + ((size_t) b * a.kv.cap + p) * 2 * a.n_kv * HD + (size_t) h * HD + d;
-                    kv_k = base[0];
-                    kv_v = base[(size_t) a.n_kv * HD];
-                }
-            }
-            sm.k[j][d] = kv_k;
-            sm.v[j][d] = kv_v;
-        }
+        stage_kv_tile<HD, PAGED>(sm.k, sm.v, a.kv, page_row, b, h, a.n_kv, t0, L);
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < 2; i++) {
@@ -661,6 +756,21 @@ __global__ void step_init_kernel(const StepArgs a) {
     }
 }
 
+// dst[0..K) = f16(q * d) of one Q8_0 embedding row, 8 values per 8-byte load
+__device__ __forceinline__ void embed_row_f16(const QRows & e, size_t row, half * dst) {
+    const int8_t * q = e.qs + row * e.K;
+    const half * d = e.ds + row * (e.K / 32);
+    for (int c = threadIdx.x; c < e.K / 8; c += blockDim.x) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(q + c * 8);
+        const float sc = __half2float(d[c >> 2]);
+        const int8_t * b = reinterpret_cast<const int8_t *>(&u);
+        half2 o[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[j] = __floats2half2_rn((float) b[2 * j] * sc, (float) b[2 * j + 1] * sc);
+        *reinterpret_cast<uint4 *>(dst + c * 8) = *reinterpret_cast<uint4 *>(o);
+    }
+}
+
 __global__ void argmax_gather_kernel(const StepArgs a, const float * logits, int ld, int V, int col, int gather_cb) {
     __shared__ float sv[32];
     __shared__ int si[32];
@@ -696,11 +806,7 @@ __global__ void argmax_gather_kernel(const StepArgs a, const float * logits, int
     }
     __syncthreads();
     if (gather_cb < 0) return;
-    const size_t row = (size_t) gather_cb * a.vs + s_code;
-    for (int d = threadIdx.x; d < a.H; d += blockDim.x) {
-        const float e = (float) a.embd.qs[row * a.embd.K + d] * __half2float(a.embd.ds[row * (a.embd.K / 32) + (d >> 5)]);
-        a.din16[(size_t) r * a.H + d] = __float2half_rn(e);
-    }
+    embed_row_f16(a.embd, (size_t) gather_cb * a.vs + s_code, a.din16 + (size_t) r * a.H);
 }
 
 __device__ __forceinline__ unsigned int f2ord(float f) {
@@ -833,27 +939,22 @@ void init_kernel_attributes() {
 void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out,
                  const GemvScratch & scr, cudaStream_t s) {
     if (rows <= 0) return;
-    if (ldx % 8 != 0 || w.K % 32 != 0) throw std::runtime_error("gemv: activation stride or K not aligned");
+    if (ldx % 2 != 0 || w.K % 32 != 0) throw std::runtime_error("gemv: activation stride or K not aligned");
     const int chunks = (rows + 63) / 64;
     const int NT = rows >= 64 ? 8 : (rows + 7) / 8;
     const int MG = (w.MT + 7) / 8;
     const int target = 2 * 148;
+    // split K only as far as needed to fill the GPU, at most kMaxSplits, each split >= one sub-chunk
     int splits = std::max(1, (target + MG * chunks - 1) / (MG * chunks));
-    int kc = (w.KB + splits - 1) / splits;
-    kc = std::max(kc, std::min(4, w.KB));
-    kc = std::min(kc, 16);
-    splits = (w.KB + kc - 1) / kc;
-    while (splits > 1 && (size_t) chunks * splits * w.MT * NT * 32 > scr.ws_elems) {
-        kc *= 2;
-        splits = (w.KB + kc - 1) / kc;
-    }
+    splits = std::min(splits, std::min(kMaxSplits, std::max(1, w.KB / kSub)));
+    int kper = (w.KB + splits - 1) / splits;
+    splits = (w.KB + kper - 1) / kper;
+    if (splits > 1 && (size_t) chunks * splits * w.MT * NT * 32 > scr.ws_elems) throw std::runtime_error("gemv: split-K scratch too small");
     if (splits > 1 && (size_t) chunks * MG > (size_t) scr.n_counters) throw std::runtime_error("gemv: counter scratch too small");
-    if (splits == 1 && kc < w.KB) throw std::runtime_error("gemv: internal tiling error");
     GemvParams p;
-    p.qs = w.qs; p.ds = w.ds; p.MT = w.MT; p.M = w.M; p.KB = w.KB; p.kc = kc; p.splits = splits; p.MG = MG;
+    p.qs = w.qs; p.ds = w.ds; p.MT = w.MT; p.M = w.M; p.KB = w.KB; p.kper = kper; p.splits = splits; p.MG = MG;
     p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.ws = scr.ws; p.counters = scr.counters;
-    const size_t smem = (size_t) kc * NT * 32 * sizeof(uint4);
-    if (smem > 200 * 1024) throw std::runtime_error("gemv: shared memory tile too large");
+    const size_t smem = (size_t) 2 * kSub * NT * 32 * sizeof(uint4);
     dim3 grid(MG, splits, chunks);
     switch (NT) {
         case 1: launch_gemv_nt<1>(p, grid, smem, s); break;

@@ -744,6 +744,19 @@ def sample_philox(logits, temp, top_k, top_p, u: np.float32) -> int:
     return int(order[-1])
 
 
+def sample_margin(logits, temp, top_k, u: np.float32) -> float:
+    """Distance of the sampler's inverse-CDF target from the nearest CDF boundary, as a
+    fraction of the total mass: how far a logit perturbation must move the CDF to change
+    the draw (used to recognise numerical ties in parity tests)."""
+    n = logits.shape[0]
+    keep = top_k if 0 < top_k < n else n
+    order = np.lexsort((np.arange(n), -logits.astype(np.float64)))[:keep]
+    t = np.float64(temp if temp > 0 else 1.0)
+    p = np.exp((logits[order].astype(np.float64) - logits[order[0]]) / t)
+    cdf = np.cumsum(p) / p.sum()
+    return float(np.min(np.abs(cdf - float(u))))
+
+
 class PhiloxStream:
     """Per-session sampler state: seed (key) and draw counter; reseeding resets the counter,
     mirroring std::mt19937::seed in src/c_api.cpp:343, 631, 816."""
@@ -849,8 +862,10 @@ class Generator:
         fr = np.concatenate([cb0[:, None], codes], axis=1)
         ae = m.audio_embed(fr)
         hs, ls = m.backbone_step_batched([s.st for s in ss], ae)
+        self.last_cb0_logits = {}
         for k, (i, s) in enumerate(zip(act, ss)):
             frames[i] = fr[k]
+            self.last_cb0_logits[s.sid] = (apply_penalties(ls[k], 1.1, s.hist, m.cfg.cb_size, m.cfg.vs), s.rng.key, s.rng.draw)
             n = self._sample_cb0(s, ls[k])
             s.steps_taken += 1
             if n == m.cfg.bb_eos or s.steps_taken >= s.max_tokens:

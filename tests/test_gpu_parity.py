@@ -135,7 +135,19 @@ def test_prefill_and_decode_steps_match_oracle(pkg, gen, tiny_oracle):
                 if frames[0][i, j + 1] != int(np.argmax(lg)):
                     assert top2_gap(lg) < TIE_GAP, (step, sid, j, top2_gap(lg))
                     ties += 1
-        assert np.array_equal(nxt, rnxt), (step, nxt, rnxt)
+        for i, sid in enumerate(ids):
+            if nxt[i] != rnxt[i]:
+                # a different draw is only acceptable on a CDF boundary tie of the same uniform
+                pl, key, draw = ref.last_cb0_logits[sid]
+                margin = bo.sample_margin(pl, 0.9, 50, bo.philox_uniform(key, draw))
+                assert margin < 2e-3, (step, sid, nxt[i], rnxt[i], margin)
+                ties += 1
+                rs = ref.sessions[sid]  # follow the engine from here
+                if rnxt[i] >= 0:
+                    rs.hist[int(rnxt[i])] -= 1
+                if nxt[i] >= 0:
+                    rs.hist[int(nxt[i])] = rs.hist.get(int(nxt[i]), 0) + 1
+                    rs.last_cb0 = int(nxt[i])
         for sid in ids:
             if ref.sessions[sid].active:
                 h = gen.debug_hidden(sid, cfg.hidden)
