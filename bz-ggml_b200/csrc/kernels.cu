@@ -8,6 +8,8 @@
 #include "kernels.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <utility>
 #include <cfloat>
 #include <cmath>
 #include <stdexcept>
@@ -23,6 +25,26 @@ namespace bzb {
 
 namespace {
 
+bool pdl_enabled() {
+    static const bool on = [] { const char * e = std::getenv("BZB_PDL"); return !(e && e[0] == '0'); }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    BZB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -33,6 +55,12 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+
+// programmatic dependent launch: every kernel of a step lets the next one start its
+// independent prologue early (trigger) and waits for its predecessor's results (wait)
+// before touching them; the wait is a no-op for launches without the PDL attribute
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ uint4 ld_stream(const uint4 * p) {
     uint4 r;
@@ -104,6 +132,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
     const uint4 * wq = p.qs + ((size_t) mt * p.KB + kb_beg) * 32 + lane;
     const half2 * wd = p.ds + ((size_t) mt * p.KB + kb_beg) * 8 + (lane >> 2);
 
+    pdl_trigger();
     uint4 a[kSub];
     half2 sc[kSub];
 #pragma unroll
@@ -113,6 +142,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
             sc[i] = wd[(size_t) i * 8];
         }
     }
+    pdl_wait();  // weights are constant; activations and outputs belong to the previous kernels
 
     // this thread's NT staged fragments per sub-chunk: fragment f = tid + 256*r covers
     // (k block f / (NT*32), row tile (f / 32) % NT, lane f % 32)
@@ -214,6 +244,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
     if (!mt_ok) return;
 
     const int g = lane >> 2, t = lane & 3;
+    if (EPI == EPI_RESID) {
+        // gather every residual value first so the loads overlap instead of alternating with
+        // stores the compiler cannot prove disjoint
+        float old[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int m = mt * 16 + g + (e >= 2 ? 8 : 0), n = row0 + nt * 8 + 2 * t + (e & 1);
+                old[nt][e] = (m < p.M && n < p.rows) ? p.out.f32[(size_t) n * p.out.ld + m] : 0.0f;
+            }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[nt][e] += old[nt][e];
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int n0 = row0 + nt * 8 + 2 * t;
@@ -222,11 +268,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
             for (int e = 0; e < 4; e++) {
                 const int m = mt * 16 + g + (e >= 2 ? 8 : 0);
                 const int n = n0 + (e & 1);
-                if (m < p.M && n < p.rows) {
-                    float * dst = p.out.f32 + (size_t) n * p.out.ld + m;
-                    if (EPI == EPI_RESID) *dst += acc[nt][e];
-                    else *dst = acc[nt][e];
-                }
+                if (m < p.M && n < p.rows) p.out.f32[(size_t) n * p.out.ld + m] = acc[nt][e];
             }
         } else {
             const int j = mt * 8 + g;
@@ -246,10 +288,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
 template <int NT>
 void launch_gemv_nt(const GemvParams & p, dim3 grid, size_t smem, cudaStream_t s) {
     switch (p.out.kind) {
-        case EPI_STORE: gemv_kernel<NT, EPI_STORE><<<grid, kGemvThreads, smem, s>>>(p); break;
-        case EPI_RESID: gemv_kernel<NT, EPI_RESID><<<grid, kGemvThreads, smem, s>>>(p); break;
-        case EPI_SWIGLU: gemv_kernel<NT, EPI_SWIGLU><<<grid, kGemvThreads, smem, s>>>(p); break;
-        default: gemv_kernel<NT, EPI_GEGLU><<<grid, kGemvThreads, smem, s>>>(p); break;
+        case EPI_STORE: launch_k(gemv_kernel<NT, EPI_STORE>, grid, kGemvThreads, smem, s, p); break;
+        case EPI_RESID: launch_k(gemv_kernel<NT, EPI_RESID>, grid, kGemvThreads, smem, s, p); break;
+        case EPI_SWIGLU: launch_k(gemv_kernel<NT, EPI_SWIGLU>, grid, kGemvThreads, smem, s, p); break;
+        default: launch_k(gemv_kernel<NT, EPI_GEGLU>, grid, kGemvThreads, smem, s, p); break;
     }
 }
 
@@ -264,6 +306,8 @@ void set_gemv_attr() {
 
 // ------------------------------------------------------------------------------------ repack
 __global__ void repack_q8_kernel(const uint8_t * raw, int M, int KB, uint4 * qs, half2 * ds) {
+    pdl_trigger();
+    pdl_wait();
     const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int MT = (M + 15) / 16;
@@ -294,6 +338,8 @@ __global__ void repack_q8_kernel(const uint8_t * raw, int M, int KB, uint4 * qs,
 }
 
 __global__ void split_q8_rows_kernel(const uint8_t * raw, long long n_blocks, int8_t * qs, half * ds) {
+    pdl_trigger();
+    pdl_wait();
     const long long b = (long long) blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= n_blocks) return;
     const uint8_t * src = raw + b * 34;
@@ -315,6 +361,8 @@ __device__ float block_sum(float v, float * red) {
 
 __global__ void rmsnorm_kernel(const float * x, int ldx, const float * w, int D, float eps, half * o16, int ld16,
                                float * o32, int ld32, int r0, const int * row_map) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const int i = blockIdx.x;
     const float4 * xr = reinterpret_cast<const float4 *>(x + (size_t) (r0 + i) * ldx);
@@ -350,6 +398,8 @@ __global__ void rmsnorm_kernel(const float * x, int ldx, const float * w, int D,
 }
 
 __global__ void norm_add_kernel(float * x, const float * t, int D, const float * w, float eps) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const int r = blockIdx.x;
     const float * tr = t + (size_t) r * D;
@@ -362,6 +412,8 @@ __global__ void norm_add_kernel(float * x, const float * t, int D, const float *
 
 // ------------------------------------------------------------------------------------ embeddings
 __global__ void embed_rows_kernel(QRows e, const int * idx, float scale, float * o32, half * o16, int ld) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     int row = idx[r];
     row = (row < 0 || row >= e.rows) ? 0 : row;
@@ -376,6 +428,8 @@ __global__ void embed_rows_kernel(QRows e, const int * idx, float scale, float *
 
 __global__ void audio_embed_kernel(QRows e, const int * frames, int ldf, int nc, int vs, float * out,
                                    const int * row_active) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const bool act = row_active ? row_active[r] != 0 : true;
     for (int k = threadIdx.x; k < e.K; k += blockDim.x) {
@@ -423,88 +477,105 @@ __device__ __forceinline__ size_t paged_off(const AttnKV & kv, const int * page_
     return ((((size_t) page * kv.n_layer + kv.layer) * 2 + kvsel) * n_kv + h) * 16 * HD + (size_t) (p & 15) * HD;
 }
 
-// stages positions [t0, t0+32) of one kv head into shared memory as f32 (zeros past `lim`);
-// every 16-byte load of the tile is issued before any conversion or store
+// K/V tile of 32 positions of one kv head, fetched by the 128 threads of a decode CTA into
+// registers (so the next tile's loads overlap this tile's math) and stored as f32 in shared
+// memory; positions past `lim` read as zero
 template <int HD, bool PAGED>
-__device__ __forceinline__ void stage_kv_tile(float (*sk)[HD + 1], float (*sv)[HD + 1], const AttnKV & kv,
-                                              const int * page_row, int b, int h, int n_kv, int t0, int lim) {
-    constexpr int VEC = PAGED ? 8 : 4;
-    constexpr int PER_ROW = HD / VEC;
-    constexpr int NV = 32 * PER_ROW;
-    constexpr int MAXV = NV / 32;  // per thread with at least one warp
-    const int nthr = blockDim.x;
-    int pg0 = 0, pg1 = 0;
-    if (PAGED) {
-        pg0 = page_row[t0 >> 4];
-        pg1 = ((t0 >> 4) + 1 < kv.max_pages) ? page_row[(t0 >> 4) + 1] : pg0;
-    }
-    for (int kvsel = 0; kvsel < 2; kvsel++) {
-        uint4 buf[MAXV];
-#pragma unroll
-        for (int i = 0; i < MAXV; i++) {
-            const int v = threadIdx.x + i * nthr;
-            buf[i] = make_uint4(0u, 0u, 0u, 0u);
-            if (v < NV) {
-                const int j = v / PER_ROW, c = v - (v / PER_ROW) * PER_ROW;
-                const int p = t0 + j;
-                if (p < lim) {
-                    if (PAGED) {
-                        const int page = (j < 16) ? pg0 : pg1;
-                        const half * src = kv.pool + ((((size_t) page * kv.n_layer + kv.layer) * 2 + kvsel) * n_kv + h) * 16 * HD +
-                                           (size_t) (p & 15) * HD + c * 8;
-                        buf[i] = *reinterpret_cast<const uint4 *>(src);
-                    } else {
-                        const float * src = kv.flat + (((size_t) b * kv.cap + p) * 2 + kvsel) * n_kv * HD + (size_t) h * HD + c * 4;
-                        buf[i] = *reinterpret_cast<const uint4 *>(src);
-                    }
-                }
-            }
+struct KvTileRegs {
+    static constexpr int VEC = PAGED ? 8 : 4;
+    static constexpr int PER_ROW = HD / VEC;
+    static constexpr int NV = 32 * PER_ROW;
+    static constexpr int PT = NV / 128;
+    uint4 k[PT], v[PT];
+
+    __device__ __forceinline__ void load(const AttnKV & kv, const int * page_row, int b, int h, int n_kv, int t0, int lim) {
+        int pg0 = 0, pg1 = 0;
+        if (PAGED) {
+            pg0 = page_row[t0 >> 4];
+            pg1 = ((t0 >> 4) + 1 < kv.max_pages) ? page_row[(t0 >> 4) + 1] : pg0;
         }
-        float (*dst)[HD + 1] = kvsel ? sv : sk;
 #pragma unroll
-        for (int i = 0; i < MAXV; i++) {
-            const int v = threadIdx.x + i * nthr;
-            if (v < NV) {
-                const int j = v / PER_ROW, c = v - (v / PER_ROW) * PER_ROW;
+        for (int i = 0; i < PT; i++) {
+            const int vi = threadIdx.x + i * 128;
+            const int j = vi / PER_ROW, c = vi % PER_ROW;
+            const int p = t0 + j;
+            k[i] = v[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (p < lim) {
                 if (PAGED) {
-                    const half2 * hv = reinterpret_cast<const half2 *>(&buf[i]);
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float2 f = __half22float2(hv[q]);
-                        dst[j][c * 8 + 2 * q] = f.x;
-                        dst[j][c * 8 + 2 * q + 1] = f.y;
-                    }
+                    const int page = (j < 16) ? pg0 : pg1;
+                    const size_t base = ((((size_t) page * kv.n_layer + kv.layer) * 2) * n_kv + h) * 16 * HD +
+                                        (size_t) (p & 15) * HD + c * 8;
+                    const size_t vstride = (size_t) n_kv * 16 * HD;
+                    k[i] = *reinterpret_cast<const uint4 *>(kv.pool + base);
+                    v[i] = *reinterpret_cast<const uint4 *>(kv.pool + base + vstride);
                 } else {
-                    const float * fv = reinterpret_cast<const float *>(&buf[i]);
-#pragma unroll
-                    for (int q = 0; q < 4; q++) dst[j][c * 4 + q] = fv[q];
+                    const size_t base = (((size_t) b * kv.cap + p) * 2) * n_kv * HD + (size_t) h * HD + c * 4;
+                    k[i] = *reinterpret_cast<const uint4 *>(kv.flat + base);
+                    v[i] = *reinterpret_cast<const uint4 *>(kv.flat + base + (size_t) n_kv * HD);
                 }
             }
         }
     }
-}
+
+    __device__ __forceinline__ void store(float (*sk)[HD + 1], float (*sv)[HD + 1]) const {
+#pragma unroll
+        for (int i = 0; i < PT; i++) {
+            const int vi = threadIdx.x + i * 128;
+            const int j = vi / PER_ROW, c = vi % PER_ROW;
+            if (PAGED) {
+                const half2 * hk = reinterpret_cast<const half2 *>(&k[i]);
+                const half2 * hv = reinterpret_cast<const half2 *>(&v[i]);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float2 fk = __half22float2(hk[q]), fv = __half22float2(hv[q]);
+                    sk[j][c * 8 + 2 * q] = fk.x;
+                    sk[j][c * 8 + 2 * q + 1] = fk.y;
+                    sv[j][c * 8 + 2 * q] = fv.x;
+                    sv[j][c * 8 + 2 * q + 1] = fv.y;
+                }
+            } else {
+                const float * fk = reinterpret_cast<const float *>(&k[i]);
+                const float * fv = reinterpret_cast<const float *>(&v[i]);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    sk[j][c * 4 + q] = fk[q];
+                    sv[j][c * 4 + q] = fv[q];
+                }
+            }
+        }
+    }
+};
 
 template <int HD>
 struct DecodeSmem {
     float k[32][HD + 1];
     float v[32][HD + 1];
-    float q[8][2][HD];
+    float q[4][2][HD];
 };
 
+// decode attention for one session and one kv head: 128 threads; warp w < G (the GQA group,
+// at most 4) owns query head h*G + w. The CTA first normalises, rotates and appends the new
+// tokens' keys and values (1 token, or 2 for the depth decoder's first sub-step), then runs an
+// online softmax over 32-position tiles of the session's cache.
 template <int HD, bool PAGED>
-__global__ void attn_decode_kernel(const AttnDecodeArgs a) {
+__global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeArgs a) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int E = HD / 32;
     __shared__ DecodeSmem<HD> sm;
     const int b = blockIdx.x, h = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = a.n_head / a.n_kv;
+    const bool qwarp = warp < G;
     const int slot = a.row_slot ? a.row_slot[b] : b;
     const bool act = (a.row_active ? a.row_active[b] != 0 : true) && slot >= 0;
     const int n_new = a.n_new;
     const int qh = h * G + warp;
     if (!act) {
-        for (int i = 0; i < n_new; i++)
-            for (int e = 0; e < E; e++)
-                a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(0.0f);
+        if (qwarp)
+            for (int i = 0; i < n_new; i++)
+                for (int e = 0; e < E; e++)
+                    a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(0.0f);
         return;
     }
     const int start = a.st ? a.st[slot].pos : a.start;
@@ -512,7 +583,7 @@ __global__ void attn_decode_kernel(const AttnDecodeArgs a) {
     const int * page_row = PAGED ? a.kv.page_table + (size_t) slot * a.kv.max_pages : nullptr;
 
     // 1. normalise, rotate and append the new tokens' keys and values
-    for (int task = warp; task < 2 * n_new; task += G) {
+    for (int task = warp; task < 2 * n_new; task += 4) {
         const int i = task >> 1;
         const int isv = task & 1;
         const int row = b + i * a.R;
@@ -536,16 +607,20 @@ __global__ void attn_decode_kernel(const AttnDecodeArgs a) {
         }
     }
     // 2. this warp's query head for each new token
-    for (int i = 0; i < n_new; i++) {
-        const float * src = a.qkv + (size_t) (b + i * a.R) * a.ldq + qh * HD;
-        float x[E];
+    if (qwarp) {
+        for (int i = 0; i < n_new; i++) {
+            const float * src = a.qkv + (size_t) (b + i * a.R) * a.ldq + qh * HD;
+            float x[E];
 #pragma unroll
-        for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
-        if (a.q_norm) head_rmsnorm<HD>(x, a.q_norm, a.eps, lane);
-        rope_apply<HD>(x, a.rope + (size_t) (start + i) * (HD / 2), lane);
+            for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
+            if (a.q_norm) head_rmsnorm<HD>(x, a.q_norm, a.eps, lane);
+            rope_apply<HD>(x, a.rope + (size_t) (start + i) * (HD / 2), lane);
 #pragma unroll
-        for (int e = 0; e < E; e++) sm.q[warp][i][lane + 32 * e] = x[e];
+            for (int e = 0; e < E; e++) sm.q[warp][i][lane + 32 * e] = x[e];
+        }
     }
+    __syncthreads();  // appended keys/values visible to the whole CTA before the first tile load
+
     float m[2] = { -INFINITY, -INFINITY }, l[2] = { 0.0f, 0.0f };
     float acc[2][E];
 #pragma unroll
@@ -553,10 +628,14 @@ __global__ void attn_decode_kernel(const AttnDecodeArgs a) {
 #pragma unroll
         for (int e = 0; e < E; e++) acc[i][e] = 0.0f;
 
+    KvTileRegs<HD, PAGED> regs;
+    regs.load(a.kv, page_row, b, h, a.n_kv, 0, L);
     for (int t0 = 0; t0 < L; t0 += 32) {
         __syncthreads();
-        stage_kv_tile<HD, PAGED>(sm.k, sm.v, a.kv, page_row, b, h, a.n_kv, t0, L);
+        regs.store(sm.k, sm.v);
         __syncthreads();
+        if (t0 + 32 < L) regs.load(a.kv, page_row, b, h, a.n_kv, t0 + 32, L);
+        if (!qwarp) continue;
 #pragma unroll
         for (int i = 0; i < 2; i++) {
             if (i >= n_new) break;
@@ -586,6 +665,7 @@ __global__ void attn_decode_kernel(const AttnDecodeArgs a) {
             m[i] = mn;
         }
     }
+    if (!qwarp) return;
 #pragma unroll
     for (int i = 0; i < 2; i++) {
         if (i >= n_new) break;
@@ -599,6 +679,8 @@ __global__ void attn_decode_kernel(const AttnDecodeArgs a) {
 // prefill: normalise/rotate q in place, k likewise, and write k,v to the cache or flat buffers
 template <int HD, bool PAGED>
 __global__ void qk_prep_kernel(const PrefillArgs a) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int E = HD / 32;
     const int r = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -636,6 +718,8 @@ constexpr int kPrefillQB = 8;
 
 template <int HD, bool PAGED>
 __global__ void attn_prefill_kernel(const PrefillArgs a) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int E = HD / 32;
     constexpr int QB = kPrefillQB;
     extern __shared__ float psm[];
@@ -733,6 +817,8 @@ __global__ void attn_prefill_kernel(const PrefillArgs a) {
 
 // ------------------------------------------------------------------------------------ step glue
 __global__ void step_init_kernel(const StepArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const int slot = a.row_slot[r];
     const bool act = slot >= 0 && a.st[slot].active != 0;
@@ -772,6 +858,8 @@ __device__ __forceinline__ void embed_row_f16(const QRows & e, size_t row, half 
 }
 
 __global__ void argmax_gather_kernel(const StepArgs a, const float * logits, int ld, int V, int col, int gather_cb) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ int s_code;
@@ -817,6 +905,8 @@ __device__ __forceinline__ unsigned int f2ord(float f) {
 constexpr int kSortN = 4096;
 
 __global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ unsigned long long keys[kSortN];
     __shared__ float lmod[kSortN];
     const int r = blockIdx.x;
@@ -921,6 +1011,8 @@ __global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
 }
 
 __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ctr) {
+    pdl_trigger();
+    pdl_wait();
     const int k = *ctr;
     for (int i = threadIdx.x; i < n; i += blockDim.x) all[(size_t) k * n + i] = cur[i];
     __syncthreads();
@@ -930,6 +1022,7 @@ __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ct
 }  // namespace
 
 // ------------------------------------------------------------------------------------ launchers
+
 void init_kernel_attributes() {
     set_gemv_attr<1>(); set_gemv_attr<2>(); set_gemv_attr<3>(); set_gemv_attr<4>();
     set_gemv_attr<5>(); set_gemv_attr<6>(); set_gemv_attr<7>(); set_gemv_attr<8>();
@@ -943,9 +1036,10 @@ void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const Gemv
     const int chunks = (rows + 63) / 64;
     const int NT = rows >= 64 ? 8 : (rows + 7) / 8;
     const int MG = (w.MT + 7) / 8;
-    const int target = 2 * 148;
-    // split K only as far as needed to fill the GPU, at most kMaxSplits, each split >= one sub-chunk
-    int splits = std::max(1, (target + MG * chunks - 1) / (MG * chunks));
+    // split K only as far as needed to fill one wave (2 CTAs on each of the 148 SMs), at most
+    // kMaxSplits, each split at least one sub-chunk
+    const int wave = 2 * 148;
+    int splits = std::max(1, wave / (MG * chunks));
     splits = std::min(splits, std::min(kMaxSplits, std::max(1, w.KB / kSub)));
     int kper = (w.KB + splits - 1) / splits;
     splits = (w.KB + kper - 1) / kper;
@@ -974,55 +1068,55 @@ void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cu
     const long long warps = (long long) MT * KB;
     const int threads = 256;
     const long long blocks = (warps * 32 + threads - 1) / threads;
-    repack_q8_kernel<<<(unsigned) blocks, threads, 0, s>>>(raw_dev, M, KB, qs, ds);
+    launch_k(repack_q8_kernel, (unsigned) blocks, threads, 0, s, raw_dev, M, KB, qs, ds);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s) {
     const long long nb = (long long) rows * (K / 32);
-    split_q8_rows_kernel<<<(unsigned) ((nb + 255) / 256), 256, 0, s>>>(raw_dev, nb, qs, ds);
+    launch_k(split_q8_rows_kernel, (unsigned) ((nb + 255) / 256), 256, 0, s, raw_dev, nb, qs, ds);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps, half * out16, int ld16,
                     float * out32, int ld32, int r0, int n, const int * row_map, cudaStream_t s) {
     if (n <= 0) return;
-    rmsnorm_kernel<<<n, 256, 0, s>>>(x, ldx, w, D, eps, out16, ld16, out32, ld32, r0, row_map);
+    launch_k(rmsnorm_kernel, n, 256, 0, s, x, ldx, w, D, eps, out16, ld16, out32, ld32, r0, row_map);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_norm_add(float * x, const float * t, int D, const float * w, float eps, int rows, cudaStream_t s) {
     if (rows <= 0) return;
-    norm_add_kernel<<<rows, 256, 0, s>>>(x, t, D, w, eps);
+    launch_k(norm_add_kernel, rows, 256, 0, s, x, t, D, w, eps);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_embed_rows(const QRows & e, const int * idx, int n, float scale, float * out32, half * out16, int ld,
                        cudaStream_t s) {
     if (n <= 0) return;
-    embed_rows_kernel<<<n, 256, 0, s>>>(e, idx, scale, out32, out16, ld);
+    launch_k(embed_rows_kernel, n, 256, 0, s, e, idx, scale, out32, out16, ld);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_audio_embed(const QRows & e, const int * frames, int ld_frames, int nc, int vs, int n, float * out32,
                         const int * row_active, cudaStream_t s) {
     if (n <= 0) return;
-    audio_embed_kernel<<<n, 256, 0, s>>>(e, frames, ld_frames, nc, vs, out32, row_active);
+    launch_k(audio_embed_kernel, n, 256, 0, s, e, frames, ld_frames, nc, vs, out32, row_active);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s) {
     const int G = a.n_head / a.n_kv;
-    if (G < 1 || G > 8 || a.n_head % a.n_kv) throw std::runtime_error("attention: unsupported head grouping");
+    if (G < 1 || G > 4 || a.n_head % a.n_kv) throw std::runtime_error("decode attention: query heads per kv head must be 1..4");
     if (a.n_new < 1 || a.n_new > 2) throw std::runtime_error("attention: 1 or 2 new tokens per session");
     dim3 grid(a.R, a.n_kv);
-    const int threads = 32 * G;
+    const int threads = 128;
     if (a.hd == 64) {
-        if (paged) attn_decode_kernel<64, true><<<grid, threads, 0, s>>>(a);
-        else attn_decode_kernel<64, false><<<grid, threads, 0, s>>>(a);
+        if (paged) launch_k(attn_decode_kernel<64, true>, grid, threads, 0, s, a);
+        else launch_k(attn_decode_kernel<64, false>, grid, threads, 0, s, a);
     } else if (a.hd == 128) {
-        if (paged) attn_decode_kernel<128, true><<<grid, threads, 0, s>>>(a);
-        else attn_decode_kernel<128, false><<<grid, threads, 0, s>>>(a);
+        if (paged) launch_k(attn_decode_kernel<128, true>, grid, threads, 0, s, a);
+        else launch_k(attn_decode_kernel<128, false>, grid, threads, 0, s, a);
     } else throw std::runtime_error("attention: head_dim must be 64 or 128 for decode");
     BZB_CUDA_CHECK(cudaGetLastError());
 }
@@ -1030,9 +1124,9 @@ void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s) {
 void launch_qk_prep(const PrefillArgs & a, bool paged, cudaStream_t s) {
     if (a.T <= 0) return;
     switch (a.hd) {
-        case 64: if (paged) qk_prep_kernel<64, true><<<a.T, 128, 0, s>>>(a); else qk_prep_kernel<64, false><<<a.T, 128, 0, s>>>(a); break;
-        case 128: if (paged) qk_prep_kernel<128, true><<<a.T, 128, 0, s>>>(a); else qk_prep_kernel<128, false><<<a.T, 128, 0, s>>>(a); break;
-        case 256: if (paged) qk_prep_kernel<256, true><<<a.T, 128, 0, s>>>(a); else qk_prep_kernel<256, false><<<a.T, 128, 0, s>>>(a); break;
+        case 64: if (paged) launch_k(qk_prep_kernel<64, true>, a.T, 128, 0, s, a); else launch_k(qk_prep_kernel<64, false>, a.T, 128, 0, s, a); break;
+        case 128: if (paged) launch_k(qk_prep_kernel<128, true>, a.T, 128, 0, s, a); else launch_k(qk_prep_kernel<128, false>, a.T, 128, 0, s, a); break;
+        case 256: if (paged) launch_k(qk_prep_kernel<256, true>, a.T, 128, 0, s, a); else launch_k(qk_prep_kernel<256, false>, a.T, 128, 0, s, a); break;
         default: throw std::runtime_error("prefill: head_dim must be 64, 128 or 256");
     }
     BZB_CUDA_CHECK(cudaGetLastError());
@@ -1043,7 +1137,7 @@ static void launch_prefill_t(const PrefillArgs & a, int G, cudaStream_t s) {
     const size_t smem = (size_t) (2 * 32 * (HD + 1) + G * kPrefillQB * HD) * sizeof(float);
     cudaFuncSetAttribute(attn_prefill_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     dim3 grid((a.T + kPrefillQB - 1) / kPrefillQB, a.n_kv);
-    attn_prefill_kernel<HD, PAGED><<<grid, 32 * G, smem, s>>>(a);
+    launch_k(attn_prefill_kernel<HD, PAGED>, grid, 32 * G, smem, s, a);
 }
 
 void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s) {
@@ -1060,24 +1154,24 @@ void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s) {
 }
 
 void launch_step_init(const StepArgs & a, cudaStream_t s) {
-    step_init_kernel<<<a.R, 256, 0, s>>>(a);
+    launch_k(step_init_kernel, a.R, 256, 0, s, a);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_argmax_gather(const StepArgs & a, const float * logits, int ld, int V, int col, int gather_cb,
                           cudaStream_t s) {
-    argmax_gather_kernel<<<a.R, 256, 0, s>>>(a, logits, ld, V, col, gather_cb);
+    launch_k(argmax_gather_kernel, a.R, 256, 0, s, a, logits, ld, V, col, gather_cb);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_sample(const SampleArgs & a, cudaStream_t s) {
     if (a.V > kSortN) throw std::runtime_error("sampler: vocabulary larger than 4096");
-    sample_kernel<<<a.R, 1024, 0, s>>>(a);
+    launch_k(sample_kernel, a.R, 1024, 0, s, a);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s) {
-    frames_commit_kernel<<<1, 256, 0, s>>>(cur, frames_all, n, step_ctr);
+    launch_k(frames_commit_kernel, 1, 256, 0, s, cur, frames_all, n, step_ctr);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
