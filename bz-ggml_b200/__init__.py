@@ -91,6 +91,8 @@ SIGNATURES = {
                                                  _c_int_p, _c_float_p]),
     "bzb_generator_debug_gemv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                 _c_float_p, _c_float_p]),
+    "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_int]),
     "bzb_gguf_inspect": (ctypes.c_int, [ctypes.c_char_p, _c_int_p, _c_int_p, _c_int_p]),
     "bzb_tokenize": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, _c_int_p, ctypes.c_int]),
 }
@@ -259,6 +261,12 @@ class GeneratorHandle:
         if self.lib.lib.bzb_generator_profile_step(self.handle, out) != 0:
             raise RuntimeError(self.lib.last_error())
         return dict(step_ms=out[0], gemm_ms=out[1], gemm_launches=int(out[2]), gemm_bytes=out[3])
+
+    def bench_gemv(self, tensor: str, rows: int, iters: int = 50, epilogue: int = 0, sub: int = -1) -> float:
+        us = self.lib.lib.bzb_generator_bench_gemv(self.handle, tensor.encode(), sub, rows, iters, epilogue)
+        if us < 0:
+            raise RuntimeError(self.lib.last_error())
+        return us
 
     def debug_hidden(self, session_id: int, hidden: int) -> np.ndarray:
         out = np.zeros(hidden, np.float32)

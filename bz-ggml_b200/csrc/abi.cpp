@@ -476,6 +476,16 @@ int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int su
     }
 }
 
+double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters, int epilogue) {
+    if (!gen || !tensor || rows <= 0 || iters <= 0) return -1.0;
+    try {
+        return gen->eng->bench_gemv(tensor, sub, rows, iters, epilogue);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1.0;
+    }
+}
+
 int bzb_gguf_inspect(const char * gguf_path, int * out_hidden, int * out_num_codebooks, int * out_n_tensors) {
     if (!gguf_path) return -1;
     try {

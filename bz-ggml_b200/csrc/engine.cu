@@ -476,13 +476,16 @@ cudaGraphExec_t Engine::graph_for(int R) {
     if (it != graphs_.end()) return it->second;
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    set_pdl_scope(true);
     try {
         enqueue_step(R);
     } catch (...) {
+        set_pdl_scope(false);
         cudaStreamEndCapture(stream_, &g);
         if (g) cudaGraphDestroy(g);
         throw;
     }
+    set_pdl_scope(false);
     CK(cudaStreamEndCapture(stream_, &g));
     size_t n_nodes = 0;
     CK(cudaGraphGetNodes(g, nullptr, &n_nodes));
@@ -883,6 +886,33 @@ void Engine::profile_step(double * out) {
     out[2] = (double) recs.size();
     out[3] = bytes;
     out[4] = (double) launches_;
+}
+
+double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int epi) {
+    const GgufTensor * t = need(tensor);
+    QMat w = sub >= 0 ? load_qmat({ t }, false, (int) (sub * t->ne[1]), (int) t->ne[1]) : load_qmat({ t }, false);
+    half * xd = nullptr;
+    float * yd = nullptr;
+    CK(cudaMalloc(&xd, (size_t) rows * w.K * sizeof(half)));
+    CK(cudaMalloc(&yd, (size_t) rows * w.M * sizeof(float)));
+    CK(cudaMemsetAsync(xd, 0, (size_t) rows * w.K * sizeof(half), stream_));
+    CK(cudaMemsetAsync(yd, 0, (size_t) rows * w.M * sizeof(float), stream_));
+    GemvOut o{ epi, yd, (half *) yd, epi >= EPI_SWIGLU ? w.M / 2 : w.M };
+    cudaEvent_t a, b;
+    CK(cudaEventCreate(&a));
+    CK(cudaEventCreate(&b));
+    for (int i = 0; i < 3; i++) launch_gemv(w, xd, w.K, rows, o, scr_, stream_);
+    CK(cudaEventRecord(a, stream_));
+    for (int i = 0; i < iters; i++) launch_gemv(w, xd, w.K, rows, o, scr_, stream_);
+    CK(cudaEventRecord(b, stream_));
+    CK(cudaEventSynchronize(b));
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaFree(xd);
+    cudaFree(yd);
+    return ms * 1000.0 / iters;
 }
 
 size_t Engine::weight_bytes_per_step() const {

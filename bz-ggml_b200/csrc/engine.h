@@ -70,6 +70,8 @@ public:
     // one eager frame step of the current batch with CUDA events around every dequant-GEMM:
     // out = {step_ms, gemm_ms, gemm_launches, gemm_algorithmic_bytes, launches}
     void profile_step(double * out);
+    // average microseconds of `iters` back-to-back launches of one dequant-GEMM (epilogue kind)
+    double bench_gemv(const char * tensor, int sub, int rows, int iters, int epi);
     size_t weight_bytes_per_step() const;
     size_t kv_bytes_per_position() const;
 

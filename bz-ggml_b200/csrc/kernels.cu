@@ -25,9 +25,13 @@ namespace bzb {
 
 namespace {
 
+// PDL is switched on only while a step graph is being captured, whose nodes are all kernels;
+// eager sequences interleave host copies, which keep plain stream ordering
+thread_local bool g_pdl_scope = false;
+
 bool pdl_enabled() {
-    static const bool on = [] { const char * e = std::getenv("BZB_PDL"); return !(e && e[0] == '0'); }();
-    return on;
+    static const bool allowed = [] { const char * e = std::getenv("BZB_PDL"); return !(e && e[0] == '0'); }();
+    return allowed && g_pdl_scope;
 }
 
 template <typename... KArgs, typename... Args>
@@ -111,7 +115,9 @@ constexpr int kGemvThreads = 256;
 constexpr int kSub = 8;        // k32 blocks per staged activation sub-chunk (= weight prefetch depth)
 constexpr int kMaxSplits = 8;
 
-__device__ __forceinline__ uint32_t ldg32(const half * p) { return __ldg(reinterpret_cast<const unsigned int *>(p)); }
+// activations are written by the previous kernel while this one may already be running
+// (programmatic dependent launch), so they are read with coherent loads, never ld.global.nc
+__device__ __forceinline__ uint32_t ldg32(const half * p) { return *reinterpret_cast<const unsigned int *>(p); }
 
 // Each CTA owns 8 m16 row tiles (one per warp), one 64-row activation chunk and a K range.
 // Activations for kSub k32 blocks are staged in shared memory in mma B-fragment order, double
@@ -1023,6 +1029,8 @@ __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ct
 
 // ------------------------------------------------------------------------------------ launchers
 
+void set_pdl_scope(bool on) { g_pdl_scope = on; }
+
 void init_kernel_attributes() {
     set_gemv_attr<1>(); set_gemv_attr<2>(); set_gemv_attr<3>(); set_gemv_attr<4>();
     set_gemv_attr<5>(); set_gemv_attr<6>(); set_gemv_attr<7>(); set_gemv_attr<8>();
@@ -1041,6 +1049,7 @@ void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const Gemv
     const int wave = 2 * 148;
     int splits = std::max(1, wave / (MG * chunks));
     splits = std::min(splits, std::min(kMaxSplits, std::max(1, w.KB / kSub)));
+    if (const char * e = std::getenv("BZB_GEMV_SPLITS")) splits = std::max(1, std::min(kMaxSplits, std::atoi(e)));
     int kper = (w.KB + splits - 1) / splits;
     splits = (w.KB + kper - 1) / kper;
     if (splits > 1 && (size_t) chunks * splits * w.MT * NT * 32 > scr.ws_elems) throw std::runtime_error("gemv: split-K scratch too small");

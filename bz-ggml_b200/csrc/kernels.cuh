@@ -53,6 +53,8 @@ struct GemvScratch {
 
 // sets the kernels' shared-memory limits; once per device before the first launch or capture
 void init_kernel_attributes();
+// launches of this thread use programmatic dependent launch while `on` (graph capture only)
+void set_pdl_scope(bool on);
 
 // y[rows, M] = x16[rows, K] . W^T with the chosen epilogue; rows may exceed 64 (column chunks)
 void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out,

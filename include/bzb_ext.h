@@ -52,6 +52,11 @@ BREEZE_API int bzb_generator_debug_depth(breeze_generator * gen, int n, const fl
 BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int sub, int rows,
                                         const float * x, float * y);
 
+/* average microseconds of back-to-back launches of one dequant-GEMM of a named Q8_0 tensor on
+   `rows` activation rows (epilogue 0 store, 1 residual add, 2 SwiGLU, 3 GeGLU), or -1 */
+BREEZE_API double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters,
+                                           int epilogue);
+
 /* GGUF inspection without a GPU: 0 and the config values, or -1 with breeze_last_error() */
 BREEZE_API int bzb_gguf_inspect(const char * gguf_path, int * out_hidden, int * out_num_codebooks,
                                 int * out_n_tensors);
