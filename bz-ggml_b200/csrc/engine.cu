@@ -134,10 +134,35 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
     uint4 * qs = dalloc<uint4>((size_t) q.MT * KB * 32);
     half2 * ds = dalloc<half2>((size_t) q.MT * KB * 8);
     repack_q8(raw_dev, M, K, qs, ds, stream_);
-    CK(cudaStreamSynchronize(stream_));
-    CK(cudaFree(raw_dev));
     q.qs = qs;
     q.ds = ds;
+    if (K % 64 == 0) {
+        // the tcgen05 layout pairs gate/up rows in 16-row groups instead of 8
+        if (interleave_pairs) {
+            const int F = M / 2;
+            for (int p = 0; p < M; p++) {
+                const int grp = p / 32, r = p % 32;
+                const GgufTensor * t = r < 16 ? parts[0] : parts[1];
+                std::memcpy(raw.data() + (size_t) p * row_bytes, gg_.data(*t) + (size_t) (grp * 16 + (r & 15)) * row_bytes, row_bytes);
+            }
+            if (F % 16) throw std::runtime_error("gate/up rows must be a multiple of 16");
+            CK(cudaStreamSynchronize(stream_));
+            CK(cudaMemcpyAsync(raw_dev, raw.data(), raw.size(), cudaMemcpyHostToDevice, stream_));
+        }
+        UMat u;
+        u.M = M;
+        u.MT = (M + 127) / 128;
+        u.K = K;
+        u.KC = K / 64;
+        uint4 * uq = dalloc<uint4>((size_t) u.MT * u.KC * 4 * 128);
+        half * ud = dalloc<half>((size_t) u.MT * u.KC * 2 * 128);
+        repack_umma(raw_dev, M, K, uq, ud, stream_);
+        u.qs = uq;
+        u.ds = ud;
+        q.u = u;
+    }
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaFree(raw_dev));
     return q;
 }
 
@@ -172,6 +197,11 @@ Engine::Engine(const std::string & path, int dev) : device(dev) {
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     init_kernel_attributes();
+    init_umma_attributes();
+    {
+        const char * e = std::getenv("BZB_GEMM");
+        use_umma_ = !(e && std::string(e) == "mma");
+    }
     std::string err;
     if (!gg_.open(path, err)) throw std::runtime_error(err);
     cfg = parse_config(gg_);
@@ -320,6 +350,8 @@ void Engine::alloc_buffers() {
     step_ctr_ = dalloc<int>(1);
     any_active_ = dalloc<int>(kmax_);
     slot_scalar_ = dalloc<int>(1);
+    err_ = dalloc<int>(1);
+    CK(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
     din16_ = dalloc<half>((size_t) R2 * H);
     dx_ = dalloc<float>((size_t) R2 * dd.hidden);
     dh16_ = dalloc<half>((size_t) R2 * dd.hidden);
@@ -377,10 +409,15 @@ void Engine::ensure_prefill_capacity(int T) {
 }
 
 // ------------------------------------------------------------------------------------ step
+void Engine::launch_gemm(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
+    if (use_umma_ && w.u.qs && ldx % 8 == 0) launch_umma_gemm(w.u, x16, ldx, rows, out, err_, stream_, pdl_scope());
+    else launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+}
+
 void Engine::gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
     launches_++;
     if (!prof_) {
-        launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+        launch_gemm(w, x16, ldx, rows, out);
         return;
     }
     ProfRec r;
@@ -389,7 +426,7 @@ void Engine::gemv(const QMat & w, const half * x16, int ldx, int rows, const Gem
     const double out_bytes = (double) rows * (out.kind == EPI_STORE || out.kind == EPI_RESID ? w.M * 4.0 : w.M);
     r.bytes = (double) w.M * w.K / 32.0 * 34.0 + (double) rows * w.K * 2.0 + out_bytes;
     CK(cudaEventRecord(r.a, stream_));
-    launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+    launch_gemm(w, x16, ldx, rows, out);
     CK(cudaEventRecord(r.b, stream_));
     prof_->push_back(r);
 }
@@ -536,7 +573,10 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     CK(cudaMemcpyAsync(fr.data(), frames_all_, fr.size() * sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaMemcpyAsync(nx.data(), next_, R * sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaMemcpyAsync(aa.data(), any_active_, K * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    int errv = 0;
+    CK(cudaMemcpyAsync(&errv, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    if (errv) throw std::runtime_error("a tensor-core pipeline wait timed out inside the frame step");
     for (int k = 0; k < K; k++) res.steps_executed += aa[k] ? 1 : 0;
     const int wcopy = std::min(width, nc);
     for (int k = 0; k < K; k++) {
@@ -842,7 +882,7 @@ void Engine::debug_gemv(const char * tensor, int sub, int rows, const float * x,
     CK(cudaMalloc(&xd, xh.size() * sizeof(half)));
     CK(cudaMalloc(&yd, (size_t) rows * M * sizeof(float)));
     CK(cudaMemcpyAsync(xd, xh.data(), xh.size() * sizeof(half), cudaMemcpyHostToDevice, stream_));
-    launch_gemv(w, xd, K, rows, GemvOut{ EPI_STORE, yd, nullptr, M }, scr_, stream_);
+    launch_gemm(w, xd, K, rows, GemvOut{ EPI_STORE, yd, nullptr, M });
     CK(cudaMemcpyAsync(y, yd, (size_t) rows * M * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
     cudaFree(xd);
@@ -901,9 +941,9 @@ double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int
     cudaEvent_t a, b;
     CK(cudaEventCreate(&a));
     CK(cudaEventCreate(&b));
-    for (int i = 0; i < 3; i++) launch_gemv(w, xd, w.K, rows, o, scr_, stream_);
+    for (int i = 0; i < 3; i++) launch_gemm(w, xd, w.K, rows, o);
     CK(cudaEventRecord(a, stream_));
-    for (int i = 0; i < iters; i++) launch_gemv(w, xd, w.K, rows, o, scr_, stream_);
+    for (int i = 0; i < iters; i++) launch_gemm(w, xd, w.K, rows, o);
     CK(cudaEventRecord(b, stream_));
     CK(cudaEventSynchronize(b));
     float ms = 0.0f;

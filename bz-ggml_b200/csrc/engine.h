@@ -90,6 +90,7 @@ private:
 
     // execution
     void gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out);
+    void launch_gemm(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out);
     void enqueue_step(int R);
     void depth_layer(int l, int rows, int R, int n_new, int start);
     void bb_decode_layer(int l, int R);
@@ -159,6 +160,8 @@ private:
     std::vector<ProfRec> * prof_ = nullptr;
     int launches_ = 0;
     int graph_nodes_ = 0;
+    bool use_umma_ = true;
+    int * err_ = nullptr;
 };
 
 }  // namespace bzb

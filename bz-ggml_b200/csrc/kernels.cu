@@ -1030,6 +1030,7 @@ __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ct
 // ------------------------------------------------------------------------------------ launchers
 
 void set_pdl_scope(bool on) { g_pdl_scope = on; }
+bool pdl_scope() { return pdl_enabled(); }
 
 void init_kernel_attributes() {
     set_gemv_attr<1>(); set_gemv_attr<2>(); set_gemv_attr<3>(); set_gemv_attr<4>();

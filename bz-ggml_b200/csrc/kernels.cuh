@@ -10,10 +10,22 @@ namespace bzb {
 // Q8_0 weight matrix [M rows, K] repacked for the dequant-GEMM: for each 16-row tile and
 // 32-wide K block, 32 lanes x 16 bytes laid out as the lanes' mma.m16n8k16 A fragments
 // (two k16 halves), plus one half2 (scale of row g, scale of row g+8) per lane group.
+
+
+// the same Q8_0 matrix in the tcgen05 kernel's layout: for each 128-row tile and 64-wide K
+// chunk, 4 x 128 rows x 16 bytes of int8 (piece (block half, 16-byte half) major, row minor)
+// and 2 x 128 f16 block scales; gate/up pairs interleave in 16-row groups
+struct UMat {
+    const uint4 * qs = nullptr;
+    const half * ds = nullptr;
+    int M = 0, MT = 0, K = 0, KC = 0;
+};
+
 struct QMat {
     const uint4 * qs = nullptr;    // [MT][KB][32] uint4
     const half2 * ds = nullptr;    // [MT][KB][8]
     int M = 0, MT = 0, K = 0, KB = 0;
+    UMat u;                        // tcgen05 layout of the same weights (when K % 64 == 0)
 };
 
 // Q8_0 rows kept for row gathers (embeddings): int8 values and f16 block scales.
@@ -61,6 +73,14 @@ void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const Gemv
                  const GemvScratch & scr, cudaStream_t s);
 
 void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s);
+
+// tcgen05 dequant-GEMM (umma_gemm.cu): same contract as launch_gemv; `err` receives 1 if a
+// bounded pipeline wait gave up
+void init_umma_attributes();
+void repack_umma(const uint8_t * raw_dev, int M, int K, uint4 * qs, half * ds, cudaStream_t s);
+void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const GemvOut & out, int * err,
+                      cudaStream_t s, bool pdl);
+bool pdl_scope();
 void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s);
 
 // out16[r] = f16(rmsnorm(x[r]) * w) (and out32 when non-null) for rows [r0, r0 + n)

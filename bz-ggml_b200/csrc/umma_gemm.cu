@@ -1,0 +1,572 @@
+// tcgen05 (5th-generation tensor core) dequant-GEMM for Q8_0 weights, sm_100a.
+//
+// y[rows, M] = x[rows, K] . W^T with W stored as Q8_0. Each CTA owns one 128-row weight tile
+// (the MMA's M), up to 64 activation rows (the MMA's N) and a K range, processed in 64-wide
+// chunks by a warp-specialised pipeline:
+//   * a loader warp streams each chunk's int8 weights and block scales (8.5 KB, contiguous in
+//     the repacked layout) with 1-D bulk async copies into a 4-deep raw ring;
+//   * a second loader warp brings the activation rows with 2-D TMA tensor loads that write the
+//     128-byte-swizzled K-major layout the MMA reads;
+//   * 8 producer warps dequantise the raw ring (one Q8_0 block of one weight row per thread)
+//     into the swizzled f16 A stage;
+//   * one MMA warp issues four tcgen05.mma.cta_group::1.kind::f16 (128 x N x 16) per chunk into
+//     a TMEM accumulator and commits them to the stage's "empty" barrier.
+// Every hand-over is an mbarrier; no thread holds global loads in flight across a fence.
+// Split-K partials of one tile are reduced on chip: the splits form a thread-block cluster and
+// each CTA sums its slice of rows from every peer's shared memory in rank order.
+#include "kernels.cuh"
+
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <stdexcept>
+#include <string>
+
+namespace cg = cooperative_groups;
+
+namespace bzb {
+
+namespace {
+
+constexpr int kTileM = 128;     // weight rows per CTA (MMA M)
+constexpr int kChunkK = 64;     // K per stage: one 128-byte swizzle atom of f16
+constexpr int kThreads = 256;
+constexpr int kABytes = kTileM * kChunkK * 2;
+constexpr long long kSpinLimit = 1ll << 22;
+
+#define UCHECK(x)                                                                             \
+    do {                                                                                      \
+        cudaError_t e_ = (x);                                                                 \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA: ") + cudaGetErrorString(e_) + " at " #x); \
+    } while (0)
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) { return (uint32_t) __cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// bounded wait for the completion of the mbarrier phase with the given parity; returns false
+// (and records the failure) when the limit is reached instead of spinning forever
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int * err) {
+    const uint32_t a = smem_u32(bar);
+    for (long long i = 0; i < kSpinLimit; i++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    if (err) atomicExch(err, 1);
+    return false;
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t * slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// K-major operand in the 128-byte swizzle layout: 8-row atoms of 1024 bytes stacked along M/N
+// (stride byte offset 1024), descriptor version 1, layout type SWIZZLE_128B
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t) ((addr & 0x3FFFF) >> 4) | ((uint64_t) 1 << 16) | ((uint64_t) (1024 >> 4) << 32) |
+           ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float * v) {
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 4 int8 -> two half2 in natural order, scaled
+__device__ __forceinline__ void dq4(uint32_t w, half2 s, uint32_t & lo, uint32_t & hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    uint32_t l = __byte_perm(u, 0x64646464u, 0x5140u);
+    uint32_t h = __byte_perm(u, 0x64646464u, 0x7362u);
+    const half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    half2 hl = __hmul2(__hsub2(*reinterpret_cast<half2 *>(&l), bias), s);
+    half2 hh = __hmul2(__hsub2(*reinterpret_cast<half2 *>(&h), bias), s);
+    lo = *reinterpret_cast<uint32_t *>(&hl);
+    hi = *reinterpret_cast<uint32_t *>(&hh);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    const float c = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(c * x * (1.0f + 0.044715f * x * x)));
+}
+
+struct UParams {
+    const uint4 * qs;
+    const half * ds;
+    int M, MT, KC, kc_per_split, splits;
+    const half * x;
+    int ldx, rows;
+    GemvOut out;
+    int * err;
+};
+
+// epilogue of one output element pair source: value v for (row n, weight row m)
+template <int EPI>
+__device__ __forceinline__ void store_out(const UParams & p, int n, int m, float v) {
+    float * dst = p.out.f32 + (size_t) n * p.out.ld + m;
+    if (EPI == EPI_RESID) *dst += v;
+    else *dst = v;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+
+// roles: warps 0-7 dequantise, warp 8 issues MMAs, warp 9 loads weights, warp 10 loads activations.
+// Rings are sized so that no load waits on a recent MMA: activations run up to kBStages chunks
+// ahead and weights kRawStages chunks ahead; the dequantised A tile only needs double buffering.
+constexpr int kRawStages = 8;
+constexpr int kAStages = 2;
+constexpr int kBStages = 6;
+constexpr int kRawBytes = kTileM * kChunkK + 2 * kTileM * 2;   // 8 KB int8 + 512 B scales
+constexpr int kAllThreads = kThreads + 96;
+
+template <int NT16>
+constexpr int umma_smem_bytes() {
+    return 1024 + kAStages * kABytes + kBStages * (16 * NT16 * kChunkK * 2) + kRawStages * kRawBytes;
+}
+
+template <int NT16, int EPI>
+__global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams p, const __grid_constant__ CUtensorMap xmap) {
+    constexpr int N = 16 * NT16;
+    constexpr int kBBytes = N * kChunkK * 2;
+    constexpr uint32_t kCols = N <= 32 ? 32 : 64;
+    constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
+    constexpr int kPartLd = N + 4;  // padded partial rows: consecutive weight rows land in different banks
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t a_full[kAStages], a_empty[kAStages], b_full[kBStages], b_empty[kBStages];
+    __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages], done_bar;
+    __shared__ uint32_t tmem_slot;
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    uint8_t * sA = smem;
+    uint8_t * sB = sA + kAStages * kABytes;
+    uint8_t * sR = sB + kBStages * kBBytes;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
+    const int c_beg = split * p.kc_per_split;
+    const int nch = max(0, min(p.KC, c_beg + p.kc_per_split) - c_beg);
+    const int row0 = chunk * 64;
+    const int rows_here = min(64, p.rows - row0);
+
+    if (warp == 8) tmem_alloc(&tmem_slot, kCols);
+    if (tid == 0) {
+        for (int i = 0; i < kAStages; i++) {
+            mbar_init(&a_full[i], kThreads);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < kBStages; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < kRawStages; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kThreads);
+        }
+        mbar_init(&done_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    // the next kernel may start only once this CTA holds its TMEM columns, so a waiting
+    // successor can never take columns this grid still needs
+    pdl_trigger();
+    bool ok = true;
+
+    if (warp < 8) {
+        // producer: weight row r, Q8_0 block hb of every chunk
+        const int r = tid & (kTileM - 1), hb = tid >> 7;
+        for (int c = 0; c < nch; c++) {
+            const int rs = c % kRawStages, ab = c % kAStages;
+            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kRawStages) & 1u, p.err);
+            const uint8_t * raw = sR + rs * kRawBytes;
+            const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
+            const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
+            const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
+            mbar_arrive(&raw_empty[rs]);
+            if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
+            const half2 s2 = __halves2half2(sc, sc);
+            const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
+            uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                uint4 o;
+                dq4(w8[2 * q], s2, o.x, o.y);
+                dq4(w8[2 * q + 1], s2, o.z, o.w);
+                const int j = hb * 4 + q;
+                *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
+            }
+            fence_proxy_async();
+            mbar_arrive(&a_full[ab]);
+        }
+    } else if (warp == 8) {
+        if (lane == 0) {
+            for (int c = 0; c < nch; c++) {
+                const int ab = c % kAStages, bb = c % kBStages;
+                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (c / kBStages) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kAStages) & 1u, p.err);
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kBBytes);
+#pragma unroll
+                for (int kk = 0; kk < kChunkK / 16; kk++)
+                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&a_empty[ab]);
+                umma_commit(&b_empty[bb]);
+            }
+            umma_commit(&done_bar);  // arrives once every MMA above has completed
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            // weights and scales are constant: stream them before the predecessor finishes
+            const uint8_t * qbase = reinterpret_cast<const uint8_t *>(p.qs) + (size_t) (mt * p.KC + c_beg) * 4 * kTileM * 16;
+            const uint8_t * dbase = reinterpret_cast<const uint8_t *>(p.ds) + (size_t) (mt * p.KC + c_beg) * 2 * kTileM * 2;
+            for (int c = 0; c < nch; c++) {
+                const int rs = c % kRawStages;
+                if (c >= kRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kRawStages) - 1) & 1u, p.err);
+                uint8_t * raw = sR + rs * kRawBytes;
+                mbar_expect_tx(&raw_full[rs], kRawBytes);
+                bulk_g2s(raw, qbase + (size_t) c * 4 * kTileM * 16, kTileM * kChunkK, &raw_full[rs]);
+                bulk_g2s(raw + kTileM * kChunkK, dbase + (size_t) c * 2 * kTileM * 2, 2 * kTileM * 2, &raw_full[rs]);
+            }
+        }
+    } else {
+        if (lane == 0) {
+            pdl_wait();  // activations come from the previous kernel
+            for (int c = 0; c < nch; c++) {
+                const int bb = c % kBStages;
+                if (c >= kBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kBStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&b_full[bb], kBBytes);
+                tma_2d(sB + bb * kBBytes, &xmap, (c_beg + c) * kChunkK, row0, &b_full[bb]);
+            }
+        }
+    }
+    pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed
+
+    // accumulator rows 32w..32w+31 (warps 0-3), all N columns
+    float v[N];
+    if (warp < 4) {
+        if (ok) ok = mbar_wait(&done_bar, 0u, p.err);
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t) (32 * warp) << 16);
+#pragma unroll
+        for (int j = 0; j < N / 16; j++) tmem_ld16(taddr + 16 * j, v + 16 * j);
+        tmem_wait_ld();
+        // the loaded registers are only valid after the wait: tie every use to it
+#pragma unroll
+        for (int j = 0; j < N; j++) asm volatile("" : "+f"(v[j]));
+        if (nch == 0 || !ok)
+#pragma unroll
+            for (int j = 0; j < N; j++) v[j] = 0.0f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) tmem_dealloc(tmem, kCols);
+
+    const int m_loc = 32 * warp + lane;
+    if (p.splits == 1) {
+        if (warp >= 4) return;
+        const int m = mt * kTileM + m_loc;
+        if (EPI == EPI_STORE || EPI == EPI_RESID) {
+            if (m < p.M) {
+#pragma unroll
+                for (int n0 = 0; n0 < N; n0 += 16) {
+                    if (EPI == EPI_RESID) {
+                        // gather 16 residual values at a time so their loads overlap
+                        float old[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++)
+                            old[e] = n0 + e < rows_here ? p.out.f32[(size_t) (row0 + n0 + e) * p.out.ld + m] : 0.0f;
+#pragma unroll
+                        for (int e = 0; e < 16; e++) v[n0 + e] += old[e];
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; e++)
+                        if (n0 + e < rows_here) p.out.f32[(size_t) (row0 + n0 + e) * p.out.ld + m] = v[n0 + e];
+                }
+            }
+        } else {
+            // 16-row interleave: lanes 0-15 hold gate rows, lanes 16-31 the matching up rows
+            const int j = mt * (kTileM / 2) + 16 * warp + lane;
+#pragma unroll
+            for (int n = 0; n < N; n++) {
+                const float up = __shfl_sync(0xffffffffu, v[n], lane + 16);
+                if (lane < 16 && n < rows_here && j < (p.M >> 1)) {
+                    const float g = v[n];
+                    const float act = EPI == EPI_SWIGLU ? silu_f(g) : gelu_tanh_f(g);
+                    p.out.f16[(size_t) (row0 + n) * p.out.ld + j] = __float2half_rn(act * up);
+                }
+            }
+        }
+        return;
+    }
+
+    // split-K: partial tile [128][N] f32 (padded rows) in shared memory, reduced across the cluster
+    float * part = reinterpret_cast<float *>(sR);  // raw ring is idle now and holds 128 x (N + 4) floats
+    if (warp < 4) {
+#pragma unroll
+        for (int n = 0; n < N; n += 4)
+            *reinterpret_cast<float4 *>(part + (size_t) m_loc * kPartLd + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
+    }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int S = p.splits;
+    const int rank = (int) cluster.block_rank();
+    const int rows_per = kTileM / S;
+    const int mbeg = rank * rows_per;
+    const float * peers[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) peers[q] = q < S ? cluster.map_shared_rank(part, q) : part;
+    const int nq = (rows_here + 3) / 4;
+    if (EPI == EPI_STORE || EPI == EPI_RESID) {
+        // lane -> weight row (coalesced stores per activation row), 4 activation rows per item
+        for (int idx = tid; idx < rows_per * nq; idx += kAllThreads) {
+            const int ml = mbeg + idx % rows_per, n4 = (idx / rows_per) * 4;
+            float4 pv[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                if (q < S) pv[q] = *reinterpret_cast<const float4 *>(peers[q] + (size_t) ml * kPartLd + n4);
+            float4 acc = pv[0];
+#pragma unroll
+            for (int q = 1; q < 8; q++)
+                if (q < S) { acc.x += pv[q].x; acc.y += pv[q].y; acc.z += pv[q].z; acc.w += pv[q].w; }
+            const int m = mt * kTileM + ml;
+            if (m < p.M) {
+                const float av[4] = { acc.x, acc.y, acc.z, acc.w };
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (n4 + e < rows_here) store_out<EPI>(p, row0 + n4 + e, m, av[e]);
+            }
+        }
+    } else {
+        // whole 32-row gate/up groups per slice (at most 4 splits for these epilogues)
+        const int pairs = rows_per / 2;
+        for (int idx = tid; idx < pairs * nq; idx += kAllThreads) {
+            const int pi = idx % pairs, n4 = (idx / pairs) * 4;
+            const int grp = mbeg + (pi / 16) * 32, i = pi % 16;
+            float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                if (q < S) {
+                    const float4 gq = *reinterpret_cast<const float4 *>(peers[q] + (size_t) (grp + i) * kPartLd + n4);
+                    const float4 uq = *reinterpret_cast<const float4 *>(peers[q] + (size_t) (grp + 16 + i) * kPartLd + n4);
+                    g.x += gq.x; g.y += gq.y; g.z += gq.z; g.w += gq.w;
+                    u.x += uq.x; u.y += uq.y; u.z += uq.z; u.w += uq.w;
+                }
+            }
+            const int j = mt * (kTileM / 2) + grp / 2 + i;
+            if (j < (p.M >> 1)) {
+                const float gv[4] = { g.x, g.y, g.z, g.w }, uv[4] = { u.x, u.y, u.z, u.w };
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    if (n4 + e < rows_here) {
+                        const float act = EPI == EPI_SWIGLU ? silu_f(gv[e]) : gelu_tanh_f(gv[e]);
+                        p.out.f16[(size_t) (row0 + n4 + e) * p.out.ld + j] = __float2half_rn(act * uv[e]);
+                    }
+                }
+            }
+        }
+    }
+    cluster.sync();
+}
+
+__global__ void repack_umma_kernel(const uint8_t * raw, int M, int KB, int KC, uint4 * qs, half * ds) {
+    const long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    const int MT = (M + kTileM - 1) / kTileM;
+    if (idx >= (long long) MT * KC * 4 * kTileM) return;
+    const int r = (int) (idx % kTileM);
+    const long long rest = idx / kTileM;
+    const int pc = (int) (rest % 2), hb = (int) ((rest / 2) % 2);
+    const long long tc = rest / 4;
+    const int c = (int) (tc % KC), mt = (int) (tc / KC);
+    const int row = mt * kTileM + r, blk = 2 * c + hb;
+    uint32_t w[4] = { 0u, 0u, 0u, 0u };
+    unsigned short d = 0;
+    if (row < M) {
+        const uint8_t * b = raw + ((size_t) row * KB + blk) * 34;
+        d = (unsigned short) (b[0] | (b[1] << 8));
+        const uint8_t * q = b + 2 + pc * 16;
+        for (int i = 0; i < 4; i++) w[i] = q[4 * i] | (q[4 * i + 1] << 8) | (q[4 * i + 2] << 16) | ((uint32_t) q[4 * i + 3] << 24);
+    }
+    qs[idx] = make_uint4(w[0], w[1], w[2], w[3]);
+    if (pc == 0) ds[((size_t) (mt * KC + c) * 2 + hb) * kTileM + r] = __ushort_as_half(d);
+}
+
+template <int NT16, int EPI>
+void set_attr_one() {
+    cudaFuncSetAttribute(umma_gemm_kernel<NT16, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, umma_smem_bytes<NT16>());
+    cudaFuncSetAttribute(umma_gemm_kernel<NT16, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+
+template <int NT16>
+void set_attr_nt() {
+    set_attr_one<NT16, EPI_STORE>();
+    set_attr_one<NT16, EPI_RESID>();
+    set_attr_one<NT16, EPI_SWIGLU>();
+    set_attr_one<NT16, EPI_GEGLU>();
+}
+
+template <int NT16, int EPI>
+void launch_one(const UParams & p, const CUtensorMap & map, dim3 grid, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kAllThreads);
+    cfg.dynamicSmemBytes = umma_smem_bytes<NT16>();
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (p.splits > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = p.splits;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    UCHECK(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<NT16, EPI>, p, map));
+}
+
+template <int NT16>
+void launch_nt(const UParams & p, const CUtensorMap & map, dim3 grid, cudaStream_t s, bool pdl) {
+    switch (p.out.kind) {
+        case EPI_STORE: launch_one<NT16, EPI_STORE>(p, map, grid, s, pdl); break;
+        case EPI_RESID: launch_one<NT16, EPI_RESID>(p, map, grid, s, pdl); break;
+        case EPI_SWIGLU: launch_one<NT16, EPI_SWIGLU>(p, map, grid, s, pdl); break;
+        default: launch_one<NT16, EPI_GEGLU>(p, map, grid, s, pdl); break;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void * f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !f)
+            throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// activation rows [rows][K] f16 with row stride ldx, read as 64 x box_rows tiles in the
+// 128-byte swizzle; rows past `rows` read as zero
+CUtensorMap make_x_map(const half * x, int K, int ldx, int rows, int box_rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = { (cuuint64_t) K, (cuuint64_t) rows };
+    const cuuint64_t strides[1] = { (cuuint64_t) ldx * sizeof(half) };
+    const cuuint32_t box[2] = { (cuuint32_t) kChunkK, (cuuint32_t) box_rows };
+    const cuuint32_t estr[2] = { 1, 1 };
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<half *>(x), dims, strides, box, estr,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string((int) r) + ")");
+    return m;
+}
+
+}  // namespace
+
+void init_umma_attributes() {
+    set_attr_nt<1>();
+    set_attr_nt<2>();
+    set_attr_nt<3>();
+    set_attr_nt<4>();
+    UCHECK(cudaGetLastError());
+}
+
+void repack_umma(const uint8_t * raw_dev, int M, int K, uint4 * qs, half * ds, cudaStream_t s) {
+    if (K % kChunkK) throw std::runtime_error("tcgen05 layout needs K % 64 == 0");
+    const int MT = (M + kTileM - 1) / kTileM, KC = K / kChunkK;
+    const long long n = (long long) MT * KC * 4 * kTileM;
+    repack_umma_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(raw_dev, M, K / 32, KC, qs, ds);
+    UCHECK(cudaGetLastError());
+}
+
+void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const GemvOut & out, int * err,
+                      cudaStream_t s, bool pdl) {
+    if (rows <= 0) return;
+    if (ldx % 8 != 0 || w.K % kChunkK != 0 || (reinterpret_cast<uintptr_t>(x16) & 15))
+        throw std::runtime_error("umma gemm: activations must be 16-byte aligned with a stride multiple of 8");
+    const int chunks = (rows + 63) / 64;
+    const int n_rows = std::min(rows, 64);
+    const int NT16 = (n_rows + 15) / 16;
+    const int tiles_chunks = w.MT * chunks;
+    // one wave of one CTA per SM: split K while the tiles leave SMs idle; the cluster reduction
+    // costs more than it saves beyond 4 splits unless the matrix has at most 8 tiles
+    const int max_splits = (tiles_chunks <= 8 && out.kind < EPI_SWIGLU) ? 8 : 4;
+    int splits = 1;
+    while (splits * 2 * tiles_chunks <= 148 && splits * 2 <= max_splits && w.KC / (splits * 2) >= 2) splits *= 2;
+    if (const char * e = std::getenv("BZB_UMMA_SPLITS")) {
+        const int f = std::atoi(e);
+        if (f == 1 || f == 2 || f == 4 || f == 8) splits = std::min(f, (out.kind >= EPI_SWIGLU) ? 4 : 8);
+    }
+    UParams p;
+    p.qs = w.qs; p.ds = w.ds; p.M = w.M; p.MT = w.MT; p.KC = w.KC;
+    p.kc_per_split = (w.KC + splits - 1) / splits;
+    p.splits = splits;
+    p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.err = err;
+    const CUtensorMap map = make_x_map(x16, w.K, ldx, rows, 16 * NT16);
+    dim3 grid(w.MT, splits, chunks);
+    switch (NT16) {
+        case 1: launch_nt<1>(p, map, grid, s, pdl); break;
+        case 2: launch_nt<2>(p, map, grid, s, pdl); break;
+        case 3: launch_nt<3>(p, map, grid, s, pdl); break;
+        default: launch_nt<4>(p, map, grid, s, pdl); break;
+    }
+}
+
+}  // namespace bzb

@@ -757,6 +757,30 @@ def sample_margin(logits, temp, top_k, u: np.float32) -> float:
     return float(np.min(np.abs(cdf - float(u))))
 
 
+def sample_reachable(logits, temp, top_k, u: np.float32, token: int, eps: float) -> bool:
+    """Whether the sampler (same top-k, temperature and uniform u) can return `token` for some
+    logits within +-eps of `logits`. A perturbation of at most eps scales every unnormalised
+    weight exp(l/T) by a factor in [e^(-eps/T), e^(eps/T)], so each CDF boundary moves by at most
+    e^(2 eps/T) - 1; the token must also be able to enter the top-k set."""
+    n = logits.shape[0]
+    keep = top_k if 0 < top_k < n else n
+    order = np.lexsort((np.arange(n), -logits.astype(np.float64)))
+    t = np.float64(temp if temp > 0 else 1.0)
+    delta = float(np.expm1(2.0 * eps / t))
+    rank = int(np.nonzero(order == token)[0][0])
+    if rank >= keep:
+        # outside the top-k: it can only displace the k-th entry, at the top of the CDF
+        if logits[token] < logits[order[keep - 1]] - 2 * eps:
+            return False
+        return float(u) >= 1.0 - delta - float(np.exp((logits[token] - logits[order[0]]) / t))
+    top = order[:keep]
+    p = np.exp((logits[top].astype(np.float64) - logits[top[0]]) / t)
+    cdf = np.cumsum(p) / p.sum()
+    lo = 0.0 if rank == 0 else cdf[rank - 1]
+    hi = cdf[rank]
+    return lo - delta <= float(u) <= hi + delta
+
+
 class PhiloxStream:
     """Per-session sampler state: seed (key) and draw counter; reseeding resets the counter,
     mirroring std::mt19937::seed in src/c_api.cpp:343, 631, 816."""

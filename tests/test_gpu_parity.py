@@ -81,6 +81,27 @@ def test_depth_decoder_teacher_forced(gen, tiny_oracle):
     assert np.array_equal(logits2, logits)
 
 
+def reconcile_cb0(ref, sid, engine_next, oracle_next, tag):
+    """Accept a different cb0 draw only where the same Philox uniform lands within reach of a
+    CDF boundary: the engine's token must be what the sampler returns for some logits within
+    LOGIT_ATOL of the oracle's. Then the oracle follows the engine's draw. Returns 1 for a
+    tolerated boundary case, 0 for agreement."""
+    if engine_next == oracle_next:
+        return 0
+    pl, key, draw = ref.last_cb0_logits[sid]
+    u = bo.philox_uniform(key, draw)
+    ok = engine_next >= 0 and oracle_next >= 0 and bo.sample_reachable(pl, 0.9, 50, u, engine_next, LOGIT_ATOL)
+    assert ok, (tag, sid, engine_next, oracle_next, bo.sample_margin(pl, 0.9, 50, u))
+    rs = ref.sessions[sid]
+    if oracle_next >= 0:
+        rs.hist[int(oracle_next)] -= 1
+    if engine_next >= 0:
+        rs.hist[int(engine_next)] = rs.hist.get(int(engine_next), 0) + 1
+        rs.last_cb0 = int(engine_next)
+        rs.active = True
+    return 1
+
+
 def _prompts(pkg):
     return {
         1: dict(text=pkg.ids_to_text([300, 4000, 77777, 1234, 900]), seed=5, max_new_tokens=6),
@@ -136,18 +157,7 @@ def test_prefill_and_decode_steps_match_oracle(pkg, gen, tiny_oracle):
                     assert top2_gap(lg) < TIE_GAP, (step, sid, j, top2_gap(lg))
                     ties += 1
         for i, sid in enumerate(ids):
-            if nxt[i] != rnxt[i]:
-                # a different draw is only acceptable on a CDF boundary tie of the same uniform
-                pl, key, draw = ref.last_cb0_logits[sid]
-                margin = bo.sample_margin(pl, 0.9, 50, bo.philox_uniform(key, draw))
-                assert margin < 2e-3, (step, sid, nxt[i], rnxt[i], margin)
-                ties += 1
-                rs = ref.sessions[sid]  # follow the engine from here
-                if rnxt[i] >= 0:
-                    rs.hist[int(rnxt[i])] -= 1
-                if nxt[i] >= 0:
-                    rs.hist[int(nxt[i])] = rs.hist.get(int(nxt[i]), 0) + 1
-                    rs.last_cb0 = int(nxt[i])
+            ties += reconcile_cb0(ref, sid, int(nxt[i]), int(rnxt[i]), step)
         for sid in ids:
             if ref.sessions[sid].active:
                 h = gen.debug_hidden(sid, cfg.hidden)
@@ -169,6 +179,14 @@ def test_burst_semantics_match_reference_abi(pkg, gen, tiny_oracle):
         gen.session_create_ext(sid, text, seed=sid, max_new_tokens=mx)
         ref.session_create(sid, text, seed=sid, max_new_tokens=mx)
     ids = gen_ids + [999]  # 999 was never created
+    try:
+        _check_burst(gen, ref, cfg, gen_ids, ids)
+    finally:
+        for sid in gen_ids:
+            gen.session_free(sid)
+
+
+def _check_burst(gen, ref, cfg, gen_ids, ids):
     nxt, frames = gen.sessions_step_burst(ids, 8, seeds=[7, 8, 9])
     frames = np.asarray(frames).transpose(1, 0, 2)          # [step][session][16]
     nc = cfg.nc
@@ -180,10 +198,14 @@ def test_burst_semantics_match_reference_abi(pkg, gen, tiny_oracle):
         was_active = [sid in ref.sessions and ref.sessions[sid].active for sid in ids]
         forced = np.where(frames[k][:, 1:nc] < 0, 0, frames[k][:, 1:nc])
         f, n = ref.step_batched(ids, seeds=[7 + k, 8 + k, 9 + k], forced_depth=forced)
+        engine_next = frames[k + 1][:, 0] if k + 1 < 8 else np.asarray(nxt)
         for i in range(3):
             if was_active[i]:
                 assert frames[k][i][0] == f[i][0], (k, i)
                 assert (frames[k][i][nc:] == -1).all()
+                if n[i] >= 0 and engine_next[i] >= 0:
+                    reconcile_cb0(ref, ids[i], int(engine_next[i]), int(n[i]), k)
+                    n[i] = engine_next[i]
                 rn[i] = n[i]
             else:
                 assert (frames[k][i] == -1).all(), (k, i)
@@ -194,7 +216,6 @@ def test_burst_semantics_match_reference_abi(pkg, gen, tiny_oracle):
     assert gen.active_session_count() == 2
     assert gen.session_free(999) == -1
     assert gen.session_free(21) == 0 and gen.active_session_count() == 1
-    gen.session_free(22)
 
 
 def test_step_batched_return_codes(pkg, gen):

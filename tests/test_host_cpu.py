@@ -209,3 +209,26 @@ def test_session_budget_semantics(tiny_oracle):
     e = np.zeros((2000, tiny_oracle.cfg.hidden), np.float32)
     _, alloc = g.session_create(2, text, embeds=e, max_new_tokens=500)
     assert alloc == 2000 + 64 + 8
+
+
+def test_sample_reachable_bounds():
+    """The parity tests' tolerance for sampled cb0 ids: the oracle's own draw is always
+    reachable, a draw far from the uniform's CDF position never is, and a boundary token
+    becomes reachable once the logit tolerance covers the gap."""
+    rng = np.random.default_rng(8)
+    logits = (rng.standard_normal(2052) * 2).astype(np.float32)
+    for d in range(50):
+        u = bo.philox_uniform(3, d)
+        tok = bo.sample_philox(logits, 0.9, 50, 1.0, u)
+        assert bo.sample_reachable(logits, 0.9, 50, u, tok, 0.0)
+    order = np.lexsort((np.arange(2052), -logits.astype(np.float64)))
+    u = np.float32(0.001)                     # the top token's interval
+    assert not bo.sample_reachable(logits, 0.9, 50, u, int(order[30]), 0.02)
+    assert not bo.sample_reachable(logits, 0.9, 50, u, int(order[200]), 0.02)
+    # two equal top logits: u just past the first interval reaches the first token only with a tolerance
+    l2 = np.full(2052, -10.0, np.float32)
+    l2[5] = l2[6] = 1.0
+    u = np.float32(0.51)
+    assert bo.sample_philox(l2, 0.9, 50, 1.0, u) == 6
+    assert not bo.sample_reachable(l2, 0.9, 50, u, 5, 0.0)
+    assert bo.sample_reachable(l2, 0.9, 50, u, 5, 0.02)
