@@ -133,26 +133,30 @@ def test_generator_without_gpu_fails_loudly(pkg, tiny_model):
 
 
 # ---- sampler semantics (src/sampling.cpp:9-60) on the CPU ---------------------------------
-def _mt_lib():
-    path = os.path.join(ROOT, "oracle", "_build", "libmtsample.so")
+def _ref_lib():
+    """The reference's own sampler and voice codec, compiled from its sources into oracle/_ref
+    (`make -C oracle ref`); skips where neither the build nor the reference checkout exists."""
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_host.so")
     if not os.path.exists(path):
         import subprocess
-        subprocess.run(["make", "-C", os.path.join(ROOT, "oracle")], check=True)
+        r = subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "ref"], capture_output=True)
+        if r.returncode != 0 or not os.path.exists(path):
+            pytest.skip("the reference's host code is not built here")
     lib = ctypes.CDLL(path)
-    lib.oracle_sample_mt.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.c_float, ctypes.c_int,
-                                     ctypes.c_float, ctypes.c_float, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
-                                     ctypes.c_int, ctypes.c_int, ctypes.c_uint, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+    lib.ref_sample_tokens.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                      ctypes.c_float, ctypes.c_float, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_uint, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
     return lib
 
 
 def mt_draws(logits, n, temp=0.9, top_k=50, top_p=1.0, rep=1.0, hist=(), sup=(2048, 2051), seed=1):
-    lib = _mt_lib()
+    lib = _ref_lib()
     l = np.ascontiguousarray(logits, np.float32)
     h = np.asarray(hist, np.int32) if len(hist) else np.zeros(1, np.int32)
     out = np.zeros(n, np.int32)
-    lib.oracle_sample_mt(l.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), l.size, temp, top_k, top_p, rep,
-                         h.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), len(hist), sup[0], sup[1], seed, n,
-                         out.ctypes.data_as(ctypes.POINTER(ctypes.c_int)))
+    lib.ref_sample_tokens(l.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), l.size, temp, top_k, top_p, rep,
+                          h.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), len(hist), sup[0], sup[1], seed, n,
+                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_int)))
     return out
 
 
