@@ -34,3 +34,19 @@ def tiny_model(pkg, model_dir):
 def tiny_oracle(tiny_model):
     import breeze_oracle as bo
     return bo.Model(tiny_model)
+
+
+@pytest.fixture(scope="session")
+def reference_bindings():
+    """The reference's own Python bindings module (python/bz_ggml/bindings.py), loaded from the
+    reference checkout that oracle/Makefile points at; skips where there is none."""
+    import importlib.util
+    import subprocess
+    r = subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "print-ref"], capture_output=True, text=True)
+    path = os.path.join(r.stdout.strip(), "python", "bz_ggml", "bindings.py")
+    if r.returncode != 0 or not os.path.exists(path):
+        pytest.skip("no reference checkout here")
+    spec = importlib.util.spec_from_file_location("reference_bindings", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod

@@ -151,3 +151,27 @@ def test_philox_sampler_matches_reference_draws(case):
     # and the support: every id the reference drew at least 1% of the time appears in ours
     frequent = {c for c in cats if np.sum(ref_toks == c) > n // 100}
     assert frequent <= set(ours)
+
+
+def test_reference_bindings_bind_this_library(pkg, reference_bindings, tiny_model, tmp_path):
+    """The drop-in check: the reference's unmodified ctypes bindings load libbreeze.so, bind
+    every symbol they declare, and see the reference's error conventions."""
+    rb = reference_bindings
+    lib = rb.BreezeLib(pkg.LIB_PATH)
+    assert lib.lib_path == pkg.LIB_PATH
+    import torch
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="Failed to initialize Generator"):
+            rb.GeneratorHandle(lib, tiny_model, 0)
+        assert "CUDA" in pkg.lib().last_error()
+    # the reference's Python voice files and this library's C reader/writer interoperate
+    codes = MG.voice_codes(4, 16, 5)
+    path = str(tmp_path / "v" / "bob.breeze")
+    rb.save_breeze_voice(path, "hi there", codes.tolist(), 4)
+    n, name, text, got, nf, ncb, sr = _load_ours(lib.lib, path, 64)
+    assert (n, name, text, nf, ncb, sr) == (64, "bob", "hi there", 4, 16, 24000)
+    assert np.array_equal(got, codes)
+    ours = str(tmp_path / "ours.breeze")
+    assert _save_ours(lib.lib, ours, "hi there", codes, 4, 16, 24000) == 0
+    v = rb.load_breeze_voice(ours)
+    assert v["codes"] == codes.tolist() and v["text"] == "hi there" and v["name"] == "ours"
