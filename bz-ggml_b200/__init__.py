@@ -93,6 +93,8 @@ SIGNATURES = {
                                                 _c_float_p, _c_float_p]),
     "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_int]),
+    "bzb_generator_gemm_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p,
+                                                  ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "bzb_gguf_inspect": (ctypes.c_int, [ctypes.c_char_p, _c_int_p, _c_int_p, _c_int_p]),
     "bzb_tokenize": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, _c_int_p, ctypes.c_int]),
 }
@@ -267,6 +269,14 @@ class GeneratorHandle:
         if us < 0:
             raise RuntimeError(self.lib.last_error())
         return us
+
+    def gemm_noalloc(self, tensor: str, rows: int, x16_ptr: int, ldx: int, y_ptr: int, ldy: int,
+                     stream_ptr: int = 0) -> None:
+        """Allocation-free dequant-GEMM on caller-owned device buffers (pointers as ints);
+        asynchronous on `stream_ptr` (0 = the generator's stream)."""
+        if self.lib.lib.bzb_generator_gemm_noalloc(self.handle, tensor.encode(), rows, x16_ptr, ldx, y_ptr, ldy,
+                                                    stream_ptr or None) != 0:
+            raise RuntimeError(self.lib.last_error())
 
     def debug_hidden(self, session_id: int, hidden: int) -> np.ndarray:
         out = np.zeros(hidden, np.float32)

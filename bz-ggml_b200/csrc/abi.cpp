@@ -476,6 +476,22 @@ int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int su
     }
 }
 
+int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * tensor, int rows, const void * x16, int ldx,
+                               float * y, int ldy, void * stream) {
+    if (!gen || !tensor) {
+        set_error("gemm_noalloc: null generator or tensor name");
+        return -1;
+    }
+    try {
+        gen->eng->gemm_noalloc(tensor, rows, static_cast<const half *>(x16), ldx, y, ldy,
+                               static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters, int epilogue) {
     if (!gen || !tensor || rows <= 0 || iters <= 0) return -1.0;
     try {

@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
@@ -953,6 +954,33 @@ double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int
     cudaFree(xd);
     cudaFree(yd);
     return ms * 1000.0 / iters;
+}
+
+const QMat * Engine::resident_matrix(const char * tensor) const {
+    // parsed without building strings: this lookup serves the allocation-free entry point
+    int l = -1, n = 0;
+    char part[32] = { 0 };
+    if (std::strcmp(tensor, "bb.lm_head.weight") == 0) return &lm_head_;
+    if (std::strcmp(tensor, "dd.in_proj.weight") == 0) return &dd_in_;
+    const std::vector<LayerW> * layers = nullptr;
+    if (std::sscanf(tensor, "bb.blk.%d.%31[a-z_].weight%n", &l, part, &n) == 2 && tensor[n] == 0) layers = &bb_;
+    else if (std::sscanf(tensor, "dd.blk.%d.%31[a-z_].weight%n", &l, part, &n) == 2 && tensor[n] == 0) layers = &dd_;
+    if (!layers || l < 0 || l >= (int) layers->size()) return nullptr;
+    if (std::strcmp(part, "attn_output") == 0) return &(*layers)[l].o;
+    if (std::strcmp(part, "ffn_down") == 0) return &(*layers)[l].down;
+    return nullptr;
+}
+
+void Engine::gemm_noalloc(const char * tensor, int rows, const half * x16, int ldx, float * y, int ldy, cudaStream_t s) {
+    const QMat * w = resident_matrix(tensor);
+    if (!w)
+        throw std::runtime_error("gemm_noalloc: not a resident unfused matrix (bb.lm_head, dd.in_proj, "
+                                 "{bb,dd}.blk.N.attn_output or ffn_down): " + std::string(tensor));
+    if (!x16 || !y) throw std::runtime_error("gemm_noalloc: null device buffer");
+    if (ldx < w->K || (ldx & 1) || (reinterpret_cast<uintptr_t>(x16) & 3) || (reinterpret_cast<uintptr_t>(y) & 3))
+        throw std::runtime_error("gemm_noalloc: x must be 4-byte aligned with an even stride >= K, y 4-byte aligned");
+    CK(cudaSetDevice(device));
+    launch_gemv_static_scratch(*w, x16, ldx, rows, y, ldy, s ? s : stream_);
 }
 
 size_t Engine::weight_bytes_per_step() const {

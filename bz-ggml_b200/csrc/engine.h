@@ -72,6 +72,9 @@ public:
     void profile_step(double * out);
     // average microseconds of `iters` back-to-back launches of one dequant-GEMM (epilogue kind)
     double bench_gemv(const char * tensor, int sub, int rows, int iters, int epi);
+    // y[rows][ldy] = x16[rows][ldx] . W^T for a resident, unfused Q8_0 matrix, allocating
+    // nothing (static-scratch GEMV); asynchronous on `s` (the engine's stream when null)
+    void gemm_noalloc(const char * tensor, int rows, const half * x16, int ldx, float * y, int ldy, cudaStream_t s);
     size_t weight_bytes_per_step() const;
     size_t kv_bytes_per_position() const;
 
@@ -98,6 +101,7 @@ private:
     void bb_prefill(int slot, int T);
     void ensure_prefill_capacity(int T);
     cudaGraphExec_t graph_for(int R);
+    const QMat * resident_matrix(const char * tensor) const;
     int acquire_slot(int sid, int n_pages);
     void release_slot(int slot);
 

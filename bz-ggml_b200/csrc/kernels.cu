@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 #include <utility>
 #include <cfloat>
 #include <cmath>
@@ -1071,6 +1072,55 @@ void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const Gemv
         default: launch_gemv_nt<8>(p, grid, smem, s); break;
     }
     BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Scratch of launch_gemv_static_scratch: file-scope device arrays, so the allocation-free
+// entry point needs no cudaMalloc. Zero-initialised at module load; the counters are cleared
+// again on the stream before every launch.
+static __device__ __align__(256) float4 g_static_gemv_ws[kStaticGemvWsElems];
+static __device__ __align__(256) int g_static_gemv_counters[kStaticGemvCounters];
+
+namespace {
+constexpr int kMaxStaticDevices = 64;
+std::mutex g_static_mu;
+GemvScratch g_static_scr[kMaxStaticDevices];
+bool g_static_ready[kMaxStaticDevices] = {};
+
+// addresses of the static scratch on the current device, looked up once per device (the
+// lookup may load the module on first use, which is why the first call precedes any capture)
+GemvScratch static_scratch() {
+    int dev = 0;
+    BZB_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxStaticDevices) throw std::runtime_error("gemv (static scratch): device index out of range");
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ready[dev]) {
+        GemvScratch s;
+        cudaError_t e = cudaGetSymbolAddress((void **) &s.ws, g_static_gemv_ws);
+        if (e != cudaSuccess)
+            throw std::runtime_error(std::string("gemv (static scratch): cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+        e = cudaGetSymbolAddress((void **) &s.counters, g_static_gemv_counters);
+        if (e != cudaSuccess)
+            throw std::runtime_error(std::string("gemv (static scratch): cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+        s.ws_elems = kStaticGemvWsElems;
+        s.n_counters = kStaticGemvCounters;
+        g_static_scr[dev] = s;
+        g_static_ready[dev] = true;
+    }
+    return g_static_scr[dev];
+}
+}  // namespace
+
+void launch_gemv_static_scratch(const QMat & w, const half * x16, int ldx, int rows, float * y, int ldy,
+                                cudaStream_t s) {
+    if (rows <= 0 || rows > kStaticGemvMaxRows)
+        throw std::runtime_error("gemv (static scratch): rows must be in [1, " + std::to_string(kStaticGemvMaxRows) + "]");
+    if (ldy < w.M) throw std::runtime_error("gemv (static scratch): output stride is below the matrix rows");
+    const GemvScratch scr = static_scratch();
+    // tile counters must start at zero; a launch that did not finish could have left them set
+    const size_t n_ctr = std::min((size_t) kStaticGemvCounters, (size_t) ((rows + 63) / 64) * ((w.MT + 7) / 8));
+    BZB_CUDA_CHECK(cudaMemsetAsync(scr.counters, 0, n_ctr * sizeof(int), s));
+    // launch_gemv rejects a split plan that does not fit the scratch before launching anything
+    launch_gemv(w, x16, ldx, rows, GemvOut{ EPI_STORE, y, nullptr, ldy }, scr, s);
 }
 
 void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s) {

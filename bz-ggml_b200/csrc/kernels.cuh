@@ -74,6 +74,19 @@ void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const Gemv
 
 void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s);
 
+// The same GEMV with its split-K partials and tile counters in fixed-size static device arrays
+// instead of caller-provided scratch, for callers that must not allocate (see
+// bzb_generator_gemm_noalloc). Limits: rows <= kStaticGemvMaxRows, and the split plan must fit
+// kStaticGemvWsElems partials and kStaticGemvCounters counters (checked: std::runtime_error).
+// The first call on a device looks up the arrays' addresses (once per device, with that device
+// current); make it before any stream capture. Concurrent calls on one device share the
+// arrays and race.
+constexpr int kStaticGemvMaxRows = 256;
+constexpr size_t kStaticGemvWsElems = (size_t) 640 << 10;   // float4: 10 MiB of partials
+constexpr int kStaticGemvCounters = 4096;
+void launch_gemv_static_scratch(const QMat & w, const half * x16, int ldx, int rows, float * y, int ldy,
+                                cudaStream_t s);
+
 // tcgen05 dequant-GEMM (umma_gemm.cu): same contract as launch_gemv; `err` receives 1 if a
 // bounded pipeline wait gave up
 void init_umma_attributes();

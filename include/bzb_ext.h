@@ -57,6 +57,22 @@ BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * ten
 BREEZE_API double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters,
                                            int epilogue);
 
+/* Allocation-free dequant-GEMM (no counterpart in the reference): y[rows][ldy] = x16[rows][ldx]
+   . W^T for a weight matrix already resident in the generator -- bb.lm_head.weight,
+   dd.in_proj.weight, or {bb,dd}.blk.N.{attn_output,ffn_down}.weight -- on caller-owned device
+   buffers (x16: f16 bits, 4-byte aligned, even ldx >= K; y: f32, ldy >= the matrix rows).
+   It performs no device or host allocation: its split-K scratch is a fixed static device
+   array (10 MiB of partials, 4096 counters), so a caller that has handed every free byte of
+   HBM to its own pools, or that runs inside a real-time loop where cudaMalloc/cudaFree may
+   synchronise the device and stall the other streams, can still run it. Limits: 1 <= rows <= 256; larger inputs are rejected with
+   -1 and breeze_last_error(). Asynchronous on `stream` (a cudaStream_t; NULL = the
+   generator's stream); it returns after enqueueing. The first call on a device sets up the
+   scratch address (once per device) and should come before any stream capture. Calls that
+   overlap on one device (other streams, other generators) share the scratch and race.
+   Returns 0, or -1 with breeze_last_error(). */
+BREEZE_API int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * tensor, int rows, const void * x16,
+                                          int ldx, float * y, int ldy, void * stream);
+
 /* GGUF inspection without a GPU: 0 and the config values, or -1 with breeze_last_error() */
 BREEZE_API int bzb_gguf_inspect(const char * gguf_path, int * out_hidden, int * out_num_codebooks,
                                 int * out_n_tensors);
