@@ -27,6 +27,7 @@ SYNTH_BIN = os.path.join(HERE, "bin", "breeze-synth")
 _c_int_p = ctypes.POINTER(ctypes.c_int)
 _c_uint_p = ctypes.POINTER(ctypes.c_uint)
 _c_float_p = ctypes.POINTER(ctypes.c_float)
+_c_double_p = ctypes.POINTER(ctypes.c_double)
 
 # every symbol include/breeze.h and include/bzb_ext.h declare: name -> (restype, argtypes)
 SIGNATURES = {
@@ -93,6 +94,7 @@ SIGNATURES = {
                                                 _c_float_p, _c_float_p]),
     "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_int]),
+    "bzb_generator_depth_trace": (ctypes.c_int, [ctypes.c_void_p, _c_double_p, ctypes.c_int]),
     "bzb_generator_gemm_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p,
                                                   ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "bzb_gguf_inspect": (ctypes.c_int, [ctypes.c_char_p, _c_int_p, _c_int_p, _c_int_p]),
@@ -269,6 +271,20 @@ class GeneratorHandle:
         if us < 0:
             raise RuntimeError(self.lib.last_error())
         return us
+
+    def depth_trace(self):
+        """Timeline of one persistent depth launch: (phase types [n], times [n][grid][slots] in
+        microseconds, -1 where a slot was not reached), or None without the persistent path."""
+        need = self.lib.lib.bzb_generator_depth_trace(self.handle, None, 0)
+        if need < 0:
+            raise RuntimeError(self.lib.last_error())
+        if need == 0:
+            return None
+        out = np.zeros(need, np.float64)
+        if self.lib.lib.bzb_generator_depth_trace(self.handle, out.ctypes.data_as(_c_double_p), need) < 0:
+            raise RuntimeError(self.lib.last_error())
+        n, g, k = int(out[0]), int(out[1]), int(out[2])
+        return out[3:3 + n].astype(int), out[3 + n:].reshape(n, g, k)
 
     def gemm_noalloc(self, tensor: str, rows: int, x16_ptr: int, ldx: int, y_ptr: int, ldy: int,
                      stream_ptr: int = 0) -> None:

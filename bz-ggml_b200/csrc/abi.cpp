@@ -492,6 +492,16 @@ int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * tensor, int 
     }
 }
 
+int bzb_generator_depth_trace(breeze_generator * gen, double * out, int capacity) {
+    if (!gen) return -1;
+    try {
+        return gen->eng->depth_trace(out, capacity);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters, int epilogue) {
     if (!gen || !tensor || rows <= 0 || iters <= 0) return -1.0;
     try {

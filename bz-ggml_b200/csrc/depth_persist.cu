@@ -1,0 +1,732 @@
+// Persistent depth decoder for sm_100a.
+//
+// The nc-1 sub-steps of a frame step's depth decode (reference src/depth_decoder.cpp:249-365:
+// in_proj, 4 pre-norm GQA layers, output norm, head j, argmax feeding the next embedding) run in
+// ONE launch of one CTA per SM. The work is a fixed schedule of phases (DpPhase) separated by
+// grid-wide barriers: a monotonically increasing arrival counter that every CTA bumps once per
+// phase (release) and polls (acquire) before it consumes another CTA's output.
+//
+// Roles inside a CTA (480 threads):
+//   warps 0-3   epilogue group: drains the TMEM accumulators of GEMM units, and runs the
+//               element-wise phases (split-K reduction + residual + norm preparation, attention,
+//               arg-max + next embedding);
+//   warps 4-11  dequantise raw Q8_0 chunks into the 128-byte-swizzled f16 A tile;
+//   warp 12     issues tcgen05.mma (128 x N x 16) and owns the TMEM columns;
+//   warp 13     streams weight chunks with bulk async copies;
+//   warp 14     loads activation chunks with 2-D TMA after the phase's input is complete.
+// Weights never depend on activations, so warps 4-13 run ahead across phase boundaries and
+// keep the next phases' weights streaming while the grid waits at a barrier; only warp 14 and
+// the epilogue group wait for other CTAs.
+//
+// RMSNorm is split around the GEMM it feeds: the reduction phase writes x * w (f16) and each
+// row's sum of squares in 64-column chunks; the consumer applies 1/sqrt(mean + eps) per row
+// after the matrix product (the norm is linear in the row scale), so no phase needs a whole
+// row before the GEMM starts.
+//
+// Every wait is bounded; on a timeout the CTA records an error code in p.err, every other wait
+// notices it and returns, copies and MMAs in flight are drained, TMEM is freed, and the host
+// reports the failure.
+#include "depth_persist.cuh"
+#include "tc_ptx.cuh"
+
+#include <climits>
+#include <stdexcept>
+#include <string>
+
+namespace bzb {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kTileM = 128;
+constexpr int kChunkK = 64;
+constexpr int kABytes = kTileM * kChunkK * 2;            // f16 A stage
+constexpr int kRawBytes = kTileM * kChunkK + 2 * kTileM * 2;  // int8 quants + f16 scales
+constexpr int kRawStages = 10;
+constexpr int kAStages = 4;
+constexpr int kBStages = 4;
+constexpr int kBStageBytes = 128 * kChunkK * 2;          // up to 128 activation rows
+constexpr int kEpiThreads = 128;
+constexpr int kDqThreads = 256;
+constexpr int kMmaWarp = 12, kWeightWarp = 13, kActWarp = 14;
+constexpr int kThreads = 480;
+constexpr int kTmemCols = 256;                           // two 128-column accumulators
+constexpr int kQFloats = 4 * 2 * 128;                    // query heads of one attention task
+constexpr long long kGridSpin = 1ll << 23;
+
+constexpr int kSmemBytes = 1024 + kAStages * kABytes + kBStages * kBStageBytes + kRawStages * kRawBytes +
+                           (kQFloats + 256 + 16) * 4;
+
+#define DCHECK(x)                                                                             \
+    do {                                                                                      \
+        cudaError_t e_ = (x);                                                                 \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA: ") + cudaGetErrorString(e_) + " at " #x); \
+    } while (0)
+
+__device__ __forceinline__ int ld_volatile(const int * p) {
+    int v;
+    asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// bounded mbarrier wait that also gives up as soon as any CTA has recorded an error. It polls
+// with the non-suspending test_wait: on this critical path a suspended waiter is woken later
+// than a spinning one sees the phase flip.
+__device__ __forceinline__ bool dwait(uint64_t * bar, uint32_t parity, int * err) {
+    const uint32_t a = smem_u32(bar);
+    for (long long i = 0; i < kSpinLimit * 16; i++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+        if ((i & 4095) == 4095 && ld_volatile(err)) return false;
+    }
+    atomicExch(err, 2);
+    return false;
+}
+
+// wait until `target` phase arrivals have been counted (every phase before the current one
+// complete on every CTA)
+__device__ __forceinline__ bool grid_wait(const unsigned * bar, unsigned target, int * err) {
+    for (long long i = 0; i < kGridSpin; i++) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+        if (v >= target) return true;
+        if ((i & 63) == 63 && ld_volatile(err)) return false;
+    }
+    atomicExch(err, 3);
+    return false;
+}
+
+__device__ __forceinline__ void grid_arrive(unsigned * bar) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ float wsum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float wmax(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// the phase table is constant for the whole launch: read it through the non-coherent path into
+// registers once per phase, so that stores to the output buffers (which the compiler cannot
+// prove do not alias the table) never force the fields to be reloaded
+__device__ __forceinline__ DpPhase load_phase(const DpPhase * src) {
+    static_assert(sizeof(DpPhase) % 16 == 0, "phase descriptor must be a whole number of 16-byte words");
+    DpPhase out;
+    const uint4 * s = reinterpret_cast<const uint4 *>(src);
+    uint4 * d = reinterpret_cast<uint4 *>(&out);
+#pragma unroll
+    for (int k = 0; k < (int) (sizeof(DpPhase) / 16); k++) d[k] = __ldg(s + k);
+    return out;
+}
+
+// which unit of GEMM phase `i` this CTA runs (valid when below n_units); rotating the
+// assignment spreads the idle CTAs, and with them the early weight streaming, over the grid
+__device__ __forceinline__ int unit_of(int i, int cta, int G) { return (int) (((long long) cta + 17ll * i) % G); }
+
+struct UnitRange {
+    int tile, split, c0, nch;
+};
+__device__ __forceinline__ UnitRange unit_range(const DpPhase ph, int u) {
+    UnitRange r;
+    r.tile = u % ph.MT;
+    r.split = u / ph.MT;
+    r.c0 = r.split * ph.kc_per;
+    r.nch = min(ph.KC - r.c0, ph.kc_per);
+    return r;
+}
+
+constexpr int kMaxSplits = 16;
+constexpr int kArgSplits = 8;   // the head's split-K is capped at this
+
+// x[e] = sum over s < S of P[s * split_stride + off + 32 e], e < 4, with all loads in flight
+// before the first add (a loop that adds as it loads waits one L2 round trip per split)
+__device__ __forceinline__ void sum_partials(const float * P, int S, size_t split_stride, size_t off, float (&x)[4]) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        float v[kMaxSplits];
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; s++) v[s] = s < S ? __ldcg(P + s * split_stride + off + 32 * e) : 0.0f;
+        float a = 0.0f;
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; s++) a += v[s];
+        x[e] = a;
+    }
+}
+
+// NEOX rotation of one 128-wide head held as x[e] = head[lane + 32 e]
+__device__ __forceinline__ void rope128(float (&x)[4], const float2 * cs, int lane) {
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const float2 c = cs[lane + 32 * j];
+        const float x0 = x[j], x1 = x[j + 2];
+        x[j] = x0 * c.x - x1 * c.y;
+        x[j + 2] = x0 * c.y + x1 * c.x;
+    }
+}
+
+// 1 / sqrt(mean square + eps) of a row from its 64-column partial sums (lanes < nch hold one)
+__device__ __forceinline__ float row_scale(const DpParams & p, int row, int lane) {
+    const int nch = p.D / kChunkK;
+    const float s = lane < nch ? __ldcg(p.ss + (size_t) row * nch + lane) : 0.0f;
+    return 1.0f / sqrtf(wsum(s) / (float) p.D + p.eps);
+}
+
+// ---- element-wise phases (epilogue group: 128 threads, warps 0-3) -------------------------
+__device__ void phase_reduce(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane) {
+    const int D = p.D, nch = D / kChunkK, rows = ph.rows;
+    const int W = G * 4;
+    for (int t = cta * 4 + warp; t < rows * nch; t += W) {
+        const int n = t / nch, c = t % nch;
+        const int col = c * kChunkK + 2 * lane;
+        // every partial load is issued before the first add, so the S loads overlap
+        float2 v[kMaxSplits];
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; s++)
+            if (s < ph.S) v[s] = __ldcg(reinterpret_cast<const float2 *>(p.P + ((size_t) s * rows + n) * D + col));
+        const float2 xo = ph.resid ? __ldcg(reinterpret_cast<const float2 *>(p.x + (size_t) n * D + col)) : make_float2(0.0f, 0.0f);
+        float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; s++)
+            if (s < ph.S) {
+                acc.x += v[s].x;
+                acc.y += v[s].y;
+            }
+        const float2 xn = ph.resid ? make_float2(xo.x + acc.x, xo.y + acc.y) : acc;
+        __stcg(reinterpret_cast<float2 *>(p.x + (size_t) n * D + col), xn);
+        const float2 w = *reinterpret_cast<const float2 *>(ph.norm_w + col);
+        half2 h = __floats2half2_rn(xn.x * w.x, xn.y * w.y);
+        __stcg(reinterpret_cast<unsigned *>(p.h16 + (size_t) n * D + col), *reinterpret_cast<unsigned *>(&h));
+        const float sq = wsum(xn.x * xn.x + xn.y * xn.y);
+        if (lane == 0) __stcg(p.ss + (size_t) n * nch + c, sq);
+    }
+}
+
+__device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane, float * sQ) {
+    const int R = p.R, hd = 128, nkv = p.n_kv, nh = p.n_head, D = p.D;
+    const int M = nh * hd + 2 * nkv * hd;
+    const int rows = ph.rows, S = ph.S, n_new = ph.n_new;
+    const int Gq = nh / nkv;  // query heads per kv head (1..4): warps >= Gq only append k/v
+    const bool qwarp = warp < Gq;
+    float * kvl = p.kv + (size_t) ph.layer * p.kv_layer;
+    for (int t = cta; t < R * nkv; t += G) {
+        const int b = t / nkv, g = t % nkv;
+        const int qh = g * Gq + warp;
+        if (!p.row_active[b]) {
+            if (qwarp)
+                for (int i = 0; i < n_new; i++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) p.att16[(size_t) (b + i * R) * D + qh * hd + lane + 32 * e] = __float2half_rn(0.0f);
+            continue;
+        }
+        float scale[2] = { 1.0f, 1.0f };
+        for (int i = 0; i < n_new; i++) scale[i] = row_scale(p, b + i * R, lane);
+        // this task's new keys and values: warp w < 2 n_new handles position w / 2, k or v
+        if (warp < 2 * n_new) {
+            const int i = warp >> 1, isv = warp & 1;
+            const int row = b + i * R, pos = ph.start + i;
+            const int col0 = nh * hd + isv * nkv * hd + g * hd;
+            float x[4];
+            sum_partials(p.P, S, (size_t) rows * M, (size_t) row * M + col0 + lane, x);
+#pragma unroll
+            for (int e = 0; e < 4; e++) x[e] *= scale[i];
+            if (!isv) rope128(x, p.rope + (size_t) pos * (hd / 2), lane);
+            float * dst = kvl + (((size_t) b * p.nc + pos) * 2 + isv) * nkv * hd + (size_t) g * hd;
+#pragma unroll
+            for (int e = 0; e < 4; e++) __stcg(dst + lane + 32 * e, x[e]);
+        }
+        // this warp's query head at each new position
+        for (int i = 0; i < n_new && qwarp; i++) {
+            const int row = b + i * R, pos = ph.start + i;
+            float x[4];
+            sum_partials(p.P, S, (size_t) rows * M, (size_t) row * M + qh * hd + lane, x);
+#pragma unroll
+            for (int e = 0; e < 4; e++) x[e] *= scale[i];
+            rope128(x, p.rope + (size_t) pos * (hd / 2), lane);
+#pragma unroll
+            for (int e = 0; e < 4; e++) sQ[(warp * 2 + i) * hd + lane + 32 * e] = x[e];
+        }
+        epi_sync();  // appended keys/values and the queries visible to the group
+        const float * kb = kvl + (size_t) b * p.nc * 2 * nkv * hd + (size_t) g * hd;
+        const size_t pstride = (size_t) 2 * nkv * hd;  // floats between consecutive positions
+        for (int i = 0; i < n_new && qwarp; i++) {
+            const int lim = ph.start + i + 1;
+            // scores: the warp reads one key row per position (lane = 4 dims), 8 rows in flight;
+            // lane pp % 32 keeps the score of position pp
+            const float4 q4 = *reinterpret_cast<const float4 *>(sQ + (warp * 2 + i) * hd + 4 * lane);
+            float sc[2] = { -INFINITY, -INFINITY };
+            for (int pp0 = 0; pp0 < lim; pp0 += 8) {
+                float4 k4[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    k4[k] = pp0 + k < lim ? __ldcg(reinterpret_cast<const float4 *>(kb + (size_t) (pp0 + k) * pstride) + lane)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int pp = pp0 + k;
+                    const float d = wsum(q4.x * k4[k].x + q4.y * k4[k].y + q4.z * k4[k].z + q4.w * k4[k].w);
+                    if (pp < lim && lane == (pp & 31)) sc[pp >> 5] = d * p.attn_scale;
+                }
+            }
+            const float mx = wmax(fmaxf(sc[0], sc[1]));
+            const float pr0 = lane < lim ? expf(sc[0] - mx) : 0.0f;
+            const float pr1 = lane + 32 < lim ? expf(sc[1] - mx) : 0.0f;
+            const float l = wsum(pr0 + pr1);
+            // values: 8 rows in flight, lane = dims lane + 32 e
+            float o[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+            for (int pp0 = 0; pp0 < lim; pp0 += 8) {
+                float vv[8][4];
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        vv[k][e] = pp0 + k < lim ? __ldcg(kb + (size_t) (pp0 + k) * pstride + nkv * hd + lane + 32 * e) : 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int pp = pp0 + k;
+                    const float pj = __shfl_sync(0xffffffffu, pp < 32 ? pr0 : pr1, pp & 31);
+                    if (pp < lim)
+#pragma unroll
+                        for (int e = 0; e < 4; e++) o[e] += pj * vv[k][e];
+                }
+            }
+            const float inv = 1.0f / l;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                p.att16[(size_t) (b + i * R) * D + qh * hd + lane + 32 * e] = __float2half_rn(o[e] * inv);
+        }
+        epi_sync();  // sQ is reused by the next task
+    }
+}
+
+__device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int G, int tid, int warp, int lane,
+                             float * sMisc) {
+    const int R = p.R, V = p.vs, nc = p.nc, j = ph.j;
+    float * sv = sMisc;
+    int * si = reinterpret_cast<int *>(sMisc + 4);
+    int * scode = reinterpret_cast<int *>(sMisc + 8);
+    float * sscale = sMisc + 9;
+    for (int b = cta; b < R; b += G) {
+        if (!p.row_active[b]) {
+            if (tid == 0) p.frames[(size_t) b * nc + j] = -1;
+            continue;
+        }
+        if (warp == 0) {
+            const float s = row_scale(p, ph.ss_row0 + b, lane);
+            if (lane == 0) *sscale = s;
+        }
+        epi_sync();
+        const float scale = *sscale;
+        float best = -INFINITY;
+        int bi = INT_MAX;
+        // 8 columns per pass, all S partial loads of the pass issued before the adds
+        for (int v0 = tid; v0 < V; v0 += 8 * kEpiThreads) {
+            float part[kArgSplits][8];
+#pragma unroll
+            for (int s = 0; s < kArgSplits; s++)
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int v = v0 + k * kEpiThreads;
+                    part[s][k] = (s < ph.S && v < V) ? __ldcg(p.P + ((size_t) s * R + b) * V + v) : 0.0f;
+                }
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int v = v0 + k * kEpiThreads;
+                if (v >= V) break;
+                float a = 0.0f;
+#pragma unroll
+                for (int s = 0; s < kArgSplits; s++)
+                    if (s < ph.S) a += part[s][k];
+                const float logit = a * scale;
+                if (p.logits_out) p.logits_out[((size_t) b * (nc - 1) + (j - 1)) * V + v] = logit;
+                if (logit > best || (bi == INT_MAX && !(logit < best))) {
+                    best = logit;
+                    bi = v;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            sv[warp] = best;
+            si[warp] = bi;
+        }
+        epi_sync();
+        if (tid == 0) {
+            float bv = sv[0];
+            int i0 = si[0];
+            for (int w = 1; w < 4; w++)
+                if (sv[w] > bv || (sv[w] == bv && si[w] < i0)) {
+                    bv = sv[w];
+                    i0 = si[w];
+                }
+            if (i0 == INT_MAX) i0 = 0;
+            p.frames[(size_t) b * nc + j] = i0;
+            *scode = i0;
+        }
+        epi_sync();
+        if (j + 1 < nc) {
+            int next = p.forced ? p.forced[(size_t) b * (nc - 1) + (j - 1)] : *scode;
+            if (next < 0 || next >= V) next = 0;
+            const size_t row = (size_t) j * V + next;
+            const int8_t * q = p.embd.qs + row * p.embd.K;
+            const half * d = p.embd.ds + row * (p.embd.K / 32);
+            for (int c = tid; c < p.embd.K / 8; c += kEpiThreads) {
+                const uint2 u = *reinterpret_cast<const uint2 *>(q + c * 8);
+                const float sc = __half2float(d[c >> 2]);
+                const int8_t * bq = reinterpret_cast<const int8_t *>(&u);
+                half2 o[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) o[k] = __floats2half2_rn((float) bq[2 * k] * sc, (float) bq[2 * k + 1] * sc);
+                __stcg(reinterpret_cast<uint4 *>(p.din16 + (size_t) b * p.H + c * 8), *reinterpret_cast<uint4 *>(o));
+            }
+        }
+        epi_sync();  // sMisc is reused by the next row
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpParams p, const __grid_constant__ DpMaps maps) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+    __shared__ uint64_t a_full[kAStages], a_empty[kAStages], b_full[kBStages], b_empty[kBStages];
+    __shared__ uint64_t acc_full[2], acc_empty[2], drain_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int s_abort;
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    uint8_t * sA = smem;
+    uint8_t * sB = sA + kAStages * kABytes;
+    uint8_t * sR = sB + kBStages * kBStageBytes;
+    float * sQ = reinterpret_cast<float *>(sR + kRawStages * kRawBytes);
+    float * sScale = sQ + kQFloats;
+    float * sMisc = sScale + 256;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    int * err = p.err;
+
+    if (warp == kMmaWarp) tmem_alloc(&tmem_slot, kTmemCols);
+    if (tid == 0) {
+        for (int i = 0; i < kRawStages; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kDqThreads);
+        }
+        for (int i = 0; i < kAStages; i++) {
+            mbar_init(&a_full[i], kDqThreads);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < kBStages; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kEpiThreads);
+        }
+        mbar_init(&drain_bar, 1);
+        s_abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp < 4) {
+        // ---------------------------------------------------------------- epilogue group
+        // s_stop is written by thread 0 only between two group barriers, so the whole group
+        // reads one value and leaves the loop together (a partial group would stall bar.sync)
+        __shared__ int s_stop;
+        uint32_t uc = 0;
+        for (int i = 0; i < p.n_phases; i++) {
+            const DpPhase ph = load_phase(p.phases + i);
+            if (tid == 0) {
+                s_stop = (s_abort || !grid_wait(p.bar, (unsigned) i * G, err)) ? 1 : 0;
+                if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots] = gtimer();
+            }
+            epi_sync();
+            if (s_stop) break;
+            if (ph.type == DP_GEMM) {
+                const int u = unit_of(i, cta, G);
+                if (u < ph.n_units) {
+                    const UnitRange ur = unit_range(ph, u);
+                    if (ph.epi == DPE_SWIGLU) {
+                        // per-row RMS scale of this phase's activation rows
+                        for (int n = warp; n < ph.nb; n += 4) {
+                            const float s = row_scale(p, ph.ss_row0 + n, lane);
+                            if (lane == 0) sScale[n] = s;
+                        }
+                        epi_sync();
+                    }
+                    const int acc = uc & 1;
+                    bool ok = dwait(&acc_full[acc], (uc >> 1) & 1, err);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (p.trace && tid == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 6] = gtimer();
+                    tc_fence_after();
+                    const uint32_t taddr = tmem + (uint32_t) (acc * 128) + ((uint32_t) (32 * warp) << 16);
+                    const int m_loc = 32 * warp + lane;
+                    if (ok) {
+                        for (int n0 = 0; n0 < ph.nb; n0 += 16) {
+                            float v[16];
+                            tmem_ld16(taddr + n0, v);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
+                            if (ph.epi == DPE_PARTIAL) {
+                                const int m = ur.tile * kTileM + m_loc;
+                                if (m < ph.M) {
+                                    float * dst = p.P + (size_t) ur.split * ph.rows * ph.M + m;
+#pragma unroll
+                                    for (int e = 0; e < 16; e++)
+                                        if (n0 + e < ph.rows) __stcg(dst + (size_t) (n0 + e) * ph.M, v[e]);
+                                }
+                            } else {
+                                // 16-row gate/up interleave: lanes 0-15 hold gate rows, lanes 16-31 the
+                                // matching up rows. Partners swap values so that every lane finishes
+                                // half of the columns: lane l < 16 the even ones, lane l + 16 the odd.
+                                const int pr = lane & 15;
+                                const int jc = ur.tile * (kTileM / 2) + 16 * warp + pr;
+                                const bool gate_lane = lane < 16;
+#pragma unroll
+                                for (int e = 0; e < 16; e++) {
+                                    const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
+                                    const int n = n0 + e;
+                                    if ((e & 1) == (gate_lane ? 0 : 1) && n < ph.rows && jc < ph.out_ld) {
+                                        const float sc = sScale[n];
+                                        const float gt = (gate_lane ? v[e] : other) * sc;
+                                        const float up = (gate_lane ? other : v[e]) * sc;
+                                        const float act = __fdividef(gt, 1.0f + __expf(-gt));
+                                        p.g16[(size_t) n * p.ffn + jc] = __float2half_rn(act * up);
+                                    }
+                                }
+                            }
+                        }
+                    } else if (tid == 0) {
+                        s_abort = 1;
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&acc_empty[acc]);
+                    uc++;
+                }
+            } else if (ph.type == DP_REDUCE) {
+                phase_reduce(p, ph, cta, G, warp, lane);
+            } else if (ph.type == DP_ATTN) {
+                phase_attn(p, ph, cta, G, warp, lane, sQ);
+            } else {
+                phase_argmax(p, ph, cta, G, tid, warp, lane, sMisc);
+            }
+            epi_sync();
+            if (tid == 0) {
+                if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 1] = gtimer();
+                __threadfence();
+                fence_proxy_async_global();
+                grid_arrive(p.bar);
+            }
+        }
+        if (tid == 0 && (s_abort || s_stop)) atomicCAS(err, 0, 4);
+    } else if (warp < 4 + kDqThreads / 32) {
+        // ---------------------------------------------------------------- dequantising producers
+        const int t = tid - kEpiThreads;
+        const int r = t & (kTileM - 1), hb = t >> 7;
+        uint32_t rc = 0;
+        bool ok = true;
+        for (int i = 0; i < p.n_phases && ok; i++) {
+            const DpPhase ph = load_phase(p.phases + i);
+            if (ph.type != DP_GEMM) continue;
+            const int u = unit_of(i, cta, G);
+            if (u >= ph.n_units) continue;
+            const UnitRange ur = unit_range(ph, u);
+            for (int c = 0; c < ur.nch && ok; c++, rc++) {
+                const int rs = rc % kRawStages, ab = rc % kAStages;
+                ok = dwait(&raw_full[rs], (rc / kRawStages) & 1u, err);
+                if (!ok) break;
+                if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
+                const uint8_t * raw = sR + rs * kRawBytes;
+                const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
+                const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
+                const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
+                mbar_arrive(&raw_empty[rs]);
+                if (rc >= kAStages) ok = dwait(&a_empty[ab], ((rc / kAStages) - 1) & 1u, err);
+                if (!ok) break;
+                const half2 s2 = __halves2half2(sc, sc);
+                const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
+                uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    uint4 o;
+                    dq4(w8[2 * q], s2, o.x, o.y);
+                    dq4(w8[2 * q + 1], s2, o.z, o.w);
+                    const int jj = hb * 4 + q;
+                    *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
+                }
+                fence_proxy_async();
+                mbar_arrive(&a_full[ab]);
+                if (p.trace && t == 0 && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 25 + c] = gtimer();
+            }
+        }
+        if (!ok) s_abort = 1;
+    } else if (warp == kMmaWarp) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            uint32_t ck = 0, uc = 0;
+            bool ok = true;
+            for (int i = 0; i < p.n_phases && ok; i++) {
+                const DpPhase ph = load_phase(p.phases + i);
+                if (ph.type != DP_GEMM) continue;
+                const int u = unit_of(i, cta, G);
+                if (u >= ph.n_units) continue;
+                const UnitRange ur = unit_range(ph, u);
+                const int acc = uc & 1;
+                if (uc >= 2) ok = dwait(&acc_empty[acc], ((uc >> 1) - 1) & 1u, err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t idesc = (1u << 4) | ((uint32_t) (ph.nb >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
+                const uint32_t d = tmem + (uint32_t) (acc * 128);
+                for (int c = 0; c < ur.nch; c++, ck++) {
+                    const int ab = ck % kAStages, bb = ck % kBStages;
+                    ok = dwait(&b_full[bb], (ck / kBStages) & 1u, err);
+                    if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 3] = gtimer();
+                    if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 9 + c] = gtimer();
+                    ok = ok && dwait(&a_full[ab], (ck / kAStages) & 1u, err);
+                    if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 4] = gtimer();
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kBStageBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kChunkK / 16; kk++)
+                        umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (c > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&a_empty[ab]);
+                    umma_commit(&b_empty[bb]);
+                    if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 41 + c] = gtimer();
+                }
+                if (!ok) break;
+                if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 5] = gtimer();
+                umma_commit(&acc_full[acc]);
+                uc++;
+            }
+            // every MMA issued above has completed before TMEM is released
+            umma_commit(&drain_bar);
+            dwait(&drain_bar, 0, err);
+            if (!ok) s_abort = 1;
+        }
+    } else if (warp == kWeightWarp) {
+        // ---------------------------------------------------------------- weight stream
+        if (lane == 0) {
+            uint32_t rc = 0;
+            bool ok = true;
+            for (int i = 0; i < p.n_phases && ok; i++) {
+                const DpPhase ph = load_phase(p.phases + i);
+                if (ph.type != DP_GEMM) continue;
+                const int u = unit_of(i, cta, G);
+                if (u >= ph.n_units) continue;
+                const UnitRange ur = unit_range(ph, u);
+                const uint8_t * qbase = reinterpret_cast<const uint8_t *>(ph.qs) + (size_t) (ur.tile * ph.KC + ur.c0) * kTileM * kChunkK;
+                const uint8_t * dbase = reinterpret_cast<const uint8_t *>(ph.ds) + (size_t) (ur.tile * ph.KC + ur.c0) * 2 * kTileM * 2;
+                for (int c = 0; c < ur.nch; c++, rc++) {
+                    const int rs = rc % kRawStages;
+                    if (rc >= kRawStages) ok = dwait(&raw_empty[rs], ((rc / kRawStages) - 1) & 1u, err);
+                    if (!ok) break;
+                    uint8_t * raw = sR + rs * kRawBytes;
+                    if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 7] = gtimer();
+                    mbar_expect_tx(&raw_full[rs], kRawBytes);
+                    bulk_g2s(raw, qbase + (size_t) c * kTileM * kChunkK, kTileM * kChunkK, &raw_full[rs]);
+                    bulk_g2s(raw + kTileM * kChunkK, dbase + (size_t) c * 2 * kTileM * 2, 2 * kTileM * 2, &raw_full[rs]);
+                }
+            }
+            // copies still in flight land before the CTA exits
+            for (uint32_t k = rc > (uint32_t) kRawStages ? rc - kRawStages : 0; k < rc; k++)
+                dwait(&raw_full[k % kRawStages], (k / kRawStages) & 1u, err);
+            if (!ok) s_abort = 1;
+        }
+    } else {
+        // ---------------------------------------------------------------- activation loads
+        if (lane == 0) {
+            uint32_t bc = 0;
+            bool ok = true;
+            for (int i = 0; i < p.n_phases && ok; i++) {
+                const DpPhase ph = load_phase(p.phases + i);
+                if (ph.type != DP_GEMM) continue;
+                const int u = unit_of(i, cta, G);
+                if (u >= ph.n_units) continue;
+                const UnitRange ur = unit_range(ph, u);
+                ok = grid_wait(p.bar, (unsigned) i * G, err);
+                if (!ok) break;
+                fence_proxy_async_global();
+                if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 2] = gtimer();
+                const uint32_t bytes = (uint32_t) ph.nb * kChunkK * 2;
+                for (int c = 0; c < ur.nch; c++, bc++) {
+                    const int bb = bc % kBStages;
+                    if (bc >= kBStages) ok = dwait(&b_empty[bb], ((bc / kBStages) - 1) & 1u, err);
+                    if (!ok) break;
+                    mbar_expect_tx(&b_full[bb], bytes);
+                    tma_2d(sB + bb * kBStageBytes, &maps.m[ph.map], (ur.c0 + c) * kChunkK, ph.b_row0, &b_full[bb]);
+                }
+            }
+            for (uint32_t k = bc > (uint32_t) kBStages ? bc - kBStages : 0; k < bc; k++)
+                dwait(&b_full[k % kBStages], (k / kBStages) & 1u, err);
+            if (!ok) s_abort = 1;
+        }
+    }
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+int depth_persist_grid() {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, depth_persist_kernel, kThreads, kSmemBytes) != cudaSuccess)
+        return 0;
+    return per_sm >= 1 ? sms : 0;
+}
+
+void init_depth_persist_attributes() {
+    DCHECK(cudaFuncSetAttribute(depth_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    DCHECK(cudaFuncSetAttribute(depth_persist_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+}
+
+void launch_depth_persist(const DpParams & p, const DpMaps & maps, int grid, cudaStream_t s) {
+    if (grid <= 0) throw std::runtime_error("persistent depth decoder: no grid");
+    DCHECK(cudaMemsetAsync(p.bar, 0, sizeof(unsigned), s));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    // all CTAs must be resident at once: the phase barriers wait for every one of them
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    DCHECK(cudaLaunchKernelEx(&cfg, depth_persist_kernel, p, maps));
+}
+
+}  // namespace bzb

@@ -1,0 +1,84 @@
+// Persistent depth decoder: every sub-step of one frame step's depth decode (codebooks 1..nc-1,
+// reference src/depth_decoder.cpp:249-365) in one launch of one CTA per SM, with grid-wide
+// phase barriers instead of kernel boundaries.
+#pragma once
+
+#include "kernels.cuh"
+
+#include <cuda.h>
+
+namespace bzb {
+
+enum DpType { DP_GEMM = 0, DP_REDUCE = 1, DP_ATTN = 2, DP_ARGMAX = 3 };
+enum DpEpi { DPE_PARTIAL = 0, DPE_SWIGLU = 1 };
+constexpr int kDpTraceSlots = 57;  // 9 phase events + 3 x 16 per-chunk events
+
+// One phase of the schedule. GEMM phases split a Q8_0 matrix (tcgen05 layout) into units of one
+// 128-row tile and one K range; a CTA runs at most one unit per phase.
+struct alignas(16) DpPhase {
+    int type = DP_GEMM;
+    // GEMM
+    const uint4 * qs = nullptr;
+    const half * ds = nullptr;
+    int MT = 0, KC = 0, M = 0, splits = 1, kc_per = 0, n_units = 0;
+    int map = 0;        // activation tensor map (DpMaps index)
+    int b_row0 = 0;     // first activation row read
+    int nb = 0;         // MMA N: activation rows per tile, a multiple of 16
+    int rows = 0;       // activation rows whose results are kept
+    int epi = DPE_PARTIAL;
+    int out_ld = 0;     // partial: the matrix rows M; SwiGLU: the FFN width
+    int ss_row0 = 0;    // rows whose RMS scale applies (SwiGLU, arg-max) start here in `ss`
+    // consumers of partials
+    int S = 1;          // splits of the GEMM that produced the partials
+    int resid = 0;      // REDUCE: add the sum into the residual stream
+    const float * norm_w = nullptr;  // REDUCE: weight of the norm that the next GEMM applies
+    int layer = 0, start = 0, n_new = 1;  // ATTN
+    int j = 0;          // ARGMAX: codebook
+};
+
+struct DpMaps {
+    CUtensorMap m[8];   // {in, h, att, ff} x {2R rows, R rows}
+};
+
+struct DpParams {
+    const DpPhase * phases = nullptr;
+    int n_phases = 0;
+    int R = 0, nc = 0, vs = 0, D = 0, H = 0, ffn = 0, n_head = 0, n_kv = 0, hd = 0;
+    float eps = 0.0f, attn_scale = 0.0f;
+    const float2 * rope = nullptr;      // [positions][hd/2] (cos, sin)
+    float * kv = nullptr;               // depth cache, layer stride kv_layer
+    size_t kv_layer = 0;
+    float * P = nullptr;                // split-K partials [S][rows][M]
+    float * x = nullptr;                // residual stream [2R][D] f32
+    half * h16 = nullptr;               // x * norm weight [2R][D] (the next GEMM's input)
+    float * ss = nullptr;               // per-row sums of squares in 64-column chunks [2R][D/64]
+    half * att16 = nullptr;             // attention output [2R][D]
+    half * g16 = nullptr;               // SwiGLU output [2R][ffn]
+    half * din16 = nullptr;             // in_proj input [2R][H]
+    QRows embd;                         // audio embedding table
+    const int * row_active = nullptr;   // [R]
+    int * frames = nullptr;             // [R][nc]
+    const int * forced = nullptr;       // [R][nc-1] teacher-forced codes, or null
+    float * logits_out = nullptr;       // [R][nc-1][vs] or null
+    unsigned * bar = nullptr;           // phase-arrival counter, zero at launch
+    int * err = nullptr;
+    // optional timeline [n_phases][grid][kDpTraceSlots] of %globaltimer (ns) per CTA and phase:
+    // 0 epilogue start, 1 epilogue end, 2 activation loads start, 3 first activation chunk
+    // landed, 4 first weight tile dequantised, 5 last MMA issued, 6 accumulator ready,
+    // 7 first weight copy issued, 8 first weight chunk landed; for chunks c < 16 of the unit:
+    // 9 + c activation chunk landed, 25 + c weight tile dequantised, 41 + c MMAs issued;
+    // null in production launches
+    unsigned long long * trace = nullptr;
+};
+
+// activation rows [rows][K] f16 with row stride ldx, read as 64 x box_rows tiles in the
+// 128-byte swizzle; rows past `rows` read as zero (umma_gemm.cu)
+CUtensorMap make_x_map(const half * x, int K, int ldx, int rows, int box_rows);
+
+// grid size (CTAs) of the persistent kernel on the current device; 0 when it cannot run
+int depth_persist_grid();
+void init_depth_persist_attributes();
+// the counter at p.bar must be zero (the launcher clears it on `s` first)
+void launch_depth_persist(const DpParams & p, const DpMaps & maps, int grid, cudaStream_t s);
+
+}  // namespace bzb

@@ -199,9 +199,12 @@ Engine::Engine(const std::string & path, int dev) : device(dev) {
     CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     init_kernel_attributes();
     init_umma_attributes();
+    init_depth_persist_attributes();
     {
         const char * e = std::getenv("BZB_GEMM");
         use_umma_ = !(e && std::string(e) == "mma");
+        const char * d = std::getenv("BZB_DEPTH_PERSIST");
+        use_dp_ = use_umma_ && !(d && d[0] == '0');
     }
     std::string err;
     if (!gg_.open(path, err)) throw std::runtime_error(err);
@@ -373,6 +376,14 @@ void Engine::alloc_buffers() {
     scr_.n_counters = 1 << 16;
     scr_.counters = dalloc<int>(scr_.n_counters);
     CK(cudaMemsetAsync(scr_.counters, 0, (size_t) scr_.n_counters * sizeof(int), stream_));
+    // persistent depth decoder: split-K partials for up to 16 splits of the widest depth
+    // matrix at 2 x 64 rows (or of the head at 64 rows), row norm sums, phase counter
+    dp_grid_ = depth_persist_grid();
+    dp_P_floats_ = std::max((size_t) 16 * 128 * std::max(dd.hidden, ddq + 2 * ddkv), (size_t) 16 * 64 * cfg.vs);
+    dp_P_ = dalloc<float>(dp_P_floats_);
+    dp_ss_ = dalloc<float>((size_t) 256 * std::max(1, dd.hidden / 64));
+    CK(cudaMemsetAsync(dp_ss_, 0, (size_t) 256 * std::max(1, dd.hidden / 64) * sizeof(float), stream_));
+    dp_bar_ = dalloc<unsigned>(1);
     CK(cudaMemsetAsync(din16_, 0, (size_t) R2 * H * sizeof(half), stream_));
     CK(cudaMemsetAsync(dkv_, 0, (size_t) dd.n_layer * rmax_ * nc * 2 * ddkv * sizeof(float), stream_));
 }
@@ -472,6 +483,142 @@ void Engine::bb_decode_layer(int l, int R) {
     gemv(w.down, bff16_, bb.ffn, R, GemvOut{ EPI_RESID, bx_, nullptr, H });
 }
 
+bool Engine::dp_supported(int R) const {
+    const DdConfig & dd = cfg.dd;
+    if (!use_dp_ || dp_grid_ <= 0 || R < 1 || R > 64) return false;
+    if (dd.hd != 128 || dd.n_kv <= 0 || dd.n_head % dd.n_kv || dd.n_head > 4 * dd.n_kv || dd.n_head * dd.hd != dd.hidden)
+        return false;
+    if (dd.hidden % 64 || cfg.hidden % 64 || dd.ffn % 64 || dd.hidden / 64 > 32) return false;
+    if (!dd_in_.u.qs) return false;
+    for (const LayerW & w : dd_)
+        if (!w.qkv.u.qs || !w.o.u.qs || !w.gu.u.qs || !w.down.u.qs || w.gu.u.MT > dp_grid_) return false;
+    for (const QMat & h : dd_head_)
+        if (!h.u.qs) return false;
+    return true;
+}
+
+const Engine::DpPlan * Engine::depth_plan(int R) {
+    if (!dp_supported(R)) return nullptr;
+    auto it = dp_plans_.find(R);
+    if (it != dp_plans_.end()) return &it->second;
+    const DdConfig & dd = cfg.dd;
+    const int D = dd.hidden, H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, G = dp_grid_;
+    const int qkvd = dd.n_head * dd.hd + 2 * dd.n_kv * dd.hd;
+    const int NB1 = round_up(R, 16), NB2 = round_up(2 * R, 16);
+    std::vector<DpPhase> ph;
+    // a GEMM phase over at most one unit per CTA: split K (up to 16 ways) while tiles leave
+    // CTAs idle; returns the split count its consumer sums over
+    auto gemm = [&](const UMat & w, int map, int b_row0, int nb, int rows, int epi, int out_ld, int max_splits = 16) {
+        DpPhase q;
+        q.type = DP_GEMM;
+        q.qs = w.qs; q.ds = w.ds; q.MT = w.MT; q.KC = w.KC; q.M = w.M;
+        int S = epi == DPE_PARTIAL ? std::max(1, std::min(max_splits, std::min(w.KC, G / w.MT))) : 1;
+        q.kc_per = (w.KC + S - 1) / S;
+        S = (w.KC + q.kc_per - 1) / q.kc_per;
+        if (w.MT * S > G) throw std::runtime_error("persistent depth decoder: a matrix has more tiles than CTAs");
+        if (epi == DPE_PARTIAL && (size_t) S * rows * w.M > dp_P_floats_)
+            throw std::runtime_error("persistent depth decoder: partial buffer too small");
+        q.splits = S; q.n_units = w.MT * S;
+        q.map = map; q.b_row0 = b_row0; q.nb = nb; q.rows = rows; q.epi = epi; q.out_ld = out_ld;
+        ph.push_back(q);
+        return S;
+    };
+    auto reduce = [&](int S, int rows, int resid, const float * norm_w) {
+        DpPhase q;
+        q.type = DP_REDUCE; q.S = S; q.rows = rows; q.resid = resid; q.norm_w = norm_w;
+        ph.push_back(q);
+    };
+    for (int j = 1; j < nc; j++) {
+        const bool first = j == 1;
+        const int rows = first ? 2 * R : R, nb = first ? NB2 : NB1, sel = first ? 0 : 1;
+        int S = gemm(dd_in_.u, 0 + sel, 0, nb, rows, DPE_PARTIAL, D);
+        reduce(S, rows, 0, dd_[0].attn_norm);
+        for (int l = 0; l < dd.n_layer; l++) {
+            const LayerW & w = dd_[l];
+            if (w.qkv.u.M != qkvd) throw std::runtime_error("persistent depth decoder: unexpected qkv rows");
+            S = gemm(w.qkv.u, 2 + sel, 0, nb, rows, DPE_PARTIAL, qkvd);
+            DpPhase a;
+            a.type = DP_ATTN; a.S = S; a.rows = rows; a.layer = l; a.start = first ? 0 : j; a.n_new = first ? 2 : 1;
+            ph.push_back(a);
+            S = gemm(w.o.u, 4 + sel, 0, nb, rows, DPE_PARTIAL, D);
+            reduce(S, rows, 1, w.ffn_norm);
+            gemm(w.gu.u, 2 + sel, 0, nb, rows, DPE_SWIGLU, dd.ffn);
+            S = gemm(w.down.u, 6 + sel, 0, nb, rows, DPE_PARTIAL, D);
+            reduce(S, rows, 1, l + 1 < dd.n_layer ? dd_[l + 1].attn_norm : dd_out_norm_);
+        }
+        // the head reads the position-1 rows in the first sub-step
+        S = gemm(dd_head_[j - 1].u, 3, first ? R : 0, NB1, R, DPE_PARTIAL, vs, 8);  // arg-max sums <= 8 splits
+        DpPhase am;
+        am.type = DP_ARGMAX; am.S = S; am.j = j; am.ss_row0 = first ? R : 0;
+        ph.push_back(am);
+    }
+    DpPlan plan;
+    plan.n = (int) ph.size();
+    plan.dev = dalloc<DpPhase>(ph.size());
+    CK(cudaMemcpyAsync(plan.dev, ph.data(), ph.size() * sizeof(DpPhase), cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    plan.maps.m[0] = make_x_map(din16_, H, H, 2 * R, NB2);
+    plan.maps.m[1] = make_x_map(din16_, H, H, 2 * R, NB1);
+    plan.maps.m[2] = make_x_map(dh16_, D, D, 2 * R, NB2);
+    plan.maps.m[3] = make_x_map(dh16_, D, D, 2 * R, NB1);
+    plan.maps.m[4] = make_x_map(datt16_, D, D, 2 * R, NB2);
+    plan.maps.m[5] = make_x_map(datt16_, D, D, 2 * R, NB1);
+    plan.maps.m[6] = make_x_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB2);
+    plan.maps.m[7] = make_x_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB1);
+    return &(dp_plans_[R] = plan);
+}
+
+int Engine::depth_trace(double * out, int max_phases) {
+    if (cur_R_ == 0) throw std::runtime_error("no batch has been stepped yet");
+    const DpPlan * pl = depth_plan(cur_R_);
+    if (!pl) return 0;
+    const int G = dp_grid_, n = pl->n, K = kDpTraceSlots;
+    const size_t count = (size_t) n * G * K;
+    const size_t total = 3 + (size_t) n + count;
+    if (!out) return (int) total;
+    if ((size_t) max_phases < total) throw std::runtime_error("depth_trace: output needs " + std::to_string(total) + " doubles");
+    unsigned long long * tr = nullptr;
+    CK(cudaMalloc(&tr, count * sizeof(unsigned long long)));
+    CK(cudaMemsetAsync(tr, 0, count * sizeof(unsigned long long), stream_));
+    enqueue_depth(cur_R_, nullptr, nullptr, tr);
+    std::vector<unsigned long long> h(count);
+    CK(cudaMemcpyAsync(h.data(), tr, count * sizeof(unsigned long long), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    cudaFree(tr);
+    unsigned long long t0 = ~0ull;
+    for (int c = 0; c < G; c++) t0 = std::min(t0, h[(size_t) c * K]);
+    std::vector<DpPhase> ph(n);
+    CK(cudaMemcpy(ph.data(), pl->dev, n * sizeof(DpPhase), cudaMemcpyDeviceToHost));
+    out[0] = n;
+    out[1] = G;
+    out[2] = K;
+    for (int i = 0; i < n; i++) out[3 + i] = ph[i].type;
+    // microseconds from the first CTA's start; slots never written are -1
+    double * tl = out + 3 + n;
+    for (size_t i = 0; i < count; i++) tl[i] = h[i] ? (double) (long long) (h[i] - t0) * 1e-3 : -1.0;
+    return (int) total;
+}
+
+void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace) {
+    const DpPlan * pl = depth_plan(R);
+    if (!pl) throw std::runtime_error("persistent depth decoder: unsupported batch");
+    const DdConfig & dd = cfg.dd;
+    DpParams p;
+    p.phases = pl->dev; p.n_phases = pl->n;
+    p.R = R; p.nc = cfg.nc; p.vs = cfg.vs; p.D = dd.hidden; p.H = cfg.hidden; p.ffn = dd.ffn;
+    p.n_head = dd.n_head; p.n_kv = dd.n_kv; p.hd = dd.hd;
+    p.eps = dd.eps; p.attn_scale = 1.0f / std::sqrt((float) dd.hd);
+    p.rope = rope_dd_;
+    p.kv = dkv_; p.kv_layer = (size_t) rmax_ * cfg.nc * 2 * dd.n_kv * dd.hd;
+    p.P = dp_P_; p.x = dx_; p.h16 = dh16_; p.ss = dp_ss_; p.att16 = datt16_; p.g16 = dff16_; p.din16 = din16_;
+    p.embd = audio_embd_;
+    p.row_active = row_active_; p.frames = cur_frames_;
+    p.forced = forced_dev; p.logits_out = logits_dev;
+    p.bar = dp_bar_; p.err = err_; p.trace = trace;
+    launch_depth_persist(p, pl->maps, dp_grid_, stream_);
+    launches_ += 2;
+}
+
 void Engine::enqueue_step(int R) {
     const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, D = cfg.dd.hidden;
     StepArgs sa;
@@ -479,18 +626,23 @@ void Engine::enqueue_step(int R) {
     sa.row_slot = row_slot_; sa.row_active = row_active_; sa.st = st_; sa.hid32 = hid32_; sa.embd = audio_embd_;
     sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
     launch_step_init(sa, stream_);
-    // depth sub-step 1: position 0 = backbone hidden, position 1 = cb0 embedding
-    gemv(dd_in_, din16_, H, 2 * R, GemvOut{ EPI_STORE, dx_, nullptr, D });
-    for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, 2 * R, R, 2, 0);
-    launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, R, R, nullptr, stream_);
-    gemv(dd_head_[0], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
-    launch_argmax_gather(sa, dlog_, vs, vs, 1, nc > 2 ? 1 : -1, stream_);
-    for (int j = 2; j < nc; j++) {
-        gemv(dd_in_, din16_, H, R, GemvOut{ EPI_STORE, dx_, nullptr, D });
-        for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, R, R, 1, j);
-        launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, 0, R, nullptr, stream_);
-        gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
-        launch_argmax_gather(sa, dlog_, vs, vs, j, j + 1 < nc ? j : -1, stream_);
+    if (dp_supported(R)) {
+        // all nc-1 depth sub-steps in one persistent launch
+        enqueue_depth(R, nullptr, nullptr);
+    } else {
+        // depth sub-step 1: position 0 = backbone hidden, position 1 = cb0 embedding
+        gemv(dd_in_, din16_, H, 2 * R, GemvOut{ EPI_STORE, dx_, nullptr, D });
+        for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, 2 * R, R, 2, 0);
+        launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, R, R, nullptr, stream_);
+        gemv(dd_head_[0], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+        launch_argmax_gather(sa, dlog_, vs, vs, 1, nc > 2 ? 1 : -1, stream_);
+        for (int j = 2; j < nc; j++) {
+            gemv(dd_in_, din16_, H, R, GemvOut{ EPI_STORE, dx_, nullptr, D });
+            for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, R, R, 1, j);
+            launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, 0, R, nullptr, stream_);
+            gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+            launch_argmax_gather(sa, dlog_, vs, vs, j, j + 1 < nc ? j : -1, stream_);
+        }
     }
     // backbone: one token per session over its own paged cache
     launch_audio_embed(audio_embd_, cur_frames_, nc, nc, vs, R, bx_, row_active_, stream_);
@@ -513,6 +665,7 @@ cudaGraphExec_t Engine::graph_for(int R) {
     auto it = graphs_.find(key);
     if (it != graphs_.end()) return it->second;
     cudaGraph_t g = nullptr;
+    depth_plan(R);  // uploads the persistent schedule outside the capture
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     set_pdl_scope(true);
     try {
@@ -577,7 +730,9 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     int errv = 0;
     CK(cudaMemcpyAsync(&errv, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
-    if (errv) throw std::runtime_error("a tensor-core pipeline wait timed out inside the frame step");
+    if (errv)
+        throw std::runtime_error("a bounded wait timed out inside the frame step (device error code " +
+                                 std::to_string(errv) + ")");
     for (int k = 0; k < K; k++) res.steps_executed += aa[k] ? 1 : 0;
     const int wcopy = std::min(width, nc);
     for (int k = 0; k < K; k++) {
@@ -848,6 +1003,33 @@ void Engine::debug_depth(int n, const float * hidden, const int * cb0, const int
     sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
     std::vector<float> lg((size_t) R * vs);
     std::vector<int> fr((size_t) R * nc);
+    if (dp_supported(R)) {
+        // the same persistent launch the frame step uses, with teacher forcing and logits out
+        int * fd = nullptr;
+        float * ld = nullptr;
+        CK(cudaMalloc(&ld, (size_t) R * (nc - 1) * vs * sizeof(float)));
+        if (forced) {
+            std::vector<int> f((size_t) R * (nc - 1), 0);
+            std::memcpy(f.data(), forced, (size_t) n * (nc - 1) * sizeof(int));
+            CK(cudaMalloc(&fd, f.size() * sizeof(int)));
+            CK(cudaMemcpyAsync(fd, f.data(), f.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        }
+        depth_plan(R);
+        enqueue_depth(R, fd, ld);
+        std::vector<float> all((size_t) R * (nc - 1) * vs);
+        int errv = 0;
+        CK(cudaMemcpyAsync(all.data(), ld, all.size() * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaMemcpyAsync(fr.data(), cur_frames_, fr.size() * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaMemcpyAsync(&errv, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+        cudaFree(ld);
+        if (fd) cudaFree(fd);
+        if (errv) throw std::runtime_error("persistent depth decoder: a bounded wait timed out (device error code " + std::to_string(errv) + ")");
+        std::memcpy(logits_out, all.data(), (size_t) n * (nc - 1) * vs * sizeof(float));
+        for (int i = 0; i < n; i++)
+            for (int j = 1; j < nc; j++) codes_out[(size_t) i * (nc - 1) + (j - 1)] = fr[(size_t) i * nc + j];
+        return;
+    }
     for (int j = 1; j < nc; j++) {
         const int rows = j == 1 ? 2 * R : R;
         gemv(dd_in_, din16_, H, rows, GemvOut{ EPI_STORE, dx_, nullptr, D });

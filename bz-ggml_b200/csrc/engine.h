@@ -2,6 +2,7 @@
 // sessions, device-resident session state and one CUDA-graph frame step per batch bucket.
 #pragma once
 
+#include "depth_persist.cuh"
 #include "host.h"
 #include "kernels.cuh"
 
@@ -72,6 +73,11 @@ public:
     void profile_step(double * out);
     // average microseconds of `iters` back-to-back launches of one dequant-GEMM (epilogue kind)
     double bench_gemv(const char * tensor, int sub, int rows, int iters, int epi);
+    // one eager persistent depth launch for the current batch with its timeline recorded:
+    // out = {n_phases, grid, slots, type[n_phases], timeline[n_phases][grid][slots]} (microseconds
+    // from the first CTA's start, -1 where a slot was not reached); returns the doubles written
+    // (the size needed when out is null), 0 when the persistent decoder is not in use
+    int depth_trace(double * out, int capacity);
     // y[rows][ldy] = x16[rows][ldx] . W^T for a resident, unfused Q8_0 matrix, allocating
     // nothing (static-scratch GEMV); asynchronous on `s` (the engine's stream when null)
     void gemm_noalloc(const char * tensor, int rows, const half * x16, int ldx, float * y, int ldy, cudaStream_t s);
@@ -102,6 +108,17 @@ private:
     void ensure_prefill_capacity(int T);
     cudaGraphExec_t graph_for(int R);
     const QMat * resident_matrix(const char * tensor) const;
+
+    // persistent depth decoder: one schedule (phase table + activation tensor maps) per batch
+    // size R; null when R or the model shape is outside what the kernel supports
+    struct DpPlan {
+        DpPhase * dev = nullptr;
+        int n = 0;
+        DpMaps maps;
+    };
+    const DpPlan * depth_plan(int R);
+    void enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace = nullptr);
+    bool dp_supported(int R) const;
     int acquire_slot(int sid, int n_pages);
     void release_slot(int slot);
 
@@ -165,6 +182,13 @@ private:
     int launches_ = 0;
     int graph_nodes_ = 0;
     bool use_umma_ = true;
+    bool use_dp_ = true;
+    int dp_grid_ = 0;
+    std::map<int, DpPlan> dp_plans_;
+    float * dp_P_ = nullptr;
+    size_t dp_P_floats_ = 0;
+    float * dp_ss_ = nullptr;
+    unsigned * dp_bar_ = nullptr;
     int * err_ = nullptr;
 };
 

@@ -15,6 +15,7 @@
 // Split-K partials of one tile are reduced on chip: the splits form a thread-block cluster and
 // each CTA sums its slice of rows from every peer's shared memory in rank order.
 #include "kernels.cuh"
+#include "tc_ptx.cuh"
 
 #include <cooperative_groups.h>
 #include <cuda.h>
@@ -31,100 +32,18 @@ namespace bzb {
 
 namespace {
 
+using namespace tc;
+
 constexpr int kTileM = 128;     // weight rows per CTA (MMA M)
 constexpr int kChunkK = 64;     // K per stage: one 128-byte swizzle atom of f16
 constexpr int kThreads = 256;
 constexpr int kABytes = kTileM * kChunkK * 2;
-constexpr long long kSpinLimit = 1ll << 22;
 
 #define UCHECK(x)                                                                             \
     do {                                                                                      \
         cudaError_t e_ = (x);                                                                 \
         if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA: ") + cudaGetErrorString(e_) + " at " #x); \
     } while (0)
-
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t smem_u32(const void * p) { return (uint32_t) __cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-
-// bounded wait for the completion of the mbarrier phase with the given parity; returns false
-// (and records the failure) when the limit is reached instead of spinning forever
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int * err) {
-    const uint32_t a = smem_u32(bar);
-    for (long long i = 0; i < kSpinLimit; i++) {
-        uint32_t done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
-        if (done) return true;
-    }
-    if (err) atomicExch(err, 1);
-    return false;
-}
-
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t * slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// K-major operand in the 128-byte swizzle layout: 8-row atoms of 1024 bytes stacked along M/N
-// (stride byte offset 1024), descriptor version 1, layout type SWIZZLE_128B
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-    return (uint64_t) ((addr & 0x3FFFF) >> 4) | ((uint64_t) 1 << 16) | ((uint64_t) (1024 >> 4) << 32) |
-           ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum) : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t * bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float * v) {
-    uint32_t r[16];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-                 : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 4 int8 -> two half2 in natural order, scaled
-__device__ __forceinline__ void dq4(uint32_t w, half2 s, uint32_t & lo, uint32_t & hi) {
-    const uint32_t u = w ^ 0x80808080u;
-    uint32_t l = __byte_perm(u, 0x64646464u, 0x5140u);
-    uint32_t h = __byte_perm(u, 0x64646464u, 0x7362u);
-    const half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
-    half2 hl = __hmul2(__hsub2(*reinterpret_cast<half2 *>(&l), bias), s);
-    half2 hh = __hmul2(__hsub2(*reinterpret_cast<half2 *>(&h), bias), s);
-    lo = *reinterpret_cast<uint32_t *>(&hl);
-    hi = *reinterpret_cast<uint32_t *>(&hh);
-}
-
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-    const float c = 0.7978845608028654f;
-    return 0.5f * x * (1.0f + tanhf(c * x * (1.0f + 0.044715f * x * x)));
-}
 
 struct UParams {
     const uint4 * qs;
@@ -142,23 +61,6 @@ __device__ __forceinline__ void store_out(const UParams & p, int n, int m, float
     float * dst = p.out.f32 + (size_t) n * p.out.ld + m;
     if (EPI == EPI_RESID) *dst += v;
     else *dst = v;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
-                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
 
 // roles: warps 0-7 dequantise, warp 8 issues MMAs, warp 9 loads weights, warp 10 loads activations.
@@ -503,6 +405,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+
+}  // namespace
+
 // activation rows [rows][K] f16 with row stride ldx, read as 64 x box_rows tiles in the
 // 128-byte swizzle; rows past `rows` read as zero
 CUtensorMap make_x_map(const half * x, int K, int ldx, int rows, int box_rows) {
@@ -518,7 +423,6 @@ CUtensorMap make_x_map(const half * x, int K, int ldx, int rows, int box_rows) {
     return m;
 }
 
-}  // namespace
 
 void init_umma_attributes() {
     set_attr_nt<1>();

@@ -57,6 +57,14 @@ BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * ten
 BREEZE_API double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters,
                                            int epilogue);
 
+/* timeline of one persistent depth-decoder launch for the last stepped batch (profiling):
+   out = {n_phases, grid, slots, phase type[n_phases] (0 GEMM, 1 reduce, 2 attention, 3 arg-max),
+   timeline[n_phases][grid][slots]} with the slots of DpParams::trace in microseconds from the
+   first CTA's start (-1 where not reached). Returns the doubles written -- the size needed when
+   out is NULL -- 0 when the batch does not use the persistent decoder, or -1 with
+   breeze_last_error() */
+BREEZE_API int bzb_generator_depth_trace(breeze_generator * gen, double * out, int capacity);
+
 /* Allocation-free dequant-GEMM (no counterpart in the reference): y[rows][ldy] = x16[rows][ldx]
    . W^T for a weight matrix already resident in the generator -- bb.lm_head.weight,
    dd.in_proj.weight, or {bb,dd}.blk.N.{attn_output,ffn_down}.weight -- on caller-owned device
