@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--prompt-cap", type=int, default=0, help="cap text prompt length (profiling runs)")
     ap.add_argument("--profile", action="store_true",
                     help="after warm-up, run one frame step between cudaProfilerStart/Stop and exit (for ncu)")
+    ap.add_argument("--model-preset", default="full", choices=["full", "depth"],
+                    help="'depth': the full-size depth decoder behind a one-layer backbone (small profiling captures)")
     return ap.parse_args()
 
 
@@ -58,10 +60,10 @@ def model_path(args, rank_local: int, barrier=None) -> str:
     import __graft_entry__ as graft
     pkg = graft.load_package()
     os.makedirs(args.model_dir, exist_ok=True)
-    path = os.path.join(args.model_dir, f"breeze_full_nc{args.nc}_q8_0_seed0_eosoff.gguf")
+    path = os.path.join(args.model_dir, f"breeze_{args.model_preset}_nc{args.nc}_q8_0_seed0_eosoff.gguf")
     if rank_local == 0 and not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        pkg.synth_model(tmp, preset="full", nc=args.nc, seed=0, eos_off=True)
+        pkg.synth_model(tmp, preset=args.model_preset, nc=args.nc, seed=0, eos_off=True)
         os.replace(tmp, path)
     if barrier:
         barrier()

@@ -42,20 +42,23 @@ using namespace tc;
 constexpr int kTileM = 128;
 constexpr int kChunkK = 64;
 constexpr int kABytes = kTileM * kChunkK * 2;            // f16 A stage
-constexpr int kRawBytes = kTileM * kChunkK + 2 * kTileM * 2;  // int8 quants + f16 scales
-constexpr int kRawStages = 10;
-constexpr int kAStages = 4;
-constexpr int kBStages = 4;
-constexpr int kBStageBytes = 128 * kChunkK * 2;          // up to 128 activation rows
+// Every bulk or tensor copy costs the SM a roughly fixed ~0.4 us of issue time whatever its size
+// up to 32 KB, so weights and activations move in groups of kDpGroup chunks per copy.
+constexpr int kRawGroups = 3;                            // weight ring: groups of 4 chunks
+constexpr int kRawGroupBytes = kDpGroup * kUChunkBytes;
+constexpr int kAStages = 3;
+constexpr int kBGroups = 2;                              // activation ring: groups of 4 chunks
+constexpr int kBChunkMax = 64 * kChunkK * 2;             // one chunk of up to 64 activation rows
+constexpr int kBGroupBytes = kDpGroup * kBChunkMax;
 constexpr int kEpiThreads = 128;
 constexpr int kDqThreads = 256;
 constexpr int kMmaWarp = 12, kWeightWarp = 13, kActWarp = 14;
 constexpr int kThreads = 480;
-constexpr int kTmemCols = 256;                           // two 128-column accumulators
+constexpr int kTmemCols = 128;                           // two 64-column accumulators
 constexpr int kQFloats = 4 * 2 * 128;                    // query heads of one attention task
 constexpr long long kGridSpin = 1ll << 23;
 
-constexpr int kSmemBytes = 1024 + kAStages * kABytes + kBStages * kBStageBytes + kRawStages * kRawBytes +
+constexpr int kSmemBytes = 1024 + kAStages * kABytes + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
                            (kQFloats + 256 + 16) * 4;
 
 #define DCHECK(x)                                                                             \
@@ -73,7 +76,10 @@ __device__ __forceinline__ int ld_volatile(const int * p) {
 // bounded mbarrier wait that also gives up as soon as any CTA has recorded an error. It polls
 // with the non-suspending test_wait: on this critical path a suspended waiter is woken later
 // than a spinning one sees the phase flip.
-__device__ __forceinline__ bool dwait(uint64_t * bar, uint32_t parity, int * err) {
+// `backoff_ns` > 0 sleeps between polls after the first few: the waiting warps then leave the
+// shared-memory pipe to the tensor core's operand reads and the copies (only the MMA issuer,
+// whose latency paces everything, polls without pause).
+__device__ __forceinline__ bool dwait(uint64_t * bar, uint32_t parity, int * err, unsigned backoff_ns = 0) {
     const uint32_t a = smem_u32(bar);
     for (long long i = 0; i < kSpinLimit * 16; i++) {
         uint32_t done;
@@ -81,10 +87,12 @@ __device__ __forceinline__ bool dwait(uint64_t * bar, uint32_t parity, int * err
                      : "=r"(done) : "r"(a), "r"(parity) : "memory");
         if (done) return true;
         if ((i & 4095) == 4095 && ld_volatile(err)) return false;
+        if (backoff_ns && i >= 4) __nanosleep(backoff_ns);
     }
     atomicExch(err, 2);
     return false;
 }
+constexpr unsigned kBackoff = 64;
 
 // wait until `target` phase arrivals have been counted (every phase before the current one
 // complete on every CTA)
@@ -94,6 +102,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned * bar, unsigned target,
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
         if (v >= target) return true;
         if ((i & 63) == 63 && ld_volatile(err)) return false;
+        if (i >= 8) __nanosleep(32);
     }
     atomicExch(err, 3);
     return false;
@@ -142,12 +151,15 @@ __device__ __forceinline__ DpPhase load_phase(const DpPhase * src) {
 __device__ __forceinline__ int unit_of(int i, int cta, int G) { return (int) (((long long) cta + 17ll * i) % G); }
 
 struct UnitRange {
-    int tile, split, c0, nch;
+    int tile, split, c0, nch, row0;
 };
 __device__ __forceinline__ UnitRange unit_range(const DpPhase ph, int u) {
     UnitRange r;
-    r.tile = u % ph.MT;
-    r.split = u / ph.MT;
+    const int per_rows = ph.MT * ph.splits;
+    const int rem = u % per_rows;
+    r.row0 = (u / per_rows) * 64;
+    r.tile = rem % ph.MT;
+    r.split = rem / ph.MT;
     r.c0 = r.split * ph.kc_per;
     r.nch = min(ph.KC - r.c0, ph.kc_per);
     return r;
@@ -187,6 +199,21 @@ __device__ __forceinline__ float row_scale(const DpParams & p, int row, int lane
     const int nch = p.D / kChunkK;
     const float s = lane < nch ? __ldcg(p.ss + (size_t) row * nch + lane) : 0.0f;
     return 1.0f / sqrtf(wsum(s) / (float) p.D + p.eps);
+}
+
+// the same for `rows` rows at once, one thread per row (D / 64 <= 32 partial loads in flight)
+__device__ __forceinline__ void row_scales(const DpParams & p, int row0, int rows, int tid, float * out) {
+    const int nch = p.D / kChunkK;
+    for (int n = tid; n < rows; n += kEpiThreads) {
+        const float * src = p.ss + (size_t) (row0 + n) * nch;
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; c++) v[c] = c < nch ? __ldcg(src + c) : 0.0f;
+        float a = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 32; c++) a += v[c];
+        out[n] = 1.0f / sqrtf(a / (float) p.D + p.eps);
+    }
 }
 
 // ---- element-wise phases (epilogue group: 128 threads, warps 0-3) -------------------------
@@ -411,16 +438,16 @@ __device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int 
 
 __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpParams p, const __grid_constant__ DpMaps maps) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-    __shared__ uint64_t a_full[kAStages], a_empty[kAStages], b_full[kBStages], b_empty[kBStages];
+    __shared__ uint64_t raw_full[kRawGroups], raw_empty[kRawGroups];
+    __shared__ uint64_t a_full[kAStages], a_empty[kAStages], b_full[kBGroups], b_empty[kBGroups];
     __shared__ uint64_t acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ int s_abort;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
     uint8_t * sB = sA + kAStages * kABytes;
-    uint8_t * sR = sB + kBStages * kBStageBytes;
-    float * sQ = reinterpret_cast<float *>(sR + kRawStages * kRawBytes);
+    uint8_t * sR = sB + kBGroups * kBGroupBytes;
+    float * sQ = reinterpret_cast<float *>(sR + kRawGroups * kRawGroupBytes);
     float * sScale = sQ + kQFloats;
     float * sMisc = sScale + 256;
 
@@ -430,21 +457,22 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
 
     if (warp == kMmaWarp) tmem_alloc(&tmem_slot, kTmemCols);
     if (tid == 0) {
-        for (int i = 0; i < kRawStages; i++) {
+        // producer and epilogue barriers count warps: each warp syncs, then its lane 0 arrives
+        for (int i = 0; i < kRawGroups; i++) {
             mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], kDqThreads);
+            mbar_init(&raw_empty[i], kDqThreads / 32);
         }
         for (int i = 0; i < kAStages; i++) {
-            mbar_init(&a_full[i], kDqThreads);
+            mbar_init(&a_full[i], kDqThreads / 32);
             mbar_init(&a_empty[i], 1);
         }
-        for (int i = 0; i < kBStages; i++) {
+        for (int i = 0; i < kBGroups; i++) {
             mbar_init(&b_full[i], 1);
             mbar_init(&b_empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], kEpiThreads);
+            mbar_init(&acc_empty[i], kEpiThreads / 32);
         }
         mbar_init(&drain_bar, 1);
         s_abort = 0;
@@ -469,23 +497,20 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
             epi_sync();
             if (s_stop) break;
             if (ph.type == DP_GEMM) {
-                const int u = unit_of(i, cta, G);
-                if (u < ph.n_units) {
+                const int v0 = unit_of(i, cta, G);
+                if (ph.epi == DPE_SWIGLU && v0 < ph.n_units) {
+                    // per-row RMS scale of this phase's activation rows
+                    row_scales(p, ph.ss_row0, ph.rows, tid, sScale);
+                    epi_sync();
+                }
+                for (int u = v0; u < ph.n_units; u += G) {
                     const UnitRange ur = unit_range(ph, u);
-                    if (ph.epi == DPE_SWIGLU) {
-                        // per-row RMS scale of this phase's activation rows
-                        for (int n = warp; n < ph.nb; n += 4) {
-                            const float s = row_scale(p, ph.ss_row0 + n, lane);
-                            if (lane == 0) sScale[n] = s;
-                        }
-                        epi_sync();
-                    }
                     const int acc = uc & 1;
-                    bool ok = dwait(&acc_full[acc], (uc >> 1) & 1, err);
+                    bool ok = dwait(&acc_full[acc], (uc >> 1) & 1, err, kBackoff);
                     ok = __all_sync(0xffffffffu, ok);
                     if (p.trace && tid == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 6] = gtimer();
                     tc_fence_after();
-                    const uint32_t taddr = tmem + (uint32_t) (acc * 128) + ((uint32_t) (32 * warp) << 16);
+                    const uint32_t taddr = tmem + (uint32_t) (acc * 64) + ((uint32_t) (32 * warp) << 16);
                     const int m_loc = 32 * warp + lane;
                     if (ok) {
                         for (int n0 = 0; n0 < ph.nb; n0 += 16) {
@@ -494,13 +519,14 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                             tmem_wait_ld();
 #pragma unroll
                             for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
+                            const int nbase = ur.row0 + n0;  // activation row of v[0]
                             if (ph.epi == DPE_PARTIAL) {
                                 const int m = ur.tile * kTileM + m_loc;
                                 if (m < ph.M) {
                                     float * dst = p.P + (size_t) ur.split * ph.rows * ph.M + m;
 #pragma unroll
                                     for (int e = 0; e < 16; e++)
-                                        if (n0 + e < ph.rows) __stcg(dst + (size_t) (n0 + e) * ph.M, v[e]);
+                                        if (nbase + e < ph.rows) __stcg(dst + (size_t) (nbase + e) * ph.M, v[e]);
                                 }
                             } else {
                                 // 16-row gate/up interleave: lanes 0-15 hold gate rows, lanes 16-31 the
@@ -512,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
 #pragma unroll
                                 for (int e = 0; e < 16; e++) {
                                     const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
-                                    const int n = n0 + e;
+                                    const int n = nbase + e;
                                     if ((e & 1) == (gate_lane ? 0 : 1) && n < ph.rows && jc < ph.out_ld) {
                                         const float sc = sScale[n];
                                         const float gt = (gate_lane ? v[e] : other) * sc;
@@ -527,7 +553,8 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                         s_abort = 1;
                     }
                     tc_fence_before();
-                    mbar_arrive(&acc_empty[acc]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
                     uc++;
                 }
             } else if (ph.type == DP_REDUCE) {
@@ -540,7 +567,8 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
             epi_sync();
             if (tid == 0) {
                 if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 1] = gtimer();
-                __threadfence();
+                // the group barrier orders the group's writes before this thread's release, which
+                // publishes them at GPU scope; the proxy fence lets TMA loads in other CTAs see them
                 fence_proxy_async_global();
                 grid_arrive(p.bar);
             }
@@ -550,81 +578,95 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
         // ---------------------------------------------------------------- dequantising producers
         const int t = tid - kEpiThreads;
         const int r = t & (kTileM - 1), hb = t >> 7;
-        uint32_t rc = 0;
+        uint32_t rg = 0, ac = 0;
         bool ok = true;
         for (int i = 0; i < p.n_phases && ok; i++) {
             const DpPhase ph = load_phase(p.phases + i);
             if (ph.type != DP_GEMM) continue;
-            const int u = unit_of(i, cta, G);
-            if (u >= ph.n_units) continue;
-            const UnitRange ur = unit_range(ph, u);
-            for (int c = 0; c < ur.nch && ok; c++, rc++) {
-                const int rs = rc % kRawStages, ab = rc % kAStages;
-                ok = dwait(&raw_full[rs], (rc / kRawStages) & 1u, err);
-                if (!ok) break;
-                if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
-                const uint8_t * raw = sR + rs * kRawBytes;
-                const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
-                const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
-                const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
-                mbar_arrive(&raw_empty[rs]);
-                if (rc >= kAStages) ok = dwait(&a_empty[ab], ((rc / kAStages) - 1) & 1u, err);
-                if (!ok) break;
-                const half2 s2 = __halves2half2(sc, sc);
-                const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
-                uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+            for (int u = unit_of(i, cta, G); u < ph.n_units && ok; u += G) {
+                const UnitRange ur = unit_range(ph, u);
+                for (int c = 0; c < ur.nch && ok; c++, ac++) {
+                    const int within = c % kDpGroup, gs = min(kDpGroup, ur.nch - (c - within));
+                    const int rs = rg % kRawGroups, ab = ac % kAStages;
+                    if (within == 0) ok = dwait(&raw_full[rs], (rg / kRawGroups) & 1u, err, kBackoff);
+                    if (!ok) break;
+                    if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
+                    const uint8_t * raw = sR + rs * kRawGroupBytes + within * kUChunkBytes;
+                    const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
+                    const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
+                    const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
+                    if (within == gs - 1) {
+                        __syncwarp();  // the whole warp has read the group
+                        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                        rg++;
+                    }
+                    if (ac >= kAStages) ok = dwait(&a_empty[ab], ((ac / kAStages) - 1) & 1u, err, kBackoff);
+                    if (!ok) break;
+                    const half2 s2 = __halves2half2(sc, sc);
+                    const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
+                    uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    uint4 o;
-                    dq4(w8[2 * q], s2, o.x, o.y);
-                    dq4(w8[2 * q + 1], s2, o.z, o.w);
-                    const int jj = hb * 4 + q;
-                    *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
+                    for (int q = 0; q < 4; q++) {
+                        uint4 o;
+                        dq4(w8[2 * q], s2, o.x, o.y);
+                        dq4(w8[2 * q + 1], s2, o.z, o.w);
+                        const int jj = hb * 4 + q;
+                        *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[ab]);
+
                 }
-                fence_proxy_async();
-                mbar_arrive(&a_full[ab]);
-                if (p.trace && t == 0 && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 25 + c] = gtimer();
             }
         }
         if (!ok) s_abort = 1;
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            uint32_t ck = 0, uc = 0;
+            uint32_t ck = 0, bg = 0, uc = 0;
             bool ok = true;
             for (int i = 0; i < p.n_phases && ok; i++) {
                 const DpPhase ph = load_phase(p.phases + i);
                 if (ph.type != DP_GEMM) continue;
-                const int u = unit_of(i, cta, G);
-                if (u >= ph.n_units) continue;
-                const UnitRange ur = unit_range(ph, u);
-                const int acc = uc & 1;
-                if (uc >= 2) ok = dwait(&acc_empty[acc], ((uc >> 1) - 1) & 1u, err);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t idesc = (1u << 4) | ((uint32_t) (ph.nb >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
-                const uint32_t d = tmem + (uint32_t) (acc * 128);
-                for (int c = 0; c < ur.nch; c++, ck++) {
-                    const int ab = ck % kAStages, bb = ck % kBStages;
-                    ok = dwait(&b_full[bb], (ck / kBStages) & 1u, err);
-                    if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 3] = gtimer();
-                    if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 9 + c] = gtimer();
-                    ok = ok && dwait(&a_full[ab], (ck / kAStages) & 1u, err);
-                    if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 4] = gtimer();
+                for (int u = unit_of(i, cta, G); u < ph.n_units && ok; u += G) {
+                    const UnitRange ur = unit_range(ph, u);
+                    const int acc = uc & 1;
+                    if (uc >= 2) ok = dwait(&acc_empty[acc], ((uc >> 1) - 1) & 1u, err);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kBStageBytes);
+                    const uint32_t idesc = (1u << 4) | ((uint32_t) (ph.nb >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
+                    const uint32_t d = tmem + (uint32_t) (acc * 64);
+                    for (int c = 0; c < ur.nch; c++, ck++) {
+                        const int within = c % kDpGroup, gs = min(kDpGroup, ur.nch - (c - within));
+                        const int ab = ck % kAStages, bs = bg % kBGroups;
+                        if (within == 0) ok = dwait(&b_full[bs], (bg / kBGroups) & 1u, err);
+                        if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 3] = gtimer();
+                        if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 9 + c] = gtimer();
+                        ok = ok && dwait(&a_full[ab], (ck / kAStages) & 1u, err);
+                        if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 4] = gtimer();
+                        if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 25 + c] = gtimer();
+                        if (!ok) break;
+                        // no tcgen05 fence here: shared-memory operands are ordered by the stage
+                        // barriers (TMA complete_tx, or the dequantisers' proxy fence + arrive); the
+                        // fence after the accumulator wait above orders the TMEM reuse
+                        const uint32_t a0 = smem_u32(sA + ab * kABytes);
+                        const uint32_t b0 = smem_u32(sB + bs * kBGroupBytes + within * ph.nb * kChunkK * 2);
 #pragma unroll
-                    for (int kk = 0; kk < kChunkK / 16; kk++)
-                        umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (c > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&a_empty[ab]);
-                    umma_commit(&b_empty[bb]);
-                    if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 41 + c] = gtimer();
+                        for (int kk = 0; kk < kChunkK / 16; kk++)
+                            umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (c > 0 || kk > 0) ? 1u : 0u);
+                        umma_commit(&a_empty[ab]);
+                        if (within == gs - 1) {
+                            umma_commit(&b_empty[bs]);  // the group's last chunk releases its stage
+                            bg++;
+                        }
+                        if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 41 + c] = gtimer();
+                    }
+                    if (!ok) break;
+                    if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 5] = gtimer();
+                    umma_commit(&acc_full[acc]);
+                    uc++;
                 }
-                if (!ok) break;
-                if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 5] = gtimer();
-                umma_commit(&acc_full[acc]);
-                uc++;
             }
             // every MMA issued above has completed before TMEM is released
             umma_commit(&drain_bar);
@@ -634,58 +676,59 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     } else if (warp == kWeightWarp) {
         // ---------------------------------------------------------------- weight stream
         if (lane == 0) {
-            uint32_t rc = 0;
+            uint32_t rg = 0;
             bool ok = true;
             for (int i = 0; i < p.n_phases && ok; i++) {
                 const DpPhase ph = load_phase(p.phases + i);
                 if (ph.type != DP_GEMM) continue;
-                const int u = unit_of(i, cta, G);
-                if (u >= ph.n_units) continue;
-                const UnitRange ur = unit_range(ph, u);
-                const uint8_t * qbase = reinterpret_cast<const uint8_t *>(ph.qs) + (size_t) (ur.tile * ph.KC + ur.c0) * kTileM * kChunkK;
-                const uint8_t * dbase = reinterpret_cast<const uint8_t *>(ph.ds) + (size_t) (ur.tile * ph.KC + ur.c0) * 2 * kTileM * 2;
-                for (int c = 0; c < ur.nch; c++, rc++) {
-                    const int rs = rc % kRawStages;
-                    if (rc >= kRawStages) ok = dwait(&raw_empty[rs], ((rc / kRawStages) - 1) & 1u, err);
-                    if (!ok) break;
-                    uint8_t * raw = sR + rs * kRawBytes;
-                    if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 7] = gtimer();
-                    mbar_expect_tx(&raw_full[rs], kRawBytes);
-                    bulk_g2s(raw, qbase + (size_t) c * kTileM * kChunkK, kTileM * kChunkK, &raw_full[rs]);
-                    bulk_g2s(raw + kTileM * kChunkK, dbase + (size_t) c * 2 * kTileM * 2, 2 * kTileM * 2, &raw_full[rs]);
+                for (int u = unit_of(i, cta, G); u < ph.n_units && ok; u += G) {
+                    const UnitRange ur = unit_range(ph, u);
+                    const uint8_t * base = ph.blk + (size_t) (ur.tile * ph.KC + ur.c0) * kUChunkBytes;
+                    for (int g0 = 0; g0 < ur.nch; g0 += kDpGroup, rg++) {
+                        const int gs = min(kDpGroup, ur.nch - g0);
+                        const int rs = rg % kRawGroups;
+                        if (rg >= kRawGroups) ok = dwait(&raw_empty[rs], ((rg / kRawGroups) - 1) & 1u, err, kBackoff);
+                        if (!ok) break;
+                        if (p.trace && g0 == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 7] = gtimer();
+                        mbar_expect_tx(&raw_full[rs], (uint32_t) gs * kUChunkBytes);
+                        bulk_g2s(sR + rs * kRawGroupBytes, base + (size_t) g0 * kUChunkBytes, (uint32_t) gs * kUChunkBytes, &raw_full[rs]);
+                    }
                 }
             }
             // copies still in flight land before the CTA exits
-            for (uint32_t k = rc > (uint32_t) kRawStages ? rc - kRawStages : 0; k < rc; k++)
-                dwait(&raw_full[k % kRawStages], (k / kRawStages) & 1u, err);
+            for (uint32_t k = rg > (uint32_t) kRawGroups ? rg - kRawGroups : 0; k < rg; k++)
+                dwait(&raw_full[k % kRawGroups], (k / kRawGroups) & 1u, err);
             if (!ok) s_abort = 1;
         }
     } else {
         // ---------------------------------------------------------------- activation loads
         if (lane == 0) {
-            uint32_t bc = 0;
+            uint32_t bg = 0;
             bool ok = true;
             for (int i = 0; i < p.n_phases && ok; i++) {
                 const DpPhase ph = load_phase(p.phases + i);
                 if (ph.type != DP_GEMM) continue;
-                const int u = unit_of(i, cta, G);
-                if (u >= ph.n_units) continue;
-                const UnitRange ur = unit_range(ph, u);
+                const int v0 = unit_of(i, cta, G);
+                if (v0 >= ph.n_units) continue;
                 ok = grid_wait(p.bar, (unsigned) i * G, err);
                 if (!ok) break;
                 fence_proxy_async_global();
                 if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 2] = gtimer();
-                const uint32_t bytes = (uint32_t) ph.nb * kChunkK * 2;
-                for (int c = 0; c < ur.nch; c++, bc++) {
-                    const int bb = bc % kBStages;
-                    if (bc >= kBStages) ok = dwait(&b_empty[bb], ((bc / kBStages) - 1) & 1u, err);
-                    if (!ok) break;
-                    mbar_expect_tx(&b_full[bb], bytes);
-                    tma_2d(sB + bb * kBStageBytes, &maps.m[ph.map], (ur.c0 + c) * kChunkK, ph.b_row0, &b_full[bb]);
+                // a box always spans kDpGroup chunks (those past the unit are loaded and unused)
+                const uint32_t bytes = (uint32_t) kDpGroup * ph.nb * kChunkK * 2;
+                for (int u = v0; u < ph.n_units && ok; u += G) {
+                    const UnitRange ur = unit_range(ph, u);
+                    for (int g0 = 0; g0 < ur.nch; g0 += kDpGroup, bg++) {
+                        const int bs = bg % kBGroups;
+                        if (bg >= kBGroups) ok = dwait(&b_empty[bs], ((bg / kBGroups) - 1) & 1u, err, kBackoff);
+                        if (!ok) break;
+                        mbar_expect_tx(&b_full[bs], bytes);
+                        tma_3d(sB + bs * kBGroupBytes, &maps.m[ph.map], 0, ph.b_row0 + ur.row0, ur.c0 + g0, &b_full[bs]);
+                    }
                 }
             }
-            for (uint32_t k = bc > (uint32_t) kBStages ? bc - kBStages : 0; k < bc; k++)
-                dwait(&b_full[k % kBStages], (k / kBStages) & 1u, err);
+            for (uint32_t k = bg > (uint32_t) kBGroups ? bg - kBGroups : 0; k < bg; k++)
+                dwait(&b_full[k % kBGroups], (k / kBGroups) & 1u, err);
             if (!ok) s_abort = 1;
         }
     }

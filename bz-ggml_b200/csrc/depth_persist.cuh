@@ -14,16 +14,17 @@ enum DpEpi { DPE_PARTIAL = 0, DPE_SWIGLU = 1 };
 constexpr int kDpTraceSlots = 57;  // 9 phase events + 3 x 16 per-chunk events
 
 // One phase of the schedule. GEMM phases split a Q8_0 matrix (tcgen05 layout) into units of one
-// 128-row tile and one K range; a CTA runs at most one unit per phase.
+// 128-row weight tile, one K range and up to 64 activation rows; CTA c runs units c', c' + grid,
+// ... where c' is c rotated by the phase index.
 struct alignas(16) DpPhase {
     int type = DP_GEMM;
     // GEMM
-    const uint4 * qs = nullptr;
-    const half * ds = nullptr;
+    const uint8_t * blk = nullptr;  // tcgen05 layout (UMat::blk)
     int MT = 0, KC = 0, M = 0, splits = 1, kc_per = 0, n_units = 0;
+    int row_chunks = 1; // activation rows are taken in chunks of 64 (one unit each)
     int map = 0;        // activation tensor map (DpMaps index)
     int b_row0 = 0;     // first activation row read
-    int nb = 0;         // MMA N: activation rows per tile, a multiple of 16
+    int nb = 0;         // MMA N: activation rows per unit, a multiple of 16, at most 64
     int rows = 0;       // activation rows whose results are kept
     int epi = DPE_PARTIAL;
     int out_ld = 0;     // partial: the matrix rows M; SwiGLU: the FFN width
@@ -36,8 +37,12 @@ struct alignas(16) DpPhase {
     int j = 0;          // ARGMAX: codebook
 };
 
+// activation buffers as 3-D tensors {64 columns, rows, K / 64 chunks}: one TMA box brings up to
+// 4 consecutive 64-wide chunks of up to 64 rows, each chunk landing as its own 128-byte-swizzled
+// tile
+constexpr int kDpGroup = 4;
 struct DpMaps {
-    CUtensorMap m[8];   // {in, h, att, ff} x {2R rows, R rows}
+    CUtensorMap m[8];   // {in, h, att, ff} x {box of 2R rows, box of R rows}
 };
 
 struct DpParams {
@@ -66,7 +71,8 @@ struct DpParams {
     // 0 epilogue start, 1 epilogue end, 2 activation loads start, 3 first activation chunk
     // landed, 4 first weight tile dequantised, 5 last MMA issued, 6 accumulator ready,
     // 7 first weight copy issued, 8 first weight chunk landed; for chunks c < 16 of the unit:
-    // 9 + c activation chunk landed, 25 + c weight tile dequantised, 41 + c MMAs issued;
+    // 9 + c activation chunk ready, 25 + c weight tile ready (as the MMA issuer sees them),
+    // 41 + c MMAs issued;
     // null in production launches
     unsigned long long * trace = nullptr;
 };
@@ -74,6 +80,8 @@ struct DpParams {
 // activation rows [rows][K] f16 with row stride ldx, read as 64 x box_rows tiles in the
 // 128-byte swizzle; rows past `rows` read as zero (umma_gemm.cu)
 CUtensorMap make_x_map(const half * x, int K, int ldx, int rows, int box_rows);
+// the same rows viewed as {64, rows, K / 64}: boxes of `group` consecutive 64-wide chunks
+CUtensorMap make_x_group_map(const half * x, int K, int ldx, int rows, int box_rows, int group);
 
 // grid size (CTAs) of the persistent kernel on the current device; 0 when it cannot run
 int depth_persist_grid();

@@ -155,11 +155,9 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
         u.MT = (M + 127) / 128;
         u.K = K;
         u.KC = K / 64;
-        uint4 * uq = dalloc<uint4>((size_t) u.MT * u.KC * 4 * 128);
-        half * ud = dalloc<half>((size_t) u.MT * u.KC * 2 * 128);
-        repack_umma(raw_dev, M, K, uq, ud, stream_);
-        u.qs = uq;
-        u.ds = ud;
+        uint8_t * ub = dalloc<uint8_t>((size_t) u.MT * u.KC * kUChunkBytes);
+        repack_umma(raw_dev, M, K, ub, stream_);
+        u.blk = ub;
         q.u = u;
     }
     CK(cudaStreamSynchronize(stream_));
@@ -422,7 +420,7 @@ void Engine::ensure_prefill_capacity(int T) {
 
 // ------------------------------------------------------------------------------------ step
 void Engine::launch_gemm(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
-    if (use_umma_ && w.u.qs && ldx % 8 == 0) launch_umma_gemm(w.u, x16, ldx, rows, out, err_, stream_, pdl_scope());
+    if (use_umma_ && w.u.blk && ldx % 8 == 0) launch_umma_gemm(w.u, x16, ldx, rows, out, err_, stream_, pdl_scope());
     else launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
 }
 
@@ -489,11 +487,11 @@ bool Engine::dp_supported(int R) const {
     if (dd.hd != 128 || dd.n_kv <= 0 || dd.n_head % dd.n_kv || dd.n_head > 4 * dd.n_kv || dd.n_head * dd.hd != dd.hidden)
         return false;
     if (dd.hidden % 64 || cfg.hidden % 64 || dd.ffn % 64 || dd.hidden / 64 > 32) return false;
-    if (!dd_in_.u.qs) return false;
+    if (!dd_in_.u.blk) return false;
     for (const LayerW & w : dd_)
-        if (!w.qkv.u.qs || !w.o.u.qs || !w.gu.u.qs || !w.down.u.qs || w.gu.u.MT > dp_grid_) return false;
+        if (!w.qkv.u.blk || !w.o.u.blk || !w.gu.u.blk || !w.down.u.blk) return false;
     for (const QMat & h : dd_head_)
-        if (!h.u.qs) return false;
+        if (!h.u.blk) return false;
     return true;
 }
 
@@ -504,22 +502,24 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     const DdConfig & dd = cfg.dd;
     const int D = dd.hidden, H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, G = dp_grid_;
     const int qkvd = dd.n_head * dd.hd + 2 * dd.n_kv * dd.hd;
-    const int NB1 = round_up(R, 16), NB2 = round_up(2 * R, 16);
+    // activation rows go to the MMA in chunks of at most 64 (N), one unit per chunk
+    const int NB1 = std::min(64, round_up(R, 16)), NB2 = std::min(64, round_up(2 * R, 16));
     std::vector<DpPhase> ph;
-    // a GEMM phase over at most one unit per CTA: split K (up to 16 ways) while tiles leave
-    // CTAs idle; returns the split count its consumer sums over
-    auto gemm = [&](const UMat & w, int map, int b_row0, int nb, int rows, int epi, int out_ld, int max_splits = 16) {
+    // a GEMM phase: split K (up to max_splits ways) while the tiles x row chunks leave CTAs
+    // idle; returns the split count its consumer sums over
+    auto gemm = [&](const UMat & w, int map, int b_row0, int rows, int epi, int out_ld, int max_splits = 16) {
         DpPhase q;
         q.type = DP_GEMM;
-        q.qs = w.qs; q.ds = w.ds; q.MT = w.MT; q.KC = w.KC; q.M = w.M;
-        int S = epi == DPE_PARTIAL ? std::max(1, std::min(max_splits, std::min(w.KC, G / w.MT))) : 1;
+        q.blk = w.blk; q.MT = w.MT; q.KC = w.KC; q.M = w.M;
+        q.row_chunks = (rows + 63) / 64;
+        q.nb = std::min(64, round_up(rows, 16));
+        int S = epi == DPE_PARTIAL ? std::max(1, std::min(max_splits, std::min(w.KC, G / (w.MT * q.row_chunks)))) : 1;
         q.kc_per = (w.KC + S - 1) / S;
         S = (w.KC + q.kc_per - 1) / q.kc_per;
-        if (w.MT * S > G) throw std::runtime_error("persistent depth decoder: a matrix has more tiles than CTAs");
         if (epi == DPE_PARTIAL && (size_t) S * rows * w.M > dp_P_floats_)
             throw std::runtime_error("persistent depth decoder: partial buffer too small");
-        q.splits = S; q.n_units = w.MT * S;
-        q.map = map; q.b_row0 = b_row0; q.nb = nb; q.rows = rows; q.epi = epi; q.out_ld = out_ld;
+        q.splits = S; q.n_units = w.MT * S * q.row_chunks;
+        q.map = map; q.b_row0 = b_row0; q.rows = rows; q.epi = epi; q.out_ld = out_ld;
         ph.push_back(q);
         return S;
     };
@@ -530,24 +530,24 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     };
     for (int j = 1; j < nc; j++) {
         const bool first = j == 1;
-        const int rows = first ? 2 * R : R, nb = first ? NB2 : NB1, sel = first ? 0 : 1;
-        int S = gemm(dd_in_.u, 0 + sel, 0, nb, rows, DPE_PARTIAL, D);
+        const int rows = first ? 2 * R : R, sel = first ? 0 : 1;
+        int S = gemm(dd_in_.u, 0 + sel, 0, rows, DPE_PARTIAL, D);
         reduce(S, rows, 0, dd_[0].attn_norm);
         for (int l = 0; l < dd.n_layer; l++) {
             const LayerW & w = dd_[l];
             if (w.qkv.u.M != qkvd) throw std::runtime_error("persistent depth decoder: unexpected qkv rows");
-            S = gemm(w.qkv.u, 2 + sel, 0, nb, rows, DPE_PARTIAL, qkvd);
+            S = gemm(w.qkv.u, 2 + sel, 0, rows, DPE_PARTIAL, qkvd);
             DpPhase a;
             a.type = DP_ATTN; a.S = S; a.rows = rows; a.layer = l; a.start = first ? 0 : j; a.n_new = first ? 2 : 1;
             ph.push_back(a);
-            S = gemm(w.o.u, 4 + sel, 0, nb, rows, DPE_PARTIAL, D);
+            S = gemm(w.o.u, 4 + sel, 0, rows, DPE_PARTIAL, D);
             reduce(S, rows, 1, w.ffn_norm);
-            gemm(w.gu.u, 2 + sel, 0, nb, rows, DPE_SWIGLU, dd.ffn);
-            S = gemm(w.down.u, 6 + sel, 0, nb, rows, DPE_PARTIAL, D);
+            gemm(w.gu.u, 2 + sel, 0, rows, DPE_SWIGLU, dd.ffn);
+            S = gemm(w.down.u, 6 + sel, 0, rows, DPE_PARTIAL, D);
             reduce(S, rows, 1, l + 1 < dd.n_layer ? dd_[l + 1].attn_norm : dd_out_norm_);
         }
         // the head reads the position-1 rows in the first sub-step
-        S = gemm(dd_head_[j - 1].u, 3, first ? R : 0, NB1, R, DPE_PARTIAL, vs, 8);  // arg-max sums <= 8 splits
+        S = gemm(dd_head_[j - 1].u, 3, first ? R : 0, R, DPE_PARTIAL, vs, 8);  // arg-max sums <= 8 splits
         DpPhase am;
         am.type = DP_ARGMAX; am.S = S; am.j = j; am.ss_row0 = first ? R : 0;
         ph.push_back(am);
@@ -557,14 +557,14 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     plan.dev = dalloc<DpPhase>(ph.size());
     CK(cudaMemcpyAsync(plan.dev, ph.data(), ph.size() * sizeof(DpPhase), cudaMemcpyHostToDevice, stream_));
     CK(cudaStreamSynchronize(stream_));
-    plan.maps.m[0] = make_x_map(din16_, H, H, 2 * R, NB2);
-    plan.maps.m[1] = make_x_map(din16_, H, H, 2 * R, NB1);
-    plan.maps.m[2] = make_x_map(dh16_, D, D, 2 * R, NB2);
-    plan.maps.m[3] = make_x_map(dh16_, D, D, 2 * R, NB1);
-    plan.maps.m[4] = make_x_map(datt16_, D, D, 2 * R, NB2);
-    plan.maps.m[5] = make_x_map(datt16_, D, D, 2 * R, NB1);
-    plan.maps.m[6] = make_x_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB2);
-    plan.maps.m[7] = make_x_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB1);
+    plan.maps.m[0] = make_x_group_map(din16_, H, H, 2 * R, NB2, kDpGroup);
+    plan.maps.m[1] = make_x_group_map(din16_, H, H, 2 * R, NB1, kDpGroup);
+    plan.maps.m[2] = make_x_group_map(dh16_, D, D, 2 * R, NB2, kDpGroup);
+    plan.maps.m[3] = make_x_group_map(dh16_, D, D, 2 * R, NB1, kDpGroup);
+    plan.maps.m[4] = make_x_group_map(datt16_, D, D, 2 * R, NB2, kDpGroup);
+    plan.maps.m[5] = make_x_group_map(datt16_, D, D, 2 * R, NB1, kDpGroup);
+    plan.maps.m[6] = make_x_group_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB2, kDpGroup);
+    plan.maps.m[7] = make_x_group_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB1, kDpGroup);
     return &(dp_plans_[R] = plan);
 }
 

@@ -12,12 +12,14 @@ namespace bzb {
 // (two k16 halves), plus one half2 (scale of row g, scale of row g+8) per lane group.
 
 
-// the same Q8_0 matrix in the tcgen05 kernel's layout: for each 128-row tile and 64-wide K
-// chunk, 4 x 128 rows x 16 bytes of int8 (piece (block half, 16-byte half) major, row minor)
-// and 2 x 128 f16 block scales; gate/up pairs interleave in 16-row groups
+// the same Q8_0 matrix in the tcgen05 kernels' layout: one contiguous block per (128-row tile,
+// 64-wide K chunk), tiles major and chunks minor, so that consecutive chunks of a tile are
+// consecutive blocks (one bulk copy can bring several). A block is 4 x 128 rows x 16 bytes of
+// int8 (piece (block half, 16-byte half) major, row minor) followed by 2 x 128 f16 block scales
+// ((block half) major, row minor). Gate/up pairs interleave in 16-row groups.
+constexpr int kUChunkBytes = 128 * 64 + 2 * 128 * 2;
 struct UMat {
-    const uint4 * qs = nullptr;
-    const half * ds = nullptr;
+    const uint8_t * blk = nullptr;
     int M = 0, MT = 0, K = 0, KC = 0;
 };
 
@@ -90,7 +92,7 @@ void launch_gemv_static_scratch(const QMat & w, const half * x16, int ldx, int r
 // tcgen05 dequant-GEMM (umma_gemm.cu): same contract as launch_gemv; `err` receives 1 if a
 // bounded pipeline wait gave up
 void init_umma_attributes();
-void repack_umma(const uint8_t * raw_dev, int M, int K, uint4 * qs, half * ds, cudaStream_t s);
+void repack_umma(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaStream_t s);
 void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const GemvOut & out, int * err,
                       cudaStream_t s, bool pdl);
 bool pdl_scope();

@@ -226,7 +226,7 @@ void fill_tensor(const Tensor & t, uint64_t key, uint8_t * dst, int n_threads) {
 
 int usage() {
     std::fprintf(stderr,
-        "usage: breeze-synth --out PATH [--preset full|tiny] [--nc N] [--quant q8_0|q4_k] [--seed S]\n"
+        "usage: breeze-synth --out PATH [--preset full|depth|tiny] [--nc N] [--quant q8_0|q4_k] [--seed S]\n"
         "                    [--eos-off] [--max-new-tokens N] [--depth-top-k K] [--threads T]\n"
         "       breeze-synth --quantize-f32 IN OUT [--quant q8_0|q4_k]   (raw f32 -> raw blocks)\n");
     return 2;
@@ -284,6 +284,11 @@ int main(int argc, char ** argv) {
         s.bb_layers = 2; s.bb_heads = 4; s.bb_kv = 2; s.bb_hd = 64; s.bb_ffn = 512;
         s.dd_hidden = 256; s.dd_layers = 2; s.dd_heads = 2; s.dd_kv = 1; s.dd_hd = 128; s.dd_ffn = 512;
         s.te_hidden = 256; s.te_layers = 2; s.te_heads = 2; s.te_kv = 1; s.te_hd = 128; s.te_ffn = 512; s.te_window = 8;
+    } else if (preset == "depth") {
+        // the full-size depth decoder behind a one-layer backbone and a small text encoder: the
+        // depth kernels at their real shapes in a model of a few hundred MB (profiling captures)
+        s.bb_layers = 1; s.bb_ffn = 512;
+        s.te_hidden = 256; s.te_layers = 1; s.te_heads = 2; s.te_kv = 1; s.te_hd = 128; s.te_ffn = 512; s.te_window = 8;
     } else if (preset != "full") return usage();
     if (nc_override > 0) s.nc = nc_override;
     if (s.qtype == G_Q4_K && (s.hidden % 256 || s.dd_hidden % 256 || s.bb_ffn % 256 || s.dd_ffn % 256 || s.te_hidden % 256)) {

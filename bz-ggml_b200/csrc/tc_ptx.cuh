@@ -113,5 +113,10 @@ __device__ __forceinline__ void tma_2d(void * dst, const CUtensorMap * map, int 
                  ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ void tma_3d(void * dst, const CUtensorMap * map, int x, int y, int z, uint64_t * bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
+
 }  // namespace tc
 }  // namespace bzb

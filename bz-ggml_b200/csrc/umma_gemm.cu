@@ -46,8 +46,7 @@ constexpr int kABytes = kTileM * kChunkK * 2;
     } while (0)
 
 struct UParams {
-    const uint4 * qs;
-    const half * ds;
+    const uint8_t * blk;
     int M, MT, KC, kc_per_split, splits;
     const half * x;
     int ldx, rows;
@@ -170,15 +169,14 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     } else if (warp == 9) {
         if (lane == 0) {
             // weights and scales are constant: stream them before the predecessor finishes
-            const uint8_t * qbase = reinterpret_cast<const uint8_t *>(p.qs) + (size_t) (mt * p.KC + c_beg) * 4 * kTileM * 16;
-            const uint8_t * dbase = reinterpret_cast<const uint8_t *>(p.ds) + (size_t) (mt * p.KC + c_beg) * 2 * kTileM * 2;
+            // one bulk copy per chunk: quants and scales are contiguous in the repacked layout
+            const uint8_t * base = p.blk + (size_t) (mt * p.KC + c_beg) * kUChunkBytes;
             for (int c = 0; c < nch; c++) {
                 const int rs = c % kRawStages;
                 if (c >= kRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kRawStages) - 1) & 1u, p.err);
                 uint8_t * raw = sR + rs * kRawBytes;
                 mbar_expect_tx(&raw_full[rs], kRawBytes);
-                bulk_g2s(raw, qbase + (size_t) c * 4 * kTileM * 16, kTileM * kChunkK, &raw_full[rs]);
-                bulk_g2s(raw + kTileM * kChunkK, dbase + (size_t) c * 2 * kTileM * 2, 2 * kTileM * 2, &raw_full[rs]);
+                bulk_g2s(raw, base + (size_t) c * kUChunkBytes, kUChunkBytes, &raw_full[rs]);
             }
         }
     } else {
@@ -321,7 +319,7 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     cluster.sync();
 }
 
-__global__ void repack_umma_kernel(const uint8_t * raw, int M, int KB, int KC, uint4 * qs, half * ds) {
+__global__ void repack_umma_kernel(const uint8_t * raw, int M, int KB, int KC, uint8_t * blk) {
     const long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x;
     const int MT = (M + kTileM - 1) / kTileM;
     if (idx >= (long long) MT * KC * 4 * kTileM) return;
@@ -330,17 +328,18 @@ __global__ void repack_umma_kernel(const uint8_t * raw, int M, int KB, int KC, u
     const int pc = (int) (rest % 2), hb = (int) ((rest / 2) % 2);
     const long long tc = rest / 4;
     const int c = (int) (tc % KC), mt = (int) (tc / KC);
-    const int row = mt * kTileM + r, blk = 2 * c + hb;
+    const int row = mt * kTileM + r, qb = 2 * c + hb;
     uint32_t w[4] = { 0u, 0u, 0u, 0u };
     unsigned short d = 0;
     if (row < M) {
-        const uint8_t * b = raw + ((size_t) row * KB + blk) * 34;
-        d = (unsigned short) (b[0] | (b[1] << 8));
-        const uint8_t * q = b + 2 + pc * 16;
+        const uint8_t * src = raw + ((size_t) row * KB + qb) * 34;
+        d = (unsigned short) (src[0] | (src[1] << 8));
+        const uint8_t * q = src + 2 + pc * 16;
         for (int i = 0; i < 4; i++) w[i] = q[4 * i] | (q[4 * i + 1] << 8) | (q[4 * i + 2] << 16) | ((uint32_t) q[4 * i + 3] << 24);
     }
-    qs[idx] = make_uint4(w[0], w[1], w[2], w[3]);
-    if (pc == 0) ds[((size_t) (mt * KC + c) * 2 + hb) * kTileM + r] = __ushort_as_half(d);
+    uint8_t * b = blk + (size_t) tc * kUChunkBytes;
+    *reinterpret_cast<uint4 *>(b + ((size_t) (hb * 2 + pc) * kTileM + r) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    if (pc == 0) *reinterpret_cast<unsigned short *>(b + kTileM * kChunkK + ((size_t) hb * kTileM + r) * 2) = d;
 }
 
 template <int NT16, int EPI>
@@ -423,6 +422,19 @@ CUtensorMap make_x_map(const half * x, int K, int ldx, int rows, int box_rows) {
     return m;
 }
 
+CUtensorMap make_x_group_map(const half * x, int K, int ldx, int rows, int box_rows, int group) {
+    CUtensorMap m;
+    const cuuint64_t dims[3] = { (cuuint64_t) kChunkK, (cuuint64_t) rows, (cuuint64_t) (K / kChunkK) };
+    const cuuint64_t strides[2] = { (cuuint64_t) ldx * sizeof(half), (cuuint64_t) kChunkK * sizeof(half) };
+    const cuuint32_t box[3] = { (cuuint32_t) kChunkK, (cuuint32_t) box_rows, (cuuint32_t) group };
+    const cuuint32_t estr[3] = { 1, 1, 1 };
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<half *>(x), dims, strides, box, estr,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3-D chunk groups) failed (" + std::to_string((int) r) + ")");
+    return m;
+}
+
 
 void init_umma_attributes() {
     set_attr_nt<1>();
@@ -432,11 +444,11 @@ void init_umma_attributes() {
     UCHECK(cudaGetLastError());
 }
 
-void repack_umma(const uint8_t * raw_dev, int M, int K, uint4 * qs, half * ds, cudaStream_t s) {
+void repack_umma(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaStream_t s) {
     if (K % kChunkK) throw std::runtime_error("tcgen05 layout needs K % 64 == 0");
     const int MT = (M + kTileM - 1) / kTileM, KC = K / kChunkK;
     const long long n = (long long) MT * KC * 4 * kTileM;
-    repack_umma_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(raw_dev, M, K / 32, KC, qs, ds);
+    repack_umma_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(raw_dev, M, K / 32, KC, blk);
     UCHECK(cudaGetLastError());
 }
 
@@ -459,7 +471,7 @@ void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const
         if (f == 1 || f == 2 || f == 4 || f == 8) splits = std::min(f, (out.kind >= EPI_SWIGLU) ? 4 : 8);
     }
     UParams p;
-    p.qs = w.qs; p.ds = w.ds; p.M = w.M; p.MT = w.MT; p.KC = w.KC;
+    p.blk = w.blk; p.M = w.M; p.MT = w.MT; p.KC = w.KC;
     p.kc_per_split = (w.KC + splits - 1) / splits;
     p.splits = splits;
     p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.err = err;
