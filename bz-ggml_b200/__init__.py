@@ -261,10 +261,11 @@ class GeneratorHandle:
         return int(self.lib.lib.bzb_generator_launches_per_step(self.handle))
 
     def profile_step(self) -> dict:
-        out = (ctypes.c_double * 5)()
+        out = (ctypes.c_double * 7)()
         if self.lib.lib.bzb_generator_profile_step(self.handle, out) != 0:
             raise RuntimeError(self.lib.last_error())
-        return dict(step_ms=out[0], gemm_ms=out[1], gemm_launches=int(out[2]), gemm_bytes=out[3])
+        return dict(step_ms=out[0], gemm_ms=out[1], gemm_launches=int(out[2]), gemm_bytes=out[3],
+                    depth_ms=out[5], depth_bytes=out[6])
 
     def bench_gemv(self, tensor: str, rows: int, iters: int = 50, epilogue: int = 0, sub: int = -1) -> float:
         us = self.lib.lib.bzb_generator_bench_gemv(self.handle, tensor.encode(), sub, rows, iters, epilogue)

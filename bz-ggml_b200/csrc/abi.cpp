@@ -431,10 +431,10 @@ long long bzb_generator_kv_bytes_per_position(breeze_generator * gen) {
 
 int bzb_generator_launches_per_step(breeze_generator * gen) { return gen ? gen->eng->launches_per_step() : -1; }
 
-int bzb_generator_profile_step(breeze_generator * gen, double * out5) {
-    if (!gen || !out5) return -1;
+int bzb_generator_profile_step(breeze_generator * gen, double * out7) {
+    if (!gen || !out7) return -1;
     try {
-        gen->eng->profile_step(out5);
+        gen->eng->profile_step(out7);
         return 0;
     } catch (const std::exception & e) {
         set_error(e.what());

@@ -615,7 +615,13 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     p.row_active = row_active_; p.frames = cur_frames_;
     p.forced = forced_dev; p.logits_out = logits_dev;
     p.bar = dp_bar_; p.err = err_; p.trace = trace;
+    if (prof_) {
+        CK(cudaEventCreate(&dprof_a_));
+        CK(cudaEventCreate(&dprof_b_));
+        CK(cudaEventRecord(dprof_a_, stream_));
+    }
     launch_depth_persist(p, pl->maps, dp_grid_, stream_);
+    if (prof_) CK(cudaEventRecord(dprof_b_, stream_));
     launches_ += 2;
 }
 
@@ -1109,6 +1115,26 @@ void Engine::profile_step(double * out) {
     out[2] = (double) recs.size();
     out[3] = bytes;
     out[4] = (double) launches_;
+    out[5] = 0.0;
+    out[6] = 0.0;
+    if (dprof_a_) {
+        float dms = 0.0f;
+        CK(cudaEventElapsedTime(&dms, dprof_a_, dprof_b_));
+        cudaEventDestroy(dprof_a_);
+        cudaEventDestroy(dprof_b_);
+        dprof_a_ = dprof_b_ = nullptr;
+        out[5] = dms;
+        out[6] = (double) depth_bytes_per_step();
+    }
+}
+
+size_t Engine::depth_bytes_per_step() const {
+    // algorithmic bytes of the depth decode of one frame step: the Q8_0 depth weights, re-read by
+    // every sub-step (in_proj, the 4 layers and that sub-step's head)
+    auto qbytes = [](const QMat & q) { return (size_t) q.M * q.K / 32 * 34; };
+    size_t dd = qbytes(dd_in_) + qbytes(dd_head_[0]);
+    for (const LayerW & w : dd_) dd += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
+    return (size_t) (cfg.nc - 1) * dd;
 }
 
 double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int epi) {

@@ -68,9 +68,11 @@ public:
     void debug_depth(int n, const float * hidden, const int * cb0, const int * forced, int * codes_out,
                      float * logits_out);
     void debug_gemv(const char * tensor, int sub, int rows, const float * x, float * y);
-    // one eager frame step of the current batch with CUDA events around every dequant-GEMM:
-    // out = {step_ms, gemm_ms, gemm_launches, gemm_algorithmic_bytes, launches}
+    // one eager frame step of the current batch with CUDA events around every dequant-GEMM and
+    // the persistent depth decoder: out = {step_ms, gemm_ms, gemm_launches,
+    // gemm_algorithmic_bytes, launches, depth_ms, depth_algorithmic_bytes}
     void profile_step(double * out);
+    size_t depth_bytes_per_step() const;
     // average microseconds of `iters` back-to-back launches of one dequant-GEMM (epilogue kind)
     double bench_gemv(const char * tensor, int sub, int rows, int iters, int epi);
     // one eager persistent depth launch for the current batch with its timeline recorded:
@@ -190,6 +192,7 @@ private:
     float * dp_ss_ = nullptr;
     unsigned * dp_bar_ = nullptr;
     int * err_ = nullptr;
+    cudaEvent_t dprof_a_ = nullptr, dprof_b_ = nullptr;
 };
 
 }  // namespace bzb

@@ -38,9 +38,11 @@ BREEZE_API long long bzb_generator_kv_bytes_per_position(breeze_generator * gen)
 
 /* kernels in one captured frame step (graph nodes of the last captured bucket) */
 BREEZE_API int bzb_generator_launches_per_step(breeze_generator * gen);
-/* one eager frame step of the last batch with CUDA events around every dequant-GEMM launch:
-   out5 = {step_ms, gemm_ms, gemm_launches, gemm_algorithmic_bytes, gemm_launches_counted} */
-BREEZE_API int bzb_generator_profile_step(breeze_generator * gen, double * out5);
+/* one eager frame step of the last batch with CUDA events around every dequant-GEMM launch and
+   the persistent depth decoder: out7 = {step_ms, gemm_ms, gemm_launches, gemm_algorithmic_bytes,
+   launches_counted, depth_ms, depth_algorithmic_bytes} (depth values 0 when the batch uses the
+   per-operation depth path) */
+BREEZE_API int bzb_generator_profile_step(breeze_generator * gen, double * out7);
 
 /* parity probes: the session's last normed backbone hidden [hidden]; one depth decode of n
    rows (hidden [n][hidden] f32, cb0 [n]; forced [n][nc-1] replaces each argmax as the next
