@@ -322,6 +322,68 @@ class GeneratorHandle:
         return y
 
 
+class VocoderHandle:
+    """Codec decoder sessions (mirror of the reference's python/bz_ggml/bindings.py
+    VocoderHandle): frames are [n_frames][num_codebooks] ints, PCM is 1920 f32 samples per frame
+    at 24 kHz."""
+
+    SAMPLES_PER_FRAME = 1920
+
+    def __init__(self, model_path: str = "", cuda_device: int = 0, generator: Optional["GeneratorHandle"] = None):
+        self.lib = lib()
+        if generator is not None:
+            self.handle = self.lib.lib.breeze_vocoder_create_from_generator(generator.handle)
+            self._gen = generator
+        else:
+            self.handle = self.lib.lib.breeze_vocoder_init(model_path.encode(), cuda_device)
+        if not self.handle:
+            raise RuntimeError(f"vocoder init failed: {self.lib.last_error()}")
+
+    def session_create(self, session_id: int) -> int:
+        return self.lib.lib.breeze_vocoder_session_create(self.handle, session_id)
+
+    def session_decode(self, session_id: int, frames: np.ndarray) -> np.ndarray:
+        f = np.ascontiguousarray(frames, np.int32)
+        n = f.shape[0]
+        out = np.zeros(n * self.SAMPLES_PER_FRAME, np.float32)
+        got = self.lib.lib.breeze_vocoder_session_decode(self.handle, session_id, _ip(f), n, _fp(out))
+        if got <= 0:
+            raise RuntimeError(f"session_decode failed: {self.lib.last_error()}")
+        return out[:got]
+
+    def session_decode_batch(self, session_ids: Sequence[int], batch_frames: Sequence[np.ndarray]) -> List[np.ndarray]:
+        nf = np.array([np.asarray(b).shape[0] for b in batch_frames], np.int32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(b, np.int32).reshape(-1) for b in batch_frames]))
+        ids = np.asarray(session_ids, np.int32)
+        pcm = np.zeros(int(nf.sum()) * self.SAMPLES_PER_FRAME, np.float32)
+        ns = np.zeros(len(ids), np.int32)
+        got = self.lib.lib.breeze_vocoder_session_decode_batch(self.handle, len(ids), _ip(ids), _ip(flat), None, _ip(nf),
+                                                               _fp(pcm), None, _ip(ns))
+        if got != len(ids):
+            raise RuntimeError(f"session_decode_batch failed: {self.lib.last_error()}")
+        offs = np.concatenate([[0], np.cumsum(ns)])
+        return [pcm[offs[i]:offs[i + 1]] for i in range(len(ids))]
+
+    def session_free(self, session_id: int) -> int:
+        return self.lib.lib.breeze_vocoder_session_free(self.handle, session_id)
+
+    def stream_decode(self, frames: np.ndarray) -> np.ndarray:
+        f = np.ascontiguousarray(frames, np.int32)
+        out = np.zeros(f.shape[0] * self.SAMPLES_PER_FRAME, np.float32)
+        got = self.lib.lib.breeze_vocoder_stream_decode(self.handle, _ip(f), f.shape[0], _fp(out))
+        if got <= 0:
+            raise RuntimeError(f"stream_decode failed: {self.lib.last_error()}")
+        return out[:got]
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.lib.breeze_vocoder_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
 def gguf_inspect(path: str):
     h, nc, nt = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     if lib().lib.bzb_gguf_inspect(path.encode(), ctypes.byref(h), ctypes.byref(nc), ctypes.byref(nt)) != 0:

@@ -4,6 +4,7 @@
 // boundary; they become the reference's error returns plus breeze_last_error().
 #include "../../include/bzb_ext.h"
 #include "engine.h"
+#include "vocoder.h"
 
 #include <cerrno>
 #include <climits>
@@ -20,8 +21,13 @@ struct breeze_generator {
     int device = 0;
 };
 
+// a vocoder either owns its model file (breeze_vocoder_init) or decodes with the weights of a
+// generator's model (breeze_vocoder_create_from_generator; the generator must outlive it, as in
+// the reference, src/c_api.cpp:971-991)
 struct breeze_vocoder {
     int device = 0;
+    std::unique_ptr<bzb::GgufFile> own_file;
+    std::unique_ptr<bzb::Vocoder> voc;
 };
 
 struct breeze_context {
@@ -266,51 +272,97 @@ int breeze_generator_encode_audio(breeze_generator * gen, const float * pcm, int
 
 // ------------------------------------------------------------------------------------ vocoder
 breeze_vocoder * breeze_vocoder_init(const char * gguf_path, int cuda_device) {
-    (void) gguf_path; (void) cuda_device;
-    set_error("the streaming vocoder is not provided by this library yet");
-    return nullptr;
+    if (!gguf_path) {
+        set_error("null model path");
+        return nullptr;
+    }
+    try {
+        auto v = std::make_unique<breeze_vocoder>();
+        v->device = cuda_device;
+        v->own_file = std::make_unique<bzb::GgufFile>();
+        std::string err;
+        if (!v->own_file->open(gguf_path, err)) throw std::runtime_error(err);
+        const bzb::ModelConfig cfg = bzb::parse_config(*v->own_file);
+        v->voc = std::make_unique<bzb::Vocoder>(*v->own_file, cfg, cuda_device);
+        return v.release();
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return nullptr;
+    }
 }
+
 void breeze_vocoder_free(breeze_vocoder * voc) { delete voc; }
+
 breeze_vocoder * breeze_vocoder_create_from_generator(breeze_generator * gen) {
-    (void) gen;
-    set_error("the streaming vocoder is not provided by this library yet");
-    return nullptr;
+    if (!gen) return nullptr;
+    try {
+        auto v = std::make_unique<breeze_vocoder>();
+        v->device = gen->device;
+        v->voc = std::make_unique<bzb::Vocoder>(gen->eng->gguf(), gen->eng->cfg, gen->device);
+        return v.release();
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return nullptr;
+    }
 }
+
 int breeze_vocoder_session_create(breeze_vocoder * voc, int session_id) {
-    (void) session_id;
-    return voc ? 0 : -1;
-}
-int breeze_vocoder_session_decode(breeze_vocoder * voc, int session_id, const int * frames, int n_frames,
-                                  float * out_pcm) {
-    (void) voc; (void) session_id; (void) frames; (void) n_frames; (void) out_pcm;
-    set_error("the streaming vocoder is not provided by this library yet");
+    if (!voc || !voc->voc) return -1;
+    voc->voc->session_create(session_id);
     return 0;
 }
+
+int breeze_vocoder_session_decode(breeze_vocoder * voc, int session_id, const int * frames, int n_frames,
+                                  float * out_pcm) {
+    if (!voc || !voc->voc || !frames || n_frames <= 0 || !out_pcm) return 0;
+    try {
+        return voc->voc->session_decode(session_id, frames, n_frames, out_pcm);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 0;
+    }
+}
+
 int breeze_vocoder_session_decode_batch(breeze_vocoder * voc, int batch_size, const int * session_ids,
                                         const int * flat_tokens, const int * token_offsets,
                                         const int * n_frames_per_stream, float * flat_pcm, const int * pcm_offsets,
                                         int * out_n_samples) {
-    (void) voc; (void) batch_size; (void) session_ids; (void) flat_tokens; (void) token_offsets;
-    (void) n_frames_per_stream; (void) flat_pcm; (void) pcm_offsets; (void) out_n_samples;
-    set_error("the streaming vocoder is not provided by this library yet");
-    return 0;
+    if (!voc || !voc->voc || batch_size <= 0 || !session_ids || !flat_tokens || !n_frames_per_stream || !flat_pcm) return 0;
+    try {
+        return voc->voc->session_decode_batch(batch_size, session_ids, flat_tokens, token_offsets, n_frames_per_stream,
+                                              flat_pcm, pcm_offsets, out_n_samples);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 0;
+    }
 }
+
 int breeze_vocoder_session_free(breeze_vocoder * voc, int session_id) {
-    (void) session_id;
-    return voc ? 0 : -1;
+    if (!voc || !voc->voc) return -1;
+    return voc->voc->session_free(session_id) ? 0 : -1;
 }
+
 int breeze_vocoder_stream_decode(breeze_vocoder * voc, const int * frames, int n_frames, float * out_pcm) {
-    (void) voc; (void) frames; (void) n_frames; (void) out_pcm;
-    set_error("the streaming vocoder is not provided by this library yet");
-    return 0;
+    if (!voc || !voc->voc || !frames || n_frames <= 0 || !out_pcm) return 0;
+    try {
+        return voc->voc->stream_decode(frames, n_frames, out_pcm);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 0;
+    }
 }
+
 int breeze_vocoder_stream_decode_batch(breeze_vocoder * voc, int batch_size, const int * flat_tokens,
                                        const int * token_offsets, const int * n_frames_per_stream, float * flat_pcm,
                                        const int * pcm_offsets, int * out_n_samples) {
-    (void) voc; (void) batch_size; (void) flat_tokens; (void) token_offsets; (void) n_frames_per_stream;
-    (void) flat_pcm; (void) pcm_offsets; (void) out_n_samples;
-    set_error("the streaming vocoder is not provided by this library yet");
-    return 0;
+    if (!voc || !voc->voc || batch_size <= 0 || !flat_tokens || !n_frames_per_stream || !flat_pcm) return 0;
+    try {
+        return voc->voc->stream_decode_batch(batch_size, flat_tokens, token_offsets, n_frames_per_stream, flat_pcm,
+                                             pcm_offsets, out_n_samples);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 0;
+    }
 }
 
 // ------------------------------------------------------------------------------------ voice files

@@ -8,6 +8,7 @@
 // Session state (positions, sampler streams, penalty histories, last hidden) never leaves the
 // device between steps; the host only uploads the row->slot table and seeds.
 #include "engine.h"
+#include "rope.h"
 
 #include <algorithm>
 #include <cmath>
@@ -26,24 +27,6 @@ namespace bzb {
 
 namespace {
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
-
-std::vector<float2> rope_table(int max_pos, int hd, float base, float fscale, const std::vector<float> * ff) {
-    // ggml NEOX rope cache: theta_i = p * theta_scale^i by repeated f32 multiplication,
-    // divided by the frequency factor and scaled by freq_scale (ext_factor 0, attn_factor 1)
-    const int half = hd / 2;
-    const float ts = powf(base, -2.0f / (float) hd);
-    std::vector<float2> tab((size_t) max_pos * half);
-    for (int p = 0; p < max_pos; p++) {
-        float theta = (float) p;
-        for (int i = 0; i < half; i++) {
-            float t = ff ? theta / (*ff)[i] : theta;
-            t = fscale * t;
-            tab[(size_t) p * half + i] = make_float2(cosf(t), sinf(t));
-            theta *= ts;
-        }
-    }
-    return tab;
-}
 
 std::vector<float> llama3_freq_factors(const DdConfig & c) {
     // src/depth_decoder.cpp:10-29

@@ -87,6 +87,7 @@ public:
     size_t kv_bytes_per_position() const;
 
     int max_rows() const { return rmax_; }
+    const GgufFile & gguf() const { return gg_; }
     int launches_per_step() const { return graph_nodes_; }
     int nc() const { return cfg.nc; }
 

@@ -264,6 +264,19 @@ ModelConfig parse_config(const GgufFile & g) {
     dd.high = g.kv_f32("breeze.dd.rope_high_freq_factor", 0.0078125f);
     dd.low = g.kv_f32("breeze.dd.rope_low_freq_factor", 0.001953125f);
     dd.orig_ctx = g.kv_u32("breeze.dd.rope_orig_ctx", 16);
+    c.voc.hidden = g.kv_u32("breeze.codec.dec.hidden_size", 512);
+    c.voc.n_layer = g.kv_u32("breeze.codec.dec.block_count", 8);
+    c.voc.n_head = g.kv_u32("breeze.codec.dec.head_count", 16);
+    c.voc.n_kv = g.kv_u32("breeze.codec.dec.head_count_kv", 16);
+    c.voc.hd = g.kv_u32("breeze.codec.dec.head_dim", 64);
+    c.voc.ffn = g.kv_u32("breeze.codec.dec.feed_forward_length", 1024);
+    c.voc.eps = g.kv_f32("breeze.codec.dec.rms_eps", 1e-5f);
+    c.voc.theta = g.kv_f32("breeze.codec.dec.rope_theta", 10000.0f);
+    c.voc.window = g.kv_u32("breeze.codec.dec.sliding_window", 72);
+    c.voc.rates = g.kv_i32_array("breeze.codec.dec.upsample_rates");
+    if (c.voc.rates.empty()) c.voc.rates = { 8, 5, 4, 3 };
+    c.voc.ratios = g.kv_i32_array("breeze.codec.dec.upsampling_ratios");
+    if (c.voc.ratios.empty()) c.voc.ratios = { 2, 2 };
     return c;
 }
 

@@ -68,6 +68,13 @@ struct DdConfig {
     float eps, theta, factor, high, low;
 };
 
+// codec decoder (vocoder) keys, src/config.cpp:84-99
+struct VocConfig {
+    int hidden, n_layer, n_head, n_kv, hd, ffn, window;
+    float eps, theta;
+    std::vector<int> rates, ratios;
+};
+
 // keys and defaults of src/config.cpp:6-102 that the generation path reads
 struct ModelConfig {
     int hidden, nc, vs, cb_size, bb_eos, cb_pad, cb_eos, sample_rate, samples_per_frame, max_new_tokens;
@@ -76,6 +83,7 @@ struct ModelConfig {
     TeConfig te;
     BbConfig bb;
     DdConfig dd;
+    VocConfig voc;
 };
 
 ModelConfig parse_config(const GgufFile & g);

@@ -144,9 +144,10 @@ struct Tensor {
     std::string name;
     std::vector<int64_t> ne;
     GgmlType type;
-    int kind;  // 0 = linear N(0, 0.02), 1 = norm 1 + N(0, 0.02)
+    int kind;  // 0 = linear N(0, 0.02), 1 = norm 1 + N(0, 0.02), 2 = N(mean, stdv)
     uint64_t offset = 0;
     uint64_t nbytes = 0;
+    float mean = 0.0f, stdv = 0.0f;
 };
 
 struct Writer {
@@ -182,6 +183,12 @@ struct Spec {
     int depth_top_k = 50;
     GgmlType qtype = G_Q8_0;
     uint64_t seed = 0;
+    // vocoder (codec decoder): quantiser embedding dim, its projection, the transformer's latent
+    // and hidden widths, heads, MLP, attention window, the conv stack's first width and the two
+    // upsampling stages (ConvNeXt stages, then SnakeBeta blocks); 2 * 8 * 6 * 5 * 4 = 1920
+    int voc_dq = 256, voc_cbdim = 512, voc_latent = 1024, voc_hidden = 512, voc_layers = 8, voc_heads = 8,
+        voc_kv = 8, voc_hd = 64, voc_ffn = 1024, voc_window = 72, voc_dec = 1536;
+    std::vector<int32_t> voc_ratios = { 2 }, voc_rates = { 8, 6, 5, 4 };
 };
 
 uint64_t tensor_bytes(const Tensor & t) {
@@ -208,7 +215,7 @@ void fill_tensor(const Tensor & t, uint64_t key, uint8_t * dst, int n_threads) {
             for (int j = 0; j < blk; j++) {
                 const uint64_t i = (uint64_t) (b * blk + j);
                 const float z = normal_at(key, i);
-                buf[j] = t.kind == 1 ? 1.0f + 0.02f * z : 0.02f * z;
+                buf[j] = t.kind == 2 ? t.mean + t.stdv * z : t.kind == 1 ? 1.0f + 0.02f * z : 0.02f * z;
             }
             if (t.type == G_F32) std::memcpy(dst + b * 4, buf.data(), 4);
             else if (t.type == G_F16) { uint16_t h = f32_to_f16(buf[0]); std::memcpy(dst + b * 2, &h, 2); }
@@ -284,6 +291,8 @@ int main(int argc, char ** argv) {
         s.bb_layers = 2; s.bb_heads = 4; s.bb_kv = 2; s.bb_hd = 64; s.bb_ffn = 512;
         s.dd_hidden = 256; s.dd_layers = 2; s.dd_heads = 2; s.dd_kv = 1; s.dd_hd = 128; s.dd_ffn = 512;
         s.te_hidden = 256; s.te_layers = 2; s.te_heads = 2; s.te_kv = 1; s.te_hd = 128; s.te_ffn = 512; s.te_window = 8;
+        s.voc_dq = 32; s.voc_cbdim = 64; s.voc_latent = 64; s.voc_hidden = 64; s.voc_layers = 2; s.voc_heads = 2;
+        s.voc_kv = 1; s.voc_hd = 32; s.voc_ffn = 128; s.voc_window = 8; s.voc_dec = 64;
     } else if (preset == "depth") {
         // the full-size depth decoder behind a one-layer backbone and a small text encoder: the
         // depth kernels at their real shapes in a model of a few hundred MB (profiling captures)
@@ -361,6 +370,85 @@ int main(int argc, char ** argv) {
     nrm("dd.output_norm.weight", s.dd_hidden);
     lin("dd.codebooks_head.weight", s.dd_hidden, s.vs, s.nc - 1);
 
+    // vocoder decoder (src/codec_decoder.cpp:11-98, src/codec_transformer.cpp:48-83); shapes in
+    // ggml order. Appended after every generator tensor so their seeds do not move. Conv kernels
+    // are F32 [K, C_in, C_out] (transposed convs [K, C_out, C_in], depthwise [C, K]) scaled by
+    // 1/sqrt(fan in); SnakeBeta alpha/beta are log-space N(0, 0.1); layer scales 0.1.
+    auto f32t = [&](const std::string & n, std::vector<int64_t> ne, float mean, float stdv) {
+        Tensor t{ n, ne, G_F32, 2 };
+        t.mean = mean;
+        t.stdv = stdv;
+        ts.push_back(t);
+    };
+    auto conv = [&](const std::string & n, int64_t K, int64_t cin, int64_t cout) {
+        f32t(n + ".weight", { K, cin, cout }, 0.0f, 0.7f / std::sqrt((float) (K * cin)));
+        f32t(n + ".bias", { cout }, 0.0f, 0.02f);
+    };
+    auto convtr = [&](const std::string & n, int64_t K, int64_t cin, int64_t cout, int64_t stride) {
+        f32t(n + ".weight", { K, cout, cin }, 0.0f, 0.7f / std::sqrt((float) (cin * K / stride)));
+        f32t(n + ".bias", { cout }, 0.0f, 0.02f);
+    };
+    f32t("codec.dq.first.0.embed", { s.voc_dq, s.vs }, 0.0f, 1.0f);
+    lin("codec.dq.first.out_proj.weight", s.voc_dq, s.voc_cbdim);
+    for (int cb = 1; cb < s.nc; cb++) f32t("codec.dq.rest." + std::to_string(cb - 1) + ".embed", { s.voc_dq, s.vs }, 0.0f, 1.0f);
+    lin("codec.dq.rest.out_proj.weight", s.voc_dq, s.voc_cbdim);
+    conv("codec.dpre.conv", 3, s.voc_cbdim, s.voc_latent);
+    lin("codec.dtf.in_proj.weight", s.voc_latent, s.voc_hidden);
+    f32t("codec.dtf.in_proj.bias", { s.voc_hidden }, 0.0f, 0.02f);
+    for (int l = 0; l < s.voc_layers; l++) {
+        const std::string p = "codec.dtf.blk." + std::to_string(l);
+        nrm(p + ".attn_norm.weight", s.voc_hidden);
+        lin(p + ".attn_q.weight", s.voc_hidden, (int64_t) s.voc_heads * s.voc_hd);
+        lin(p + ".attn_k.weight", s.voc_hidden, (int64_t) s.voc_kv * s.voc_hd);
+        lin(p + ".attn_v.weight", s.voc_hidden, (int64_t) s.voc_kv * s.voc_hd);
+        lin(p + ".attn_output.weight", (int64_t) s.voc_heads * s.voc_hd, s.voc_hidden);
+        f32t(p + ".attn_scale", { s.voc_hidden }, 0.1f, 0.01f);
+        nrm(p + ".ffn_norm.weight", s.voc_hidden);
+        lin(p + ".ffn_gate.weight", s.voc_hidden, s.voc_ffn);
+        lin(p + ".ffn_up.weight", s.voc_hidden, s.voc_ffn);
+        lin(p + ".ffn_down.weight", s.voc_ffn, s.voc_hidden);
+        f32t(p + ".ffn_scale", { s.voc_hidden }, 0.1f, 0.01f);
+    }
+    nrm("codec.dtf.norm.weight", s.voc_hidden);
+    lin("codec.dtf.out_proj.weight", s.voc_hidden, s.voc_latent);
+    f32t("codec.dtf.out_proj.bias", { s.voc_latent }, 0.0f, 0.02f);
+    for (size_t i = 0; i < s.voc_ratios.size(); i++) {
+        const std::string p = "codec.dup." + std::to_string(i);
+        const int r = s.voc_ratios[i];
+        convtr(p + ".up.conv", 2 * r, s.voc_latent, s.voc_latent, r);
+        f32t(p + ".dw.weight", { s.voc_latent, 7 }, 0.0f, 0.7f / std::sqrt(7.0f));
+        f32t(p + ".dw.bias", { s.voc_latent }, 0.0f, 0.02f);
+        nrm(p + ".norm.weight", s.voc_latent);
+        f32t(p + ".norm.bias", { s.voc_latent }, 0.0f, 0.02f);
+        lin(p + ".pw1.weight", s.voc_latent, 4 * s.voc_latent);
+        f32t(p + ".pw1.bias", { 4 * s.voc_latent }, 0.0f, 0.02f);
+        lin(p + ".pw2.weight", 4 * s.voc_latent, s.voc_latent);
+        f32t(p + ".pw2.bias", { s.voc_latent }, 0.0f, 0.02f);
+        f32t(p + ".gamma", { s.voc_latent }, 0.1f, 0.01f);
+    }
+    conv("codec.dhead.conv", 7, s.voc_latent, s.voc_dec);
+    int64_t ch = s.voc_dec;
+    for (size_t i = 0; i < s.voc_rates.size(); i++) {
+        const std::string p = "codec.dblk." + std::to_string(i);
+        const int r = s.voc_rates[i];
+        f32t(p + ".alpha", { ch }, 0.0f, 0.1f);
+        f32t(p + ".beta", { ch }, 0.0f, 0.1f);
+        convtr(p + ".up.conv", 2 * r, ch, ch / 2, r);
+        ch /= 2;
+        for (int j = 0; j < 3; j++) {
+            const std::string q = p + ".res." + std::to_string(j);
+            f32t(q + ".a1", { ch }, 0.0f, 0.1f);
+            f32t(q + ".b1", { ch }, 0.0f, 0.1f);
+            conv(q + ".conv1.conv", 7, ch, ch);
+            f32t(q + ".a2", { ch }, 0.0f, 0.1f);
+            f32t(q + ".b2", { ch }, 0.0f, 0.1f);
+            conv(q + ".conv2.conv", 1, ch, ch);
+        }
+    }
+    f32t("codec.dfin.alpha", { ch }, 0.0f, 0.1f);
+    f32t("codec.dfin.beta", { ch }, 0.0f, 0.1f);
+    conv("codec.dfin.conv", 7, ch, 1);
+
     Writer w;
     w.kv_str("general.architecture", "breeze");
     w.kv_str("general.name", "breeze-synthetic-" + preset);
@@ -421,6 +509,20 @@ int main(int argc, char ** argv) {
     w.kv_f32("breeze.dd.rope_high_freq_factor", 0.0078125f);
     w.kv_f32("breeze.dd.rope_low_freq_factor", 0.001953125f);
     w.kv_u32("breeze.dd.rope_orig_ctx", 16);
+    w.kv_u32("breeze.codec.dec.hidden_size", s.voc_hidden);
+    w.kv_u32("breeze.codec.dec.block_count", s.voc_layers);
+    w.kv_u32("breeze.codec.dec.head_count", s.voc_heads);
+    w.kv_u32("breeze.codec.dec.head_count_kv", s.voc_kv);
+    w.kv_u32("breeze.codec.dec.head_dim", s.voc_hd);
+    w.kv_u32("breeze.codec.dec.feed_forward_length", s.voc_ffn);
+    w.kv_f32("breeze.codec.dec.rms_eps", 1e-5f);
+    w.kv_f32("breeze.codec.dec.rope_theta", 10000.0f);
+    w.kv_u32("breeze.codec.dec.sliding_window", s.voc_window);
+    w.kv_u32("breeze.codec.dec.latent_dim", s.voc_latent);
+    w.kv_u32("breeze.codec.dec.codebook_dim", s.voc_cbdim);
+    w.kv_u32("breeze.codec.dec.decoder_dim", s.voc_dec);
+    w.kv_i32_arr("breeze.codec.dec.upsample_rates", s.voc_rates);
+    w.kv_i32_arr("breeze.codec.dec.upsampling_ratios", s.voc_ratios);
 
     // tokenizer (src/tokenizer.cpp:19-41): every id >= 264 has a unique special spelling so an
     // id list maps to text exactly; bytes are <0xNN>; [S0]/<ins_bos>/<ins_eos> are control tokens

@@ -1,0 +1,747 @@
+// Codec decoder on the GPU (reference: src/codec_decoder.cpp:11-98, src/codec_conv.cpp:9-59,
+// src/codec_transformer.cpp:48-83, src/codec.cpp:15-59, src/c_api.cpp:952-1229).
+//
+// Activations of the convolution stack are [channels][time] f32 (the reference's ggml [L, C]
+// tensors, time contiguous); the transformer and the ConvNeXt MLPs work on [time][channels] rows
+// so that their Q8_0 linears run through the dequant-GEMV. Convolutions are direct f32 kernels
+// tiled 64 output channels x 64 time steps with the input window and kernel slice staged in
+// shared memory.
+#include "vocoder.h"
+#include "rope.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+namespace bzb {
+
+#define VCHECK(x)                                                                             \
+    do {                                                                                      \
+        cudaError_t e_ = (x);                                                                 \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " (" #x ")"); \
+    } while (0)
+
+namespace {
+
+constexpr int kTile = 64;   // output channels and time steps per conv CTA
+constexpr int kCi = 8;      // input channels staged per pass
+
+// sum over codebooks of the quantiser embeddings (src/codec_decoder.cpp:41-62): out_first[t] =
+// E_first[code0], out_rest[t] = sum_{cb>=1} E_rest[cb-1][code_cb], both f16 for the projections
+__global__ void voc_embed_kernel(const float * first, const float * rest, const int * codes, int nc, int n_cb, int dq,
+                                 int vs, half * out_first, half * out_rest) {
+    const int t = blockIdx.x;
+    for (int d = threadIdx.x; d < dq; d += blockDim.x) {
+        int c0 = codes[(size_t) t * nc];
+        c0 = min(max(c0, 0), vs - 1);
+        out_first[(size_t) t * dq + d] = __float2half_rn(first[(size_t) c0 * dq + d]);
+        float acc = 0.0f;
+        for (int cb = 1; cb < n_cb; cb++) {
+            int c = codes[(size_t) t * nc + cb];
+            c = min(max(c, 0), vs - 1);
+            acc += rest[((size_t) (cb - 1) * vs + c) * dq + d];
+        }
+        out_rest[(size_t) t * dq + d] = __float2half_rn(acc);
+    }
+}
+
+// out[c][r] = in[r][c] (+ add[c][r] when non-null)
+__global__ void voc_transpose_kernel(const float * in, int R, int C, float * out, const float * add) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        tile[i][threadIdx.x] = (r < R && c < C) ? in[(size_t) r * C + c] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (c < C && r < R) {
+            float v = tile[threadIdx.x][i];
+            if (add) v += add[(size_t) c * R + r];
+            out[(size_t) c * R + r] = v;
+        }
+    }
+}
+
+// causal conv, stride 1 (src/codec_conv.cpp:9-23): y[o][t] = b[o] + sum_i sum_k w[o][i][k]
+// x[i][t - (K-1-k) d]; optional SnakeBeta on the input as it is staged (alpha, beta per input
+// channel), optional residual add of `res` [Cout][L]
+__global__ void __launch_bounds__(256) voc_conv1d_kernel(const float * x, int cin, int L, const float * w,
+                                                         const float * b, int cout, int K, int dil, const float * snake_a,
+                                                         const float * snake_b, const float * res, float * y) {
+    extern __shared__ float sm[];
+    const int halo = (K - 1) * dil;
+    const int xw = kTile + halo;
+    float * xs = sm;                        // [kCi][xw]
+    float * ws = sm + kCi * xw;             // [kCi][K][kTile]
+    const int t0 = blockIdx.x * kTile, o0 = blockIdx.y * kTile;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    float acc[4][4] = {};
+    for (int i0 = 0; i0 < cin; i0 += kCi) {
+        for (int idx = threadIdx.x; idx < kCi * xw; idx += 256) {
+            const int i = idx / xw, j = idx % xw;
+            const int ci = i0 + i, t = t0 - halo + j;
+            float v = 0.0f;
+            if (ci < cin && t >= 0 && t < L) {
+                v = x[(size_t) ci * L + t];
+                if (snake_a) {
+                    const float s = sinf(v * snake_a[ci]);
+                    v = v + (s * s) / snake_b[ci];
+                }
+            }
+            xs[idx] = v;
+        }
+        for (int idx = threadIdx.x; idx < kCi * K * kTile; idx += 256) {
+            const int o = idx % kTile, k = (idx / kTile) % K, i = idx / (kTile * K);
+            const int ci = i0 + i, co = o0 + o;
+            ws[idx] = (ci < cin && co < cout) ? w[((size_t) co * cin + ci) * K + k] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = 0; i < kCi; i++) {
+            for (int k = 0; k < K; k++) {
+                float xv[4], wv[4];
+#pragma unroll
+                for (int jt = 0; jt < 4; jt++) xv[jt] = xs[i * xw + tx * 4 + jt + k * dil];
+#pragma unroll
+                for (int jo = 0; jo < 4; jo++) wv[jo] = ws[(i * K + k) * kTile + ty * 4 + jo];
+#pragma unroll
+                for (int jo = 0; jo < 4; jo++)
+#pragma unroll
+                    for (int jt = 0; jt < 4; jt++) acc[jo][jt] += wv[jo] * xv[jt];
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int jo = 0; jo < 4; jo++) {
+        const int co = o0 + ty * 4 + jo;
+        if (co >= cout) continue;
+#pragma unroll
+        for (int jt = 0; jt < 4; jt++) {
+            const int t = t0 + tx * 4 + jt;
+            if (t >= L) continue;
+            float v = acc[jo][jt] + (b ? b[co] : 0.0f);
+            if (res) v += res[(size_t) co * L + t];
+            y[(size_t) co * L + t] = v;
+        }
+    }
+}
+
+// causal transposed conv (src/codec_conv.cpp:25-32): y[o][u] = b[o] + sum_i sum_{k = u mod s +
+// m s < K} w[i][o][k] x[i][(u - k) / s], first L s outputs; optional SnakeBeta on the input
+__global__ void __launch_bounds__(256) voc_convtr_kernel(const float * x, int cin, int L, const float * w,
+                                                         const float * b, int cout, int K, int s, const float * snake_a,
+                                                         const float * snake_b, float * y) {
+    extern __shared__ float sm[];
+    const int Lo = L * s;
+    const int u0 = blockIdx.x * kTile, o0 = blockIdx.y * kTile;
+    // input steps that reach outputs [u0, u0 + 64): t in [(u0 - K + 1) / s, (u0 + 63) / s]
+    const int tlo = max(0, (u0 - K + 1 + s - 1) / s - 1);
+    const int thi = min(L - 1, (u0 + kTile - 1) / s);
+    const int xw = thi - tlo + 1;
+    float * xs = sm;                        // [kCi][128]: xw <= (63 + K) / s + 3 <= 66 for s >= 2, K <= 64
+    float * ws = sm + kCi * (kTile + 64);   // [kCi][K][kTile]
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    float acc[4][4] = {};
+    for (int i0 = 0; i0 < cin; i0 += kCi) {
+        for (int idx = threadIdx.x; idx < kCi * xw; idx += 256) {
+            const int i = idx / xw, j = idx % xw;
+            const int ci = i0 + i, t = tlo + j;
+            float v = 0.0f;
+            if (ci < cin && t < L) {
+                v = x[(size_t) ci * L + t];
+                if (snake_a) {
+                    const float sn = sinf(v * snake_a[ci]);
+                    v = v + (sn * sn) / snake_b[ci];
+                }
+            }
+            xs[i * (kTile + 64) + j] = v;
+        }
+        for (int idx = threadIdx.x; idx < kCi * K * kTile; idx += 256) {
+            const int o = idx % kTile, k = (idx / kTile) % K, i = idx / (kTile * K);
+            const int ci = i0 + i, co = o0 + o;
+            ws[idx] = (ci < cin && co < cout) ? w[((size_t) ci * cout + co) * K + k] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = 0; i < kCi; i++) {
+#pragma unroll
+            for (int jt = 0; jt < 4; jt++) {
+                const int u = u0 + tx * 4 + jt;
+                for (int k = u % s; k < K; k += s) {
+                    const int t = (u - k) / s;
+                    if (u - k < 0 || t >= L) continue;
+                    const float xv = xs[i * (kTile + 64) + (t - tlo)];
+#pragma unroll
+                    for (int jo = 0; jo < 4; jo++) acc[jo][jt] += ws[(i * K + k) * kTile + ty * 4 + jo] * xv;
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int jo = 0; jo < 4; jo++) {
+        const int co = o0 + ty * 4 + jo;
+        if (co >= cout) continue;
+#pragma unroll
+        for (int jt = 0; jt < 4; jt++) {
+            const int u = u0 + tx * 4 + jt;
+            if (u < Lo) y[(size_t) co * Lo + u] = acc[jo][jt] + (b ? b[co] : 0.0f);
+        }
+    }
+}
+
+// causal depthwise conv (src/codec_conv.cpp:42-59), w [K][C]: y[c][t] = b[c] + sum_k w[k][c]
+// x[c][t - (K-1) + k]
+__global__ void voc_depthwise_kernel(const float * x, int C, int L, const float * w, const float * b, int K, float * y) {
+    const size_t n = (size_t) C * L;
+    for (size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (size_t) gridDim.x * blockDim.x) {
+        const int c = (int) (idx / L), t = (int) (idx % L);
+        float acc = 0.0f;
+        for (int k = 0; k < K; k++) {
+            const int tt = t - (K - 1) + k;
+            if (tt >= 0) acc += w[(size_t) k * C + c] * x[(size_t) c * L + tt];
+        }
+        y[idx] = acc + (b ? b[c] : 0.0f);
+    }
+}
+
+// layer norm over each row of [R][C] (mean and variance in double, src/common.cpp:131-134) -> f16
+__global__ void voc_layernorm_kernel(const float * x, int C, const float * w, const float * b, float eps, half * y) {
+    __shared__ double red[2][32];
+    const int r = blockIdx.x;
+    const float * xr = x + (size_t) r * C;
+    double s = 0.0;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) s += xr[c];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (lane == 0) red[0][warp] = s;
+    __syncthreads();
+    double mean = 0.0;
+    for (int i = 0; i < nw; i++) mean += red[0][i];
+    mean /= C;
+    const float mf = (float) mean;
+    double v = 0.0;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float d = xr[c] - mf;
+        v += (double) d * d;
+    }
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[1][warp] = v;
+    __syncthreads();
+    double var = 0.0;
+    for (int i = 0; i < nw; i++) var += red[1][i];
+    var /= C;
+    const float scale = 1.0f / sqrtf((float) var + eps);
+    for (int c = threadIdx.x; c < C; c += blockDim.x)
+        y[(size_t) r * C + c] = __float2half_rn(((xr[c] - mf) * scale) * w[c] + b[c]);
+}
+
+// rows [R][C] += bias, then GELU (erf) to f16 when `gelu`, else plain f32 in place
+__global__ void voc_bias_gelu_kernel(float * x, size_t n, int C, const float * b, half * y16) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const float v = x[i] + b[i % C];
+        y16[i] = __float2half_rn(0.5f * v * (1.0f + erff(v * 0.70710678118654752f)));
+    }
+}
+
+// h[r][c] = (h[r][c] + b[c]) * scale[c] (bias and layer scale of a branch), or with b null just
+// the scale
+__global__ void voc_bias_scale_kernel(float * x, size_t n, int C, const float * b, const float * scale) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const int c = (int) (i % C);
+        x[i] = (x[i] + (b ? b[c] : 0.0f)) * (scale ? scale[c] : 1.0f);
+    }
+}
+
+// h[i] += o[i] * scale[i % C]
+__global__ void voc_scaled_add_kernel(float * h, const float * o, size_t n, int C, const float * scale) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x)
+        h[i] += o[i] * scale[i % C];
+}
+
+// y16 = f16(silu(g) * u)
+__global__ void voc_silu_mul_kernel(const float * g, const float * u, size_t n, half * y16) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const float a = g[i];
+        y16[i] = __float2half_rn((a / (1.0f + expf(-a))) * u[i]);
+    }
+}
+
+// x16 = f16(x) for [R][C] rows
+__global__ void voc_to_f16_kernel(const float * x, size_t n, half * y) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x)
+        y[i] = __float2half_rn(x[i]);
+}
+
+// causal sliding-window GQA attention with NEOX RoPE on q and k (src/codec_transformer.cpp:60-70,
+// src/common.cpp:147-173): one warp per (query t, head h); keys t - window < k <= t; hd <= 128
+__global__ void voc_attn_kernel(const float * q, const float * k, const float * v, int T, int nh, int nkv, int hd,
+                                int window, const float2 * rope, float scale, half * out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T * nh) return;
+    const int t = warp / nh, h = warp % nh, g = h / (nh / nkv);
+    const int E = hd / 32, half_d = hd / 2;
+    float qv[4];
+    // rotated query: element d pairs with d +- hd/2
+    for (int e = 0; e < E; e++) {
+        const int d = lane + 32 * e;
+        const int dp = d < half_d ? d + half_d : d - half_d;
+        const float x0 = q[((size_t) t * nh + h) * hd + d], x1 = q[((size_t) t * nh + h) * hd + dp];
+        const float2 cs = rope[(size_t) t * half_d + (d < half_d ? d : d - half_d)];
+        qv[e] = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
+    }
+    const int k0 = max(0, window > 0 ? t - window + 1 : 0);
+    float m = -INFINITY, l = 0.0f, acc[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+    for (int kk = k0; kk <= t; kk++) {
+        float dot = 0.0f;
+        for (int e = 0; e < E; e++) {
+            const int d = lane + 32 * e;
+            const int dp = d < half_d ? d + half_d : d - half_d;
+            const float x0 = k[((size_t) kk * nkv + g) * hd + d], x1 = k[((size_t) kk * nkv + g) * hd + dp];
+            const float2 cs = rope[(size_t) kk * half_d + (d < half_d ? d : d - half_d)];
+            const float kr = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
+            dot += qv[e] * kr;
+        }
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float sc = dot * scale;
+        const float mn = fmaxf(m, sc);
+        const float corr = expf(m - mn), p = expf(sc - mn);
+        l = l * corr + p;
+        for (int e = 0; e < E; e++) acc[e] = acc[e] * corr + p * v[((size_t) kk * nkv + g) * hd + lane + 32 * e];
+        m = mn;
+    }
+    for (int e = 0; e < E; e++) out[((size_t) t * nh + h) * hd + lane + 32 * e] = __float2half_rn(acc[e] / l);
+}
+
+__global__ void voc_clamp_kernel(const float * x, size_t n, float * y) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x)
+        y[i] = fminf(1.0f, fmaxf(-1.0f, x[i]));
+}
+
+unsigned grid_for(size_t n) { return (unsigned) std::min<size_t>((n + 255) / 256, 148 * 16); }
+
+size_t conv_smem(int K, int dil) { return ((size_t) kCi * (kTile + (K - 1) * dil) + (size_t) kCi * K * kTile) * sizeof(float); }
+size_t convtr_smem(int K) { return ((size_t) kCi * (kTile + 64) + (size_t) kCi * K * kTile) * sizeof(float); }
+constexpr size_t kMaxSmem = 227 * 1024;
+
+}  // namespace
+
+template <class T> T * Vocoder::dalloc(size_t n) {
+    void * p = nullptr;
+    VCHECK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    allocs_.push_back(p);
+    return (T *) p;
+}
+
+const GgufTensor & Vocoder::need(const std::string & name) const {
+    for (const GgufTensor & t : gg_.tensors)
+        if (t.name == name) return t;
+    throw std::runtime_error("vocoder: tensor " + name + " missing from the GGUF");
+}
+
+float * Vocoder::load_f32(const std::string & name, int64_t expect, bool exp_of) {
+    const GgufTensor & t = need(name);
+    if (t.type != 0 || (expect >= 0 && t.nelem() != expect))
+        throw std::runtime_error("vocoder: " + name + " must be F32 with " + std::to_string(expect) + " elements");
+    std::vector<float> h((size_t) t.nelem());
+    std::memcpy(h.data(), gg_.data(t), h.size() * 4);
+    if (exp_of)
+        for (float & v : h) v = expf(v);  // SnakeBeta parameters are stored as logarithms
+    float * d = dalloc<float>(h.size());
+    VCHECK(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+    return d;
+}
+
+QMat Vocoder::load_q8(const std::string & name) {
+    const GgufTensor & t = need(name);
+    if (t.type != 8) throw std::runtime_error("vocoder: " + name + " must be Q8_0");
+    const int K = (int) t.ne[0], M = (int) t.rows();
+    QMat q;
+    q.M = M;
+    q.K = K;
+    q.KB = K / 32;
+    q.MT = (M + 15) / 16;
+    uint8_t * raw = nullptr;
+    VCHECK(cudaMalloc(&raw, t.nbytes));
+    VCHECK(cudaMemcpy(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice));
+    uint4 * qs = dalloc<uint4>((size_t) q.MT * q.KB * 32);
+    half2 * ds = dalloc<half2>((size_t) q.MT * q.KB * 8);
+    repack_q8(raw, M, K, qs, ds, stream_);
+    VCHECK(cudaStreamSynchronize(stream_));
+    cudaFree(raw);
+    q.qs = qs;
+    q.ds = ds;
+    return q;
+}
+
+Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int cout, bool transposed) {
+    Conv c;
+    c.K = K;
+    c.cin = cin;
+    c.cout = cout;
+    const GgufTensor & t = need(name + ".weight");
+    if (t.ne.size() != 3 || t.ne[0] != K || t.ne[1] != (transposed ? cout : cin) || t.ne[2] != (transposed ? cin : cout))
+        throw std::runtime_error("vocoder: unexpected shape of " + name + ".weight");
+    c.w = load_f32(name + ".weight", (int64_t) K * cin * cout);
+    c.b = load_f32(name + ".bias", cout);
+    return c;
+}
+
+Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_(gg), cfg_(cfg), vc_(cfg.voc), device_(device) {
+    VCHECK(cudaSetDevice(device));
+    VCHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    const GgufTensor & e0 = need("codec.dq.first.0.embed");
+    dq_ = (int) e0.ne[0];
+    if (e0.ne[1] < cfg_.vs) throw std::runtime_error("vocoder: codebook tables need at least audio_vocab_size rows");
+    // tables are read for rows < vs only; keep exactly vs rows of each
+    auto table = [&](const std::string & n, float * dst) {
+        const GgufTensor & t = need(n);
+        if (t.type != 0 || t.ne[0] != dq_) throw std::runtime_error("vocoder: " + n + " must be F32 [dq, rows]");
+        VCHECK(cudaMemcpy(dst, gg_.data(t), (size_t) cfg_.vs * dq_ * 4, cudaMemcpyHostToDevice));
+    };
+    emb_first_ = dalloc<float>((size_t) cfg_.vs * dq_);
+    table("codec.dq.first.0.embed", emb_first_);
+    float * rest = dalloc<float>((size_t) std::max(1, cfg_.nc - 1) * cfg_.vs * dq_);
+    for (int cb = 1; cb < cfg_.nc; cb++) table("codec.dq.rest." + std::to_string(cb - 1) + ".embed", rest + (size_t) (cb - 1) * cfg_.vs * dq_);
+    emb_rest_.assign(1, rest);
+    dq_first_out_ = load_q8("codec.dq.first.out_proj.weight");
+    dq_rest_out_ = load_q8("codec.dq.rest.out_proj.weight");
+    cbdim_ = dq_first_out_.M;
+    const GgufTensor & pre = need("codec.dpre.conv.weight");
+    latent_ = (int) pre.ne[2];
+    dpre_ = load_conv("codec.dpre.conv", (int) pre.ne[0], cbdim_, latent_, false);
+    in_proj_ = load_q8("codec.dtf.in_proj.weight");
+    in_proj_b_ = load_f32("codec.dtf.in_proj.bias", vc_.hidden);
+    for (int l = 0; l < vc_.n_layer; l++) {
+        const std::string p = "codec.dtf.blk." + std::to_string(l);
+        Layer L;
+        L.attn_norm = load_f32(p + ".attn_norm.weight", vc_.hidden);
+        L.q = load_q8(p + ".attn_q.weight");
+        L.k = load_q8(p + ".attn_k.weight");
+        L.v = load_q8(p + ".attn_v.weight");
+        L.o = load_q8(p + ".attn_output.weight");
+        L.attn_scale = load_f32(p + ".attn_scale", vc_.hidden);
+        L.ffn_norm = load_f32(p + ".ffn_norm.weight", vc_.hidden);
+        L.gate = load_q8(p + ".ffn_gate.weight");
+        L.up = load_q8(p + ".ffn_up.weight");
+        L.down = load_q8(p + ".ffn_down.weight");
+        L.ffn_scale = load_f32(p + ".ffn_scale", vc_.hidden);
+        layers_.push_back(L);
+    }
+    out_norm_ = load_f32("codec.dtf.norm.weight", vc_.hidden);
+    out_proj_ = load_q8("codec.dtf.out_proj.weight");
+    out_proj_b_ = load_f32("codec.dtf.out_proj.bias", latent_);
+    for (size_t i = 0; i < vc_.ratios.size(); i++) {
+        const std::string p = "codec.dup." + std::to_string(i);
+        Up u;
+        u.ratio = vc_.ratios[i];
+        const GgufTensor & ut = need(p + ".up.conv.weight");
+        u.up = load_conv(p + ".up.conv", (int) ut.ne[0], latent_, latent_, true);
+        const GgufTensor & dw = need(p + ".dw.weight");
+        u.dw.K = (int) dw.ne[1];
+        u.dw.cin = u.dw.cout = latent_;
+        u.dw.w = load_f32(p + ".dw.weight", (int64_t) latent_ * u.dw.K);
+        u.dw.b = load_f32(p + ".dw.bias", latent_);
+        u.norm_w = load_f32(p + ".norm.weight", latent_);
+        u.norm_b = load_f32(p + ".norm.bias", latent_);
+        u.pw1 = load_q8(p + ".pw1.weight");
+        u.pw1_b = load_f32(p + ".pw1.bias", u.pw1.M);
+        u.pw2 = load_q8(p + ".pw2.weight");
+        u.pw2_b = load_f32(p + ".pw2.bias", latent_);
+        u.gamma = load_f32(p + ".gamma", latent_);
+        ups_.push_back(u);
+    }
+    const GgufTensor & hd = need("codec.dhead.conv.weight");
+    dec_ = (int) hd.ne[2];
+    dhead_ = load_conv("codec.dhead.conv", (int) hd.ne[0], latent_, dec_, false);
+    int ch = dec_;
+    for (size_t i = 0; i < vc_.rates.size(); i++) {
+        const std::string p = "codec.dblk." + std::to_string(i);
+        Blk b;
+        b.rate = vc_.rates[i];
+        b.alpha = load_f32(p + ".alpha", ch, true);
+        b.beta = load_f32(p + ".beta", ch, true);
+        const GgufTensor & ut = need(p + ".up.conv.weight");
+        const int co = (int) ut.ne[1];
+        b.up = load_conv(p + ".up.conv", (int) ut.ne[0], ch, co, true);
+        ch = co;
+        for (int j = 0; j < 3; j++) {
+            const std::string q = p + ".res." + std::to_string(j);
+            Res r;
+            r.a1 = load_f32(q + ".a1", ch, true);
+            r.b1 = load_f32(q + ".b1", ch, true);
+            r.c1 = load_conv(q + ".conv1.conv", (int) need(q + ".conv1.conv.weight").ne[0], ch, ch, false);
+            r.a2 = load_f32(q + ".a2", ch, true);
+            r.b2 = load_f32(q + ".b2", ch, true);
+            r.c2 = load_conv(q + ".conv2.conv", (int) need(q + ".conv2.conv.weight").ne[0], ch, ch, false);
+            b.res[j] = r;
+        }
+        blks_.push_back(b);
+    }
+    fin_alpha_ = load_f32("codec.dfin.alpha", ch, true);
+    fin_beta_ = load_f32("codec.dfin.beta", ch, true);
+    dfin_ = load_conv("codec.dfin.conv", (int) need("codec.dfin.conv.weight").ne[0], ch, 1, false);
+    int up_total = 1;
+    for (int r : vc_.ratios) up_total *= r;
+    for (int r : vc_.rates) up_total *= r;
+    if (up_total != kSamplesPerFrame)
+        throw std::runtime_error("vocoder: the upsampling stages give " + std::to_string(up_total) +
+                                 " samples per frame, the C API assumes 1920");
+    // dynamic shared memory of the GEMV variants and of the largest convolution
+    init_kernel_attributes();
+    size_t conv_mx = conv_smem(std::max({ dpre_.K, dhead_.K, dfin_.K }), 1), convtr_mx = 0;
+    for (const Up & u : ups_) convtr_mx = std::max(convtr_mx, convtr_smem(u.up.K));
+    for (const Blk & b : blks_) {
+        convtr_mx = std::max(convtr_mx, convtr_smem(b.up.K));
+        for (int j = 0; j < 3; j++)
+            conv_mx = std::max({ conv_mx, conv_smem(b.res[j].c1.K, 9), conv_smem(b.res[j].c2.K, 1) });
+    }
+    if (conv_mx > kMaxSmem || convtr_mx > kMaxSmem) throw std::runtime_error("vocoder: convolution kernel too long");
+    VCHECK(cudaFuncSetAttribute(voc_conv1d_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) conv_mx));
+    VCHECK(cudaFuncSetAttribute(voc_convtr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) convtr_mx));
+    scr_.ws_elems = (size_t) 1 << 20;
+    scr_.ws = dalloc<float4>(scr_.ws_elems);
+    scr_.n_counters = 4096;
+    scr_.counters = dalloc<int>(scr_.n_counters);
+    VCHECK(cudaMemset(scr_.counters, 0, scr_.n_counters * sizeof(int)));
+}
+
+Vocoder::~Vocoder() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (void * p : scratch_allocs_) cudaFree(p);
+    for (void * p : allocs_) cudaFree(p);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Vocoder::ensure(int T) {
+    if (T <= tcap_) return;
+    VCHECK(cudaStreamSynchronize(stream_));
+    for (void * p : scratch_allocs_) cudaFree(p);
+    scratch_allocs_.clear();
+    tcap_ = std::max(T, 64);
+    const size_t Tc = (size_t) tcap_;
+    // the largest [C][L] activation of the conv stack
+    size_t L = Tc, mx = Tc * std::max({ cbdim_, latent_, vc_.hidden });
+    for (const Up & u : ups_) {
+        L *= u.ratio;
+        mx = std::max(mx, (size_t) latent_ * L);
+    }
+    mx = std::max(mx, (size_t) dec_ * L);
+    int ch = dec_;
+    for (const Blk & b : blks_) {
+        L *= b.rate;
+        ch = b.up.cout;
+        mx = std::max(mx, (size_t) ch * L);
+    }
+    act_elems_ = mx;
+    size_t up_rows = Tc;
+    for (const Up & u : ups_) up_rows *= u.ratio;
+    const size_t wide = std::max({ (size_t) vc_.n_head * vc_.hd, (size_t) vc_.ffn, (size_t) 4 * latent_, (size_t) latent_,
+                                   (size_t) cbdim_, (size_t) dq_ });
+    auto fa = [&](size_t n) { void * p = nullptr; VCHECK(cudaMalloc(&p, std::max<size_t>(n, 16) * 4)); scratch_allocs_.push_back(p); return (float *) p; };
+    auto ha = [&](size_t n) { void * p = nullptr; VCHECK(cudaMalloc(&p, std::max<size_t>(n, 16) * 2)); scratch_allocs_.push_back(p); return (half *) p; };
+    a_ = fa(act_elems_);
+    b_ = fa(act_elems_);
+    c_ = fa(act_elems_);
+    t32_ = fa(up_rows * wide);
+    q_ = fa(Tc * vc_.n_head * vc_.hd);
+    k_ = fa(Tc * vc_.n_kv * vc_.hd);
+    v_ = fa(Tc * vc_.n_kv * vc_.hd);
+    o_ = fa(up_rows * wide);
+    g_ = fa(Tc * vc_.ffn);
+    pcm_ = fa(Tc * kSamplesPerFrame);
+    u_ = fa(Tc * vc_.ffn);
+    t16_ = ha(up_rows * wide);
+    att16_ = ha(Tc * vc_.n_head * vc_.hd);
+    f16_ = ha(std::max(up_rows * wide, Tc * (size_t) dq_ * 2));
+    void * pc = nullptr;
+    VCHECK(cudaMalloc(&pc, Tc * cfg_.nc * sizeof(int)));
+    scratch_allocs_.push_back(pc);
+    codes_ = (int *) pc;
+    if (rope_max_ < tcap_) {
+        const std::vector<float2> tab = rope_table(tcap_, vc_.hd, vc_.theta, 1.0f, nullptr);
+        void * pr = nullptr;
+        VCHECK(cudaMalloc(&pr, tab.size() * sizeof(float2)));
+        scratch_allocs_.push_back(pr);
+        VCHECK(cudaMemcpy(pr, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        rope_ = (float2 *) pr;
+        rope_max_ = tcap_;
+    }
+}
+
+void Vocoder::decode(const int * codes, int T, float * pcm) {
+    if (T <= 0) return;
+    VCHECK(cudaSetDevice(device_));
+    ensure(T);
+    cudaStream_t s = stream_;
+    const int nc = cfg_.nc, H = vc_.hidden, nh = vc_.n_head, nkv = vc_.n_kv, hd = vc_.hd, F = vc_.ffn;
+    if (hd > 128 || hd % 32 || nh % nkv) throw std::runtime_error("vocoder: head_dim must be 32..128 (multiple of 32), heads a multiple of kv heads");
+    VCHECK(cudaMemcpyAsync(codes_, codes, (size_t) T * nc * sizeof(int), cudaMemcpyHostToDevice, s));
+
+    // quantiser decode -> [T][cbdim] -> [cbdim][T]
+    half * e_first = f16_, * e_rest = f16_ + (size_t) T * dq_;
+    voc_embed_kernel<<<T, 128, 0, s>>>(emb_first_, emb_rest_[0], codes_, nc, nc, dq_, cfg_.vs, e_first, e_rest);
+    launch_gemv(dq_first_out_, e_first, dq_, T, GemvOut{ EPI_STORE, t32_, nullptr, cbdim_ }, scr_, s);
+    if (nc > 1) launch_gemv(dq_rest_out_, e_rest, dq_, T, GemvOut{ EPI_RESID, t32_, nullptr, cbdim_ }, scr_, s);
+    auto transpose = [&](const float * in, int R, int C, float * out, const float * add) {
+        voc_transpose_kernel<<<dim3((C + 31) / 32, (R + 31) / 32), dim3(32, 8), 0, s>>>(in, R, C, out, add);
+    };
+    auto conv = [&](const Conv & c, const float * x, int L, int dil, const float * sa, const float * sb, const float * res,
+                    float * y) {
+        const size_t smem = conv_smem(c.K, dil);
+        voc_conv1d_kernel<<<dim3((L + kTile - 1) / kTile, (c.cout + kTile - 1) / kTile), 256, smem, s>>>(
+            x, c.cin, L, c.w, c.b, c.cout, c.K, dil, sa, sb, res, y);
+    };
+    auto convtr = [&](const Conv & c, const float * x, int L, int stride, const float * sa, const float * sb, float * y) {
+        // the staged input window holds (64 + K) / stride + 3 steps, within its 128-float rows
+        if (c.K > 64 || stride < 2 || stride > 16) throw std::runtime_error("vocoder: transposed conv needs stride 2..16 and K <= 64");
+        const size_t smem = convtr_smem(c.K);
+        voc_convtr_kernel<<<dim3((L * stride + kTile - 1) / kTile, (c.cout + kTile - 1) / kTile), 256, smem, s>>>(
+            x, c.cin, L, c.w, c.b, c.cout, c.K, stride, sa, sb, y);
+    };
+    transpose(t32_, T, cbdim_, a_, nullptr);
+    conv(dpre_, a_, T, 1, nullptr, nullptr, nullptr, b_);           // [latent][T]
+
+    // transformer on [T][latent] rows
+    transpose(b_, latent_, T, a_, nullptr);                          // a_ = [T][latent]
+    voc_to_f16_kernel<<<grid_for((size_t) T * latent_), 256, 0, s>>>(a_, (size_t) T * latent_, t16_);
+    float * h = c_;                                                  // [T][H]
+    launch_gemv(in_proj_, t16_, latent_, T, GemvOut{ EPI_STORE, h, nullptr, H }, scr_, s);
+    voc_bias_scale_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, (size_t) T * H, H, in_proj_b_, nullptr);
+    const float scale = 1.0f / std::sqrt((float) hd);
+    for (const Layer & Ly : layers_) {
+        launch_rmsnorm(h, H, Ly.attn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
+        launch_gemv(Ly.q, t16_, H, T, GemvOut{ EPI_STORE, q_, nullptr, nh * hd }, scr_, s);
+        launch_gemv(Ly.k, t16_, H, T, GemvOut{ EPI_STORE, k_, nullptr, nkv * hd }, scr_, s);
+        launch_gemv(Ly.v, t16_, H, T, GemvOut{ EPI_STORE, v_, nullptr, nkv * hd }, scr_, s);
+        const int warps = T * nh;
+        voc_attn_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, k_, v_, T, nh, nkv, hd, vc_.window, rope_, scale, att16_);
+        launch_gemv(Ly.o, att16_, nh * hd, T, GemvOut{ EPI_STORE, o_, nullptr, H }, scr_, s);
+        voc_scaled_add_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, o_, (size_t) T * H, H, Ly.attn_scale);
+        launch_rmsnorm(h, H, Ly.ffn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
+        launch_gemv(Ly.gate, t16_, H, T, GemvOut{ EPI_STORE, g_, nullptr, F }, scr_, s);
+        launch_gemv(Ly.up, t16_, H, T, GemvOut{ EPI_STORE, u_, nullptr, F }, scr_, s);
+        voc_silu_mul_kernel<<<grid_for((size_t) T * F), 256, 0, s>>>(g_, u_, (size_t) T * F, t16_);
+        launch_gemv(Ly.down, t16_, F, T, GemvOut{ EPI_STORE, o_, nullptr, H }, scr_, s);
+        voc_scaled_add_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, o_, (size_t) T * H, H, Ly.ffn_scale);
+    }
+    launch_rmsnorm(h, H, out_norm_, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
+    launch_gemv(out_proj_, t16_, H, T, GemvOut{ EPI_STORE, o_, nullptr, latent_ }, scr_, s);
+    voc_bias_scale_kernel<<<grid_for((size_t) T * latent_), 256, 0, s>>>(o_, (size_t) T * latent_, latent_, out_proj_b_, nullptr);
+    transpose(o_, T, latent_, a_, nullptr);                          // a_ = [latent][T]
+
+    // ConvNeXt upsampling stages
+    int L = T;
+    float * x = a_;
+    float * y = b_;
+    for (const Up & u : ups_) {
+        convtr(u.up, x, L, u.ratio, nullptr, nullptr, y);
+        L *= u.ratio;
+        std::swap(x, y);                                             // x = [latent][L]
+        const size_t n = (size_t) L * latent_;
+        voc_depthwise_kernel<<<grid_for(n), 256, 0, s>>>(x, latent_, L, u.dw.w, u.dw.b, u.dw.K, y);
+        transpose(y, latent_, L, t32_, nullptr);                     // [L][latent]
+        voc_layernorm_kernel<<<L, 256, 0, s>>>(t32_, latent_, u.norm_w, u.norm_b, 1e-6f, t16_);
+        const int F4 = u.pw1.M;
+        launch_gemv(u.pw1, t16_, latent_, L, GemvOut{ EPI_STORE, o_, nullptr, F4 }, scr_, s);
+        voc_bias_gelu_kernel<<<grid_for((size_t) L * F4), 256, 0, s>>>(o_, (size_t) L * F4, F4, u.pw1_b, f16_);
+        launch_gemv(u.pw2, f16_, F4, L, GemvOut{ EPI_STORE, t32_, nullptr, latent_ }, scr_, s);
+        voc_bias_scale_kernel<<<grid_for(n), 256, 0, s>>>(t32_, n, latent_, u.pw2_b, u.gamma);
+        transpose(t32_, L, latent_, y, x);                           // y = x + branch^T
+        std::swap(x, y);
+    }
+    conv(dhead_, x, L, 1, nullptr, nullptr, nullptr, y);
+    std::swap(x, y);                                                 // [dec][L]
+    const int dil[3] = { 1, 3, 9 };
+    float * z = c_;                                                  // third buffer of the residual units
+    for (const Blk & b : blks_) {
+        // SnakeBeta fused into the transposed conv's input staging
+        convtr(b.up, x, L, b.rate, b.alpha, b.beta, y);
+        L *= b.rate;
+        std::swap(x, y);
+        for (int j = 0; j < 3; j++) {
+            const Res & r = b.res[j];
+            conv(r.c1, x, L, dil[j], r.a1, r.b1, nullptr, y);
+            conv(r.c2, y, L, 1, r.a2, r.b2, x, z);                   // residual add of x
+            std::swap(x, z);
+        }
+    }
+    conv(dfin_, x, L, 1, fin_alpha_, fin_beta_, nullptr, y);
+    if (L != T * kSamplesPerFrame) throw std::runtime_error("vocoder: unexpected output length");
+    voc_clamp_kernel<<<grid_for((size_t) L), 256, 0, s>>>(y, (size_t) L, pcm_);
+    VCHECK(cudaGetLastError());
+    VCHECK(cudaMemcpyAsync(pcm, pcm_, (size_t) L * sizeof(float), cudaMemcpyDeviceToHost, s));
+    VCHECK(cudaStreamSynchronize(s));
+}
+
+// ---------------------------------------------------------------------------------- sessions
+void Vocoder::session_create(int sid) {
+    std::lock_guard<std::mutex> lk(mu_);
+    history_[sid].clear();
+}
+
+bool Vocoder::session_free(int sid) {
+    std::lock_guard<std::mutex> lk(mu_);
+    return history_.erase(sid) > 0;
+}
+
+int Vocoder::session_decode(int sid, const int * frames, int n_frames, float * out_pcm) {
+    std::lock_guard<std::mutex> lk(mu_);
+    const int nc = cfg_.nc, spf = kSamplesPerFrame;
+    std::vector<int> & hist = history_[sid];  // an unknown session is created (src/c_api.cpp:1011-1018)
+    const int past = (int) hist.size() / nc;
+    std::vector<int> all(hist);
+    all.insert(all.end(), frames, frames + (size_t) n_frames * nc);
+    std::vector<float> audio((size_t) (past + n_frames) * spf);
+    decode(all.data(), past + n_frames, audio.data());
+    std::memcpy(out_pcm, audio.data() + (size_t) past * spf, (size_t) n_frames * spf * sizeof(float));
+    hist.insert(hist.end(), frames, frames + (size_t) n_frames * nc);
+    const int cur = (int) hist.size() / nc;
+    if (cur > kMaxHistory) hist.erase(hist.begin(), hist.begin() + (size_t) (cur - kMaxHistory) * nc);
+    return n_frames * spf;
+}
+
+int Vocoder::session_decode_batch(int batch, const int * sids, const int * flat_tokens, const int * token_offsets,
+                                  const int * n_frames, float * flat_pcm, const int * pcm_offsets, int * out_n_samples) {
+    int running_tok = 0, running_pcm = 0;
+    const int nc = cfg_.nc, spf = kSamplesPerFrame;
+    for (int b = 0; b < batch; b++) {
+        const int nf = n_frames[b];
+        const int off = token_offsets ? token_offsets[b] : running_tok;
+        const int poff = pcm_offsets ? pcm_offsets[b] : running_pcm;
+        if (nf > 0) session_decode(sids[b], flat_tokens + off, nf, flat_pcm + poff);
+        if (out_n_samples) out_n_samples[b] = nf * spf;
+        running_tok += nf * nc;
+        running_pcm += nf * spf;
+    }
+    return batch;
+}
+
+int Vocoder::stream_decode(const int * frames, int n_frames, float * out_pcm) {
+    std::lock_guard<std::mutex> lk(mu_);
+    decode(frames, n_frames, out_pcm);
+    return n_frames * kSamplesPerFrame;
+}
+
+int Vocoder::stream_decode_batch(int batch, const int * flat_tokens, const int * token_offsets, const int * n_frames,
+                                 float * flat_pcm, const int * pcm_offsets, int * out_n_samples) {
+    std::lock_guard<std::mutex> lk(mu_);
+    int running_tok = 0, running_pcm = 0;
+    const int nc = cfg_.nc, spf = kSamplesPerFrame;
+    for (int b = 0; b < batch; b++) {
+        const int nf = n_frames[b];
+        const int off = token_offsets ? token_offsets[b] : running_tok;
+        const int poff = pcm_offsets ? pcm_offsets[b] : running_pcm;
+        if (nf > 0) decode(flat_tokens + off, nf, flat_pcm + poff);
+        if (out_n_samples) out_n_samples[b] = nf * spf;
+        running_tok += nf * nc;
+        running_pcm += nf * spf;
+    }
+    return batch;
+}
+
+}  // namespace bzb

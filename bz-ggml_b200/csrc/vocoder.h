@@ -1,0 +1,111 @@
+// The codec decoder ("vocoder"): codebook frames -> 24 kHz PCM on the GPU, with the reference's
+// session semantics (src/c_api.cpp:952-1229) and decode graph (src/codec_decoder.cpp:65-98).
+#pragma once
+
+#include "host.h"
+#include "kernels.cuh"
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace bzb {
+
+class Vocoder {
+public:
+    // loads the `codec.*` tensors of an open GGUF onto `device`
+    Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device);
+    ~Vocoder();
+
+    static constexpr int kSamplesPerFrame = 1920;  // a constant of the reference C API
+    static constexpr int kMaxHistory = 32;          // frames kept per session for the causal lookback
+
+    // codes frame-major [T][nc] (host) -> PCM [T * 1920] (host), clamped to [-1, 1]
+    void decode(const int * codes, int T, float * pcm);
+
+    // reference session API (breeze_vocoder_session_*); every call serialised on one mutex
+    void session_create(int sid);
+    int session_decode(int sid, const int * frames, int n_frames, float * out_pcm);
+    int session_decode_batch(int batch, const int * sids, const int * flat_tokens, const int * token_offsets,
+                             const int * n_frames, float * flat_pcm, const int * pcm_offsets, int * out_n_samples);
+    bool session_free(int sid);
+    int stream_decode(const int * frames, int n_frames, float * out_pcm);
+    int stream_decode_batch(int batch, const int * flat_tokens, const int * token_offsets, const int * n_frames,
+                            float * flat_pcm, const int * pcm_offsets, int * out_n_samples);
+
+    int nc() const { return cfg_.nc; }
+    int device() const { return device_; }
+
+private:
+    struct Conv {
+        float * w = nullptr;  // [Cout][Cin][K] (transposed convs [Cin][Cout][K]; depthwise [K][C])
+        float * b = nullptr;
+        int cin = 0, cout = 0, K = 0;
+    };
+    struct Layer {
+        QMat q, k, v, o, gate, up, down;
+        float * attn_norm = nullptr, * ffn_norm = nullptr, * attn_scale = nullptr, * ffn_scale = nullptr;
+    };
+    struct Up {  // ConvNeXt upsampling stage
+        Conv up, dw;
+        float * norm_w = nullptr, * norm_b = nullptr, * pw1_b = nullptr, * pw2_b = nullptr, * gamma = nullptr;
+        QMat pw1, pw2;
+        int ratio = 0;
+    };
+    struct Res {
+        float * a1 = nullptr, * b1 = nullptr, * a2 = nullptr, * b2 = nullptr;  // exp(log alpha), exp(log beta)
+        Conv c1, c2;
+    };
+    struct Blk {
+        float * alpha = nullptr, * beta = nullptr;
+        Conv up;
+        Res res[3];
+        int rate = 0;
+    };
+
+    const GgufTensor & need(const std::string & name) const;
+    float * load_f32(const std::string & name, int64_t expect, bool exp_of = false);
+    QMat load_q8(const std::string & name);
+    Conv load_conv(const std::string & name, int K, int cin, int cout, bool transposed);
+    void ensure(int T);
+    template <class T> T * dalloc(size_t n);
+
+    const GgufFile & gg_;
+    ModelConfig cfg_;
+    VocConfig vc_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    std::vector<void *> allocs_;
+    std::vector<void *> scratch_allocs_;
+
+    // weights
+    float * emb_first_ = nullptr;
+    std::vector<float *> emb_rest_;
+    int dq_ = 0, cbdim_ = 0, latent_ = 0, dec_ = 0;
+    QMat dq_first_out_, dq_rest_out_, in_proj_, out_proj_;
+    float * in_proj_b_ = nullptr, * out_proj_b_ = nullptr, * out_norm_ = nullptr;
+    Conv dpre_, dhead_, dfin_;
+    float * fin_alpha_ = nullptr, * fin_beta_ = nullptr;
+    std::vector<Layer> layers_;
+    std::vector<Up> ups_;
+    std::vector<Blk> blks_;
+    float2 * rope_ = nullptr;
+    int rope_max_ = 0;
+    GemvScratch scr_;
+
+    // activations, grown on demand (T frames at a time)
+    int tcap_ = 0;
+    size_t act_elems_ = 0;
+    float * a_ = nullptr, * b_ = nullptr, * c_ = nullptr;   // conv-stack ping-pong [C][L]
+    float * t32_ = nullptr, * q_ = nullptr, * k_ = nullptr, * v_ = nullptr, * o_ = nullptr;
+    float * g_ = nullptr, * u_ = nullptr, * pcm_ = nullptr;
+    half * t16_ = nullptr, * att16_ = nullptr, * f16_ = nullptr;
+    int * codes_ = nullptr;
+
+    std::mutex mu_;
+    std::map<int, std::vector<int>> history_;
+};
+
+}  // namespace bzb

@@ -182,6 +182,7 @@ class Config:
     te: dict = field(default_factory=dict)
     bb: dict = field(default_factory=dict)
     dd: dict = field(default_factory=dict)
+    voc: dict = field(default_factory=dict)
 
 
 def parse_config(g: GGUFFile) -> Config:
@@ -222,6 +223,14 @@ def parse_config(g: GGUFFile) -> Config:
                 high=g.kv("breeze.dd.rope_high_freq_factor", 0.0078125),
                 low=g.kv("breeze.dd.rope_low_freq_factor", 0.001953125),
                 orig=g.kv("breeze.dd.rope_orig_ctx", 16))
+    # src/config.cpp:84-99
+    c.voc = dict(hidden=g.kv("breeze.codec.dec.hidden_size", 512), n_layer=g.kv("breeze.codec.dec.block_count", 8),
+                 n_head=g.kv("breeze.codec.dec.head_count", 16), n_kv=g.kv("breeze.codec.dec.head_count_kv", 16),
+                 hd=g.kv("breeze.codec.dec.head_dim", 64), ffn=g.kv("breeze.codec.dec.feed_forward_length", 1024),
+                 eps=g.kv("breeze.codec.dec.rms_eps", 1e-5), theta=g.kv("breeze.codec.dec.rope_theta", 10000.0),
+                 window=g.kv("breeze.codec.dec.sliding_window", 72),
+                 rates=list(g.kv("breeze.codec.dec.upsample_rates", []) or [8, 5, 4, 3]),
+                 ratios=list(g.kv("breeze.codec.dec.upsampling_ratios", []) or [2, 2]))
     return c
 
 
@@ -900,3 +909,205 @@ class Generator:
                 s.last_hidden = hs[k]
                 nxt[i] = n
         return frames, nxt
+
+
+# ----------------------------------------------------------------------------- vocoder
+# Codec decoder (src/codec_decoder.cpp:11-98, src/codec_conv.cpp:9-59,
+# src/codec_transformer.cpp:48-83). Activations are [channels, time] as in the reference's ggml
+# [L, C] tensors (time contiguous); the transformer works on [time, channels].
+
+def conv1d_causal(x, w, b, stride=1, dilation=1):
+    """src/codec_conv.cpp:9-23: ggml_conv_1d with pad = (K-1)*dilation - (stride-1) on both sides,
+    keeping the first n_out outputs, plus bias. x [Cin, L], w [Cout, Cin, K] -> [Cout, n_out]."""
+    cout, cin, K = w.shape
+    L = x.shape[1]
+    pad = max(0, (K - 1) * dilation - (stride - 1))
+    n_out = (L + pad - dilation * (K - 1) - 1) // stride + 1
+    xp = np.concatenate([np.zeros((cin, pad), np.float32), x.astype(np.float32),
+                         np.zeros((cin, pad), np.float32)], axis=1)
+    y = np.zeros((cout, n_out), np.float64)
+    for k in range(K):
+        cols = xp[:, k * dilation: k * dilation + (n_out - 1) * stride + 1: stride]
+        y += w[:, :, k].astype(np.float64) @ cols.astype(np.float64)
+    if b is not None:
+        y += b.astype(np.float64)[:, None]
+    return y.astype(np.float32)
+
+
+def convtr1d_causal(x, w, b, stride):
+    """src/codec_conv.cpp:25-32: ggml_conv_transpose_1d (padding 0), the first L*stride outputs
+    kept, plus bias. x [Cin, L], w [Cin, Cout, K] -> [Cout, L*stride]."""
+    cin, cout, K = w.shape
+    L = x.shape[1]
+    full = np.zeros((cout, (L - 1) * stride + K), np.float64)
+    for k in range(K):
+        contrib = w[:, :, k].astype(np.float64).T @ x.astype(np.float64)     # [Cout, L]
+        full[:, k: k + (L - 1) * stride + 1: stride] += contrib
+    y = full[:, : L * stride]
+    if b is not None:
+        y = y + b.astype(np.float64)[:, None]
+    return y.astype(np.float32)
+
+
+def depthwise1d_causal(x, w, b):
+    """src/codec_conv.cpp:42-59: y[c, t] = sum_k w[k, c] x[c, t - (K-1) + k] + b[c]; w [K, C]."""
+    K = w.shape[0]
+    C, L = x.shape
+    xp = np.concatenate([np.zeros((C, K - 1), np.float32), x.astype(np.float32)], axis=1)
+    y = np.zeros((C, L), np.float64)
+    for k in range(K):
+        y += w[k].astype(np.float64)[:, None] * xp[:, k: k + L]
+    if b is not None:
+        y += b.astype(np.float64)[:, None]
+    return y.astype(np.float32)
+
+
+def snake_beta(x, la, lb):
+    """src/codec_decoder.cpp:10-16: x + sin(x * exp(la))^2 / exp(lb), per channel."""
+    a = np.exp(la.astype(np.float32))[:, None]
+    bb = np.exp(lb.astype(np.float32))[:, None]
+    s = np.sin((x * a).astype(np.float32)).astype(np.float32)
+    return (x + (s * s) / bb).astype(np.float32)
+
+
+def layer_norm_rows(x, w, b, eps):
+    """ggml_norm over each row (mean and variance accumulated in double) times w plus b
+    (src/common.cpp:131-134). x [rows, C]."""
+    x = x.astype(np.float32)
+    mean = x.astype(np.float64).mean(axis=-1, keepdims=True)
+    xc = (x - mean.astype(np.float32)).astype(np.float32)
+    var = (xc.astype(np.float64) ** 2).mean(axis=-1, keepdims=True)
+    scale = (np.float32(1.0) / np.sqrt((var + eps).astype(np.float32))).astype(np.float32)
+    return ((xc * scale).astype(np.float32) * w.astype(np.float32) + b.astype(np.float32)).astype(np.float32)
+
+
+def gelu_erf(x):
+    x = x.astype(np.float64)
+    from math import sqrt
+    from scipy.special import erf
+    return (0.5 * x * (1.0 + erf(x / sqrt(2.0)))).astype(np.float32)
+
+
+def sliding_causal_mask(T, window):
+    """src/common.cpp:162-173: key k visible to query q when k <= q and q - k < window."""
+    q = np.arange(T)[:, None]
+    k = np.arange(T)[None, :]
+    ok = (k <= q) & ((window <= 0) | (q - k < window))
+    return np.where(ok, 0.0, -np.inf).astype(np.float32)
+
+
+class Vocoder:
+    """Batch-free restatement of MimiCodec::decode (src/codec.cpp:15-24) on the model's
+    `codec.*` tensors, and of the vocoder sessions' windowed decoding (src/c_api.cpp:1004-1064)."""
+
+    SAMPLES_PER_FRAME = 1920   # src/c_api.cpp:1025 (a constant of the C API)
+    MAX_HISTORY = 32           # src/c_api.cpp:1051
+
+    def __init__(self, model: "Model"):
+        self.m = model
+        self.c = model.cfg.voc
+        self.history = {}
+
+    def w(self, name):
+        return self.m.w(name)
+
+    def _conv_w(self, name):
+        return self.w(name)           # ggml [K, Cin, Cout] -> numpy [Cout, Cin, K]
+
+    def quantizer_decode(self, codes, n_cb):
+        """src/codec_decoder.cpp:40-63 -> [codebook_dim, T]."""
+        codes = np.asarray(codes, np.int64).reshape(-1, self.m.cfg.nc)
+        first = self.w("codec.dq.first.0.embed")[codes[:, 0]]
+        first = linear(first, self.w("codec.dq.first.out_proj.weight"))
+        if n_cb > 1:
+            rest = None
+            for cb in range(1, n_cb):
+                e = self.w(f"codec.dq.rest.{cb - 1}.embed")[codes[:, cb]]
+                rest = e if rest is None else (rest + e).astype(np.float32)
+            rest = linear(rest, self.w("codec.dq.rest.out_proj.weight"))
+            first = (first + rest).astype(np.float32)
+        return first.T.copy()
+
+    def transformer(self, x):
+        """src/codec_transformer.cpp:48-83. x [T, latent] -> [T, latent]."""
+        c = self.c
+        T = x.shape[0]
+        h = (linear(x, self.w("codec.dtf.in_proj.weight")) + self.w("codec.dtf.in_proj.bias")).astype(np.float32)
+        cos, sin = rope_cos_sin(np.arange(T), c["hd"], c["theta"])
+        mask = sliding_causal_mask(T, c["window"])
+        scale = 1.0 / math.sqrt(c["hd"])
+        for il in range(c["n_layer"]):
+            p = f"codec.dtf.blk.{il}"
+            res = h
+            cur = rms_norm(h, self.w(p + ".attn_norm.weight"), c["eps"])
+            q = linear(cur, self.w(p + ".attn_q.weight")).reshape(T, c["n_head"], c["hd"])
+            k = linear(cur, self.w(p + ".attn_k.weight")).reshape(T, c["n_kv"], c["hd"])
+            v = linear(cur, self.w(p + ".attn_v.weight")).reshape(T, c["n_kv"], c["hd"])
+            q = rope_neox(q, cos, sin)
+            k = rope_neox(k, cos, sin)
+            a = attention(q, k, v, scale, mask)
+            a = linear(a, self.w(p + ".attn_output.weight")) * self.w(p + ".attn_scale")
+            h = (res + a).astype(np.float32)
+            res = h
+            cur = rms_norm(h, self.w(p + ".ffn_norm.weight"), c["eps"])
+            g = silu(linear(cur, self.w(p + ".ffn_gate.weight")))
+            u = linear(cur, self.w(p + ".ffn_up.weight"))
+            cur = linear((g * u).astype(np.float32), self.w(p + ".ffn_down.weight")) * self.w(p + ".ffn_scale")
+            h = (res + cur).astype(np.float32)
+        h = rms_norm(h, self.w("codec.dtf.norm.weight"), c["eps"])
+        return (linear(h, self.w("codec.dtf.out_proj.weight")) + self.w("codec.dtf.out_proj.bias")).astype(np.float32)
+
+    def convnext(self, p, x):
+        """src/codec_decoder.cpp:18-29 over x [C, L]."""
+        h = depthwise1d_causal(x, self.w(p + ".dw.weight"), self.w(p + ".dw.bias"))
+        h = layer_norm_rows(h.T, self.w(p + ".norm.weight"), self.w(p + ".norm.bias"), 1e-6)
+        h = (linear(h, self.w(p + ".pw1.weight")) + self.w(p + ".pw1.bias")).astype(np.float32)
+        h = gelu_erf(h)
+        h = (linear(h, self.w(p + ".pw2.weight")) + self.w(p + ".pw2.bias")).astype(np.float32)
+        h = (h * self.w(p + ".gamma")).astype(np.float32)
+        return (x + h.T).astype(np.float32)
+
+    def residual_unit(self, p, x, dilation):
+        """src/codec_decoder.cpp:31-38."""
+        h = snake_beta(x, self.w(p + ".a1"), self.w(p + ".b1"))
+        h = conv1d_causal(h, self._conv_w(p + ".conv1.conv.weight"), self.w(p + ".conv1.conv.bias"), 1, dilation)
+        h = snake_beta(h, self.w(p + ".a2"), self.w(p + ".b2"))
+        h = conv1d_causal(h, self._conv_w(p + ".conv2.conv.weight"), self.w(p + ".conv2.conv.bias"), 1, 1)
+        return (x + h).astype(np.float32)
+
+    def decode(self, codes, T, n_cb=0):
+        """src/codec_decoder.cpp:65-98: codes frame-major [T * nc] -> PCM [T * 1920] in [-1, 1]."""
+        c = self.c
+        n_cb = n_cb or self.m.cfg.nc
+        h = self.quantizer_decode(codes, n_cb)
+        h = conv1d_causal(h, self._conv_w("codec.dpre.conv.weight"), self.w("codec.dpre.conv.bias"))
+        h = self.transformer(h.T).T.copy()
+        for i, r in enumerate(c["ratios"]):
+            p = f"codec.dup.{i}"
+            h = convtr1d_causal(h, self.w(p + ".up.conv.weight"), self.w(p + ".up.conv.bias"), r)
+            h = self.convnext(p, h)
+        h = conv1d_causal(h, self._conv_w("codec.dhead.conv.weight"), self.w("codec.dhead.conv.bias"))
+        for i, r in enumerate(c["rates"]):
+            p = f"codec.dblk.{i}"
+            h = snake_beta(h, self.w(p + ".alpha"), self.w(p + ".beta"))
+            h = convtr1d_causal(h, self.w(p + ".up.conv.weight"), self.w(p + ".up.conv.bias"), r)
+            for j, d in enumerate((1, 3, 9)):
+                h = self.residual_unit(p + f".res.{j}", h, d)
+        h = snake_beta(h, self.w("codec.dfin.alpha"), self.w("codec.dfin.beta"))
+        h = conv1d_causal(h, self._conv_w("codec.dfin.conv.weight"), self.w("codec.dfin.conv.bias"))
+        return np.clip(h.reshape(-1), -1.0, 1.0).astype(np.float32)
+
+    def session_decode(self, sid, frames, n_frames):
+        """src/c_api.cpp:1004-1064: decode the kept history plus the new frames, return the new
+        frames' samples, keep the last 32 frames."""
+        nc = self.m.cfg.nc
+        new = np.asarray(frames, np.int64).reshape(-1)[: n_frames * nc]
+        hist = self.history.get(sid, np.zeros(0, np.int64))
+        past = hist.size // nc
+        audio = self.decode(np.concatenate([hist, new]), past + n_frames)
+        out = audio[past * self.SAMPLES_PER_FRAME: (past + n_frames) * self.SAMPLES_PER_FRAME]
+        hist = np.concatenate([hist, new])
+        if hist.size // nc > self.MAX_HISTORY:
+            hist = hist[(hist.size // nc - self.MAX_HISTORY) * nc:]
+        self.history[sid] = hist
+        return out

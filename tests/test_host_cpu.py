@@ -130,6 +130,35 @@ def test_generator_without_gpu_fails_loudly(pkg, tiny_model):
         pytest.skip("a CUDA device is present")
     with pytest.raises(RuntimeError, match="CUDA"):
         pkg.GeneratorHandle(tiny_model, 0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.VocoderHandle(tiny_model, 0)
+
+
+def test_oracle_conv_ops_follow_their_definitions():
+    """The restated conv ops against their defining sums on small random inputs: causal conv
+    (zero history, dilation), transposed conv truncated to L * stride, causal depthwise."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((3, 11)).astype(np.float32)
+    w = rng.standard_normal((5, 3, 4)).astype(np.float32)
+    b = rng.standard_normal(5).astype(np.float32)
+    y = bo.conv1d_causal(x, w, b, 1, 2)
+    ref = np.zeros((5, 11))
+    for o in range(5):
+        for t in range(11):
+            ref[o, t] = b[o] + sum(w[o, i, k] * x[i, t - (3 - k) * 2] for i in range(3) for k in range(4) if t - (3 - k) * 2 >= 0)
+    assert np.allclose(y, ref, atol=1e-4)
+    wt = rng.standard_normal((3, 5, 6)).astype(np.float32)
+    y = bo.convtr1d_causal(x, wt, b, 3)
+    ref = np.zeros((5, 33))
+    for o in range(5):
+        for u in range(33):
+            ref[o, u] = b[o] + sum(wt[i, o, k] * x[i, (u - k) // 3] for i in range(3) for k in range(6)
+                                   if u - k >= 0 and (u - k) % 3 == 0 and (u - k) // 3 < 11)
+    assert np.allclose(y, ref, atol=1e-4)
+    wd = rng.standard_normal((7, 3)).astype(np.float32)
+    y = bo.depthwise1d_causal(x, wd, b[:3])
+    ref = np.array([[b[c] + sum(wd[k, c] * x[c, t - 6 + k] for k in range(7) if t - 6 + k >= 0) for t in range(11)] for c in range(3)])
+    assert np.allclose(y, ref, atol=1e-4)
 
 
 # ---- sampler semantics (src/sampling.cpp:9-60) on the CPU ---------------------------------
