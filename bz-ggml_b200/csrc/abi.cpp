@@ -141,12 +141,13 @@ int breeze_generator_prefill(breeze_generator * gen, const char * text, const ch
 }
 
 int breeze_generator_step_frame(breeze_generator * gen, int cb0, unsigned int seed, int * out_frame_16) {
-    (void) cb0; (void) seed;
+    (void) cb0;  // the session's own last cb0 is the one the reference's caller passes back
     if (!gen || !out_frame_16 || !gen->eng->session_active(kLegacySession)) return -1;
     try {
         const int sid = kLegacySession;
         int next = -1;
-        gen->eng->step(&sid, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false);
+        // depth codes from the GGUF's depth sampler with the call's seed (src/c_api.cpp:297-299)
+        gen->eng->step(&sid, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false, true, &seed);
         return next;
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -176,12 +177,12 @@ int breeze_generator_session_create(breeze_generator * gen, int session_id, cons
 }
 
 int breeze_generator_session_step(breeze_generator * gen, int session_id, unsigned int seed, int * out_frame_16) {
-    (void) seed;
     if (!gen || !out_frame_16) return -1;
     if (!gen->eng->session_active(session_id)) return -1;
     try {
         int next = -1;
-        gen->eng->step(&session_id, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false);
+        // depth codes from the GGUF's depth sampler with the call's seed (src/c_api.cpp:468-479)
+        gen->eng->step(&session_id, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false, true, &seed);
         return next;
     } catch (const std::exception & e) {
         set_error(e.what());

@@ -330,6 +330,9 @@ void Engine::alloc_buffers() {
     row_active_ = dalloc<int>(rmax_);
     next_ = dalloc<int>(rmax_);
     seeds_ = dalloc<uint32_t>(rmax_);
+    dseeds_ = dalloc<uint32_t>(rmax_);
+    row_pair_ = dalloc<int>(rmax_);
+    create_rows_ = dalloc<int>(4);
     cur_frames_ = dalloc<int>((size_t) rmax_ * nc);
     frames_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
     step_ctr_ = dalloc<int>(1);
@@ -384,7 +387,7 @@ void Engine::ensure_prefill_capacity(int T) {
     pff16_ = (half *) pa((size_t) tmax_ * bb.ffn * 2);
     pqkv_ = (float *) pa((size_t) tmax_ * (bbq + 2 * bbkv) * 4);
     patt16_ = (half *) pa((size_t) tmax_ * bbq * 2);
-    plog_ = (float *) pa((size_t) vbb_ * 4);
+    plog_ = (float *) pa((size_t) 2 * vbb_ * 4);   // conditional and unconditional branch
     ptok_ = (int *) pa((size_t) tmax_ * 4);
     pframes_ = (int *) pa((size_t) tmax_ * cfg.nc * 4);
     if (has_te_) {
@@ -608,14 +611,28 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     launches_ += 2;
 }
 
-void Engine::enqueue_step(int R) {
+void Engine::enqueue_step(int R, int flags) {
     const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, D = cfg.dd.hidden;
     StepArgs sa;
     sa.R = R; sa.nc = nc; sa.vs = vs; sa.H = H;
     sa.row_slot = row_slot_; sa.row_active = row_active_; sa.st = st_; sa.hid32 = hid32_; sa.embd = audio_embd_;
     sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
     launch_step_init(sa, stream_);
-    if (dp_supported(R)) {
+    const bool sampled = (flags & kFlagSampled) != 0;
+    // code j of every row from the depth logits; gather_cb >= 0 stages the next sub-step's input
+    auto pick = [&](int j, int gather_cb) {
+        if (!sampled) {
+            launch_argmax_gather(sa, dlog_, vs, vs, j, gather_cb, stream_);
+            return;
+        }
+        DepthSampleArgs da;
+        da.s = sa; da.logits = dlog_; da.ld = vs; da.V = vs; da.col = j; da.gather_cb = gather_cb;
+        da.row_pair = row_pair_;
+        da.seeds = (flags & kFlagSeeds) ? seeds_ : nullptr;
+        da.dseeds = (flags & kFlagDepthSeeds) ? dseeds_ : nullptr;
+        launch_depth_sample_gather(da, stream_);
+    };
+    if (!sampled && dp_supported(R)) {
         // all nc-1 depth sub-steps in one persistent launch
         enqueue_depth(R, nullptr, nullptr);
     } else {
@@ -624,13 +641,13 @@ void Engine::enqueue_step(int R) {
         for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, 2 * R, R, 2, 0);
         launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, R, R, nullptr, stream_);
         gemv(dd_head_[0], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
-        launch_argmax_gather(sa, dlog_, vs, vs, 1, nc > 2 ? 1 : -1, stream_);
+        pick(1, nc > 2 ? 1 : -1);
         for (int j = 2; j < nc; j++) {
             gemv(dd_in_, din16_, H, R, GemvOut{ EPI_STORE, dx_, nullptr, D });
             for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, R, R, 1, j);
             launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, 0, R, nullptr, stream_);
             gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
-            launch_argmax_gather(sa, dlog_, vs, vs, j, j + 1 < nc ? j : -1, stream_);
+            pick(j, j + 1 < nc ? j : -1);
         }
     }
     // backbone: one token per session over its own paged cache
@@ -641,24 +658,24 @@ void Engine::enqueue_step(int R) {
     SampleArgs sm;
     sm.logits = blog_; sm.ld = vbb_; sm.V = vbb_; sm.R = R;
     sm.row_slot = row_slot_; sm.row_active = row_active_; sm.st = st_; sm.hist = hist_; sm.hist_ld = hist_ld_;
-    // the generator ABI hard-codes the cb0 sampler (src/c_api.cpp:343-351)
+    // suppression of the non-code ids [codebook size, audio vocab) (src/c_api.cpp:348-350)
     sm.sup_lo = cfg.cb_size; sm.sup_hi = cfg.vs; sm.eos = cfg.bb_eos;
-    sm.temp = 0.9f; sm.rep = 1.1f; sm.top_p = 1.0f; sm.top_k = 50;
-    sm.seeds = seeds_enabled_ ? seeds_ : nullptr; sm.step_ctr = step_ctr_; sm.next_out = next_;
+    sm.row_pair = row_pair_;
+    sm.seeds = (flags & kFlagSeeds) ? seeds_ : nullptr; sm.step_ctr = step_ctr_; sm.next_out = next_;
     launch_sample(sm, stream_);
     launch_frames_commit(cur_frames_, frames_all_, R * nc, step_ctr_, stream_);
 }
 
-cudaGraphExec_t Engine::graph_for(int R) {
-    const auto key = std::make_pair(R, seeds_enabled_ ? 1 : 0);
+cudaGraphExec_t Engine::graph_for(int R, int flags) {
+    const auto key = std::make_pair(R, flags);
     auto it = graphs_.find(key);
     if (it != graphs_.end()) return it->second;
     cudaGraph_t g = nullptr;
-    depth_plan(R);  // uploads the persistent schedule outside the capture
+    if (!(flags & kFlagSampled)) depth_plan(R);  // uploads the persistent schedule outside the capture
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     set_pdl_scope(true);
     try {
-        enqueue_step(R);
+        enqueue_step(R, flags);
     } catch (...) {
         set_pdl_scope(false);
         cudaStreamEndCapture(stream_, &g);
@@ -678,15 +695,16 @@ cudaGraphExec_t Engine::graph_for(int R) {
 }
 
 StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
-                        int width, int * next_out, bool fill_inactive) {
+                        int width, int * next_out, bool fill_inactive, bool sampled_depth,
+                        const uint32_t * depth_seeds) {
     StepResult res;
     const int nc = cfg.nc;
     if (n > rmax_) throw std::runtime_error("batch of " + std::to_string(n) + " sessions exceeds the engine's " + std::to_string(rmax_) + " rows (BZB_MAX_BATCH)");
     if (K > kmax_) throw std::runtime_error("burst longer than 64 steps");
-    const int R = std::max(8, round_up(n, 8));
-    std::vector<int> rs(R, -1);
+    std::vector<int> rs(n, -1);
     std::vector<char> used(max_slots_, 0);
     bool any = false;
+    int n_pairs = 0;
     for (int i = 0; i < n; i++) {
         auto it = sid_to_slot_.find(sids[i]);
         if (it == sid_to_slot_.end()) continue;
@@ -695,18 +713,45 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
         used[s] = 1;
         rs[i] = s;
         any = true;
+        if (slots_[s].partner >= 0) n_pairs++;
     }
     for (int i = 0; i < n; i++) next_out[i] = -1;
     if (burst && fill_inactive) std::fill_n(frames_out, (size_t) K * n * width, -1);
     if (!any) return res;
-    seeds_enabled_ = seeds != nullptr;
-    cudaGraphExec_t g = graph_for(R);
+    // rows: the listed sessions in order, then the unconditional branches of two-branch sessions
+    if (n + n_pairs > rmax_) throw std::runtime_error("batch of " + std::to_string(n + n_pairs) + " branches exceeds the engine's " + std::to_string(rmax_) + " rows (BZB_MAX_BATCH)");
+    const int R = std::max(8, round_up(n + n_pairs, 8));
+    rs.resize(R, -1);
+    std::vector<int> rp(R, -1);
+    for (int i = 0, k = n; i < n; i++) {
+        if (rs[i] < 0 || slots_[rs[i]].partner < 0) continue;
+        rs[k] = slots_[rs[i]].partner;
+        rp[i] = k;
+        rp[k] = -2 - i;
+        k++;
+    }
+    // sampled depth: any two-branch session (src/depth_decoder.cpp:252-257), or on request unless
+    // every session's depth sampler is top-1 (the argmax)
+    bool sampled = n_pairs > 0;
+    if (!sampled && sampled_depth)
+        for (int i = 0; i < n; i++)
+            if (rs[i] >= 0 && slots_[rs[i]].dtop_k != 1) sampled = true;
+    const int flags = (seeds ? kFlagSeeds : 0) | (sampled ? kFlagSampled : 0) |
+                      (sampled && depth_seeds && !seeds ? kFlagDepthSeeds : 0);
+    cudaGraphExec_t g = graph_for(R, flags);
     cur_R_ = R;
+    cur_flags_ = flags;
     CK(cudaMemcpyAsync(row_slot_, rs.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(row_pair_, rp.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
     if (seeds) {
         std::vector<uint32_t> sd(R, 0);
         for (int i = 0; i < n; i++) sd[i] = seeds[i];
         CK(cudaMemcpyAsync(seeds_, sd.data(), R * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    }
+    if (flags & kFlagDepthSeeds) {
+        std::vector<uint32_t> sd(R, 0);
+        for (int i = 0; i < n; i++) sd[i] = depth_seeds[i];
+        CK(cudaMemcpyAsync(dseeds_, sd.data(), R * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
     }
     CK(cudaMemsetAsync(step_ctr_, 0, sizeof(int), stream_));
     CK(cudaMemsetAsync(any_active_, 0, kmax_ * sizeof(int), stream_));
@@ -735,7 +780,10 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     }
     for (int i = 0; i < n; i++) {
         next_out[i] = rs[i] >= 0 ? nx[i] : -1;
-        if (rs[i] >= 0 && nx[i] < 0) slots_[rs[i]].active = false;
+        if (rs[i] >= 0 && nx[i] < 0) {
+            slots_[rs[i]].active = false;
+            if (slots_[rs[i]].partner >= 0) slots_[slots_[rs[i]].partner].active = false;
+        }
         if (next_out[i] >= 0) res.still_active++;
     }
     return res;
@@ -744,7 +792,7 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
 void Engine::step_device_only(int K) {
     if (cur_R_ == 0) throw std::runtime_error("no batch has been stepped yet");
     if (K > kmax_) throw std::runtime_error("burst longer than 64 steps");
-    cudaGraphExec_t g = graph_for(cur_R_);
+    cudaGraphExec_t g = graph_for(cur_R_, cur_flags_);
     CK(cudaMemsetAsync(step_ctr_, 0, sizeof(int), stream_));
     for (int k = 0; k < K; k++) CK(cudaGraphLaunch(g, stream_));
 }
@@ -757,7 +805,7 @@ bool Engine::session_active(int sid) const {
 }
 
 // ------------------------------------------------------------------------------------ sessions
-int Engine::acquire_slot(int sid, int n_pages) {
+int Engine::acquire_slot(int sid, int n_pages, bool register_sid) {
     if (free_slots_.empty()) throw std::runtime_error("no free session slot");
     if ((int) free_pages_.size() < n_pages) throw std::runtime_error("KV page pool exhausted");
     const int slot = free_slots_.back();
@@ -774,16 +822,19 @@ int Engine::acquire_slot(int sid, int n_pages) {
     CK(cudaMemcpyAsync(page_table_ + (size_t) slot * max_pages_, row.data(), max_pages_ * sizeof(int),
                        cudaMemcpyHostToDevice, stream_));
     CK(cudaStreamSynchronize(stream_));
-    sid_to_slot_[sid] = slot;
+    if (register_sid) sid_to_slot_[sid] = slot;
+    else s.follower = true;
     return slot;
 }
 
 void Engine::release_slot(int slot) {
     SlotHost & s = slots_[slot];
+    const int partner = s.partner;
     for (int p : s.pages) free_pages_.push_back(p);
-    sid_to_slot_.erase(s.sid);
+    if (!s.follower) sid_to_slot_.erase(s.sid);
     s = SlotHost();
     free_slots_.push_back(slot);
+    if (partner >= 0) release_slot(partner);  // the session's unconditional branch
 }
 
 bool Engine::session_free(int sid) {
@@ -831,7 +882,7 @@ void Engine::te_forward(const std::vector<int> & tokens, float * out_rows) {
     gemv(te_proj_, th16_, D, T, GemvOut{ EPI_STORE, out_rows, nullptr, cfg.hidden });
 }
 
-void Engine::bb_prefill(int slot, int T) {
+void Engine::bb_prefill(int slot, int T, float * logits) {
     const BbConfig & bb = cfg.bb;
     const int H = cfg.hidden, q = bb.n_head * bb.hd, kv = bb.n_kv * bb.hd, qkvd = q + 2 * kv;
     for (int l = 0; l < bb.n_layer; l++) {
@@ -856,14 +907,22 @@ void Engine::bb_prefill(int slot, int T) {
     }
     CK(cudaMemcpyAsync(slot_scalar_, &slot, sizeof(int), cudaMemcpyHostToDevice, stream_));
     launch_rmsnorm(px_, H, bb_out_norm_, H, bb.eps, ph16_, H, hid32_, H, T - 1, 1, slot_scalar_, stream_);
-    gemv(lm_head_, ph16_, H, 1, GemvOut{ EPI_STORE, plog_, nullptr, vbb_ });
+    gemv(lm_head_, ph16_, H, 1, GemvOut{ EPI_STORE, logits, nullptr, vbb_ });
+}
+
+SessionParams Engine::abi_params(float cfg_scale) const {
+    SessionParams p;
+    p.cfg = cfg_scale > 0.0f ? cfg_scale : 1.0f;
+    // cb0: fixed by the generator ABI (src/c_api.cpp:343-347); depth: the GGUF's breeze.depth_*
+    p.temp = 0.9f; p.top_k = 50; p.top_p = 1.0f; p.rep = 1.1f;
+    p.dtemp = cfg.depth_temperature; p.dtop_k = cfg.depth_top_k; p.dtop_p = cfg.depth_top_p;
+    return p;
 }
 
 void Engine::session_create(int sid, const std::string & text, const char * instruction, const char * ref_text,
                             const int * ref_codes, int ref_frames, float cfg_scale, uint32_t seed, int max_new_tokens,
                             int * out_cb0, int * out_alloc) {
-    const float scale = cfg_scale > 0.0f ? cfg_scale : 1.0f;
-    if (scale != 1.0f) throw std::runtime_error("classifier-free guidance (cfg_scale != 1) is not supported by this engine yet");
+    const SessionParams sp = abi_params(cfg_scale);
     // output length estimate (src/c_api.cpp:354-364)
     int est = max_new_tokens;
     if (est <= 0) {
@@ -878,54 +937,85 @@ void Engine::session_create(int sid, const std::string & text, const char * inst
     const std::string spk = "[S0]";
     const std::string ins = instruction ? instruction : "Speak clearly and naturally.";
     const bool has_ref = ref_codes != nullptr && ref_frames > 0 && ref_text != nullptr && std::strlen(ref_text) > 0;
-    std::vector<std::vector<int>> segs;
+    std::vector<std::vector<int>> segs, segs_u;
     if (has_ref) segs.push_back(tok_.encode(spk + ref_text, true));
     segs.push_back(tok_.encode(spk + "<ins_bos>" + ins + "<ins_eos>" + text, true));
-    session_create_tokens(sid, segs, has_ref ? ref_codes : nullptr, has_ref ? ref_frames : 0, seed, est, out_cb0, out_alloc);
+    // the unconditional branch drops the instruction (src/c_api.cpp:411-423)
+    if (sp.cfg != 1.0f) {
+        if (has_ref) segs_u.push_back(segs[0]);
+        segs_u.push_back(tok_.encode(spk + text, true));
+    }
+    session_create_tokens(sid, segs, sp.cfg != 1.0f ? &segs_u : nullptr, has_ref ? ref_codes : nullptr,
+                          has_ref ? ref_frames : 0, seed, est, sp, true, out_cb0, out_alloc);
 }
 
-void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> & segs, const int * ref_codes,
-                                   int ref_frames, uint32_t seed, int est, int * out_cb0, int * out_alloc) {
+void Engine::prefill_prompt(int slot, const std::vector<std::vector<int>> & segs, const int * ref_codes,
+                            int ref_frames, float * logits) {
     const int H = cfg.hidden, nc = cfg.nc;
+    int off = 0;
+    auto add_text = [&](const std::vector<int> & toks) {
+        te_forward(toks, px_ + (size_t) off * H);
+        off += (int) toks.size();
+    };
+    auto add_frames = [&](const int * codes, int F) {
+        CK(cudaMemcpyAsync(pframes_, codes, (size_t) F * nc * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        launch_audio_embed(audio_embd_, pframes_, nc, nc, cfg.vs, F, px_ + (size_t) off * H, nullptr, stream_);
+        CK(cudaStreamSynchronize(stream_));
+        off += F;
+    };
+    if (ref_codes) {
+        add_text(segs[0]);
+        add_frames(ref_codes, ref_frames);
+        std::vector<int> eos((size_t) nc, cfg.cb_eos);
+        add_frames(eos.data(), 1);
+        add_text(segs[1]);
+    } else {
+        add_text(segs.back());
+    }
+    bb_prefill(slot, off, logits);
+}
+
+void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> & segs,
+                                   const std::vector<std::vector<int>> * segs_u, const int * ref_codes,
+                                   int ref_frames, uint32_t seed, int est, const SessionParams & sp, bool clamp_total,
+                                   int * out_cb0, int * out_alloc) {
     // prompt layout (src/c_api.cpp:388-396): [ref text][ref frames][EOS frame] then the tail text
-    int total = 0;
-    for (auto & s : segs) total += (int) s.size();
-    if (ref_codes) total += ref_frames + 1;
-    if (total <= 0) throw std::runtime_error("empty prompt");
-    const int max_available = 2040 - total;
-    if (est > max_available) est = std::max(64, max_available);
+    auto prompt_len = [&](const std::vector<std::vector<int>> & sg) {
+        if (sg.empty() || (ref_codes && sg.size() < 2)) throw std::runtime_error("prompt segments missing");
+        int t = 0;
+        if (ref_codes) t = (int) sg[0].size() + ref_frames + 1 + (int) sg[1].size();
+        else t = (int) sg.back().size();
+        return t;
+    };
+    const int total = prompt_len(segs);
+    const int total_u = segs_u ? prompt_len(*segs_u) : 0;
+    if (total <= 0 || (segs_u && total_u <= 0)) throw std::runtime_error("empty prompt");
+    if (est <= 0) throw std::runtime_error("generation budget must be positive");
+    if (clamp_total) {
+        // src/c_api.cpp:398-403: prompt plus budget stays within 2040 positions
+        const int max_available = 2040 - total;
+        if (est > max_available) est = std::max(64, max_available);
+    }
     const int alloc = total + est + 8;
-    const int n_pages = (alloc + 15) / 16;
-    if (n_pages > max_pages_) throw std::runtime_error("prompt plus generation budget exceeds 4096 positions");
+    const int alloc_u = segs_u ? total_u + est + 8 : 0;
+    const int n_pages = (alloc + 15) / 16, n_pages_u = (alloc_u + 15) / 16;
+    if (n_pages > max_pages_ || n_pages_u > max_pages_)
+        throw std::runtime_error("prompt plus generation budget exceeds 4096 positions");
     auto old = sid_to_slot_.find(sid);
     if (old != sid_to_slot_.end()) {
         CK(cudaStreamSynchronize(stream_));
         release_slot(old->second);
     }
+    ensure_prefill_capacity(std::max(total, total_u));
     const int slot = acquire_slot(sid, n_pages);
     try {
-        ensure_prefill_capacity(total);
-        int off = 0;
-        auto add_text = [&](const std::vector<int> & toks) {
-            te_forward(toks, px_ + (size_t) off * H);
-            off += (int) toks.size();
-        };
-        auto add_frames = [&](const int * codes, int F) {
-            CK(cudaMemcpyAsync(pframes_, codes, (size_t) F * nc * sizeof(int), cudaMemcpyHostToDevice, stream_));
-            launch_audio_embed(audio_embd_, pframes_, nc, nc, cfg.vs, F, px_ + (size_t) off * H, nullptr, stream_);
-            CK(cudaStreamSynchronize(stream_));
-            off += F;
-        };
-        if (ref_codes) {
-            add_text(segs[0]);
-            add_frames(ref_codes, ref_frames);
-            std::vector<int> eos((size_t) nc, cfg.cb_eos);
-            add_frames(eos.data(), 1);
-            add_text(segs[1]);
-        } else {
-            add_text(segs.back());
+        int slot_u = -1;
+        if (segs_u) {
+            slot_u = acquire_slot(sid, n_pages_u, false);
+            slots_[slot].partner = slot_u;
         }
-        bb_prefill(slot, total);
+        prefill_prompt(slot, segs, ref_codes, ref_frames, plog_);
+        if (segs_u) prefill_prompt(slot_u, *segs_u, ref_codes, ref_frames, plog_ + vbb_);
         SessState s{};
         s.active = 1;
         s.pos = total;
@@ -934,13 +1024,24 @@ void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> 
         s.last_cb0 = -1;
         s.key = seed;
         s.draw = 0;
+        s.top_k = sp.top_k; s.temp = sp.temp; s.top_p = sp.top_p; s.rep = sp.rep;
+        s.cfg = segs_u ? sp.cfg : 1.0f;
+        s.dtemp = sp.dtemp; s.dtop_p = sp.dtop_p; s.dtop_k = sp.dtop_k;
         CK(cudaMemcpyAsync(st_ + slot, &s, sizeof(SessState), cudaMemcpyHostToDevice, stream_));
+        if (slot_u >= 0) {
+            SessState su = s;
+            su.pos = total_u;
+            CK(cudaMemcpyAsync(st_ + slot_u, &su, sizeof(SessState), cudaMemcpyHostToDevice, stream_));
+        }
         CK(cudaMemsetAsync(hist_ + (size_t) slot * hist_ld_, 0, hist_ld_ * sizeof(uint16_t), stream_));
+        // the first cb0 from the prefill logits (combined with the unconditional branch's)
+        const int rows[4] = { slot, slot_u, slot_u >= 0 ? 1 : -1, -2 };
+        CK(cudaMemcpyAsync(create_rows_, rows, sizeof(rows), cudaMemcpyHostToDevice, stream_));
         SampleArgs sm;
         sm.logits = plog_; sm.ld = vbb_; sm.V = vbb_; sm.R = 1;
-        sm.row_slot = slot_scalar_; sm.row_active = nullptr; sm.st = st_; sm.hist = hist_; sm.hist_ld = hist_ld_;
+        sm.row_slot = create_rows_; sm.row_active = nullptr; sm.st = st_; sm.hist = hist_; sm.hist_ld = hist_ld_;
+        sm.row_pair = create_rows_ + 2;
         sm.sup_lo = cfg.cb_size; sm.sup_hi = cfg.vs; sm.eos = cfg.bb_eos;
-        sm.temp = 0.9f; sm.rep = 1.1f; sm.top_p = 1.0f; sm.top_k = 50;
         sm.seeds = nullptr; sm.step_ctr = nullptr; sm.next_out = next_; sm.update_hist_first = 1;
         launch_sample(sm, stream_);
         int cb0 = -1;
@@ -950,8 +1051,14 @@ void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> 
         sh.active = true;
         sh.max_tokens = est;
         sh.alloc = alloc;
+        sh.dtop_k = sp.dtop_k;
+        if (slot_u >= 0) {
+            slots_[slot_u].active = true;
+            slots_[slot_u].max_tokens = est;
+            slots_[slot_u].alloc = alloc_u;
+        }
         *out_cb0 = cb0;
-        if (out_alloc) *out_alloc = alloc;
+        if (out_alloc) *out_alloc = alloc + alloc_u;
     } catch (...) {
         cudaStreamSynchronize(stream_);
         release_slot(slot);
@@ -1072,7 +1179,7 @@ void Engine::profile_step(double * out) {
     launches_ = 0;
     CK(cudaEventRecord(a, stream_));
     try {
-        enqueue_step(cur_R_);
+        enqueue_step(cur_R_, cur_flags_);
     } catch (...) {
         prof_ = nullptr;
         throw;

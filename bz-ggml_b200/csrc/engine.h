@@ -25,7 +25,20 @@ struct SlotHost {
     bool active = false;
     int max_tokens = 0;
     int alloc = 0;
+    int partner = -1;       // slot of this session's unconditional branch (two-branch sessions)
+    bool follower = false;  // this slot is another session's unconditional branch
+    int dtop_k = 1;         // depth sampler top-k (1: the argmax schedule serves it)
     std::vector<int> pages;
+};
+
+// Sampler and guidance parameters of a new session (src/sampling.h SampleParams,
+// src/c_api.cpp:340-351, src/generation.cpp:122-128).
+struct SessionParams {
+    float cfg = 1.0f;                               // != 1: a second, unconditional branch
+    float temp = 0.9f, top_p = 1.0f, rep = 1.1f;    // cb0
+    int top_k = 50;
+    float dtemp = 0.9f, dtop_p = 1.0f;              // depth codes (sampled-depth mode only)
+    int dtop_k = 50;
 };
 
 struct StepResult {
@@ -45,18 +58,29 @@ public:
     void session_create(int sid, const std::string & text, const char * instruction, const char * ref_text,
                         const int * ref_codes, int ref_frames, float cfg_scale, uint32_t seed, int max_new_tokens,
                         int * out_cb0, int * out_alloc);
+    // prompt = [ref text segment][ref frames][EOS frame] tail segment (the ref parts only when
+    // ref_codes is non-null); `uncond` adds the unconditional branch's segments (params.cfg != 1).
+    // With clamp_total the budget is clamped so prompt + budget <= 2040 (the generator ABI).
     void session_create_tokens(int sid, const std::vector<std::vector<int>> & text_segments,
-                               const int * ref_codes, int ref_frames, uint32_t seed, int max_tokens,
-                               int * out_cb0, int * out_alloc);
+                               const std::vector<std::vector<int>> * uncond_segments, const int * ref_codes,
+                               int ref_frames, uint32_t seed, int max_tokens, const SessionParams & params,
+                               bool clamp_total, int * out_cb0, int * out_alloc);
+    // the generator ABI's sampler for a session (fixed cb0 sampler, the GGUF's depth sampler)
+    SessionParams abi_params(float cfg_scale) const;
+    const Tokenizer & tokenizer() const { return tok_; }
     bool session_free(int sid);
     int session_count() const { return (int) sid_to_slot_.size(); }
     bool session_active(int sid) const;
     bool session_exists(int sid) const { return sid_to_slot_.count(sid) > 0; }
 
     // K frame steps over a session list (reference: src/c_api.cpp:601-949). frames_out is
-    // [K][n][width]; rows of sessions not stepped keep their initial contents.
+    // [K][n][width]; rows of sessions not stepped keep their initial contents. Depth codes are
+    // the argmax unless the batch holds a two-branch session or `sampled_depth` is set (then
+    // each session's depth sampler, src/depth_decoder.cpp:130-247); `depth_seeds` [n] reseeds the
+    // depth draws per call (src/c_api.cpp:468).
     StepResult step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
-                    int width, int * next_out, bool fill_inactive);
+                    int width, int * next_out, bool fill_inactive, bool sampled_depth = false,
+                    const uint32_t * depth_seeds = nullptr);
 
     // device-resident run of K steps for the current batch (no host copies): timing entry
     void step_device_only(int K);
@@ -103,13 +127,18 @@ private:
     // execution
     void gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out);
     void launch_gemm(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out);
-    void enqueue_step(int R);
+    // graph flags: kFlagSeeds (per-row reseed of the samplers), kFlagSampled (sampled depth),
+    // kFlagDepthSeeds (per-call depth seeds)
+    static constexpr int kFlagSeeds = 1, kFlagSampled = 2, kFlagDepthSeeds = 4;
+    void enqueue_step(int R, int flags);
+    void prefill_prompt(int slot, const std::vector<std::vector<int>> & segs, const int * ref_codes, int ref_frames,
+                        float * logits);
     void depth_layer(int l, int rows, int R, int n_new, int start);
     void bb_decode_layer(int l, int R);
     void te_forward(const std::vector<int> & tokens, float * out_rows);
-    void bb_prefill(int slot, int T);
+    void bb_prefill(int slot, int T, float * logits);
     void ensure_prefill_capacity(int T);
-    cudaGraphExec_t graph_for(int R);
+    cudaGraphExec_t graph_for(int R, int flags);
     const QMat * resident_matrix(const char * tensor) const;
 
     // persistent depth decoder: one schedule (phase table + activation tensor maps) per batch
@@ -122,7 +151,7 @@ private:
     const DpPlan * depth_plan(int R);
     void enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace = nullptr);
     bool dp_supported(int R) const;
-    int acquire_slot(int sid, int n_pages);
+    int acquire_slot(int sid, int n_pages, bool register_sid = true);
     void release_slot(int slot);
 
     GgufFile gg_;
@@ -159,14 +188,14 @@ private:
     int rmax_ = 0, kmax_ = 0;
     int * row_slot_ = nullptr, * row_active_ = nullptr, * next_ = nullptr, * cur_frames_ = nullptr;
     int * frames_all_ = nullptr, * step_ctr_ = nullptr, * any_active_ = nullptr, * slot_scalar_ = nullptr;
-    uint32_t * seeds_ = nullptr;
+    uint32_t * seeds_ = nullptr, * dseeds_ = nullptr;
+    int * row_pair_ = nullptr, * create_rows_ = nullptr;
     half * din16_ = nullptr, * dh16_ = nullptr, * dff16_ = nullptr, * datt16_ = nullptr;
     float * dx_ = nullptr, * dqkv_ = nullptr, * dkv_ = nullptr, * dlog_ = nullptr;
     half * bh16_ = nullptr, * bff16_ = nullptr, * batt16_ = nullptr;
     float * bx_ = nullptr, * bqkv_ = nullptr, * blog_ = nullptr;
     GemvScratch scr_;
-    bool seeds_enabled_ = false;
-    int cur_R_ = 0;
+    int cur_R_ = 0, cur_flags_ = 0;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs_;
     std::map<std::pair<int, int>, cudaGraph_t> graph_defs_;
 

@@ -911,35 +911,22 @@ __device__ __forceinline__ unsigned int f2ord(float f) {
 
 constexpr int kSortN = 4096;
 
-__global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
-    pdl_trigger();
-    pdl_wait();
-    __shared__ unsigned long long keys[kSortN];
-    __shared__ float lmod[kSortN];
-    const int r = blockIdx.x;
-    const int slot = a.row_slot[r];
-    if (slot < 0) return;
-    if (a.row_active && !a.row_active[r]) return;
-    SessState & s = a.st[slot];
-    if (!s.active) return;
-    const float * lr = a.logits + (size_t) r * a.ld;
-    const uint16_t * hr = a.hist + (size_t) slot * a.hist_ld;
-    for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
-        unsigned long long key = 0ull;
-        if (i < a.V) {
-            float l = lr[i];
-            if (i >= a.sup_lo && i < a.sup_hi) l = -INFINITY;
-            if (a.rep != 1.0f && i < a.hist_ld) {
-                const int c = hr[i];
-                for (int q = 0; q < c; q++) l = l > 0.0f ? l / a.rep : l * a.rep;
-            }
-            lmod[i] = l;
-            key = ((unsigned long long) f2ord(l) << 32) | (unsigned long long) (0xFFFFFFFFu - (unsigned) i);
-        }
-        keys[i] = key;
-    }
-    __syncthreads();
-    // bitonic sort, descending
+// sort key: logit descending, then index ascending (the order of std::partial_sort's survivors
+// when logits tie is unspecified; this picks the lowest index first)
+__device__ __forceinline__ unsigned long long sort_key(float l, int i) {
+    return ((unsigned long long) f2ord(l) << 32) | (unsigned long long) (0xFFFFFFFFu - (unsigned) i);
+}
+__device__ __forceinline__ int key_index(unsigned long long k) {
+    return (int) (0xFFFFFFFFu - (unsigned) (k & 0xFFFFFFFFull));
+}
+// the logit back from its key (f2ord is a bijection on the bit patterns)
+__device__ __forceinline__ float key_logit(unsigned long long k) {
+    const unsigned int o = (unsigned int) (k >> 32);
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+
+// descending bitonic sort of kSortN keys by the whole block
+__device__ void sort_keys_desc(unsigned long long * keys) {
     for (int kk = 2; kk <= kSortN; kk <<= 1) {
         for (int j = kk >> 1; j > 0; j >>= 1) {
             for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
@@ -953,68 +940,198 @@ __global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
             __syncthreads();
         }
     }
-    if (threadIdx.x != 0) return;
-    const int V = a.V;
-    const int keep = (a.top_k > 0 && a.top_k < V) ? a.top_k : V;
-    const float temp = a.temp > 0.0f ? a.temp : 1.0f;
-    auto idx_at = [&](int i) -> int { return (int) (0xFFFFFFFFu - (unsigned) (keys[i] & 0xFFFFFFFFull)); };
-    const float maxl = lmod[idx_at(0)];
+}
+
+// One thread: src/sampling.cpp:25-59 over the sorted keys of the modified logits: keep the top k,
+// softmax at the temperature, optional top-p cut with renormalisation, then the inverse CDF at the
+// uniform u in place of std::discrete_distribution.
+__device__ int pick_from_sorted(const unsigned long long * keys, int V, float temp_in, int top_k, float top_p,
+                                float u) {
+    const int keep = (top_k > 0 && top_k < V) ? top_k : V;
+    const float temp = temp_in > 0.0f ? temp_in : 1.0f;
+    const float maxl = key_logit(keys[0]);
     float sum = 0.0f;
-    for (int i = 0; i < keep; i++) sum += expf((lmod[idx_at(i)] - maxl) / temp);
+    for (int i = 0; i < keep; i++) sum += expf((key_logit(keys[i]) - maxl) / temp);
     int cut = keep;
     float total = 1.0f;
-    if (a.top_p < 1.0f) {
+    if (top_p < 1.0f) {
         float cum = 0.0f;
         for (int i = 0; i < keep; i++) {
-            cum += expf((lmod[idx_at(i)] - maxl) / temp) / sum;
-            if (cum >= a.top_p) { cut = i + 1; break; }
+            cum += expf((key_logit(keys[i]) - maxl) / temp) / sum;
+            if (cum >= top_p) { cut = i + 1; break; }
         }
         total = 0.0f;
-        for (int i = 0; i < cut; i++) total += expf((lmod[idx_at(i)] - maxl) / temp) / sum;
+        for (int i = 0; i < cut; i++) total += expf((key_logit(keys[i]) - maxl) / temp) / sum;
     }
-    uint32_t key = s.key, draw = s.draw;
-    if (a.seeds) { key = a.seeds[r] + (uint32_t) (a.step_ctr ? *a.step_ctr : 0); draw = 0; }
-    const uint32_t w = philox_word0(key, draw, 0u);
-    s.key = key;
-    s.draw = draw + 1;
-    const float u = (float) (w >> 8) * (1.0f / 16777216.0f);
     // cdf over the kept probabilities (renormalised by `total` when top-p cut them)
     float cdf_last = 0.0f;
     for (int i = 0; i < cut; i++) {
-        float pi = expf((lmod[idx_at(i)] - maxl) / temp) / sum;
-        if (a.top_p < 1.0f) pi = pi / total;
+        float pi = expf((key_logit(keys[i]) - maxl) / temp) / sum;
+        if (top_p < 1.0f) pi = pi / total;
         cdf_last += pi;
     }
     const float target = u * cdf_last;
-    int pick = idx_at(cut - 1);
+    int pick = key_index(keys[cut - 1]);
     float cdf = 0.0f;
     for (int i = 0; i < cut; i++) {
-        float pi = expf((lmod[idx_at(i)] - maxl) / temp) / sum;
-        if (a.top_p < 1.0f) pi = pi / total;
+        float pi = expf((key_logit(keys[i]) - maxl) / temp) / sum;
+        if (top_p < 1.0f) pi = pi / total;
         cdf += pi;
-        if (target < cdf) { pick = idx_at(i); break; }
+        if (target < cdf) { pick = key_index(keys[i]); break; }
     }
+    return pick;
+}
+
+__device__ __forceinline__ float philox_unit(uint32_t key, uint32_t draw, uint32_t hi) {
+    return (float) (philox_word0(key, draw, hi) >> 8) * (1.0f / 16777216.0f);
+}
+
+__global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned long long keys[kSortN];
+    const int r = blockIdx.x;
+    const int slot = a.row_slot[r];
+    if (slot < 0) return;
+    if (a.row_active && !a.row_active[r]) return;
+    const int pr = a.row_pair ? a.row_pair[r] : -1;
+    if (pr <= -2) return;  // the unconditional branch of a pair: its leader samples for both
+    SessState & s = a.st[slot];
+    if (!s.active) return;
+    const float * lr = a.logits + (size_t) r * a.ld;
+    const float * lu = pr >= 0 ? a.logits + (size_t) pr * a.ld : nullptr;
+    const float cfg = s.cfg, rep = s.rep;
+    const uint16_t * hr = a.hist + (size_t) slot * a.hist_ld;
+    for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
+        unsigned long long key = 0ull;
+        if (i < a.V) {
+            float l = lr[i];
+            if (lu) l = lu[i] + cfg * (l - lu[i]);
+            if (i >= a.sup_lo && i < a.sup_hi) l = -INFINITY;
+            if (rep != 1.0f && i < a.hist_ld) {
+                const int c = hr[i];
+                for (int q = 0; q < c; q++) l = l > 0.0f ? l / rep : l * rep;
+            }
+            key = sort_key(l, i);
+        }
+        keys[i] = key;
+    }
+    __syncthreads();
+    sort_keys_desc(keys);
+    if (threadIdx.x != 0) return;
+    uint32_t key = s.key, draw = s.draw;
+    if (a.seeds) { key = a.seeds[r] + (uint32_t) (a.step_ctr ? *a.step_ctr : 0); draw = 0; }
+    const int pick = pick_from_sorted(keys, a.V, s.temp, s.top_k, s.top_p, philox_unit(key, draw, 0u));
+    s.key = key;
+    s.draw = draw + 1;
+    SessState * u = pr >= 0 ? &a.st[a.row_slot[pr]] : nullptr;  // the unconditional branch's state
     uint16_t * hw = a.hist + (size_t) slot * a.hist_ld;
     if (a.update_hist_first) {
         if (pick < a.hist_ld) hw[pick] = (uint16_t) min(65535, hw[pick] + 1);
         s.last_cb0 = pick;
+        if (u) u->last_cb0 = pick;
         a.next_out[r] = pick;
         return;
     }
     s.steps += 1;
     if (a.advance_pos) s.pos += 1;
+    if (u) {
+        u->steps = s.steps;
+        if (a.advance_pos) u->pos += 1;
+    }
     if (pick == a.eos || s.steps >= s.max_tokens) {
         s.active = 0;
+        if (u) u->active = 0;
         if (a.clamp_on_finish) {
+            // src/c_api.cpp:924-930: both branches' positions clamp to max_tokens - 1
             s.last_cb0 = -1;
             s.pos = min(s.pos, s.max_tokens - 1);
+            if (u) {
+                u->last_cb0 = -1;
+                u->pos = min(u->pos, s.max_tokens - 1);
+            }
         }
         a.next_out[r] = -1;
     } else {
         if (pick < a.hist_ld) hw[pick] = (uint16_t) min(65535, hw[pick] + 1);
         s.last_cb0 = pick;
+        if (u) u->last_cb0 = pick;
         a.next_out[r] = pick;
     }
+}
+
+__global__ void __launch_bounds__(1024) depth_sample_kernel(const DepthSampleArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned long long keys[kSortN];
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int s_code;
+    const StepArgs & sa = a.s;
+    const int r = blockIdx.x;
+    if (!sa.row_active[r]) {
+        if (threadIdx.x == 0) sa.frames[(size_t) r * sa.nc + a.col] = -1;
+        return;
+    }
+    const int pr = a.row_pair ? a.row_pair[r] : -1;
+    if (pr <= -2) return;  // written by its leader
+    const SessState & s = sa.st[sa.row_slot[r]];
+    const float * lc = a.logits + (size_t) r * a.ld;
+    const float * lu = pr >= 0 ? a.logits + (size_t) pr * a.ld : nullptr;
+    const float cfg = s.cfg;
+    const int V = a.V;
+    if (s.dtop_k == 1) {
+        // top-1 is the first argmax (no draw)
+        float best = -INFINITY;
+        int bi = INT_MAX;
+        for (int i = threadIdx.x; i < V; i += blockDim.x) {
+            float v = lc[i];
+            if (lu) v = lu[i] + cfg * (v - lu[i]);
+            if (v > best || (bi == INT_MAX && !(v < best))) { best = v; bi = i; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float b = sv[0];
+            int i0 = si[0];
+            for (int w = 1; w < (int) (blockDim.x >> 5); w++)
+                if (sv[w] > b || (sv[w] == b && si[w] < i0)) { b = sv[w]; i0 = si[w]; }
+            s_code = i0 == INT_MAX ? 0 : i0;
+        }
+    } else {
+        for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
+            unsigned long long key = 0ull;
+            if (i < V) {
+                float l = lc[i];
+                if (lu) l = lu[i] + cfg * (l - lu[i]);
+                key = sort_key(l, i);
+            }
+            keys[i] = key;
+        }
+        __syncthreads();
+        sort_keys_desc(keys);
+        if (threadIdx.x == 0) {
+            uint32_t key = s.key, draw = s.draw;
+            if (a.seeds) { key = a.seeds[r] + (uint32_t) *sa.step_ctr; draw = 0; }
+            else if (a.dseeds) { key = a.dseeds[r]; draw = 0; }
+            s_code = pick_from_sorted(keys, V, s.dtemp, s.dtop_k, s.dtop_p, philox_unit(key, draw, (uint32_t) a.col));
+        }
+    }
+    __syncthreads();
+    const int code = s_code;
+    if (threadIdx.x == 0) {
+        sa.frames[(size_t) r * sa.nc + a.col] = code;
+        if (pr >= 0) sa.frames[(size_t) pr * sa.nc + a.col] = code;
+    }
+    if (a.gather_cb < 0) return;
+    embed_row_f16(sa.embd, (size_t) a.gather_cb * sa.vs + code, sa.din16 + (size_t) r * sa.H);
+    if (pr >= 0) embed_row_f16(sa.embd, (size_t) a.gather_cb * sa.vs + code, sa.din16 + (size_t) pr * sa.H);
 }
 
 __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ctr) {
@@ -1227,6 +1344,13 @@ void launch_argmax_gather(const StepArgs & a, const float * logits, int ld, int 
 void launch_sample(const SampleArgs & a, cudaStream_t s) {
     if (a.V > kSortN) throw std::runtime_error("sampler: vocabulary larger than 4096");
     launch_k(sample_kernel, a.R, 1024, 0, s, a);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_depth_sample_gather(const DepthSampleArgs & a, cudaStream_t s) {
+    if (a.V > kSortN) throw std::runtime_error("depth sampler: vocabulary larger than 4096");
+    if (a.col < 1 || a.col >= a.s.nc) throw std::runtime_error("depth sampler: codebook out of range");
+    launch_k(depth_sample_kernel, a.s.R, 1024, 0, s, a);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

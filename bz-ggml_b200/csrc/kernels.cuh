@@ -46,6 +46,14 @@ struct SessState {
     int last_cb0;
     uint32_t key;     // Philox key (the session's current seed)
     uint32_t draw;    // Philox draw counter under that key
+    // cb0 sampler (src/sampling.cpp:9-60 parameters; the generator ABI fixes T 0.9, top-k 50,
+    // top-p 1, repetition 1.1, src/c_api.cpp:343-351)
+    int top_k;
+    float temp, top_p, rep;
+    float cfg;        // guidance scale of a two-branch session, 1 for a single branch
+    // depth sampler of the sampled-depth mode (breeze.depth_* of the GGUF, src/depth_decoder.cpp:134-140)
+    float dtemp, dtop_p;
+    int dtop_k;
     int pad;
 };
 
@@ -179,6 +187,26 @@ void launch_step_init(const StepArgs & a, cudaStream_t s);
 void launch_argmax_gather(const StepArgs & a, const float * logits, int ld, int V, int col, int gather_cb,
                           cudaStream_t s);
 
+// Row pairing of two-branch (classifier-free guidance) sessions: row_pair[r] = the row of r's
+// unconditional branch (r leads), -2 - leader for that branch's own row (r follows), -1 for a
+// single-branch row. A leader's logits are combined as lu + cfg (lc - lu) (src/c_api.cpp:148-155,
+// src/depth_decoder.cpp:149-152) and its pick is written to both rows.
+//
+// Sampled depth sub-step (src/depth_decoder.cpp:130-161, 163-247): codes[r] = the depth sampler's
+// pick from logits[r] (the session's dtemp / dtop_k / dtop_p; dtop_k 1 is the first argmax), with
+// the Philox uniform for (key, draw, codebook col): key/draw are the session's, or (seeds[r] +
+// step, 0) / (dseeds[r], 0) when those per-row reseeds are given; frames and the next input row
+// as launch_argmax_gather.
+struct DepthSampleArgs {
+    StepArgs s;
+    const float * logits = nullptr;
+    int ld = 0, V = 0, col = 1, gather_cb = -1;
+    const int * row_pair = nullptr;
+    const uint32_t * seeds = nullptr;    // batched reseed: key = seeds[r] + step
+    const uint32_t * dseeds = nullptr;   // per-call depth seed: key = dseeds[r]
+};
+void launch_depth_sample_gather(const DepthSampleArgs & a, cudaStream_t s);
+
 struct SampleArgs {
     const float * logits = nullptr;
     int ld = 0, V = 0, R = 0;
@@ -188,8 +216,8 @@ struct SampleArgs {
     uint16_t * hist = nullptr;      // [slot][hist_ld]
     int hist_ld = 0;
     int sup_lo = 0, sup_hi = 0, eos = 0;
-    float temp = 0.9f, rep = 1.1f, top_p = 1.0f;
-    int top_k = 50;
+    // temperature, top-k, top-p, repetition penalty and guidance scale are the session's (SessState)
+    const int * row_pair = nullptr;     // two-branch pairing (see DepthSampleArgs), or null
     const uint32_t * seeds = nullptr;   // per-row reseed (key = seeds[r] + step) when non-null
     const int * step_ctr = nullptr;
     int * next_out = nullptr;           // [R]

@@ -595,12 +595,25 @@ class Model:
         sub-step's logits come from head j-1 and its argmax feeds the next embedding.
         `forced` [N, nc-1] replaces the argmax as the next input (teacher forcing).
         Returns (codes [N, nc-1], logits [N, nc-1, vs])."""
+        N = hiddens.shape[0]
+        codes = np.zeros((N, self.cfg.nc - 1), np.int64)
+
+        def choose(j, lg):
+            codes[:, j - 1] = np.argmax(lg, axis=1)
+            return codes[:, j - 1] if forced is None else np.asarray(forced)[:, j - 1]
+
+        logits_all = self.depth_chain(hiddens, cb0, choose)
+        return codes, logits_all
+
+    def depth_chain(self, hiddens: np.ndarray, cb0: np.ndarray, choose):
+        """The depth decode of src/depth_decoder.cpp:89-128 over N rows (branches), with the code
+        of each sub-step j = 1..nc-1 chosen by choose(j, logits [N, vs]) -> codes [N] (fed to
+        the next sub-step). Returns the logits [N, nc-1, vs]."""
         c = self.cfg.dd
         nc, vs = self.cfg.nc, self.cfg.vs
         N = hiddens.shape[0]
         kc = np.zeros((c["n_layer"], N, nc + 1, c["n_kv"], c["hd"]), np.float32)
         vc = np.zeros_like(kc)
-        codes = np.zeros((N, nc - 1), np.int64)
         logits_all = np.zeros((N, nc - 1, vs), np.float32)
         scale = 1.0 / math.sqrt(c["hd"])
 
@@ -643,17 +656,16 @@ class Model:
         last = rms_norm(x[:, 1], self.w("dd.output_norm.weight"), c["eps"])
         lg = self.lin(last, "dd.codebooks_head.weight", 0)
         logits_all[:, 0] = lg
-        codes[:, 0] = np.argmax(lg, axis=1)
+        prev = np.asarray(choose(1, lg), np.int64)
         for j in range(2, nc):
-            prev = codes[:, j - 2] if forced is None else np.asarray(forced)[:, j - 2]
             e = self.embed_rows("audio_embd.weight", (j - 1) * vs + prev)
             x = self.lin(e, "dd.in_proj.weight").reshape(N, 1, -1)
             x = run_layers(x, j, 1)
             last = rms_norm(x[:, 0], self.w("dd.output_norm.weight"), c["eps"])
             lg = self.lin(last, "dd.codebooks_head.weight", j - 1)
             logits_all[:, j - 1] = lg
-            codes[:, j - 1] = np.argmax(lg, axis=1)
-        return codes, logits_all
+            prev = np.asarray(choose(j, lg), np.int64)
+        return logits_all
 
 
 @dataclass
@@ -809,6 +821,19 @@ class PhiloxStream:
 
 # ----------------------------------------------------------------------------- sessions
 @dataclass
+class SamplerParams:
+    """src/sampling.h SampleParams for cb0 plus the depth sampler (src/depth_decoder.cpp:134-140);
+    the generator ABI fixes the cb0 part (src/c_api.cpp:343-347)."""
+    temp: float = 0.9
+    top_k: int = 50
+    top_p: float = 1.0
+    rep: float = 1.1
+    dtemp: float = 0.9
+    dtop_k: int = 50
+    dtop_p: float = 1.0
+
+
+@dataclass
 class Session:
     sid: int
     st: BBState
@@ -819,22 +844,46 @@ class Session:
     max_tokens: int
     steps_taken: int = 0
     active: bool = True
+    cfg: float = 1.0               # guidance scale; != 1 adds the unconditional branch below
+    st_u: BBState = None
+    last_hidden_u: np.ndarray = None
+    sp: SamplerParams = field(default_factory=SamplerParams)
+
+
+def combine_logits(lc, lu, scale):
+    """src/c_api.cpp:148-155: uncond + scale * (cond - uncond)."""
+    if lu is None:
+        return lc
+    return (lu + np.float32(scale) * (lc - lu).astype(np.float32)).astype(np.float32)
+
+
+def depth_uniform(key: int, draw: int, j: int) -> np.float32:
+    """The engine's depth draw for codebook j: Philox counter (draw, j) under the key, so depth
+    draws never collide with the cb0 draws (counter (draw, 0))."""
+    return philox_uniform(key, (draw & 0xFFFFFFFF) | (j << 32))
 
 
 class Generator:
-    """Session semantics of the generator C ABI (src/c_api.cpp:325-451, 601-949) with the
-    engine's Philox sampler; CFG (cfg_scale != 1) is not restated."""
+    """Session semantics of the generator C ABI (src/c_api.cpp:325-451, 459-519, 601-949) with
+    the engine's Philox sampler, including the two-branch (classifier-free guidance) sessions and
+    the sampled depth decode (src/depth_decoder.cpp:130-247)."""
 
     def __init__(self, model: Model):
         self.m = model
         self.sessions = {}
 
+    def abi_params(self) -> SamplerParams:
+        c = self.m.cfg
+        return SamplerParams(0.9, 50, 1.0, 1.1, c.depth_temperature, c.depth_top_k, c.depth_top_p)
+
     def _sample_cb0(self, sess: Session, logits) -> int:
         c = self.m.cfg
-        l = apply_penalties(logits, 1.1, sess.hist, c.cb_size, c.vs)
-        return sample_philox(l, 0.9, 50, 1.0, sess.rng.next_uniform())
+        sp = sess.sp
+        l = apply_penalties(logits, sp.rep, sess.hist, c.cb_size, c.vs)
+        return sample_philox(l, sp.temp, sp.top_k, sp.top_p, sess.rng.next_uniform())
 
-    def prompt_embeds(self, text, instruction=None, ref_text=None, ref_codes=None):
+    def prompt_embeds(self, text, instruction=None, ref_text=None, ref_codes=None, cond=True):
+        """src/c_api.cpp:366-396 (cond) and 411-423 (the unconditional branch: no instruction)."""
         m = self.m
         ins = instruction if instruction is not None else "Speak clearly and naturally."
         has_ref = ref_codes is not None and len(ref_codes) > 0 and ref_text
@@ -843,35 +892,53 @@ class Generator:
             embs.append(m.text_encoder(m.tok.encode("[S0]" + ref_text, True)))
             embs.append(m.audio_embed(np.asarray(ref_codes).reshape(-1, m.cfg.nc)))
             embs.append(m.audio_embed(np.full((1, m.cfg.nc), m.cfg.cb_eos)))
-        embs.append(m.text_encoder(m.tok.encode("[S0]<ins_bos>" + ins + "<ins_eos>" + text, True)))
+        tail = "[S0]<ins_bos>" + ins + "<ins_eos>" + text if cond else "[S0]" + text
+        embs.append(m.text_encoder(m.tok.encode(tail, True)))
         return np.concatenate(embs, axis=0)
 
     def session_create(self, sid, text, instruction=None, ref_text=None, ref_codes=None,
-                       seed=0, max_new_tokens=0, embeds=None):
+                       seed=0, max_new_tokens=0, embeds=None, cfg_scale=1.0, params=None,
+                       embeds_u=None, clamp_total=True):
+        cfg = cfg_scale if cfg_scale > 0 else 1.0
         if embeds is None:
             embeds = self.prompt_embeds(text, instruction, ref_text, ref_codes)
+        if cfg != 1.0 and embeds_u is None:
+            embeds_u = self.prompt_embeds(text, instruction, ref_text, ref_codes, cond=False)
         est = max_new_tokens
         if est <= 0:
             words = len(text.split())
             est = min(1000, int(math.ceil(words * 1.5)) + 30)
         total = embeds.shape[0]
-        avail = 2040 - total
-        if est > avail:
-            est = max(64, avail)
+        if clamp_total:
+            avail = 2040 - total
+            if est > avail:
+                est = max(64, avail)
         st = BBState.new(self.m, total + est + 8)
         h, lg = self.m.backbone_run(st, embeds)
-        sess = Session(sid, st, {}, h, -1, PhiloxStream(seed), est)
-        cb0 = self._sample_cb0(sess, lg)
+        sess = Session(sid, st, {}, h, -1, PhiloxStream(seed), est, sp=params or self.abi_params())
+        alloc = total + est + 8
+        lu = None
+        if cfg != 1.0:
+            sess.cfg = cfg
+            sess.st_u = BBState.new(self.m, embeds_u.shape[0] + est + 8)
+            sess.last_hidden_u, lu = self.m.backbone_run(sess.st_u, embeds_u)
+            alloc += embeds_u.shape[0] + est + 8
+        cb0 = self._sample_cb0(sess, combine_logits(lg, lu, sess.cfg))
         sess.hist[cb0] = sess.hist.get(cb0, 0) + 1
         sess.last_cb0 = cb0
         self.sessions[sid] = sess
-        return cb0, total + est + 8
+        return cb0, alloc
 
-    def step_batched(self, sids, seeds=None, forced_depth=None, depth_logits_out=None):
+    def step_batched(self, sids, seeds=None, forced_depth=None, depth_logits_out=None, sampled_depth=False,
+                     depth_seeds=None):
         """One frame for each active session; returns (frames [N, nc], next_cb0 [N]).
-        `forced_depth` [N, nc-1] (rows of `sids`) teacher-forces the depth codes: they become
-        the frame and the next inputs, and the oracle's own logits go to `depth_logits_out`
-        (a dict filled per session id) for tie analysis."""
+        Depth codes are the argmax, or each session's depth sampler when a listed session has two
+        branches (src/depth_decoder.cpp:252-257) or `sampled_depth` is set (the single-session
+        steps, src/c_api.cpp:468-479) unless every session's depth top-k is 1. `depth_seeds` [N]
+        reseed the depth draws per call. `forced_depth` [N, nc-1] (rows of `sids`) teacher-forces
+        the depth codes: they become the frame and the next inputs; the oracle's own (combined)
+        logits go to `depth_logits_out` (a dict filled per session id) and the uniforms it would
+        have drawn to `self.last_depth_uniforms`."""
         m = self.m
         nc = m.cfg.nc
         act = [i for i, s in enumerate(sids) if s in self.sessions and self.sessions[s].active]
@@ -883,31 +950,66 @@ class Generator:
         if seeds is not None:
             for i, s in zip(act, ss):
                 s.rng.seed(int(seeds[i]))
-        hid = np.stack([s.last_hidden for s in ss])
-        cb0 = np.array([s.last_cb0 for s in ss])
+        pairs = [k for k, s in enumerate(ss) if s.cfg != 1.0]
+        sampled = bool(pairs) or (sampled_depth and any(s.sp.dtop_k != 1 for s in ss))
+        n = len(ss)
+        hid = np.stack([s.last_hidden for s in ss] + [ss[k].last_hidden_u for k in pairs])
+        cb0 = np.array([s.last_cb0 for s in ss] + [ss[k].last_cb0 for k in pairs])
+        urow = {k: n + q for q, k in enumerate(pairs)}
         forced = None if forced_depth is None else np.asarray(forced_depth)[act]
-        codes, dl = m.depth_logits_chain(hid, cb0, forced)
-        if forced is not None:
-            codes = forced.astype(np.int64)
+        comb_logits = np.zeros((n, nc - 1, m.cfg.vs), np.float32)
+        self.last_depth_uniforms = {}
+        chosen = np.zeros((n, nc - 1), np.int64)
+
+        def choose(j, lg):
+            out = np.zeros(lg.shape[0], np.int64)
+            for k, s in enumerate(ss):
+                l = combine_logits(lg[k], lg[urow[k]] if k in urow else None, s.cfg)
+                comb_logits[k, j - 1] = l
+                if not sampled or s.sp.dtop_k == 1:
+                    code = int(np.argmax(l))
+                else:
+                    if seeds is not None:
+                        key, draw = s.rng.key, 0
+                    elif depth_seeds is not None:
+                        key, draw = int(depth_seeds[act[k]]) & 0xFFFFFFFF, 0
+                    else:
+                        key, draw = s.rng.key, s.rng.draw
+                    u = depth_uniform(key, draw, j)
+                    self.last_depth_uniforms.setdefault(s.sid, {})[j - 1] = u
+                    code = sample_philox(l, s.sp.dtemp, s.sp.dtop_k, s.sp.dtop_p, u)
+                if forced is not None:
+                    code = int(forced[k, j - 1])
+                chosen[k, j - 1] = code
+                out[k] = code
+                if k in urow:
+                    out[urow[k]] = code
+            return out
+
+        m.depth_chain(hid, cb0, choose)
         if depth_logits_out is not None:
             for k, i in enumerate(act):
-                depth_logits_out[sids[i]] = dl[k]
-        fr = np.concatenate([cb0[:, None], codes], axis=1)
-        ae = m.audio_embed(fr)
-        hs, ls = m.backbone_step_batched([s.st for s in ss], ae)
+                depth_logits_out[sids[i]] = comb_logits[k]
+        fr = np.concatenate([cb0[:n, None], chosen], axis=1)
+        ae = m.audio_embed(np.concatenate([fr, fr[pairs]], axis=0) if pairs else fr)
+        hs, ls = m.backbone_step_batched([s.st for s in ss] + [ss[k].st_u for k in pairs], ae)
         self.last_cb0_logits = {}
         for k, (i, s) in enumerate(zip(act, ss)):
             frames[i] = fr[k]
-            self.last_cb0_logits[s.sid] = (apply_penalties(ls[k], 1.1, s.hist, m.cfg.cb_size, m.cfg.vs), s.rng.key, s.rng.draw)
-            n = self._sample_cb0(s, ls[k])
+            lk = combine_logits(ls[k], ls[urow[k]] if k in urow else None, s.cfg)
+            self.last_cb0_logits[s.sid] = (apply_penalties(lk, s.sp.rep, s.hist, m.cfg.cb_size, m.cfg.vs),
+                                           s.rng.key, s.rng.draw)
+            nx = self._sample_cb0(s, lk)
             s.steps_taken += 1
-            if n == m.cfg.bb_eos or s.steps_taken >= s.max_tokens:
+            if nx == m.cfg.bb_eos or s.steps_taken >= s.max_tokens:
                 s.active = False
             else:
-                s.hist[n] = s.hist.get(n, 0) + 1
-                s.last_cb0 = n
+                s.hist[nx] = s.hist.get(nx, 0) + 1
+                s.last_cb0 = nx
                 s.last_hidden = hs[k]
-                nxt[i] = n
+                if k in urow:
+                    s.last_hidden_u = hs[urow[k]]
+                nxt[i] = nx
         return frames, nxt
 
 
