@@ -29,6 +29,18 @@ _c_uint_p = ctypes.POINTER(ctypes.c_uint)
 _c_float_p = ctypes.POINTER(ctypes.c_float)
 _c_double_p = ctypes.POINTER(ctypes.c_double)
 
+
+class BreezeRequest(ctypes.Structure):
+    """breeze_request of include/breeze.h (reference include/breeze/breeze.h:25-45)."""
+    _fields_ = [("text", ctypes.c_char_p), ("instruction", ctypes.c_char_p), ("ref_text", ctypes.c_char_p),
+                ("ref_audio", _c_float_p), ("ref_audio_len", ctypes.c_int), ("cfg_scale", ctypes.c_float),
+                ("seed", ctypes.c_int), ("max_new_tokens", ctypes.c_int), ("split_chars", ctypes.c_int),
+                ("temperature", ctypes.c_float), ("top_k", ctypes.c_int), ("top_p", ctypes.c_float),
+                ("repetition_penalty", ctypes.c_float)]
+
+
+AUDIO_CB = ctypes.CFUNCTYPE(ctypes.c_int, _c_float_p, ctypes.c_int, ctypes.c_void_p)
+
 # every symbol include/breeze.h and include/bzb_ext.h declare: name -> (restype, argtypes)
 SIGNATURES = {
     "breeze_init": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_int]),
@@ -99,6 +111,10 @@ SIGNATURES = {
                                                   ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "bzb_gguf_inspect": (ctypes.c_int, [ctypes.c_char_p, _c_int_p, _c_int_p, _c_int_p]),
     "bzb_tokenize": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, _c_int_p, ctypes.c_int]),
+    "bzb_generate_codes": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _c_int_p, ctypes.c_int, ctypes.c_void_p,
+                                          ctypes.c_void_p, _c_int_p, ctypes.c_int, _c_int_p, _c_double_p]),
+    "bzb_split_text": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]),
+    "bzb_write_wav": (ctypes.c_int, [ctypes.c_char_p, _c_float_p, ctypes.c_int, ctypes.c_int]),
 }
 
 
@@ -382,6 +398,87 @@ class VocoderHandle:
 
     def __del__(self):
         self.close()
+
+
+class ContextHandle:
+    """breeze_init / breeze_generate / breeze_generate_wav (reference src/c_api.cpp:50-108): one
+    request at a time, PCM streamed through a callback."""
+
+    def __init__(self, model_path: str, use_gpu: int = 1):
+        self.lib = lib()
+        self.handle = self.lib.lib.breeze_init(model_path.encode(), use_gpu)
+        if not self.handle:
+            raise RuntimeError(f"breeze_init failed: {self.lib.last_error()}")
+        self.nc = gguf_inspect(model_path)[1]
+
+    @property
+    def sample_rate(self) -> int:
+        return self.lib.lib.breeze_sample_rate(self.handle)
+
+    @staticmethod
+    def request(text: str, instruction: Optional[str] = None, ref_text: Optional[str] = None, cfg_scale: float = 0.0,
+                seed: int = 42, max_new_tokens: int = 0, split_chars: int = 0, temperature: float = 0.0,
+                top_k: int = 0, top_p: float = 0.0, repetition_penalty: float = 0.0) -> BreezeRequest:
+        enc = lambda x: None if x is None else x.encode("utf-8")
+        return BreezeRequest(enc(text), enc(instruction), enc(ref_text), None, 0, cfg_scale, seed, max_new_tokens,
+                             split_chars, temperature, top_k, top_p, repetition_penalty)
+
+    def generate(self, req: BreezeRequest, stop_after_chunks: int = 0, ref_codes: Optional[np.ndarray] = None,
+                 max_frames: int = 4096):
+        """Runs one request (bzb_generate_codes: breeze_generate plus encoded reference codes);
+        returns (pcm, chunk sizes, frames [F][nc], F, timings dict). With stop_after_chunks > 0
+        the callback asks to stop after that many chunks."""
+        chunks: List[np.ndarray] = []
+
+        def on_audio(ptr, n, user):
+            chunks.append(np.ctypeslib.as_array(ptr, shape=(n,)).copy())
+            return 1 if stop_after_chunks and len(chunks) >= stop_after_chunks else 0
+
+        cb = AUDIO_CB(on_audio)
+        codes = np.zeros((max_frames, self.nc), np.int32)
+        nf = ctypes.c_int()
+        tm = np.zeros(7, np.float64)
+        rc = None if ref_codes is None else np.ascontiguousarray(ref_codes, np.int32)
+        res = self.lib.lib.bzb_generate_codes(self.handle, ctypes.byref(req), None if rc is None else _ip(rc),
+                                              0 if rc is None else rc.shape[0], ctypes.cast(cb, ctypes.c_void_p), None,
+                                              _ip(codes), max_frames, ctypes.byref(nf), tm.ctypes.data_as(_c_double_p))
+        if res != 0:
+            raise RuntimeError(f"breeze_generate failed: {self.lib.last_error()}")
+        pcm = np.concatenate(chunks) if chunks else np.zeros(0, np.float32)
+        timings = dict(zip(["prefill_ms", "steps_ms", "vocoder_ms", "first_audio_ms", "frames", "flushes", "pieces"],
+                           tm.tolist()))
+        n = int(nf.value)
+        return pcm, [c.size for c in chunks], codes[:min(n, max_frames)], n, timings
+
+    def generate_wav(self, req: BreezeRequest, path: str) -> None:
+        if self.lib.lib.breeze_generate_wav(self.handle, ctypes.byref(req), path.encode()) != 0:
+            raise RuntimeError(f"breeze_generate_wav failed: {self.lib.last_error()}")
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.lib.breeze_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+def split_text(text: str, budget: int, first_budget: int = 0) -> List[str]:
+    """The library's long-text splitter (bzb_split_text)."""
+    need = lib().lib.bzb_split_text(text.encode("utf-8"), budget, first_budget, None, 0)
+    buf = ctypes.create_string_buffer(-need)
+    n = lib().lib.bzb_split_text(text.encode("utf-8"), budget, first_budget, buf, len(buf))
+    if n < 0:
+        raise RuntimeError("split_text: buffer sizing failed")
+    parts = buf.raw.split(b"\0")[:n]
+    return [p.decode("utf-8") for p in parts]
+
+
+def write_wav(path: str, samples: np.ndarray, sample_rate: int) -> None:
+    """The library's 16-bit WAV writer (bzb_write_wav)."""
+    x = np.ascontiguousarray(samples, np.float32)
+    if lib().lib.bzb_write_wav(path.encode(), _fp(x), x.size, sample_rate) != 0:
+        raise RuntimeError(lib().last_error())
 
 
 def gguf_inspect(path: str):

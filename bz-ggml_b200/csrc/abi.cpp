@@ -4,6 +4,7 @@
 // boundary; they become the reference's error returns plus breeze_last_error().
 #include "../../include/bzb_ext.h"
 #include "engine.h"
+#include "generate.h"
 #include "vocoder.h"
 
 #include <cerrno>
@@ -30,8 +31,10 @@ struct breeze_vocoder {
     std::unique_ptr<bzb::Vocoder> voc;
 };
 
+// breeze_init's context: a generator and a vocoder sharing its model (src/c_api.cpp:22-25)
 struct breeze_context {
     breeze_generator * gen = nullptr;
+    std::unique_ptr<bzb::Vocoder> voc;
 };
 
 namespace {
@@ -43,6 +46,52 @@ void set_error(const std::string & e) { g_error = e; }
 
 constexpr int kLegacySession = INT_MIN;
 constexpr int kAbiFrameWidth = 16;
+
+// breeze_request -> GenRequest (src/c_api.cpp:30-48)
+bzb::GenRequest to_gen_request(const breeze_request * r) {
+    bzb::GenRequest g;
+    g.text = r->text ? r->text : "";
+    g.instruction = r->instruction ? r->instruction : "Speak clearly and naturally.";
+    g.ref_text = r->ref_text ? r->ref_text : "";
+    if (r->ref_audio && r->ref_audio_len > 0) g.ref_audio.assign(r->ref_audio, r->ref_audio + r->ref_audio_len);
+    g.cfg_scale = r->cfg_scale > 0 ? r->cfg_scale : 1.0f;
+    g.seed = r->seed;
+    g.max_new_tokens = r->max_new_tokens;
+    if (r->split_chars != 0) g.split_chars = r->split_chars < 0 ? 0 : r->split_chars;
+    g.temperature = r->temperature;
+    g.top_k = r->top_k;
+    g.top_p = r->top_p;
+    g.repetition_penalty = r->repetition_penalty;
+    return g;
+}
+
+// breeze_generate with optional encoded reference codes, the generated frames and stage timings
+int generate_impl(breeze_context * ctx, const breeze_request * req, const int * ref_codes, int ref_frames,
+                  breeze_audio_cb cb, void * user, int * out_codes, int max_frames, int * out_n_frames,
+                  double * out_timings) {
+    if (!ctx || !req) { set_error("null context or request"); return 1; }
+    try {
+        bzb::GenRequest g = to_gen_request(req);
+        const int nc = ctx->gen->eng->cfg.nc;
+        if (ref_codes && ref_frames > 0) g.ref_codes.assign(ref_codes, ref_codes + (size_t) ref_frames * nc), g.ref_frames = ref_frames;
+        std::vector<int> codes;
+        bzb::GenTimings tm;
+        bzb::generate(*ctx->gen->eng, *ctx->voc, g, [&](const float * s, int n) { return cb ? cb(s, n, user) == 0 : true; },
+                      &tm, out_codes || out_n_frames ? &codes : nullptr);
+        const int F = (int) codes.size() / nc;
+        if (out_n_frames) *out_n_frames = F;
+        if (out_codes) std::memcpy(out_codes, codes.data(), (size_t) std::min(F, max_frames) * nc * sizeof(int));
+        if (out_timings) {
+            const double t[7] = { tm.prefill, tm.steps, tm.vocoder, tm.first_audio, (double) tm.frames,
+                                  (double) tm.flushes, (double) tm.pieces };
+            std::memcpy(out_timings, t, sizeof(t));
+        }
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 1;
+    }
+    return 0;
+}
 
 int burst_impl(breeze_generator * gen, const int * ids, int n, int K, const unsigned int * seeds, int * out,
                int width, int * next) {
@@ -77,13 +126,21 @@ breeze_context * breeze_init(const char * gguf_path, int use_gpu) {
     if (!use_gpu) { set_error("this library runs on CUDA devices only; use_gpu=0 has no CPU backend here"); return nullptr; }
     breeze_generator * gen = breeze_generator_init(gguf_path, 0);
     if (!gen) return nullptr;
-    breeze_context * ctx = new breeze_context();
-    ctx->gen = gen;
-    return ctx;
+    try {
+        auto ctx = std::make_unique<breeze_context>();
+        ctx->gen = gen;
+        ctx->voc = std::make_unique<bzb::Vocoder>(gen->eng->gguf(), gen->eng->cfg, gen->device);
+        return ctx.release();
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        breeze_generator_free(gen);
+        return nullptr;
+    }
 }
 
 void breeze_free(breeze_context * ctx) {
     if (!ctx) return;
+    ctx->voc.reset();
     breeze_generator_free(ctx->gen);
     delete ctx;
 }
@@ -93,15 +150,27 @@ int breeze_sample_rate(breeze_context * ctx) {
 }
 
 int breeze_generate(breeze_context * ctx, const breeze_request * req, breeze_audio_cb cb, void * user) {
-    (void) cb; (void) user;
-    if (!ctx || !req || !req->text) { set_error("null context or request"); return 1; }
-    set_error("breeze_generate streams PCM through the vocoder, which this library does not provide yet");
-    return 1;
+    return generate_impl(ctx, req, nullptr, 0, cb, user, nullptr, 0, nullptr, nullptr);
 }
 
 int breeze_generate_wav(breeze_context * ctx, const breeze_request * req, const char * out_path) {
     if (!ctx || !req || !out_path) { set_error("null argument"); return 1; }
-    return breeze_generate(ctx, req, nullptr, nullptr);
+    try {
+        std::vector<float> audio;
+        const bzb::GenRequest g = to_gen_request(req);
+        bzb::generate(*ctx->gen->eng, *ctx->voc, g, [&](const float * s, int n) {
+            audio.insert(audio.end(), s, s + n);
+            return true;
+        });
+        if (!bzb::write_wav(out_path, audio, ctx->gen->eng->cfg.sample_rate)) {
+            set_error("failed to write wav");
+            return 1;
+        }
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 1;
+    }
+    return 0;
 }
 
 const char * breeze_last_error(void) { return g_error.c_str(); }
@@ -597,6 +666,48 @@ int bzb_tokenize(const char * gguf_path, const char * text, int add_bos, int * o
     } catch (const std::exception & e) {
         set_error(e.what());
         return -1;
+    }
+}
+
+int bzb_generate_codes(breeze_context * ctx, const breeze_request * req, const int * ref_codes, int ref_frames,
+                       breeze_audio_cb cb, void * user, int * out_codes, int max_frames, int * out_n_frames,
+                       double * out_timings7) {
+    if (out_codes && max_frames < 0) { set_error("negative max_frames"); return 1; }
+    return generate_impl(ctx, req, ref_codes, ref_frames, cb, user, out_codes, max_frames, out_n_frames, out_timings7);
+}
+
+int bzb_write_wav(const char * path, const float * samples, int n, int sample_rate) {
+    if (!path || n < 0 || (n > 0 && !samples)) { set_error("bad arguments"); return -1; }
+    try {
+        if (!bzb::write_wav(path, std::vector<float>(samples, samples + n), sample_rate)) {
+            set_error("failed to write wav");
+            return -1;
+        }
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_split_text(const char * text, int budget, int first_budget, char * out, int capacity) {
+    if (!text || (capacity > 0 && !out)) return -1;
+    try {
+        const std::vector<std::string> parts = bzb::split_text(text, budget, first_budget);
+        size_t need = 0;
+        for (const std::string & p : parts) need += p.size() + 1;
+        if (out && (size_t) capacity >= need) {
+            char * w = out;
+            for (const std::string & p : parts) {
+                std::memcpy(w, p.data(), p.size());
+                w += p.size();
+                *w++ = '\0';
+            }
+        }
+        return (size_t) capacity >= need ? (int) parts.size() : -(int) need;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return 0;
     }
 }
 

@@ -87,6 +87,22 @@ BREEZE_API int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * t
 BREEZE_API int bzb_gguf_inspect(const char * gguf_path, int * out_hidden, int * out_num_codebooks,
                                 int * out_n_tensors);
 /* tokenizer without a GPU: writes up to max_ids ids, returns the count or -1 */
+/* breeze_generate (include/breeze.h; reference src/c_api.cpp:78-89) with encoded reference codes
+ * (ref_frames x num_codebooks, frame-major; the reference's GenRequest::ref_codes,
+ * src/generation.h:19-22, which breeze_request cannot carry), and with the generated frames
+ * (frame-major, at most max_frames written, the total in *out_n_frames) and the stage timings
+ * out_timings7 = {prefill ms, frame steps ms, vocoder ms, first audio ms, frames, flushes,
+ * pieces}. Every output pointer may be null. Returns 0, or 1 with breeze_last_error(). */
+BREEZE_API int bzb_generate_codes(breeze_context * ctx, const breeze_request * req, const int * ref_codes,
+                                  int ref_frames, breeze_audio_cb cb, void * user, int * out_codes, int max_frames,
+                                  int * out_n_frames, double * out_timings7);
+/* The long-text splitter of breeze_generate (reference src/text_split.cpp:89-111): writes the
+ * pieces NUL-terminated one after another into out and returns their count, or -(bytes needed)
+ * when capacity is too small. */
+/* The WAV writer of breeze_generate_wav (reference src/audio.cpp:80-107): 16-bit mono PCM at
+ * sample_rate. Returns 0, or -1 with breeze_last_error(). */
+BREEZE_API int bzb_write_wav(const char * path, const float * samples, int n, int sample_rate);
+BREEZE_API int bzb_split_text(const char * text, int budget, int first_budget, char * out, int capacity);
 BREEZE_API int bzb_tokenize(const char * gguf_path, const char * text, int add_bos, int * out_ids, int max_ids);
 
 #ifdef __cplusplus

@@ -1213,3 +1213,137 @@ class Vocoder:
             hist = hist[(hist.size // nc - self.MAX_HISTORY) * nc:]
         self.history[sid] = hist
         return out
+
+
+# ----------------------------------------------------------------------------- generate
+# breeze_generate's host logic: the long-text splitter (src/text_split.cpp:6-111) and the
+# streaming flush schedule of src/generation.cpp:137-168.
+
+def _utf8_chars(text: str):
+    """(character, UTF-8 byte length) pairs."""
+    return [(ch, len(ch.encode("utf-8"))) for ch in text]
+
+
+def text_weight(text: str) -> int:
+    """One per single-byte character, three per multi-byte one (src/text_split.cpp:16-24)."""
+    return sum(1 if n == 1 else 3 for _, n in _utf8_chars(text))
+
+
+_CJK_STOPS = {"。", "！", "？", "；", "…", "．"}
+
+
+def split_sentences(t: str):
+    """src/text_split.cpp:32-62: a newline, or . ! ? ; followed (after closing quotes/brackets)
+    by a space, newline or the end, or a full-width stop ends a sentence."""
+    out, cur, i = [], "", 0
+    while i < len(t):
+        ch = t[i]
+        cur += ch
+        i += 1
+        brk = False
+        if len(ch.encode("utf-8")) > 1:
+            brk = ch in _CJK_STOPS
+        elif ch == "\n":
+            brk = True
+        elif ch in ".!?;":
+            j = i
+            while j < len(t) and t[j] in "\"')]":
+                j += 1
+            brk = j >= len(t) or t[j] in " \n"
+            if brk:
+                cur += t[i:j]
+                i = j
+        if brk:
+            out.append(cur)
+            cur = ""
+    if cur:
+        out.append(cur)
+    return out
+
+
+def split_clauses(s: str, budget: int):
+    """src/text_split.cpp:64-87."""
+    if text_weight(s) <= budget:
+        return [s]
+    out, cur, cw, since = [], "", 0, 0
+    for ch, n in _utf8_chars(s):
+        cur += ch
+        w = 1 if n == 1 else 3
+        cw += w
+        since += w
+        comma = ch in (",", "，", "、", ":")
+        space = ch == " "
+        if cw >= budget and (comma or (space and since > budget // 4)):
+            out.append(cur)
+            cur, cw, since = "", 0, 0
+        elif comma or space:
+            since = 0
+    if cur:
+        out.append(cur)
+    return out
+
+
+def split_text(text: str, budget: int, first_budget: int = 0):
+    """src/text_split.cpp:89-111."""
+    if budget <= 0 or text_weight(text) <= budget:
+        return [text]
+    out, cur, cw = [], "", 0
+    limit = first_budget if first_budget > 0 else budget
+    for s in split_sentences(text):
+        for p in split_clauses(s, budget):
+            w = text_weight(p)
+            if cw > 0 and cw + w > limit:
+                out.append(cur)
+                cur, cw = "", 0
+                limit = budget
+            cur += p
+            cw += w
+    if cur:
+        out.append(cur)
+    return out or [text]
+
+
+def stream_chunks(voc: "Vocoder", frames: np.ndarray, chunk_first: int = 4, chunk_max: int = 25, stop_after: int = 0):
+    """PCM chunks that one piece's frames [F, nc] stream through the callback, frames arriving
+    one at a time (src/generation.cpp:137-168): each window decodes up to window + 16 frames of
+    left context and emits only the new frames' samples; chunk sizes ramp c -> c + c//3 + 1."""
+    frames = np.asarray(frames).reshape(-1, voc.m.cfg.nc)
+    spf = Vocoder.SAMPLES_PER_FRAME
+    ctx = voc.c["window"] + 16
+    chunk_max = max(1, chunk_max)
+    chunk = min(max(1, chunk_first), chunk_max)
+    emitted = 0
+    out = []
+
+    def flush(have, final):
+        nonlocal emitted, chunk
+        while have - emitted >= chunk or (final and have > emitted):
+            start = emitted
+            count = have - emitted if final else chunk
+            cs = start - ctx if start > ctx else 0
+            audio = voc.decode(frames[cs:start + count].reshape(-1), start + count - cs)
+            out.append(audio[(start - cs) * spf:(start - cs + count) * spf])
+            if stop_after and len(out) >= stop_after:
+                return False
+            emitted += count
+            chunk = min(chunk + chunk // 3 + 1, chunk_max)
+            if not final and have - emitted < chunk:
+                break
+        return True
+
+    for have in range(1, frames.shape[0] + 1):
+        if not flush(have, False):
+            return out
+    flush(frames.shape[0], True)
+    return out
+
+
+def wav_bytes(samples, sample_rate: int) -> bytes:
+    """16-bit mono PCM WAV (src/audio.cpp:80-107): clamp to [-1, 1], scale by 32767, truncate
+    toward zero, little-endian, 44-byte RIFF header."""
+    import struct
+    x = np.clip(np.asarray(samples, np.float32), -1.0, 1.0)
+    pcm = (x * np.float32(32767.0)).astype(np.float32).astype(np.int16).astype("<i2").tobytes()
+    hdr = b"RIFF" + struct.pack("<I", 36 + len(pcm)) + b"WAVE" + b"fmt " + struct.pack(
+        "<IHHIIHH", 16, 1, 1, sample_rate, sample_rate * 2, 2, 16) + b"data" + struct.pack("<I", len(pcm))
+    return hdr + pcm

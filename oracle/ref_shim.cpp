@@ -2,8 +2,13 @@
 // is compiled unmodified from its sources by `make -C oracle ref`:
 //   breeze::sample_token      sharjeel103/bz-ggml src/sampling.cpp:9-60
 //   breeze::save_voice/load   sharjeel103/bz-ggml src/voice.cpp:16-67
+//   breeze::split_text        sharjeel103/bz-ggml src/text_split.cpp:89-111
+//   breeze::write_wav         sharjeel103/bz-ggml src/audio.cpp:80-107
 // The tests use them to pin the engine's sampler semantics (suppression, repetition penalty,
-// top-k, temperature) and the BRZV voice-file format against the reference itself.
+// top-k, temperature), the BRZV voice-file format, the long-text splitter and the WAV layout
+// against the reference itself.
+#include "breeze/audio.h"
+#include "breeze/generation.h"
 #include "breeze/sampling.h"
 #include "breeze/voice.h"
 
@@ -63,4 +68,22 @@ extern "C" int ref_voice_load(const char * path, char * name, int name_cap, char
     *n_codebooks = v.n_codebooks;
     *sample_rate = v.sample_rate;
     return (int) v.codes.size();
+}
+
+// pieces NUL-terminated one after another; returns the count, or -(bytes needed)
+extern "C" int ref_split_text(const char * text, int budget, int first_budget, char * out, int cap) {
+    const std::vector<std::string> parts = breeze::split_text(text, budget, first_budget);
+    size_t need = 0;
+    for (const std::string & p : parts) need += p.size() + 1;
+    if ((size_t) cap < need) return -(int) need;
+    for (const std::string & p : parts) {
+        std::memcpy(out, p.data(), p.size());
+        out += p.size();
+        *out++ = 0;
+    }
+    return (int) parts.size();
+}
+
+extern "C" int ref_write_wav(const char * path, const float * samples, int n, int sample_rate) {
+    return breeze::write_wav(path, std::vector<float>(samples, samples + n), sample_rate) ? 0 : -1;
 }

@@ -6,11 +6,15 @@ reference checkout is present; the fixtures are committed so that the tests need
   sampler_mt.npz   logits and the token sequences drawn from them by the reference's own C++
                    sampler (src/sampling.cpp:9-60, compiled unmodified into oracle/_ref by
                    `make -C oracle ref`), std::mt19937 seeded per case
+  split_text.json  texts, budgets and the pieces the reference's long-text splitter returns
+                   (src/text_split.cpp:89-111, compiled into oracle/_ref)
+  wav_ref.wav      a WAV the reference's writer (src/audio.cpp:80-107) makes of wav_samples()
 
 usage: python tests/golden/make_golden.py [reference checkout, default /root/reference]
 """
 import ctypes
 import importlib.util
+import json
 import os
 import subprocess
 import sys
@@ -34,6 +38,38 @@ SAMPLER_CASES = [
     ("topp08", 13, 0.7, 0, 0.8, 1.0, [], (2048, 2051), 4000),
     ("greedy", 14, 0.9, 1, 1.0, 1.1, [3, 3], (2048, 2051), 64),
 ]
+
+
+# name, text, budget, first budget
+SPLIT_CASES = [
+    ("short", "Short enough to stay whole.", 600, 200),
+    ("sentences", "One sentence here. Another one follows! Does a third? Yes; a fourth.", 20, 0),
+    ("first_budget", "Alpha beta gamma. Delta epsilon zeta. Eta theta iota. Kappa lambda mu.", 30, 45),
+    ("decimals", "Pi is 3.14 and Dr. Who said \"hi.\" (quietly.) Then left.\nNew line here.", 12, 0),
+    ("clauses", "a long clause, with commas, and colons: and plenty of spaces between the words that go on", 25, 0),
+    ("cjk", "你好。今天天气很好！你呢？我们一起去吧；好的…再见．", 6, 0),
+    ("cjk_commas", "这是一个很长的句子，里面有很多逗号、顿号，还有更多的文字需要分开", 12, 0),
+    ("mixed", "Hello 世界. Mixed text, 中文，and English; together! 结束。", 10, 4),
+    ("no_budget", "Stays whole. Even with stops.", 0, 0),
+    ("empty", "", 10, 0),
+]
+FUZZ_ALPHABET = list("abc de f. ! ? ; , : \n\"')]") + ["你", "好", "。", "！", "，", "、", "…", "．", "é"]
+
+
+def fuzz_split_cases(n=200, seed=7):
+    rng = np.random.default_rng(seed)
+    cases = []
+    for i in range(n):
+        text = "".join(FUZZ_ALPHABET[j] for j in rng.integers(0, len(FUZZ_ALPHABET), int(rng.integers(0, 120))))
+        cases.append((f"fuzz{i}", text, int(rng.choice([0, 5, 10, 17, 40, 600])), int(rng.choice([0, 3, 8, 200]))))
+    return cases
+
+
+def wav_samples():
+    t = np.arange(600, dtype=np.float32)
+    x = (np.sin(t * np.float32(0.05)) * np.float32(1.3)).astype(np.float32)
+    x[:6] = [1.0, -1.0, 0.99999, -0.99999, 2.0, -2.0]
+    return x
 
 
 def voice_codes(frames, ncb, seed):
@@ -69,6 +105,20 @@ def main(ref):
         out[name + "_logits"] = logits
         out[name + "_tokens"] = toks
     np.savez_compressed(os.path.join(HERE, "sampler_mt.npz"), **out)
+
+    split = []
+    for name, text, budget, first in SPLIT_CASES + fuzz_split_cases():
+        raw = text.encode("utf-8")
+        need = -lib.ref_split_text(raw, budget, first, None, 0)
+        buf = ctypes.create_string_buffer(max(need, 1))
+        n = lib.ref_split_text(raw, budget, first, buf, len(buf))
+        pieces = [p.decode("utf-8") for p in buf.raw.split(b"\0")[:n]]
+        split.append(dict(name=name, text=text, budget=budget, first_budget=first, pieces=pieces))
+    with open(os.path.join(HERE, "split_text.json"), "w", encoding="utf-8") as f:
+        json.dump(split, f, ensure_ascii=False, indent=0)
+
+    x = wav_samples()
+    lib.ref_write_wav(os.path.join(HERE, "wav_ref.wav").encode(), x.ctypes.data_as(ctypes.c_void_p), x.size, 24000)
 
 
 if __name__ == "__main__":

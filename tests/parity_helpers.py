@@ -1,0 +1,72 @@
+"""Shared checks of the engine's sampled tokens against the oracle (test infrastructure).
+
+The engine and the oracle draw the same Philox uniforms. Their logits agree within LOGIT_ATOL,
+so a draw may land on different sides of a CDF boundary only when the uniform is within reach of
+one. A differing token is accepted when the sampler, given logits within the tolerance of the
+oracle's, can return it with that uniform. The oracle then follows the engine's token.
+"""
+import numpy as np
+
+import breeze_oracle as bo
+
+LOGIT_ATOL = 2e-2
+TIE_GAP = 1e-3
+
+
+def gain(scale):
+    """How much a guidance combination lu + s (lc - lu) amplifies a logit error."""
+    return abs(1.0 - scale) + abs(scale)
+
+
+def check_depth(ref, nc, sid, engine_codes, dl, scale, tag):
+    """Each engine depth code against the oracle's (combined) logits: a sampled code must be
+    reachable with the same uniform; an argmax code may differ only at a numerical tie. Returns
+    how many codes differ from the oracle's own pick."""
+    sp = ref.sessions[sid].sp
+    us = ref.last_depth_uniforms.get(sid, {})
+    eps = LOGIT_ATOL * gain(scale)
+    flips = 0
+    for j in range(nc - 1):
+        lg = dl[sid][j]
+        code = int(engine_codes[j])
+        if j in us:
+            ok = bo.sample_reachable(lg, sp.dtemp, sp.dtop_k, us[j], code, eps)
+            assert ok, (tag, sid, j, code, bo.sample_margin(lg, sp.dtemp, sp.dtop_k, us[j]))
+            flips += int(code != bo.sample_philox(lg, sp.dtemp, sp.dtop_k, sp.dtop_p, us[j]))
+        elif code != int(np.argmax(lg)):
+            s = np.sort(lg)
+            assert s[-1] - s[-2] < TIE_GAP * gain(scale), (tag, sid, j)
+            flips += 1
+    return flips
+
+
+def reconcile_cb0(ref, sid, engine_next, oracle_next, scale, tag):
+    """Accepts a differing cb0 only within reach of a CDF boundary (or a top-1 tie), then makes
+    the oracle follow the engine's token. Returns 1 for a tolerated difference, 0 for agreement."""
+    if engine_next == oracle_next:
+        return 0
+    pl, key, draw = ref.last_cb0_logits[sid]
+    sp = ref.sessions[sid].sp
+    u = bo.philox_uniform(key, draw)
+    eps = LOGIT_ATOL * gain(scale)
+    ok = engine_next >= 0 and oracle_next >= 0 and bo.sample_reachable(pl, sp.temp, sp.top_k, u, engine_next, eps)
+    assert ok, (tag, sid, engine_next, oracle_next)
+    rs = ref.sessions[sid]
+    rs.hist[int(oracle_next)] -= 1
+    rs.hist[int(engine_next)] = rs.hist.get(int(engine_next), 0) + 1
+    rs.last_cb0 = int(engine_next)
+    rs.active = True
+    return 1
+
+
+def flip_budget(draws):
+    """Tolerated draws that land on the other side of a CDF boundary. Near-flat top-k 50 logits put
+    a boundary every ~2% of the mass, and a 1e-3 logit difference moves each by a few 1e-4, so a
+    few percent of the draws flip."""
+    return max(3, int(0.08 * draws))
+
+
+def snr_db(ref, got):
+    ref = np.asarray(ref, np.float64)
+    err = np.asarray(got, np.float64) - ref
+    return 10.0 * np.log10((ref @ ref + 1e-30) / (err @ err + 1e-30))

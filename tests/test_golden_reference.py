@@ -175,3 +175,44 @@ def test_reference_bindings_bind_this_library(pkg, reference_bindings, tiny_mode
     assert _save_ours(lib.lib, ours, "hi there", codes, 4, 16, 24000) == 0
     v = rb.load_breeze_voice(ours)
     assert v["codes"] == codes.tolist() and v["text"] == "hi there" and v["name"] == "ours"
+
+
+def _split_cases():
+    import json
+    with open(os.path.join(GOLDEN, "split_text.json"), encoding="utf-8") as f:
+        return json.load(f)
+
+
+def test_split_text_matches_reference_fixture(pkg):
+    """The long-text splitter of breeze_generate, the library's (C++) and the oracle's, against
+    the pieces the reference's own src/text_split.cpp returned for the same texts and budgets."""
+    cases = _split_cases()
+    assert len(cases) >= 200
+    for c in cases:
+        assert bo.split_text(c["text"], c["budget"], c["first_budget"]) == c["pieces"], c["name"]
+        assert pkg.split_text(c["text"], c["budget"], c["first_budget"]) == c["pieces"], c["name"]
+
+
+def test_split_text_matches_reference_live(pkg):
+    ref = _ref_lib()
+    rng = np.random.default_rng(2024)
+    for _ in range(500):
+        text = "".join(MG.FUZZ_ALPHABET[j] for j in rng.integers(0, len(MG.FUZZ_ALPHABET), int(rng.integers(0, 200))))
+        budget, first = int(rng.integers(-1, 60)), int(rng.integers(-1, 30))
+        raw = text.encode("utf-8")
+        buf = ctypes.create_string_buffer(-ref.ref_split_text(raw, budget, first, None, 0))
+        n = ref.ref_split_text(raw, budget, first, buf, len(buf))
+        want = [p.decode("utf-8") for p in buf.raw.split(b"\0")[:n]]
+        assert pkg.split_text(text, budget, first) == want, (text, budget, first)
+
+
+def test_wav_writer_matches_reference_fixture(pkg, tmp_path):
+    """breeze_generate_wav's file layout: the library's writer and the oracle's restatement give the
+    bytes the reference's src/audio.cpp wrote for the same samples (clamping and truncation)."""
+    with open(os.path.join(GOLDEN, "wav_ref.wav"), "rb") as f:
+        want = f.read()
+    x = MG.wav_samples()
+    out = tmp_path / "ours.wav"
+    pkg.write_wav(str(out), x, 24000)
+    assert out.read_bytes() == want
+    assert bo.wav_bytes(x, 24000) == want
