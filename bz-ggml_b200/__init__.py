@@ -330,6 +330,16 @@ class GeneratorHandle:
             raise RuntimeError(self.lib.last_error())
         return codes, logits
 
+    def load_q4_depth(self, q4_model_path: str) -> bool:
+        """The Q4_K depth override (dd.* of a second GGUF) for flagged sessions."""
+        if self.lib.lib.breeze_generator_load_q4_depth(self.handle, q4_model_path.encode("utf-8")) != 0:
+            raise RuntimeError(f"Failed to load modular Q4 depth decoder on Generator (device {self.device}): "
+                               f"{self.lib.last_error()}")
+        return True
+
+    def session_set_q4(self, session_id: int, use_q4: bool = True) -> bool:
+        return self.lib.lib.breeze_generator_session_set_q4(self.handle, session_id, 1 if use_q4 else 0) == 0
+
     def debug_gemv(self, tensor: str, x: np.ndarray, out_dim: int, sub: int = -1) -> np.ndarray:
         xx = np.ascontiguousarray(x, np.float32)
         y = np.zeros((xx.shape[0], out_dim), np.float32)

@@ -271,15 +271,19 @@ int breeze_generator_session_free(breeze_generator * gen, int session_id) {
 
 int breeze_generator_load_q4_depth(breeze_generator * gen, const char * q4_gguf_path) {
     if (!gen || !q4_gguf_path) return -1;
-    set_error("the Q4_K depth-decoder override is not supported by this library yet");
-    return -1;
+    try {
+        gen->eng->load_q4_depth(q4_gguf_path);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(std::string("failed to load the Q4 depth decoder: ") + e.what());
+        return -1;
+    }
 }
 
 int breeze_generator_session_set_q4(breeze_generator * gen, int session_id, int use_q4) {
-    (void) use_q4;
     if (!gen) return -1;
     // without a loaded Q4 depth piece the flag resolves to off (src/c_api.cpp:576)
-    return gen->eng->session_exists(session_id) ? 0 : -1;
+    return gen->eng->session_set_q4(session_id, use_q4 != 0) ? 0 : -1;
 }
 
 int breeze_generator_session_count(breeze_generator * gen) { return gen ? gen->eng->session_count() : 0; }

@@ -351,6 +351,7 @@ __device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int 
     int * scode = reinterpret_cast<int *>(sMisc + 8);
     float * sscale = sMisc + 9;
     for (int b = cta; b < R; b += G) {
+        if (p.row_set && p.row_set[b] != p.set_id) continue;  // a row of the other weight set's pass
         if (!p.row_active[b]) {
             if (tid == 0) p.frames[(size_t) b * nc + j] = -1;
             continue;
@@ -422,13 +423,14 @@ __device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int 
             const size_t row = (size_t) j * V + next;
             const int8_t * q = p.embd.qs + row * p.embd.K;
             const half * d = p.embd.ds + row * (p.embd.K / 32);
+            const half * mn = p.embd.ms ? p.embd.ms + row * (p.embd.K / 32) : nullptr;
             for (int c = tid; c < p.embd.K / 8; c += kEpiThreads) {
                 const uint2 u = *reinterpret_cast<const uint2 *>(q + c * 8);
-                const float sc = __half2float(d[c >> 2]);
+                const float sc = __half2float(d[c >> 2]), m = mn ? __half2float(mn[c >> 2]) : 0.0f;
                 const int8_t * bq = reinterpret_cast<const int8_t *>(&u);
                 half2 o[4];
 #pragma unroll
-                for (int k = 0; k < 4; k++) o[k] = __floats2half2_rn((float) bq[2 * k] * sc, (float) bq[2 * k + 1] * sc);
+                for (int k = 0; k < 4; k++) o[k] = __floats2half2_rn((float) bq[2 * k] * sc - m, (float) bq[2 * k + 1] * sc - m);
                 __stcg(reinterpret_cast<uint4 *>(p.din16 + (size_t) b * p.H + c * 8), *reinterpret_cast<uint4 *>(o));
             }
         }
@@ -591,10 +593,20 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     if (within == 0) ok = dwait(&raw_full[rs], (rg / kRawGroups) & 1u, err, kBackoff);
                     if (!ok) break;
                     if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
-                    const uint8_t * raw = sR + rs * kRawGroupBytes + within * kUChunkBytes;
-                    const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
-                    const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
-                    const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
+                    const uint8_t * raw = sR + rs * kRawGroupBytes + within * umat_chunk_bytes(ph.q4);
+                    uint4 q0, q1;
+                    half sc, mn = __float2half_rn(0.0f);
+                    if (ph.q4) {
+                        // one 32-value Q4_K sub-block: 16 bytes of nibbles, its scale and min
+                        q0 = *reinterpret_cast<const uint4 *>(raw + (hb * kTileM + r) * 16);
+                        q1 = q0;
+                        sc = *reinterpret_cast<const half *>(raw + kTileM * 32 + (hb * kTileM + r) * 2);
+                        mn = *reinterpret_cast<const half *>(raw + kTileM * 32 + 2 * kTileM * 2 + (hb * kTileM + r) * 2);
+                    } else {
+                        q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
+                        q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
+                        sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
+                    }
                     if (within == gs - 1) {
                         __syncwarp();  // the whole warp has read the group
                         if (lane == 0) mbar_arrive(&raw_empty[rs]);
@@ -603,15 +615,27 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     if (ac >= kAStages) ok = dwait(&a_empty[ab], ((ac / kAStages) - 1) & 1u, err, kBackoff);
                     if (!ok) break;
                     const half2 s2 = __halves2half2(sc, sc);
-                    const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
                     uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+                    if (ph.q4) {
+                        const half2 nb2 = __hneg2(__halves2half2(mn, mn));
+                        const uint32_t w4[4] = { q0.x, q0.y, q0.z, q0.w };
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        uint4 o;
-                        dq4(w8[2 * q], s2, o.x, o.y);
-                        dq4(w8[2 * q + 1], s2, o.z, o.w);
-                        const int jj = hb * 4 + q;
-                        *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
+                        for (int q = 0; q < 4; q++) {
+                            uint32_t o[4];
+                            dq8_nib(w4[q], s2, nb2, o);
+                            const int jj = hb * 4 + q;
+                            *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
+                    } else {
+                        const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            uint4 o;
+                            dq4(w8[2 * q], s2, o.x, o.y);
+                            dq4(w8[2 * q + 1], s2, o.z, o.w);
+                            const int jj = hb * 4 + q;
+                            *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
+                        }
                     }
                     fence_proxy_async();
                     __syncwarp();
@@ -683,15 +707,16 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                 if (ph.type != DP_GEMM) continue;
                 for (int u = unit_of(i, cta, G); u < ph.n_units && ok; u += G) {
                     const UnitRange ur = unit_range(ph, u);
-                    const uint8_t * base = ph.blk + (size_t) (ur.tile * ph.KC + ur.c0) * kUChunkBytes;
+                    const int cb = umat_chunk_bytes(ph.q4);
+                    const uint8_t * base = ph.blk + (size_t) (ur.tile * ph.KC + ur.c0) * cb;
                     for (int g0 = 0; g0 < ur.nch; g0 += kDpGroup, rg++) {
                         const int gs = min(kDpGroup, ur.nch - g0);
                         const int rs = rg % kRawGroups;
                         if (rg >= kRawGroups) ok = dwait(&raw_empty[rs], ((rg / kRawGroups) - 1) & 1u, err, kBackoff);
                         if (!ok) break;
                         if (p.trace && g0 == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 7] = gtimer();
-                        mbar_expect_tx(&raw_full[rs], (uint32_t) gs * kUChunkBytes);
-                        bulk_g2s(sR + rs * kRawGroupBytes, base + (size_t) g0 * kUChunkBytes, (uint32_t) gs * kUChunkBytes, &raw_full[rs]);
+                        mbar_expect_tx(&raw_full[rs], (uint32_t) (gs * cb));
+                        bulk_g2s(sR + rs * kRawGroupBytes, base + (size_t) g0 * cb, (uint32_t) (gs * cb), &raw_full[rs]);
                     }
                 }
             }

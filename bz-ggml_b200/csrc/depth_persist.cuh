@@ -18,6 +18,7 @@ constexpr int kDpTraceSlots = 57;  // 9 phase events + 3 x 16 per-chunk events
 // ... where c' is c rotated by the phase index.
 struct alignas(16) DpPhase {
     int type = DP_GEMM;
+    int q4 = 0;                     // GEMM weight chunk format (UMat::q4)
     // GEMM
     const uint8_t * blk = nullptr;  // tcgen05 layout (UMat::blk)
     int MT = 0, KC = 0, M = 0, splits = 1, kc_per = 0, n_units = 0;
@@ -62,6 +63,8 @@ struct DpParams {
     half * din16 = nullptr;             // in_proj input [2R][H]
     QRows embd;                         // audio embedding table
     const int * row_active = nullptr;   // [R]
+    const int * row_set = nullptr;      // [R] depth weight set of each row, or null (all rows)
+    int set_id = 0;                     // the set this launch's weights are; other rows are left alone
     int * frames = nullptr;             // [R][nc]
     const int * forced = nullptr;       // [R][nc-1] teacher-forced codes, or null
     float * logits_out = nullptr;       // [R][nc-1][vs] or null

@@ -27,6 +27,8 @@ namespace bzb {
 
 namespace {
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
+// stored bytes of a quantised matrix: Q8_0 34 per 32 weights, Q4_K 144 per 256
+size_t qmat_bytes(const QMat & q) { return q.u.q4 ? (size_t) q.M * q.K / 256 * 144 : (size_t) q.M * q.K / 32 * 34; }
 
 std::vector<float> llama3_freq_factors(const DdConfig & c) {
     // src/depth_decoder.cpp:10-29
@@ -74,19 +76,23 @@ template <class T> T * Engine::dalloc(size_t n) {
 }
 
 const GgufTensor * Engine::need(const std::string & name) {
-    const GgufTensor * t = gg_.find(name);
+    const GgufTensor * t = src().find(name);
     if (!t) throw std::runtime_error("missing tensor: " + name);
     return t;
 }
 
 QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool interleave_pairs, int row0, int rows) {
     const int K = (int) parts[0]->ne[0];
+    const bool q4 = parts[0]->type == GT_Q4_K;
     for (auto * t : parts) {
-        if (t->type != GT_Q8_0) throw std::runtime_error(t->name + ": only Q8_0 linear weights are supported by this engine");
+        if (t->type != GT_Q8_0 && t->type != GT_Q4_K)
+            throw std::runtime_error(t->name + ": linear weights must be Q8_0 or Q4_K");
+        if (t->type != parts[0]->type) throw std::runtime_error(t->name + ": quantisation differs from its fused partner");
         if (t->ne[0] != K) throw std::runtime_error(t->name + ": row length differs from its fused partner");
     }
+    if (q4 && K % 256) throw std::runtime_error(parts[0]->name + ": Q4_K rows need a length that is a multiple of 256");
     const int KB = K / 32;
-    const size_t row_bytes = (size_t) KB * 34;
+    const size_t row_bytes = q4 ? (size_t) (K / 256) * 144 : (size_t) KB * 34;
     std::vector<const uint8_t *> src_rows;
     if (interleave_pairs) {
         const int F = (int) parts[0]->rows();
@@ -95,14 +101,14 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
         for (int p = 0; p < 2 * F; p++) {
             const int tile = p / 16, r = p % 16;
             const GgufTensor * t = r < 8 ? parts[0] : parts[1];
-            const int src = tile * 8 + (r & 7);
-            src_rows[p] = gg_.data(*t) + (size_t) src * row_bytes;
+            const int srow = tile * 8 + (r & 7);
+            src_rows[p] = src().data(*t) + (size_t) srow * row_bytes;
         }
     } else if (rows >= 0) {
-        for (int r = 0; r < rows; r++) src_rows.push_back(gg_.data(*parts[0]) + (size_t) (row0 + r) * row_bytes);
+        for (int r = 0; r < rows; r++) src_rows.push_back(src().data(*parts[0]) + (size_t) (row0 + r) * row_bytes);
     } else {
         for (auto * t : parts)
-            for (int64_t r = 0; r < t->rows(); r++) src_rows.push_back(gg_.data(*t) + (size_t) r * row_bytes);
+            for (int64_t r = 0; r < t->rows(); r++) src_rows.push_back(src().data(*t) + (size_t) r * row_bytes);
     }
     const int M = (int) src_rows.size();
     std::vector<uint8_t> raw((size_t) M * row_bytes);
@@ -115,11 +121,14 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
     q.MT = (M + 15) / 16;
     q.K = K;
     q.KB = KB;
-    uint4 * qs = dalloc<uint4>((size_t) q.MT * KB * 32);
-    half2 * ds = dalloc<half2>((size_t) q.MT * KB * 8);
-    repack_q8(raw_dev, M, K, qs, ds, stream_);
-    q.qs = qs;
-    q.ds = ds;
+    if (!q4) {
+        // the mma.sync layout serves Q8_0 only; Q4_K matrices run on the tcgen05 path alone
+        uint4 * qs = dalloc<uint4>((size_t) q.MT * KB * 32);
+        half2 * ds = dalloc<half2>((size_t) q.MT * KB * 8);
+        repack_q8(raw_dev, M, K, qs, ds, stream_);
+        q.qs = qs;
+        q.ds = ds;
+    }
     if (K % 64 == 0) {
         // the tcgen05 layout pairs gate/up rows in 16-row groups instead of 8
         if (interleave_pairs) {
@@ -127,7 +136,7 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
             for (int p = 0; p < M; p++) {
                 const int grp = p / 32, r = p % 32;
                 const GgufTensor * t = r < 16 ? parts[0] : parts[1];
-                std::memcpy(raw.data() + (size_t) p * row_bytes, gg_.data(*t) + (size_t) (grp * 16 + (r & 15)) * row_bytes, row_bytes);
+                std::memcpy(raw.data() + (size_t) p * row_bytes, src().data(*t) + (size_t) (grp * 16 + (r & 15)) * row_bytes, row_bytes);
             }
             if (F % 16) throw std::runtime_error("gate/up rows must be a multiple of 16");
             CK(cudaStreamSynchronize(stream_));
@@ -138,8 +147,10 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
         u.MT = (M + 127) / 128;
         u.K = K;
         u.KC = K / 64;
-        uint8_t * ub = dalloc<uint8_t>((size_t) u.MT * u.KC * kUChunkBytes);
-        repack_umma(raw_dev, M, K, ub, stream_);
+        u.q4 = q4 ? 1 : 0;
+        uint8_t * ub = dalloc<uint8_t>((size_t) u.MT * u.KC * umat_chunk_bytes(u.q4));
+        if (q4) repack_umma_q4k(raw_dev, M, K, ub, stream_);
+        else repack_umma(raw_dev, M, K, ub, stream_);
         u.blk = ub;
         q.u = u;
     }
@@ -149,16 +160,22 @@ QMat Engine::load_qmat(const std::vector<const GgufTensor *> & parts, bool inter
 }
 
 QRows Engine::load_qrows(const GgufTensor * t) {
-    if (t->type != GT_Q8_0) throw std::runtime_error(t->name + ": embedding tables must be Q8_0");
+    if (t->type != GT_Q8_0 && t->type != GT_Q4_K) throw std::runtime_error(t->name + ": embedding tables must be Q8_0 or Q4_K");
     QRows e;
     e.K = (int) t->ne[0];
     e.rows = (int) t->rows();
     uint8_t * raw_dev = nullptr;
     CK(cudaMalloc(&raw_dev, t->nbytes));
-    CK(cudaMemcpyAsync(raw_dev, gg_.data(*t), t->nbytes, cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(raw_dev, src().data(*t), t->nbytes, cudaMemcpyHostToDevice, stream_));
     int8_t * qs = dalloc<int8_t>((size_t) e.rows * e.K);
     half * ds = dalloc<half>((size_t) e.rows * (e.K / 32));
-    split_q8_rows(raw_dev, e.rows, e.K, qs, ds, stream_);
+    if (t->type == GT_Q4_K) {
+        half * ms = dalloc<half>((size_t) e.rows * (e.K / 32));
+        split_q4k_rows(raw_dev, e.rows, e.K, qs, ds, ms, stream_);
+        e.ms = ms;
+    } else {
+        split_q8_rows(raw_dev, e.rows, e.K, qs, ds, stream_);
+    }
     CK(cudaStreamSynchronize(stream_));
     CK(cudaFree(raw_dev));
     e.qs = qs;
@@ -171,7 +188,7 @@ float * Engine::load_f32(const std::string & name, int expect) {
     if (t->type != GT_F32 || t->nelem() != expect)
         throw std::runtime_error(name + ": expected an F32 vector of " + std::to_string(expect));
     float * d = dalloc<float>(expect);
-    CK(cudaMemcpyAsync(d, gg_.data(*t), (size_t) expect * 4, cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(d, src().data(*t), (size_t) expect * 4, cudaMemcpyHostToDevice, stream_));
     return d;
 }
 
@@ -218,23 +235,7 @@ Engine::Engine(const std::string & path, int dev) : device(dev) {
     vbb_ = lm_head_.M;
     if (vbb_ > 4096) throw std::runtime_error("lm_head wider than the sampler's 4096 entries");
 
-    // depth decoder
-    const DdConfig & dd = cfg.dd;
-    dd_in_ = load_qmat({ need("dd.in_proj.weight") }, false);
-    for (int l = 0; l < dd.n_layer; l++) {
-        const std::string p = "dd.blk." + std::to_string(l);
-        LayerW w;
-        w.qkv = load_qmat({ need(p + ".attn_q.weight"), need(p + ".attn_k.weight"), need(p + ".attn_v.weight") }, false);
-        w.o = load_qmat({ need(p + ".attn_output.weight") }, false);
-        w.gu = load_qmat({ need(p + ".ffn_gate.weight"), need(p + ".ffn_up.weight") }, true);
-        w.down = load_qmat({ need(p + ".ffn_down.weight") }, false);
-        w.attn_norm = load_f32(p + ".attn_norm.weight", dd.hidden);
-        w.ffn_norm = load_f32(p + ".ffn_norm.weight", dd.hidden);
-        dd_.push_back(w);
-    }
-    dd_out_norm_ = load_f32("dd.output_norm.weight", dd.hidden);
-    const GgufTensor * head = need("dd.codebooks_head.weight");
-    for (int j = 0; j < nc - 1; j++) dd_head_.push_back(load_qmat({ head }, false, j * vs, vs));
+    load_depth_weights();
     audio_embd_ = load_qrows(need("audio_embd.weight"));
 
     // text encoder (prefill)
@@ -265,12 +266,107 @@ Engine::Engine(const std::string & path, int dev) : device(dev) {
     CK(cudaStreamSynchronize(stream_));
 }
 
+// the dd.* tensors of the current source file into the current depth set (the reference's
+// depth decoder weights, src/depth_decoder.cpp:48-85, 119-125)
+void Engine::load_depth_weights() {
+    const DdConfig & dd = cfg.dd;
+    const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs;
+    check_shape(*need("dd.in_proj.weight"), H, dd.hidden);
+    check_shape(*need("dd.codebooks_head.weight"), dd.hidden, vs, nc - 1);
+    dd_.clear();
+    dd_head_.clear();
+    dd_in_ = load_qmat({ need("dd.in_proj.weight") }, false);
+    for (int l = 0; l < dd.n_layer; l++) {
+        const std::string p = "dd.blk." + std::to_string(l);
+        LayerW w;
+        w.qkv = load_qmat({ need(p + ".attn_q.weight"), need(p + ".attn_k.weight"), need(p + ".attn_v.weight") }, false);
+        w.o = load_qmat({ need(p + ".attn_output.weight") }, false);
+        w.gu = load_qmat({ need(p + ".ffn_gate.weight"), need(p + ".ffn_up.weight") }, true);
+        w.down = load_qmat({ need(p + ".ffn_down.weight") }, false);
+        w.attn_norm = load_f32(p + ".attn_norm.weight", dd.hidden);
+        w.ffn_norm = load_f32(p + ".ffn_norm.weight", dd.hidden);
+        if (w.qkv.M != (dd.n_head + 2 * dd.n_kv) * dd.hd || w.qkv.K != dd.hidden || w.gu.M != 2 * dd.ffn)
+            throw std::runtime_error(p + ": depth shapes do not match the model's config");
+        dd_.push_back(w);
+    }
+    dd_out_norm_ = load_f32("dd.output_norm.weight", dd.hidden);
+    const GgufTensor * head = need("dd.codebooks_head.weight");
+    for (int j = 0; j < nc - 1; j++) dd_head_.push_back(load_qmat({ head }, false, j * vs, vs));
+}
+
+void Engine::swap_depth_sets() {
+    std::swap(dd_, q4_dd_);
+    std::swap(dd_in_, q4_dd_in_);
+    std::swap(dd_head_, q4_dd_head_);
+    std::swap(dd_out_norm_, q4_dd_out_norm_);
+    cur_set_ ^= 1;
+}
+
+void Engine::load_q4_depth(const std::string & path) {
+    auto file = std::make_unique<GgufFile>();
+    std::string err;
+    if (!file->open(path, err)) throw std::runtime_error(err);
+    CK(cudaStreamSynchronize(stream_));
+    // the previous override, its graphs and its depth schedules go first
+    for (auto it = graphs_.begin(); it != graphs_.end();) {
+        if (it->first.second & kFlagQ4) {
+            cudaGraphExecDestroy(it->second);
+            cudaGraphDestroy(graph_defs_[it->first]);
+            graph_defs_.erase(it->first);
+            it = graphs_.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    for (auto it = dp_plans_.begin(); it != dp_plans_.end();) {
+        if (it->first >> 16) {
+            cudaFree(it->second.dev);
+            it = dp_plans_.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    for (void * p : q4_allocs_) cudaFree(p);
+    q4_allocs_.clear();
+    has_q4_ = false;
+    const size_t mark = allocs_.size();
+    src_ = file.get();
+    swap_depth_sets();
+    try {
+        load_depth_weights();
+    } catch (...) {
+        swap_depth_sets();
+        src_ = nullptr;
+        q4_allocs_.assign(allocs_.begin() + mark, allocs_.end());
+        allocs_.resize(mark);
+        throw;
+    }
+    swap_depth_sets();
+    src_ = nullptr;
+    CK(cudaStreamSynchronize(stream_));
+    q4_allocs_.assign(allocs_.begin() + mark, allocs_.end());
+    allocs_.resize(mark);
+    q4_gg_ = std::move(file);
+    has_q4_ = true;
+}
+
+bool Engine::session_set_q4(int sid, bool on) {
+    auto it = sid_to_slot_.find(sid);
+    if (it == sid_to_slot_.end()) return false;
+    SlotHost & s = slots_[it->second];
+    s.use_q4 = on && has_q4_;  // src/c_api.cpp:576: the flag resolves to off without a loaded override
+    if (s.partner >= 0) slots_[s.partner].use_q4 = s.use_q4;
+    return true;
+}
+
 Engine::~Engine() {
     cudaSetDevice(device);
     if (stream_) cudaStreamSynchronize(stream_);
     for (auto & kv : graphs_) cudaGraphExecDestroy(kv.second);
     for (auto & kv : graph_defs_) cudaGraphDestroy(kv.second);
     for (void * p : prefill_allocs_) cudaFree(p);
+    for (void * p : q4_allocs_) cudaFree(p);
+    for (auto & kv : dp_plans_) cudaFree(kv.second.dev);
     for (void * p : allocs_) cudaFree(p);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -332,6 +428,7 @@ void Engine::alloc_buffers() {
     seeds_ = dalloc<uint32_t>(rmax_);
     dseeds_ = dalloc<uint32_t>(rmax_);
     row_pair_ = dalloc<int>(rmax_);
+    row_set_ = dalloc<int>(rmax_);
     create_rows_ = dalloc<int>(4);
     cur_frames_ = dalloc<int>((size_t) rmax_ * nc);
     frames_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
@@ -406,8 +503,9 @@ void Engine::ensure_prefill_capacity(int T) {
 
 // ------------------------------------------------------------------------------------ step
 void Engine::launch_gemm(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
-    if (use_umma_ && w.u.blk && ldx % 8 == 0) launch_umma_gemm(w.u, x16, ldx, rows, out, err_, stream_, pdl_scope());
-    else launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+    if (w.u.blk && (use_umma_ || !w.qs) && ldx % 8 == 0) launch_umma_gemm(w.u, x16, ldx, rows, out, err_, stream_, pdl_scope());
+    else if (w.qs) launch_gemv(w, x16, ldx, rows, out, scr_, stream_);
+    else throw std::runtime_error("Q4_K matrices need activation rows with a stride that is a multiple of 8");
 }
 
 void Engine::gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
@@ -420,7 +518,7 @@ void Engine::gemv(const QMat & w, const half * x16, int ldx, int rows, const Gem
     CK(cudaEventCreate(&r.a));
     CK(cudaEventCreate(&r.b));
     const double out_bytes = (double) rows * (out.kind == EPI_STORE || out.kind == EPI_RESID ? w.M * 4.0 : w.M);
-    r.bytes = (double) w.M * w.K / 32.0 * 34.0 + (double) rows * w.K * 2.0 + out_bytes;
+    r.bytes = (double) qmat_bytes(w) + (double) rows * w.K * 2.0 + out_bytes;
     CK(cudaEventRecord(r.a, stream_));
     launch_gemm(w, x16, ldx, rows, out);
     CK(cudaEventRecord(r.b, stream_));
@@ -483,7 +581,9 @@ bool Engine::dp_supported(int R) const {
 
 const Engine::DpPlan * Engine::depth_plan(int R) {
     if (!dp_supported(R)) return nullptr;
-    auto it = dp_plans_.find(R);
+    // one schedule per batch size and depth weight set (the set's weight pointers are in it)
+    const int key = R | (cur_set_ << 16);
+    auto it = dp_plans_.find(key);
     if (it != dp_plans_.end()) return &it->second;
     const DdConfig & dd = cfg.dd;
     const int D = dd.hidden, H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, G = dp_grid_;
@@ -496,7 +596,7 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     auto gemm = [&](const UMat & w, int map, int b_row0, int rows, int epi, int out_ld, int max_splits = 16) {
         DpPhase q;
         q.type = DP_GEMM;
-        q.blk = w.blk; q.MT = w.MT; q.KC = w.KC; q.M = w.M;
+        q.blk = w.blk; q.q4 = w.q4; q.MT = w.MT; q.KC = w.KC; q.M = w.M;
         q.row_chunks = (rows + 63) / 64;
         q.nb = std::min(64, round_up(rows, 16));
         int S = epi == DPE_PARTIAL ? std::max(1, std::min(max_splits, std::min(w.KC, G / (w.MT * q.row_chunks)))) : 1;
@@ -540,7 +640,7 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     }
     DpPlan plan;
     plan.n = (int) ph.size();
-    plan.dev = dalloc<DpPhase>(ph.size());
+    CK(cudaMalloc(&plan.dev, ph.size() * sizeof(DpPhase)));
     CK(cudaMemcpyAsync(plan.dev, ph.data(), ph.size() * sizeof(DpPhase), cudaMemcpyHostToDevice, stream_));
     CK(cudaStreamSynchronize(stream_));
     plan.maps.m[0] = make_x_group_map(din16_, H, H, 2 * R, NB2, kDpGroup);
@@ -551,7 +651,7 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     plan.maps.m[5] = make_x_group_map(datt16_, D, D, 2 * R, NB1, kDpGroup);
     plan.maps.m[6] = make_x_group_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB2, kDpGroup);
     plan.maps.m[7] = make_x_group_map(dff16_, dd.ffn, dd.ffn, 2 * R, NB1, kDpGroup);
-    return &(dp_plans_[R] = plan);
+    return &(dp_plans_[key] = plan);
 }
 
 int Engine::depth_trace(double * out, int max_phases) {
@@ -585,7 +685,8 @@ int Engine::depth_trace(double * out, int max_phases) {
     return (int) total;
 }
 
-void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace) {
+void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace,
+                           const int * row_set) {
     const DpPlan * pl = depth_plan(R);
     if (!pl) throw std::runtime_error("persistent depth decoder: unsupported batch");
     const DdConfig & dd = cfg.dd;
@@ -599,6 +700,7 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     p.P = dp_P_; p.x = dx_; p.h16 = dh16_; p.ss = dp_ss_; p.att16 = datt16_; p.g16 = dff16_; p.din16 = din16_;
     p.embd = audio_embd_;
     p.row_active = row_active_; p.frames = cur_frames_;
+    p.row_set = row_set; p.set_id = cur_set_;
     p.forced = forced_dev; p.logits_out = logits_dev;
     p.bar = dp_bar_; p.err = err_; p.trace = trace;
     if (prof_) {
@@ -611,44 +713,71 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     launches_ += 2;
 }
 
-void Engine::enqueue_step(int R, int flags) {
+// all nc-1 depth sub-steps of the current batch with weight set `set` (0 the model's, 1 the
+// Q4_K override); with kFlagQ4 only the rows of that set receive codes
+void Engine::depth_pass(int R, int flags, int set, const StepArgs & sa_in) {
     const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, D = cfg.dd.hidden;
+    const bool masked = (flags & kFlagQ4) != 0;
+    if (set == 1 && !has_q4_) throw std::runtime_error("no Q4_K depth override is loaded");
+    if (set != cur_set_) swap_depth_sets();
+    StepArgs sa = sa_in;
+    sa.row_set = masked ? row_set_ : nullptr;
+    sa.set_id = set;
+    const bool sampled = (flags & kFlagSampled) != 0;
+    try {
+        // code j of every row from the depth logits; gather_cb >= 0 stages the next sub-step's input
+        auto pick = [&](int j, int gather_cb) {
+            if (!sampled) {
+                launch_argmax_gather(sa, dlog_, vs, vs, j, gather_cb, stream_);
+                return;
+            }
+            DepthSampleArgs da;
+            da.s = sa; da.logits = dlog_; da.ld = vs; da.V = vs; da.col = j; da.gather_cb = gather_cb;
+            da.row_pair = row_pair_;
+            da.seeds = (flags & kFlagSeeds) ? seeds_ : nullptr;
+            da.dseeds = (flags & kFlagDepthSeeds) ? dseeds_ : nullptr;
+            launch_depth_sample_gather(da, stream_);
+        };
+        if (!sampled && dp_supported(R)) {
+            // all nc-1 depth sub-steps in one persistent launch
+            enqueue_depth(R, nullptr, nullptr, nullptr, sa.row_set);
+        } else {
+            // depth sub-step 1: position 0 = backbone hidden, position 1 = cb0 embedding
+            gemv(dd_in_, din16_, H, 2 * R, GemvOut{ EPI_STORE, dx_, nullptr, D });
+            for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, 2 * R, R, 2, 0);
+            launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, R, R, nullptr, stream_);
+            gemv(dd_head_[0], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+            pick(1, nc > 2 ? 1 : -1);
+            for (int j = 2; j < nc; j++) {
+                gemv(dd_in_, din16_, H, R, GemvOut{ EPI_STORE, dx_, nullptr, D });
+                for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, R, R, 1, j);
+                launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, 0, R, nullptr, stream_);
+                gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
+                pick(j, j + 1 < nc ? j : -1);
+            }
+        }
+    } catch (...) {
+        if (cur_set_ != 0) swap_depth_sets();
+        throw;
+    }
+    if (cur_set_ != 0) swap_depth_sets();
+}
+
+void Engine::enqueue_step(int R, int flags) {
+    const int H = cfg.hidden, nc = cfg.nc, vs = cfg.vs;
     StepArgs sa;
     sa.R = R; sa.nc = nc; sa.vs = vs; sa.H = H;
     sa.row_slot = row_slot_; sa.row_active = row_active_; sa.st = st_; sa.hid32 = hid32_; sa.embd = audio_embd_;
     sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
     launch_step_init(sa, stream_);
-    const bool sampled = (flags & kFlagSampled) != 0;
-    // code j of every row from the depth logits; gather_cb >= 0 stages the next sub-step's input
-    auto pick = [&](int j, int gather_cb) {
-        if (!sampled) {
-            launch_argmax_gather(sa, dlog_, vs, vs, j, gather_cb, stream_);
-            return;
-        }
-        DepthSampleArgs da;
-        da.s = sa; da.logits = dlog_; da.ld = vs; da.V = vs; da.col = j; da.gather_cb = gather_cb;
-        da.row_pair = row_pair_;
-        da.seeds = (flags & kFlagSeeds) ? seeds_ : nullptr;
-        da.dseeds = (flags & kFlagDepthSeeds) ? dseeds_ : nullptr;
-        launch_depth_sample_gather(da, stream_);
-    };
-    if (!sampled && dp_supported(R)) {
-        // all nc-1 depth sub-steps in one persistent launch
-        enqueue_depth(R, nullptr, nullptr);
+    if (flags & kFlagQ4) {
+        // the rows of each depth weight set take their codes from their own pass; the second
+        // pass starts again from the backbone hidden and cb0 embedding rows
+        depth_pass(R, flags, 0, sa);
+        launch_step_init(sa, stream_);
+        depth_pass(R, flags, 1, sa);
     } else {
-        // depth sub-step 1: position 0 = backbone hidden, position 1 = cb0 embedding
-        gemv(dd_in_, din16_, H, 2 * R, GemvOut{ EPI_STORE, dx_, nullptr, D });
-        for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, 2 * R, R, 2, 0);
-        launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, R, R, nullptr, stream_);
-        gemv(dd_head_[0], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
-        pick(1, nc > 2 ? 1 : -1);
-        for (int j = 2; j < nc; j++) {
-            gemv(dd_in_, din16_, H, R, GemvOut{ EPI_STORE, dx_, nullptr, D });
-            for (int l = 0; l < cfg.dd.n_layer; l++) depth_layer(l, R, R, 1, j);
-            launch_rmsnorm(dx_, D, dd_out_norm_, D, cfg.dd.eps, dh16_, D, nullptr, 0, 0, R, nullptr, stream_);
-            gemv(dd_head_[j - 1], dh16_, D, R, GemvOut{ EPI_STORE, dlog_, nullptr, vs });
-            pick(j, j + 1 < nc ? j : -1);
-        }
+        depth_pass(R, flags, 0, sa);
     }
     // backbone: one token per session over its own paged cache
     launch_audio_embed(audio_embd_, cur_frames_, nc, nc, vs, R, bx_, row_active_, stream_);
@@ -671,7 +800,20 @@ cudaGraphExec_t Engine::graph_for(int R, int flags) {
     auto it = graphs_.find(key);
     if (it != graphs_.end()) return it->second;
     cudaGraph_t g = nullptr;
-    if (!(flags & kFlagSampled)) depth_plan(R);  // uploads the persistent schedule outside the capture
+    if (!(flags & kFlagSampled)) {
+        // the persistent schedules (one per depth weight set) are uploaded outside the capture
+        depth_plan(R);
+        if (flags & kFlagQ4) {
+            swap_depth_sets();
+            try {
+                depth_plan(R);
+            } catch (...) {
+                swap_depth_sets();
+                throw;
+            }
+            swap_depth_sets();
+        }
+    }
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     set_pdl_scope(true);
     try {
@@ -736,13 +878,19 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     if (!sampled && sampled_depth)
         for (int i = 0; i < n; i++)
             if (rs[i] >= 0 && slots_[rs[i]].dtop_k != 1) sampled = true;
+    // rows whose sessions take their depth codes from the Q4_K override (src/c_api.cpp:622-650)
+    std::vector<int> rset(R, 0);
+    bool any_q4 = false;
+    for (int r = 0; r < R; r++)
+        if (rs[r] >= 0 && slots_[rs[r]].use_q4) rset[r] = 1, any_q4 = true;
     const int flags = (seeds ? kFlagSeeds : 0) | (sampled ? kFlagSampled : 0) |
-                      (sampled && depth_seeds && !seeds ? kFlagDepthSeeds : 0);
+                      (sampled && depth_seeds && !seeds ? kFlagDepthSeeds : 0) | (any_q4 ? kFlagQ4 : 0);
     cudaGraphExec_t g = graph_for(R, flags);
     cur_R_ = R;
     cur_flags_ = flags;
     CK(cudaMemcpyAsync(row_slot_, rs.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
     CK(cudaMemcpyAsync(row_pair_, rp.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    if (any_q4) CK(cudaMemcpyAsync(row_set_, rset.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
     if (seeds) {
         std::vector<uint32_t> sd(R, 0);
         for (int i = 0; i < n; i++) sd[i] = seeds[i];
@@ -1221,7 +1369,7 @@ void Engine::profile_step(double * out) {
 size_t Engine::depth_bytes_per_step() const {
     // algorithmic bytes of the depth decode of one frame step: the Q8_0 depth weights, re-read by
     // every sub-step (in_proj, the 4 layers and that sub-step's head)
-    auto qbytes = [](const QMat & q) { return (size_t) q.M * q.K / 32 * 34; };
+    auto qbytes = [](const QMat & q) { return qmat_bytes(q); };
     size_t dd = qbytes(dd_in_) + qbytes(dd_head_[0]);
     for (const LayerW & w : dd_) dd += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
     return (size_t) (cfg.nc - 1) * dd;
@@ -1275,6 +1423,7 @@ void Engine::gemm_noalloc(const char * tensor, int rows, const half * x16, int l
         throw std::runtime_error("gemm_noalloc: not a resident unfused matrix (bb.lm_head, dd.in_proj, "
                                  "{bb,dd}.blk.N.attn_output or ffn_down): " + std::string(tensor));
     if (!x16 || !y) throw std::runtime_error("gemm_noalloc: null device buffer");
+    if (!w->qs) throw std::runtime_error("gemm_noalloc: the allocation-free GEMV serves Q8_0 matrices only");
     if (ldx < w->K || (ldx & 1) || (reinterpret_cast<uintptr_t>(x16) & 3) || (reinterpret_cast<uintptr_t>(y) & 3))
         throw std::runtime_error("gemm_noalloc: x must be 4-byte aligned with an even stride >= K, y 4-byte aligned");
     CK(cudaSetDevice(device));
@@ -1282,9 +1431,9 @@ void Engine::gemm_noalloc(const char * tensor, int rows, const half * x16, int l
 }
 
 size_t Engine::weight_bytes_per_step() const {
-    // algorithmic weight bytes of one frame step at Q8_0 (34 bytes per 32 weights): backbone
-    // + lm_head once, depth in_proj + layers + one head per sub-step
-    auto qbytes = [](const QMat & q) { return (size_t) q.M * q.K / 32 * 34; };
+    // algorithmic weight bytes of one frame step (Q8_0: 34 bytes per 32 weights, Q4_K: 144 per
+    // 256): backbone + lm_head once, depth in_proj + layers + one head per sub-step
+    auto qbytes = [](const QMat & q) { return qmat_bytes(q); };
     size_t bb = qbytes(lm_head_);
     for (const LayerW & w : bb_) bb += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
     size_t dd = qbytes(dd_in_) + qbytes(dd_head_[0]);

@@ -28,6 +28,7 @@ struct SlotHost {
     int partner = -1;       // slot of this session's unconditional branch (two-branch sessions)
     bool follower = false;  // this slot is another session's unconditional branch
     int dtop_k = 1;         // depth sampler top-k (1: the argmax schedule serves it)
+    bool use_q4 = false;    // depth codes from the Q4_K override weights (src/c_api.cpp:570-578)
     std::vector<int> pages;
 };
 
@@ -69,6 +70,11 @@ public:
     SessionParams abi_params(float cfg_scale) const;
     const Tokenizer & tokenizer() const { return tok_; }
     bool session_free(int sid);
+    // the Q4_K depth override (src/c_api.cpp:532-578): dd.* of a second GGUF, used for the depth
+    // codes of the sessions flagged with session_set_q4; loading again replaces it
+    void load_q4_depth(const std::string & path);
+    bool has_q4_depth() const { return has_q4_; }
+    bool session_set_q4(int sid, bool on);
     int session_count() const { return (int) sid_to_slot_.size(); }
     bool session_active(int sid) const;
     bool session_exists(int sid) const { return sid_to_slot_.count(sid) > 0; }
@@ -129,7 +135,12 @@ private:
     void launch_gemm(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out);
     // graph flags: kFlagSeeds (per-row reseed of the samplers), kFlagSampled (sampled depth),
     // kFlagDepthSeeds (per-call depth seeds)
-    static constexpr int kFlagSeeds = 1, kFlagSampled = 2, kFlagDepthSeeds = 4;
+    // kFlagQ4 (some rows take their depth codes from the Q4_K override: two masked depth passes)
+    static constexpr int kFlagSeeds = 1, kFlagSampled = 2, kFlagDepthSeeds = 4, kFlagQ4 = 8;
+    void depth_pass(int R, int flags, int set, const StepArgs & sa);
+    void load_depth_weights();
+    void swap_depth_sets();
+    const GgufFile & src() const { return src_ ? *src_ : gg_; }
     void enqueue_step(int R, int flags);
     void prefill_prompt(int slot, const std::vector<std::vector<int>> & segs, const int * ref_codes, int ref_frames,
                         float * logits);
@@ -149,7 +160,8 @@ private:
         DpMaps maps;
     };
     const DpPlan * depth_plan(int R);
-    void enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace = nullptr);
+    void enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace = nullptr,
+                       const int * row_set = nullptr);
     bool dp_supported(int R) const;
     int acquire_slot(int sid, int n_pages, bool register_sid = true);
     void release_slot(int slot);
@@ -164,6 +176,16 @@ private:
     std::vector<LayerW> bb_, dd_, te_;
     QMat lm_head_, dd_in_, te_proj_;
     std::vector<QMat> dd_head_;
+    // the other depth weight set (swapped in while a pass for the Q4_K override is enqueued)
+    std::vector<LayerW> q4_dd_;
+    QMat q4_dd_in_;
+    std::vector<QMat> q4_dd_head_;
+    float * q4_dd_out_norm_ = nullptr;
+    int cur_set_ = 0;
+    bool has_q4_ = false;
+    std::unique_ptr<GgufFile> q4_gg_;
+    const GgufFile * src_ = nullptr;   // file the loaders read (the model's own when null)
+    std::vector<void *> q4_allocs_;
     QRows audio_embd_, te_embd_;
     float * bb_out_norm_ = nullptr, * dd_out_norm_ = nullptr, * te_out_norm_ = nullptr;
     float2 * rope_bb_ = nullptr, * rope_dd_ = nullptr, * rope_te_full_ = nullptr, * rope_te_slide_ = nullptr;
@@ -189,7 +211,7 @@ private:
     int * row_slot_ = nullptr, * row_active_ = nullptr, * next_ = nullptr, * cur_frames_ = nullptr;
     int * frames_all_ = nullptr, * step_ctr_ = nullptr, * any_active_ = nullptr, * slot_scalar_ = nullptr;
     uint32_t * seeds_ = nullptr, * dseeds_ = nullptr;
-    int * row_pair_ = nullptr, * create_rows_ = nullptr;
+    int * row_pair_ = nullptr, * create_rows_ = nullptr, * row_set_ = nullptr;
     half * din16_ = nullptr, * dh16_ = nullptr, * dff16_ = nullptr, * datt16_ = nullptr;
     float * dx_ = nullptr, * dqkv_ = nullptr, * dkv_ = nullptr, * dlog_ = nullptr;
     half * bh16_ = nullptr, * bff16_ = nullptr, * batt16_ = nullptr;

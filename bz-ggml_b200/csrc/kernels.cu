@@ -6,6 +6,7 @@
 // per CTA in shared memory in B-fragment order. Split-K partials are reduced in a fixed order
 // by the last CTA of each output tile, so results do not depend on scheduling.
 #include "kernels.cuh"
+#include "q4k.cuh"
 
 #include <algorithm>
 #include <cstdlib>
@@ -354,6 +355,21 @@ __global__ void split_q8_rows_kernel(const uint8_t * raw, long long n_blocks, in
     for (int j = 0; j < 32; j++) qs[b * 32 + j] = (int8_t) src[2 + j];
 }
 
+// one thread per (row, 32-value sub-block) of Q4_K rows
+__global__ void split_q4k_rows_kernel(const uint8_t * raw, long long n_sub, int8_t * qs, half * ds, half * ms) {
+    pdl_trigger();
+    pdl_wait();
+    const long long b = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_sub) return;
+    const uint8_t * blk = raw + (b / 8) * kQ4KBlockBytes;
+    half a, mn;
+    uint8_t q[32];
+    q4k_sub_block(blk, (int) (b % 8), a, mn, q);
+    ds[b] = a;
+    ms[b] = mn;
+    for (int j = 0; j < 32; j++) qs[b * 32 + j] = (int8_t) q[j];
+}
+
 // ------------------------------------------------------------------------------------ norms
 __device__ float block_sum(float v, float * red) {
     v = warp_sum(v);
@@ -426,8 +442,9 @@ __global__ void embed_rows_kernel(QRows e, const int * idx, float scale, float *
     row = (row < 0 || row >= e.rows) ? 0 : row;
     const int8_t * q = e.qs + (size_t) row * e.K;
     const half * d = e.ds + (size_t) row * (e.K / 32);
+    const half * mn = e.ms ? e.ms + (size_t) row * (e.K / 32) : nullptr;
     for (int k = threadIdx.x; k < e.K; k += blockDim.x) {
-        const float v = ((float) q[k] * __half2float(d[k >> 5])) * scale;
+        const float v = ((float) q[k] * __half2float(d[k >> 5]) - (mn ? __half2float(mn[k >> 5]) : 0.0f)) * scale;
         if (o32) o32[(size_t) r * ld + k] = v;
         if (o16) o16[(size_t) r * ld + k] = __float2half_rn(v);
     }
@@ -446,7 +463,8 @@ __global__ void audio_embed_kernel(QRows e, const int * frames, int ldf, int nc,
                 int code = frames[(size_t) r * ldf + cb];
                 code = (code < 0 || code >= vs) ? 0 : code;
                 const size_t row = (size_t) cb * vs + code;
-                acc += (float) e.qs[row * e.K + k] * __half2float(e.ds[row * (e.K / 32) + (k >> 5)]);
+                acc += (float) e.qs[row * e.K + k] * __half2float(e.ds[row * (e.K / 32) + (k >> 5)]) -
+                       (e.ms ? __half2float(e.ms[row * (e.K / 32) + (k >> 5)]) : 0.0f);
             }
         }
         out[(size_t) r * e.K + k] = acc;
@@ -841,7 +859,9 @@ __global__ void step_init_kernel(const StepArgs a) {
         half h0 = __float2half_rn(0.0f), h1 = __float2half_rn(0.0f);
         if (act) {
             h0 = __float2half_rn(a.hid32[(size_t) slot * a.H + d]);
-            const float e = (float) a.embd.qs[(size_t) row * a.embd.K + d] * __half2float(a.embd.ds[(size_t) row * (a.embd.K / 32) + (d >> 5)]);
+            const size_t sb = (size_t) row * (a.embd.K / 32) + (d >> 5);
+            const float e = (float) a.embd.qs[(size_t) row * a.embd.K + d] * __half2float(a.embd.ds[sb]) -
+                            (a.embd.ms ? __half2float(a.embd.ms[sb]) : 0.0f);
             h1 = __float2half_rn(e);
         }
         a.din16[(size_t) r * a.H + d] = h0;
@@ -853,13 +873,14 @@ __global__ void step_init_kernel(const StepArgs a) {
 __device__ __forceinline__ void embed_row_f16(const QRows & e, size_t row, half * dst) {
     const int8_t * q = e.qs + row * e.K;
     const half * d = e.ds + row * (e.K / 32);
+    const half * mn = e.ms ? e.ms + row * (e.K / 32) : nullptr;
     for (int c = threadIdx.x; c < e.K / 8; c += blockDim.x) {
         const uint2 u = *reinterpret_cast<const uint2 *>(q + c * 8);
-        const float sc = __half2float(d[c >> 2]);
+        const float sc = __half2float(d[c >> 2]), m = mn ? __half2float(mn[c >> 2]) : 0.0f;
         const int8_t * b = reinterpret_cast<const int8_t *>(&u);
         half2 o[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) o[j] = __floats2half2_rn((float) b[2 * j] * sc, (float) b[2 * j + 1] * sc);
+        for (int j = 0; j < 4; j++) o[j] = __floats2half2_rn((float) b[2 * j] * sc - m, (float) b[2 * j + 1] * sc - m);
         *reinterpret_cast<uint4 *>(dst + c * 8) = *reinterpret_cast<uint4 *>(o);
     }
 }
@@ -871,6 +892,7 @@ __global__ void argmax_gather_kernel(const StepArgs a, const float * logits, int
     __shared__ int si[32];
     __shared__ int s_code;
     const int r = blockIdx.x;
+    if (a.row_set && a.row_set[r] != a.set_id) return;
     if (!a.row_active[r]) {
         if (threadIdx.x == 0) a.frames[(size_t) r * a.nc + col] = -1;
         return;
@@ -1069,6 +1091,7 @@ __global__ void __launch_bounds__(1024) depth_sample_kernel(const DepthSampleArg
     __shared__ int s_code;
     const StepArgs & sa = a.s;
     const int r = blockIdx.x;
+    if (sa.row_set && sa.row_set[r] != sa.set_id) return;
     if (!sa.row_active[r]) {
         if (threadIdx.x == 0) sa.frames[(size_t) r * sa.nc + a.col] = -1;
         return;
@@ -1252,6 +1275,13 @@ void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cu
 void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s) {
     const long long nb = (long long) rows * (K / 32);
     launch_k(split_q8_rows_kernel, (unsigned) ((nb + 255) / 256), 256, 0, s, raw_dev, nb, qs, ds);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void split_q4k_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, half * ms, cudaStream_t s) {
+    if (K % kQ4KBlockValues) throw std::runtime_error("Q4_K rows need a length that is a multiple of 256");
+    const long long nb = (long long) rows * (K / 32);
+    launch_k(split_q4k_rows_kernel, (unsigned) ((nb + 255) / 256), 256, 0, s, raw_dev, nb, qs, ds, ms);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -18,10 +18,16 @@ namespace bzb {
 // int8 (piece (block half, 16-byte half) major, row minor) followed by 2 x 128 f16 block scales
 // ((block half) major, row minor). Gate/up pairs interleave in 16-row groups.
 constexpr int kUChunkBytes = 128 * 64 + 2 * 128 * 2;
+// The same chunk for Q4_K weights (w = a q - b per 32-value sub-block, q in [0, 15]): the 4-bit
+// quants [half][row][16 B] (each 32-bit word holds 8 consecutive values, even ones in nibbles
+// 0-3 and odd ones in nibbles 4-7), then the f16 scales a and the f16 mins b, each [half][row].
+constexpr int kUChunkBytesQ4 = 128 * 32 + 2 * 2 * 128 * 2;
 struct UMat {
     const uint8_t * blk = nullptr;
     int M = 0, MT = 0, K = 0, KC = 0;
+    int q4 = 0;                    // chunk format: 0 Q8_0, 1 Q4_K
 };
+__host__ __device__ inline int umat_chunk_bytes(int q4) { return q4 ? kUChunkBytesQ4 : kUChunkBytes; }
 
 struct QMat {
     const uint4 * qs = nullptr;    // [MT][KB][32] uint4
@@ -31,9 +37,12 @@ struct QMat {
 };
 
 // Q8_0 rows kept for row gathers (embeddings): int8 values and f16 block scales.
+// embedding rows: value = qs * ds - ms per 32-value block (ms null for Q8_0; Q4_K rows keep
+// their 4-bit values in qs and the sub-block scale and min in ds and ms)
 struct QRows {
     const int8_t * qs = nullptr;   // [rows][K]
     const half * ds = nullptr;     // [rows][K/32]
+    const half * ms = nullptr;     // [rows][K/32] or null
     int rows = 0, K = 0;
 };
 
@@ -101,10 +110,14 @@ void launch_gemv_static_scratch(const QMat & w, const half * x16, int ldx, int r
 // bounded pipeline wait gave up
 void init_umma_attributes();
 void repack_umma(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaStream_t s);
+// Q4_K rows (144-byte super-blocks of 256 values, K % 256 == 0) into kUChunkBytesQ4 chunks
+void repack_umma_q4k(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaStream_t s);
 void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const GemvOut & out, int * err,
                       cudaStream_t s, bool pdl);
 bool pdl_scope();
 void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s);
+// Q4_K rows into 4-bit values (one per byte), sub-block scales and mins
+void split_q4k_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, half * ms, cudaStream_t s);
 
 // out16[r] = f16(rmsnorm(x[r]) * w) (and out32 when non-null) for rows [r0, r0 + n)
 void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps, half * out16, int ld16,
@@ -180,6 +193,9 @@ struct StepArgs {
     int * frames = nullptr;         // current frame [R][nc]
     int * step_ctr = nullptr;       // burst step index
     int * any_active = nullptr;     // [Kmax]
+    // depth passes of one weight set: rows whose row_set differs from set_id are left alone
+    const int * row_set = nullptr;
+    int set_id = 0;
 };
 void launch_step_init(const StepArgs & a, cudaStream_t s);
 // codes[r] = first argmax of logits[r]; frames[..][r][col] = code; when gather_cb >= 0 the

@@ -307,8 +307,11 @@ int main(int argc, char ** argv) {
 
     const GgmlType q = s.qtype;
     std::vector<Tensor> ts;
+    // a Q4_K file keeps Q8_0 for tensors whose rows are not whole 256-value super-blocks (the
+    // way llama.cpp's quantiser falls back), e.g. the small vocoder's 32-wide projections
     auto lin = [&](const std::string & n, int64_t in, int64_t outd, int64_t n2 = 0) {
-        Tensor t{ n, n2 ? std::vector<int64_t>{ in, outd, n2 } : std::vector<int64_t>{ in, outd }, q, 0 };
+        const GgmlType tq = (q == G_Q4_K && in % 256) ? G_Q8_0 : q;
+        Tensor t{ n, n2 ? std::vector<int64_t>{ in, outd, n2 } : std::vector<int64_t>{ in, outd }, tq, 0 };
         ts.push_back(t);
     };
     auto nrm = [&](const std::string & n, int64_t d) { ts.push_back(Tensor{ n, { d }, G_F32, 1 }); };

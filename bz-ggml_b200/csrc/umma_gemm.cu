@@ -1,4 +1,4 @@
-// tcgen05 (5th-generation tensor core) dequant-GEMM for Q8_0 weights, sm_100a.
+// tcgen05 (5th-generation tensor core) dequant-GEMM for Q8_0 and Q4_K weights, sm_100a.
 //
 // y[rows, M] = x[rows, K] . W^T with W stored as Q8_0. Each CTA owns one 128-row weight tile
 // (the MMA's M), up to 64 activation rows (the MMA's N) and a K range, processed in 64-wide
@@ -15,6 +15,7 @@
 // Split-K partials of one tile are reduced on chip: the splits form a thread-block cluster and
 // each CTA sums its slice of rows from every peer's shared memory in rank order.
 #include "kernels.cuh"
+#include "q4k.cuh"
 #include "tc_ptx.cuh"
 
 #include <cooperative_groups.h>
@@ -47,6 +48,7 @@ constexpr int kABytes = kTileM * kChunkK * 2;
 
 struct UParams {
     const uint8_t * blk;
+    int q4;          // chunk format (UMat::q4)
     int M, MT, KC, kc_per_split, splits;
     const half * x;
     int ldx, rows;
@@ -131,6 +133,27 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
             const int rs = c % kRawStages, ab = c % kAStages;
             if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kRawStages) & 1u, p.err);
             const uint8_t * raw = sR + rs * kRawBytes;
+            uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+            if (p.q4) {
+                // one 32-value Q4_K sub-block of row r: 16 bytes of nibbles, its scale and min
+                const uint4 qv = *reinterpret_cast<const uint4 *>(raw + (hb * kTileM + r) * 16);
+                const half a = *reinterpret_cast<const half *>(raw + kTileM * 32 + (hb * kTileM + r) * 2);
+                const half b = *reinterpret_cast<const half *>(raw + kTileM * 32 + 2 * kTileM * 2 + (hb * kTileM + r) * 2);
+                mbar_arrive(&raw_empty[rs]);
+                if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
+                const half2 a2 = __halves2half2(a, a), nb2 = __hneg2(__halves2half2(b, b));
+                const uint32_t w4[4] = { qv.x, qv.y, qv.z, qv.w };
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    uint32_t o[4];
+                    dq8_nib(w4[q], a2, nb2, o);
+                    const int j = hb * 4 + q;
+                    *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+                fence_proxy_async();
+                mbar_arrive(&a_full[ab]);
+                continue;
+            }
             const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
             const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
             const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
@@ -138,7 +161,6 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
             if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
             const half2 s2 = __halves2half2(sc, sc);
             const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
-            uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 uint4 o;
@@ -170,13 +192,14 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
         if (lane == 0) {
             // weights and scales are constant: stream them before the predecessor finishes
             // one bulk copy per chunk: quants and scales are contiguous in the repacked layout
-            const uint8_t * base = p.blk + (size_t) (mt * p.KC + c_beg) * kUChunkBytes;
+            const int cb = umat_chunk_bytes(p.q4);
+            const uint8_t * base = p.blk + (size_t) (mt * p.KC + c_beg) * cb;
             for (int c = 0; c < nch; c++) {
                 const int rs = c % kRawStages;
                 if (c >= kRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kRawStages) - 1) & 1u, p.err);
                 uint8_t * raw = sR + rs * kRawBytes;
-                mbar_expect_tx(&raw_full[rs], kRawBytes);
-                bulk_g2s(raw, base + (size_t) c * kUChunkBytes, kUChunkBytes, &raw_full[rs]);
+                mbar_expect_tx(&raw_full[rs], (uint32_t) cb);
+                bulk_g2s(raw, base + (size_t) c * cb, (uint32_t) cb, &raw_full[rs]);
             }
         }
     } else {
@@ -319,6 +342,35 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     cluster.sync();
 }
 
+// one thread per (tile, chunk, sub-block half, row): the Q4_K sub-block's values repacked into
+// words of 8 (even values in nibbles 0-3, odd in 4-7), with its f16 scale and min
+__global__ void repack_umma_q4k_kernel(const uint8_t * raw, int M, int K, int KC, uint8_t * blk) {
+    const long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    const int MT = (M + kTileM - 1) / kTileM;
+    if (idx >= (long long) MT * KC * 2 * kTileM) return;
+    const int r = (int) (idx % kTileM), hb = (int) ((idx / kTileM) % 2);
+    const long long tc = idx / (2 * kTileM);
+    const int c = (int) (tc % KC), mt = (int) (tc / KC);
+    const int row = mt * kTileM + r;
+    uint32_t w[4] = { 0u, 0u, 0u, 0u };
+    half a = __float2half_rn(0.0f), b = a;
+    if (row < M) {
+        const int v0 = c * kChunkK + hb * 32;  // first value of the sub-block within the row
+        const uint8_t * sblk = raw + ((size_t) row * (K / kQ4KBlockValues) + (size_t) (v0 / kQ4KBlockValues)) * kQ4KBlockBytes;
+        uint8_t q[32];
+        q4k_sub_block(sblk, (v0 % kQ4KBlockValues) / 32, a, b, q);
+#pragma unroll
+        for (int wi = 0; wi < 4; wi++)
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                w[wi] |= ((uint32_t) q[8 * wi + 2 * k] << (4 * k)) | ((uint32_t) q[8 * wi + 2 * k + 1] << (16 + 4 * k));
+    }
+    uint8_t * bp = blk + (size_t) tc * kUChunkBytesQ4;
+    *reinterpret_cast<uint4 *>(bp + ((size_t) hb * kTileM + r) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<half *>(bp + kTileM * 32 + ((size_t) hb * kTileM + r) * 2) = a;
+    *reinterpret_cast<half *>(bp + kTileM * 32 + 2 * kTileM * 2 + ((size_t) hb * kTileM + r) * 2) = b;
+}
+
 __global__ void repack_umma_kernel(const uint8_t * raw, int M, int KB, int KC, uint8_t * blk) {
     const long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x;
     const int MT = (M + kTileM - 1) / kTileM;
@@ -452,6 +504,14 @@ void repack_umma(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaStrea
     UCHECK(cudaGetLastError());
 }
 
+void repack_umma_q4k(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaStream_t s) {
+    if (K % kQ4KBlockValues) throw std::runtime_error("Q4_K rows need a length that is a multiple of 256");
+    const int MT = (M + kTileM - 1) / kTileM, KC = K / kChunkK;
+    const long long n = (long long) MT * KC * 2 * kTileM;
+    repack_umma_q4k_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, s>>>(raw_dev, M, K, KC, blk);
+    UCHECK(cudaGetLastError());
+}
+
 void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const GemvOut & out, int * err,
                       cudaStream_t s, bool pdl) {
     if (rows <= 0) return;
@@ -471,7 +531,7 @@ void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const
         if (f == 1 || f == 2 || f == 4 || f == 8) splits = std::min(f, (out.kind >= EPI_SWIGLU) ? 4 : 8);
     }
     UParams p;
-    p.blk = w.blk; p.M = w.M; p.MT = w.MT; p.KC = w.KC;
+    p.blk = w.blk; p.q4 = w.q4; p.M = w.M; p.MT = w.MT; p.KC = w.KC;
     p.kc_per_split = (w.KC + splits - 1) / splits;
     p.splits = splits;
     p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.err = err;

@@ -357,7 +357,7 @@ float * Vocoder::load_f32(const std::string & name, int64_t expect, bool exp_of)
 
 QMat Vocoder::load_q8(const std::string & name) {
     const GgufTensor & t = need(name);
-    if (t.type != 8) throw std::runtime_error("vocoder: " + name + " must be Q8_0");
+    if (t.type != GT_Q8_0 && t.type != GT_Q4_K) throw std::runtime_error("vocoder: " + name + " must be Q8_0 or Q4_K");
     const int K = (int) t.ne[0], M = (int) t.rows();
     QMat q;
     q.M = M;
@@ -367,14 +367,30 @@ QMat Vocoder::load_q8(const std::string & name) {
     uint8_t * raw = nullptr;
     VCHECK(cudaMalloc(&raw, t.nbytes));
     VCHECK(cudaMemcpy(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice));
-    uint4 * qs = dalloc<uint4>((size_t) q.MT * q.KB * 32);
-    half2 * ds = dalloc<half2>((size_t) q.MT * q.KB * 8);
-    repack_q8(raw, M, K, qs, ds, stream_);
+    if (t.type == GT_Q4_K) {
+        // Q4_K linears run on the tcgen05 dequant-GEMM (its 4-bit tile layout)
+        if (K % 256) throw std::runtime_error("vocoder: " + name + " is Q4_K with rows not a multiple of 256");
+        UMat u;
+        u.M = M; u.MT = (M + 127) / 128; u.K = K; u.KC = K / 64; u.q4 = 1;
+        uint8_t * ub = dalloc<uint8_t>((size_t) u.MT * u.KC * kUChunkBytesQ4);
+        repack_umma_q4k(raw, M, K, ub, stream_);
+        u.blk = ub;
+        q.u = u;
+    } else {
+        uint4 * qs = dalloc<uint4>((size_t) q.MT * q.KB * 32);
+        half2 * ds = dalloc<half2>((size_t) q.MT * q.KB * 8);
+        repack_q8(raw, M, K, qs, ds, stream_);
+        q.qs = qs;
+        q.ds = ds;
+    }
     VCHECK(cudaStreamSynchronize(stream_));
     cudaFree(raw);
-    q.qs = qs;
-    q.ds = ds;
     return q;
+}
+
+void Vocoder::linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s) {
+    if (w.qs) launch_gemv(w, x16, ldx, rows, out, scr_, s);
+    else launch_umma_gemm(w.u, x16, ldx, rows, out, err_, s, false);
 }
 
 Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int cout, bool transposed) {
@@ -490,8 +506,11 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
     if (up_total != kSamplesPerFrame)
         throw std::runtime_error("vocoder: the upsampling stages give " + std::to_string(up_total) +
                                  " samples per frame, the C API assumes 1920");
-    // dynamic shared memory of the GEMV variants and of the largest convolution
+    // dynamic shared memory of the GEMV and tcgen05 GEMM variants and of the largest convolution
     init_kernel_attributes();
+    init_umma_attributes();
+    err_ = dalloc<int>(1);
+    VCHECK(cudaMemset(err_, 0, sizeof(int)));
     size_t conv_mx = conv_smem(std::max({ dpre_.K, dhead_.K, dfin_.K }), 1), convtr_mx = 0;
     for (const Up & u : ups_) convtr_mx = std::max(convtr_mx, convtr_smem(u.up.K));
     for (const Blk & b : blks_) {
@@ -585,8 +604,8 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
     // quantiser decode -> [T][cbdim] -> [cbdim][T]
     half * e_first = f16_, * e_rest = f16_ + (size_t) T * dq_;
     voc_embed_kernel<<<T, 128, 0, s>>>(emb_first_, emb_rest_[0], codes_, nc, nc, dq_, cfg_.vs, e_first, e_rest);
-    launch_gemv(dq_first_out_, e_first, dq_, T, GemvOut{ EPI_STORE, t32_, nullptr, cbdim_ }, scr_, s);
-    if (nc > 1) launch_gemv(dq_rest_out_, e_rest, dq_, T, GemvOut{ EPI_RESID, t32_, nullptr, cbdim_ }, scr_, s);
+    linear(dq_first_out_, e_first, dq_, T, GemvOut{ EPI_STORE, t32_, nullptr, cbdim_ }, s);
+    if (nc > 1) linear(dq_rest_out_, e_rest, dq_, T, GemvOut{ EPI_RESID, t32_, nullptr, cbdim_ }, s);
     auto transpose = [&](const float * in, int R, int C, float * out, const float * add) {
         voc_transpose_kernel<<<dim3((C + 31) / 32, (R + 31) / 32), dim3(32, 8), 0, s>>>(in, R, C, out, add);
     };
@@ -610,27 +629,27 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
     transpose(b_, latent_, T, a_, nullptr);                          // a_ = [T][latent]
     voc_to_f16_kernel<<<grid_for((size_t) T * latent_), 256, 0, s>>>(a_, (size_t) T * latent_, t16_);
     float * h = c_;                                                  // [T][H]
-    launch_gemv(in_proj_, t16_, latent_, T, GemvOut{ EPI_STORE, h, nullptr, H }, scr_, s);
+    linear(in_proj_, t16_, latent_, T, GemvOut{ EPI_STORE, h, nullptr, H }, s);
     voc_bias_scale_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, (size_t) T * H, H, in_proj_b_, nullptr);
     const float scale = 1.0f / std::sqrt((float) hd);
     for (const Layer & Ly : layers_) {
         launch_rmsnorm(h, H, Ly.attn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
-        launch_gemv(Ly.q, t16_, H, T, GemvOut{ EPI_STORE, q_, nullptr, nh * hd }, scr_, s);
-        launch_gemv(Ly.k, t16_, H, T, GemvOut{ EPI_STORE, k_, nullptr, nkv * hd }, scr_, s);
-        launch_gemv(Ly.v, t16_, H, T, GemvOut{ EPI_STORE, v_, nullptr, nkv * hd }, scr_, s);
+        linear(Ly.q, t16_, H, T, GemvOut{ EPI_STORE, q_, nullptr, nh * hd }, s);
+        linear(Ly.k, t16_, H, T, GemvOut{ EPI_STORE, k_, nullptr, nkv * hd }, s);
+        linear(Ly.v, t16_, H, T, GemvOut{ EPI_STORE, v_, nullptr, nkv * hd }, s);
         const int warps = T * nh;
         voc_attn_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, k_, v_, T, nh, nkv, hd, vc_.window, rope_, scale, att16_);
-        launch_gemv(Ly.o, att16_, nh * hd, T, GemvOut{ EPI_STORE, o_, nullptr, H }, scr_, s);
+        linear(Ly.o, att16_, nh * hd, T, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
         voc_scaled_add_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, o_, (size_t) T * H, H, Ly.attn_scale);
         launch_rmsnorm(h, H, Ly.ffn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
-        launch_gemv(Ly.gate, t16_, H, T, GemvOut{ EPI_STORE, g_, nullptr, F }, scr_, s);
-        launch_gemv(Ly.up, t16_, H, T, GemvOut{ EPI_STORE, u_, nullptr, F }, scr_, s);
+        linear(Ly.gate, t16_, H, T, GemvOut{ EPI_STORE, g_, nullptr, F }, s);
+        linear(Ly.up, t16_, H, T, GemvOut{ EPI_STORE, u_, nullptr, F }, s);
         voc_silu_mul_kernel<<<grid_for((size_t) T * F), 256, 0, s>>>(g_, u_, (size_t) T * F, t16_);
-        launch_gemv(Ly.down, t16_, F, T, GemvOut{ EPI_STORE, o_, nullptr, H }, scr_, s);
+        linear(Ly.down, t16_, F, T, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
         voc_scaled_add_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, o_, (size_t) T * H, H, Ly.ffn_scale);
     }
     launch_rmsnorm(h, H, out_norm_, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
-    launch_gemv(out_proj_, t16_, H, T, GemvOut{ EPI_STORE, o_, nullptr, latent_ }, scr_, s);
+    linear(out_proj_, t16_, H, T, GemvOut{ EPI_STORE, o_, nullptr, latent_ }, s);
     voc_bias_scale_kernel<<<grid_for((size_t) T * latent_), 256, 0, s>>>(o_, (size_t) T * latent_, latent_, out_proj_b_, nullptr);
     transpose(o_, T, latent_, a_, nullptr);                          // a_ = [latent][T]
 
@@ -647,9 +666,9 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
         transpose(y, latent_, L, t32_, nullptr);                     // [L][latent]
         voc_layernorm_kernel<<<L, 256, 0, s>>>(t32_, latent_, u.norm_w, u.norm_b, 1e-6f, t16_);
         const int F4 = u.pw1.M;
-        launch_gemv(u.pw1, t16_, latent_, L, GemvOut{ EPI_STORE, o_, nullptr, F4 }, scr_, s);
+        linear(u.pw1, t16_, latent_, L, GemvOut{ EPI_STORE, o_, nullptr, F4 }, s);
         voc_bias_gelu_kernel<<<grid_for((size_t) L * F4), 256, 0, s>>>(o_, (size_t) L * F4, F4, u.pw1_b, f16_);
-        launch_gemv(u.pw2, f16_, F4, L, GemvOut{ EPI_STORE, t32_, nullptr, latent_ }, scr_, s);
+        linear(u.pw2, f16_, F4, L, GemvOut{ EPI_STORE, t32_, nullptr, latent_ }, s);
         voc_bias_scale_kernel<<<grid_for(n), 256, 0, s>>>(t32_, n, latent_, u.pw2_b, u.gamma);
         transpose(t32_, L, latent_, y, x);                           // y = x + branch^T
         std::swap(x, y);
@@ -675,7 +694,10 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
     voc_clamp_kernel<<<grid_for((size_t) L), 256, 0, s>>>(y, (size_t) L, pcm_);
     VCHECK(cudaGetLastError());
     VCHECK(cudaMemcpyAsync(pcm, pcm_, (size_t) L * sizeof(float), cudaMemcpyDeviceToHost, s));
+    int err = 0;
+    VCHECK(cudaMemcpyAsync(&err, err_, sizeof(int), cudaMemcpyDeviceToHost, s));
     VCHECK(cudaStreamSynchronize(s));
+    if (err) throw std::runtime_error("vocoder: a bounded wait timed out in the tcgen05 GEMM");
 }
 
 // ---------------------------------------------------------------------------------- sessions

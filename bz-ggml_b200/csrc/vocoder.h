@@ -67,7 +67,8 @@ private:
 
     const GgufTensor & need(const std::string & name) const;
     float * load_f32(const std::string & name, int64_t expect, bool exp_of = false);
-    QMat load_q8(const std::string & name);
+    QMat load_q8(const std::string & name);  // Q8_0 (mma.sync layout) or Q4_K (tcgen05 layout)
+    void linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s);
     Conv load_conv(const std::string & name, int K, int cin, int cout, bool transposed);
     void ensure(int T);
     template <class T> T * dalloc(size_t n);
@@ -94,6 +95,7 @@ private:
     float2 * rope_ = nullptr;
     int rope_max_ = 0;
     GemvScratch scr_;
+    int * err_ = nullptr;  // bounded-wait error flag of the tcgen05 GEMM
 
     // activations, grown on demand (T frames at a time)
     int tcap_ = 0;

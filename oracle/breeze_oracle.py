@@ -429,8 +429,20 @@ class Model:
         self.mode = mode
         self.dd_ff = llama3_freq_factors(self.cfg.dd)
 
+    def _file(self, name) -> "GGUFFile":
+        dd = getattr(self, "dd_file", None)
+        return dd if dd is not None and name.startswith("dd.") else self.g
+
     def w(self, name):
-        return self.g.weight(name)
+        return self._file(name).weight(name)
+
+    def with_depth_override(self, path: str) -> "Model":
+        """This model with its dd.* tensors read from another GGUF: the Q4_K depth override of
+        src/c_api.cpp:532-566 (BreezeModel::w routes dd.* to dd_override, src/model.h:26-43)."""
+        import copy
+        m = copy.copy(self)
+        m.dd_file = GGUFFile(path)
+        return m
 
     def lin(self, x, name, sub: int = -1):
         """Quantised linear; `sub` selects one [rows, in] slice of a 3-D weight."""
@@ -438,8 +450,9 @@ class Model:
         if sub >= 0:
             w = w[sub]
         w = w.reshape(-1, w.shape[-1])
-        if self.mode == "ggml" and self.g.tensors[name].type == Q8_0:
-            return linear_q8(x, self.g.tensors[name].raw, w.shape[0], w.shape[1], max(sub, 0) * w.shape[0])
+        t = self._file(name).tensors[name]
+        if self.mode == "ggml" and t.type == Q8_0:
+            return linear_q8(x, t.raw, w.shape[0], w.shape[1], max(sub, 0) * w.shape[0])
         return linear(x, w)
 
     def embed_rows(self, name, idx) -> np.ndarray:
@@ -848,6 +861,7 @@ class Session:
     st_u: BBState = None
     last_hidden_u: np.ndarray = None
     sp: SamplerParams = field(default_factory=SamplerParams)
+    use_q4: bool = False           # depth codes from the Q4_K override (src/c_api.cpp:570-578)
 
 
 def combine_logits(lc, lu, scale):
@@ -871,6 +885,16 @@ class Generator:
     def __init__(self, model: Model):
         self.m = model
         self.sessions = {}
+        self.q4 = None
+
+    def load_q4_depth(self, path: str):
+        self.q4 = self.m.with_depth_override(path)
+
+    def session_set_q4(self, sid, on: bool) -> int:
+        if sid not in self.sessions:
+            return -1
+        self.sessions[sid].use_q4 = bool(on) and self.q4 is not None
+        return 0
 
     def abi_params(self) -> SamplerParams:
         c = self.m.cfg
@@ -961,9 +985,10 @@ class Generator:
         self.last_depth_uniforms = {}
         chosen = np.zeros((n, nc - 1), np.int64)
 
-        def choose(j, lg):
+        def choose(j, lg, ks):
             out = np.zeros(lg.shape[0], np.int64)
-            for k, s in enumerate(ss):
+            for k in ks:
+                s = ss[k]
                 l = combine_logits(lg[k], lg[urow[k]] if k in urow else None, s.cfg)
                 comb_logits[k, j - 1] = l
                 if not sampled or s.sp.dtop_k == 1:
@@ -986,7 +1011,20 @@ class Generator:
                     out[urow[k]] = code
             return out
 
-        m.depth_chain(hid, cb0, choose)
+        # each depth weight set decodes its own sessions' rows (src/c_api.cpp:622-650)
+        for use_q4 in (False, True):
+            ks = [k for k in range(n) if ss[k].use_q4 == use_q4]
+            if not ks:
+                continue
+            model = self.q4 if use_q4 else m
+            rows = ks + [urow[k] for k in ks if k in urow]
+
+            def choose_set(j, lg_local, ks=ks, rows=rows):
+                lg = np.zeros((hid.shape[0], lg_local.shape[1]), np.float32)
+                lg[rows] = lg_local
+                return choose(j, lg, ks)[rows]
+
+            model.depth_chain(hid[rows], cb0[rows], choose_set)
         if depth_logits_out is not None:
             for k, i in enumerate(act):
                 depth_logits_out[sids[i]] = comb_logits[k]
