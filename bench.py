@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--nc", type=int, default=32)
     ap.add_argument("--model-dir", default=os.environ.get("BZB_MODEL_DIR", "/tmp/bzb_models"))
     ap.add_argument("--cpu-sample-sessions", type=int, default=4)
+    ap.add_argument("--ttfa-arrivals", type=int, default=8, help="sessions admitted into the running batch for TTFA")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt-cap", type=int, default=0, help="cap text prompt length (profiling runs)")
     ap.add_argument("--profile", action="store_true",
@@ -136,6 +137,50 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
+CHUNK_FIRST = 4  # frames in the first streamed chunk (src/generation.h GenRequest::chunk_first)
+
+
+def measure_ttfa(pkg, gen, ids, seeds, n_arrivals: int, seed: int):
+    """Time to first audio of sessions admitted into the running batch (host wall clock, no
+    queueing): one live session retires, the arrival is created in its place (text encoder and
+    backbone prefill, first cb0), the whole batch steps until the arrival holds its first chunk
+    of CHUNK_FIRST frames, and the vocoder (sharing the generator's weights) decodes that chunk
+    to PCM through the C ABI."""
+    voc = pkg.VocoderHandle(generator=gen)
+    arrivals = workload(n_arrivals, seed, 8 * CHUNK_FIRST)
+    rows = []
+    try:
+        for a, s in enumerate(arrivals):
+            sid = ids[(7 * a) % len(ids)]
+            gen.session_free(sid)
+            ref_codes = ref_text = None
+            if s["vframes"] > 0:
+                ref_codes = np.random.default_rng(sid).integers(0, 2048, (s["vframes"], gen.nc)).astype(np.int32)
+                ref_text = pkg.ids_to_text(s["ref_ids"])
+            gen.sync()
+            t0 = time.perf_counter()
+            gen.session_create_ext(sid, pkg.ids_to_text(s["ids"]), ref_text=ref_text, ref_codes=ref_codes,
+                                   ref_frames=s["vframes"], seed=s["seed"], max_new_tokens=s["gen_len"])
+            t1 = time.perf_counter()
+            _, frames, _ = gen.step_frames(ids, CHUNK_FIRST, seeds + 700 + CHUNK_FIRST * a)
+            t2 = time.perf_counter()
+            pcm = voc.session_decode(10_000 + a, frames[:, ids.index(sid), :])
+            t3 = time.perf_counter()
+            assert pcm.size == CHUNK_FIRST * 1920
+            rows.append(((t3 - t0) * 1e3, (t1 - t0) * 1e3, (t2 - t1) * 1e3, (t3 - t2) * 1e3,
+                         len(s["ids"]), s["vframes"]))
+    finally:
+        voc.close()
+    tot = [r[0] for r in rows]
+    return {"p50_ms": statistics.median(tot), "p90_ms": float(np.percentile(tot, 90)), "n": len(rows),
+            "prefill_ms_p50": statistics.median(r[1] for r in rows),
+            "first_chunk_steps_ms_p50": statistics.median(r[2] for r in rows),
+            "vocoder_ms_p50": statistics.median(r[3] for r in rows),
+            "method": f"arrival admitted into the running {len(ids)}-session batch (no queueing): prefill + "
+                      f"{CHUNK_FIRST} batched frame steps + vocoder decode of the first {CHUNK_FIRST}-frame chunk, "
+                      "host wall clock through the C ABI"}
+
+
 def cpu_oracle_rtf(path: str, n_sessions: int, steps: int, warmup: int, seed: int = 7):
     """Aggregate RTF of the CPU port (numpy, all host threads) on a bounded sample: n sessions
     with 32-token prompts (prefill untimed), `steps` timed frame steps after `warmup`."""
@@ -203,7 +248,7 @@ def main():
     gen = pkg.GeneratorHandle(path, local)
     t_load = time.perf_counter() - t_load
     nc = gen.nc
-    total_steps = args.warmup + 2 * args.steps + 2
+    total_steps = args.warmup + 2 * args.steps + 2 + CHUNK_FIRST * args.ttfa_arrivals
     sessions = workload(args.sessions, 1000 + rank, total_steps + 1, args.prompt_cap)
     prefill_ms = []
     ctx0 = []
@@ -264,6 +309,7 @@ def main():
     ms_e2e = timed(e2e_loop)
     prof = gen.profile_step()
     launches = gen.launches_per_step()
+    ttfa = measure_ttfa(pkg, gen, ids, seeds, args.ttfa_arrivals, 5000 + rank) if args.ttfa_arrivals > 0 else None
 
     step_ms = ms_dev / args.steps
     audio_s = world * args.sessions * args.steps * FRAME_S
@@ -323,6 +369,7 @@ def main():
             "step_roofline": {"bytes_per_step": b_step, "achieved": step_gbs, "peak": hbm, "unit": "GB/s",
                               "frac": step_gbs / hbm},
             "cpu_baseline": cpu,
+            "ttfa": ttfa,
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
         }

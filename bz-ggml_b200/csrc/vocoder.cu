@@ -25,8 +25,6 @@ namespace bzb {
 
 namespace {
 
-constexpr int kTile = 64;   // output channels and time steps per conv CTA
-constexpr int kCi = 8;      // input channels staged per pass
 
 // sum over codebooks of the quantiser embeddings (src/codec_decoder.cpp:41-62): out_first[t] =
 // E_first[code0], out_rest[t] = sum_{cb>=1} E_rest[cb-1][code_cb], both f16 for the projections
@@ -66,129 +64,147 @@ __global__ void voc_transpose_kernel(const float * in, int R, int C, float * out
     }
 }
 
-// causal conv, stride 1 (src/codec_conv.cpp:9-23): y[o][t] = b[o] + sum_i sum_k w[o][i][k]
-// x[i][t - (K-1-k) d]; optional SnakeBeta on the input as it is staged (alpha, beta per input
-// channel), optional residual add of `res` [Cout][L]
-__global__ void __launch_bounds__(256) voc_conv1d_kernel(const float * x, int cin, int L, const float * w,
-                                                         const float * b, int cout, int K, int dil, const float * snake_a,
-                                                         const float * snake_b, const float * res, float * y) {
-    extern __shared__ float sm[];
-    const int halo = (K - 1) * dil;
-    const int xw = kTile + halo;
-    float * xs = sm;                        // [kCi][xw]
-    float * ws = sm + kCi * xw;             // [kCi][K][kTile]
-    const int t0 = blockIdx.x * kTile, o0 = blockIdx.y * kTile;
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    float acc[4][4] = {};
-    for (int i0 = 0; i0 < cin; i0 += kCi) {
-        for (int idx = threadIdx.x; idx < kCi * xw; idx += 256) {
-            const int i = idx / xw, j = idx % xw;
-            const int ci = i0 + i, t = t0 - halo + j;
-            float v = 0.0f;
-            if (ci < cin && t >= 0 && t < L) {
-                v = x[(size_t) ci * L + t];
-                if (snake_a) {
-                    const float s = sinf(v * snake_a[ci]);
-                    v = v + (s * s) / snake_b[ci];
-                }
-            }
-            xs[idx] = v;
-        }
-        for (int idx = threadIdx.x; idx < kCi * K * kTile; idx += 256) {
-            const int o = idx % kTile, k = (idx / kTile) % K, i = idx / (kTile * K);
-            const int ci = i0 + i, co = o0 + o;
-            ws[idx] = (ci < cin && co < cout) ? w[((size_t) co * cin + ci) * K + k] : 0.0f;
-        }
-        __syncthreads();
-        for (int i = 0; i < kCi; i++) {
-            for (int k = 0; k < K; k++) {
-                float xv[4], wv[4];
-#pragma unroll
-                for (int jt = 0; jt < 4; jt++) xv[jt] = xs[i * xw + tx * 4 + jt + k * dil];
-#pragma unroll
-                for (int jo = 0; jo < 4; jo++) wv[jo] = ws[(i * K + k) * kTile + ty * 4 + jo];
-#pragma unroll
-                for (int jo = 0; jo < 4; jo++)
-#pragma unroll
-                    for (int jt = 0; jt < 4; jt++) acc[jo][jt] += wv[jo] * xv[jt];
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int jo = 0; jo < 4; jo++) {
-        const int co = o0 + ty * 4 + jo;
-        if (co >= cout) continue;
-#pragma unroll
-        for (int jt = 0; jt < 4; jt++) {
-            const int t = t0 + tx * 4 + jt;
-            if (t >= L) continue;
-            float v = acc[jo][jt] + (b ? b[co] : 0.0f);
-            if (res) v += res[(size_t) co * L + t];
-            y[(size_t) co * L + t] = v;
-        }
-    }
+// Causal convolutions as TF32 tensor-core implicit GEMMs (mma.sync m16n8k8):
+//   y[o][t] = b[o] + sum_{i,k} W[o][i*taps + k] * x[i][t - (taps-1-k) dil]
+// M = output channels, N = time, reduction = cin * taps, im2col done while staging the input
+// tile. A stride-s transposed conv (src/codec_conv.cpp:25-32) is s such convolutions with 2 taps
+// each, one per output phase p: y[o][s t + p] = b[o] + sum_{i,m} w[i][o][p + m s] x[i][t - m]
+// (blockIdx.z = phase; the phase weights are re-laid out at load). The epilogue adds the bias and
+// an optional residual, then stores the value or its SnakeBeta (and optionally a second,
+// SnakeBeta-activated copy for the next consumer), clamped to [-1, 1] for the final PCM.
+constexpr int kCBM = 64, kCBN = 64, kCBK = 32, kCThreads = 128;
+
+struct ConvArgs {
+    const float * x = nullptr;          // input [cin][L]
+    int cin = 0, L = 0;
+    const float * w = nullptr;          // [phases][cout][cin * taps]
+    int taps = 1, dil = 1;
+    const float * bias = nullptr;
+    int cout = 0;
+    float * y = nullptr;                // y[o * ldy + t * ostride + phase]
+    int ldy = 0, ostride = 1;
+    const float * res = nullptr;        // residual added before the activations (same indexing), or null
+    const float * sa = nullptr, * sb = nullptr;     // SnakeBeta (alpha, beta) of the stored value, or null
+    float * y2 = nullptr;               // second output: SnakeBeta(value) with (s2a, s2b), or null
+    const float * s2a = nullptr, * s2b = nullptr;
+    int clamp = 0;
+};
+
+__device__ __forceinline__ uint32_t to_tf32(float f) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(f));
+    return r;
 }
 
-// causal transposed conv (src/codec_conv.cpp:25-32): y[o][u] = b[o] + sum_i sum_{k = u mod s +
-// m s < K} w[i][o][k] x[i][(u - k) / s], first L s outputs; optional SnakeBeta on the input
-__global__ void __launch_bounds__(256) voc_convtr_kernel(const float * x, int cin, int L, const float * w,
-                                                         const float * b, int cout, int K, int s, const float * snake_a,
-                                                         const float * snake_b, float * y) {
-    extern __shared__ float sm[];
-    const int Lo = L * s;
-    const int u0 = blockIdx.x * kTile, o0 = blockIdx.y * kTile;
-    // input steps that reach outputs [u0, u0 + 64): t in [(u0 - K + 1) / s, (u0 + 63) / s]
-    const int tlo = max(0, (u0 - K + 1 + s - 1) / s - 1);
-    const int thi = min(L - 1, (u0 + kTile - 1) / s);
-    const int xw = thi - tlo + 1;
-    float * xs = sm;                        // [kCi][128]: xw <= (63 + K) / s + 3 <= 66 for s >= 2, K <= 64
-    float * ws = sm + kCi * (kTile + 64);   // [kCi][K][kTile]
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    float acc[4][4] = {};
-    for (int i0 = 0; i0 < cin; i0 += kCi) {
-        for (int idx = threadIdx.x; idx < kCi * xw; idx += 256) {
-            const int i = idx / xw, j = idx % xw;
-            const int ci = i0 + i, t = tlo + j;
+__device__ __forceinline__ void mma_tf32(float c[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ float snake_beta(float v, float alpha, float beta) {
+    const float s = sinf(v * alpha);
+    return v + (s * s) / beta;
+}
+
+__global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs a) {
+    __shared__ float As[2][kCBM][kCBK + 4];   // weight tile, row = output channel
+    __shared__ float Bs[2][kCBK][kCBN + 8];   // input tile, row = (channel, tap)
+    const int phase = blockIdx.z;
+    const int KD = a.cin * a.taps;
+    const float * W = a.w + (size_t) phase * a.cout * KD;
+    const int t0 = blockIdx.x * kCBN, o0 = blockIdx.y * kCBM;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int nk = (KD + kCBK - 1) / kCBK;
+    float acc[2][4][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; mi++)
+#pragma unroll
+        for (int ni = 0; ni < 4; ni++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[mi][ni][e] = 0.0f;
+    float ra[16], rb[16];
+    // stage reduction tile kt into registers: A rows are contiguous weights (coalesced), B rows
+    // are shifted windows of one input channel (coalesced, zero before t = 0)
+    auto load = [&](int kt) {
+        const int kd0 = kt * kCBK;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int e = tid + kCThreads * j;
+            const int o = o0 + (e >> 5), kd = kd0 + (e & 31);
+            ra[j] = (o < a.cout && kd < KD) ? __ldg(W + (size_t) o * KD + kd) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int e = tid + kCThreads * j;
+            const int kd = kd0 + (e >> 6), t = t0 + (e & 63);
             float v = 0.0f;
-            if (ci < cin && t < L) {
-                v = x[(size_t) ci * L + t];
-                if (snake_a) {
-                    const float sn = sinf(v * snake_a[ci]);
-                    v = v + (sn * sn) / snake_b[ci];
-                }
+            if (kd < KD && t < a.L) {
+                const int i = kd / a.taps, k = kd - i * a.taps;
+                const int ts = t - (a.taps - 1 - k) * a.dil;
+                if (ts >= 0) v = a.x[(size_t) i * a.L + ts];
             }
-            xs[i * (kTile + 64) + j] = v;
+            rb[j] = v;
         }
-        for (int idx = threadIdx.x; idx < kCi * K * kTile; idx += 256) {
-            const int o = idx % kTile, k = (idx / kTile) % K, i = idx / (kTile * K);
-            const int ci = i0 + i, co = o0 + o;
-            ws[idx] = (ci < cin && co < cout) ? w[((size_t) ci * cout + co) * K + k] : 0.0f;
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int e = tid + kCThreads * j;
+            As[buf][e >> 5][e & 31] = ra[j];
+            Bs[buf][e >> 6][e & 63] = rb[j];
         }
-        __syncthreads();
-        for (int i = 0; i < kCi; i++) {
+    };
+    load(0);
+    store(0);
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        const int cur = kt & 1;
+        if (kt + 1 < nk) load(kt + 1);  // the next tile's global loads overlap these MMAs
 #pragma unroll
-            for (int jt = 0; jt < 4; jt++) {
-                const int u = u0 + tx * 4 + jt;
-                for (int k = u % s; k < K; k += s) {
-                    const int t = (u - k) / s;
-                    if (u - k < 0 || t >= L) continue;
-                    const float xv = xs[i * (kTile + 64) + (t - tlo)];
+        for (int kk = 0; kk < kCBK; kk += 8) {
+            uint32_t af[2][4], bf[4][2];
 #pragma unroll
-                    for (int jo = 0; jo < 4; jo++) acc[jo][jt] += ws[(i * K + k) * kTile + ty * 4 + jo] * xv;
-                }
+            for (int mi = 0; mi < 2; mi++) {
+                const int r = wm + mi * 16 + g;
+                af[mi][0] = to_tf32(As[cur][r][kk + t4]);
+                af[mi][1] = to_tf32(As[cur][r + 8][kk + t4]);
+                af[mi][2] = to_tf32(As[cur][r][kk + t4 + 4]);
+                af[mi][3] = to_tf32(As[cur][r + 8][kk + t4 + 4]);
             }
+#pragma unroll
+            for (int ni = 0; ni < 4; ni++) {
+                const int c = wn + ni * 8 + g;
+                bf[ni][0] = to_tf32(Bs[cur][kk + t4][c]);
+                bf[ni][1] = to_tf32(Bs[cur][kk + t4 + 4][c]);
+            }
+#pragma unroll
+            for (int mi = 0; mi < 2; mi++)
+#pragma unroll
+                for (int ni = 0; ni < 4; ni++) mma_tf32(acc[mi][ni], af[mi], bf[ni]);
         }
+        if (kt + 1 < nk) store(cur ^ 1);
         __syncthreads();
     }
 #pragma unroll
-    for (int jo = 0; jo < 4; jo++) {
-        const int co = o0 + ty * 4 + jo;
-        if (co >= cout) continue;
+    for (int mi = 0; mi < 2; mi++) {
 #pragma unroll
-        for (int jt = 0; jt < 4; jt++) {
-            const int u = u0 + tx * 4 + jt;
-            if (u < Lo) y[(size_t) co * Lo + u] = acc[jo][jt] + (b ? b[co] : 0.0f);
+        for (int ni = 0; ni < 4; ni++) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int o = o0 + wm + mi * 16 + g + (e >= 2 ? 8 : 0);
+                const int t = t0 + wn + ni * 8 + 2 * t4 + (e & 1);
+                if (o >= a.cout || t >= a.L) continue;
+                const size_t idx = (size_t) o * a.ldy + (size_t) t * a.ostride + phase;
+                float v = acc[mi][ni][e] + (a.bias ? __ldg(a.bias + o) : 0.0f);
+                if (a.res) v += a.res[idx];
+                float out = a.sa ? snake_beta(v, __ldg(a.sa + o), __ldg(a.sb + o)) : v;
+                if (a.clamp) out = fminf(1.0f, fmaxf(-1.0f, out));
+                a.y[idx] = out;
+                if (a.y2) a.y2[idx] = snake_beta(v, __ldg(a.s2a + o), __ldg(a.s2b + o));
+            }
         }
     }
 }
@@ -316,16 +332,13 @@ __global__ void voc_attn_kernel(const float * q, const float * k, const float * 
     for (int e = 0; e < E; e++) out[((size_t) t * nh + h) * hd + lane + 32 * e] = __float2half_rn(acc[e] / l);
 }
 
-__global__ void voc_clamp_kernel(const float * x, size_t n, float * y) {
-    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x)
-        y[i] = fminf(1.0f, fmaxf(-1.0f, x[i]));
-}
-
 unsigned grid_for(size_t n) { return (unsigned) std::min<size_t>((n + 255) / 256, 148 * 16); }
 
-size_t conv_smem(int K, int dil) { return ((size_t) kCi * (kTile + (K - 1) * dil) + (size_t) kCi * K * kTile) * sizeof(float); }
-size_t convtr_smem(int K) { return ((size_t) kCi * (kTile + 64) + (size_t) kCi * K * kTile) * sizeof(float); }
-constexpr size_t kMaxSmem = 227 * 1024;
+void launch_conv(const ConvArgs & a, int phases, cudaStream_t s) {
+    if (a.L <= 0) return;
+    const dim3 grid((unsigned) ((a.L + kCBN - 1) / kCBN), (unsigned) ((a.cout + kCBM - 1) / kCBM), (unsigned) phases);
+    voc_conv_mma_kernel<<<grid, kCThreads, 0, s>>>(a);
+}
 
 }  // namespace
 
@@ -393,16 +406,41 @@ void Vocoder::linear(const QMat & w, const half * x16, int ldx, int rows, const 
     else launch_umma_gemm(w.u, x16, ldx, rows, out, err_, s, false);
 }
 
-Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int cout, bool transposed) {
+Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int cout, int stride) {
     Conv c;
     c.K = K;
     c.cin = cin;
     c.cout = cout;
+    const bool transposed = stride > 0;
     const GgufTensor & t = need(name + ".weight");
-    if (t.ne.size() != 3 || t.ne[0] != K || t.ne[1] != (transposed ? cout : cin) || t.ne[2] != (transposed ? cin : cout))
-        throw std::runtime_error("vocoder: unexpected shape of " + name + ".weight");
-    c.w = load_f32(name + ".weight", (int64_t) K * cin * cout);
+    if (t.type != GT_F32 || t.ne.size() != 3 || t.ne[0] != K || t.ne[1] != (transposed ? cout : cin) ||
+        t.ne[2] != (transposed ? cin : cout))
+        throw std::runtime_error("vocoder: unexpected shape or type of " + name + ".weight");
     c.b = load_f32(name + ".bias", cout);
+    const float * src = reinterpret_cast<const float *>(gg_.data(t));
+    if (!transposed) {
+        // [cout][cin][K]: each output channel's reduction row is already contiguous
+        c.taps = K;
+        c.phases = 1;
+        c.w = load_f32(name + ".weight", (int64_t) K * cin * cout);
+        return c;
+    }
+    // [cin][cout][K] -> per output phase p: [cout][cin][taps]; the input step t - m meets weight
+    // k = p + m s (zero where k >= K) and sits at tap taps-1-m, so each phase is a causal conv
+    c.stride = stride;
+    c.phases = stride;
+    c.taps = (K + stride - 1) / stride;
+    std::vector<float> h((size_t) stride * cout * cin * c.taps, 0.0f);
+    for (int p = 0; p < stride; p++)
+        for (int o = 0; o < cout; o++)
+            for (int i = 0; i < cin; i++)
+                for (int m = 0; m < c.taps; m++) {
+                    const int k = p + m * stride;
+                    if (k < K) h[(((size_t) p * cout + o) * cin + i) * c.taps + (c.taps - 1 - m)] = src[((size_t) i * cout + o) * K + k];
+                }
+    float * d = dalloc<float>(h.size());
+    VCHECK(cudaMemcpy(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+    c.w = d;
     return c;
 }
 
@@ -428,7 +466,7 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
     cbdim_ = dq_first_out_.M;
     const GgufTensor & pre = need("codec.dpre.conv.weight");
     latent_ = (int) pre.ne[2];
-    dpre_ = load_conv("codec.dpre.conv", (int) pre.ne[0], cbdim_, latent_, false);
+    dpre_ = load_conv("codec.dpre.conv", (int) pre.ne[0], cbdim_, latent_, 0);
     in_proj_ = load_q8("codec.dtf.in_proj.weight");
     in_proj_b_ = load_f32("codec.dtf.in_proj.bias", vc_.hidden);
     for (int l = 0; l < vc_.n_layer; l++) {
@@ -455,7 +493,7 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
         Up u;
         u.ratio = vc_.ratios[i];
         const GgufTensor & ut = need(p + ".up.conv.weight");
-        u.up = load_conv(p + ".up.conv", (int) ut.ne[0], latent_, latent_, true);
+        u.up = load_conv(p + ".up.conv", (int) ut.ne[0], latent_, latent_, u.ratio);
         const GgufTensor & dw = need(p + ".dw.weight");
         u.dw.K = (int) dw.ne[1];
         u.dw.cin = u.dw.cout = latent_;
@@ -472,7 +510,7 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
     }
     const GgufTensor & hd = need("codec.dhead.conv.weight");
     dec_ = (int) hd.ne[2];
-    dhead_ = load_conv("codec.dhead.conv", (int) hd.ne[0], latent_, dec_, false);
+    dhead_ = load_conv("codec.dhead.conv", (int) hd.ne[0], latent_, dec_, 0);
     int ch = dec_;
     for (size_t i = 0; i < vc_.rates.size(); i++) {
         const std::string p = "codec.dblk." + std::to_string(i);
@@ -482,45 +520,35 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
         b.beta = load_f32(p + ".beta", ch, true);
         const GgufTensor & ut = need(p + ".up.conv.weight");
         const int co = (int) ut.ne[1];
-        b.up = load_conv(p + ".up.conv", (int) ut.ne[0], ch, co, true);
+        b.up = load_conv(p + ".up.conv", (int) ut.ne[0], ch, co, b.rate);
         ch = co;
         for (int j = 0; j < 3; j++) {
             const std::string q = p + ".res." + std::to_string(j);
             Res r;
             r.a1 = load_f32(q + ".a1", ch, true);
             r.b1 = load_f32(q + ".b1", ch, true);
-            r.c1 = load_conv(q + ".conv1.conv", (int) need(q + ".conv1.conv.weight").ne[0], ch, ch, false);
+            r.c1 = load_conv(q + ".conv1.conv", (int) need(q + ".conv1.conv.weight").ne[0], ch, ch, 0);
             r.a2 = load_f32(q + ".a2", ch, true);
             r.b2 = load_f32(q + ".b2", ch, true);
-            r.c2 = load_conv(q + ".conv2.conv", (int) need(q + ".conv2.conv.weight").ne[0], ch, ch, false);
+            r.c2 = load_conv(q + ".conv2.conv", (int) need(q + ".conv2.conv.weight").ne[0], ch, ch, 0);
             b.res[j] = r;
         }
         blks_.push_back(b);
     }
     fin_alpha_ = load_f32("codec.dfin.alpha", ch, true);
     fin_beta_ = load_f32("codec.dfin.beta", ch, true);
-    dfin_ = load_conv("codec.dfin.conv", (int) need("codec.dfin.conv.weight").ne[0], ch, 1, false);
+    dfin_ = load_conv("codec.dfin.conv", (int) need("codec.dfin.conv.weight").ne[0], ch, 1, 0);
     int up_total = 1;
     for (int r : vc_.ratios) up_total *= r;
     for (int r : vc_.rates) up_total *= r;
     if (up_total != kSamplesPerFrame)
         throw std::runtime_error("vocoder: the upsampling stages give " + std::to_string(up_total) +
                                  " samples per frame, the C API assumes 1920");
-    // dynamic shared memory of the GEMV and tcgen05 GEMM variants and of the largest convolution
+    // dynamic shared memory of the GEMV and tcgen05 GEMM variants
     init_kernel_attributes();
     init_umma_attributes();
     err_ = dalloc<int>(1);
     VCHECK(cudaMemset(err_, 0, sizeof(int)));
-    size_t conv_mx = conv_smem(std::max({ dpre_.K, dhead_.K, dfin_.K }), 1), convtr_mx = 0;
-    for (const Up & u : ups_) convtr_mx = std::max(convtr_mx, convtr_smem(u.up.K));
-    for (const Blk & b : blks_) {
-        convtr_mx = std::max(convtr_mx, convtr_smem(b.up.K));
-        for (int j = 0; j < 3; j++)
-            conv_mx = std::max({ conv_mx, conv_smem(b.res[j].c1.K, 9), conv_smem(b.res[j].c2.K, 1) });
-    }
-    if (conv_mx > kMaxSmem || convtr_mx > kMaxSmem) throw std::runtime_error("vocoder: convolution kernel too long");
-    VCHECK(cudaFuncSetAttribute(voc_conv1d_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) conv_mx));
-    VCHECK(cudaFuncSetAttribute(voc_convtr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) convtr_mx));
     scr_.ws_elems = (size_t) 1 << 20;
     scr_.ws = dalloc<float4>(scr_.ws_elems);
     scr_.n_counters = 4096;
@@ -609,21 +637,24 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
     auto transpose = [&](const float * in, int R, int C, float * out, const float * add) {
         voc_transpose_kernel<<<dim3((C + 31) / 32, (R + 31) / 32), dim3(32, 8), 0, s>>>(in, R, C, out, add);
     };
-    auto conv = [&](const Conv & c, const float * x, int L, int dil, const float * sa, const float * sb, const float * res,
-                    float * y) {
-        const size_t smem = conv_smem(c.K, dil);
-        voc_conv1d_kernel<<<dim3((L + kTile - 1) / kTile, (c.cout + kTile - 1) / kTile), 256, smem, s>>>(
-            x, c.cin, L, c.w, c.b, c.cout, c.K, dil, sa, sb, res, y);
-    };
-    auto convtr = [&](const Conv & c, const float * x, int L, int stride, const float * sa, const float * sb, float * y) {
-        // the staged input window holds (64 + K) / stride + 3 steps, within its 128-float rows
-        if (c.K > 64 || stride < 2 || stride > 16) throw std::runtime_error("vocoder: transposed conv needs stride 2..16 and K <= 64");
-        const size_t smem = convtr_smem(c.K);
-        voc_convtr_kernel<<<dim3((L * stride + kTile - 1) / kTile, (c.cout + kTile - 1) / kTile), 256, smem, s>>>(
-            x, c.cin, L, c.w, c.b, c.cout, c.K, stride, sa, sb, y);
+    // one causal conv (or the phases of a transposed conv) over x [cin][L]; the output
+    // [cout][L * phases] holds v = conv + bias (+ res), or SnakeBeta(v) with (sa, sb); y2, when
+    // given, receives SnakeBeta(v) with (s2a, s2b)
+    struct Act { const float * a = nullptr, * b = nullptr; };
+    auto conv = [&](const Conv & c, const float * x, int L, int dil, float * y, Act act = {}, const float * res = nullptr,
+                    float * y2 = nullptr, Act act2 = {}, bool clamp = false) {
+        ConvArgs ca;
+        ca.x = x; ca.cin = c.cin; ca.L = L;
+        ca.w = c.w; ca.taps = c.taps; ca.dil = dil;
+        ca.bias = c.b; ca.cout = c.cout;
+        ca.y = y; ca.ldy = L * c.phases; ca.ostride = c.phases;
+        ca.res = res; ca.sa = act.a; ca.sb = act.b;
+        ca.y2 = y2; ca.s2a = act2.a; ca.s2b = act2.b;
+        ca.clamp = clamp ? 1 : 0;
+        launch_conv(ca, c.phases, s);
     };
     transpose(t32_, T, cbdim_, a_, nullptr);
-    conv(dpre_, a_, T, 1, nullptr, nullptr, nullptr, b_);           // [latent][T]
+    conv(dpre_, a_, T, 1, b_);                                       // [latent][T]
 
     // transformer on [T][latent] rows
     transpose(b_, latent_, T, a_, nullptr);                          // a_ = [T][latent]
@@ -658,7 +689,7 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
     float * x = a_;
     float * y = b_;
     for (const Up & u : ups_) {
-        convtr(u.up, x, L, u.ratio, nullptr, nullptr, y);
+        conv(u.up, x, L, 1, y);
         L *= u.ratio;
         std::swap(x, y);                                             // x = [latent][L]
         const size_t n = (size_t) L * latent_;
@@ -673,25 +704,32 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
         transpose(t32_, L, latent_, y, x);                           // y = x + branch^T
         std::swap(x, y);
     }
-    conv(dhead_, x, L, 1, nullptr, nullptr, nullptr, y);
-    std::swap(x, y);                                                 // [dec][L]
+    // SEANet decoder (src/codec_decoder.cpp:80-97). Every SnakeBeta is applied by the conv that
+    // produces its input: Xb holds a block's residual stream, Sb the SnakeBeta of it that the
+    // next conv reads, Hb the first conv of a residual unit (already SnakeBeta'd for the second).
+    // The second conv of a unit adds Xb in place and also writes the next activation into Sb.
+    float * Xb = c_, * Sb = y, * Hb = x;
+    auto next_act = [&](size_t bi, int j) -> Act {
+        if (j + 1 < 3) return { blks_[bi].res[j + 1].a1, blks_[bi].res[j + 1].b1 };
+        if (bi + 1 < blks_.size()) return { blks_[bi + 1].alpha, blks_[bi + 1].beta };
+        return { fin_alpha_, fin_beta_ };
+    };
+    if (blks_.empty()) throw std::runtime_error("vocoder: the decoder has no upsampling blocks");
+    conv(dhead_, x, L, 1, Sb, { blks_[0].alpha, blks_[0].beta });
     const int dil[3] = { 1, 3, 9 };
-    float * z = c_;                                                  // third buffer of the residual units
-    for (const Blk & b : blks_) {
-        // SnakeBeta fused into the transposed conv's input staging
-        convtr(b.up, x, L, b.rate, b.alpha, b.beta, y);
+    for (size_t bi = 0; bi < blks_.size(); bi++) {
+        const Blk & b = blks_[bi];
+        conv(b.up, Sb, L, 1, Xb, {}, nullptr, Hb, { b.res[0].a1, b.res[0].b1 });
         L *= b.rate;
-        std::swap(x, y);
+        std::swap(Sb, Hb);
         for (int j = 0; j < 3; j++) {
             const Res & r = b.res[j];
-            conv(r.c1, x, L, dil[j], r.a1, r.b1, nullptr, y);
-            conv(r.c2, y, L, 1, r.a2, r.b2, x, z);                   // residual add of x
-            std::swap(x, z);
+            conv(r.c1, Sb, L, dil[j], Hb, { r.a2, r.b2 });
+            conv(r.c2, Hb, L, 1, Xb, {}, Xb, Sb, next_act(bi, j));
         }
     }
-    conv(dfin_, x, L, 1, fin_alpha_, fin_beta_, nullptr, y);
     if (L != T * kSamplesPerFrame) throw std::runtime_error("vocoder: unexpected output length");
-    voc_clamp_kernel<<<grid_for((size_t) L), 256, 0, s>>>(y, (size_t) L, pcm_);
+    conv(dfin_, Sb, L, 1, pcm_, {}, nullptr, nullptr, {}, true);
     VCHECK(cudaGetLastError());
     VCHECK(cudaMemcpyAsync(pcm, pcm_, (size_t) L * sizeof(float), cudaMemcpyDeviceToHost, s));
     int err = 0;

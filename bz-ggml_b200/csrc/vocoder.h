@@ -40,9 +40,12 @@ public:
 
 private:
     struct Conv {
-        float * w = nullptr;  // [Cout][Cin][K] (transposed convs [Cin][Cout][K]; depthwise [K][C])
+        // [phases][Cout][Cin][taps]: a conv has one phase of K taps; a stride-s transposed conv
+        // has s phases of ceil(K / s) taps (depthwise: [K][C])
+        float * w = nullptr;
         float * b = nullptr;
         int cin = 0, cout = 0, K = 0;
+        int taps = 0, phases = 1, stride = 0;
     };
     struct Layer {
         QMat q, k, v, o, gate, up, down;
@@ -69,7 +72,8 @@ private:
     float * load_f32(const std::string & name, int64_t expect, bool exp_of = false);
     QMat load_q8(const std::string & name);  // Q8_0 (mma.sync layout) or Q4_K (tcgen05 layout)
     void linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s);
-    Conv load_conv(const std::string & name, int K, int cin, int cout, bool transposed);
+    // stride 0: a causal conv; stride s > 0: a transposed conv, split into s phase convs
+    Conv load_conv(const std::string & name, int K, int cin, int cout, int stride);
     void ensure(int T);
     template <class T> T * dalloc(size_t n);
 
