@@ -344,6 +344,8 @@ def main():
     b_step = gen.weight_bytes_per_step() + float(kv_pos * live_ctx.sum())
     step_gbs = b_step / (step_ms / 1e3) / 1e9
     cpu = None
+    if barrier:
+        barrier()  # every rank's GPU work is done: the CPU port gets the host's cores to itself
     if rank == 0 and not args.no_cpu_baseline:
         try:
             v, dt, cores = cpu_oracle_rtf(path, args.cpu_sample_sessions, 3, 1)

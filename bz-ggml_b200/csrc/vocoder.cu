@@ -65,19 +65,23 @@ __global__ void voc_transpose_kernel(const float * in, int R, int C, float * out
 }
 
 // Causal convolutions as TF32 tensor-core implicit GEMMs (mma.sync m16n8k8):
-//   y[o][t] = b[o] + sum_{i,k} W[o][i*taps + k] * x[i][t - (taps-1-k) dil]
-// M = output channels, N = time, reduction = cin * taps, im2col done while staging the input
-// tile. A stride-s transposed conv (src/codec_conv.cpp:25-32) is s such convolutions with 2 taps
-// each, one per output phase p: y[o][s t + p] = b[o] + sum_{i,m} w[i][o][p + m s] x[i][t - m]
-// (blockIdx.z = phase; the phase weights are re-laid out at load). The epilogue adds the bias and
-// an optional residual, then stores the value or its SnakeBeta (and optionally a second,
-// SnakeBeta-activated copy for the next consumer), clamped to [-1, 1] for the final PCM.
-constexpr int kCBM = 64, kCBN = 64, kCBK = 32, kCThreads = 128;
+//   y[o][t] = b[o] + sum_{k,i} W[o][k][i] * x[i][t - (taps-1-k) dil]
+// M = output channels, N = time, reduction = taps x input channels, ordered as 32-channel
+// chunks outer and taps inner. Each chunk's input window x[i][t0 - halo .. t0 + 63] is staged in
+// shared memory once and every tap reads its shifted view of it, so the im2col is free. The
+// weights are laid out tap-major at load, so a (tap, chunk) weight tile is 64 rows of 32
+// contiguous floats. A stride-s transposed conv (src/codec_conv.cpp:25-32) is s such convs with
+// 2 taps, one per output phase p: y[o][s t + p] = b[o] + sum_{i,m} w[i][o][p + m s] x[i][t - m].
+// When the grid is small (a few frames) the channel chunks are split across CTAs, which write
+// partial sums that a second kernel adds. The epilogue (bias, optional residual, SnakeBeta of
+// the stored value and/or of a second copy for the next consumer, PCM clamp) runs in whichever
+// kernel finishes the sum.
+constexpr int kCBM = 64, kCBN = 64, kCCI = 32, kCThreads = 128;
 
 struct ConvArgs {
     const float * x = nullptr;          // input [cin][L]
     int cin = 0, L = 0;
-    const float * w = nullptr;          // [phases][cout][cin * taps]
+    const float * w = nullptr;          // [phases][cout][taps][cin]
     int taps = 1, dil = 1;
     const float * bias = nullptr;
     int cout = 0;
@@ -88,6 +92,11 @@ struct ConvArgs {
     float * y2 = nullptr;               // second output: SnakeBeta(value) with (s2a, s2b), or null
     const float * s2a = nullptr, * s2b = nullptr;
     int clamp = 0;
+    // split of the input channels over blockIdx.z / phases (1: no split); partial sums go to
+    // part[split][o * ldy + t * ostride + phase]
+    int splits = 1, ci_per_split = 0;
+    float * part = nullptr;
+    int lxp = 0;                        // staged window row stride (floats)
 };
 
 __device__ __forceinline__ uint32_t to_tf32(float f) {
@@ -107,17 +116,29 @@ __device__ __forceinline__ float snake_beta(float v, float alpha, float beta) {
     return v + (s * s) / beta;
 }
 
+__device__ __forceinline__ void conv_epilogue(const ConvArgs & a, int o, size_t idx, float v) {
+    v += a.bias ? __ldg(a.bias + o) : 0.0f;
+    if (a.res) v += a.res[idx];
+    float out = a.sa ? snake_beta(v, __ldg(a.sa + o), __ldg(a.sb + o)) : v;
+    if (a.clamp) out = fminf(1.0f, fmaxf(-1.0f, out));
+    a.y[idx] = out;
+    if (a.y2) a.y2[idx] = snake_beta(v, __ldg(a.s2a + o), __ldg(a.s2b + o));
+}
+
 __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs a) {
-    __shared__ float As[2][kCBM][kCBK + 4];   // weight tile, row = output channel
-    __shared__ float Bs[2][kCBK][kCBN + 8];   // input tile, row = (channel, tap)
-    const int phase = blockIdx.z;
-    const int KD = a.cin * a.taps;
-    const float * W = a.w + (size_t) phase * a.cout * KD;
+    extern __shared__ float csm[];
+    constexpr int kAld = kCCI + 4;
+    float * As = csm;                                   // [2][kCBM][kAld]: weight tile of one tap
+    float * xs = csm + 2 * kCBM * kAld;                 // [kCCI][lxp]: input window of one chunk
+    const int phases = a.ostride;
+    const int phase = blockIdx.z % phases, split = blockIdx.z / phases;
+    const int ci_beg = split * a.ci_per_split, ci_end = min(a.cin, ci_beg + a.ci_per_split);
+    const float * W = a.w + (size_t) phase * a.cout * a.taps * a.cin;
     const int t0 = blockIdx.x * kCBN, o0 = blockIdx.y * kCBM;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
     const int g = lane >> 2, t4 = lane & 3;
-    const int nk = (KD + kCBK - 1) / kCBK;
+    const int halo = (a.taps - 1) * a.dil, lx = kCBN + halo;
     float acc[2][4][4];
 #pragma unroll
     for (int mi = 0; mi < 2; mi++)
@@ -125,68 +146,82 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
         for (int ni = 0; ni < 4; ni++)
 #pragma unroll
             for (int e = 0; e < 4; e++) acc[mi][ni][e] = 0.0f;
-    float ra[16], rb[16];
-    // stage reduction tile kt into registers: A rows are contiguous weights (coalesced), B rows
-    // are shifted windows of one input channel (coalesced, zero before t = 0)
-    auto load = [&](int kt) {
-        const int kd0 = kt * kCBK;
+    const int n_chunks = max(0, (ci_end - ci_beg + kCCI - 1) / kCCI);
+    const int n_iter = n_chunks * a.taps;  // (chunk, tap) steps
+    float4 ra[4];
+    // weight tile of step it: rows o0.., tap k, channels c0..c0+31 (8 float4 per row)
+    auto load_a = [&](int it) {
+        const int c0 = ci_beg + (it / a.taps) * kCCI, k = it % a.taps;
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const int e = tid + kCThreads * j;
-            const int o = o0 + (e >> 5), kd = kd0 + (e & 31);
-            ra[j] = (o < a.cout && kd < KD) ? __ldg(W + (size_t) o * KD + kd) : 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const int e = tid + kCThreads * j;
-            const int kd = kd0 + (e >> 6), t = t0 + (e & 63);
-            float v = 0.0f;
-            if (kd < KD && t < a.L) {
-                const int i = kd / a.taps, k = kd - i * a.taps;
-                const int ts = t - (a.taps - 1 - k) * a.dil;
-                if (ts >= 0) v = a.x[(size_t) i * a.L + ts];
+        for (int j = 0; j < 4; j++) {
+            const int e = tid + kCThreads * j;          // 512 float4 of the 64 x 32 tile
+            const int r = e >> 3, c = (e & 7) * 4;
+            const int o = o0 + r, ci = c0 + c;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (o < a.cout) {
+                const float * src = W + ((size_t) o * a.taps + k) * a.cin + ci;
+                if (ci + 3 < ci_end && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
+                    v = __ldg(reinterpret_cast<const float4 *>(src));
+                } else {
+                    if (ci < ci_end) v.x = __ldg(src);
+                    if (ci + 1 < ci_end) v.y = __ldg(src + 1);
+                    if (ci + 2 < ci_end) v.z = __ldg(src + 2);
+                    if (ci + 3 < ci_end) v.w = __ldg(src + 3);
+                }
             }
-            rb[j] = v;
+            ra[j] = v;
         }
     };
-    auto store = [&](int buf) {
+    auto store_a = [&](int buf) {
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < 4; j++) {
             const int e = tid + kCThreads * j;
-            As[buf][e >> 5][e & 31] = ra[j];
-            Bs[buf][e >> 6][e & 63] = rb[j];
+            *reinterpret_cast<float4 *>(As + ((size_t) buf * kCBM + (e >> 3)) * kAld + (e & 7) * 4) = ra[j];
         }
     };
-    load(0);
-    store(0);
-    __syncthreads();
-    for (int kt = 0; kt < nk; kt++) {
-        const int cur = kt & 1;
-        if (kt + 1 < nk) load(kt + 1);  // the next tile's global loads overlap these MMAs
+    if (n_iter > 0) {
+        load_a(0);
+        store_a(0);
+    }
+    for (int it = 0; it < n_iter; it++) {
+        const int k = it % a.taps, cur = it & 1;
+        if (k == 0) {
+            // a new channel chunk: stage its input window (zero before t = 0 and past the chunk)
+            __syncthreads();  // every warp is done with the previous window
+            const int c0 = ci_beg + (it / a.taps) * kCCI;
+            for (int e = tid; e < kCCI * lx; e += kCThreads) {
+                const int i = e / lx, u = e - i * lx;
+                const int ci = c0 + i, t = t0 - halo + u;
+                xs[i * a.lxp + u] = (ci < ci_end && t >= 0 && t < a.L) ? a.x[(size_t) ci * a.L + t] : 0.0f;
+            }
+        }
+        __syncthreads();  // weight tile `cur` and the window are in place
+        if (it + 1 < n_iter) load_a(it + 1);  // next tile's global loads overlap these MMAs
+        const float * At = As + (size_t) cur * kCBM * kAld;
+        const int shift = halo - (a.taps - 1 - k) * a.dil;  // window column of output t0 for tap k
 #pragma unroll
-        for (int kk = 0; kk < kCBK; kk += 8) {
+        for (int kk = 0; kk < kCCI; kk += 8) {
             uint32_t af[2][4], bf[4][2];
 #pragma unroll
             for (int mi = 0; mi < 2; mi++) {
                 const int r = wm + mi * 16 + g;
-                af[mi][0] = to_tf32(As[cur][r][kk + t4]);
-                af[mi][1] = to_tf32(As[cur][r + 8][kk + t4]);
-                af[mi][2] = to_tf32(As[cur][r][kk + t4 + 4]);
-                af[mi][3] = to_tf32(As[cur][r + 8][kk + t4 + 4]);
+                af[mi][0] = to_tf32(At[r * kAld + kk + t4]);
+                af[mi][1] = to_tf32(At[(r + 8) * kAld + kk + t4]);
+                af[mi][2] = to_tf32(At[r * kAld + kk + t4 + 4]);
+                af[mi][3] = to_tf32(At[(r + 8) * kAld + kk + t4 + 4]);
             }
 #pragma unroll
             for (int ni = 0; ni < 4; ni++) {
-                const int c = wn + ni * 8 + g;
-                bf[ni][0] = to_tf32(Bs[cur][kk + t4][c]);
-                bf[ni][1] = to_tf32(Bs[cur][kk + t4 + 4][c]);
+                const int col = wn + ni * 8 + g + shift;
+                bf[ni][0] = to_tf32(xs[(kk + t4) * a.lxp + col]);
+                bf[ni][1] = to_tf32(xs[(kk + t4 + 4) * a.lxp + col]);
             }
 #pragma unroll
             for (int mi = 0; mi < 2; mi++)
 #pragma unroll
                 for (int ni = 0; ni < 4; ni++) mma_tf32(acc[mi][ni], af[mi], bf[ni]);
         }
-        if (kt + 1 < nk) store(cur ^ 1);
-        __syncthreads();
+        if (it + 1 < n_iter) store_a(cur ^ 1);  // the other buffer was last read before this step's barrier
     }
 #pragma unroll
     for (int mi = 0; mi < 2; mi++) {
@@ -198,14 +233,20 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
                 const int t = t0 + wn + ni * 8 + 2 * t4 + (e & 1);
                 if (o >= a.cout || t >= a.L) continue;
                 const size_t idx = (size_t) o * a.ldy + (size_t) t * a.ostride + phase;
-                float v = acc[mi][ni][e] + (a.bias ? __ldg(a.bias + o) : 0.0f);
-                if (a.res) v += a.res[idx];
-                float out = a.sa ? snake_beta(v, __ldg(a.sa + o), __ldg(a.sb + o)) : v;
-                if (a.clamp) out = fminf(1.0f, fmaxf(-1.0f, out));
-                a.y[idx] = out;
-                if (a.y2) a.y2[idx] = snake_beta(v, __ldg(a.s2a + o), __ldg(a.s2b + o));
+                if (a.splits > 1) a.part[(size_t) split * a.cout * a.ldy + idx] = acc[mi][ni][e];
+                else conv_epilogue(a, o, idx, acc[mi][ni][e]);
             }
         }
+    }
+}
+
+// sums the channel-split partials in split order and applies the epilogue
+__global__ void voc_conv_reduce_kernel(const ConvArgs a) {
+    const size_t n = (size_t) a.cout * a.ldy;
+    for (size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (size_t) gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        for (int sp = 0; sp < a.splits; sp++) v += a.part[(size_t) sp * n + idx];
+        conv_epilogue(a, (int) (idx / a.ldy), idx, v);
     }
 }
 
@@ -334,10 +375,34 @@ __global__ void voc_attn_kernel(const float * q, const float * k, const float * 
 
 unsigned grid_for(size_t n) { return (unsigned) std::min<size_t>((n + 255) / 256, 148 * 16); }
 
-void launch_conv(const ConvArgs & a, int phases, cudaStream_t s) {
+size_t conv_smem_bytes(int lxp) { return ((size_t) 2 * kCBM * (kCCI + 4) + (size_t) kCCI * lxp) * sizeof(float); }
+int conv_lxp(int taps, int dil) {
+    // window row stride: at least 64 + halo, and 8 mod 32 so that the 4 x 8 B-fragment reads
+    // of a warp fall in distinct banks
+    const int lx = kCBN + (taps - 1) * dil;
+    return (lx + 23) / 32 * 32 + 8;
+}
+
+// `a` with x, w, y, ... set; fills the launch shape (and the channel split when the grid would
+// leave SMs idle and the scratch can hold the partials)
+void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats, cudaStream_t s) {
     if (a.L <= 0) return;
-    const dim3 grid((unsigned) ((a.L + kCBN - 1) / kCBN), (unsigned) ((a.cout + kCBM - 1) / kCBM), (unsigned) phases);
-    voc_conv_mma_kernel<<<grid, kCThreads, 0, s>>>(a);
+    const int tiles = ((a.L + kCBN - 1) / kCBN) * ((a.cout + kCBM - 1) / kCBM) * phases;
+    const int chunks = (a.cin + kCCI - 1) / kCCI;
+    int splits = 1;
+    while (tiles * splits * 2 <= 2 * 148 && splits * 2 <= chunks && splits < 16 &&
+           (size_t) splits * 2 * a.cout * a.ldy <= scratch_floats)
+        splits *= 2;
+    a.splits = splits;
+    a.ci_per_split = ((chunks + splits - 1) / splits) * kCCI;
+    a.part = scratch;
+    a.lxp = conv_lxp(a.taps, a.dil);
+    const dim3 grid((unsigned) ((a.L + kCBN - 1) / kCBN), (unsigned) ((a.cout + kCBM - 1) / kCBM), (unsigned) (phases * splits));
+    voc_conv_mma_kernel<<<grid, kCThreads, conv_smem_bytes(a.lxp), s>>>(a);
+    if (splits > 1) {
+        const size_t n = (size_t) a.cout * a.ldy;
+        voc_conv_reduce_kernel<<<(unsigned) std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(a);
+    }
 }
 
 }  // namespace
@@ -419,14 +484,21 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
     c.b = load_f32(name + ".bias", cout);
     const float * src = reinterpret_cast<const float *>(gg_.data(t));
     if (!transposed) {
-        // [cout][cin][K]: each output channel's reduction row is already contiguous
+        // [cout][cin][K] -> tap-major [cout][K][cin]
         c.taps = K;
         c.phases = 1;
-        c.w = load_f32(name + ".weight", (int64_t) K * cin * cout);
+        std::vector<float> h((size_t) cout * K * cin);
+        for (int o = 0; o < cout; o++)
+            for (int i = 0; i < cin; i++)
+                for (int k = 0; k < K; k++) h[((size_t) o * K + k) * cin + i] = src[((size_t) o * cin + i) * K + k];
+        float * d = dalloc<float>(h.size());
+        VCHECK(cudaMemcpy(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+        c.w = d;
         return c;
     }
-    // [cin][cout][K] -> per output phase p: [cout][cin][taps]; the input step t - m meets weight
-    // k = p + m s (zero where k >= K) and sits at tap taps-1-m, so each phase is a causal conv
+    // [cin][cout][K] -> per output phase p: tap-major [cout][taps][cin]; the input step t - m
+    // meets weight k = p + m s (zero where k >= K) and sits at tap taps-1-m, so each phase is a
+    // causal conv
     c.stride = stride;
     c.phases = stride;
     c.taps = (K + stride - 1) / stride;
@@ -436,7 +508,7 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
             for (int i = 0; i < cin; i++)
                 for (int m = 0; m < c.taps; m++) {
                     const int k = p + m * stride;
-                    if (k < K) h[(((size_t) p * cout + o) * cin + i) * c.taps + (c.taps - 1 - m)] = src[((size_t) i * cout + o) * K + k];
+                    if (k < K) h[(((size_t) p * cout + o) * c.taps + (c.taps - 1 - m)) * cin + i] = src[((size_t) i * cout + o) * K + k];
                 }
     float * d = dalloc<float>(h.size());
     VCHECK(cudaMemcpy(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -544,9 +616,21 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
     if (up_total != kSamplesPerFrame)
         throw std::runtime_error("vocoder: the upsampling stages give " + std::to_string(up_total) +
                                  " samples per frame, the C API assumes 1920");
-    // dynamic shared memory of the GEMV and tcgen05 GEMM variants
+    // dynamic shared memory of the GEMV and tcgen05 GEMM variants and of the widest conv window
     init_kernel_attributes();
     init_umma_attributes();
+    {
+        int lxp = conv_lxp(std::max({ dpre_.taps, dhead_.taps, dfin_.taps }), 1);
+        for (const Up & u : ups_) lxp = std::max(lxp, conv_lxp(u.up.taps, 1));
+        const int dil_max[3] = { 1, 3, 9 };
+        for (const Blk & b : blks_) {
+            lxp = std::max(lxp, conv_lxp(b.up.taps, 1));
+            for (int j = 0; j < 3; j++)
+                lxp = std::max({ lxp, conv_lxp(b.res[j].c1.taps, dil_max[j]), conv_lxp(b.res[j].c2.taps, 1) });
+        }
+        if (conv_smem_bytes(lxp) > 227 * 1024) throw std::runtime_error("vocoder: convolution window too wide");
+        VCHECK(cudaFuncSetAttribute(voc_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) conv_smem_bytes(lxp)));
+    }
     err_ = dalloc<int>(1);
     VCHECK(cudaMemset(err_, 0, sizeof(int)));
     scr_.ws_elems = (size_t) 1 << 20;
@@ -594,6 +678,7 @@ void Vocoder::ensure(int T) {
     a_ = fa(act_elems_);
     b_ = fa(act_elems_);
     c_ = fa(act_elems_);
+    part_ = fa(2 * act_elems_);
     t32_ = fa(up_rows * wide);
     q_ = fa(Tc * vc_.n_head * vc_.hd);
     k_ = fa(Tc * vc_.n_kv * vc_.hd);
@@ -651,7 +736,7 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
         ca.res = res; ca.sa = act.a; ca.sb = act.b;
         ca.y2 = y2; ca.s2a = act2.a; ca.s2b = act2.b;
         ca.clamp = clamp ? 1 : 0;
-        launch_conv(ca, c.phases, s);
+        launch_conv(ca, c.phases, part_, 2 * act_elems_, s);
     };
     transpose(t32_, T, cbdim_, a_, nullptr);
     conv(dpre_, a_, T, 1, b_);                                       // [latent][T]

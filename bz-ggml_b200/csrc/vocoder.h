@@ -40,8 +40,8 @@ public:
 
 private:
     struct Conv {
-        // [phases][Cout][Cin][taps]: a conv has one phase of K taps; a stride-s transposed conv
-        // has s phases of ceil(K / s) taps (depthwise: [K][C])
+        // [phases][Cout][taps][Cin] (tap-major): a conv has one phase of K taps; a stride-s
+        // transposed conv has s phases of ceil(K / s) taps (depthwise: [K][C])
         float * w = nullptr;
         float * b = nullptr;
         int cin = 0, cout = 0, K = 0;
@@ -107,6 +107,7 @@ private:
     float * a_ = nullptr, * b_ = nullptr, * c_ = nullptr;   // conv-stack ping-pong [C][L]
     float * t32_ = nullptr, * q_ = nullptr, * k_ = nullptr, * v_ = nullptr, * o_ = nullptr;
     float * g_ = nullptr, * u_ = nullptr, * pcm_ = nullptr;
+    float * part_ = nullptr;  // channel-split partial sums of the convolutions
     half * t16_ = nullptr, * att16_ = nullptr, * f16_ = nullptr;
     int * codes_ = nullptr;
 
