@@ -115,6 +115,8 @@ SIGNATURES = {
                                           ctypes.c_void_p, _c_int_p, ctypes.c_int, _c_int_p, _c_double_p]),
     "bzb_split_text": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]),
     "bzb_write_wav": (ctypes.c_int, [ctypes.c_char_p, _c_float_p, ctypes.c_int, ctypes.c_int]),
+    "bzb_generator_encode_audio_full": (ctypes.c_int, [ctypes.c_void_p, _c_float_p, ctypes.c_int, _c_int_p, ctypes.c_int,
+                                                       _c_int_p]),
 }
 
 
@@ -330,6 +332,30 @@ class GeneratorHandle:
             raise RuntimeError(self.lib.last_error())
         return codes, logits
 
+    def encode_audio(self, pcm_samples) -> Tuple[List[int], int]:
+        """24 kHz mono PCM -> (codes, n_frames), min(num_codebooks, 16) codes per frame
+        (mirrors bz_ggml.bindings.GeneratorHandle.encode_audio)."""
+        x = np.ascontiguousarray(np.asarray(pcm_samples, np.float32))
+        if x.size == 0:
+            return [], 0
+        w = min(self.nc, 16)
+        out = np.zeros((x.size // 1920 + 64) * w, np.int32)
+        nf = ctypes.c_int(0)
+        res = self.lib.lib.breeze_generator_encode_audio(self.handle, _fp(x), x.size, _ip(out), ctypes.byref(nf))
+        if res < 0:
+            raise RuntimeError(f"Audio encoding failed on Generator (device {self.device}): {self.lib.last_error()}")
+        return out[: nf.value * w].tolist(), nf.value
+
+    def encode_audio_full(self, pcm_samples) -> np.ndarray:
+        """All num_codebooks codes per frame: [n_frames][num_codebooks] int32."""
+        x = np.ascontiguousarray(np.asarray(pcm_samples, np.float32))
+        mf = x.size // 1920
+        out = np.zeros((max(mf, 1), self.nc), np.int32)
+        nf = ctypes.c_int(0)
+        if self.lib.lib.bzb_generator_encode_audio_full(self.handle, _fp(x), x.size, _ip(out), mf, ctypes.byref(nf)) < 0:
+            raise RuntimeError(self.lib.last_error())
+        return out[: nf.value]
+
     def load_q4_depth(self, q4_model_path: str) -> bool:
         """The Q4_K depth override (dd.* of a second GGUF) for flagged sessions."""
         if self.lib.lib.breeze_generator_load_q4_depth(self.handle, q4_model_path.encode("utf-8")) != 0:
@@ -428,10 +454,15 @@ class ContextHandle:
     @staticmethod
     def request(text: str, instruction: Optional[str] = None, ref_text: Optional[str] = None, cfg_scale: float = 0.0,
                 seed: int = 42, max_new_tokens: int = 0, split_chars: int = 0, temperature: float = 0.0,
-                top_k: int = 0, top_p: float = 0.0, repetition_penalty: float = 0.0) -> BreezeRequest:
+                top_k: int = 0, top_p: float = 0.0, repetition_penalty: float = 0.0,
+                ref_audio: Optional[np.ndarray] = None) -> BreezeRequest:
         enc = lambda x: None if x is None else x.encode("utf-8")
-        return BreezeRequest(enc(text), enc(instruction), enc(ref_text), None, 0, cfg_scale, seed, max_new_tokens,
-                             split_chars, temperature, top_k, top_p, repetition_penalty)
+        ra = None if ref_audio is None else np.ascontiguousarray(ref_audio, np.float32)
+        r = BreezeRequest(enc(text), enc(instruction), enc(ref_text), None if ra is None else _fp(ra),
+                          0 if ra is None else ra.size, cfg_scale, seed, max_new_tokens, split_chars, temperature,
+                          top_k, top_p, repetition_penalty)
+        r._keep = ra  # the PCM must outlive the request
+        return r
 
     def generate(self, req: BreezeRequest, stop_after_chunks: int = 0, ref_codes: Optional[np.ndarray] = None,
                  max_frames: int = 4096):

@@ -20,6 +20,11 @@
 struct breeze_generator {
     std::unique_ptr<bzb::Engine> eng;
     int device = 0;
+    std::unique_ptr<bzb::CodecEncoder> enc;  // built on first use (encode_audio)
+    bzb::CodecEncoder & encoder() {
+        if (!enc) enc = std::make_unique<bzb::CodecEncoder>(eng->gguf(), eng->cfg, device);
+        return *enc;
+    }
 };
 
 // a vocoder either owns its model file (breeze_vocoder_init) or decodes with the weights of a
@@ -65,6 +70,15 @@ bzb::GenRequest to_gen_request(const breeze_request * r) {
     return g;
 }
 
+// a reference clip with its transcript becomes encoded reference codes (src/generation.cpp:219-228)
+void encode_ref_audio(breeze_context * ctx, bzb::GenRequest & g) {
+    if (!g.ref_codes.empty() || g.ref_audio.empty() || g.ref_text.empty()) return;
+    std::vector<int> codes;
+    g.ref_frames = ctx->gen->encoder().encode(g.ref_audio.data(), (int) g.ref_audio.size(), codes);
+    g.ref_codes = std::move(codes);
+    g.ref_audio.clear();
+}
+
 // breeze_generate with optional encoded reference codes, the generated frames and stage timings
 int generate_impl(breeze_context * ctx, const breeze_request * req, const int * ref_codes, int ref_frames,
                   breeze_audio_cb cb, void * user, int * out_codes, int max_frames, int * out_n_frames,
@@ -74,6 +88,7 @@ int generate_impl(breeze_context * ctx, const breeze_request * req, const int * 
         bzb::GenRequest g = to_gen_request(req);
         const int nc = ctx->gen->eng->cfg.nc;
         if (ref_codes && ref_frames > 0) g.ref_codes.assign(ref_codes, ref_codes + (size_t) ref_frames * nc), g.ref_frames = ref_frames;
+        encode_ref_audio(ctx, g);
         std::vector<int> codes;
         bzb::GenTimings tm;
         bzb::generate(*ctx->gen->eng, *ctx->voc, g, [&](const float * s, int n) { return cb ? cb(s, n, user) == 0 : true; },
@@ -157,7 +172,8 @@ int breeze_generate_wav(breeze_context * ctx, const breeze_request * req, const 
     if (!ctx || !req || !out_path) { set_error("null argument"); return 1; }
     try {
         std::vector<float> audio;
-        const bzb::GenRequest g = to_gen_request(req);
+        bzb::GenRequest g = to_gen_request(req);
+        encode_ref_audio(ctx, g);
         bzb::generate(*ctx->gen->eng, *ctx->voc, g, [&](const float * s, int n) {
             audio.insert(audio.end(), s, s + n);
             return true;
@@ -340,8 +356,19 @@ int breeze_generator_convert_voice(breeze_generator * gen, const int * src_codes
 int breeze_generator_encode_audio(breeze_generator * gen, const float * pcm, int n_samples, int * out_codes,
                                   int * out_n_frames) {
     if (!gen || !pcm || n_samples <= 0 || !out_codes || !out_n_frames) return -1;
-    set_error("audio encoding needs the codec encoder, which this library does not provide yet");
-    return -1;
+    try {
+        // frames of min(num_codebooks, 16) codes: the ABI's frame width (the bindings size the
+        // buffer at 16 codes per frame, python/bz_ggml/bindings.py:444-446)
+        std::vector<int> codes;
+        const int T = gen->encoder().encode(pcm, n_samples, codes);
+        const int nc = gen->eng->cfg.nc, w = std::min(nc, kAbiFrameWidth);
+        for (int f = 0; f < T; f++) std::memcpy(out_codes + (size_t) f * w, codes.data() + (size_t) f * nc, (size_t) w * sizeof(int));
+        *out_n_frames = T;
+        return T * w;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
 }
 
 // ------------------------------------------------------------------------------------ vocoder
@@ -678,6 +705,22 @@ int bzb_generate_codes(breeze_context * ctx, const breeze_request * req, const i
                        double * out_timings7) {
     if (out_codes && max_frames < 0) { set_error("negative max_frames"); return 1; }
     return generate_impl(ctx, req, ref_codes, ref_frames, cb, user, out_codes, max_frames, out_n_frames, out_timings7);
+}
+
+int bzb_generator_encode_audio_full(breeze_generator * gen, const float * pcm, int n_samples, int * out_codes,
+                                    int max_frames, int * out_n_frames) {
+    if (!gen || !pcm || n_samples <= 0 || !out_codes || max_frames < 0 || !out_n_frames) return -1;
+    try {
+        std::vector<int> codes;
+        const int T = gen->encoder().encode(pcm, n_samples, codes);
+        const int nc = gen->eng->cfg.nc;
+        std::memcpy(out_codes, codes.data(), (size_t) std::min(T, max_frames) * nc * sizeof(int));
+        *out_n_frames = T;
+        return T * nc;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
 }
 
 int bzb_write_wav(const char * path, const float * samples, int n, int sample_rate) {

@@ -277,6 +277,19 @@ ModelConfig parse_config(const GgufFile & g) {
     if (c.voc.rates.empty()) c.voc.rates = { 8, 5, 4, 3 };
     c.voc.ratios = g.kv_i32_array("breeze.codec.dec.upsampling_ratios");
     if (c.voc.ratios.empty()) c.voc.ratios = { 2, 2 };
+    c.enc.hidden = g.kv_u32("breeze.codec.hidden_size", 512);
+    c.enc.n_layer = g.kv_u32("breeze.codec.block_count", 8);
+    c.enc.n_head = g.kv_u32("breeze.codec.head_count", 8);
+    c.enc.hd = g.kv_u32("breeze.codec.head_dim", 64);
+    c.enc.ffn = g.kv_u32("breeze.codec.feed_forward_length", 2048);
+    c.enc.theta = g.kv_f32("breeze.codec.rope_theta", 10000.0f);
+    c.enc.window = g.kv_u32("breeze.codec.sliding_window", 250);
+    c.enc.nf = g.kv_u32("breeze.codec.num_filters", 64);
+    c.enc.dim = g.kv_u32("breeze.codec.codebook_dim", 256);
+    c.enc.n_sem = g.kv_u32("breeze.codec.num_semantic", 1);
+    c.enc.eps = g.kv_f32("breeze.codec.layer_norm_eps", 1e-5f);
+    c.enc.ratios = g.kv_i32_array("breeze.codec.upsampling_ratios");
+    if (c.enc.ratios.empty()) c.enc.ratios = { 8, 6, 5, 4 };
     return c;
 }
 

@@ -75,6 +75,13 @@ struct VocConfig {
     std::vector<int> rates, ratios;
 };
 
+// the codec encoder (src/config.cpp:68-81): SEANet filters and ratios, Mimi transformer, RVQ
+struct EncConfig {
+    int hidden, n_layer, n_head, hd, ffn, window, nf, dim, n_sem;
+    float eps, theta;
+    std::vector<int> ratios;
+};
+
 // keys and defaults of src/config.cpp:6-102 that the generation path reads
 struct ModelConfig {
     int hidden, nc, vs, cb_size, bb_eos, cb_pad, cb_eos, sample_rate, samples_per_frame, max_new_tokens;
@@ -84,6 +91,7 @@ struct ModelConfig {
     BbConfig bb;
     DdConfig dd;
     VocConfig voc;
+    EncConfig enc;
 };
 
 ModelConfig parse_config(const GgufFile & g);

@@ -189,6 +189,12 @@ struct Spec {
     int voc_dq = 256, voc_cbdim = 512, voc_latent = 1024, voc_hidden = 512, voc_layers = 8, voc_heads = 8,
         voc_kv = 8, voc_hd = 64, voc_ffn = 1024, voc_window = 72, voc_dec = 1536;
     std::vector<int32_t> voc_ratios = { 2 }, voc_rates = { 8, 6, 5, 4 };
+    // codec encoder (src/codec.cpp:80-123, src/codec_conv.cpp:60-77, src/codec_transformer.cpp:9-45):
+    // SEANet filters, transformer width/layers/heads/MLP/window, codebook dim; the SEANet strides
+    // run the upsampling ratios in reverse, then a stride-2 downsample: 4 * 5 * 6 * 8 * 2 = 1920
+    int enc_nf = 64, enc_hidden = 512, enc_layers = 8, enc_heads = 8, enc_hd = 64, enc_ffn = 2048,
+        enc_window = 250, enc_dim = 256;
+    std::vector<int32_t> enc_ratios = { 8, 6, 5, 4 };
 };
 
 uint64_t tensor_bytes(const Tensor & t) {
@@ -293,6 +299,8 @@ int main(int argc, char ** argv) {
         s.te_hidden = 256; s.te_layers = 2; s.te_heads = 2; s.te_kv = 1; s.te_hd = 128; s.te_ffn = 512; s.te_window = 8;
         s.voc_dq = 32; s.voc_cbdim = 64; s.voc_latent = 64; s.voc_hidden = 64; s.voc_layers = 2; s.voc_heads = 2;
         s.voc_kv = 1; s.voc_hd = 32; s.voc_ffn = 128; s.voc_window = 8; s.voc_dec = 64;
+        s.enc_nf = 8; s.enc_hidden = 64; s.enc_layers = 2; s.enc_heads = 2; s.enc_hd = 32; s.enc_ffn = 128;
+        s.enc_window = 8; s.enc_dim = 32;
     } else if (preset == "depth") {
         // the full-size depth decoder behind a one-layer backbone and a small text encoder: the
         // depth kernels at their real shapes in a model of a few hundred MB (profiling captures)
@@ -452,6 +460,45 @@ int main(int argc, char ** argv) {
     f32t("codec.dfin.beta", { ch }, 0.0f, 0.1f);
     conv("codec.dfin.conv", 7, ch, 1);
 
+    // codec encoder, appended after every decoder tensor: SEANet (conv 0; per stage a residual
+    // block, ELU and a strided conv doubling the channels; ELU and conv 14), the Mimi encoder
+    // transformer (LayerNorm, MHA, GELU MLP, layer scales), the stride-2 downsample and the
+    // semantic / acoustic quantiser projections and codebooks (F32 [dim, codebook size])
+    conv("codec.enc.0.conv", 7, 1, s.enc_nf);
+    {
+        const int res_idx[4] = { 1, 4, 7, 10 }, conv_idx[4] = { 3, 6, 9, 12 };
+        int64_t c = s.enc_nf;
+        for (int st = 0; st < 4; st++) {
+            const std::string rb = "codec.enc." + std::to_string(res_idx[st]);
+            conv(rb + ".block.1.conv", 3, c, c / 2);
+            conv(rb + ".block.3.conv", 1, c / 2, c);
+            const int r = s.enc_ratios[3 - st];
+            conv("codec.enc." + std::to_string(conv_idx[st]) + ".conv", 2 * r, c, 2 * c);
+            c *= 2;
+        }
+        conv("codec.enc.14.conv", 3, c, s.enc_hidden);
+    }
+    for (int l = 0; l < s.enc_layers; l++) {
+        const std::string p = "codec.enct.blk." + std::to_string(l);
+        nrm(p + ".attn_norm.weight", s.enc_hidden);
+        f32t(p + ".attn_norm.bias", { s.enc_hidden }, 0.0f, 0.02f);
+        lin(p + ".attn_q.weight", s.enc_hidden, (int64_t) s.enc_heads * s.enc_hd);
+        lin(p + ".attn_k.weight", s.enc_hidden, (int64_t) s.enc_heads * s.enc_hd);
+        lin(p + ".attn_v.weight", s.enc_hidden, (int64_t) s.enc_heads * s.enc_hd);
+        lin(p + ".attn_output.weight", (int64_t) s.enc_heads * s.enc_hd, s.enc_hidden);
+        f32t(p + ".attn_scale", { s.enc_hidden }, 0.1f, 0.01f);
+        nrm(p + ".ffn_norm.weight", s.enc_hidden);
+        f32t(p + ".ffn_norm.bias", { s.enc_hidden }, 0.0f, 0.02f);
+        lin(p + ".ffn_up.weight", s.enc_hidden, s.enc_ffn);
+        lin(p + ".ffn_down.weight", s.enc_ffn, s.enc_hidden);
+        f32t(p + ".ffn_scale", { s.enc_hidden }, 0.1f, 0.01f);
+    }
+    f32t("codec.downsample.conv.weight", { 4, s.enc_hidden, s.enc_hidden }, 0.0f, 0.7f / std::sqrt((float) (4 * s.enc_hidden)));
+    lin("codec.sq.in_proj.weight", s.enc_hidden, s.enc_dim);
+    f32t("codec.sq.0.embed", { s.enc_dim, s.cb_size }, 0.0f, 0.05f);
+    lin("codec.aq.in_proj.weight", s.enc_hidden, s.enc_dim);
+    for (int i = 0; i < s.nc - 1; i++) f32t("codec.aq." + std::to_string(i) + ".embed", { s.enc_dim, s.cb_size }, 0.0f, 0.05f);
+
     Writer w;
     w.kv_str("general.architecture", "breeze");
     w.kv_str("general.name", "breeze-synthetic-" + preset);
@@ -526,6 +573,18 @@ int main(int argc, char ** argv) {
     w.kv_u32("breeze.codec.dec.decoder_dim", s.voc_dec);
     w.kv_i32_arr("breeze.codec.dec.upsample_rates", s.voc_rates);
     w.kv_i32_arr("breeze.codec.dec.upsampling_ratios", s.voc_ratios);
+    w.kv_u32("breeze.codec.hidden_size", s.enc_hidden);
+    w.kv_u32("breeze.codec.block_count", s.enc_layers);
+    w.kv_u32("breeze.codec.head_count", s.enc_heads);
+    w.kv_u32("breeze.codec.head_dim", s.enc_hd);
+    w.kv_u32("breeze.codec.feed_forward_length", s.enc_ffn);
+    w.kv_f32("breeze.codec.rope_theta", 10000.0f);
+    w.kv_u32("breeze.codec.sliding_window", s.enc_window);
+    w.kv_u32("breeze.codec.num_filters", s.enc_nf);
+    w.kv_u32("breeze.codec.codebook_dim", s.enc_dim);
+    w.kv_u32("breeze.codec.num_semantic", 1);
+    w.kv_f32("breeze.codec.layer_norm_eps", 1e-5f);
+    w.kv_i32_arr("breeze.codec.upsampling_ratios", s.enc_ratios);
 
     // tokenizer (src/tokenizer.cpp:19-41): every id >= 264 has a unique special spelling so an
     // id list maps to text exactly; bytes are <0xNN>; [S0]/<ins_bos>/<ins_eos> are control tokens

@@ -79,8 +79,11 @@ __global__ void voc_transpose_kernel(const float * in, int R, int C, float * out
 constexpr int kCBM = 64, kCBN = 64, kCCI = 32, kCThreads = 128;
 
 struct ConvArgs {
-    const float * x = nullptr;          // input [cin][L]
-    int cin = 0, L = 0;
+    const float * x = nullptr;          // input [cin][L] (with istride > 1: see below)
+    int cin = 0, L = 0;                 // reduction channels, output length
+    // a stride-s conv runs as a causal conv over s phase channels per input channel: channel
+    // i*s + r at step t reads x[i][t*s + r] of the [cin/s][Lin] input (istride 1: Lin = L)
+    int istride = 1, Lin = 0;
     const float * w = nullptr;          // [phases][cout][taps][cin]
     int taps = 1, dil = 1;
     const float * bias = nullptr;
@@ -89,8 +92,9 @@ struct ConvArgs {
     int ldy = 0, ostride = 1;
     const float * res = nullptr;        // residual added before the activations (same indexing), or null
     const float * sa = nullptr, * sb = nullptr;     // SnakeBeta (alpha, beta) of the stored value, or null
-    float * y2 = nullptr;               // second output: SnakeBeta(value) with (s2a, s2b), or null
+    float * y2 = nullptr;               // second output: SnakeBeta(value) with (s2a, s2b), or ELU(value), or null
     const float * s2a = nullptr, * s2b = nullptr;
+    int elu1 = 0, elu2 = 0;             // ELU instead of SnakeBeta for the stored value / the second output
     int clamp = 0;
     // split of the input channels over blockIdx.z / phases (1: no split); partial sums go to
     // part[split][o * ldy + t * ostride + phase]
@@ -116,13 +120,16 @@ __device__ __forceinline__ float snake_beta(float v, float alpha, float beta) {
     return v + (s * s) / beta;
 }
 
+// ELU as ggml_elu: x for x > 0, exp(x) - 1 otherwise
+__device__ __forceinline__ float elu_f(float v) { return v > 0.0f ? v : expm1f(v); }
+
 __device__ __forceinline__ void conv_epilogue(const ConvArgs & a, int o, size_t idx, float v) {
     v += a.bias ? __ldg(a.bias + o) : 0.0f;
     if (a.res) v += a.res[idx];
-    float out = a.sa ? snake_beta(v, __ldg(a.sa + o), __ldg(a.sb + o)) : v;
+    float out = a.elu1 ? elu_f(v) : a.sa ? snake_beta(v, __ldg(a.sa + o), __ldg(a.sb + o)) : v;
     if (a.clamp) out = fminf(1.0f, fmaxf(-1.0f, out));
     a.y[idx] = out;
-    if (a.y2) a.y2[idx] = snake_beta(v, __ldg(a.s2a + o), __ldg(a.s2b + o));
+    if (a.y2) a.y2[idx] = a.elu2 ? elu_f(v) : snake_beta(v, __ldg(a.s2a + o), __ldg(a.s2b + o));
 }
 
 __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs a) {
@@ -192,7 +199,12 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
             for (int e = tid; e < kCCI * lx; e += kCThreads) {
                 const int i = e / lx, u = e - i * lx;
                 const int ci = c0 + i, t = t0 - halo + u;
-                xs[i * a.lxp + u] = (ci < ci_end && t >= 0 && t < a.L) ? a.x[(size_t) ci * a.L + t] : 0.0f;
+                float v = 0.0f;
+                if (ci < ci_end && t >= 0 && t < a.L) {
+                    const int src = ci / a.istride, ph = ci - src * a.istride;
+                    v = a.x[(size_t) src * a.Lin + (size_t) t * a.istride + ph];
+                }
+                xs[i * a.lxp + u] = v;
             }
         }
         __syncthreads();  // weight tile `cur` and the window are in place
@@ -299,7 +311,7 @@ __global__ void voc_layernorm_kernel(const float * x, int C, const float * w, co
 // rows [R][C] += bias, then GELU (erf) to f16 when `gelu`, else plain f32 in place
 __global__ void voc_bias_gelu_kernel(float * x, size_t n, int C, const float * b, half * y16) {
     for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
-        const float v = x[i] + b[i % C];
+        const float v = x[i] + (b ? b[i % C] : 0.0f);
         y16[i] = __float2half_rn(0.5f * v * (1.0f + erff(v * 0.70710678118654752f)));
     }
 }
@@ -383,10 +395,25 @@ int conv_lxp(int taps, int dil) {
     return (lx + 23) / 32 * 32 + 8;
 }
 
+// the conv kernel's dynamic shared-memory limit is a per-device function attribute shared by every
+// vocoder and encoder in the process: it only ever grows
+void raise_conv_smem_limit(size_t bytes) {
+    static std::mutex mu;
+    static std::map<int, size_t> set_on;
+    int dev = 0;
+    VCHECK(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if (bytes <= set_on[dev]) return;
+    if (bytes > 227 * 1024) throw std::runtime_error("vocoder: convolution window too wide");
+    VCHECK(cudaFuncSetAttribute(voc_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) bytes));
+    set_on[dev] = bytes;
+}
+
 // `a` with x, w, y, ... set; fills the launch shape (and the channel split when the grid would
 // leave SMs idle and the scratch can hold the partials)
 void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats, cudaStream_t s) {
     if (a.L <= 0) return;
+    if (a.Lin == 0) a.Lin = a.L;
     const int tiles = ((a.L + kCBN - 1) / kCBN) * ((a.cout + kCBM - 1) / kCBM) * phases;
     const int chunks = (a.cin + kCCI - 1) / kCCI;
     int splits = 1;
@@ -628,8 +655,7 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
             for (int j = 0; j < 3; j++)
                 lxp = std::max({ lxp, conv_lxp(b.res[j].c1.taps, dil_max[j]), conv_lxp(b.res[j].c2.taps, 1) });
         }
-        if (conv_smem_bytes(lxp) > 227 * 1024) throw std::runtime_error("vocoder: convolution window too wide");
-        VCHECK(cudaFuncSetAttribute(voc_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) conv_smem_bytes(lxp)));
+        raise_conv_smem_limit(conv_smem_bytes(lxp));
     }
     err_ = dalloc<int>(1);
     VCHECK(cudaMemset(err_, 0, sizeof(int)));
@@ -887,6 +913,368 @@ int Vocoder::stream_decode_batch(int batch, const int * flat_tokens, const int *
         running_pcm += nf * spf;
     }
     return batch;
+}
+
+}  // namespace bzb
+
+// ================================================================================= codec encoder
+namespace bzb {
+
+namespace {
+
+constexpr int kRvqThreads = 256;  // codebook entries per distance block
+
+// squared distances of frame f's vector to codebook entries [256 chunk, 256 chunk + 256) in f32,
+// summed over the dimension in order with separately rounded products (as src/codec.cpp:61-74
+// computes them), then the chunk's first minimum
+__global__ void __launch_bounds__(kRvqThreads) rvq_dist_kernel(const float * vec, int dim, const float * bookT, int n,
+                                                              float * dmin, int * imin, int chunks) {
+    extern __shared__ float sv[];
+    __shared__ float bd[kRvqThreads / 32];
+    __shared__ int bi[kRvqThreads / 32];
+    const int f = blockIdx.x, chunk = blockIdx.y;
+    for (int k = threadIdx.x; k < dim; k += blockDim.x) sv[k] = vec[(size_t) f * dim + k];
+    __syncthreads();
+    const int c = chunk * kRvqThreads + threadIdx.x;
+    float d = INFINITY;
+    int idx = INT_MAX;
+    if (c < n) {
+        d = 0.0f;
+        for (int k = 0; k < dim; k++) {
+            const float diff = __fsub_rn(sv[k], __ldg(bookT + (size_t) k * n + c));
+            d = __fadd_rn(d, __fmul_rn(diff, diff));
+        }
+        idx = c;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float od = __shfl_xor_sync(0xffffffffu, d, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (od < d || (od == d && oi < idx)) { d = od; idx = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { bd[warp] = d; bi[warp] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kRvqThreads / 32; w++)
+            if (bd[w] < bd[0] || (bd[w] == bd[0] && bi[w] < bi[0])) { bd[0] = bd[w]; bi[0] = bi[w]; }
+        dmin[(size_t) f * chunks + chunk] = bd[0];
+        imin[(size_t) f * chunks + chunk] = bi[0];
+    }
+}
+
+// the first minimum over the chunks becomes the frame's code in column `col`; with `update` the
+// chosen entry is subtracted from the residual (the next acoustic stage's input)
+__global__ void rvq_pick_kernel(float * res, int dim, const float * bookT, int n, const float * dmin, const int * imin,
+                                int chunks, int * codes, int ld_codes, int col, int update) {
+    __shared__ int sc;
+    const int f = blockIdx.x;
+    if (threadIdx.x == 0) {
+        float b = dmin[(size_t) f * chunks];
+        int bix = imin[(size_t) f * chunks];
+        for (int c = 1; c < chunks; c++)
+            if (dmin[(size_t) f * chunks + c] < b) { b = dmin[(size_t) f * chunks + c]; bix = imin[(size_t) f * chunks + c]; }
+        if (bix == INT_MAX) bix = 0;
+        sc = bix;
+        codes[(size_t) f * ld_codes + col] = bix;
+    }
+    __syncthreads();
+    if (!update) return;
+    for (int k = threadIdx.x; k < dim; k += blockDim.x)
+        res[(size_t) f * dim + k] = __fsub_rn(res[(size_t) f * dim + k], __ldg(bookT + (size_t) k * n + sc));
+}
+
+}  // namespace
+
+#define ECHECK(x) VCHECK(x)
+
+const GgufTensor & CodecEncoder::need(const std::string & name) const {
+    const GgufTensor * t = gg_.find(name);
+    if (!t) throw std::runtime_error("codec encoder: tensor " + name + " missing from the GGUF");
+    return *t;
+}
+
+float * CodecEncoder::upload(const std::vector<float> & h) {
+    void * p = nullptr;
+    ECHECK(cudaMalloc(&p, std::max<size_t>(h.size(), 1) * sizeof(float)));
+    allocs_.push_back(p);
+    ECHECK(cudaMemcpy(p, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return (float *) p;
+}
+
+float * CodecEncoder::load_f32(const std::string & name, int64_t expect) {
+    const GgufTensor & t = need(name);
+    if (t.type != GT_F32 || (expect >= 0 && t.nelem() != expect))
+        throw std::runtime_error("codec encoder: " + name + " must be F32 with " + std::to_string(expect) + " elements");
+    const float * src = reinterpret_cast<const float *>(gg_.data(t));
+    return upload(std::vector<float>(src, src + t.nelem()));
+}
+
+QMat CodecEncoder::load_lin(const std::string & name) {
+    const GgufTensor & t = need(name);
+    if (t.type != GT_Q8_0 && t.type != GT_Q4_K) throw std::runtime_error("codec encoder: " + name + " must be Q8_0 or Q4_K");
+    const int K = (int) t.ne[0], M = (int) t.rows();
+    QMat q;
+    q.M = M; q.K = K; q.KB = K / 32; q.MT = (M + 15) / 16;
+    uint8_t * raw = nullptr;
+    ECHECK(cudaMalloc(&raw, t.nbytes));
+    ECHECK(cudaMemcpy(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice));
+    auto dal = [&](size_t bytes) { void * p = nullptr; ECHECK(cudaMalloc(&p, bytes)); allocs_.push_back(p); return p; };
+    if (t.type == GT_Q4_K) {
+        if (K % 256) throw std::runtime_error("codec encoder: " + name + " is Q4_K with rows not a multiple of 256");
+        UMat u;
+        u.M = M; u.MT = (M + 127) / 128; u.K = K; u.KC = K / 64; u.q4 = 1;
+        uint8_t * ub = (uint8_t *) dal((size_t) u.MT * u.KC * kUChunkBytesQ4);
+        repack_umma_q4k(raw, M, K, ub, stream_);
+        u.blk = ub;
+        q.u = u;
+    } else {
+        q.qs = (uint4 *) dal((size_t) q.MT * q.KB * 32 * sizeof(uint4));
+        q.ds = (half2 *) dal((size_t) q.MT * q.KB * 8 * sizeof(half2));
+        repack_q8(raw, M, K, const_cast<uint4 *>(q.qs), const_cast<half2 *>(q.ds), stream_);
+    }
+    ECHECK(cudaStreamSynchronize(stream_));
+    cudaFree(raw);
+    return q;
+}
+
+// [Cout][Cin][K] (ggml [K, Cin, Cout]) with stride s -> tap-major polyphase [Cout][taps][Cin * s]:
+// output t reads x[i][s t + k - pad], pad = K - s; with k - pad = s m + r (0 <= r < s) that is phase
+// channel i*s + r at step t + m, tap taps-1+m
+CodecEncoder::Conv CodecEncoder::load_conv(const std::string & name, int cin, int cout, int stride, bool bias) {
+    const GgufTensor & t = need(name + ".weight");
+    if (t.type != GT_F32 || t.ne.size() != 3 || t.ne[1] != cin || t.ne[2] != cout)
+        throw std::runtime_error("codec encoder: unexpected shape or type of " + name + ".weight");
+    const int K = (int) t.ne[0], s = stride;
+    if (K < s) throw std::runtime_error("codec encoder: " + name + " has a kernel shorter than its stride");
+    Conv c;
+    c.cin = cin; c.cout = cout; c.stride = s;
+    c.taps = (K + s - 1) / s;
+    const int pad = K - s;
+    const float * src = reinterpret_cast<const float *>(gg_.data(t));
+    std::vector<float> h((size_t) cout * c.taps * cin * s, 0.0f);
+    for (int o = 0; o < cout; o++)
+        for (int i = 0; i < cin; i++)
+            for (int k = 0; k < K; k++) {
+                const int rel = k - pad;
+                const int m = rel >= 0 ? rel / s : -((-rel + s - 1) / s);
+                const int r = rel - m * s, kk = m + c.taps - 1;
+                h[((size_t) o * c.taps + kk) * cin * s + (size_t) i * s + r] = src[((size_t) o * cin + i) * K + k];
+            }
+    c.w = upload(h);
+    if (bias) c.b = load_f32(name + ".bias", cout);
+    return c;
+}
+
+CodecEncoder::CodecEncoder(const GgufFile & gg, const ModelConfig & cfg, int device)
+    : gg_(gg), cfg_(cfg), ec_(cfg.enc), device_(device) {
+    ECHECK(cudaSetDevice(device));
+    ECHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    init_kernel_attributes();
+    init_umma_attributes();
+    const std::vector<int> & rt = ec_.ratios;
+    if (rt.size() != 4) throw std::runtime_error("codec encoder: four SEANet ratios expected");
+    if (rt[0] * rt[1] * rt[2] * rt[3] * 2 != kSamplesPerFrame) throw std::runtime_error("codec encoder: the ratios do not give 1920 samples per frame");
+    const int nf = ec_.nf;
+    c0_ = load_conv("codec.enc.0.conv", 1, nf, 1, true);
+    const int res_idx[4] = { 1, 4, 7, 10 }, conv_idx[4] = { 3, 6, 9, 12 };
+    int ch = nf;
+    for (int st = 0; st < 4; st++) {
+        const std::string rb = "codec.enc." + std::to_string(res_idx[st]);
+        res1_[st] = load_conv(rb + ".block.1.conv", ch, ch / 2, 1, true);
+        res3_[st] = load_conv(rb + ".block.3.conv", ch / 2, ch, 1, true);
+        strided_[st] = load_conv("codec.enc." + std::to_string(conv_idx[st]) + ".conv", ch, 2 * ch, rt[3 - st], true);
+        ch *= 2;
+    }
+    c14_ = load_conv("codec.enc.14.conv", ch, ec_.hidden, 1, true);
+    const int H = ec_.hidden;
+    if (ec_.n_head * ec_.hd != H || ec_.hd > 128 || ec_.hd % 32) throw std::runtime_error("codec encoder: unsupported attention shape");
+    for (int l = 0; l < ec_.n_layer; l++) {
+        const std::string p = "codec.enct.blk." + std::to_string(l);
+        Layer L;
+        L.an_w = load_f32(p + ".attn_norm.weight", H);
+        L.an_b = load_f32(p + ".attn_norm.bias", H);
+        L.q = load_lin(p + ".attn_q.weight");
+        L.k = load_lin(p + ".attn_k.weight");
+        L.v = load_lin(p + ".attn_v.weight");
+        L.o = load_lin(p + ".attn_output.weight");
+        L.attn_scale = load_f32(p + ".attn_scale", H);
+        L.fn_w = load_f32(p + ".ffn_norm.weight", H);
+        L.fn_b = load_f32(p + ".ffn_norm.bias", H);
+        L.up = load_lin(p + ".ffn_up.weight");
+        L.down = load_lin(p + ".ffn_down.weight");
+        L.ffn_scale = load_f32(p + ".ffn_scale", H);
+        layers_.push_back(L);
+    }
+    down_ = load_conv("codec.downsample.conv", H, H, 2, false);
+    sq_in_ = load_lin("codec.sq.in_proj.weight");
+    aq_in_ = load_lin("codec.aq.in_proj.weight");
+    if (sq_in_.M != ec_.dim || aq_in_.M != ec_.dim) throw std::runtime_error("codec encoder: quantiser projections do not match codebook_dim");
+    // codebooks, transposed to [dim][entries] so that a distance block reads them coalesced
+    const int nc = cfg_.nc, n_ac = nc - ec_.n_sem;
+    if (ec_.n_sem != 1 || n_ac < 0) throw std::runtime_error("codec encoder: one semantic codebook expected");
+    const GgufTensor & b0 = need("codec.sq.0.embed");
+    book_n_ = (int) b0.ne[1];
+    std::vector<float> books((size_t) nc * ec_.dim * book_n_);
+    for (int bi = 0; bi < nc; bi++) {
+        const GgufTensor & t = need(bi == 0 ? std::string("codec.sq.0.embed") : "codec.aq." + std::to_string(bi - 1) + ".embed");
+        if (t.type != GT_F32 || t.ne[0] != ec_.dim || t.ne[1] != book_n_) throw std::runtime_error("codec encoder: codebook " + t.name + " has an unexpected shape");
+        const float * src = reinterpret_cast<const float *>(gg_.data(t));
+        float * dst = books.data() + (size_t) bi * ec_.dim * book_n_;
+        for (int e = 0; e < book_n_; e++)
+            for (int k = 0; k < ec_.dim; k++) dst[(size_t) k * book_n_ + e] = src[(size_t) e * ec_.dim + k];
+    }
+    books_ = upload(books);
+    {
+        void * p = nullptr;
+        scr_.ws_elems = (size_t) 1 << 20;
+        ECHECK(cudaMalloc(&p, scr_.ws_elems * sizeof(float4)));
+        allocs_.push_back(p);
+        scr_.ws = (float4 *) p;
+        scr_.n_counters = 4096;
+        ECHECK(cudaMalloc(&p, scr_.n_counters * sizeof(int)));
+        allocs_.push_back(p);
+        scr_.counters = (int *) p;
+        ECHECK(cudaMemset(scr_.counters, 0, scr_.n_counters * sizeof(int)));
+        ECHECK(cudaMalloc(&p, sizeof(int)));
+        allocs_.push_back(p);
+        err_ = (int *) p;
+        ECHECK(cudaMemset(err_, 0, sizeof(int)));
+    }
+    // widest conv window: dynamic shared memory of the conv kernel
+    int lxp = conv_lxp(c0_.taps, 1);
+    for (int st = 0; st < 4; st++)
+        lxp = std::max({ lxp, conv_lxp(res1_[st].taps, 1), conv_lxp(res3_[st].taps, 1), conv_lxp(strided_[st].taps, 1) });
+    lxp = std::max({ lxp, conv_lxp(c14_.taps, 1), conv_lxp(down_.taps, 1) });
+    raise_conv_smem_limit(conv_smem_bytes(lxp));
+}
+
+CodecEncoder::~CodecEncoder() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (void * p : scratch_) cudaFree(p);
+    for (void * p : allocs_) cudaFree(p);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void CodecEncoder::ensure(int L) {
+    if (L <= lcap_) return;
+    ECHECK(cudaStreamSynchronize(stream_));
+    for (void * p : scratch_) cudaFree(p);
+    scratch_.clear();
+    lcap_ = std::max(L, 64 * kSamplesPerFrame);
+    const size_t Lc = (size_t) lcap_;
+    act_ = std::max((size_t) ec_.nf * Lc, (size_t) 1024);
+    const size_t T1 = Lc / (kSamplesPerFrame / 2) + 1, T2 = Lc / kSamplesPerFrame + 1;
+    const size_t wide = (size_t) std::max({ ec_.hidden, ec_.ffn, ec_.dim });
+    auto fa = [&](size_t n) { void * p = nullptr; ECHECK(cudaMalloc(&p, std::max<size_t>(n, 16) * 4)); scratch_.push_back(p); return (float *) p; };
+    auto ha = [&](size_t n) { void * p = nullptr; ECHECK(cudaMalloc(&p, std::max<size_t>(n, 16) * 2)); scratch_.push_back(p); return (half *) p; };
+    X_ = fa(act_); E_ = fa(act_); H_ = fa(act_); part_ = fa(2 * act_);
+    t32_ = fa(T1 * wide); q_ = fa(T1 * wide); k_ = fa(T1 * wide); v_ = fa(T1 * wide); o_ = fa(T1 * wide); res_ = fa(T1 * wide);
+    t16_ = ha(T1 * wide); att16_ = ha(T1 * wide); f16_ = ha(T1 * wide);
+    const int chunks = (book_n_ + kRvqThreads - 1) / kRvqThreads;
+    dpart_ = fa(T2 * chunks);
+    ipart_ = (int *) fa(T2 * chunks);
+    codes_ = (int *) fa(T2 * cfg_.nc);
+    if (rope_max_ < (int) T1) {
+        const std::vector<float2> tab = rope_table((int) T1, ec_.hd, ec_.theta, 1.0f, nullptr);
+        void * p = nullptr;
+        ECHECK(cudaMalloc(&p, tab.size() * sizeof(float2)));
+        scratch_.push_back(p);
+        ECHECK(cudaMemcpy(p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        rope_ = (float2 *) p;
+        rope_max_ = (int) T1;
+    }
+}
+
+void CodecEncoder::conv(const Conv & c, const float * x, int Lin, float * y, bool elu_out, const float * res, float * y2,
+                        bool elu2, cudaStream_t s) {
+    ConvArgs ca;
+    ca.x = x; ca.cin = c.cin * c.stride; ca.L = Lin / c.stride; ca.istride = c.stride; ca.Lin = Lin;
+    ca.w = c.w; ca.taps = c.taps; ca.dil = 1;
+    ca.bias = c.b; ca.cout = c.cout;
+    ca.y = y; ca.ldy = ca.L; ca.ostride = 1;
+    ca.res = res;
+    ca.elu1 = elu_out ? 1 : 0;
+    ca.y2 = y2; ca.elu2 = elu2 ? 1 : 0;
+    launch_conv(ca, 1, part_, 2 * act_, s);
+}
+
+int CodecEncoder::encode(const float * pcm, int n, std::vector<int> & codes) {
+    std::lock_guard<std::mutex> lk(mu_);
+    const int T = n / kSamplesPerFrame;
+    codes.assign((size_t) std::max(T, 0) * cfg_.nc, 0);
+    if (T <= 0) return 0;
+    ECHECK(cudaSetDevice(device_));
+    int L = T * kSamplesPerFrame;
+    ensure(L);
+    cudaStream_t s = stream_;
+    // the PCM goes in as a [1][L] input row
+    ECHECK(cudaMemcpyAsync(H_, pcm, (size_t) L * sizeof(float), cudaMemcpyHostToDevice, s));
+    float * X = X_, * E = E_, * Hb = H_;
+    // SEANet (src/codec_conv.cpp:60-77): X the stage's residual stream, E = ELU(X) (the next
+    // conv's input), Hb the residual block's middle activation
+    conv(c0_, Hb, L, X, false, nullptr, E, true, s);
+    for (int st = 0; st < 4; st++) {
+        conv(res1_[st], E, L, Hb, true, nullptr, nullptr, false, s);     // ELU(conv(ELU(x)))
+        conv(res3_[st], Hb, L, X, false, X, E, true, s);                 // x += conv(...); E = ELU(x)
+        conv(strided_[st], E, L, X, false, nullptr, Hb, true, s);        // strided conv of ELU(x)
+        L /= strided_[st].stride;
+        std::swap(E, Hb);
+    }
+    conv(c14_, E, L, Hb, false, nullptr, nullptr, false, s);             // [hidden][T1]
+    const int T1 = L, H = ec_.hidden, nh = ec_.n_head, hd = ec_.hd, F = ec_.ffn;
+    auto transpose = [&](const float * in, int R, int C, float * out) {
+        voc_transpose_kernel<<<dim3((C + 31) / 32, (R + 31) / 32), dim3(32, 8), 0, s>>>(in, R, C, out, nullptr);
+    };
+    auto lin = [&](const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out) {
+        if (w.qs) launch_gemv(w, x16, ldx, rows, out, scr_, s);
+        else launch_umma_gemm(w.u, x16, ldx, rows, out, err_, s, false);
+    };
+    // Mimi encoder transformer (src/codec_transformer.cpp:9-45) on [T1][hidden] rows
+    transpose(Hb, H, T1, t32_);
+    const float scale = 1.0f / std::sqrt((float) hd);
+    for (const Layer & Ly : layers_) {
+        voc_layernorm_kernel<<<T1, 256, 0, s>>>(t32_, H, Ly.an_w, Ly.an_b, ec_.eps, t16_);
+        lin(Ly.q, t16_, H, T1, GemvOut{ EPI_STORE, q_, nullptr, H });
+        lin(Ly.k, t16_, H, T1, GemvOut{ EPI_STORE, k_, nullptr, H });
+        lin(Ly.v, t16_, H, T1, GemvOut{ EPI_STORE, v_, nullptr, H });
+        const int warps = T1 * nh;
+        voc_attn_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, k_, v_, T1, nh, nh, hd, ec_.window, rope_, scale, att16_);
+        lin(Ly.o, att16_, H, T1, GemvOut{ EPI_STORE, o_, nullptr, H });
+        voc_scaled_add_kernel<<<grid_for((size_t) T1 * H), 256, 0, s>>>(t32_, o_, (size_t) T1 * H, H, Ly.attn_scale);
+        voc_layernorm_kernel<<<T1, 256, 0, s>>>(t32_, H, Ly.fn_w, Ly.fn_b, ec_.eps, t16_);
+        lin(Ly.up, t16_, H, T1, GemvOut{ EPI_STORE, o_, nullptr, F });
+        voc_bias_gelu_kernel<<<grid_for((size_t) T1 * F), 256, 0, s>>>(o_, (size_t) T1 * F, F, nullptr, f16_);
+        lin(Ly.down, f16_, F, T1, GemvOut{ EPI_STORE, res_, nullptr, H });
+        voc_scaled_add_kernel<<<grid_for((size_t) T1 * H), 256, 0, s>>>(t32_, res_, (size_t) T1 * H, H, Ly.ffn_scale);
+    }
+    // stride-2 downsample, then the quantiser projections on [T2][hidden] rows
+    transpose(t32_, T1, H, X);                                           // [hidden][T1]
+    conv(down_, X, T1, E, false, nullptr, nullptr, false, s);            // [hidden][T2]
+    const int T2 = T1 / 2;
+    transpose(E, H, T2, t32_);
+    voc_to_f16_kernel<<<grid_for((size_t) T2 * H), 256, 0, s>>>(t32_, (size_t) T2 * H, t16_);
+    const int dim = ec_.dim;
+    lin(sq_in_, t16_, H, T2, GemvOut{ EPI_STORE, q_, nullptr, dim });   // semantic input
+    lin(aq_in_, t16_, H, T2, GemvOut{ EPI_STORE, k_, nullptr, dim });   // acoustic residual
+    // nearest codebook entries (src/codec.cpp:104-120)
+    const int nc = cfg_.nc, chunks = (book_n_ + kRvqThreads - 1) / kRvqThreads;
+    const size_t book_stride = (size_t) dim * book_n_;
+    for (int bi = 0; bi < nc; bi++) {
+        const float * vec = bi == 0 ? q_ : k_;
+        rvq_dist_kernel<<<dim3(T2, chunks), kRvqThreads, dim * sizeof(float), s>>>(vec, dim, books_ + bi * book_stride, book_n_,
+                                                                                   dpart_, ipart_, chunks);
+        rvq_pick_kernel<<<T2, 128, 0, s>>>(k_, dim, books_ + bi * book_stride, book_n_, dpart_, ipart_, chunks, codes_, nc, bi,
+                                           bi > 0 ? 1 : 0);
+    }
+    ECHECK(cudaGetLastError());
+    codes.assign((size_t) T2 * nc, 0);
+    ECHECK(cudaMemcpyAsync(codes.data(), codes_, codes.size() * sizeof(int), cudaMemcpyDeviceToHost, s));
+    int err = 0;
+    ECHECK(cudaMemcpyAsync(&err, err_, sizeof(int), cudaMemcpyDeviceToHost, s));
+    ECHECK(cudaStreamSynchronize(s));
+    if (err) throw std::runtime_error("codec encoder: a bounded wait timed out in the tcgen05 GEMM");
+    return T2;
 }
 
 }  // namespace bzb

@@ -115,4 +115,64 @@ private:
     std::map<int, std::vector<int>> history_;
 };
 
+// The codec encoder: 24 kHz PCM -> codebook frames (MimiCodec::encode, src/codec.cpp:80-123) on
+// the GPU: the SEANet encoder's convolutions on the vocoder's TF32 conv kernel (strided convs as
+// polyphase causal convs), the Mimi encoder transformer, the stride-2 downsample, the quantiser
+// projections and the semantic + residual acoustic nearest-codebook search.
+class CodecEncoder {
+public:
+    CodecEncoder(const GgufFile & gg, const ModelConfig & cfg, int device);
+    ~CodecEncoder();
+    static constexpr int kSamplesPerFrame = 1920;
+    // PCM [n] -> codes frame-major [T][nc] with T = n / 1920 (a trailing partial frame does not
+    // change the frames before it: every stage is causal); returns T
+    int encode(const float * pcm, int n, std::vector<int> & codes);
+    int nc() const { return cfg_.nc; }
+
+private:
+    struct Conv {
+        float * w = nullptr, * b = nullptr;  // tap-major [cout][taps][cin * stride]
+        int cin = 0, cout = 0, taps = 0, stride = 1;
+    };
+    struct Layer {
+        QMat q, k, v, o, up, down;
+        float * an_w = nullptr, * an_b = nullptr, * fn_w = nullptr, * fn_b = nullptr;
+        float * attn_scale = nullptr, * ffn_scale = nullptr;
+    };
+    const GgufTensor & need(const std::string & name) const;
+    float * upload(const std::vector<float> & h);
+    float * load_f32(const std::string & name, int64_t expect);
+    QMat load_lin(const std::string & name);
+    Conv load_conv(const std::string & name, int cin, int cout, int stride, bool bias);
+    void ensure(int L);
+    void conv(const Conv & c, const float * x, int Lin, float * y, bool elu_out, const float * res, float * y2, bool elu2,
+              cudaStream_t s);
+
+    const GgufFile & gg_;
+    ModelConfig cfg_;
+    EncConfig ec_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    std::vector<void *> allocs_, scratch_;
+    Conv c0_, c14_, down_;
+    Conv res1_[4], res3_[4], strided_[4];
+    std::vector<Layer> layers_;
+    QMat sq_in_, aq_in_;
+    float * books_ = nullptr;  // [nc][dim][codebook size]: the semantic book, then the acoustic ones, transposed
+    int book_n_ = 0;
+    float2 * rope_ = nullptr;
+    int rope_max_ = 0;
+    GemvScratch scr_;
+    int * err_ = nullptr;
+    // activations (grown on demand)
+    int lcap_ = 0;
+    size_t act_ = 0;
+    float * X_ = nullptr, * E_ = nullptr, * H_ = nullptr, * part_ = nullptr;
+    float * t32_ = nullptr, * q_ = nullptr, * k_ = nullptr, * v_ = nullptr, * o_ = nullptr, * res_ = nullptr;
+    half * t16_ = nullptr, * att16_ = nullptr, * f16_ = nullptr;
+    float * dpart_ = nullptr;
+    int * ipart_ = nullptr, * codes_ = nullptr;
+    std::mutex mu_;
+};
+
 }  // namespace bzb

@@ -99,6 +99,11 @@ BREEZE_API int bzb_generate_codes(breeze_context * ctx, const breeze_request * r
 /* The long-text splitter of breeze_generate (reference src/text_split.cpp:89-111): writes the
  * pieces NUL-terminated one after another into out and returns their count, or -(bytes needed)
  * when capacity is too small. */
+/* breeze_generator_encode_audio (reference src/c_api.cpp:1302-1331) at the model's full width:
+ * num_codebooks codes per frame, frame-major, at most max_frames frames written; returns the
+ * codes produced (frames * num_codebooks) or -1. */
+BREEZE_API int bzb_generator_encode_audio_full(breeze_generator * gen, const float * pcm, int n_samples, int * out_codes,
+                                               int max_frames, int * out_n_frames);
 /* The WAV writer of breeze_generate_wav (reference src/audio.cpp:80-107): 16-bit mono PCM at
  * sample_rate. Returns 0, or -1 with breeze_last_error(). */
 BREEZE_API int bzb_write_wav(const char * path, const float * samples, int n, int sample_rate);

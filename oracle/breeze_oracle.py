@@ -183,6 +183,7 @@ class Config:
     bb: dict = field(default_factory=dict)
     dd: dict = field(default_factory=dict)
     voc: dict = field(default_factory=dict)
+    codec: dict = field(default_factory=dict)
 
 
 def parse_config(g: GGUFFile) -> Config:
@@ -231,6 +232,14 @@ def parse_config(g: GGUFFile) -> Config:
                  window=g.kv("breeze.codec.dec.sliding_window", 72),
                  rates=list(g.kv("breeze.codec.dec.upsample_rates", []) or [8, 5, 4, 3]),
                  ratios=list(g.kv("breeze.codec.dec.upsampling_ratios", []) or [2, 2]))
+    # src/config.cpp:68-81 (the codec encoder)
+    c.codec = dict(hidden=g.kv("breeze.codec.hidden_size", 512), n_layer=g.kv("breeze.codec.block_count", 8),
+                   n_head=g.kv("breeze.codec.head_count", 8), hd=g.kv("breeze.codec.head_dim", 64),
+                   ffn=g.kv("breeze.codec.feed_forward_length", 2048), theta=g.kv("breeze.codec.rope_theta", 10000.0),
+                   window=g.kv("breeze.codec.sliding_window", 250), nf=g.kv("breeze.codec.num_filters", 64),
+                   dim=g.kv("breeze.codec.codebook_dim", 256), n_sem=g.kv("breeze.codec.num_semantic", 1),
+                   eps=g.kv("breeze.codec.layer_norm_eps", 1e-5),
+                   ratios=list(g.kv("breeze.codec.upsampling_ratios", []) or [8, 6, 5, 4]))
     return c
 
 
@@ -1385,3 +1394,127 @@ def wav_bytes(samples, sample_rate: int) -> bytes:
     hdr = b"RIFF" + struct.pack("<I", 36 + len(pcm)) + b"WAVE" + b"fmt " + struct.pack(
         "<IHHIIHH", 16, 1, 1, sample_rate, sample_rate * 2, 2, 16) + b"data" + struct.pack("<I", len(pcm))
     return hdr + pcm
+
+
+# ----------------------------------------------------------------------------- codec encoder
+def elu(x):
+    """ggml_elu: x for x > 0, exp(x) - 1 otherwise."""
+    x = x.astype(np.float32)
+    return np.where(x > 0, x, np.expm1(np.minimum(x, 0).astype(np.float64)).astype(np.float32)).astype(np.float32)
+
+
+class CodecEncoder:
+    """MimiCodec::encode (src/codec.cpp:80-123): SEANet encoder (src/codec_conv.cpp:33-78), the
+    Mimi encoder transformer (src/codec_transformer.cpp:9-45), the stride-2 downsample and the
+    semantic + residual acoustic nearest-codebook search. PCM [L] at 24 kHz -> codes [T][nc]."""
+
+    def __init__(self, model: "Model"):
+        self.m = model
+        self.c = model.cfg.codec
+
+    def w(self, name):
+        return self.m.w(name)
+
+    def seanet(self, x):
+        """src/codec_conv.cpp:60-77 over [1, L] -> [hidden, T]."""
+        ratios = self.c["ratios"]
+        rev = [ratios[3], ratios[2], ratios[1], ratios[0]]
+
+        def conv(i, h, stride):
+            p = f"codec.enc.{i}.conv"
+            return conv1d_causal(h, self.w(p + ".weight"), self.w(p + ".bias"), stride, 1)
+
+        h = conv(0, x, 1)
+        for st, (ri, ci) in enumerate(zip((1, 4, 7, 10), (3, 6, 9, 12))):
+            p = f"codec.enc.{ri}"
+            r = elu(h)
+            r = conv1d_causal(r, self.w(p + ".block.1.conv.weight"), self.w(p + ".block.1.conv.bias"), 1, 1)
+            r = elu(r)
+            r = conv1d_causal(r, self.w(p + ".block.3.conv.weight"), self.w(p + ".block.3.conv.bias"), 1, 1)
+            h = (h + r).astype(np.float32)
+            h = conv(ci, elu(h), rev[st])
+        return conv(14, elu(h), 1)
+
+    def transformer(self, x):
+        """src/codec_transformer.cpp:9-45 over [T, hidden]."""
+        c = self.c
+        T = x.shape[0]
+        cos, sin = rope_cos_sin(np.arange(T), c["hd"], c["theta"])
+        mask = sliding_causal_mask(T, c["window"])
+        scale = 1.0 / math.sqrt(c["hd"])
+        h = x.astype(np.float32)
+        for il in range(c["n_layer"]):
+            p = f"codec.enct.blk.{il}"
+            cur = layer_norm_rows(h, self.w(p + ".attn_norm.weight"), self.w(p + ".attn_norm.bias"), c["eps"])
+            q = linear(cur, self.w(p + ".attn_q.weight")).reshape(T, c["n_head"], c["hd"])
+            k = linear(cur, self.w(p + ".attn_k.weight")).reshape(T, c["n_head"], c["hd"])
+            v = linear(cur, self.w(p + ".attn_v.weight")).reshape(T, c["n_head"], c["hd"])
+            a = attention(rope_neox(q, cos, sin), rope_neox(k, cos, sin), v, scale, mask)
+            a = (linear(a, self.w(p + ".attn_output.weight")) * self.w(p + ".attn_scale")).astype(np.float32)
+            h = (h + a).astype(np.float32)
+            cur = layer_norm_rows(h, self.w(p + ".ffn_norm.weight"), self.w(p + ".ffn_norm.bias"), c["eps"])
+            cur = gelu_erf(linear(cur, self.w(p + ".ffn_up.weight")))
+            cur = (linear(cur, self.w(p + ".ffn_down.weight")) * self.w(p + ".ffn_scale")).astype(np.float32)
+            h = (h + cur).astype(np.float32)
+        return h
+
+    def embeddings(self, audio):
+        """The projected quantiser inputs: (semantic [T2, dim], acoustic [T2, dim])."""
+        x = np.asarray(audio, np.float32).reshape(1, -1)
+        h = self.seanet(x)                                   # [hidden, T]
+        h = self.transformer(h.T).T                          # [hidden, T]
+        h = conv1d_causal(h, self.w("codec.downsample.conv.weight"), None, 2, 1)   # [hidden, T2]
+        emb = h.T.astype(np.float32)
+        return linear(emb, self.w("codec.sq.in_proj.weight")), linear(emb, self.w("codec.aq.in_proj.weight"))
+
+    @staticmethod
+    def nearest(book, v):
+        """src/codec.cpp:61-74: the first entry with the least squared distance (f32, summed
+        over the dimension in order). book [n, dim], v [dim]."""
+        d = ((v[None, :].astype(np.float32) - book.astype(np.float32)) ** 2).astype(np.float32)
+        dist = np.zeros(book.shape[0], np.float32)
+        for k in range(book.shape[1]):
+            dist = (dist + d[:, k]).astype(np.float32)
+        return int(np.argmin(dist)), dist
+
+    def encode(self, audio, want_dists=False):
+        c = self.c
+        nc = self.m.cfg.nc
+        rs, ra = self.embeddings(audio)
+        T = rs.shape[0]
+        sbook = self.w("codec.sq.0.embed")                   # [book, dim]
+        abooks = [self.w(f"codec.aq.{i}.embed") for i in range(nc - c["n_sem"])]
+        codes = np.zeros((T, nc), np.int64)
+        dists = []
+        for f in range(T):
+            codes[f, 0], d0 = self.nearest(sbook, rs[f])
+            res = ra[f].astype(np.float32).copy()
+            fd = [d0]
+            for i, book in enumerate(abooks):
+                ci, di = self.nearest(book, res)
+                codes[f, c["n_sem"] + i] = ci
+                res = (res - book[ci]).astype(np.float32)
+                fd.append(di)
+            dists.append(fd)
+        return (codes, dists) if want_dists else codes
+
+    def follow(self, audio, codes):
+        """Walks the quantiser chain with the given codes [T][nc] in place of the nearest
+        choices (teacher forcing) and returns, per frame and codebook, the squared distances of
+        the given code and of the nearest entry at that stage."""
+        c = self.c
+        nc = self.m.cfg.nc
+        rs, ra = self.embeddings(audio)
+        sbook = self.w("codec.sq.0.embed")
+        abooks = [self.w(f"codec.aq.{i}.embed") for i in range(nc - c["n_sem"])]
+        out = np.zeros((rs.shape[0], nc, 2), np.float64)
+        for f in range(min(rs.shape[0], len(codes))):
+            _, d = self.nearest(sbook, rs[f])
+            out[f, 0] = (d[int(codes[f][0])], d.min())
+            res = ra[f].astype(np.float32).copy()
+            for i, book in enumerate(abooks):
+                _, d = self.nearest(book, res)
+                ci = int(codes[f][c["n_sem"] + i])
+                out[f, c["n_sem"] + i] = (d[ci], d.min())
+                res = (res - book[ci]).astype(np.float32)
+        return out
