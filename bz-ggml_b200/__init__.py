@@ -332,6 +332,27 @@ class GeneratorHandle:
             raise RuntimeError(self.lib.last_error())
         return codes, logits
 
+    def convert_voice(self, src_codes: Sequence[int], src_T: int, ref_audio=None, ref_codes: Optional[Sequence[int]] = None,
+                      ref_frames: int = 0, ref_text: Optional[str] = None, src_text: Optional[str] = None,
+                      cfg_scale: float = 1.5, keep_acoustic: int = 0, feed_source: bool = True, seed: int = 42,
+                      return_pcm: bool = True):
+        """Voice conversion of encoded source frames into the reference voice (mirrors
+        bz_ggml.bindings.GeneratorHandle.convert_voice): returns (pcm or None, codes)."""
+        src = np.ascontiguousarray(np.asarray(src_codes, np.int32))
+        ra = None if ref_audio is None or len(ref_audio) == 0 else np.ascontiguousarray(np.asarray(ref_audio, np.float32))
+        rc = None if not ref_codes or ref_frames <= 0 else np.ascontiguousarray(np.asarray(ref_codes, np.int32))
+        out_codes = np.zeros(src_T * 16, np.int32)
+        pcm = np.zeros(src_T * 1920 + 32000, np.float32) if return_pcm else None
+        res = self.lib.lib.breeze_generator_convert_voice(
+            self.handle, _ip(src), src_T, None if ra is None else _fp(ra), 0 if ra is None else ra.size,
+            None if rc is None else _ip(rc), 0 if rc is None else ref_frames,
+            ref_text.encode("utf-8") if ref_text else None, src_text.encode("utf-8") if src_text else None,
+            ctypes.c_float(cfg_scale), keep_acoustic, 1 if feed_source else 0, ctypes.c_uint(seed & 0xFFFFFFFF),
+            _ip(out_codes), None if pcm is None else _fp(pcm), 0 if pcm is None else pcm.size)
+        if res < 0:
+            raise RuntimeError(f"Voice conversion failed on Generator (device {self.device}): {self.lib.last_error()}")
+        return (pcm[:res].tolist() if return_pcm else None), out_codes.tolist()
+
     def encode_audio(self, pcm_samples) -> Tuple[List[int], int]:
         """24 kHz mono PCM -> (codes, n_frames), min(num_codebooks, 16) codes per frame
         (mirrors bz_ggml.bindings.GeneratorHandle.encode_audio)."""

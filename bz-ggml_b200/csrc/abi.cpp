@@ -20,10 +20,15 @@
 struct breeze_generator {
     std::unique_ptr<bzb::Engine> eng;
     int device = 0;
-    std::unique_ptr<bzb::CodecEncoder> enc;  // built on first use (encode_audio)
+    std::unique_ptr<bzb::CodecEncoder> enc;  // built on first use (encode_audio, convert_voice)
+    std::unique_ptr<bzb::Vocoder> voc;       // built on first use (convert_voice PCM)
     bzb::CodecEncoder & encoder() {
         if (!enc) enc = std::make_unique<bzb::CodecEncoder>(eng->gguf(), eng->cfg, device);
         return *enc;
+    }
+    bzb::Vocoder & vocoder() {
+        if (!voc) voc = std::make_unique<bzb::Vocoder>(eng->gguf(), eng->cfg, device);
+        return *voc;
     }
 };
 
@@ -50,6 +55,7 @@ thread_local std::string g_error;
 void set_error(const std::string & e) { g_error = e; }
 
 constexpr int kLegacySession = INT_MIN;
+constexpr int kConvertSession = INT_MIN + 1;  // the engine session of a voice conversion
 constexpr int kAbiFrameWidth = 16;
 
 // breeze_request -> GenRequest (src/c_api.cpp:30-48)
@@ -345,12 +351,85 @@ int breeze_generator_convert_voice(breeze_generator * gen, const int * src_codes
                                    int ref_audio_len, const int * ref_codes, int ref_frames, const char * ref_text,
                                    const char * src_text, float cfg_scale, int keep_acoustic, int feed_source,
                                    unsigned int seed, int * out_codes, float * out_pcm, int max_out_pcm) {
-    (void) ref_audio; (void) ref_audio_len; (void) ref_codes; (void) ref_frames; (void) ref_text; (void) src_text;
-    (void) cfg_scale; (void) keep_acoustic; (void) feed_source; (void) seed; (void) out_codes; (void) out_pcm;
-    (void) max_out_pcm;
     if (!gen || !src_codes || src_T <= 0) return -1;
-    set_error("voice conversion needs the codec encoder, which this library does not provide yet");
-    return -1;
+    try {
+        bzb::Engine & eng = *gen->eng;
+        const int nc = eng.cfg.nc, spf = bzb::Vocoder::kSamplesPerFrame;
+        // frames are num_codebooks codes apart (the reference indexes them so, src/generation.cpp:346-364);
+        // the ABI copies 16 codes per frame (src/c_api.cpp:1262, 1271), which bounds num_codebooks
+        if (nc > kAbiFrameWidth) throw std::runtime_error("voice conversion through the generator ABI needs num_codebooks <= 16");
+        // the reference voice: given codes, else the clip encoded (src/generation.cpp:319-325)
+        std::vector<int> ref;
+        int ref_T = 0;
+        if (ref_codes && ref_frames > 0) {
+            ref.assign(ref_codes, ref_codes + (size_t) ref_frames * nc);
+            ref_T = ref_frames;
+        } else if (ref_audio && ref_audio_len > 0) {
+            ref_T = gen->encoder().encode(ref_audio, ref_audio_len, ref);
+        }
+        const std::string text = (src_text && std::strlen(src_text) > 0)
+                                     ? std::string(src_text)
+                                     : bzb::filler_text((double) src_T * spf / eng.cfg.sample_rate);
+        // prompts (src/generation.cpp:332-337): the conditional one always carries the reference
+        // (its text, frames and EOS frame) and no instruction; the unconditional one drops it
+        const bzb::Tokenizer & tok = eng.tokenizer();
+        std::vector<std::vector<int>> segs = { tok.encode("[S0]" + std::string(ref_text ? ref_text : ""), true),
+                                               tok.encode("[S0]" + text, true) };
+        std::vector<std::vector<int>> segs_u = { tok.encode("[S0]" + text, true) };
+        const bool use_cfg = cfg_scale != 1.0f;
+        // ConvertOptions (src/generation.h:48-63): the depth codes take the top-1 of temperature 0.3
+        bzb::SessionParams sp;
+        sp.cfg = cfg_scale;
+        sp.dtemp = 0.3f; sp.dtop_k = 1; sp.dtop_p = 1.0f;
+        const int sid = kConvertSession;
+        int cb0 = 0;
+        const int dummy = 0;
+        eng.session_create_tokens(sid, segs, use_cfg ? &segs_u : nullptr, ref.empty() ? &dummy : ref.data(), ref_T, seed,
+                                  src_T, sp, false, &cb0, nullptr, false);
+        std::vector<int> out((size_t) src_T * nc);
+        try {
+            const int keep = std::max(0, std::min(keep_acoustic, nc - 1));
+            std::vector<int> force, feed;
+            for (int t0 = 0; t0 < src_T; t0 += 64) {
+                const int K = std::min(64, src_T - t0);
+                force.assign((size_t) K * nc, -1);
+                feed.assign(src_codes + (size_t) t0 * nc, src_codes + (size_t) (t0 + K) * nc);
+                for (int k = 0; k < K; k++)
+                    for (int c = 0; c <= keep; c++) force[(size_t) k * nc + c] = src_codes[(size_t) (t0 + k) * nc + c];
+                bzb::StepForce fs;
+                fs.codes = force.data();
+                fs.feed = feed_source ? feed.data() : nullptr;
+                int next = 0;
+                const bzb::StepResult r = eng.step(&sid, 1, K, nullptr, true, out.data() + (size_t) t0 * nc, nc, &next, true,
+                                                   true, nullptr, &fs);
+                if (r.steps_executed != K) throw std::runtime_error("voice conversion stopped early");
+            }
+        } catch (...) {
+            eng.session_free(sid);
+            throw;
+        }
+        eng.session_free(sid);
+        if (out_codes) std::memcpy(out_codes, out.data(), out.size() * sizeof(int));
+        if (!out_pcm || max_out_pcm <= 0) return src_T;  // tokens only
+        // PCM in windows of 40 frames with sliding_window + 16 frames of left context
+        // (src/generation.cpp:374-387)
+        bzb::Vocoder & voc = gen->vocoder();
+        const int ctx = eng.cfg.voc.window + 16, step = 40;
+        std::vector<float> audio, part;
+        audio.reserve((size_t) src_T * spf);
+        for (int start = 0; start < src_T; start += step) {
+            const int count = std::min(step, src_T - start), cs = start > ctx ? start - ctx : 0;
+            part.resize((size_t) (start + count - cs) * spf);
+            voc.decode(out.data() + (size_t) cs * nc, start + count - cs, part.data());
+            audio.insert(audio.end(), part.begin() + (size_t) (start - cs) * spf, part.begin() + (size_t) (start - cs + count) * spf);
+        }
+        const int written = (int) std::min<size_t>(audio.size(), (size_t) max_out_pcm);
+        std::memcpy(out_pcm, audio.data(), (size_t) written * sizeof(float));
+        return written;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
 }
 
 int breeze_generator_encode_audio(breeze_generator * gen, const float * pcm, int n_samples, int * out_codes,

@@ -429,6 +429,10 @@ void Engine::alloc_buffers() {
     dseeds_ = dalloc<uint32_t>(rmax_);
     row_pair_ = dalloc<int>(rmax_);
     row_set_ = dalloc<int>(rmax_);
+    force_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
+    feed_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
+    cur_force_ = dalloc<int>((size_t) rmax_ * nc);
+    cur_feed_ = dalloc<int>((size_t) rmax_ * nc);
     create_rows_ = dalloc<int>(4);
     cur_frames_ = dalloc<int>((size_t) rmax_ * nc);
     frames_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
@@ -769,6 +773,11 @@ void Engine::enqueue_step(int R, int flags) {
     sa.R = R; sa.nc = nc; sa.vs = vs; sa.H = H;
     sa.row_slot = row_slot_; sa.row_active = row_active_; sa.st = st_; sa.hid32 = hid32_; sa.embd = audio_embd_;
     sa.din16 = din16_; sa.frames = cur_frames_; sa.step_ctr = step_ctr_; sa.any_active = any_active_;
+    if (flags & kFlagForce) {
+        launch_stage_forced(force_all_, (flags & kFlagFeed) ? feed_all_ : nullptr, step_ctr_, R * nc, cur_force_, cur_feed_,
+                            stream_);
+        sa.force = cur_force_;
+    }
     launch_step_init(sa, stream_);
     if (flags & kFlagQ4) {
         // the rows of each depth weight set take their codes from their own pass; the second
@@ -780,7 +789,7 @@ void Engine::enqueue_step(int R, int flags) {
         depth_pass(R, flags, 0, sa);
     }
     // backbone: one token per session over its own paged cache
-    launch_audio_embed(audio_embd_, cur_frames_, nc, nc, vs, R, bx_, row_active_, stream_);
+    launch_audio_embed(audio_embd_, (flags & kFlagFeed) ? cur_feed_ : cur_frames_, nc, nc, vs, R, bx_, row_active_, stream_);
     for (int l = 0; l < cfg.bb.n_layer; l++) bb_decode_layer(l, R);
     launch_rmsnorm(bx_, H, bb_out_norm_, H, cfg.bb.eps, bh16_, H, hid32_, H, 0, R, row_slot_, stream_);
     gemv(lm_head_, bh16_, H, R, GemvOut{ EPI_STORE, blog_, nullptr, vbb_ });
@@ -791,7 +800,8 @@ void Engine::enqueue_step(int R, int flags) {
     sm.sup_lo = cfg.cb_size; sm.sup_hi = cfg.vs; sm.eos = cfg.bb_eos;
     sm.row_pair = row_pair_;
     sm.seeds = (flags & kFlagSeeds) ? seeds_ : nullptr; sm.step_ctr = step_ctr_; sm.next_out = next_;
-    launch_sample(sm, stream_);
+    if (flags & kFlagForce) launch_advance(row_slot_, row_active_, row_pair_, st_, R, next_, stream_);
+    else launch_sample(sm, stream_);
     launch_frames_commit(cur_frames_, frames_all_, R * nc, step_ctr_, stream_);
 }
 
@@ -838,7 +848,7 @@ cudaGraphExec_t Engine::graph_for(int R, int flags) {
 
 StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
                         int width, int * next_out, bool fill_inactive, bool sampled_depth,
-                        const uint32_t * depth_seeds) {
+                        const uint32_t * depth_seeds, const StepForce * force) {
     StepResult res;
     const int nc = cfg.nc;
     if (n > rmax_) throw std::runtime_error("batch of " + std::to_string(n) + " sessions exceeds the engine's " + std::to_string(rmax_) + " rows (BZB_MAX_BATCH)");
@@ -883,14 +893,36 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     bool any_q4 = false;
     for (int r = 0; r < R; r++)
         if (rs[r] >= 0 && slots_[rs[r]].use_q4) rset[r] = 1, any_q4 = true;
+    // teacher-forced frames run the sampled-depth kernels (forced codes bypass the draw)
+    if (force) sampled = true;
     const int flags = (seeds ? kFlagSeeds : 0) | (sampled ? kFlagSampled : 0) |
-                      (sampled && depth_seeds && !seeds ? kFlagDepthSeeds : 0) | (any_q4 ? kFlagQ4 : 0);
+                      (sampled && depth_seeds && !seeds ? kFlagDepthSeeds : 0) | (any_q4 ? kFlagQ4 : 0) |
+                      (force ? kFlagForce : 0) | (force && force->feed ? kFlagFeed : 0);
     cudaGraphExec_t g = graph_for(R, flags);
     cur_R_ = R;
     cur_flags_ = flags;
     CK(cudaMemcpyAsync(row_slot_, rs.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
     CK(cudaMemcpyAsync(row_pair_, rp.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
     if (any_q4) CK(cudaMemcpyAsync(row_set_, rset.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    if (force) {
+        // [K][R][nc]: each listed session's frames on its row and its unconditional branch's row
+        std::vector<int> fa((size_t) K * R * nc, -1), fe;
+        if (force->feed) fe.assign((size_t) K * R * nc, 0);
+        for (int k = 0; k < K; k++)
+            for (int r = 0; r < R; r++) {
+                const int lead = r < n ? r : (rp[r] <= -2 ? -2 - rp[r] : -1);
+                if (lead < 0 || rs[r] < 0) continue;
+                const int * src = force->codes + ((size_t) k * n + lead) * nc;
+                std::copy(src, src + nc, fa.begin() + ((size_t) k * R + r) * nc);
+                if (force->feed) {
+                    const int * fs = force->feed + ((size_t) k * n + lead) * nc;
+                    std::copy(fs, fs + nc, fe.begin() + ((size_t) k * R + r) * nc);
+                }
+            }
+        CK(cudaMemcpyAsync(force_all_, fa.data(), fa.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        if (force->feed) CK(cudaMemcpyAsync(feed_all_, fe.data(), fe.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        CK(cudaStreamSynchronize(stream_));  // the host vectors go out of scope
+    }
     if (seeds) {
         std::vector<uint32_t> sd(R, 0);
         for (int i = 0; i < n; i++) sd[i] = seeds[i];
@@ -1106,6 +1138,7 @@ void Engine::prefill_prompt(int slot, const std::vector<std::vector<int>> & segs
         off += (int) toks.size();
     };
     auto add_frames = [&](const int * codes, int F) {
+        if (F <= 0) return;  // a reference segment without frames still gets its EOS frame
         CK(cudaMemcpyAsync(pframes_, codes, (size_t) F * nc * sizeof(int), cudaMemcpyHostToDevice, stream_));
         launch_audio_embed(audio_embd_, pframes_, nc, nc, cfg.vs, F, px_ + (size_t) off * H, nullptr, stream_);
         CK(cudaStreamSynchronize(stream_));
@@ -1126,17 +1159,18 @@ void Engine::prefill_prompt(int slot, const std::vector<std::vector<int>> & segs
 void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> & segs,
                                    const std::vector<std::vector<int>> * segs_u, const int * ref_codes,
                                    int ref_frames, uint32_t seed, int est, const SessionParams & sp, bool clamp_total,
-                                   int * out_cb0, int * out_alloc) {
+                                   int * out_cb0, int * out_alloc, bool uncond_has_ref) {
     // prompt layout (src/c_api.cpp:388-396): [ref text][ref frames][EOS frame] then the tail text
-    auto prompt_len = [&](const std::vector<std::vector<int>> & sg) {
-        if (sg.empty() || (ref_codes && sg.size() < 2)) throw std::runtime_error("prompt segments missing");
+    auto prompt_len = [&](const std::vector<std::vector<int>> & sg, bool with_ref) {
+        if (sg.empty() || (with_ref && sg.size() < 2)) throw std::runtime_error("prompt segments missing");
         int t = 0;
-        if (ref_codes) t = (int) sg[0].size() + ref_frames + 1 + (int) sg[1].size();
+        if (with_ref) t = (int) sg[0].size() + ref_frames + 1 + (int) sg[1].size();
         else t = (int) sg.back().size();
         return t;
     };
-    const int total = prompt_len(segs);
-    const int total_u = segs_u ? prompt_len(*segs_u) : 0;
+    const bool ref_u = ref_codes && uncond_has_ref;
+    const int total = prompt_len(segs, ref_codes != nullptr);
+    const int total_u = segs_u ? prompt_len(*segs_u, ref_u) : 0;
     if (total <= 0 || (segs_u && total_u <= 0)) throw std::runtime_error("empty prompt");
     if (est <= 0) throw std::runtime_error("generation budget must be positive");
     if (clamp_total) {
@@ -1163,7 +1197,7 @@ void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> 
             slots_[slot].partner = slot_u;
         }
         prefill_prompt(slot, segs, ref_codes, ref_frames, plog_);
-        if (segs_u) prefill_prompt(slot_u, *segs_u, ref_codes, ref_frames, plog_ + vbb_);
+        if (segs_u) prefill_prompt(slot_u, *segs_u, ref_u ? ref_codes : nullptr, ref_frames, plog_ + vbb_);
         SessState s{};
         s.active = 1;
         s.pos = total;

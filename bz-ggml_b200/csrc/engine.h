@@ -42,6 +42,14 @@ struct SessionParams {
     int dtop_k = 50;
 };
 
+// teacher-forced frames for a step call (host, [K][n][nc]): `codes` holds each frame's cb0 and
+// the depth codes to force (-1: the depth sampler picks); `feed`, when given, is the frame the
+// backbone consumes instead of the produced one (src/generation.cpp:361-367)
+struct StepForce {
+    const int * codes = nullptr;
+    const int * feed = nullptr;
+};
+
 struct StepResult {
     int steps_executed = 0;
     int still_active = 0;
@@ -62,10 +70,11 @@ public:
     // prompt = [ref text segment][ref frames][EOS frame] tail segment (the ref parts only when
     // ref_codes is non-null); `uncond` adds the unconditional branch's segments (params.cfg != 1).
     // With clamp_total the budget is clamped so prompt + budget <= 2040 (the generator ABI).
+    // (uncond_has_ref false: the reference parts belong to the conditional prompt only)
     void session_create_tokens(int sid, const std::vector<std::vector<int>> & text_segments,
                                const std::vector<std::vector<int>> * uncond_segments, const int * ref_codes,
                                int ref_frames, uint32_t seed, int max_tokens, const SessionParams & params,
-                               bool clamp_total, int * out_cb0, int * out_alloc);
+                               bool clamp_total, int * out_cb0, int * out_alloc, bool uncond_has_ref = true);
     // the generator ABI's sampler for a session (fixed cb0 sampler, the GGUF's depth sampler)
     SessionParams abi_params(float cfg_scale) const;
     const Tokenizer & tokenizer() const { return tok_; }
@@ -86,7 +95,7 @@ public:
     // depth draws per call (src/c_api.cpp:468).
     StepResult step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
                     int width, int * next_out, bool fill_inactive, bool sampled_depth = false,
-                    const uint32_t * depth_seeds = nullptr);
+                    const uint32_t * depth_seeds = nullptr, const StepForce * force = nullptr);
 
     // device-resident run of K steps for the current batch (no host copies): timing entry
     void step_device_only(int K);
@@ -136,7 +145,9 @@ private:
     // graph flags: kFlagSeeds (per-row reseed of the samplers), kFlagSampled (sampled depth),
     // kFlagDepthSeeds (per-call depth seeds)
     // kFlagQ4 (some rows take their depth codes from the Q4_K override: two masked depth passes)
-    static constexpr int kFlagSeeds = 1, kFlagSampled = 2, kFlagDepthSeeds = 4, kFlagQ4 = 8;
+    // kFlagForce (teacher-forced frames, no cb0 draw), kFlagFeed (the backbone consumes given frames)
+    static constexpr int kFlagSeeds = 1, kFlagSampled = 2, kFlagDepthSeeds = 4, kFlagQ4 = 8, kFlagForce = 16,
+                         kFlagFeed = 32;
     void depth_pass(int R, int flags, int set, const StepArgs & sa);
     void load_depth_weights();
     void swap_depth_sets();
@@ -212,6 +223,7 @@ private:
     int * frames_all_ = nullptr, * step_ctr_ = nullptr, * any_active_ = nullptr, * slot_scalar_ = nullptr;
     uint32_t * seeds_ = nullptr, * dseeds_ = nullptr;
     int * row_pair_ = nullptr, * create_rows_ = nullptr, * row_set_ = nullptr;
+    int * force_all_ = nullptr, * feed_all_ = nullptr, * cur_force_ = nullptr, * cur_feed_ = nullptr;
     half * din16_ = nullptr, * dh16_ = nullptr, * dff16_ = nullptr, * datt16_ = nullptr;
     float * dx_ = nullptr, * dqkv_ = nullptr, * dkv_ = nullptr, * dlog_ = nullptr;
     half * bh16_ = nullptr, * bff16_ = nullptr, * batt16_ = nullptr;

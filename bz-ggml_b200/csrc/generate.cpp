@@ -283,6 +283,19 @@ bool generate(Engine & eng, Vocoder & voc, const GenRequest & req, const AudioCa
     return true;
 }
 
+std::string filler_text(double seconds) {
+    static const char * const kLines[] = {
+        "A calm voice reads a short passage at an even pace. ",
+        "Each sentence here is plain and carries no special meaning. ",
+        "The reading goes on for a while in the same steady tone. ",
+        "There is nothing to remember from these words at all. ",
+    };
+    const size_t want = (size_t) (seconds * 17.0) + 16;
+    std::string s;
+    for (int i = 0; s.size() < want; i++) s += kLines[i % 4];
+    return s;
+}
+
 bool write_wav(const std::string & path, const std::vector<float> & samples, int sample_rate) {
     FILE * f = std::fopen(path.c_str(), "wb");
     if (!f) return false;

@@ -49,6 +49,11 @@ std::vector<std::string> split_text(const std::string & text, int budget, int fi
 bool generate(Engine & eng, Vocoder & voc, const GenRequest & req, const AudioCallback & cb,
               GenTimings * timings = nullptr, std::vector<int> * codes_out = nullptr);
 
+// a transcript stand-in for voice conversion without one: neutral sentences repeated to about
+// 17 characters per second of source audio plus 16 (the length rule of src/generation.cpp:287-299;
+// the reference states the wording does not matter, and these sentences are this library's own)
+std::string filler_text(double seconds);
+
 // 16-bit mono PCM WAV (src/audio.cpp:80-107: clamp, scale by 32767, truncate)
 bool write_wav(const std::string & path, const std::vector<float> & samples, int sample_rate);
 

@@ -850,10 +850,10 @@ __global__ void step_init_kernel(const StepArgs a) {
     const int k = *a.step_ctr;
     if (threadIdx.x == 0) {
         a.row_active[r] = act ? 1 : 0;
-        a.frames[(size_t) r * a.nc] = act ? a.st[slot].last_cb0 : -1;
+        a.frames[(size_t) r * a.nc] = act ? (a.force ? a.force[(size_t) r * a.nc] : a.st[slot].last_cb0) : -1;
         if (act) atomicOr(&a.any_active[k], 1);
     }
-    const int cb0 = act ? a.st[slot].last_cb0 : 0;
+    const int cb0 = act ? (a.force ? a.force[(size_t) r * a.nc] : a.st[slot].last_cb0) : 0;
     const int row = (cb0 < 0 || cb0 >= a.embd.rows) ? 0 : cb0;
     for (int d = threadIdx.x; d < a.H; d += blockDim.x) {
         half h0 = __float2half_rn(0.0f), h1 = __float2half_rn(0.0f);
@@ -1103,7 +1103,11 @@ __global__ void __launch_bounds__(1024) depth_sample_kernel(const DepthSampleArg
     const float * lu = pr >= 0 ? a.logits + (size_t) pr * a.ld : nullptr;
     const float cfg = s.cfg;
     const int V = a.V;
-    if (s.dtop_k == 1) {
+    const int forced = sa.force ? sa.force[(size_t) r * sa.nc + a.col] : -1;
+    if (forced >= 0) {
+        // a teacher-forced code (src/depth_decoder.cpp:158-159): no draw
+        if (threadIdx.x == 0) s_code = forced;
+    } else if (s.dtop_k == 1) {
         // top-1 is the first argmax (no draw)
         float best = -INFINITY;
         int bi = INT_MAX;
@@ -1155,6 +1159,38 @@ __global__ void __launch_bounds__(1024) depth_sample_kernel(const DepthSampleArg
     if (a.gather_cb < 0) return;
     embed_row_f16(sa.embd, (size_t) a.gather_cb * sa.vs + code, sa.din16 + (size_t) r * sa.H);
     if (pr >= 0) embed_row_f16(sa.embd, (size_t) a.gather_cb * sa.vs + code, sa.din16 + (size_t) pr * sa.H);
+}
+
+__global__ void stage_forced_kernel(const int * force_all, const int * feed_all, const int * ctr, int n, int * cur_force,
+                                    int * cur_feed) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t base = (size_t) (*ctr) * n;
+    for (int i = threadIdx.x + blockIdx.x * blockDim.x; i < n; i += blockDim.x * gridDim.x) {
+        cur_force[i] = force_all[base + i];
+        if (feed_all) cur_feed[i] = feed_all[base + i];
+    }
+}
+
+__global__ void advance_kernel(const int * row_slot, const int * row_active, const int * row_pair, SessState * st, int R,
+                               int * next_out) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int slot = row_slot[r];
+    if (slot < 0 || !row_active[r]) return;
+    const int pr = row_pair ? row_pair[r] : -1;
+    if (pr <= -2) return;  // the unconditional branch: its leader advances it
+    SessState & s = st[slot];
+    s.steps += 1;
+    s.pos += 1;
+    if (pr >= 0) {
+        SessState & u = st[row_slot[pr]];
+        u.steps = s.steps;
+        u.pos += 1;
+    }
+    next_out[r] = 0;
 }
 
 __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ctr) {
@@ -1381,6 +1417,19 @@ void launch_depth_sample_gather(const DepthSampleArgs & a, cudaStream_t s) {
     if (a.V > kSortN) throw std::runtime_error("depth sampler: vocabulary larger than 4096");
     if (a.col < 1 || a.col >= a.s.nc) throw std::runtime_error("depth sampler: codebook out of range");
     launch_k(depth_sample_kernel, a.s.R, 1024, 0, s, a);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_stage_forced(const int * force_all, const int * feed_all, const int * step_ctr, int n, int * cur_force,
+                         int * cur_feed, cudaStream_t s) {
+    launch_k(stage_forced_kernel, (unsigned) std::max(1, std::min(64, (n + 255) / 256)), 256, 0, s, force_all, feed_all,
+             step_ctr, n, cur_force, cur_feed);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_advance(const int * row_slot, const int * row_active, const int * row_pair, SessState * st, int R,
+                    int * next_out, cudaStream_t s) {
+    launch_k(advance_kernel, (unsigned) ((R + 127) / 128), 128, 0, s, row_slot, row_active, row_pair, st, R, next_out);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -196,6 +196,8 @@ struct StepArgs {
     // depth passes of one weight set: rows whose row_set differs from set_id are left alone
     const int * row_set = nullptr;
     int set_id = 0;
+    // teacher-forced steps: codes [R][nc] of this step (cb0 always, depth codes where >= 0)
+    const int * force = nullptr;
 };
 void launch_step_init(const StepArgs & a, cudaStream_t s);
 // codes[r] = first argmax of logits[r]; frames[..][r][col] = code; when gather_cb >= 0 the
@@ -242,6 +244,14 @@ struct SampleArgs {
     int update_hist_first = 0;          // prefill: first cb0 is always recorded
 };
 void launch_sample(const SampleArgs & a, cudaStream_t s);
+// teacher-forced steps: copies step *step_ctr's rows of force_all / feed_all ([K][n] ints) into
+// cur_force / cur_feed (feed may be null)
+void launch_stage_forced(const int * force_all, const int * feed_all, const int * step_ctr, int n, int * cur_force,
+                         int * cur_feed, cudaStream_t s);
+// teacher-forced steps draw no cb0: every active leading row advances its (and its pair's)
+// position and step count, next_out[r] = 0 (still active)
+void launch_advance(const int * row_slot, const int * row_active, const int * row_pair, SessState * st, int R,
+                    int * next_out, cudaStream_t s);
 // copies the current frame into frames_all[step] and advances the burst step counter
 void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s);
 

@@ -962,8 +962,23 @@ class Generator:
         self.sessions[sid] = sess
         return cb0, alloc
 
+    def convert_create(self, sid, text, ref_codes=None, ref_frames=0, ref_text="", cfg_scale=1.5, seed=42, src_T=1):
+        """Voice-conversion session (src/generation.cpp:315-345): the conditional prompt carries the
+        reference (its text, frames and EOS frame) and no instruction, the unconditional one the
+        text alone; depth codes from the top-1 of temperature 0.3 (ConvertOptions)."""
+        m = self.m
+        embs = [m.text_encoder(m.tok.encode("[S0]" + (ref_text or ""), True))]
+        if ref_frames > 0:
+            embs.append(m.audio_embed(np.asarray(ref_codes).reshape(-1, m.cfg.nc)[:ref_frames]))
+        embs.append(m.audio_embed(np.full((1, m.cfg.nc), m.cfg.cb_eos)))
+        embs.append(m.text_encoder(m.tok.encode("[S0]" + text, True)))
+        eu = m.text_encoder(m.tok.encode("[S0]" + text, True)) if cfg_scale != 1.0 else None
+        return self.session_create(sid, text, embeds=np.concatenate(embs), embeds_u=eu, cfg_scale=cfg_scale,
+                                   seed=seed, max_new_tokens=src_T, clamp_total=False,
+                                   params=SamplerParams(0.9, 50, 1.0, 1.1, 0.3, 1, 1.0))
+
     def step_batched(self, sids, seeds=None, forced_depth=None, depth_logits_out=None, sampled_depth=False,
-                     depth_seeds=None):
+                     depth_seeds=None, force_frames=None, feed_frames=None):
         """One frame for each active session; returns (frames [N, nc], next_cb0 [N]).
         Depth codes are the argmax, or each session's depth sampler when a listed session has two
         branches (src/depth_decoder.cpp:252-257) or `sampled_depth` is set (the single-session
@@ -971,7 +986,9 @@ class Generator:
         reseed the depth draws per call. `forced_depth` [N, nc-1] (rows of `sids`) teacher-forces
         the depth codes: they become the frame and the next inputs; the oracle's own (combined)
         logits go to `depth_logits_out` (a dict filled per session id) and the uniforms it would
-        have drawn to `self.last_depth_uniforms`."""
+        have drawn to `self.last_depth_uniforms`. `force_frames` [N, nc] teacher-forces a voice
+        conversion step (src/generation.cpp:347-368): cb0 and the depth codes >= 0 come from it,
+        no cb0 is drawn, and `feed_frames` [N, nc], when given, is what the backbone consumes."""
         m = self.m
         nc = m.cfg.nc
         act = [i for i, s in enumerate(sids) if s in self.sessions and self.sessions[s].active]
@@ -984,10 +1001,13 @@ class Generator:
             for i, s in zip(act, ss):
                 s.rng.seed(int(seeds[i]))
         pairs = [k for k, s in enumerate(ss) if s.cfg != 1.0]
-        sampled = bool(pairs) or (sampled_depth and any(s.sp.dtop_k != 1 for s in ss))
+        sampled = bool(pairs) or (sampled_depth and any(s.sp.dtop_k != 1 for s in ss)) or force_frames is not None
+        ff = None if force_frames is None else np.asarray(force_frames)[act]
         n = len(ss)
         hid = np.stack([s.last_hidden for s in ss] + [ss[k].last_hidden_u for k in pairs])
         cb0 = np.array([s.last_cb0 for s in ss] + [ss[k].last_cb0 for k in pairs])
+        if ff is not None:
+            cb0 = np.array([int(ff[k, 0]) for k in range(len(ss))] + [int(ff[k, 0]) for k in pairs])
         urow = {k: n + q for q, k in enumerate(pairs)}
         forced = None if forced_depth is None else np.asarray(forced_depth)[act]
         comb_logits = np.zeros((n, nc - 1, m.cfg.vs), np.float32)
@@ -1000,7 +1020,9 @@ class Generator:
                 s = ss[k]
                 l = combine_logits(lg[k], lg[urow[k]] if k in urow else None, s.cfg)
                 comb_logits[k, j - 1] = l
-                if not sampled or s.sp.dtop_k == 1:
+                if ff is not None and ff[k, j] >= 0:
+                    code = int(ff[k, j])
+                elif not sampled or s.sp.dtop_k == 1:
                     code = int(np.argmax(l))
                 else:
                     if seeds is not None:
@@ -1038,11 +1060,19 @@ class Generator:
             for k, i in enumerate(act):
                 depth_logits_out[sids[i]] = comb_logits[k]
         fr = np.concatenate([cb0[:n, None], chosen], axis=1)
-        ae = m.audio_embed(np.concatenate([fr, fr[pairs]], axis=0) if pairs else fr)
+        fed = fr if feed_frames is None else np.asarray(feed_frames)[act].astype(np.int64)
+        ae = m.audio_embed(np.concatenate([fed, fed[pairs]], axis=0) if pairs else fed)
         hs, ls = m.backbone_step_batched([s.st for s in ss] + [ss[k].st_u for k in pairs], ae)
         self.last_cb0_logits = {}
         for k, (i, s) in enumerate(zip(act, ss)):
             frames[i] = fr[k]
+            if ff is not None:
+                s.steps_taken += 1
+                s.last_hidden = hs[k]
+                if k in urow:
+                    s.last_hidden_u = hs[urow[k]]
+                nxt[i] = 0
+                continue
             lk = combine_logits(ls[k], ls[urow[k]] if k in urow else None, s.cfg)
             self.last_cb0_logits[s.sid] = (apply_penalties(lk, s.sp.rep, s.hist, m.cfg.cb_size, m.cfg.vs),
                                            s.rng.key, s.rng.draw)
