@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--model-dir", default=os.environ.get("BZB_MODEL_DIR", "/tmp/bzb_models"))
     ap.add_argument("--cpu-sample-sessions", type=int, default=4)
     ap.add_argument("--ttfa-arrivals", type=int, default=8, help="sessions admitted into the running batch for TTFA")
+    ap.add_argument("--no-burst-admission", action="store_true",
+                    help="skip the all-arrive-at-once admission measurement (sequential vs batched create)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt-cap", type=int, default=0, help="cap text prompt length (profiling runs)")
     ap.add_argument("--profile", action="store_true",
@@ -181,6 +183,55 @@ def measure_ttfa(pkg, gen, ids, seeds, n_arrivals: int, seed: int):
                       "host wall clock through the C ABI"}
 
 
+def session_specs(pkg, sessions, nc):
+    """The arguments of each session's creation (reference frames seeded by session id)."""
+    specs = []
+    for sid, s in enumerate(sessions):
+        sp = dict(session_id=sid, text=pkg.ids_to_text(s["ids"]), seed=s["seed"], max_new_tokens=s["gen_len"])
+        if s["vframes"] > 0:
+            sp.update(ref_codes=np.random.default_rng(sid).integers(0, 2048, (s["vframes"], nc)).astype(np.int32),
+                      ref_text=pkg.ids_to_text(s["ref_ids"]), ref_frames=s["vframes"])
+        specs.append(sp)
+    return specs
+
+
+def measure_burst_admission(pkg, gen, specs, seeds):
+    """Every session arriving at once (host wall clock through the C ABI): the sessions created one
+    call at a time, then, after freeing them, all in one batched call (prompts prefilled as packed
+    rows); then the whole batch steps CHUNK_FIRST frames and the vocoder decodes every session's
+    first chunk in one batched call. burst_ttfa_ms is the time until the last arrival has audio."""
+    ids = [sp["session_id"] for sp in specs]
+    for sid in ids:
+        gen.session_free(sid)
+    gen.sync()
+    t0 = time.perf_counter()
+    for sp in specs:
+        kw = {k: v for k, v in sp.items() if k not in ("session_id", "text")}
+        gen.session_create_ext(sp["session_id"], sp["text"], **kw)
+    seq_ms = (time.perf_counter() - t0) * 1e3
+    for sid in ids:
+        gen.session_free(sid)
+    voc = pkg.VocoderHandle(generator=gen)
+    try:
+        gen.sync()
+        t0 = time.perf_counter()
+        gen.sessions_create_batch(specs)
+        t1 = time.perf_counter()
+        _, frames, _ = gen.step_frames(ids, CHUNK_FIRST, seeds + 9000)
+        t2 = time.perf_counter()
+        pcm = voc.session_decode_batch([30_000 + i for i in range(len(ids))], [frames[:, i, :] for i in range(len(ids))])
+        t3 = time.perf_counter()
+        assert all(p.size == CHUNK_FIRST * 1920 for p in pcm)
+    finally:
+        voc.close()
+    return {"arrivals": len(ids), "sequential_create_ms": seq_ms, "batch_create_ms": (t1 - t0) * 1e3,
+            "first_chunk_steps_ms": (t2 - t1) * 1e3, "vocoder_batch_ms": (t3 - t2) * 1e3,
+            "burst_ttfa_ms": (t3 - t0) * 1e3,
+            "method": f"{len(ids)} sessions arriving together: one batched create (packed prefill of every prompt), "
+                      f"{CHUNK_FIRST} batched frame steps, one batched vocoder decode of every first chunk; "
+                      "sequential_create_ms creates the same sessions one call at a time"}
+
+
 def cpu_oracle_rtf(path: str, n_sessions: int, steps: int, warmup: int, seed: int = 7):
     """Aggregate RTF of the CPU port (numpy, all host threads) on a bounded sample: n sessions
     with 32-token prompts (prefill untimed), `steps` timed frame steps after `warmup`."""
@@ -310,6 +361,9 @@ def main():
     prof = gen.profile_step()
     launches = gen.launches_per_step()
     ttfa = measure_ttfa(pkg, gen, ids, seeds, args.ttfa_arrivals, 5000 + rank) if args.ttfa_arrivals > 0 else None
+    burst = None
+    if not args.no_burst_admission:
+        burst = measure_burst_admission(pkg, gen, session_specs(pkg, sessions, nc), seeds)
 
     step_ms = ms_dev / args.steps
     audio_s = world * args.sessions * args.steps * FRAME_S
@@ -372,6 +426,7 @@ def main():
                               "frac": step_gbs / hbm},
             "cpu_baseline": cpu,
             "ttfa": ttfa,
+            "burst_admission": burst,
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
         }

@@ -115,6 +115,9 @@ SIGNATURES = {
                                           ctypes.c_void_p, _c_int_p, ctypes.c_int, _c_int_p, _c_double_p]),
     "bzb_split_text": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]),
     "bzb_write_wav": (ctypes.c_int, [ctypes.c_char_p, _c_float_p, ctypes.c_int, ctypes.c_int]),
+    "bzb_generator_sessions_create_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_int_p, ctypes.c_void_p,
+                                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_int_p,
+                                                           _c_float_p, _c_uint_p, _c_int_p, _c_int_p, _c_int_p]),
     "bzb_generator_encode_audio_full": (ctypes.c_int, [ctypes.c_void_p, _c_float_p, ctypes.c_int, _c_int_p, ctypes.c_int,
                                                        _c_int_p]),
 }
@@ -210,6 +213,43 @@ class GeneratorHandle:
         if res != 0:
             raise RuntimeError(f"Session create ext failed (session {session_id}): {self.lib.last_error()}")
         return cb0.value, alloc.value
+
+    def sessions_create_batch(self, specs: Sequence[dict]) -> Tuple[List[int], List[int]]:
+        """session_create_ext for every spec (dicts of its keyword arguments plus session_id and
+        text) in one call, the prompts prefilled as packed rows. Returns (cb0s, allocations)."""
+        n = len(specs)
+        keep = []
+
+        def strs(key, default=None):
+            arr = (ctypes.c_char_p * max(n, 1))()
+            for i, sp in enumerate(specs):
+                v = sp.get(key, default)
+                arr[i] = v.encode("utf-8") if v else None
+            keep.append(arr)
+            return ctypes.cast(arr, ctypes.c_void_p)
+
+        codes = (ctypes.POINTER(ctypes.c_int) * max(n, 1))()
+        frames = np.zeros(max(n, 1), np.int32)
+        for i, sp in enumerate(specs):
+            rc, rf = sp.get("ref_codes"), int(sp.get("ref_frames", 0))
+            if rc is not None and rf > 0:
+                arr = np.ascontiguousarray(np.asarray(rc, dtype=np.int32).reshape(-1))
+                keep.append(arr)
+                codes[i] = _ip(arr)
+                frames[i] = rf
+        ids = np.asarray([sp["session_id"] for sp in specs] or [0], np.int32)
+        scales = np.asarray([sp.get("cfg_scale", 1.0) for sp in specs] or [1.0], np.float32)
+        seeds = np.asarray([sp.get("seed", 42) & 0xFFFFFFFF for sp in specs] or [0], np.uint32)
+        budgets = np.asarray([sp.get("max_new_tokens", 0) for sp in specs] or [0], np.int32)
+        cb0 = np.zeros(max(n, 1), np.int32)
+        alloc = np.zeros(max(n, 1), np.int32)
+        res = self.lib.lib.bzb_generator_sessions_create_batch(
+            self.handle, n, _ip(ids), strs("text"), strs("instruction", "Speak clearly and naturally."),
+            strs("ref_text"), ctypes.cast(codes, ctypes.c_void_p), _ip(frames), _fp(scales),
+            seeds.ctypes.data_as(_c_uint_p), _ip(budgets), _ip(cb0), _ip(alloc))
+        if res != 0:
+            raise RuntimeError(f"Batched session create failed: {self.lib.last_error()}")
+        return cb0[:n].tolist(), alloc[:n].tolist()
 
     def session_step(self, session_id: int, seed: int) -> Tuple[int, List[int]]:
         fr = np.zeros(16, np.int32)

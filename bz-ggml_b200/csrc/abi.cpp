@@ -786,6 +786,35 @@ int bzb_generate_codes(breeze_context * ctx, const breeze_request * req, const i
     return generate_impl(ctx, req, ref_codes, ref_frames, cb, user, out_codes, max_frames, out_n_frames, out_timings7);
 }
 
+int bzb_generator_sessions_create_batch(breeze_generator * gen, int n, const int * session_ids,
+                                        const char * const * texts, const char * const * instructions,
+                                        const char * const * ref_texts, const int * const * ref_codes,
+                                        const int * ref_frames, const float * cfg_scales, const unsigned int * seeds,
+                                        const int * max_new_tokens, int * out_cb0, int * out_allocated_tokens) {
+    if (!gen || n < 0 || (n > 0 && (!session_ids || !texts || !out_cb0))) return -1;
+    try {
+        std::vector<bzb::CreateSpec> specs(n);
+        for (int i = 0; i < n; i++) {
+            if (!texts[i]) throw std::runtime_error("null text");
+            bzb::CreateSpec & c = specs[i];
+            c.sid = session_ids[i];
+            c.text = texts[i];
+            c.instruction = instructions ? instructions[i] : nullptr;
+            c.ref_text = ref_texts ? ref_texts[i] : nullptr;
+            c.ref_codes = ref_codes ? ref_codes[i] : nullptr;
+            c.ref_frames = ref_frames ? ref_frames[i] : 0;
+            c.cfg_scale = cfg_scales ? cfg_scales[i] : 1.0f;
+            c.seed = seeds ? seeds[i] : 42u;
+            c.max_new_tokens = max_new_tokens ? max_new_tokens[i] : 0;
+        }
+        gen->eng->sessions_create_batch(specs, out_cb0, out_allocated_tokens);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 int bzb_generator_encode_audio_full(breeze_generator * gen, const float * pcm, int n_samples, int * out_codes,
                                     int max_frames, int * out_n_frames) {
     if (!gen || !pcm || n_samples <= 0 || !out_codes || max_frames < 0 || !out_n_frames) return -1;

@@ -434,6 +434,11 @@ void Engine::alloc_buffers() {
     cur_force_ = dalloc<int>((size_t) rmax_ * nc);
     cur_feed_ = dalloc<int>((size_t) rmax_ * nc);
     create_rows_ = dalloc<int>(4);
+    pslot_ = dalloc<int>(kPackSegs);
+    ppair_ = dalloc<int>(kPackSegs);
+    pnext_ = dalloc<int>(kPackSegs);
+    plast_ = dalloc<float>((size_t) kPackSegs * H);
+    plogs_ = dalloc<float>((size_t) kPackSegs * vbb_);
     cur_frames_ = dalloc<int>((size_t) rmax_ * nc);
     frames_all_ = dalloc<int>((size_t) kmax_ * rmax_ * nc);
     step_ctr_ = dalloc<int>(1);
@@ -491,6 +496,11 @@ void Engine::ensure_prefill_capacity(int T) {
     plog_ = (float *) pa((size_t) 2 * vbb_ * 4);   // conditional and unconditional branch
     ptok_ = (int *) pa((size_t) tmax_ * 4);
     pframes_ = (int *) pa((size_t) tmax_ * cfg.nc * 4);
+    pseg_ = (int *) pa((size_t) tmax_ * 4);
+    pidx_ = (int *) pa((size_t) tmax_ * 4);
+    psegs_ = (int4 *) pa((size_t) tmax_ * sizeof(int4));
+    pqb_ = (int2 *) pa((size_t) (tmax_ + tmax_ / kPrefillQBlock + 1) * sizeof(int2));
+    pstage_ = (float *) pa((size_t) tmax_ * H * 4);
     if (has_te_) {
         const TeConfig & te = cfg.te;
         const int teq = te.n_head * te.hd, tekv = te.n_kv * te.hd;
@@ -1245,6 +1255,296 @@ void Engine::session_create_tokens(int sid, const std::vector<std::vector<int>> 
         cudaStreamSynchronize(stream_);
         release_slot(slot);
         throw;
+    }
+}
+
+// ------------------------------------------------------------------------------------ packed prefill
+namespace {
+// per-row segment ids, the segments and the attention query blocks of packed sequences
+void pack_meta(const std::vector<int4> & segs, std::vector<int> & row_seg, std::vector<int2> & qb) {
+    row_seg.clear();
+    qb.clear();
+    for (int i = 0; i < (int) segs.size(); i++) {
+        for (int r = 0; r < segs[i].y; r++) row_seg.push_back(i);
+        for (int r = 0; r < segs[i].y; r += kPrefillQBlock) qb.push_back(make_int2(i, r));
+    }
+}
+}  // namespace
+
+void Engine::te_forward_packed(const std::vector<const std::vector<int> *> & tsegs, float * out_rows) {
+    if (!has_te_) throw std::runtime_error("GGUF has no text encoder (te.*) tensors");
+    const TeConfig & te = cfg.te;
+    std::vector<int> toks;
+    std::vector<int4> segs;
+    for (const std::vector<int> * t : tsegs) {
+        if (t->empty()) throw std::runtime_error("empty text segment");
+        if ((int) t->size() > rope_te_max_) throw std::runtime_error("text segment longer than 4096 tokens");
+        segs.push_back(make_int4((int) toks.size(), (int) t->size(), 0, 0));
+        toks.insert(toks.end(), t->begin(), t->end());
+    }
+    const int T = (int) toks.size();
+    ensure_prefill_capacity(T);
+    std::vector<int> row_seg;
+    std::vector<int2> qb;
+    pack_meta(segs, row_seg, qb);
+    CK(cudaMemcpyAsync(ptok_, toks.data(), T * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(pseg_, row_seg.data(), T * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(psegs_, segs.data(), segs.size() * sizeof(int4), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(pqb_, qb.data(), qb.size() * sizeof(int2), cudaMemcpyHostToDevice, stream_));
+    const int D = te.hidden, q = te.n_head * te.hd, kv = te.n_kv * te.hd, qkvd = q + 2 * kv;
+    launch_embed_rows(te_embd_, ptok_, T, te.embed_scale, tx_, nullptr, D, stream_);
+    for (int l = 0; l < te.n_layer; l++) {
+        const LayerW & w = te_[l];
+        const bool full = l < (int) te.is_full.size() && te.is_full[l] != 0;
+        launch_rmsnorm(tx_, D, w.attn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.qkv, th16_, D, T, GemvOut{ EPI_STORE, tqkv_, nullptr, qkvd });
+        PrefillArgs pa;
+        pa.qkv = tqkv_; pa.ldq = qkvd; pa.T = T; pa.start = 0;
+        pa.n_head = te.n_head; pa.n_kv = te.n_kv; pa.hd = te.hd;
+        pa.q_norm = w.q_norm; pa.k_norm = w.k_norm; pa.eps = te.eps;
+        pa.rope = full ? rope_te_full_ : rope_te_slide_;
+        pa.scale = 1.0f / std::sqrt(te.qpas);
+        pa.flat_k = tk_; pa.flat_v = tv_;
+        pa.window = full ? 0 : te.window;
+        pa.causal = false;
+        pa.out = tatt16_; pa.ldo = q;
+        pa.row_seg = pseg_; pa.segs = psegs_; pa.qblocks = pqb_; pa.n_qblocks = (int) qb.size();
+        launch_qk_prep(pa, false, stream_);
+        launch_attn_prefill(pa, false, stream_);
+        gemv(w.o, tatt16_, q, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
+        launch_norm_add(tx_, ttmp_, D, w.post_attn, te.eps, T, stream_);
+        launch_rmsnorm(tx_, D, w.ffn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.gu, th16_, D, T, GemvOut{ EPI_GEGLU, nullptr, tff16_, te.ffn });
+        gemv(w.down, tff16_, te.ffn, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
+        launch_norm_add(tx_, ttmp_, D, w.post_ffn, te.eps, T, stream_);
+    }
+    launch_rmsnorm(tx_, D, te_out_norm_, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+    gemv(te_proj_, th16_, D, T, GemvOut{ EPI_STORE, out_rows, nullptr, cfg.hidden });
+}
+
+void Engine::bb_prefill_packed(const std::vector<int4> & segs, float * logits) {
+    const BbConfig & bb = cfg.bb;
+    const int H = cfg.hidden, q = bb.n_head * bb.hd, kv = bb.n_kv * bb.hd, qkvd = q + 2 * kv;
+    int T = 0;
+    for (const int4 & g : segs) T = std::max(T, g.x + g.y);
+    const int nb = (int) segs.size();
+    std::vector<int> row_seg, last(nb), slots(nb);
+    std::vector<int2> qb;
+    pack_meta(segs, row_seg, qb);
+    for (int b = 0; b < nb; b++) {
+        last[b] = segs[b].x + segs[b].y - 1;
+        slots[b] = segs[b].z;
+    }
+    CK(cudaMemcpyAsync(pseg_, row_seg.data(), T * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(psegs_, segs.data(), nb * sizeof(int4), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(pqb_, qb.data(), qb.size() * sizeof(int2), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(pidx_, last.data(), nb * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(pslot_, slots.data(), nb * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    for (int l = 0; l < bb.n_layer; l++) {
+        const LayerW & w = bb_[l];
+        launch_rmsnorm(px_, H, w.attn_norm, H, bb.eps, ph16_, H, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.qkv, ph16_, H, T, GemvOut{ EPI_STORE, pqkv_, nullptr, qkvd });
+        PrefillArgs pa;
+        pa.qkv = pqkv_; pa.ldq = qkvd; pa.T = T; pa.start = 0;
+        pa.n_head = bb.n_head; pa.n_kv = bb.n_kv; pa.hd = bb.hd;
+        pa.q_norm = w.q_norm; pa.k_norm = w.k_norm; pa.eps = bb.eps; pa.rope = rope_bb_;
+        pa.scale = 1.0f / std::sqrt((float) bb.hd);
+        pa.kv.pool = kv_pool_; pa.kv.n_layer = bb.n_layer; pa.kv.layer = l;
+        pa.kv.page_table = page_table_; pa.kv.max_pages = max_pages_;
+        pa.causal = true;
+        pa.out = patt16_; pa.ldo = q;
+        pa.row_seg = pseg_; pa.segs = psegs_; pa.qblocks = pqb_; pa.n_qblocks = (int) qb.size();
+        launch_qk_prep(pa, true, stream_);
+        launch_attn_prefill(pa, true, stream_);
+        gemv(w.o, patt16_, q, T, GemvOut{ EPI_RESID, px_, nullptr, H });
+        launch_rmsnorm(px_, H, w.ffn_norm, H, bb.eps, ph16_, H, nullptr, 0, 0, T, nullptr, stream_);
+        gemv(w.gu, ph16_, H, T, GemvOut{ EPI_SWIGLU, nullptr, pff16_, bb.ffn });
+        gemv(w.down, pff16_, bb.ffn, T, GemvOut{ EPI_RESID, px_, nullptr, H });
+    }
+    // each segment's last row: hidden (normed, kept per slot) and logits
+    launch_copy_rows(px_, H, pidx_, plast_, H, nullptr, nb, H, stream_);
+    launch_rmsnorm(plast_, H, bb_out_norm_, H, bb.eps, ph16_, H, hid32_, H, 0, nb, pslot_, stream_);
+    gemv(lm_head_, ph16_, H, nb, GemvOut{ EPI_STORE, logits, nullptr, vbb_ });
+}
+
+void Engine::sessions_create_batch(const std::vector<CreateSpec> & specs, int * out_cb0, int * out_alloc) {
+    const int H = cfg.hidden, nc = cfg.nc;
+    const int n = (int) specs.size();
+    {
+        std::vector<int> ids;
+        for (const CreateSpec & c : specs) ids.push_back(c.sid);
+        std::sort(ids.begin(), ids.end());
+        if (std::adjacent_find(ids.begin(), ids.end()) != ids.end()) throw std::runtime_error("a session id appears twice in one batch");
+    }
+    // the prompts, budgets and sampler of session_create for every spec
+    struct Prep {
+        SessionParams sp;
+        std::vector<std::vector<int>> segs, segs_u;
+        bool ref = false;
+        int total = 0, total_u = 0, est = 0;
+    };
+    std::vector<Prep> prep(n);
+    const std::string spk = "[S0]";
+    for (int i = 0; i < n; i++) {
+        const CreateSpec & c = specs[i];
+        Prep & p = prep[i];
+        p.sp = abi_params(c.cfg_scale);
+        int est = c.max_new_tokens;
+        if (est <= 0) {
+            int words = 0;
+            bool in_w = false;
+            for (unsigned char ch : c.text) {
+                if (std::isspace(ch)) in_w = false;
+                else if (!in_w) { in_w = true; words++; }
+            }
+            est = std::min(1000, (int) std::ceil(words * 1.5f) + 30);
+        }
+        const std::string ins = c.instruction ? c.instruction : "Speak clearly and naturally.";
+        p.ref = c.ref_codes != nullptr && c.ref_frames > 0 && c.ref_text != nullptr && std::strlen(c.ref_text) > 0;
+        if (p.ref) p.segs.push_back(tok_.encode(spk + c.ref_text, true));
+        p.segs.push_back(tok_.encode(spk + "<ins_bos>" + ins + "<ins_eos>" + c.text, true));
+        if (p.sp.cfg != 1.0f) {
+            if (p.ref) p.segs_u.push_back(p.segs[0]);
+            p.segs_u.push_back(tok_.encode(spk + c.text, true));
+        }
+        auto len = [&](const std::vector<std::vector<int>> & sg) {
+            return p.ref ? (int) sg[0].size() + c.ref_frames + 1 + (int) sg[1].size() : (int) sg.back().size();
+        };
+        p.total = len(p.segs);
+        p.total_u = p.segs_u.empty() ? 0 : len(p.segs_u);
+        const int max_available = 2040 - p.total;
+        if (est > max_available) est = std::max(64, max_available);
+        p.est = est;
+        if ((p.total + est + 8 + 15) / 16 > max_pages_ || (p.total_u && (p.total_u + est + 8 + 15) / 16 > max_pages_))
+            throw std::runtime_error("prompt plus generation budget exceeds 4096 positions");
+    }
+    // groups of sessions whose packed prompts stay within the row and segment budgets
+    for (int g0 = 0; g0 < n;) {
+        int g1 = g0, rows = 0, nseg = 0;
+        while (g1 < n && (g1 == g0 || (rows + prep[g1].total + prep[g1].total_u <= kPackRows &&
+                                       nseg + (prep[g1].total_u ? 2 : 1) <= kPackSegs))) {
+            rows += prep[g1].total + prep[g1].total_u;
+            nseg += prep[g1].total_u ? 2 : 1;
+            g1++;
+        }
+        CK(cudaStreamSynchronize(stream_));
+        // slots (a reused id frees its old slot first, src/c_api.cpp:333-337)
+        std::vector<int> slot_c(g1 - g0, -1), slot_u(g1 - g0, -1);
+        try {
+            for (int i = g0; i < g1; i++) {
+                auto old = sid_to_slot_.find(specs[i].sid);
+                if (old != sid_to_slot_.end()) release_slot(old->second);
+                const Prep & p = prep[i];
+                slot_c[i - g0] = acquire_slot(specs[i].sid, (p.total + p.est + 8 + 15) / 16);
+                if (p.total_u) {
+                    slot_u[i - g0] = acquire_slot(specs[i].sid, (p.total_u + p.est + 8 + 15) / 16, false);
+                    slots_[slot_c[i - g0]].partner = slot_u[i - g0];
+                }
+            }
+            ensure_prefill_capacity(rows);
+            // packed rows: branch by branch ([ref text][ref frames][EOS] tail), conditional first
+            std::vector<int4> segs;                       // {first row, rows, slot, session index}
+            std::vector<const std::vector<int> *> tsegs;  // text segments in encoder order
+            std::vector<int> tdst, fdst, frames;          // destination rows of encoder / embedding rows
+            int row = 0;
+            for (int i = g0; i < g1; i++) {
+                const Prep & p = prep[i];
+                for (int br = 0; br < (p.total_u ? 2 : 1); br++) {
+                    const std::vector<std::vector<int>> & sg = br ? p.segs_u : p.segs;
+                    const int first = row;
+                    auto text = [&](const std::vector<int> & t) {
+                        tsegs.push_back(&t);
+                        for (int r = 0; r < (int) t.size(); r++) tdst.push_back(row + r);
+                        row += (int) t.size();
+                    };
+                    if (p.ref) {
+                        text(sg[0]);
+                        frames.insert(frames.end(), specs[i].ref_codes, specs[i].ref_codes + (size_t) specs[i].ref_frames * nc);
+                        for (int f = 0; f < specs[i].ref_frames; f++) fdst.push_back(row + f);
+                        row += specs[i].ref_frames;
+                        frames.insert(frames.end(), (size_t) nc, cfg.cb_eos);
+                        fdst.push_back(row++);
+                        text(sg[1]);
+                    } else {
+                        text(sg.back());
+                    }
+                    segs.push_back(make_int4(first, row - first, br ? slot_u[i - g0] : slot_c[i - g0], i));
+                }
+            }
+            // text encoder over every text segment, placed into the prompt rows
+            te_forward_packed(tsegs, pstage_);
+            CK(cudaMemcpyAsync(pidx_, tdst.data(), tdst.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            launch_copy_rows(pstage_, H, nullptr, px_, H, pidx_, (int) tdst.size(), H, stream_);
+            // audio-frame embeddings of the reference segments
+            if (!fdst.empty()) {
+                const int F = (int) fdst.size();
+                CK(cudaMemcpyAsync(pframes_, frames.data(), frames.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+                launch_audio_embed(audio_embd_, pframes_, nc, nc, cfg.vs, F, pstage_, nullptr, stream_);
+                CK(cudaMemcpyAsync(pidx_, fdst.data(), F * sizeof(int), cudaMemcpyHostToDevice, stream_));
+                launch_copy_rows(pstage_, H, nullptr, px_, H, pidx_, F, H, stream_);
+            }
+            CK(cudaStreamSynchronize(stream_));  // host vectors feeding the copies go out of scope
+            bb_prefill_packed(segs, plogs_);
+            // session states, histories, and the first cb0 of every session (guidance-combined)
+            const int nb = (int) segs.size();
+            std::vector<int> rslot(nb), rpair(nb, -1), lead_of_spec(g1 - g0, -1);
+            for (int b = 0; b < nb; b++) {
+                const int i = segs[b].w;
+                const Prep & p = prep[i];
+                const bool is_u = segs[b].z == slot_u[i - g0];
+                rslot[b] = segs[b].z;
+                SessState st{};
+                st.active = 1;
+                st.pos = is_u ? p.total_u : p.total;
+                st.max_tokens = p.est;
+                st.last_cb0 = -1;
+                st.key = specs[i].seed;
+                st.top_k = p.sp.top_k; st.temp = p.sp.temp; st.top_p = p.sp.top_p; st.rep = p.sp.rep;
+                st.cfg = p.total_u ? p.sp.cfg : 1.0f;
+                st.dtemp = p.sp.dtemp; st.dtop_p = p.sp.dtop_p; st.dtop_k = p.sp.dtop_k;
+                CK(cudaMemcpyAsync(st_ + segs[b].z, &st, sizeof(SessState), cudaMemcpyHostToDevice, stream_));
+                if (!is_u) {
+                    lead_of_spec[i - g0] = b;
+                    CK(cudaMemsetAsync(hist_ + (size_t) segs[b].z * hist_ld_, 0, hist_ld_ * sizeof(uint16_t), stream_));
+                } else {
+                    rpair[lead_of_spec[i - g0]] = b;
+                    rpair[b] = -2 - lead_of_spec[i - g0];
+                }
+            }
+            CK(cudaMemcpyAsync(pslot_, rslot.data(), nb * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            CK(cudaMemcpyAsync(ppair_, rpair.data(), nb * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            SampleArgs sm;
+            sm.logits = plogs_; sm.ld = vbb_; sm.V = vbb_; sm.R = nb;
+            sm.row_slot = pslot_; sm.row_active = nullptr; sm.st = st_; sm.hist = hist_; sm.hist_ld = hist_ld_;
+            sm.row_pair = ppair_;
+            sm.sup_lo = cfg.cb_size; sm.sup_hi = cfg.vs; sm.eos = cfg.bb_eos;
+            sm.next_out = pnext_; sm.update_hist_first = 1;
+            launch_sample(sm, stream_);
+            std::vector<int> nx(nb);
+            CK(cudaMemcpyAsync(nx.data(), pnext_, nb * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+            CK(cudaStreamSynchronize(stream_));
+            for (int i = g0; i < g1; i++) {
+                const Prep & p = prep[i];
+                SlotHost & sh = slots_[slot_c[i - g0]];
+                sh.active = true;
+                sh.max_tokens = p.est;
+                sh.alloc = p.total + p.est + 8;
+                sh.dtop_k = p.sp.dtop_k;
+                if (slot_u[i - g0] >= 0) {
+                    slots_[slot_u[i - g0]].active = true;
+                    slots_[slot_u[i - g0]].max_tokens = p.est;
+                    slots_[slot_u[i - g0]].alloc = p.total_u + p.est + 8;
+                }
+                out_cb0[i] = nx[lead_of_spec[i - g0]];
+                if (out_alloc) out_alloc[i] = p.total + p.est + 8 + (p.total_u ? p.total_u + p.est + 8 : 0);
+            }
+        } catch (...) {
+            cudaStreamSynchronize(stream_);
+            for (int k = 0; k < g1 - g0; k++)
+                if (slot_c[k] >= 0) release_slot(slot_c[k]);
+            throw;
+        }
+        g0 = g1;
     }
 }
 

@@ -50,6 +50,18 @@ struct StepForce {
     const int * feed = nullptr;
 };
 
+// one session of a batched creation (the arguments of breeze_generator_session_create_ext)
+struct CreateSpec {
+    int sid = 0;
+    std::string text;
+    const char * instruction = nullptr, * ref_text = nullptr;
+    const int * ref_codes = nullptr;
+    int ref_frames = 0;
+    float cfg_scale = 1.0f;
+    uint32_t seed = 0;
+    int max_new_tokens = 0;
+};
+
 struct StepResult {
     int steps_executed = 0;
     int still_active = 0;
@@ -79,6 +91,12 @@ public:
     SessionParams abi_params(float cfg_scale) const;
     const Tokenizer & tokenizer() const { return tok_; }
     bool session_free(int sid);
+    // many session_create calls at once (the same prompts, budgets and first cb0 semantics), their
+    // prompts prefilled as packed rows: one text-encoder pass and one backbone pass per group of
+    // sessions instead of two per session
+    void sessions_create_batch(const std::vector<CreateSpec> & specs, int * out_cb0, int * out_alloc);
+    static constexpr int kPackRows = 16384;  // prompt rows of one packed prefill pass
+    static constexpr int kPackSegs = 256;    // branches (prompts) of one packed prefill pass
     // the Q4_K depth override (src/c_api.cpp:532-578): dd.* of a second GGUF, used for the depth
     // codes of the sessions flagged with session_set_q4; loading again replaces it
     void load_q4_depth(const std::string & path);
@@ -158,6 +176,11 @@ private:
     void depth_layer(int l, int rows, int R, int n_new, int start);
     void bb_decode_layer(int l, int R);
     void te_forward(const std::vector<int> & tokens, float * out_rows);
+    // text encoder over several token segments at once: out [sum of lengths][hidden], segment order
+    void te_forward_packed(const std::vector<const std::vector<int> *> & segs, float * out_rows);
+    // backbone prefill of the packed prompt rows in px_: segment b = rows [first_b, first_b + len_b)
+    // of slot_b; writes each segment's last hidden to hid32[slot] and its lm_head logits to logits[b]
+    void bb_prefill_packed(const std::vector<int4> & segs, float * logits);
     void bb_prefill(int slot, int T, float * logits);
     void ensure_prefill_capacity(int T);
     cudaGraphExec_t graph_for(int R, int flags);
@@ -240,6 +263,12 @@ private:
     half * ph16_ = nullptr, * pff16_ = nullptr, * patt16_ = nullptr, * th16_ = nullptr, * tff16_ = nullptr,
          * tatt16_ = nullptr;
     int * ptok_ = nullptr, * pframes_ = nullptr;
+    // packed prefill: per-row segment, segments, attention query blocks, row copy indices, the
+    // text-encoder / audio-embedding output rows before they are placed, logits per segment
+    int * pseg_ = nullptr, * pidx_ = nullptr, * pslot_ = nullptr, * ppair_ = nullptr, * pnext_ = nullptr;
+    int4 * psegs_ = nullptr;
+    int2 * pqb_ = nullptr;
+    float * pstage_ = nullptr, * plast_ = nullptr, * plogs_ = nullptr;
     std::vector<void *> prefill_allocs_;
 
     // profiling of one eager step

@@ -709,7 +709,13 @@ __global__ void qk_prep_kernel(const PrefillArgs a) {
     constexpr int E = HD / 32;
     const int r = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int p = a.start + r;
+    int p = a.start + r;
+    const int * page_row = a.page_row;
+    if (a.segs) {
+        const int4 sg = a.segs[a.row_seg[r]];
+        p = r - sg.x;
+        if (PAGED) page_row = a.kv.page_table + (size_t) sg.z * a.kv.max_pages;
+    }
     float * row = a.qkv + (size_t) r * a.ldq;
     const int tasks = a.n_head + 2 * a.n_kv;
     for (int task = warp; task < tasks; task += nw) {
@@ -728,7 +734,7 @@ __global__ void qk_prep_kernel(const PrefillArgs a) {
 #pragma unroll
             for (int e = 0; e < E; e++) src[lane + 32 * e] = x[e];
         } else if (PAGED) {
-            half * dst = a.kv.pool + paged_off(a.kv, a.page_row, p, kind - 1, h, a.n_kv, HD);
+            half * dst = a.kv.pool + paged_off(a.kv, page_row, p, kind - 1, h, a.n_kv, HD);
 #pragma unroll
             for (int e = 0; e < E; e++) dst[lane + 32 * e] = __float2half_rn(x[e]);
         } else {
@@ -739,7 +745,7 @@ __global__ void qk_prep_kernel(const PrefillArgs a) {
     }
 }
 
-constexpr int kPrefillQB = 8;
+constexpr int kPrefillQB = kPrefillQBlock;
 
 template <int HD, bool PAGED>
 __global__ void attn_prefill_kernel(const PrefillArgs a) {
@@ -752,9 +758,18 @@ __global__ void attn_prefill_kernel(const PrefillArgs a) {
     float * sk = psm;                         // [32][HD+1]
     float * sv = sk + 32 * (HD + 1);          // [32][HD+1]
     float * sq = sv + 32 * (HD + 1);          // [G][QB][HD]
-    const int r0 = blockIdx.x * QB, h = blockIdx.y;
+    // this CTA's sequence: rows [base, base + T) of the packed rows (one sequence: all of them)
+    int base = 0, T = a.T, r0 = blockIdx.x * QB;
+    const int * page_row = a.page_row;
+    if (a.qblocks) {
+        const int2 qb = a.qblocks[blockIdx.x];
+        const int4 sg = a.segs[qb.x];
+        base = sg.x; T = sg.y; r0 = qb.y;
+        if (PAGED) page_row = a.kv.page_table + (size_t) sg.z * a.kv.max_pages;
+    }
+    const int h = blockIdx.y;
     const int qh = h * G + warp;
-    const int nq = min(QB, a.T - r0);
+    const int nq = min(QB, T - r0);
     const int left = (a.window + 1) / 2, right = a.window / 2 + 1;
     int lo[QB], hi[QB];
     int lo_min = INT_MAX, hi_max = 0;
@@ -762,13 +777,13 @@ __global__ void attn_prefill_kernel(const PrefillArgs a) {
         const int r = r0 + i;
         if (i >= nq) { lo[i] = 0; hi[i] = 0; continue; }
         if (a.causal) { lo[i] = 0; hi[i] = a.start + r + 1; }
-        else if (a.window > 0) { lo[i] = max(0, r - left + 1); hi[i] = min(a.T, r + right); }
-        else { lo[i] = 0; hi[i] = a.T; }
+        else if (a.window > 0) { lo[i] = max(0, r - left + 1); hi[i] = min(T, r + right); }
+        else { lo[i] = 0; hi[i] = T; }
         lo_min = min(lo_min, lo[i]);
         hi_max = max(hi_max, hi[i]);
     }
     for (int i = 0; i < nq; i++) {
-        const float * src = a.qkv + (size_t) (r0 + i) * a.ldq + qh * HD;
+        const float * src = a.qkv + (size_t) (base + r0 + i) * a.ldq + qh * HD;
         for (int e = 0; e < E; e++) sq[((size_t) warp * QB + i) * HD + lane + 32 * e] = src[lane + 32 * e];
     }
     float m[QB], l[QB], acc[QB][E];
@@ -788,11 +803,11 @@ __global__ void attn_prefill_kernel(const PrefillArgs a) {
             float vk = 0.0f, vv = 0.0f;
             if (p < hi_max) {
                 if (PAGED) {
-                    vk = __half2float(a.kv.pool[paged_off(a.kv, a.page_row, p, 0, h, a.n_kv, HD) + d]);
-                    vv = __half2float(a.kv.pool[paged_off(a.kv, a.page_row, p, 1, h, a.n_kv, HD) + d]);
+                    vk = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 0, h, a.n_kv, HD) + d]);
+                    vv = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 1, h, a.n_kv, HD) + d]);
                 } else {
-                    vk = a.flat_k[((size_t) p * a.n_kv + h) * HD + d];
-                    vv = a.flat_v[((size_t) p * a.n_kv + h) * HD + d];
+                    vk = a.flat_k[((size_t) (base + p) * a.n_kv + h) * HD + d];
+                    vv = a.flat_v[((size_t) (base + p) * a.n_kv + h) * HD + d];
                 }
             }
             sk[j * (HD + 1) + d] = vk;
@@ -836,7 +851,7 @@ __global__ void attn_prefill_kernel(const PrefillArgs a) {
         const float inv = l[i] > 0.0f ? 1.0f / l[i] : 0.0f;
 #pragma unroll
         for (int e = 0; e < E; e++)
-            a.out[(size_t) (r0 + i) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
+            a.out[(size_t) (base + r0 + i) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
     }
 }
 
@@ -1161,6 +1176,16 @@ __global__ void __launch_bounds__(1024) depth_sample_kernel(const DepthSampleArg
     if (pr >= 0) embed_row_f16(sa.embd, (size_t) a.gather_cb * sa.vs + code, sa.din16 + (size_t) pr * sa.H);
 }
 
+__global__ void copy_rows_kernel(const float * src, int lds, const int * src_idx, float * dst, int ldd, const int * dst_idx,
+                                 int cols) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x;
+    const float * sr = src + (size_t) (src_idx ? src_idx[i] : i) * lds;
+    float * dr = dst + (size_t) (dst_idx ? dst_idx[i] : i) * ldd;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) dr[c] = sr[c];
+}
+
 __global__ void stage_forced_kernel(const int * force_all, const int * feed_all, const int * ctr, int n, int * cur_force,
                                     int * cur_feed) {
     pdl_trigger();
@@ -1379,7 +1404,7 @@ template <int HD, bool PAGED>
 static void launch_prefill_t(const PrefillArgs & a, int G, cudaStream_t s) {
     const size_t smem = (size_t) (2 * 32 * (HD + 1) + G * kPrefillQB * HD) * sizeof(float);
     cudaFuncSetAttribute(attn_prefill_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-    dim3 grid((a.T + kPrefillQB - 1) / kPrefillQB, a.n_kv);
+    dim3 grid(a.qblocks ? a.n_qblocks : (a.T + kPrefillQB - 1) / kPrefillQB, a.n_kv);
     launch_k(attn_prefill_kernel<HD, PAGED>, grid, 32 * G, smem, s, a);
 }
 
@@ -1417,6 +1442,13 @@ void launch_depth_sample_gather(const DepthSampleArgs & a, cudaStream_t s) {
     if (a.V > kSortN) throw std::runtime_error("depth sampler: vocabulary larger than 4096");
     if (a.col < 1 || a.col >= a.s.nc) throw std::runtime_error("depth sampler: codebook out of range");
     launch_k(depth_sample_kernel, a.s.R, 1024, 0, s, a);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_copy_rows(const float * src, int lds, const int * src_idx, float * dst, int ldd, const int * dst_idx, int n,
+                      int cols, cudaStream_t s) {
+    if (n <= 0) return;
+    launch_k(copy_rows_kernel, (unsigned) n, 256, 0, s, src, lds, src_idx, dst, ldd, dst_idx, cols);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -122,6 +122,9 @@ void split_q4k_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half 
 // out16[r] = f16(rmsnorm(x[r]) * w) (and out32 when non-null) for rows [r0, r0 + n)
 void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps, half * out16, int ld16,
                     float * out32, int ld32, int r0, int n, const int * row_map, cudaStream_t s);
+// dst[dst_idx ? dst_idx[i] : i][:cols] = src[src_idx ? src_idx[i] : i][:cols] for i < n (f32 rows)
+void launch_copy_rows(const float * src, int lds, const int * src_idx, float * dst, int ldd, const int * dst_idx, int n,
+                      int cols, cudaStream_t s);
 // x[r] += rmsnorm(t[r]) * w  (Gemma post-norms)
 void launch_norm_add(float * x, const float * t, int D, const float * w, float eps, int rows, cudaStream_t s);
 
@@ -178,8 +181,16 @@ struct PrefillArgs {
     bool causal = true;
     half * out = nullptr;
     int ldo = 0;
+    // packed prefill of several sequences in one launch (null: one sequence from `start`): each
+    // row's segment, each segment's {first row, length, KV slot (paged), 0}, and the attention's
+    // query blocks {segment, first query row within it}; positions start at 0 in every segment
+    const int * row_seg = nullptr;
+    const int4 * segs = nullptr;
+    const int2 * qblocks = nullptr;
+    int n_qblocks = 0;
 };
 void launch_qk_prep(const PrefillArgs & a, bool paged, cudaStream_t s);
+constexpr int kPrefillQBlock = 8;  // query rows per attention-prefill CTA
 void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s);
 
 struct StepArgs {

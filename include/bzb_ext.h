@@ -106,6 +106,22 @@ BREEZE_API int bzb_generator_encode_audio_full(breeze_generator * gen, const flo
                                                int max_frames, int * out_n_frames);
 /* The WAV writer of breeze_generate_wav (reference src/audio.cpp:80-107): 16-bit mono PCM at
  * sample_rate. Returns 0, or -1 with breeze_last_error(). */
+/* breeze_generator_session_create_ext (reference src/c_api.cpp:326-445) for n sessions at once:
+ * session i takes session_ids[i], texts[i], instructions[i], ref_texts[i], ref_codes[i] (frame-major
+ * [ref_frames[i]][num_codebooks]), ref_frames[i], cfg_scales[i], seeds[i] and max_new_tokens[i],
+ * and gets the same prompt, budget, slot pages and first cb0 as that call. A NULL list means NULL
+ * entries (instructions: the default instruction; ref_*: no reference), cfg 1, seed 42 or the
+ * length estimate. The prompts of all sessions and both guidance branches are prefilled together as
+ * packed rows (one text-encoder and one backbone pass per group of up to 16384 rows and 256
+ * branches). Returns 0 with out_cb0[i] and out_allocated_tokens[i] (optional) filled, or -1 with
+ * breeze_last_error(); on an error the sessions of earlier groups stay created, those of the failing
+ * group do not. A session id that appears twice is an error. */
+BREEZE_API int bzb_generator_sessions_create_batch(breeze_generator * gen, int n, const int * session_ids,
+                                                   const char * const * texts, const char * const * instructions,
+                                                   const char * const * ref_texts, const int * const * ref_codes,
+                                                   const int * ref_frames, const float * cfg_scales,
+                                                   const unsigned int * seeds, const int * max_new_tokens,
+                                                   int * out_cb0, int * out_allocated_tokens);
 BREEZE_API int bzb_write_wav(const char * path, const float * samples, int n, int sample_rate);
 BREEZE_API int bzb_split_text(const char * text, int budget, int first_budget, char * out, int capacity);
 BREEZE_API int bzb_tokenize(const char * gguf_path, const char * text, int add_bos, int * out_ids, int max_ids);
