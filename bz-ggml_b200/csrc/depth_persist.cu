@@ -27,6 +27,7 @@
 // notices it and returns, copies and MMAs in flight are drained, TMEM is freed, and the host
 // reports the failure.
 #include "depth_persist.cuh"
+#include "q4k.cuh"
 #include "tc_ptx.cuh"
 
 #include <climits>
@@ -595,13 +596,13 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
                     const uint8_t * raw = sR + rs * kRawGroupBytes + within * umat_chunk_bytes(ph.q4);
                     uint4 q0, q1;
-                    half sc, mn = __float2half_rn(0.0f);
+                    half sc = __float2half_rn(0.0f);
+                    uint2 meta = make_uint2(0u, 0u);
                     if (ph.q4) {
-                        // one 32-value Q4_K sub-block: 16 bytes of nibbles, its scale and min
+                        // one 32-value Q4_K sub-block: 16 bytes of nibbles, the row's scale data
                         q0 = *reinterpret_cast<const uint4 *>(raw + (hb * kTileM + r) * 16);
                         q1 = q0;
-                        sc = *reinterpret_cast<const half *>(raw + kTileM * 32 + (hb * kTileM + r) * 2);
-                        mn = *reinterpret_cast<const half *>(raw + kTileM * 32 + 2 * kTileM * 2 + (hb * kTileM + r) * 2);
+                        meta = *reinterpret_cast<const uint2 *>(raw + kTileM * 32 + r * 8);
                     } else {
                         q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
                         q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
@@ -617,12 +618,13 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     const half2 s2 = __halves2half2(sc, sc);
                     uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
                     if (ph.q4) {
-                        const half2 nb2 = __hneg2(__halves2half2(mn, mn));
+                        float qa, qb;
+                        q4k_chunk_scale_min(meta, hb, qa, qb);
                         const uint32_t w4[4] = { q0.x, q0.y, q0.z, q0.w };
 #pragma unroll
                         for (int q = 0; q < 4; q++) {
                             uint32_t o[4];
-                            dq8_nib(w4[q], s2, nb2, o);
+                            dq8_nib_f32(w4[q], qa, qb, o);
                             const int jj = hb * 4 + q;
                             *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                         }

@@ -18,10 +18,12 @@ namespace bzb {
 // int8 (piece (block half, 16-byte half) major, row minor) followed by 2 x 128 f16 block scales
 // ((block half) major, row minor). Gate/up pairs interleave in 16-row groups.
 constexpr int kUChunkBytes = 128 * 64 + 2 * 128 * 2;
-// The same chunk for Q4_K weights (w = a q - b per 32-value sub-block, q in [0, 15]): the 4-bit
-// quants [half][row][16 B] (each 32-bit word holds 8 consecutive values, even ones in nibbles
-// 0-3 and odd ones in nibbles 4-7), then the f16 scales a and the f16 mins b, each [half][row].
-constexpr int kUChunkBytesQ4 = 128 * 32 + 2 * 2 * 128 * 2;
+// The same chunk for Q4_K weights (w = d scale q - dmin min per 32-value sub-block, q in [0, 15]):
+// the 4-bit quants [half][row][16 B] (each 32-bit word holds 8 consecutive values, even ones in
+// nibbles 0-3 and odd ones in nibbles 4-7), then 8 bytes per row: the super-block's f16 d and
+// dmin, the two sub-blocks' 6-bit scales (one byte each), then their 6-bit mins. The kernels form
+// d scale and dmin min as exact f32 products, so a weight is rounded once, to f16.
+constexpr int kUChunkBytesQ4 = 128 * 32 + 128 * 8;
 struct UMat {
     const uint8_t * blk = nullptr;
     int M = 0, MT = 0, K = 0, KC = 0;

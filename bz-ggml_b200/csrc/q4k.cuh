@@ -26,19 +26,34 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t * packed, int s, int
     }
 }
 
-// sub-block s of the super-block at blk: its f16 scale a = d * scale, min b = dmin * min (f32
-// products rounded once to f16) and its 32 values q (0..15)
-__device__ __forceinline__ void q4k_sub_block(const uint8_t * blk, int s, half & a, half & b, uint8_t q[32]) {
-    const float d = __half2float(__ushort_as_half((unsigned short) (blk[0] | (blk[1] << 8))));
-    const float dmin = __half2float(__ushort_as_half((unsigned short) (blk[2] | (blk[3] << 8))));
-    int scale = 0, mn = 0;
+// sub-block s of the super-block at blk as stored: the f16 bits of d and dmin, the 6-bit scale
+// and min, and its 32 values q (0..15)
+__device__ __forceinline__ void q4k_sub_block_raw(const uint8_t * blk, int s, uint16_t & d, uint16_t & dmin,
+                                                  int & scale, int & mn, uint8_t q[32]) {
+    d = (uint16_t) (blk[0] | (blk[1] << 8));
+    dmin = (uint16_t) (blk[2] | (blk[3] << 8));
     q4k_scale_min(blk + 4, s, scale, mn);
-    a = __float2half_rn(d * (float) scale);
-    b = __float2half_rn(dmin * (float) mn);
     const uint8_t * qs = blk + 16 + 32 * (s >> 1);
     const int shift = (s & 1) * 4;
 #pragma unroll
     for (int i = 0; i < 32; i++) q[i] = (uint8_t) ((qs[i] >> shift) & 0x0F);
+}
+
+// sub-block s of the super-block at blk: its f16 scale a = d * scale, min b = dmin * min (f32
+// products rounded once to f16) and its 32 values q (0..15)
+__device__ __forceinline__ void q4k_sub_block(const uint8_t * blk, int s, half & a, half & b, uint8_t q[32]) {
+    uint16_t d = 0, dmin = 0;
+    int scale = 0, mn = 0;
+    q4k_sub_block_raw(blk, s, d, dmin, scale, mn, q);
+    a = __float2half_rn(__half2float(__ushort_as_half(d)) * (float) scale);
+    b = __float2half_rn(__half2float(__ushort_as_half(dmin)) * (float) mn);
+}
+
+// the f32 scale and min of sub-block hb (0 or 1) from a tcgen05 chunk's 8 bytes of row data
+// (f16 d, f16 dmin, u8 scales[2], u8 mins[2]): products of an f16 and a 6-bit integer, exact in f32
+__device__ __forceinline__ void q4k_chunk_scale_min(uint2 meta, int hb, float & a, float & b) {
+    a = __half2float(__ushort_as_half((unsigned short) (meta.x & 0xFFFFu))) * (float) ((meta.y >> (8 * hb)) & 0xFFu);
+    b = __half2float(__ushort_as_half((unsigned short) (meta.x >> 16))) * (float) ((meta.y >> (16 + 8 * hb)) & 0xFFu);
 }
 
 }  // namespace bzb

@@ -90,16 +90,17 @@ __device__ __forceinline__ void dq4(uint32_t w, half2 s, uint32_t & lo, uint32_t
     hi = *reinterpret_cast<uint32_t *>(&hh);
 }
 
-// 8 Q4_K values of one word (even values in nibbles 0-3, odd ones in nibbles 4-7) -> 4 f16
-// pairs a q + nb (nb = -min): 0x6400 | q is the f16 1024 + q exactly, subtracting 1024 leaves q,
-// and one fused multiply-add applies the scale and the min with a single rounding
-__device__ __forceinline__ void dq8_nib(uint32_t w, half2 a, half2 nb, uint32_t o[4]) {
+// 8 Q4_K values of one word (even values in nibbles 0-3, odd ones in nibbles 4-7) -> 4 f16 pairs
+// a q - b: 0x6400 | q is the f16 1024 + q exactly and subtracting 1024 leaves q; a q - b is one
+// f32 fused multiply-add (a and b are exact f32 products), rounded once to f16
+__device__ __forceinline__ void dq8_nib_f32(uint32_t w, float a, float b, uint32_t o[4]) {
     const half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         uint32_t h;
         asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(h) : "r"(w >> (4 * k)), "r"(0x000F000Fu), "r"(0x64006400u));
-        const half2 v = __hfma2(__hsub2(*reinterpret_cast<half2 *>(&h), k1024), a, nb);
+        const float2 q = __half22float2(__hsub2(*reinterpret_cast<half2 *>(&h), k1024));
+        const half2 v = __floats2half2_rn(fmaf(a, q.x, -b), fmaf(a, q.y, -b));
         o[k] = *reinterpret_cast<const uint32_t *>(&v);
     }
 }

@@ -135,18 +135,18 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
             const uint8_t * raw = sR + rs * kRawBytes;
             uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
             if (p.q4) {
-                // one 32-value Q4_K sub-block of row r: 16 bytes of nibbles, its scale and min
+                // one 32-value Q4_K sub-block of row r: 16 bytes of nibbles, the row's scale data
                 const uint4 qv = *reinterpret_cast<const uint4 *>(raw + (hb * kTileM + r) * 16);
-                const half a = *reinterpret_cast<const half *>(raw + kTileM * 32 + (hb * kTileM + r) * 2);
-                const half b = *reinterpret_cast<const half *>(raw + kTileM * 32 + 2 * kTileM * 2 + (hb * kTileM + r) * 2);
+                const uint2 meta = *reinterpret_cast<const uint2 *>(raw + kTileM * 32 + r * 8);
                 mbar_arrive(&raw_empty[rs]);
                 if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
-                const half2 a2 = __halves2half2(a, a), nb2 = __hneg2(__halves2half2(b, b));
+                float a, b;
+                q4k_chunk_scale_min(meta, hb, a, b);
                 const uint32_t w4[4] = { qv.x, qv.y, qv.z, qv.w };
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     uint32_t o[4];
-                    dq8_nib(w4[q], a2, nb2, o);
+                    dq8_nib_f32(w4[q], a, b, o);
                     const int j = hb * 4 + q;
                     *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
@@ -343,7 +343,8 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
 }
 
 // one thread per (tile, chunk, sub-block half, row): the Q4_K sub-block's values repacked into
-// words of 8 (even values in nibbles 0-3, odd in 4-7), with its f16 scale and min
+// words of 8 (even values in nibbles 0-3, odd in 4-7), with the row's d and dmin (half 0 writes
+// them) and the sub-block's 6-bit scale and min bytes
 __global__ void repack_umma_q4k_kernel(const uint8_t * raw, int M, int K, int KC, uint8_t * blk) {
     const long long idx = (long long) blockIdx.x * blockDim.x + threadIdx.x;
     const int MT = (M + kTileM - 1) / kTileM;
@@ -353,12 +354,13 @@ __global__ void repack_umma_q4k_kernel(const uint8_t * raw, int M, int K, int KC
     const int c = (int) (tc % KC), mt = (int) (tc / KC);
     const int row = mt * kTileM + r;
     uint32_t w[4] = { 0u, 0u, 0u, 0u };
-    half a = __float2half_rn(0.0f), b = a;
+    uint16_t d = 0, dmin = 0;  // padded rows: zero scales give zero weights
+    int sc = 0, mn = 0;
     if (row < M) {
         const int v0 = c * kChunkK + hb * 32;  // first value of the sub-block within the row
         const uint8_t * sblk = raw + ((size_t) row * (K / kQ4KBlockValues) + (size_t) (v0 / kQ4KBlockValues)) * kQ4KBlockBytes;
         uint8_t q[32];
-        q4k_sub_block(sblk, (v0 % kQ4KBlockValues) / 32, a, b, q);
+        q4k_sub_block_raw(sblk, (v0 % kQ4KBlockValues) / 32, d, dmin, sc, mn, q);
 #pragma unroll
         for (int wi = 0; wi < 4; wi++)
 #pragma unroll
@@ -367,8 +369,10 @@ __global__ void repack_umma_q4k_kernel(const uint8_t * raw, int M, int K, int KC
     }
     uint8_t * bp = blk + (size_t) tc * kUChunkBytesQ4;
     *reinterpret_cast<uint4 *>(bp + ((size_t) hb * kTileM + r) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-    *reinterpret_cast<half *>(bp + kTileM * 32 + ((size_t) hb * kTileM + r) * 2) = a;
-    *reinterpret_cast<half *>(bp + kTileM * 32 + 2 * kTileM * 2 + ((size_t) hb * kTileM + r) * 2) = b;
+    uint8_t * meta = bp + kTileM * 32 + (size_t) r * 8;
+    if (hb == 0) *reinterpret_cast<uint32_t *>(meta) = (uint32_t) d | ((uint32_t) dmin << 16);
+    meta[4 + hb] = (uint8_t) sc;
+    meta[6 + hb] = (uint8_t) mn;
 }
 
 __global__ void repack_umma_kernel(const uint8_t * raw, int M, int KB, int KC, uint8_t * blk) {

@@ -7,9 +7,10 @@ Two uses are covered:
   (src/c_api.cpp:532-578). It routes the depth codes of flagged sessions through the dd.*
   tensors of a second file.
 
-The kernel dequantises each 32-value sub-block as f16(a q - b). Here a = f16(d * scale) and
-b = f16(dmin * min), fused in one rounding. The GEMM check restates exactly that; the model
-checks use the oracle's f32 dequantisation and its logit tolerance.
+The kernel dequantises each 32-value sub-block as f16(a q - b), with a = d * scale and
+b = dmin * min exact f32 products and a q - b one f32 fused multiply-add. The GEMM check
+restates exactly that; the model checks use the oracle's f32 dequantisation and its logit
+tolerance.
 """
 import numpy as np
 import pytest
@@ -46,20 +47,20 @@ def q4_gen(pkg, q4_model):
 
 
 def kernel_weights_q4k(raw: np.ndarray, rows: int, K: int) -> np.ndarray:
-    """The f16 weights the kernel feeds the tensor cores: per sub-block a = f16(d * scale),
-    b = f16(dmin * min) and w = f16(a q - b) with a single rounding."""
+    """The f16 weights the kernel feeds the tensor cores: per sub-block a = d * scale and
+    b = dmin * min (exact), w = a q - b by one f32 fused multiply-add, then rounded to f16."""
     blocks = raw[: rows * K // 256 * 144].reshape(-1, 144)
     d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
     dmin = blocks[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
     sc, mn = bo.q4k_scale_min(blocks[:, 4:16])
-    a = (d[:, None] * sc.astype(np.float32)).astype(np.float16).astype(np.float64)
-    b = (dmin[:, None] * mn.astype(np.float32)).astype(np.float16).astype(np.float64)
+    a = d[:, None].astype(np.float64) * sc.astype(np.float64)
+    b = dmin[:, None].astype(np.float64) * mn.astype(np.float64)
     qs = blocks[:, 16:]
     q = np.empty((blocks.shape[0], 8, 32), np.float64)
     for s in range(8):
         byte = qs[:, 32 * (s // 2): 32 * (s // 2) + 32]
         q[:, s] = (byte >> (4 * (s % 2))) & 0xF
-    w = (a[:, :, None] * q - b[:, :, None]).astype(np.float16)
+    w = (a[:, :, None] * q - b[:, :, None]).astype(np.float32).astype(np.float16)
     return w.reshape(rows, K).astype(np.float64)
 
 
