@@ -73,6 +73,56 @@ constexpr int kBStages = 6;
 constexpr int kRawBytes = kTileM * kChunkK + 2 * kTileM * 2;   // 8 KB int8 + 512 B scales
 constexpr int kAllThreads = kThreads + 96;
 
+// one producer thread's share of a chunk (weight row r, half hb: two Q8_0 blocks' halves or one
+// Q4_K sub-block), read from the raw ring into registers so the ring slot can be released before
+// the thread waits for its A stage
+struct RawPiece {
+    uint4 q0, q1;
+    uint2 meta;  // Q8_0: the block scale bits in x; Q4_K: the row's d, dmin, scales and mins
+};
+
+__device__ __forceinline__ RawPiece read_piece(const uint8_t * raw, int q4, int r, int hb) {
+    RawPiece pc;
+    if (q4) {
+        pc.q0 = *reinterpret_cast<const uint4 *>(raw + (hb * kTileM + r) * 16);
+        pc.q1 = pc.q0;
+        pc.meta = *reinterpret_cast<const uint2 *>(raw + kTileM * 32 + r * 8);
+    } else {
+        pc.q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
+        pc.q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
+        pc.meta = make_uint2(*reinterpret_cast<const unsigned short *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2), 0u);
+    }
+    return pc;
+}
+
+// the piece dequantised to f16 into row r of a swizzled A stage (arow = the row's 128 bytes)
+__device__ __forceinline__ void write_piece(const RawPiece & pc, int q4, int r, int hb, uint8_t * arow) {
+    if (q4) {
+        float a, b;
+        q4k_chunk_scale_min(pc.meta, hb, a, b);
+        const uint32_t w4[4] = { pc.q0.x, pc.q0.y, pc.q0.z, pc.q0.w };
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t o[4];
+            dq8_nib_f32(w4[q], a, b, o);
+            const int j = hb * 4 + q;
+            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        return;
+    }
+    const half sc = __ushort_as_half((unsigned short) pc.meta.x);
+    const half2 s2 = __halves2half2(sc, sc);
+    const uint32_t w8[8] = { pc.q0.x, pc.q0.y, pc.q0.z, pc.q0.w, pc.q1.x, pc.q1.y, pc.q1.z, pc.q1.w };
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        uint4 o;
+        dq4(w8[2 * q], s2, o.x, o.y);
+        dq4(w8[2 * q + 1], s2, o.z, o.w);
+        const int j = hb * 4 + q;
+        *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
+    }
+}
+
 template <int NT16>
 constexpr int umma_smem_bytes() {
     return 1024 + kAStages * kABytes + kBStages * (16 * NT16 * kChunkK * 2) + kRawStages * kRawBytes;
@@ -132,43 +182,10 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
         for (int c = 0; c < nch; c++) {
             const int rs = c % kRawStages, ab = c % kAStages;
             if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kRawStages) & 1u, p.err);
-            const uint8_t * raw = sR + rs * kRawBytes;
-            uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
-            if (p.q4) {
-                // one 32-value Q4_K sub-block of row r: 16 bytes of nibbles, the row's scale data
-                const uint4 qv = *reinterpret_cast<const uint4 *>(raw + (hb * kTileM + r) * 16);
-                const uint2 meta = *reinterpret_cast<const uint2 *>(raw + kTileM * 32 + r * 8);
-                mbar_arrive(&raw_empty[rs]);
-                if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
-                float a, b;
-                q4k_chunk_scale_min(meta, hb, a, b);
-                const uint32_t w4[4] = { qv.x, qv.y, qv.z, qv.w };
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    uint32_t o[4];
-                    dq8_nib_f32(w4[q], a, b, o);
-                    const int j = hb * 4 + q;
-                    *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                }
-                fence_proxy_async();
-                mbar_arrive(&a_full[ab]);
-                continue;
-            }
-            const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 0) * kTileM + r) * 16);
-            const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + ((hb * 2 + 1) * kTileM + r) * 16);
-            const half sc = *reinterpret_cast<const half *>(raw + kTileM * kChunkK + (hb * kTileM + r) * 2);
+            const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
             mbar_arrive(&raw_empty[rs]);
             if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
-            const half2 s2 = __halves2half2(sc, sc);
-            const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                uint4 o;
-                dq4(w8[2 * q], s2, o.x, o.y);
-                dq4(w8[2 * q + 1], s2, o.z, o.w);
-                const int j = hb * 4 + q;
-                *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
-            }
+            write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
             fence_proxy_async();
             mbar_arrive(&a_full[ab]);
         }
@@ -342,6 +359,163 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     cluster.sync();
 }
 
+// Prefill shape: 256 activation rows per CTA (MMA N = 256), so each dequantised weight chunk feeds
+// four times the rows of the decode shape and the MMA issues 4x the work per instruction. One CTA
+// per (128-row weight tile, 256-row activation tile) over the whole K, no split; the same roles
+// as the decode kernel, and the 8 dequantising warps drain the 128 x 256 f32 accumulator (warp w
+// reads TMEM lanes 32 (w % 4) .. + 31, activation rows 128 (w / 4) .. + 127).
+constexpr int kPN = 256;
+constexpr int kPRawStages = 4;
+constexpr int kPAStages = 2;
+constexpr int kPBStages = 4;
+constexpr int kPBBytes = kPN * kChunkK * 2;
+constexpr int kPrefillSmem = 1024 + kPAStages * kABytes + kPBStages * kPBBytes + kPRawStages * kRawBytes;
+static_assert(kPrefillSmem <= 227 * 1024, "prefill GEMM shared memory");
+
+template <int EPI>
+__global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UParams p, const __grid_constant__ CUtensorMap xmap) {
+    constexpr uint32_t kCols = kPN;
+    constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t) (kPN >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t a_full[kPAStages], a_empty[kPAStages], b_full[kPBStages], b_empty[kPBStages];
+    __shared__ uint64_t raw_full[kPRawStages], raw_empty[kPRawStages], done_bar;
+    __shared__ uint32_t tmem_slot;
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    uint8_t * sA = smem;
+    uint8_t * sB = sA + kPAStages * kABytes;
+    uint8_t * sR = sB + kPBStages * kPBBytes;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x, row0 = blockIdx.y * kPN;
+    const int rows_here = min(kPN, p.rows - row0);
+    const int nch = p.KC;
+
+    if (warp == 8) tmem_alloc(&tmem_slot, kCols);
+    if (tid == 0) {
+        for (int i = 0; i < kPAStages; i++) {
+            mbar_init(&a_full[i], kThreads);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < kPBStages; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < kPRawStages; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kThreads);
+        }
+        mbar_init(&done_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    pdl_trigger();
+    bool ok = true;
+
+    if (warp < 8) {
+        const int r = tid & (kTileM - 1), hb = tid >> 7;
+        for (int c = 0; c < nch; c++) {
+            const int rs = c % kPRawStages, ab = c % kPAStages;
+            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kPRawStages) & 1u, p.err);
+            const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
+            mbar_arrive(&raw_empty[rs]);
+            if (c >= kPAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kPAStages) - 1) & 1u, p.err);
+            write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
+            fence_proxy_async();
+            mbar_arrive(&a_full[ab]);
+        }
+    } else if (warp == 8) {
+        if (lane == 0) {
+            for (int c = 0; c < nch; c++) {
+                const int ab = c % kPAStages, bb = c % kPBStages;
+                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (c / kPBStages) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kPAStages) & 1u, p.err);
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kPBBytes);
+#pragma unroll
+                for (int kk = 0; kk < kChunkK / 16; kk++)
+                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&a_empty[ab]);
+                umma_commit(&b_empty[bb]);
+            }
+            umma_commit(&done_bar);
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            const int cb = umat_chunk_bytes(p.q4);
+            const uint8_t * base = p.blk + (size_t) mt * p.KC * cb;
+            for (int c = 0; c < nch; c++) {
+                const int rs = c % kPRawStages;
+                if (c >= kPRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kPRawStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&raw_full[rs], (uint32_t) cb);
+                bulk_g2s(sR + rs * kRawBytes, base + (size_t) c * cb, (uint32_t) cb, &raw_full[rs]);
+            }
+        }
+    } else {
+        if (lane == 0) {
+            pdl_wait();  // activations come from the previous kernel
+            for (int c = 0; c < nch; c++) {
+                const int bb = c % kPBStages;
+                if (c >= kPBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kPBStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&b_full[bb], kPBBytes);
+                tma_2d(sB + bb * kPBBytes, &xmap, c * kChunkK, row0, &b_full[bb]);
+            }
+        }
+    }
+    pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed
+
+    if (warp < 8) {
+        if (ok) ok = mbar_wait(&done_bar, 0u, p.err);
+        tc_fence_after();
+        const int q = warp & 3, h = warp >> 2;
+        const uint32_t taddr = tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (128 * h);
+        const int m = mt * kTileM + 32 * q + lane;
+        for (int sl = 0; sl < 8; sl++) {
+            const int n0 = 128 * h + 16 * sl;  // warp-uniform
+            if (n0 >= rows_here) break;
+            float v[16];
+            tmem_ld16(taddr + 16 * sl, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
+            if (!ok)
+#pragma unroll
+                for (int e = 0; e < 16; e++) v[e] = 0.0f;
+            if (EPI == EPI_STORE || EPI == EPI_RESID) {
+                if (m < p.M) {
+                    if (EPI == EPI_RESID) {
+                        float old[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++)
+                            old[e] = n0 + e < rows_here ? p.out.f32[(size_t) (row0 + n0 + e) * p.out.ld + m] : 0.0f;
+#pragma unroll
+                        for (int e = 0; e < 16; e++) v[e] += old[e];
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; e++)
+                        if (n0 + e < rows_here) p.out.f32[(size_t) (row0 + n0 + e) * p.out.ld + m] = v[e];
+                }
+            } else {
+                // 16-row interleave: lanes 0-15 hold gate rows, lanes 16-31 the matching up rows
+                const int j = mt * (kTileM / 2) + 16 * q + lane;
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const float up = __shfl_sync(0xffffffffu, v[e], lane + 16);
+                    if (lane < 16 && n0 + e < rows_here && j < (p.M >> 1)) {
+                        const float g = v[e];
+                        const float act = EPI == EPI_SWIGLU ? silu_f(g) : gelu_tanh_f(g);
+                        p.out.f16[(size_t) (row0 + n0 + e) * p.out.ld + j] = __float2half_rn(act * up);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) tmem_dealloc(tmem, kCols);
+}
+
 // one thread per (tile, chunk, sub-block half, row): the Q4_K sub-block's values repacked into
 // words of 8 (even values in nibbles 0-3, odd in 4-7), with the row's d and dmin (half 0 writes
 // them) and the sub-block's 6-bit scale and min bytes
@@ -438,6 +612,25 @@ void launch_one(const UParams & p, const CUtensorMap & map, dim3 grid, cudaStrea
     UCHECK(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<NT16, EPI>, p, map));
 }
 
+template <int EPI>
+void launch_prefill_one(const UParams & p, const CUtensorMap & map, dim3 grid, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kAllThreads);
+    cfg.dynamicSmemBytes = kPrefillSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    int na = 0;
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    UCHECK(cudaLaunchKernelEx(&cfg, umma_prefill_kernel<EPI>, p, map));
+}
+
 template <int NT16>
 void launch_nt(const UParams & p, const CUtensorMap & map, dim3 grid, cudaStream_t s, bool pdl) {
     switch (p.out.kind) {
@@ -493,6 +686,11 @@ CUtensorMap make_x_group_map(const half * x, int K, int ldx, int rows, int box_r
 
 
 void init_umma_attributes() {
+    for (const void * f : { (const void *) umma_prefill_kernel<EPI_STORE>, (const void *) umma_prefill_kernel<EPI_RESID>,
+                            (const void *) umma_prefill_kernel<EPI_SWIGLU>, (const void *) umma_prefill_kernel<EPI_GEGLU> }) {
+        cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrefillSmem);
+        cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    }
     set_attr_nt<1>();
     set_attr_nt<2>();
     set_attr_nt<3>();
@@ -533,6 +731,31 @@ void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const
     if (const char * e = std::getenv("BZB_UMMA_SPLITS")) {
         const int f = std::atoi(e);
         if (f == 1 || f == 2 || f == 4 || f == 8) splits = std::min(f, (out.kind >= EPI_SWIGLU) ? 4 : 8);
+    }
+    // Over 64 rows, the 256-row shape runs when it takes fewer chunk steps per SM: a chunk costs
+    // both shapes about the same time (measured), so compare waves of CTAs x chunks per CTA.
+    // BZB_PREFILL_GEMM=0 / 1 forces the decode / prefill shape.
+    if (rows > 64) {
+        const int row_tiles = (rows + kPN - 1) / kPN;
+        const long long t_decode = (long long) ((tiles_chunks * splits + 147) / 148) * ((w.KC + splits - 1) / splits);
+        const long long t_prefill = (long long) ((w.MT * row_tiles + 147) / 148) * w.KC;
+        const char * pm = std::getenv("BZB_PREFILL_GEMM");
+        const int mode = pm ? std::atoi(pm) : -1;
+        if (mode == 1 || (mode != 0 && t_prefill < t_decode)) {
+            UParams p;
+            p.blk = w.blk; p.q4 = w.q4; p.M = w.M; p.MT = w.MT; p.KC = w.KC;
+            p.kc_per_split = w.KC; p.splits = 1;
+            p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.err = err;
+            const CUtensorMap map = make_x_map(x16, w.K, ldx, rows, kPN);
+            const dim3 grid(w.MT, row_tiles);
+            switch (out.kind) {
+                case EPI_STORE: launch_prefill_one<EPI_STORE>(p, map, grid, s, pdl); break;
+                case EPI_RESID: launch_prefill_one<EPI_RESID>(p, map, grid, s, pdl); break;
+                case EPI_SWIGLU: launch_prefill_one<EPI_SWIGLU>(p, map, grid, s, pdl); break;
+                default: launch_prefill_one<EPI_GEGLU>(p, map, grid, s, pdl); break;
+            }
+            return;
+        }
     }
     UParams p;
     p.blk = w.blk; p.q4 = w.q4; p.M = w.M; p.MT = w.MT; p.KC = w.KC;

@@ -47,6 +47,7 @@ def _specs(pkg, cfg, rng):
              ref_text=words(list(range(400, 420))), ref_codes=rng.integers(0, 2048, (9, cfg.nc)).astype(np.int32),
              ref_frames=9),
         dict(session_id=85, text=words(list(range(5000, 5013))), seed=5, max_new_tokens=0),
+        dict(session_id=86, text=words(list(range(7000, 7190))) + " long", seed=6, max_new_tokens=5),
     ]
 
 
@@ -66,20 +67,24 @@ def _create(gen, specs, mode):
 _FLIPS = {}
 
 
-@pytest.mark.parametrize("mode", ["sequential", "batch"])
-def test_batch_create_then_steps_match_oracle(pkg, gen, tiny_oracle, mode):
+@pytest.mark.parametrize("mode", ["sequential", "batch", "batch-prefill-gemm"])
+def test_batch_create_then_steps_match_oracle(pkg, gen, tiny_oracle, mode, monkeypatch):
     """The same checks for one session_create_ext call per session and for the batched call. The
     draws that land across a CDF boundary are counted per session and step in both modes; the
     batch must flip exactly where the one-at-a-time creation does. The tiny random-init model's
     depth logits are near flat (a boundary every ~2% of the mass), so about one draw in ten of
-    these prompts flips in either mode."""
+    these prompts flips in either mode. The third mode forces the 256-row prefill GEMM
+    (BZB_PREFILL_GEMM=1) for every linear of the packed passes (over 300 rows here), so its four
+    epilogues (store, residual add, SwiGLU, GeGLU) run on the same checks."""
+    if mode == "batch-prefill-gemm":
+        monkeypatch.setenv("BZB_PREFILL_GEMM", "1")
     cfg = tiny_oracle.cfg
     ref = bo.Generator(tiny_oracle)
     specs = _specs(pkg, cfg, np.random.default_rng(8))
     # a live session whose id the batch reuses: the batch replaces it (src/c_api.cpp:333-337)
     gen.session_create_ext(81, pkg.ids_to_text([301, 302]), seed=9, max_new_tokens=3)
     try:
-        cb0s, allocs = _create(gen, specs, mode)
+        cb0s, allocs = _create(gen, specs, "sequential" if mode == "sequential" else "batch")
         scales = {}
         for sp, cb0, alloc in zip(specs, cb0s, allocs):
             sid = sp["session_id"]

@@ -38,8 +38,13 @@ def gen(pkg, tiny_model):
 @pytest.mark.parametrize("tensor,sub", [("bb.blk.0.attn_q.weight", -1), ("bb.blk.1.ffn_down.weight", -1),
                                         ("dd.codebooks_head.weight", 3), ("te.blk.0.ffn_gate.weight", -1),
                                         ("bb.lm_head.weight", -1)])
-@pytest.mark.parametrize("rows", [1, 7, 16, 64, 100, 300])
-def test_dequant_gemm_matches_oracle(gen, tiny_oracle, tensor, sub, rows):
+@pytest.mark.parametrize("rows,prefill", [(1, "auto"), (7, "auto"), (16, "auto"), (64, "auto"), (100, "auto"),
+                                          (300, "auto"), (300, "1"), (600, "1"), (2100, "auto")])
+def test_dequant_gemm_matches_oracle(gen, tiny_oracle, tensor, sub, rows, prefill, monkeypatch):
+    """Decode-shaped GEMM (<= 64 rows per CTA, split K) and prefill-shaped GEMM (256 rows per CTA,
+    BZB_PREFILL_GEMM=1 forces it from 256 rows; 2100 rows of the LM head take it by default)."""
+    if prefill != "auto":
+        monkeypatch.setenv("BZB_PREFILL_GEMM", prefill)
     w = tiny_oracle.w(tensor)
     if sub >= 0:
         w = w[sub]

@@ -67,8 +67,11 @@ def kernel_weights_q4k(raw: np.ndarray, rows: int, K: int) -> np.ndarray:
 @pytest.mark.parametrize("tensor,sub", [("bb.blk.0.attn_q.weight", -1), ("bb.blk.1.ffn_down.weight", -1),
                                         ("dd.codebooks_head.weight", 3), ("te.blk.0.ffn_gate.weight", -1),
                                         ("bb.lm_head.weight", -1)])
-@pytest.mark.parametrize("rows", [1, 16, 100])
-def test_q4k_gemm_matches_oracle(q4_gen, q4_oracle, tensor, sub, rows):
+@pytest.mark.parametrize("rows,prefill", [(1, "auto"), (16, "auto"), (100, "auto"), (300, "1")])
+def test_q4k_gemm_matches_oracle(q4_gen, q4_oracle, tensor, sub, rows, prefill, monkeypatch):
+    """Decode-shaped and (forced from 256 rows by BZB_PREFILL_GEMM=1) prefill-shaped GEMM."""
+    if prefill != "auto":
+        monkeypatch.setenv("BZB_PREFILL_GEMM", prefill)
     t = q4_oracle.g.tensors[tensor]
     assert t.type == bo.Q4_K
     w = q4_oracle.w(tensor)
