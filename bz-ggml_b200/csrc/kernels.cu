@@ -745,19 +745,41 @@ __global__ void qk_prep_kernel(const PrefillArgs a) {
     }
 }
 
-constexpr int kPrefillQB = kPrefillQBlock;
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
 
+template <int HD>
+__host__ __device__ constexpr int prefill_kb() { return HD >= 256 ? 32 : 64; }
+template <int HD>
+constexpr size_t prefill_smem() { return (size_t) (kPrefillQBlock + 2 * prefill_kb<HD>()) * (HD + 8) * sizeof(half); }
+
+// Prefill attention on the tensor cores (mma.sync m16n8k16, f16 operands, f32 accumulation and
+// online softmax): one CTA per (query block of 64 rows of one sequence, query head), 4 warps of
+// 16 query rows. Q is staged once as f16; K and V tiles of KB positions are converted to f16 in
+// shared memory (rows padded by 8 halves so ldmatrix rows fall in distinct banks). S = Q K^T
+// comes from ldmatrix fragments of Q and K, P = exp(S - max) is repacked from the accumulator
+// registers into A fragments, and V is read with the transposing ldmatrix. Causal, windowed
+// (text encoder) and full spans are per query row, as in the f32 restatement.
 template <int HD, bool PAGED>
-__global__ void attn_prefill_kernel(const PrefillArgs a) {
+__global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillArgs a) {
     pdl_trigger();
     pdl_wait();
-    constexpr int E = HD / 32;
-    constexpr int QB = kPrefillQB;
-    extern __shared__ float psm[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = blockDim.x >> 5;
-    float * sk = psm;                         // [32][HD+1]
-    float * sv = sk + 32 * (HD + 1);          // [32][HD+1]
-    float * sq = sv + 32 * (HD + 1);          // [G][QB][HD]
+    constexpr int QB = kPrefillQBlock, KB = prefill_kb<HD>(), LD = HD + 8;
+    extern __shared__ __align__(16) unsigned char psm_raw[];
+    half * sq = reinterpret_cast<half *>(psm_raw);  // [QB][LD]
+    half * sk = sq + QB * LD;                        // [KB][LD]
+    half * sv = sk + KB * LD;                        // [KB][LD]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     // this CTA's sequence: rows [base, base + T) of the packed rows (one sequence: all of them)
     int base = 0, T = a.T, r0 = blockIdx.x * QB;
     const int * page_row = a.page_row;
@@ -767,91 +789,151 @@ __global__ void attn_prefill_kernel(const PrefillArgs a) {
         base = sg.x; T = sg.y; r0 = qb.y;
         if (PAGED) page_row = a.kv.page_table + (size_t) sg.z * a.kv.max_pages;
     }
-    const int h = blockIdx.y;
-    const int qh = h * G + warp;
+    const int qh = blockIdx.y, h = qh / (a.n_head / a.n_kv);
     const int nq = min(QB, T - r0);
     const int left = (a.window + 1) / 2, right = a.window / 2 + 1;
-    int lo[QB], hi[QB];
-    int lo_min = INT_MAX, hi_max = 0;
-    for (int i = 0; i < QB; i++) {
-        const int r = r0 + i;
-        if (i >= nq) { lo[i] = 0; hi[i] = 0; continue; }
-        if (a.causal) { lo[i] = 0; hi[i] = a.start + r + 1; }
-        else if (a.window > 0) { lo[i] = max(0, r - left + 1); hi[i] = min(T, r + right); }
-        else { lo[i] = 0; hi[i] = T; }
-        lo_min = min(lo_min, lo[i]);
-        hi_max = max(hi_max, hi[i]);
+    auto span = [&](int r, int & lo, int & hi) {
+        if (a.causal) { lo = 0; hi = a.start + r + 1; }
+        else if (a.window > 0) { lo = max(0, r - left + 1); hi = min(T, r + right); }
+        else { lo = 0; hi = T; }
+    };
+    int lo_min, hi_max, tmp;
+    span(r0, lo_min, tmp);
+    span(r0 + nq - 1, tmp, hi_max);
+    // Q block as f16 (rows past the sequence are zero)
+    for (int i = threadIdx.x; i < QB * (HD / 4); i += blockDim.x) {
+        const int row = i / (HD / 4), c4 = i - row * (HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < nq) v = *reinterpret_cast<const float4 *>(a.qkv + (size_t) (base + r0 + row) * a.ldq + qh * HD + 4 * c4);
+        half2 * d = reinterpret_cast<half2 *>(sq + row * LD + 4 * c4);
+        d[0] = __floats2half2_rn(v.x, v.y);
+        d[1] = __floats2half2_rn(v.z, v.w);
     }
-    for (int i = 0; i < nq; i++) {
-        const float * src = a.qkv + (size_t) (base + r0 + i) * a.ldq + qh * HD;
-        for (int e = 0; e < E; e++) sq[((size_t) warp * QB + i) * HD + lane + 32 * e] = src[lane + 32 * e];
-    }
-    float m[QB], l[QB], acc[QB][E];
+    // this thread's two query rows and their spans
+    const int ra = r0 + 16 * warp + g, rb = ra + 8;
+    int lo_a = 0, hi_a = 0, lo_b = 0, hi_b = 0;
+    if (ra < r0 + nq) span(ra, lo_a, hi_a);
+    if (rb < r0 + nq) span(rb, lo_b, hi_b);
+    const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
+    float o[HD / 8][4];
 #pragma unroll
-    for (int i = 0; i < QB; i++) {
-        m[i] = -INFINITY;
-        l[i] = 0.0f;
-#pragma unroll
-        for (int e = 0; e < E; e++) acc[i][e] = 0.0f;
-    }
-    const int t_begin = (lo_min / 32) * 32;
-    for (int t0 = t_begin; t0 < hi_max; t0 += 32) {
+    for (int n = 0; n < HD / 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+    const uint32_t sq_u = (uint32_t) __cvta_generic_to_shared(sq), sk_u = (uint32_t) __cvta_generic_to_shared(sk),
+                   sv_u = (uint32_t) __cvta_generic_to_shared(sv);
+    for (int t0 = (lo_min / KB) * KB; t0 < hi_max; t0 += KB) {
         __syncthreads();
-        for (int idx = threadIdx.x; idx < 32 * HD; idx += blockDim.x) {
-            const int j = idx / HD, d = idx - (idx / HD) * HD;
-            const int p = t0 + j;
-            float vk = 0.0f, vv = 0.0f;
-            if (p < hi_max) {
+        for (int i = threadIdx.x; i < KB * (HD / 8); i += blockDim.x) {
+            const int j = i / (HD / 8), c8 = i - j * (HD / 8);
+            const int pos = t0 + j;
+            uint4 kq = make_uint4(0u, 0u, 0u, 0u), vq = kq;
+            if (pos < hi_max) {
                 if (PAGED) {
-                    vk = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 0, h, a.n_kv, HD) + d]);
-                    vv = __half2float(a.kv.pool[paged_off(a.kv, page_row, p, 1, h, a.n_kv, HD) + d]);
+                    kq = *reinterpret_cast<const uint4 *>(a.kv.pool + paged_off(a.kv, page_row, pos, 0, h, a.n_kv, HD) + 8 * c8);
+                    vq = *reinterpret_cast<const uint4 *>(a.kv.pool + paged_off(a.kv, page_row, pos, 1, h, a.n_kv, HD) + 8 * c8);
                 } else {
-                    vk = a.flat_k[((size_t) (base + p) * a.n_kv + h) * HD + d];
-                    vv = a.flat_v[((size_t) (base + p) * a.n_kv + h) * HD + d];
+                    const size_t off = ((size_t) (base + pos) * a.n_kv + h) * HD + 8 * c8;
+                    const float4 k0 = *reinterpret_cast<const float4 *>(a.flat_k + off), k1 = *reinterpret_cast<const float4 *>(a.flat_k + off + 4);
+                    const float4 v0 = *reinterpret_cast<const float4 *>(a.flat_v + off), v1 = *reinterpret_cast<const float4 *>(a.flat_v + off + 4);
+                    kq = make_uint4(pack_h2(k0.x, k0.y), pack_h2(k0.z, k0.w), pack_h2(k1.x, k1.y), pack_h2(k1.z, k1.w));
+                    vq = make_uint4(pack_h2(v0.x, v0.y), pack_h2(v0.z, v0.w), pack_h2(v1.x, v1.y), pack_h2(v1.z, v1.w));
                 }
             }
-            sk[j * (HD + 1) + d] = vk;
-            sv[j * (HD + 1) + d] = vv;
+            *reinterpret_cast<uint4 *>(sk + j * LD + 8 * c8) = kq;
+            *reinterpret_cast<uint4 *>(sv + j * LD + 8 * c8) = vq;
         }
         __syncthreads();
+        // S = Q K^T for rows 16w..16w+15 and the tile's KB positions
+        float sc[KB / 8][4];
 #pragma unroll
-        for (int i = 0; i < QB; i++) {
-            if (i >= nq) continue;
-            const int p = t0 + lane;
-            const bool ok = p >= lo[i] && p < hi[i];
-            float sc = -INFINITY;
-            if (ok) {
-                float dot = 0.0f;
-                const float * q = sq + ((size_t) warp * QB + i) * HD;
-#pragma unroll 16
-                for (int d = 0; d < HD; d++) dot += q[d] * sk[lane * (HD + 1) + d];
-                sc = dot * a.scale;
+        for (int n = 0; n < KB / 8; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            uint32_t af[4];
+            const int qr = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, qc = 16 * kk + (lane >> 4) * 8;
+            ldsm_x4(sq_u + (uint32_t) (qr * LD + qc) * 2, af[0], af[1], af[2], af[3]);
+#pragma unroll
+            for (int n2 = 0; n2 < KB / 16; n2++) {
+                uint32_t b0, b1, b2, b3;
+                const int kr = 16 * n2 + (lane & 7) + (lane >> 4) * 8, kc = 16 * kk + ((lane >> 3) & 1) * 8;
+                ldsm_x4(sk_u + (uint32_t) (kr * LD + kc) * 2, b0, b1, b2, b3);
+                mma16816(sc[2 * n2], af, b0, b1);
+                mma16816(sc[2 * n2 + 1], af, b2, b3);
             }
-            const float tmax = warp_max(sc);
-            if (tmax == -INFINITY) continue;
-            const float mn = fmaxf(m[i], tmax);
-            const float corr = expf(m[i] - mn);
-            const float pr = ok ? expf(sc - mn) : 0.0f;
-            l[i] = l[i] * corr + warp_sum(pr);
+        }
+        // masks, running maxima and probabilities (rows ra: elements 0-1, rb: elements 2-3)
+        float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < E; e++) acc[i][e] *= corr;
-            for (int j = 0; j < 32; j++) {
-                const float pj = __shfl_sync(0xffffffffu, pr, j);
-                if (pj != 0.0f) {
+        for (int n = 0; n < KB / 8; n++) {
 #pragma unroll
-                    for (int e = 0; e < E; e++) acc[i][e] += pj * sv[j * (HD + 1) + lane + 32 * e];
-                }
+            for (int e = 0; e < 2; e++) {
+                const int pos = t0 + 8 * n + 2 * tg + e;
+                sc[n][e] = (pos >= lo_a && pos < hi_a) ? sc[n][e] * sl2 : -INFINITY;
+                sc[n][2 + e] = (pos >= lo_b && pos < hi_b) ? sc[n][2 + e] * sl2 : -INFINITY;
+                mx_a = fmaxf(mx_a, sc[n][e]);
+                mx_b = fmaxf(mx_b, sc[n][2 + e]);
             }
-            m[i] = mn;
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+        }
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        // a row with no position yet keeps its (zero) state: its scores are all -inf
+        const float c_a = mn_a == -INFINITY ? 1.0f : exp2f(m_a - mn_a);
+        const float c_b = mn_b == -INFINITY ? 1.0f : exp2f(m_b - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
+        float sum_a = 0.0f, sum_b = 0.0f;
+#pragma unroll
+        for (int n = 0; n < KB / 8; n++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                sc[n][e] = sc[n][e] == -INFINITY ? 0.0f : exp2f(sc[n][e] - mn_a);
+                sc[n][2 + e] = sc[n][2 + e] == -INFINITY ? 0.0f : exp2f(sc[n][2 + e] - mn_b);
+                sum_a += sc[n][e];
+                sum_b += sc[n][2 + e];
+            }
+        }
+        l_a = l_a * c_a + sum_a;
+        l_b = l_b * c_b + sum_b;
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++) {
+            o[n][0] *= c_a; o[n][1] *= c_a;
+            o[n][2] *= c_b; o[n][3] *= c_b;
+        }
+        // O += P V: P's accumulator layout is the A fragment layout of two adjacent position tiles
+#pragma unroll
+        for (int k2 = 0; k2 < KB / 16; k2++) {
+            uint32_t pf[4];
+            pf[0] = pack_h2(sc[2 * k2][0], sc[2 * k2][1]);
+            pf[1] = pack_h2(sc[2 * k2][2], sc[2 * k2][3]);
+            pf[2] = pack_h2(sc[2 * k2 + 1][0], sc[2 * k2 + 1][1]);
+            pf[3] = pack_h2(sc[2 * k2 + 1][2], sc[2 * k2 + 1][3]);
+#pragma unroll
+            for (int n2 = 0; n2 < HD / 16; n2++) {
+                uint32_t b0, b1, b2, b3;
+                const int vr = 16 * k2 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = 16 * n2 + (lane >> 4) * 8;
+                ldsm_x4_t(sv_u + (uint32_t) (vr * LD + vc) * 2, b0, b1, b2, b3);
+                mma16816(o[2 * n2], pf, b0, b1);
+                mma16816(o[2 * n2 + 1], pf, b2, b3);
+            }
         }
     }
 #pragma unroll
-    for (int i = 0; i < QB; i++) {
-        if (i >= nq) continue;
-        const float inv = l[i] > 0.0f ? 1.0f / l[i] : 0.0f;
+    for (int off = 1; off <= 2; off <<= 1) {
+        l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+        l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+    }
+    const float inv_a = l_a > 0.0f ? 1.0f / l_a : 0.0f, inv_b = l_b > 0.0f ? 1.0f / l_b : 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; e++)
-            a.out[(size_t) (base + r0 + i) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
+    for (int n = 0; n < HD / 8; n++) {
+        const int col = qh * HD + 8 * n + 2 * tg;
+        if (ra < r0 + nq)
+            *reinterpret_cast<half2 *>(a.out + (size_t) (base + ra) * a.ldo + col) = __floats2half2_rn(o[n][0] * inv_a, o[n][1] * inv_a);
+        if (rb < r0 + nq)
+            *reinterpret_cast<half2 *>(a.out + (size_t) (base + rb) * a.ldo + col) = __floats2half2_rn(o[n][2] * inv_b, o[n][3] * inv_b);
     }
 }
 
@@ -1401,21 +1483,20 @@ void launch_qk_prep(const PrefillArgs & a, bool paged, cudaStream_t s) {
 }
 
 template <int HD, bool PAGED>
-static void launch_prefill_t(const PrefillArgs & a, int G, cudaStream_t s) {
-    const size_t smem = (size_t) (2 * 32 * (HD + 1) + G * kPrefillQB * HD) * sizeof(float);
+static void launch_prefill_t(const PrefillArgs & a, cudaStream_t s) {
+    const size_t smem = prefill_smem<HD>();
     cudaFuncSetAttribute(attn_prefill_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-    dim3 grid(a.qblocks ? a.n_qblocks : (a.T + kPrefillQB - 1) / kPrefillQB, a.n_kv);
-    launch_k(attn_prefill_kernel<HD, PAGED>, grid, 32 * G, smem, s, a);
+    dim3 grid(a.qblocks ? a.n_qblocks : (a.T + kPrefillQBlock - 1) / kPrefillQBlock, a.n_head);
+    launch_k(attn_prefill_kernel<HD, PAGED>, grid, 128, smem, s, a);
 }
 
 void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s) {
     if (a.T <= 0) return;
-    const int G = a.n_head / a.n_kv;
-    if (G < 1 || G > 8 || a.n_head % a.n_kv) throw std::runtime_error("prefill attention: unsupported head grouping");
+    if (a.n_kv < 1 || a.n_head % a.n_kv) throw std::runtime_error("prefill attention: unsupported head grouping");
     switch (a.hd) {
-        case 64: if (paged) launch_prefill_t<64, true>(a, G, s); else launch_prefill_t<64, false>(a, G, s); break;
-        case 128: if (paged) launch_prefill_t<128, true>(a, G, s); else launch_prefill_t<128, false>(a, G, s); break;
-        case 256: if (paged) launch_prefill_t<256, true>(a, G, s); else launch_prefill_t<256, false>(a, G, s); break;
+        case 64: if (paged) launch_prefill_t<64, true>(a, s); else launch_prefill_t<64, false>(a, s); break;
+        case 128: if (paged) launch_prefill_t<128, true>(a, s); else launch_prefill_t<128, false>(a, s); break;
+        case 256: if (paged) launch_prefill_t<256, true>(a, s); else launch_prefill_t<256, false>(a, s); break;
         default: throw std::runtime_error("prefill attention: head_dim must be 64, 128 or 256");
     }
     BZB_CUDA_CHECK(cudaGetLastError());

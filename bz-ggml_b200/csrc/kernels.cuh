@@ -192,7 +192,7 @@ struct PrefillArgs {
     int n_qblocks = 0;
 };
 void launch_qk_prep(const PrefillArgs & a, bool paged, cudaStream_t s);
-constexpr int kPrefillQBlock = 8;  // query rows per attention-prefill CTA
+constexpr int kPrefillQBlock = 64;  // query rows per attention-prefill CTA
 void launch_attn_prefill(const PrefillArgs & a, bool paged, cudaStream_t s);
 
 struct StepArgs {

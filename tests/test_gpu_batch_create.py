@@ -115,7 +115,7 @@ def test_batch_create_then_steps_match_oracle(pkg, gen, tiny_oracle, mode, monke
                 per[(sid, step)] = f
                 flips += f
         _FLIPS[mode] = per
-        assert flips <= max(flip_budget(4 * len(ids) * cfg.nc), int(0.1 * 4 * len(ids) * cfg.nc)), (flips, sorted(per.items()))
+        assert flips <= flip_budget(4 * len(ids) * cfg.nc), (flips, sorted(per.items()))
         if mode == "batch" and "sequential" in _FLIPS:
             assert per == _FLIPS["sequential"]
     finally:
