@@ -65,15 +65,11 @@ __device__ __forceinline__ void store_out(const UParams & p, int n, int m, float
 }
 
 // roles: warps 0-7 dequantise, warp 8 issues MMAs, warp 9 loads weights, warp 10 loads activations.
-// The raw weight ring is per chunk; the dequantised A tiles and the activation tiles move in
-// groups of kGroup chunks with one barrier hand-over per group. The MMA-issuing thread spends
-// several hundred cycles per hand-over (waits, commits) while the tensor pipe idles, which at
-// one chunk per hand-over paced a chunk at ~0.7 us whatever its N; a group spreads that over
-// kGroup chunks of MMAs.
-constexpr int kGroup = 2;
+// Rings are sized so that no load waits on a recent MMA: activations run up to kBStages chunks
+// ahead and weights kRawStages chunks ahead; the dequantised A tile only needs double buffering.
 constexpr int kRawStages = 8;
-constexpr int kAStages = 2;     // groups
-constexpr int kBStages = 3;     // groups
+constexpr int kAStages = 2;
+constexpr int kBStages = 6;
 constexpr int kRawBytes = kTileM * kChunkK + 2 * kTileM * 2;   // 8 KB int8 + 512 B scales
 constexpr int kAllThreads = kThreads + 96;
 
@@ -129,66 +125,7 @@ __device__ __forceinline__ void write_piece(const RawPiece & pc, int q4, int r, 
 
 template <int NT16>
 constexpr int umma_smem_bytes() {
-    return 1024 + kAStages * kGroup * kABytes + kBStages * kGroup * (16 * NT16 * kChunkK * 2) + kRawStages * kRawBytes;
-}
-
-// The dequantising producers over chunk groups: each thread dequantises its piece of every chunk
-// into the group's A slot; the last chunk of a group publishes the slot (proxy fence + arrival).
-template <int RS, int AG>
-__device__ __forceinline__ void produce_groups(int q4, int nch, int r, int hb, const uint8_t * sR, uint8_t * sA,
-                                               uint64_t * raw_full, uint64_t * raw_empty, uint64_t * a_full,
-                                               uint64_t * a_empty, bool & ok, int * err) {
-    const int roff = (r >> 3) * 1024 + (r & 7) * 128;
-    for (int c = 0; c < nch; c++) {
-        const int g = c / kGroup, within = c - g * kGroup, slot = g % AG, rs = c % RS;
-        if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / RS) & 1u, err);
-        const RawPiece pc = read_piece(sR + rs * kRawBytes, q4, r, hb);
-        mbar_arrive(&raw_empty[rs]);
-        if (within == 0 && g >= AG && ok) ok = mbar_wait(&a_empty[slot], (uint32_t) ((g / AG) - 1) & 1u, err);
-        write_piece(pc, q4, r, hb, sA + (slot * kGroup + within) * kABytes + roff);
-        if (within == kGroup - 1 || c == nch - 1) {
-            fence_proxy_async();
-            mbar_arrive(&a_full[slot]);
-        }
-    }
-}
-
-// The MMA issuer over chunk groups: one wait per operand and one commit per operand per group.
-// bbytes is one chunk's activation tile.
-template <int AG, int BG, uint32_t IDESC>
-__device__ __forceinline__ void mma_groups(int nch, uint32_t tmem, const uint8_t * sA, const uint8_t * sB, int bbytes,
-                                           uint64_t * a_full, uint64_t * a_empty, uint64_t * b_full, uint64_t * b_empty,
-                                           uint64_t * done_bar, bool & ok, int * err) {
-    const int ngr = (nch + kGroup - 1) / kGroup;
-    for (int g = 0; g < ngr; g++) {
-        const int n_in = min(kGroup, nch - g * kGroup), as = g % AG, bs = g % BG;
-        if (ok) ok = mbar_wait(&b_full[bs], (uint32_t) (g / BG) & 1u, err);
-        if (ok) ok = mbar_wait(&a_full[as], (uint32_t) (g / AG) & 1u, err);
-        tc_fence_after();
-        for (int w = 0; w < n_in; w++) {
-            const uint32_t a0 = smem_u32(sA + (as * kGroup + w) * kABytes), b0 = smem_u32(sB + (bs * kGroup + w) * bbytes);
-#pragma unroll
-            for (int kk = 0; kk < kChunkK / 16; kk++)
-                umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), IDESC, (g > 0 || w > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&a_empty[as]);
-        umma_commit(&b_empty[bs]);
-    }
-    umma_commit(done_bar);  // arrives once every MMA above has completed
-}
-
-// The activation loader over chunk groups: the group's tiles land on one barrier.
-template <int BG>
-__device__ __forceinline__ void load_x_groups(int nch, int c_first, int row0, const CUtensorMap * xmap, uint8_t * sB,
-                                              int bbytes, uint64_t * b_full, uint64_t * b_empty, bool & ok, int * err) {
-    const int ngr = (nch + kGroup - 1) / kGroup;
-    for (int g = 0; g < ngr; g++) {
-        const int n_in = min(kGroup, nch - g * kGroup), bs = g % BG;
-        if (g >= BG && ok) ok = mbar_wait(&b_empty[bs], (uint32_t) ((g / BG) - 1) & 1u, err);
-        mbar_expect_tx(&b_full[bs], (uint32_t) (n_in * bbytes));
-        for (int w = 0; w < n_in; w++)
-            tma_2d(sB + (bs * kGroup + w) * bbytes, xmap, (c_first + g * kGroup + w) * kChunkK, row0, &b_full[bs]);
-    }
+    return 1024 + kAStages * kABytes + kBStages * (16 * NT16 * kChunkK * 2) + kRawStages * kRawBytes;
 }
 
 template <int NT16, int EPI>
@@ -204,8 +141,8 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     __shared__ uint32_t tmem_slot;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
-    uint8_t * sB = sA + kAStages * kGroup * kABytes;
-    uint8_t * sR = sB + kBStages * kGroup * kBBytes;
+    uint8_t * sB = sA + kAStages * kABytes;
+    uint8_t * sR = sB + kBStages * kBBytes;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
@@ -242,10 +179,32 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     if (warp < 8) {
         // producer: weight row r, Q8_0 block hb of every chunk
         const int r = tid & (kTileM - 1), hb = tid >> 7;
-        produce_groups<kRawStages, kAStages>(p.q4, nch, r, hb, sR, sA, raw_full, raw_empty, a_full, a_empty, ok, p.err);
+        for (int c = 0; c < nch; c++) {
+            const int rs = c % kRawStages, ab = c % kAStages;
+            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kRawStages) & 1u, p.err);
+            const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
+            mbar_arrive(&raw_empty[rs]);
+            if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
+            write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
+            fence_proxy_async();
+            mbar_arrive(&a_full[ab]);
+        }
     } else if (warp == 8) {
-        if (lane == 0)
-            mma_groups<kAStages, kBStages, kIdesc>(nch, tmem, sA, sB, kBBytes, a_full, a_empty, b_full, b_empty, &done_bar, ok, p.err);
+        if (lane == 0) {
+            for (int c = 0; c < nch; c++) {
+                const int ab = c % kAStages, bb = c % kBStages;
+                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (c / kBStages) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kAStages) & 1u, p.err);
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kBBytes);
+#pragma unroll
+                for (int kk = 0; kk < kChunkK / 16; kk++)
+                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&a_empty[ab]);
+                umma_commit(&b_empty[bb]);
+            }
+            umma_commit(&done_bar);  // arrives once every MMA above has completed
+        }
     } else if (warp == 9) {
         if (lane == 0) {
             // weights and scales are constant: stream them before the predecessor finishes
@@ -263,7 +222,12 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     } else {
         if (lane == 0) {
             pdl_wait();  // activations come from the previous kernel
-            load_x_groups<kBStages>(nch, c_beg, row0, &xmap, sB, kBBytes, b_full, b_empty, ok, p.err);
+            for (int c = 0; c < nch; c++) {
+                const int bb = c % kBStages;
+                if (c >= kBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kBStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&b_full[bb], kBBytes);
+                tma_2d(sB + bb * kBBytes, &xmap, (c_beg + c) * kChunkK, row0, &b_full[bb]);
+            }
         }
     }
     pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed
@@ -401,11 +365,11 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
 // as the decode kernel, and the 8 dequantising warps drain the 128 x 256 f32 accumulator (warp w
 // reads TMEM lanes 32 (w % 4) .. + 31, activation rows 128 (w / 4) .. + 127).
 constexpr int kPN = 256;
-constexpr int kPRawStages = 3;
-constexpr int kPAStages = 2;    // groups
-constexpr int kPBStages = 2;    // groups
+constexpr int kPRawStages = 4;
+constexpr int kPAStages = 2;
+constexpr int kPBStages = 4;
 constexpr int kPBBytes = kPN * kChunkK * 2;
-constexpr int kPrefillSmem = 1024 + kPAStages * kGroup * kABytes + kPBStages * kGroup * kPBBytes + kPRawStages * kRawBytes;
+constexpr int kPrefillSmem = 1024 + kPAStages * kABytes + kPBStages * kPBBytes + kPRawStages * kRawBytes;
 static_assert(kPrefillSmem <= 227 * 1024, "prefill GEMM shared memory");
 
 template <int EPI>
@@ -418,8 +382,8 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
     __shared__ uint32_t tmem_slot;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
-    uint8_t * sB = sA + kPAStages * kGroup * kABytes;
-    uint8_t * sR = sB + kPBStages * kGroup * kPBBytes;
+    uint8_t * sB = sA + kPAStages * kABytes;
+    uint8_t * sR = sB + kPBStages * kPBBytes;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, row0 = blockIdx.y * kPN;
@@ -451,10 +415,32 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
 
     if (warp < 8) {
         const int r = tid & (kTileM - 1), hb = tid >> 7;
-        produce_groups<kPRawStages, kPAStages>(p.q4, nch, r, hb, sR, sA, raw_full, raw_empty, a_full, a_empty, ok, p.err);
+        for (int c = 0; c < nch; c++) {
+            const int rs = c % kPRawStages, ab = c % kPAStages;
+            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kPRawStages) & 1u, p.err);
+            const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
+            mbar_arrive(&raw_empty[rs]);
+            if (c >= kPAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kPAStages) - 1) & 1u, p.err);
+            write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
+            fence_proxy_async();
+            mbar_arrive(&a_full[ab]);
+        }
     } else if (warp == 8) {
-        if (lane == 0)
-            mma_groups<kPAStages, kPBStages, kIdesc>(nch, tmem, sA, sB, kPBBytes, a_full, a_empty, b_full, b_empty, &done_bar, ok, p.err);
+        if (lane == 0) {
+            for (int c = 0; c < nch; c++) {
+                const int ab = c % kPAStages, bb = c % kPBStages;
+                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (c / kPBStages) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kPAStages) & 1u, p.err);
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kPBBytes);
+#pragma unroll
+                for (int kk = 0; kk < kChunkK / 16; kk++)
+                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&a_empty[ab]);
+                umma_commit(&b_empty[bb]);
+            }
+            umma_commit(&done_bar);
+        }
     } else if (warp == 9) {
         if (lane == 0) {
             const int cb = umat_chunk_bytes(p.q4);
@@ -469,7 +455,12 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
     } else {
         if (lane == 0) {
             pdl_wait();  // activations come from the previous kernel
-            load_x_groups<kPBStages>(nch, 0, row0, &xmap, sB, kPBBytes, b_full, b_empty, ok, p.err);
+            for (int c = 0; c < nch; c++) {
+                const int bb = c % kPBStages;
+                if (c >= kPBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kPBStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&b_full[bb], kPBBytes);
+                tma_2d(sB + bb * kPBBytes, &xmap, c * kChunkK, row0, &b_full[bb]);
+            }
         }
     }
     pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed

@@ -456,7 +456,7 @@ float * Vocoder::load_f32(const std::string & name, int64_t expect, bool exp_of)
     if (exp_of)
         for (float & v : h) v = expf(v);  // SnakeBeta parameters are stored as logarithms
     float * d = dalloc<float>(h.size());
-    VCHECK(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+    VCHECK(cudaMemcpyAsync(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice, stream_));
     return d;
 }
 
@@ -471,7 +471,7 @@ QMat Vocoder::load_q8(const std::string & name) {
     q.MT = (M + 15) / 16;
     uint8_t * raw = nullptr;
     VCHECK(cudaMalloc(&raw, t.nbytes));
-    VCHECK(cudaMemcpy(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice));
+    VCHECK(cudaMemcpyAsync(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice, stream_));
     if (t.type == GT_Q4_K) {
         // Q4_K linears run on the tcgen05 dequant-GEMM (its 4-bit tile layout)
         if (K % 256) throw std::runtime_error("vocoder: " + name + " is Q4_K with rows not a multiple of 256");
@@ -519,7 +519,7 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
             for (int i = 0; i < cin; i++)
                 for (int k = 0; k < K; k++) h[((size_t) o * K + k) * cin + i] = src[((size_t) o * cin + i) * K + k];
         float * d = dalloc<float>(h.size());
-        VCHECK(cudaMemcpy(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+        VCHECK(cudaMemcpyAsync(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice, stream_));
         c.w = d;
         return c;
     }
@@ -538,7 +538,7 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
                     if (k < K) h[(((size_t) p * cout + o) * c.taps + (c.taps - 1 - m)) * cin + i] = src[((size_t) i * cout + o) * K + k];
                 }
     float * d = dalloc<float>(h.size());
-    VCHECK(cudaMemcpy(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+    VCHECK(cudaMemcpyAsync(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice, stream_));
     c.w = d;
     return c;
 }
@@ -553,7 +553,7 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
     auto table = [&](const std::string & n, float * dst) {
         const GgufTensor & t = need(n);
         if (t.type != 0 || t.ne[0] != dq_) throw std::runtime_error("vocoder: " + n + " must be F32 [dq, rows]");
-        VCHECK(cudaMemcpy(dst, gg_.data(t), (size_t) cfg_.vs * dq_ * 4, cudaMemcpyHostToDevice));
+        VCHECK(cudaMemcpyAsync(dst, gg_.data(t), (size_t) cfg_.vs * dq_ * 4, cudaMemcpyHostToDevice, stream_));
     };
     emb_first_ = dalloc<float>((size_t) cfg_.vs * dq_);
     table("codec.dq.first.0.embed", emb_first_);
@@ -658,12 +658,15 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
         raise_conv_smem_limit(conv_smem_bytes(lxp));
     }
     err_ = dalloc<int>(1);
-    VCHECK(cudaMemset(err_, 0, sizeof(int)));
+    VCHECK(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
     scr_.ws_elems = (size_t) 1 << 20;
     scr_.ws = dalloc<float4>(scr_.ws_elems);
     scr_.n_counters = 4096;
     scr_.counters = dalloc<int>(scr_.n_counters);
-    VCHECK(cudaMemset(scr_.counters, 0, scr_.n_counters * sizeof(int)));
+    VCHECK(cudaMemsetAsync(scr_.counters, 0, scr_.n_counters * sizeof(int), stream_));
+    // every upload above is ordered on stream_ (a plain cudaMemcpy from pageable memory may still
+    // be in flight when it returns, and a non-blocking stream does not wait for it)
+    VCHECK(cudaStreamSynchronize(stream_));
 }
 
 Vocoder::~Vocoder() {
@@ -725,7 +728,7 @@ void Vocoder::ensure(int T) {
         void * pr = nullptr;
         VCHECK(cudaMalloc(&pr, tab.size() * sizeof(float2)));
         scratch_allocs_.push_back(pr);
-        VCHECK(cudaMemcpy(pr, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        VCHECK(cudaMemcpyAsync(pr, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream_));
         rope_ = (float2 *) pr;
         rope_max_ = tcap_;
     }
@@ -997,7 +1000,7 @@ float * CodecEncoder::upload(const std::vector<float> & h) {
     void * p = nullptr;
     ECHECK(cudaMalloc(&p, std::max<size_t>(h.size(), 1) * sizeof(float)));
     allocs_.push_back(p);
-    ECHECK(cudaMemcpy(p, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+    ECHECK(cudaMemcpyAsync(p, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice, stream_));
     return (float *) p;
 }
 
@@ -1017,7 +1020,7 @@ QMat CodecEncoder::load_lin(const std::string & name) {
     q.M = M; q.K = K; q.KB = K / 32; q.MT = (M + 15) / 16;
     uint8_t * raw = nullptr;
     ECHECK(cudaMalloc(&raw, t.nbytes));
-    ECHECK(cudaMemcpy(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice));
+    ECHECK(cudaMemcpyAsync(raw, gg_.data(t), t.nbytes, cudaMemcpyHostToDevice, stream_));
     auto dal = [&](size_t bytes) { void * p = nullptr; ECHECK(cudaMalloc(&p, bytes)); allocs_.push_back(p); return p; };
     if (t.type == GT_Q4_K) {
         if (K % 256) throw std::runtime_error("codec encoder: " + name + " is Q4_K with rows not a multiple of 256");
@@ -1134,11 +1137,11 @@ CodecEncoder::CodecEncoder(const GgufFile & gg, const ModelConfig & cfg, int dev
         ECHECK(cudaMalloc(&p, scr_.n_counters * sizeof(int)));
         allocs_.push_back(p);
         scr_.counters = (int *) p;
-        ECHECK(cudaMemset(scr_.counters, 0, scr_.n_counters * sizeof(int)));
+        ECHECK(cudaMemsetAsync(scr_.counters, 0, scr_.n_counters * sizeof(int), stream_));
         ECHECK(cudaMalloc(&p, sizeof(int)));
         allocs_.push_back(p);
         err_ = (int *) p;
-        ECHECK(cudaMemset(err_, 0, sizeof(int)));
+        ECHECK(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
     }
     // widest conv window: dynamic shared memory of the conv kernel
     int lxp = conv_lxp(c0_.taps, 1);
@@ -1146,6 +1149,7 @@ CodecEncoder::CodecEncoder(const GgufFile & gg, const ModelConfig & cfg, int dev
         lxp = std::max({ lxp, conv_lxp(res1_[st].taps, 1), conv_lxp(res3_[st].taps, 1), conv_lxp(strided_[st].taps, 1) });
     lxp = std::max({ lxp, conv_lxp(c14_.taps, 1), conv_lxp(down_.taps, 1) });
     raise_conv_smem_limit(conv_smem_bytes(lxp));
+    ECHECK(cudaStreamSynchronize(stream_));  // the uploads above are ordered on stream_
 }
 
 CodecEncoder::~CodecEncoder() {
@@ -1180,7 +1184,7 @@ void CodecEncoder::ensure(int L) {
         void * p = nullptr;
         ECHECK(cudaMalloc(&p, tab.size() * sizeof(float2)));
         scratch_.push_back(p);
-        ECHECK(cudaMemcpy(p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        ECHECK(cudaMemcpyAsync(p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream_));
         rope_ = (float2 *) p;
         rope_max_ = (int) T1;
     }

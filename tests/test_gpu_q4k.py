@@ -196,3 +196,25 @@ def test_q4k_vocoder_full_shapes(pkg, model_dir):
         assert snr_db(ref, pcm) > 40.0, snr_db(ref, pcm)
     finally:
         voc.close()
+
+
+def test_vocoder_load_independent_of_stale_device_memory(pkg, model_dir):
+    """Weights uploaded at load must be complete before the repacking kernels read them: two
+    vocoders built on device memory last filled with different values decode bit-identical PCM.
+    (A pageable cudaMemcpy may still be in flight when it returns, and the load's own stream does
+    not wait for it; the repack then read part of the previous contents.)"""
+    import torch
+    path = pkg.synth_model(str(model_dir / "depth_q4k.gguf"), preset="depth", quant="q4_k", seed=4)
+    codes = np.random.default_rng(8).integers(0, 2048, (3, bo.Model(path).cfg.nc)).astype(np.int32)
+    outs = []
+    for fill in (1e30, -3.0, float("nan")):
+        junk = torch.full((1 << 30,), fill, device="cuda")  # 4 GB, freed back to the driver below
+        del junk
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        voc = pkg.VocoderHandle(path, 0)
+        try:
+            outs.append(voc.stream_decode(codes))
+        finally:
+            voc.close()
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
