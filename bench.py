@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--prompt-cap", type=int, default=0, help="cap text prompt length (profiling runs)")
     ap.add_argument("--profile", action="store_true",
                     help="after warm-up, run one frame step between cudaProfilerStart/Stop and exit (for ncu)")
+    ap.add_argument("--profile-create", action="store_true",
+                    help="after warm-up, free every session and create them all again in one batched call between "
+                         "cudaProfilerStart/Stop, then exit (for ncu)")
     ap.add_argument("--model-preset", default="full", choices=["full", "depth"],
                     help="'depth': the full-size depth decoder behind a one-layer backbone (small profiling captures)")
     return ap.parse_args()
@@ -320,6 +323,22 @@ def main():
     for w in range(args.warmup):
         gen.step_frames(ids, 1, seeds + w)
     gen.sync()
+    if args.profile_create:
+        specs = session_specs(pkg, sessions, nc)
+        for sid in ids:
+            gen.session_free(sid)
+        gen.sessions_create_batch(specs)  # first batch: buffers sized, kernels loaded
+        for sid in ids:
+            gen.session_free(sid)
+        gen.sync()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        gen.sessions_create_batch(specs)
+        gen.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled": "sessions_create_batch", "sessions": args.sessions}))
+        gen.close()
+        return
     if args.profile:
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
