@@ -9,6 +9,9 @@ reference checkout is present; the fixtures are committed so that the tests need
   split_text.json  texts, budgets and the pieces the reference's long-text splitter returns
                    (src/text_split.cpp:89-111, compiled into oracle/_ref)
   wav_ref.wav      a WAV the reference's writer (src/audio.cpp:80-107) makes of wav_samples()
+  cluster_sched.json  the serving harness's scheduling rules evaluated by the reference's own
+                   python/bz_ggml/cluster.py: estimate_speech_profile, select_burst_steps and
+                   a TieredSlotPool acquire/release trace
 
 usage: python tests/golden/make_golden.py [reference checkout, default /root/reference]
 """
@@ -119,6 +122,54 @@ def main(ref):
 
     x = wav_samples()
     lib.ref_write_wav(os.path.join(HERE, "wav_ref.wav").encode(), x.ctypes.data_as(ctypes.c_void_p), x.size, 24000)
+
+    with open(os.path.join(HERE, "cluster_sched.json"), "w") as f:
+        json.dump(cluster_cases(ref), f, indent=0)
+
+
+def cluster_cases(ref):
+    """The reference harness's pure scheduling functions on seeded inputs."""
+    pkg_dir = os.path.join(ref, "python", "bz_ggml")
+    spec = importlib.util.spec_from_file_location("ref_bz_ggml", os.path.join(pkg_dir, "__init__.py"),
+                                                  submodule_search_locations=[pkg_dir])
+    pkg = importlib.util.module_from_spec(spec)
+    sys.modules["ref_bz_ggml"] = pkg
+    cspec = importlib.util.spec_from_file_location("ref_bz_ggml.cluster", os.path.join(pkg_dir, "cluster.py"))
+    cl = importlib.util.module_from_spec(cspec)
+    sys.modules["ref_bz_ggml.cluster"] = cl
+    cspec.loader.exec_module(cl)
+    rng = np.random.default_rng(21)
+    words = ["alpha", "beta", "gamma", "delta", "epsilon", "zeta", "eta", "theta"]
+    profiles = []
+    for i in range(60):
+        n = int(rng.integers(0, 120))
+        text = " ".join(rng.choice(words, n)) if n else ""
+        ins = [None, "", "Speak clearly and naturally.", "Whisper softly please"][i % 4]
+        ref_frames = int(rng.integers(0, 200)) if i % 3 else 0
+        cfg = [1.0, 1.5, 0.5, 2.0][i % 4]
+        profiles.append(dict(text=text, instruction=ins, ref_frames=ref_frames, cfg_scale=cfg,
+                             out=cl.estimate_speech_profile(text, ins, ref_frames, cfg_scale=cfg)))
+    bursts = []
+    for i in range(200):
+        n = int(rng.integers(0, 12))
+        sess = {j: {"expected_eos": int(rng.integers(0, 120)), "total_frames": int(rng.integers(0, 120))} for j in range(n)}
+        mb = [16, 8, 4, 32][i % 4]
+        bursts.append(dict(sessions=[[s["expected_eos"], s["total_frames"]] for s in sess.values()], max_burst=mb,
+                           out=cl.select_burst_steps(sess, max_burst=mb)))
+    pool = cl.TieredSlotPool(short_slots=3, standard_slots=2, long_slots=2)
+    held, trace = [], []
+    for i in range(120):
+        if held and rng.random() < 0.4:
+            slot = held.pop(int(rng.integers(0, len(held))))
+            pool.release(slot)
+            trace.append(["release", slot, pool.active_count()])
+        else:
+            need = int(rng.integers(50, 2600))
+            got = pool.acquire(need)
+            if got is not None:
+                held.append(got[0])
+            trace.append(["acquire", need, list(got) if got else None, pool.active_count()])
+    return dict(profiles=profiles, bursts=bursts, pool=dict(tiers=[3, 2, 2], trace=trace))
 
 
 if __name__ == "__main__":
