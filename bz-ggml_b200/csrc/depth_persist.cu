@@ -418,7 +418,31 @@ __device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int 
             *scode = i0;
         }
         epi_sync();
-        if (j + 1 < nc) {
+        if (j + 1 < nc && p.in_tab) {
+            int next = p.forced ? p.forced[(size_t) b * (nc - 1) + (j - 1)] : *scode;
+            if (next < 0 || next >= V) next = 0;
+            // the next sub-step's layer-0 input, as its in_proj + reduce phases would leave it:
+            // x (f32), x * norm weight (f16) and the sum of squares of each 64-column chunk
+            const int D = p.D;
+            const float * src = p.in_tab + ((size_t) (j - 1) * V + next) * D;
+            for (int c0 = tid * 8; c0 < D; c0 += kEpiThreads * 8) {
+                const float4 a = __ldcg(reinterpret_cast<const float4 *>(src + c0));
+                const float4 b2 = __ldcg(reinterpret_cast<const float4 *>(src + c0 + 4));
+                const float4 wa = *reinterpret_cast<const float4 *>(p.in_norm + c0);
+                const float4 wb = *reinterpret_cast<const float4 *>(p.in_norm + c0 + 4);
+                __stcg(reinterpret_cast<float4 *>(p.x + (size_t) b * D + c0), a);
+                __stcg(reinterpret_cast<float4 *>(p.x + (size_t) b * D + c0 + 4), b2);
+                half2 h[4] = { __floats2half2_rn(a.x * wa.x, a.y * wa.y), __floats2half2_rn(a.z * wa.z, a.w * wa.w),
+                               __floats2half2_rn(b2.x * wb.x, b2.y * wb.y), __floats2half2_rn(b2.z * wb.z, b2.w * wb.w) };
+                __stcg(reinterpret_cast<uint4 *>(p.h16 + (size_t) b * D + c0), *reinterpret_cast<uint4 *>(h));
+                // 8 consecutive threads cover one 64-column chunk
+                float sq = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b2.x * b2.x + b2.y * b2.y + b2.z * b2.z + b2.w * b2.w;
+                sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+                if ((lane & 7) == 0) __stcg(p.ss + (size_t) b * (D / kChunkK) + c0 / kChunkK, sq);
+            }
+        } else if (j + 1 < nc) {
             int next = p.forced ? p.forced[(size_t) b * (nc - 1) + (j - 1)] : *scode;
             if (next < 0 || next >= V) next = 0;
             const size_t row = (size_t) j * V + next;

@@ -62,6 +62,12 @@ struct DpParams {
     half * g16 = nullptr;               // SwiGLU output [2R][ffn]
     half * din16 = nullptr;             // in_proj input [2R][H]
     QRows embd;                         // audio embedding table
+    // in_proj of every code of codebooks 1..nc-2, [nc-2][vs][D] f32, or null: the arg-max phase
+    // then writes sub-step j+1's input (x, x * in_norm, chunk sums of squares) from row
+    // (j-1, code) instead of the embedding gather, and the plan has no in_proj phases after the
+    // first sub-step
+    const float * in_tab = nullptr;
+    const float * in_norm = nullptr;    // layer 0's attention norm weight
     const int * row_active = nullptr;   // [R]
     const int * row_set = nullptr;      // [R] depth weight set of each row, or null (all rows)
     int set_id = 0;                     // the set this launch's weights are; other rows are left alone

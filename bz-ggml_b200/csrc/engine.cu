@@ -593,6 +593,38 @@ bool Engine::dp_supported(int R) const {
     return true;
 }
 
+// The depth decoder's input from sub-step 2 on is one codebook embedding row, and in_proj is
+// linear: in_proj(E_j[code]) is precomputed once per weight set for every code of codebooks
+// 1..nc-2 (the same f16 embedding values and f16 weights as the in_proj phase, f32 results), so
+// the arg-max phase can write the next sub-step's input directly and the plan drops one GEMM and
+// one reduction phase per sub-step. [nc-2][vs][D] f32 (252 MB at nc 32).
+const float * Engine::in_tab_for_set() {
+    const DdConfig & dd = cfg.dd;
+    const int D = dd.hidden, H = cfg.hidden, vs = cfg.vs, ncb = cfg.nc - 2;
+    if (ncb <= 0 || D % 256 != 0 || audio_embd_.K != H) return nullptr;
+    if (dp_in_tab_[cur_set_]) return dp_in_tab_[cur_set_];
+    const long long total = (long long) ncb * vs;
+    float * tab = dalloc<float>((size_t) total * D);
+    const int chunk = 8192;
+    half * x16 = nullptr;
+    CK(cudaMalloc(&x16, (size_t) chunk * H * sizeof(half)));
+    try {
+        for (long long r0 = 0; r0 < total; r0 += chunk) {
+            const int n = (int) std::min<long long>(chunk, total - r0);
+            launch_qrows_to_f16(audio_embd_, (long long) vs + r0, n, x16, stream_);  // codebook 1 starts at row vs
+            launch_gemm(dd_in_, x16, H, n, GemvOut{ EPI_STORE, tab + (size_t) r0 * D, nullptr, D });
+        }
+        CK(cudaStreamSynchronize(stream_));
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        cudaFree(x16);
+        throw;
+    }
+    CK(cudaFree(x16));
+    dp_in_tab_[cur_set_] = tab;
+    return tab;
+}
+
 const Engine::DpPlan * Engine::depth_plan(int R) {
     if (!dp_supported(R)) return nullptr;
     // one schedule per batch size and depth weight set (the set's weight pointers are in it)
@@ -602,6 +634,7 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     const DdConfig & dd = cfg.dd;
     const int D = dd.hidden, H = cfg.hidden, nc = cfg.nc, vs = cfg.vs, G = dp_grid_;
     const int qkvd = dd.n_head * dd.hd + 2 * dd.n_kv * dd.hd;
+    const bool tab = in_tab_for_set() != nullptr;
     // activation rows go to the MMA in chunks of at most 64 (N), one unit per chunk
     const int NB1 = std::min(64, round_up(R, 16)), NB2 = std::min(64, round_up(2 * R, 16));
     std::vector<DpPhase> ph;
@@ -631,8 +664,11 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
     for (int j = 1; j < nc; j++) {
         const bool first = j == 1;
         const int rows = first ? 2 * R : R, sel = first ? 0 : 1;
-        int S = gemm(dd_in_.u, 0 + sel, 0, rows, DPE_PARTIAL, D);
-        reduce(S, rows, 0, dd_[0].attn_norm);
+        int S = 1;
+        if (first || !tab) {
+            S = gemm(dd_in_.u, 0 + sel, 0, rows, DPE_PARTIAL, D);
+            reduce(S, rows, 0, dd_[0].attn_norm);
+        }
         for (int l = 0; l < dd.n_layer; l++) {
             const LayerW & w = dd_[l];
             if (w.qkv.u.M != qkvd) throw std::runtime_error("persistent depth decoder: unexpected qkv rows");
@@ -713,6 +749,8 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     p.kv = dkv_; p.kv_layer = (size_t) rmax_ * cfg.nc * 2 * dd.n_kv * dd.hd;
     p.P = dp_P_; p.x = dx_; p.h16 = dh16_; p.ss = dp_ss_; p.att16 = datt16_; p.g16 = dff16_; p.din16 = din16_;
     p.embd = audio_embd_;
+    p.in_tab = dp_in_tab_[cur_set_];
+    p.in_norm = dd_[0].attn_norm;
     p.row_active = row_active_; p.frames = cur_frames_;
     p.row_set = row_set; p.set_id = cur_set_;
     p.forced = forced_dev; p.logits_out = logits_dev;
@@ -1702,11 +1740,14 @@ void Engine::profile_step(double * out) {
 
 size_t Engine::depth_bytes_per_step() const {
     // algorithmic bytes of the depth decode of one frame step: the Q8_0 depth weights, re-read by
-    // every sub-step (in_proj, the 4 layers and that sub-step's head)
+    // every sub-step (the 4 layers and that sub-step's head); in_proj is read by the first
+    // sub-step and, with the precomputed in_proj table, the later ones read one table row (D f32)
+    // per session instead
     auto qbytes = [](const QMat & q) { return qmat_bytes(q); };
-    size_t dd = qbytes(dd_in_) + qbytes(dd_head_[0]);
+    size_t dd = qbytes(dd_head_[0]);
     for (const LayerW & w : dd_) dd += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
-    return (size_t) (cfg.nc - 1) * dd;
+    const size_t later = dp_in_tab_[cur_set_] ? (size_t) cur_R_ * cfg.dd.hidden * sizeof(float) : qbytes(dd_in_);
+    return (size_t) (cfg.nc - 1) * dd + qbytes(dd_in_) + (size_t) (cfg.nc - 2) * later;
 }
 
 double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int epi) {

@@ -280,6 +280,9 @@ private:
     bool use_dp_ = true;
     int dp_grid_ = 0;
     std::map<int, DpPlan> dp_plans_;
+    // in_proj of every input code of sub-steps 2..nc-1 for each depth weight set (see DpParams::in_tab)
+    float * dp_in_tab_[2] = { nullptr, nullptr };
+    const float * in_tab_for_set();
     float * dp_P_ = nullptr;
     size_t dp_P_floats_ = 0;
     float * dp_ss_ = nullptr;

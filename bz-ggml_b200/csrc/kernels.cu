@@ -1526,6 +1526,30 @@ void launch_depth_sample_gather(const DepthSampleArgs & a, cudaStream_t s) {
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
+__global__ void qrows_to_f16_kernel(const QRows e, long long row0, int n, half * out) {
+    const long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x;  // one 8-value group
+    const int g = e.K / 8;
+    if (i >= (long long) n * g) return;
+    const long long row = row0 + i / g;
+    const int c = (int) (i % g);
+    const uint2 u = *reinterpret_cast<const uint2 *>(e.qs + row * e.K + c * 8);
+    const float sc = __half2float(e.ds[row * (e.K / 32) + (c >> 2)]);
+    const float m = e.ms ? __half2float(e.ms[row * (e.K / 32) + (c >> 2)]) : 0.0f;
+    const int8_t * bq = reinterpret_cast<const int8_t *>(&u);
+    half2 o[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) o[k] = __floats2half2_rn((float) bq[2 * k] * sc - m, (float) bq[2 * k + 1] * sc - m);
+    *reinterpret_cast<uint4 *>(out + (i / g) * e.K + c * 8) = *reinterpret_cast<uint4 *>(o);
+}
+
+void launch_qrows_to_f16(const QRows & e, long long row0, int n, half * out, cudaStream_t s) {
+    if (n <= 0) return;
+    if (e.K % 32 || row0 < 0 || row0 + n > e.rows) throw std::runtime_error("qrows_to_f16: rows out of the table");
+    const long long groups = (long long) n * (e.K / 8);
+    qrows_to_f16_kernel<<<(unsigned) ((groups + 255) / 256), 256, 0, s>>>(e, row0, n, out);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
 void launch_copy_rows(const float * src, int lds, const int * src_idx, float * dst, int ldd, const int * dst_idx, int n,
                       int cols, cudaStream_t s) {
     if (n <= 0) return;

@@ -125,6 +125,9 @@ void split_q4k_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half 
 void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps, half * out16, int ld16,
                     float * out32, int ld32, int r0, int n, const int * row_map, cudaStream_t s);
 // dst[dst_idx ? dst_idx[i] : i][:cols] = src[src_idx ? src_idx[i] : i][:cols] for i < n (f32 rows)
+// rows [row0, row0 + n) of a quantised table as f16 rows [n][K]: f16(q * d - m), the embedding
+// value the depth decoder's input gather writes
+void launch_qrows_to_f16(const QRows & e, long long row0, int n, half * out, cudaStream_t s);
 void launch_copy_rows(const float * src, int lds, const int * src_idx, float * dst, int ldd, const int * dst_idx, int n,
                       int cols, cudaStream_t s);
 // x[r] += rmsnorm(t[r]) * w  (Gemma post-norms)
