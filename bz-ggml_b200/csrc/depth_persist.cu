@@ -250,7 +250,8 @@ __device__ void phase_reduce(const DpParams & p, const DpPhase ph, int cta, int 
 __device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane, float * sQ) {
     const int R = p.R, hd = 128, nkv = p.n_kv, nh = p.n_head, D = p.D;
     const int M = nh * hd + 2 * nkv * hd;
-    const int rows = ph.rows, S = ph.S, n_new = ph.n_new;
+    const int rows = ph.rows, S = ph.alt ? 1 : ph.S, n_new = ph.n_new;
+    const float * part = ph.alt ? p.P2 : p.P;
     const int Gq = nh / nkv;  // query heads per kv head (1..4): warps >= Gq only append k/v
     const bool qwarp = warp < Gq;
     float * kvl = p.kv + (size_t) ph.layer * p.kv_layer;
@@ -272,7 +273,7 @@ __device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G,
             const int row = b + i * R, pos = ph.start + i;
             const int col0 = nh * hd + isv * nkv * hd + g * hd;
             float x[4];
-            sum_partials(p.P, S, (size_t) rows * M, (size_t) row * M + col0 + lane, x);
+            sum_partials(part, S, (size_t) rows * M, (size_t) row * M + col0 + lane, x);
 #pragma unroll
             for (int e = 0; e < 4; e++) x[e] *= scale[i];
             if (!isv) rope128(x, p.rope + (size_t) pos * (hd / 2), lane);
@@ -284,7 +285,7 @@ __device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G,
         for (int i = 0; i < n_new && qwarp; i++) {
             const int row = b + i * R, pos = ph.start + i;
             float x[4];
-            sum_partials(p.P, S, (size_t) rows * M, (size_t) row * M + qh * hd + lane, x);
+            sum_partials(part, S, (size_t) rows * M, (size_t) row * M + qh * hd + lane, x);
 #pragma unroll
             for (int e = 0; e < 4; e++) x[e] *= scale[i];
             rope128(x, p.rope + (size_t) pos * (hd / 2), lane);
@@ -441,6 +442,12 @@ __device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int 
                 sq += __shfl_xor_sync(0xffffffffu, sq, 2);
                 sq += __shfl_xor_sync(0xffffffffu, sq, 4);
                 if ((lane & 7) == 0) __stcg(p.ss + (size_t) b * (D / kChunkK) + c0 / kChunkK, sq);
+            }
+            if (p.qkv_tab) {
+                const int M = p.n_head * p.hd + 2 * p.n_kv * p.hd;
+                const float * qs = p.qkv_tab + ((size_t) (j - 1) * V + next) * M;
+                for (int c0 = tid * 4; c0 < M; c0 += kEpiThreads * 4)
+                    __stcg(reinterpret_cast<float4 *>(p.P2 + (size_t) b * M + c0), __ldcg(reinterpret_cast<const float4 *>(qs + c0)));
             }
         } else if (j + 1 < nc) {
             int next = p.forced ? p.forced[(size_t) b * (nc - 1) + (j - 1)] : *scode;

@@ -36,6 +36,7 @@ struct alignas(16) DpPhase {
     const float * norm_w = nullptr;  // REDUCE: weight of the norm that the next GEMM applies
     int layer = 0, start = 0, n_new = 1;  // ATTN
     int j = 0;          // ARGMAX: codebook
+    int alt = 0;        // ATTN: the q/k/v come from P2 (written by the arg-max phase), not from partials
 };
 
 // activation buffers as 3-D tensors {64 columns, rows, K / 64 chunks}: one TMA box brings up to
@@ -55,6 +56,7 @@ struct DpParams {
     float * kv = nullptr;               // depth cache, layer stride kv_layer
     size_t kv_layer = 0;
     float * P = nullptr;                // split-K partials [S][rows][M]
+    float * P2 = nullptr;               // layer 0's q/k/v rows from qkv_tab [R][q + 2 kv]
     float * x = nullptr;                // residual stream [2R][D] f32
     half * h16 = nullptr;               // x * norm weight [2R][D] (the next GEMM's input)
     float * ss = nullptr;               // per-row sums of squares in 64-column chunks [2R][D/64]
@@ -68,6 +70,10 @@ struct DpParams {
     // first sub-step
     const float * in_tab = nullptr;
     const float * in_norm = nullptr;    // layer 0's attention norm weight
+    // layer 0's q/k/v projection of the same inputs, [nc-2][vs][q + 2 kv] f32, or null: with it
+    // the arg-max phase also writes P2 and the plan has no layer-0 qkv phase after the first
+    // sub-step (the RMS scale is applied by the attention phase, as for partials)
+    const float * qkv_tab = nullptr;
     const int * row_active = nullptr;   // [R]
     const int * row_set = nullptr;      // [R] depth weight set of each row, or null (all rows)
     int set_id = 0;                     // the set this launch's weights are; other rows are left alone

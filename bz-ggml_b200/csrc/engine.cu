@@ -471,6 +471,7 @@ void Engine::alloc_buffers() {
     dp_grid_ = depth_persist_grid();
     dp_P_floats_ = std::max((size_t) 16 * 128 * std::max(dd.hidden, ddq + 2 * ddkv), (size_t) 16 * 64 * cfg.vs);
     dp_P_ = dalloc<float>(dp_P_floats_);
+    dp_P2_ = dalloc<float>((size_t) rmax_ * (ddq + 2 * ddkv));
     dp_ss_ = dalloc<float>((size_t) 256 * std::max(1, dd.hidden / 64));
     CK(cudaMemsetAsync(dp_ss_, 0, (size_t) 256 * std::max(1, dd.hidden / 64) * sizeof(float), stream_));
     dp_bar_ = dalloc<unsigned>(1);
@@ -604,15 +605,20 @@ const float * Engine::in_tab_for_set() {
     if (ncb <= 0 || D % 256 != 0 || audio_embd_.K != H) return nullptr;
     if (dp_in_tab_[cur_set_]) return dp_in_tab_[cur_set_];
     const long long total = (long long) ncb * vs;
+    const int qkvd = dd_[0].qkv.M;
     float * tab = dalloc<float>((size_t) total * D);
+    float * qtab = dalloc<float>((size_t) total * qkvd);
     const int chunk = 8192;
     half * x16 = nullptr;
-    CK(cudaMalloc(&x16, (size_t) chunk * H * sizeof(half)));
+    CK(cudaMalloc(&x16, (size_t) chunk * std::max(H, D) * sizeof(half)));
     try {
         for (long long r0 = 0; r0 < total; r0 += chunk) {
             const int n = (int) std::min<long long>(chunk, total - r0);
             launch_qrows_to_f16(audio_embd_, (long long) vs + r0, n, x16, stream_);  // codebook 1 starts at row vs
             launch_gemm(dd_in_, x16, H, n, GemvOut{ EPI_STORE, tab + (size_t) r0 * D, nullptr, D });
+            // layer 0's q/k/v of the same rows, from the f16 norm product its GEMM phase reads
+            launch_scale_rows_f16(tab + (size_t) r0 * D, dd_[0].attn_norm, n, D, x16, stream_);
+            launch_gemm(dd_[0].qkv, x16, D, n, GemvOut{ EPI_STORE, qtab + (size_t) r0 * qkvd, nullptr, qkvd });
         }
         CK(cudaStreamSynchronize(stream_));
     } catch (...) {
@@ -622,6 +628,7 @@ const float * Engine::in_tab_for_set() {
     }
     CK(cudaFree(x16));
     dp_in_tab_[cur_set_] = tab;
+    dp_qkv_tab_[cur_set_] = qtab;
     return tab;
 }
 
@@ -672,9 +679,12 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
         for (int l = 0; l < dd.n_layer; l++) {
             const LayerW & w = dd_[l];
             if (w.qkv.u.M != qkvd) throw std::runtime_error("persistent depth decoder: unexpected qkv rows");
-            S = gemm(w.qkv.u, 2 + sel, 0, rows, DPE_PARTIAL, qkvd);
+            // from the second sub-step on, layer 0's q/k/v come from the table (arg-max phase)
+            const bool from_tab = l == 0 && !first && tab;
+            if (!from_tab) S = gemm(w.qkv.u, 2 + sel, 0, rows, DPE_PARTIAL, qkvd);
             DpPhase a;
-            a.type = DP_ATTN; a.S = S; a.rows = rows; a.layer = l; a.start = first ? 0 : j; a.n_new = first ? 2 : 1;
+            a.type = DP_ATTN; a.S = from_tab ? 1 : S; a.alt = from_tab ? 1 : 0;
+            a.rows = rows; a.layer = l; a.start = first ? 0 : j; a.n_new = first ? 2 : 1;
             ph.push_back(a);
             S = gemm(w.o.u, 4 + sel, 0, rows, DPE_PARTIAL, D);
             reduce(S, rows, 1, w.ffn_norm);
@@ -750,6 +760,8 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     p.P = dp_P_; p.x = dx_; p.h16 = dh16_; p.ss = dp_ss_; p.att16 = datt16_; p.g16 = dff16_; p.din16 = din16_;
     p.embd = audio_embd_;
     p.in_tab = dp_in_tab_[cur_set_];
+    p.qkv_tab = dp_qkv_tab_[cur_set_];
+    p.P2 = dp_P2_;
     p.in_norm = dd_[0].attn_norm;
     p.row_active = row_active_; p.frames = cur_frames_;
     p.row_set = row_set; p.set_id = cur_set_;
@@ -1746,8 +1758,12 @@ size_t Engine::depth_bytes_per_step() const {
     auto qbytes = [](const QMat & q) { return qmat_bytes(q); };
     size_t dd = qbytes(dd_head_[0]);
     for (const LayerW & w : dd_) dd += qbytes(w.qkv) + qbytes(w.o) + qbytes(w.gu) + qbytes(w.down);
-    const size_t later = dp_in_tab_[cur_set_] ? (size_t) cur_R_ * cfg.dd.hidden * sizeof(float) : qbytes(dd_in_);
-    return (size_t) (cfg.nc - 1) * dd + qbytes(dd_in_) + (size_t) (cfg.nc - 2) * later;
+    // the later sub-steps read table rows (in_proj output and layer-0 q/k/v) instead of in_proj
+    // and layer 0's qkv weights
+    const size_t tab_row = (size_t) (cfg.dd.hidden + dd_[0].qkv.M) * sizeof(float);
+    const size_t later = dp_in_tab_[cur_set_] ? (size_t) cur_R_ * tab_row : qbytes(dd_in_) + qbytes(dd_[0].qkv);
+    return (size_t) (cfg.nc - 1) * dd - (size_t) (cfg.nc - 2) * qbytes(dd_[0].qkv) + qbytes(dd_in_) +
+           (size_t) (cfg.nc - 2) * later;
 }
 
 double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int epi) {

@@ -282,6 +282,8 @@ private:
     std::map<int, DpPlan> dp_plans_;
     // in_proj of every input code of sub-steps 2..nc-1 for each depth weight set (see DpParams::in_tab)
     float * dp_in_tab_[2] = { nullptr, nullptr };
+    float * dp_qkv_tab_[2] = { nullptr, nullptr };  // layer-0 q/k/v of the same inputs (DpParams::qkv_tab)
+    float * dp_P2_ = nullptr;
     const float * in_tab_for_set();
     float * dp_P_ = nullptr;
     size_t dp_P_floats_ = 0;

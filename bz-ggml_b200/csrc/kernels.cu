@@ -1542,6 +1542,19 @@ __global__ void qrows_to_f16_kernel(const QRows e, long long row0, int n, half *
     *reinterpret_cast<uint4 *>(out + (i / g) * e.K + c * 8) = *reinterpret_cast<uint4 *>(o);
 }
 
+__global__ void scale_rows_f16_kernel(const float * x, const float * w, long long total, int D, half * out) {
+    const long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    out[i] = __float2half_rn(x[i] * w[i % D]);
+}
+
+void launch_scale_rows_f16(const float * x, const float * w, int n, int D, half * out, cudaStream_t s) {
+    const long long total = (long long) n * D;
+    if (total <= 0) return;
+    scale_rows_f16_kernel<<<(unsigned) ((total + 255) / 256), 256, 0, s>>>(x, w, total, D, out);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
 void launch_qrows_to_f16(const QRows & e, long long row0, int n, half * out, cudaStream_t s) {
     if (n <= 0) return;
     if (e.K % 32 || row0 < 0 || row0 + n > e.rows) throw std::runtime_error("qrows_to_f16: rows out of the table");

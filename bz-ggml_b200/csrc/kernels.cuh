@@ -128,6 +128,8 @@ void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps,
 // rows [row0, row0 + n) of a quantised table as f16 rows [n][K]: f16(q * d - m), the embedding
 // value the depth decoder's input gather writes
 void launch_qrows_to_f16(const QRows & e, long long row0, int n, half * out, cudaStream_t s);
+// out[r][c] = f16(x[r][c] * w[c]) for n rows of D columns (the norm product a GEMM phase reads)
+void launch_scale_rows_f16(const float * x, const float * w, int n, int D, half * out, cudaStream_t s);
 void launch_copy_rows(const float * src, int lds, const int * src_idx, float * dst, int ldd, const int * dst_idx, int n,
                       int cols, cudaStream_t s);
 // x[r] += rmsnorm(t[r]) * w  (Gemma post-norms)
