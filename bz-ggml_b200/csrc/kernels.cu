@@ -454,20 +454,49 @@ __global__ void audio_embed_kernel(QRows e, const int * frames, int ldf, int nc,
                                    const int * row_active) {
     pdl_trigger();
     pdl_wait();
+    // one CTA per frame; a thread owns 8 consecutive columns (one 8-byte load of int8 quants per
+    // codebook) and sums the codebooks in order, eight rows of loads in flight at a time
+    __shared__ int codes[128];
     const int r = blockIdx.x;
     const bool act = row_active ? row_active[r] != 0 : true;
-    for (int k = threadIdx.x; k < e.K; k += blockDim.x) {
-        float acc = 0.0f;
+    for (int cb = threadIdx.x; cb < nc && cb < 128; cb += blockDim.x) {
+        const int c = frames[(size_t) r * ldf + cb];
+        codes[cb] = (c < 0 || c >= vs) ? 0 : c;
+    }
+    __syncthreads();
+    const int kb = e.K / 32;
+    for (int c8 = threadIdx.x; c8 < e.K / 8; c8 += blockDim.x) {
+        float acc[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) acc[q] = 0.0f;
         if (act) {
-            for (int cb = 0; cb < nc; cb++) {
-                int code = frames[(size_t) r * ldf + cb];
-                code = (code < 0 || code >= vs) ? 0 : code;
-                const size_t row = (size_t) cb * vs + code;
-                acc += (float) e.qs[row * e.K + k] * __half2float(e.ds[row * (e.K / 32) + (k >> 5)]) -
-                       (e.ms ? __half2float(e.ms[row * (e.K / 32) + (k >> 5)]) : 0.0f);
+            for (int cb0 = 0; cb0 < nc; cb0 += 8) {
+                uint2 u[8];
+                float d[8], m[8];
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    const int cb = cb0 + t;
+                    u[t] = make_uint2(0u, 0u);
+                    d[t] = m[t] = 0.0f;
+                    if (cb < nc) {
+                        const size_t row = (size_t) cb * vs + (cb < 128 ? codes[cb] : 0);
+                        u[t] = *reinterpret_cast<const uint2 *>(e.qs + row * e.K + c8 * 8);
+                        d[t] = __half2float(e.ds[row * kb + (c8 >> 2)]);
+                        m[t] = e.ms ? __half2float(e.ms[row * kb + (c8 >> 2)]) : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    if (cb0 + t >= nc) break;
+                    const int8_t * q8 = reinterpret_cast<const int8_t *>(&u[t]);
+#pragma unroll
+                    for (int q = 0; q < 8; q++) acc[q] += (float) q8[q] * d[t] - m[t];
+                }
             }
         }
-        out[(size_t) r * e.K + k] = acc;
+        float4 * o = reinterpret_cast<float4 *>(out + (size_t) r * e.K + c8 * 8);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 
@@ -1451,6 +1480,7 @@ void launch_embed_rows(const QRows & e, const int * idx, int n, float scale, flo
 void launch_audio_embed(const QRows & e, const int * frames, int ld_frames, int nc, int vs, int n, float * out32,
                         const int * row_active, cudaStream_t s) {
     if (n <= 0) return;
+    if (nc > 128 || e.K % 32) throw std::runtime_error("audio embedding: at most 128 codebooks, rows a multiple of 32");
     launch_k(audio_embed_kernel, n, 256, 0, s, e, frames, ld_frames, nc, vs, out32, row_active);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
