@@ -460,6 +460,9 @@ void Engine::alloc_buffers() {
     bff16_ = dalloc<half>((size_t) rmax_ * bb.ffn);
     bqkv_ = dalloc<float>((size_t) rmax_ * (bbq + 2 * bbkv));
     batt16_ = dalloc<half>((size_t) rmax_ * bbq);
+    battn_part_ = dalloc<float>((size_t) rmax_ * bb.n_kv * kAttnMaxSplits * 8 * (bb.hd + 2));
+    battn_ctr_ = dalloc<int>((size_t) rmax_ * bb.n_kv);
+    CK(cudaMemsetAsync(battn_ctr_, 0, (size_t) rmax_ * bb.n_kv * sizeof(int), stream_));
     blog_ = dalloc<float>((size_t) rmax_ * vbb_);
     scr_.ws_elems = (size_t) 16 << 20;
     scr_.ws = dalloc<float4>(scr_.ws_elems);
@@ -573,6 +576,11 @@ void Engine::bb_decode_layer(int l, int R) {
     a.scale = 1.0f / std::sqrt((float) bb.hd);
     a.kv.pool = kv_pool_; a.kv.page_table = page_table_; a.kv.max_pages = max_pages_; a.kv.n_layer = bb.n_layer; a.kv.layer = l;
     a.out = batt16_; a.ldo = q;
+    // split the cached positions over up to 8 CTAs per (session, kv head) while the grid is
+    // small (about 2048 CTAs for the whole batch); BZB_ATTN_SPLITS overrides
+    int splits = std::max(1, std::min(kAttnMaxSplits, 2048 / std::max(1, R * bb.n_kv)));
+    if (const char * e = std::getenv("BZB_ATTN_SPLITS")) splits = std::max(1, std::min(kAttnMaxSplits, std::atoi(e)));
+    a.splits = splits; a.part = battn_part_; a.counters = battn_ctr_;
     launch_attn_decode(a, true, stream_);
     gemv(w.o, batt16_, q, R, GemvOut{ EPI_RESID, bx_, nullptr, H });
     launch_rmsnorm(bx_, H, w.ffn_norm, H, bb.eps, bh16_, H, nullptr, 0, 0, R, nullptr, stream_);

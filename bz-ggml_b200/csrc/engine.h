@@ -284,6 +284,9 @@ private:
     float * dp_in_tab_[2] = { nullptr, nullptr };
     float * dp_qkv_tab_[2] = { nullptr, nullptr };  // layer-0 q/k/v of the same inputs (DpParams::qkv_tab)
     float * dp_P2_ = nullptr;
+    float * battn_part_ = nullptr;  // split-KV partials of the backbone decode attention
+    int * battn_ctr_ = nullptr;     // their per-(row, kv head) arrival counters
+    static constexpr int kAttnMaxSplits = 8;
     const float * in_tab_for_set();
     float * dp_P_ = nullptr;
     size_t dp_P_floats_ = 0;

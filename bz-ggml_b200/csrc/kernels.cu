@@ -617,7 +617,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeArgs a
     pdl_wait();
     constexpr int E = HD / 32;
     __shared__ DecodeSmem<HD> sm;
-    const int b = blockIdx.x, h = blockIdx.y;
+    const int b = blockIdx.x, h = blockIdx.y, z = blockIdx.z, S = a.splits;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.n_head / a.n_kv;
     const bool qwarp = warp < G;
@@ -626,7 +626,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeArgs a
     const int n_new = a.n_new;
     const int qh = h * G + warp;
     if (!act) {
-        if (qwarp)
+        if (qwarp && z == 0)
             for (int i = 0; i < n_new; i++)
                 for (int e = 0; e < E; e++)
                     a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(0.0f);
@@ -635,11 +635,16 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeArgs a
     const int start = a.st ? a.st[slot].pos : a.start;
     const int L = start + n_new;
     const int * page_row = PAGED ? a.kv.page_table + (size_t) slot * a.kv.max_pages : nullptr;
+    // this CTA's positions [p0, p1): equal 32-aligned shares of the cache
+    const int share = ((L + S - 1) / S + 31) & ~31;
+    const int p0 = min(L, z * share), p1 = min(L, p0 + share);
 
-    // 1. normalise, rotate and append the new tokens' keys and values
+    // 1. normalise, rotate and append the new tokens' keys and values (each split appends the
+    //    new positions in its own range, the only ones it reads)
     for (int task = warp; task < 2 * n_new; task += 4) {
         const int i = task >> 1;
         const int isv = task & 1;
+        if (start + i < p0 || start + i >= p1) continue;
         const int row = b + i * a.R;
         const float * src = a.qkv + (size_t) row * a.ldq + a.n_head * HD + isv * a.n_kv * HD + h * HD;
         float x[E];
@@ -683,17 +688,17 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeArgs a
         for (int e = 0; e < E; e++) acc[i][e] = 0.0f;
 
     KvTileRegs<HD, PAGED> regs;
-    regs.load(a.kv, page_row, b, h, a.n_kv, 0, L);
-    for (int t0 = 0; t0 < L; t0 += 32) {
+    if (p0 < p1) regs.load(a.kv, page_row, b, h, a.n_kv, p0, p1);
+    for (int t0 = p0; t0 < p1; t0 += 32) {
         __syncthreads();
         regs.store(sm.k, sm.v);
         __syncthreads();
-        if (t0 + 32 < L) regs.load(a.kv, page_row, b, h, a.n_kv, t0 + 32, L);
+        if (t0 + 32 < p1) regs.load(a.kv, page_row, b, h, a.n_kv, t0 + 32, p1);
         if (!qwarp) continue;
 #pragma unroll
         for (int i = 0; i < 2; i++) {
             if (i >= n_new) break;
-            const int lim = start + i + 1;
+            const int lim = min(start + i + 1, p1);
             const int p = t0 + lane;
             float sc = -INFINITY;
             if (p < lim) {
@@ -719,14 +724,63 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeArgs a
             m[i] = mn;
         }
     }
-    if (!qwarp) return;
+    if (S == 1) {
+        if (!qwarp) return;
 #pragma unroll
-    for (int i = 0; i < 2; i++) {
-        if (i >= n_new) break;
-        const float inv = 1.0f / l[i];
+        for (int i = 0; i < 2; i++) {
+            if (i >= n_new) break;
+            const float inv = 1.0f / l[i];
+#pragma unroll
+            for (int e = 0; e < E; e++)
+                a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
+        }
+        return;
+    }
+    // split-KV: publish this range's state, then the last CTA of (b, h) combines every range
+    constexpr int PL = HD + 2;
+    float * base = a.part + ((size_t) (b * a.n_kv + h) * S) * (4 * 2 * PL);
+    if (qwarp) {
+        for (int i = 0; i < n_new; i++) {
+            float * pp = base + ((size_t) z * 8 + warp * 2 + i) * PL;
+#pragma unroll
+            for (int e = 0; e < E; e++) pp[lane + 32 * e] = acc[i][e];
+            if (lane == 0) {
+                pp[HD] = m[i];
+                pp[HD + 1] = l[i];
+            }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+        int * ctr = a.counters + (size_t) b * a.n_kv + h;
+        const int prev = atomicAdd(ctr, 1);
+        s_last = prev == S - 1;
+        if (s_last) *ctr = 0;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last || !qwarp) return;
+    __threadfence();
+    for (int i = 0; i < n_new; i++) {
+        float mx = -INFINITY;
+        for (int zz = 0; zz < S; zz++) mx = fmaxf(mx, __ldcg(base + ((size_t) zz * 8 + warp * 2 + i) * PL + HD));
+        float lsum = 0.0f, o[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) o[e] = 0.0f;
+        for (int zz = 0; zz < S; zz++) {
+            const float * pp = base + ((size_t) zz * 8 + warp * 2 + i) * PL;
+            const float mz = __ldcg(pp + HD), lz = __ldcg(pp + HD + 1);
+            if (lz == 0.0f || mz == -INFINITY) continue;  // an empty range
+            const float w = expf(mz - mx);
+            lsum += lz * w;
+#pragma unroll
+            for (int e = 0; e < E; e++) o[e] += w * __ldcg(pp + lane + 32 * e);
+        }
+        const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
 #pragma unroll
         for (int e = 0; e < E; e++)
-            a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(acc[i][e] * inv);
+            a.out[(size_t) (b + i * a.R) * a.ldo + qh * HD + lane + 32 * e] = __float2half_rn(o[e] * inv);
     }
 }
 
@@ -1489,7 +1543,9 @@ void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s) {
     const int G = a.n_head / a.n_kv;
     if (G < 1 || G > 4 || a.n_head % a.n_kv) throw std::runtime_error("decode attention: query heads per kv head must be 1..4");
     if (a.n_new < 1 || a.n_new > 2) throw std::runtime_error("attention: 1 or 2 new tokens per session");
-    dim3 grid(a.R, a.n_kv);
+    if (a.splits < 1 || a.splits > 16 || (a.splits > 1 && (!a.part || !a.counters)))
+        throw std::runtime_error("decode attention: split-KV needs 1..16 splits, scratch and counters");
+    dim3 grid(a.R, a.n_kv, a.splits);
     const int threads = 128;
     if (a.hd == 64) {
         if (paged) launch_k(attn_decode_kernel<64, true>, grid, threads, 0, s, a);

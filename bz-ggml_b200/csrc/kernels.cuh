@@ -169,6 +169,12 @@ struct AttnDecodeArgs {
     AttnKV kv;
     half * out = nullptr;
     int ldo = 0;
+    // split-KV: each (session, kv head) runs `splits` CTAs over equal 32-aligned position ranges,
+    // each writing its (max, sum, weighted values) per query head to `part`; the last CTA to
+    // arrive (per-(session, kv head) counter, left at zero) combines them. 1: no split.
+    int splits = 1;
+    float * part = nullptr;   // [R][n_kv][splits][4 heads][2 tokens][hd + 2]
+    int * counters = nullptr; // [R][n_kv], zero between launches
 };
 void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s);
 
