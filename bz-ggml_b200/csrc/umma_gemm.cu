@@ -2,18 +2,19 @@
 //
 // y[rows, M] = x[rows, K] . W^T with W stored as Q8_0. Each CTA owns one 128-row weight tile
 // (the MMA's M), up to 64 activation rows (the MMA's N) and a K range, processed in 64-wide
-// chunks by a warp-specialised pipeline:
-//   * a loader warp streams each chunk's int8 weights and block scales (8.5 KB, contiguous in
-//     the repacked layout) with 1-D bulk async copies into a 4-deep raw ring;
+// chunks, two chunks per pipeline stage, by a warp-specialised pipeline:
+//   * a loader warp streams each stage's int8 weights and block scales (2 x 8.5 KB, contiguous
+//     in the repacked layout) with one 1-D bulk async copy into a 4-stage raw ring;
 //   * a second loader warp brings the activation rows with 2-D TMA tensor loads that write the
 //     128-byte-swizzled K-major layout the MMA reads;
 //   * 8 producer warps dequantise the raw ring (one Q8_0 block of one weight row per thread)
 //     into the swizzled f16 A stage;
 //   * one MMA warp issues four tcgen05.mma.cta_group::1.kind::f16 (128 x N x 16) per chunk into
-//     a TMEM accumulator and commits them to the stage's "empty" barrier.
+//     a TMEM accumulator and commits each stage's MMAs to its "empty" barriers.
 // Every hand-over is an mbarrier; no thread holds global loads in flight across a fence.
-// Split-K partials of one tile are reduced on chip: the splits form a thread-block cluster and
-// each CTA sums its slice of rows from every peer's shared memory in rank order.
+// Split-K partials of one tile are reduced on chip: the splits form a thread-block cluster, each
+// CTA pushes the rows another split owns into that split's receive buffer (distributed shared
+// memory stores) and sums the slices of its own rows in rank order.
 #include "kernels.cuh"
 #include "q4k.cuh"
 #include "tc_ptx.cuh"
@@ -65,11 +66,14 @@ __device__ __forceinline__ void store_out(const UParams & p, int n, int m, float
 }
 
 // roles: warps 0-7 dequantise, warp 8 issues MMAs, warp 9 loads weights, warp 10 loads activations.
-// Rings are sized so that no load waits on a recent MMA: activations run up to kBStages chunks
-// ahead and weights kRawStages chunks ahead; the dequantised A tile only needs double buffering.
-constexpr int kRawStages = 8;
+// Every ring moves stages of kSC chunks: each mbarrier wait costs the waiting thread ~220 cycles
+// even on a completed phase (measured), so a hand-over per two chunks halves that cost per chunk.
+// Rings are sized so that no load waits on a recent MMA: activations run up to kBStages stages
+// ahead and weights kRawStages stages ahead; the dequantised A tile only needs double buffering.
+constexpr int kSC = 2;
+constexpr int kRawStages = 8 / kSC;
 constexpr int kAStages = 2;
-constexpr int kBStages = 6;
+constexpr int kBStages = 6 / kSC;
 constexpr int kRawBytes = kTileM * kChunkK + 2 * kTileM * 2;   // 8 KB int8 + 512 B scales
 constexpr int kAllThreads = kThreads + 96;
 
@@ -125,8 +129,14 @@ __device__ __forceinline__ void write_piece(const RawPiece & pc, int q4, int r, 
 
 template <int NT16>
 constexpr int umma_smem_bytes() {
-    return 1024 + kAStages * kABytes + kBStages * (16 * NT16 * kChunkK * 2) + kRawStages * kRawBytes;
+    return 1024 + kSC * (kAStages * kABytes + kBStages * (16 * NT16 * kChunkK * 2) + kRawStages * kRawBytes) +
+           kTileM * (16 * NT16 + 4) * 4;  // split-K receive buffer
 }
+
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+static_assert(umma_smem_bytes<4>() <= 227 * 1024, "decode GEMM shared memory");
 
 template <int NT16, int EPI>
 __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams p, const __grid_constant__ CUtensorMap xmap) {
@@ -141,13 +151,15 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     __shared__ uint32_t tmem_slot;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
-    uint8_t * sB = sA + kAStages * kABytes;
-    uint8_t * sR = sB + kBStages * kBBytes;
+    uint8_t * sB = sA + kSC * kAStages * kABytes;
+    uint8_t * sR = sB + kSC * kBStages * kBBytes;
+    float * recv = reinterpret_cast<float *>(sR + kSC * kRawStages * kRawBytes);  // [splits][128 / splits][N + 4]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
     const int c_beg = split * p.kc_per_split;
     const int nch = max(0, min(p.KC, c_beg + p.kc_per_split) - c_beg);
+    const int nst = (nch + kSC - 1) / kSC;  // stages; the last one may hold fewer than kSC chunks
     const int row0 = chunk * 64;
     const int rows_here = min(64, p.rows - row0);
 
@@ -174,32 +186,46 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     // the next kernel may start only once this CTA holds its TMEM columns, so a waiting
     // successor can never take columns this grid still needs
     pdl_trigger();
+    // split-K: the first cluster phase only tells each CTA that its peers have started (their
+    // shared memory may be written); it completes long before the partial sums are pushed
+    if (p.splits > 1) cluster_arrive_relaxed();
     bool ok = true;
 
+    const int cb = umat_chunk_bytes(p.q4);
     if (warp < 8) {
         // producer: weight row r, Q8_0 block hb of every chunk
         const int r = tid & (kTileM - 1), hb = tid >> 7;
-        for (int c = 0; c < nch; c++) {
-            const int rs = c % kRawStages, ab = c % kAStages;
-            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kRawStages) & 1u, p.err);
-            const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
+        for (int s = 0; s < nst; s++) {
+            const int rs = s % kRawStages, ab = s % kAStages, nsub = min(kSC, nch - s * kSC);
+            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (s / kRawStages) & 1u, p.err);
+            RawPiece pc[kSC];
+#pragma unroll
+            for (int j = 0; j < kSC; j++)
+                if (j < nsub) pc[j] = read_piece(sR + rs * kSC * kRawBytes + j * cb, p.q4, r, hb);
             mbar_arrive(&raw_empty[rs]);
-            if (c >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kAStages) - 1) & 1u, p.err);
-            write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
+            if (s >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((s / kAStages) - 1) & 1u, p.err);
+#pragma unroll
+            for (int j = 0; j < kSC; j++)
+                if (j < nsub) write_piece(pc[j], p.q4, r, hb, sA + (ab * kSC + j) * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
             fence_proxy_async();
             mbar_arrive(&a_full[ab]);
         }
     } else if (warp == 8) {
         if (lane == 0) {
-            for (int c = 0; c < nch; c++) {
-                const int ab = c % kAStages, bb = c % kBStages;
-                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (c / kBStages) & 1u, p.err);
-                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kAStages) & 1u, p.err);
+            for (int s = 0; s < nst; s++) {
+                const int ab = s % kAStages, bb = s % kBStages, nsub = min(kSC, nch - s * kSC);
+                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (s / kBStages) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (s / kAStages) & 1u, p.err);
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kBBytes);
 #pragma unroll
-                for (int kk = 0; kk < kChunkK / 16; kk++)
-                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+                for (int j = 0; j < kSC; j++) {
+                    if (j < nsub) {
+                        const uint32_t a0 = smem_u32(sA + (ab * kSC + j) * kABytes), b0 = smem_u32(sB + (bb * kSC + j) * kBBytes);
+#pragma unroll
+                        for (int kk = 0; kk < kChunkK / 16; kk++)
+                            umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (s > 0 || j > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
                 umma_commit(&a_empty[ab]);
                 umma_commit(&b_empty[bb]);
             }
@@ -207,26 +233,25 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
         }
     } else if (warp == 9) {
         if (lane == 0) {
-            // weights and scales are constant: stream them before the predecessor finishes
-            // one bulk copy per chunk: quants and scales are contiguous in the repacked layout
-            const int cb = umat_chunk_bytes(p.q4);
+            // weights and scales are constant: stream them before the predecessor finishes;
+            // one bulk copy per stage: a tile's chunks are contiguous in the repacked layout
             const uint8_t * base = p.blk + (size_t) (mt * p.KC + c_beg) * cb;
-            for (int c = 0; c < nch; c++) {
-                const int rs = c % kRawStages;
-                if (c >= kRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kRawStages) - 1) & 1u, p.err);
-                uint8_t * raw = sR + rs * kRawBytes;
-                mbar_expect_tx(&raw_full[rs], (uint32_t) cb);
-                bulk_g2s(raw, base + (size_t) c * cb, (uint32_t) cb, &raw_full[rs]);
+            for (int s = 0; s < nst; s++) {
+                const int rs = s % kRawStages, nsub = min(kSC, nch - s * kSC);
+                if (s >= kRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((s / kRawStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&raw_full[rs], (uint32_t) (nsub * cb));
+                bulk_g2s(sR + rs * kSC * kRawBytes, base + (size_t) s * kSC * cb, (uint32_t) (nsub * cb), &raw_full[rs]);
             }
         }
     } else {
         if (lane == 0) {
             pdl_wait();  // activations come from the previous kernel
-            for (int c = 0; c < nch; c++) {
-                const int bb = c % kBStages;
-                if (c >= kBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kBStages) - 1) & 1u, p.err);
-                mbar_expect_tx(&b_full[bb], kBBytes);
-                tma_2d(sB + bb * kBBytes, &xmap, (c_beg + c) * kChunkK, row0, &b_full[bb]);
+            for (int s = 0; s < nst; s++) {
+                const int bb = s % kBStages, nsub = min(kSC, nch - s * kSC);
+                if (s >= kBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((s / kBStages) - 1) & 1u, p.err);
+                mbar_expect_tx(&b_full[bb], (uint32_t) (nsub * kBBytes));
+                for (int j = 0; j < nsub; j++)
+                    tma_2d(sB + (bb * kSC + j) * kBBytes, &xmap, (c_beg + s * kSC + j) * kChunkK, row0, &b_full[bb]);
             }
         }
     }
@@ -290,22 +315,27 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
         return;
     }
 
-    // split-K: partial tile [128][N] f32 (padded rows) in shared memory, reduced across the cluster
-    float * part = reinterpret_cast<float *>(sR);  // raw ring is idle now and holds 128 x (N + 4) floats
-    if (warp < 4) {
-#pragma unroll
-        for (int n = 0; n < N; n += 4)
-            *reinterpret_cast<float4 *>(part + (size_t) m_loc * kPartLd + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
-    }
+    // split-K: each CTA pushes the rows of its partial tile that another split owns into that
+    // split's receive buffer (distributed shared memory stores, no remote loads), then sums the
+    // splits' slices of its own rows in rank order (deterministic)
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
     const int S = p.splits;
     const int rank = (int) cluster.block_rank();
     const int rows_per = kTileM / S;
     const int mbeg = rank * rows_per;
+    cluster_wait();
+    if (warp < 4) {
+        float * dst = cluster.map_shared_rank(recv, m_loc / rows_per) + (size_t) (rank * rows_per + m_loc % rows_per) * kPartLd;
+#pragma unroll
+        for (int n = 0; n < N; n += 4)
+            *reinterpret_cast<float4 *>(dst + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
+    }
+    cluster_arrive();
+    cluster_wait();
+    // peers[q] + ml * kPartLd addresses split q's partial of tile row ml (mbeg <= ml < mbeg + rows_per)
     const float * peers[8];
 #pragma unroll
-    for (int q = 0; q < 8; q++) peers[q] = q < S ? cluster.map_shared_rank(part, q) : part;
+    for (int q = 0; q < 8; q++) peers[q] = recv + (ptrdiff_t) (q * rows_per - mbeg) * kPartLd;
     const int nq = (rows_here + 3) / 4;
     if (EPI == EPI_STORE || EPI == EPI_RESID) {
         // lane -> weight row (coalesced stores per activation row), 4 activation rows per item
@@ -356,7 +386,6 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
             }
         }
     }
-    cluster.sync();
 }
 
 // Prefill shape: 256 activation rows per CTA (MMA N = 256), so each dequantised weight chunk feeds
