@@ -841,6 +841,246 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// Backbone decode attention on the tensor cores (mma.sync m16n8k16, f16 operands, f32
+// accumulation): one CTA per (session, kv head, position range) as in attn_decode_kernel, for one
+// new token and head_dim HD in the paged cache. The G query heads of the kv head are the first G
+// rows of a 16-row A tile (the rest zero); the range is read in chunks of 64 positions (four
+// 16-position pages, one per warp) that go from the f16 cache to shared memory unchanged, so
+// S = Q K^T and O += P V are two MMAs per 8 positions or 8 values instead of one FMA per
+// (position, value). Each warp keeps an online softmax over its pages; the four warps' states
+// are merged in shared memory, and split ranges are published and combined exactly as in
+// attn_decode_kernel.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnDecodeArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int E = HD / 32, LD = HD + 8, CH = 64, PL = HD + 2;
+    constexpr int V4 = CH * HD / 8 / 128;  // 16-byte pieces of K (and of V) per thread per chunk
+    __shared__ __align__(16) half sq[16 * LD];
+    __shared__ __align__(16) half sk[CH * LD];
+    __shared__ __align__(16) half sv[CH * LD];
+    __shared__ float sst[4][4][PL];  // per warp, per query head: weighted values, max (log2 units), sum
+    __shared__ int s_last;
+    const int b = blockIdx.x, h = blockIdx.y, z = blockIdx.z, S = a.splits;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tg = lane & 3;
+    const int G = a.n_head / a.n_kv;
+    const int slot = a.row_slot ? a.row_slot[b] : b;
+    const bool act = (a.row_active ? a.row_active[b] != 0 : true) && slot >= 0;
+    if (!act) {
+        if (warp < G && z == 0)
+            for (int e = 0; e < E; e++) a.out[(size_t) b * a.ldo + (h * G + warp) * HD + lane + 32 * e] = __float2half_rn(0.0f);
+        return;
+    }
+    const int start = a.st ? a.st[slot].pos : a.start;
+    const int L = start + 1;
+    const int * page_row = a.kv.page_table + (size_t) slot * a.kv.max_pages;
+    const int share = ((L + S - 1) / S + 31) & ~31;
+    const int p0 = min(L, z * share), p1 = min(L, p0 + share);
+
+    // 1. the new token's key and value (if in this range) and the query heads, as f16 rows
+    if (warp < 2 && start >= p0 && start < p1) {
+        const int isv = warp;
+        const float * src = a.qkv + (size_t) b * a.ldq + a.n_head * HD + isv * a.n_kv * HD + h * HD;
+        float x[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
+        if (!isv) {
+            if (a.k_norm) head_rmsnorm<HD>(x, a.k_norm, a.eps, lane);
+            rope_apply<HD>(x, a.rope + (size_t) start * (HD / 2), lane);
+        }
+        half * dst = a.kv.pool + paged_off(a.kv, page_row, start, isv, h, a.n_kv, HD);
+#pragma unroll
+        for (int e = 0; e < E; e++) dst[lane + 32 * e] = __float2half_rn(x[e]);
+    }
+    if (warp < G) {
+        const float * src = a.qkv + (size_t) b * a.ldq + (h * G + warp) * HD;
+        float x[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = src[lane + 32 * e];
+        if (a.q_norm) head_rmsnorm<HD>(x, a.q_norm, a.eps, lane);
+        rope_apply<HD>(x, a.rope + (size_t) start * (HD / 2), lane);
+#pragma unroll
+        for (int e = 0; e < E; e++) sq[warp * LD + lane + 32 * e] = __float2half_rn(x[e]);
+    }
+    for (int i = tid; i < (16 - G) * HD; i += 128) sq[(G + i / HD) * LD + i % HD] = __float2half_rn(0.0f);
+
+    // 2. chunks of 64 positions; the next chunk's pages are loaded into registers meanwhile
+    uint4 kr[V4], vr[V4];
+    auto load_chunk = [&](int t0) {
+#pragma unroll
+        for (int i = 0; i < V4; i++) {
+            const int vi = tid + 128 * i, j = vi / (HD / 8), c8 = vi % (HD / 8), pos = t0 + j;
+            kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (pos < p1) {
+                const size_t off = paged_off(a.kv, page_row, pos, 0, h, a.n_kv, HD) + 8 * c8;
+                const size_t vstride = (size_t) a.n_kv * 16 * HD;
+                kr[i] = *reinterpret_cast<const uint4 *>(a.kv.pool + off);
+                vr[i] = *reinterpret_cast<const uint4 *>(a.kv.pool + off + vstride);
+            }
+        }
+    };
+    __syncthreads();  // the appended key/value (global) and the query rows (shared) are visible
+    const float sl2 = a.scale * 1.4426950408889634f;
+    float o[HD / 8][4];
+#pragma unroll
+    for (int n = 0; n < HD / 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+    const uint32_t sq_u = (uint32_t) __cvta_generic_to_shared(sq), sk_u = (uint32_t) __cvta_generic_to_shared(sk),
+                   sv_u = (uint32_t) __cvta_generic_to_shared(sv);
+    if (p0 < p1) load_chunk(p0);
+    for (int t0 = p0; t0 < p1; t0 += CH) {
+#pragma unroll
+        for (int i = 0; i < V4; i++) {
+            const int vi = tid + 128 * i, j = vi / (HD / 8), c8 = vi % (HD / 8);
+            *reinterpret_cast<uint4 *>(sk + j * LD + 8 * c8) = kr[i];
+            *reinterpret_cast<uint4 *>(sv + j * LD + 8 * c8) = vr[i];
+        }
+        __syncthreads();
+        if (t0 + CH < p1) load_chunk(t0 + CH);
+        const int w0 = t0 + 16 * warp;  // this warp's page
+        if (w0 < p1) {
+            float sc[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; kk++) {
+                uint32_t af[4], b0, b1, b2, b3;
+                const int qr = (lane & 7) + ((lane >> 3) & 1) * 8, qc = 16 * kk + (lane >> 4) * 8;
+                ldsm_x4(sq_u + (uint32_t) (qr * LD + qc) * 2, af[0], af[1], af[2], af[3]);
+                const int kr_ = 16 * warp + (lane & 7) + (lane >> 4) * 8, kc = 16 * kk + ((lane >> 3) & 1) * 8;
+                ldsm_x4(sk_u + (uint32_t) (kr_ * LD + kc) * 2, b0, b1, b2, b3);
+                mma16816(sc[0], af, b0, b1);
+                mma16816(sc[1], af, b2, b3);
+            }
+            float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+            for (int n = 0; n < 2; n++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const bool ok = w0 + 8 * n + 2 * tg + e < p1;
+                    sc[n][e] = ok ? sc[n][e] * sl2 : -INFINITY;
+                    sc[n][2 + e] = ok ? sc[n][2 + e] * sl2 : -INFINITY;
+                    mx_a = fmaxf(mx_a, sc[n][e]);
+                    mx_b = fmaxf(mx_b, sc[n][2 + e]);
+                }
+            }
+#pragma unroll
+            for (int off = 1; off <= 2; off <<= 1) {
+                mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+                mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+            }
+            // every page holds at least one valid position, so the new maxima are finite
+            const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+            const float c_a = exp2f(m_a - mn_a), c_b = exp2f(m_b - mn_b);
+            m_a = mn_a;
+            m_b = mn_b;
+            float sum_a = 0.0f, sum_b = 0.0f;
+#pragma unroll
+            for (int n = 0; n < 2; n++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    sc[n][e] = sc[n][e] == -INFINITY ? 0.0f : exp2f(sc[n][e] - mn_a);
+                    sc[n][2 + e] = sc[n][2 + e] == -INFINITY ? 0.0f : exp2f(sc[n][2 + e] - mn_b);
+                    sum_a += sc[n][e];
+                    sum_b += sc[n][2 + e];
+                }
+            }
+            l_a = l_a * c_a + sum_a;
+            l_b = l_b * c_b + sum_b;
+            uint32_t pf[4];
+            pf[0] = pack_h2(sc[0][0], sc[0][1]);
+            pf[1] = pack_h2(sc[0][2], sc[0][3]);
+            pf[2] = pack_h2(sc[1][0], sc[1][1]);
+            pf[3] = pack_h2(sc[1][2], sc[1][3]);
+#pragma unroll
+            for (int n2 = 0; n2 < HD / 16; n2++) {
+                o[2 * n2][0] *= c_a; o[2 * n2][1] *= c_a; o[2 * n2][2] *= c_b; o[2 * n2][3] *= c_b;
+                o[2 * n2 + 1][0] *= c_a; o[2 * n2 + 1][1] *= c_a; o[2 * n2 + 1][2] *= c_b; o[2 * n2 + 1][3] *= c_b;
+                uint32_t b0, b1, b2, b3;
+                const int vr_ = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, vc = 16 * n2 + (lane >> 4) * 8;
+                ldsm_x4_t(sv_u + (uint32_t) (vr_ * LD + vc) * 2, b0, b1, b2, b3);
+                mma16816(o[2 * n2], pf, b0, b1);
+                mma16816(o[2 * n2 + 1], pf, b2, b3);
+            }
+        }
+        __syncthreads();  // every warp is done with this chunk before the next one is stored
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+
+    // 3. merge the four warps' states of each query head (rows g < G live in lanes 0..4G-1)
+    if (g < G) {
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++) {
+            sst[warp][g][8 * n + 2 * tg] = o[n][0];
+            sst[warp][g][8 * n + 2 * tg + 1] = o[n][1];
+        }
+        if (tg == 0) {
+            sst[warp][g][HD] = m_a;
+            sst[warp][g][HD + 1] = l_a;
+        }
+    }
+    __syncthreads();
+    float * base = a.part + ((size_t) (b * a.n_kv + h) * S) * (4 * 2 * PL);
+    for (int i = tid; i < G * HD; i += 128) {
+        const int r = i / HD, d = i % HD;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) mx = fmaxf(mx, sst[w][r][HD]);
+        float ov = 0.0f, lv = 0.0f;
+        if (mx != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                const float mw = sst[w][r][HD];
+                if (mw == -INFINITY) continue;
+                const float f = exp2f(mw - mx);
+                ov += f * sst[w][r][d];
+                lv += f * sst[w][r][HD + 1];
+            }
+        }
+        if (S == 1) {
+            a.out[(size_t) b * a.ldo + (h * G + r) * HD + d] = __float2half_rn(lv > 0.0f ? ov / lv : 0.0f);
+        } else {
+            // the published state in natural-log units, as attn_decode_kernel writes it
+            float * pp = base + ((size_t) z * 8 + r * 2) * PL;
+            pp[d] = ov;
+            if (d == 0) {
+                pp[HD] = mx == -INFINITY ? -INFINITY : mx * 0.6931471805599453f;
+                pp[HD + 1] = lv;
+            }
+        }
+    }
+    if (S == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        int * ctr = a.counters + (size_t) b * a.n_kv + h;
+        const int prev = atomicAdd(ctr, 1);
+        s_last = prev == S - 1;
+        if (s_last) *ctr = 0;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last || warp >= G) return;
+    __threadfence();
+    float mx = -INFINITY;
+    for (int zz = 0; zz < S; zz++) mx = fmaxf(mx, __ldcg(base + ((size_t) zz * 8 + warp * 2) * PL + HD));
+    float lsum = 0.0f, ov[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) ov[e] = 0.0f;
+    for (int zz = 0; zz < S; zz++) {
+        const float * pp = base + ((size_t) zz * 8 + warp * 2) * PL;
+        const float mz = __ldcg(pp + HD), lz = __ldcg(pp + HD + 1);
+        if (lz == 0.0f || mz == -INFINITY) continue;  // an empty range
+        const float w = expf(mz - mx);
+        lsum += lz * w;
+#pragma unroll
+        for (int e = 0; e < E; e++) ov[e] += w * __ldcg(pp + lane + 32 * e);
+    }
+    const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; e++) a.out[(size_t) b * a.ldo + (h * G + warp) * HD + lane + 32 * e] = __float2half_rn(ov[e] * inv);
+}
+
 template <int HD>
 __host__ __device__ constexpr int prefill_kb() { return HD >= 256 ? 32 : 64; }
 template <int HD>
@@ -1547,6 +1787,14 @@ void launch_attn_decode(const AttnDecodeArgs & a, bool paged, cudaStream_t s) {
         throw std::runtime_error("decode attention: split-KV needs 1..16 splits, scratch and counters");
     dim3 grid(a.R, a.n_kv, a.splits);
     const int threads = 128;
+    // one new token over the paged cache at head_dim 64 (the backbone): the tensor-core kernel;
+    // BZB_ATTN_MMA=0 selects the scalar one
+    static const bool mma_off = [] { const char * e = std::getenv("BZB_ATTN_MMA"); return e && std::atoi(e) == 0; }();
+    if (paged && a.hd == 64 && a.n_new == 1 && !mma_off) {
+        launch_k(attn_decode_mma_kernel<64>, grid, threads, 0, s, a);
+        BZB_CUDA_CHECK(cudaGetLastError());
+        return;
+    }
     if (a.hd == 64) {
         if (paged) launch_k(attn_decode_kernel<64, true>, grid, threads, 0, s, a);
         else launch_k(attn_decode_kernel<64, false>, grid, threads, 0, s, a);
