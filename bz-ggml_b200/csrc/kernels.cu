@@ -841,11 +841,18 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void * src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // Backbone decode attention on the tensor cores (mma.sync m16n8k16, f16 operands, f32
 // accumulation): one CTA per (session, kv head, position range) as in attn_decode_kernel, for one
 // new token and head_dim HD in the paged cache. The G query heads of the kv head are the first G
 // rows of a 16-row A tile (the rest zero); the range is read in chunks of 64 positions (four
-// 16-position pages, one per warp) that go from the f16 cache to shared memory unchanged, so
+// 16-position pages, one per warp) that asynchronous copies bring from the f16 cache to shared
+// memory unchanged, one chunk ahead of the MMAs, so
 // S = Q K^T and O += P V are two MMAs per 8 positions or 8 values instead of one FMA per
 // (position, value). Each warp keeps an online softmax over its pages; the four warps' states
 // are merged in shared memory, and split ranges are published and combined exactly as in
@@ -857,8 +864,8 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnDecodeAr
     constexpr int E = HD / 32, LD = HD + 8, CH = 64, PL = HD + 2;
     constexpr int V4 = CH * HD / 8 / 128;  // 16-byte pieces of K (and of V) per thread per chunk
     __shared__ __align__(16) half sq[16 * LD];
-    __shared__ __align__(16) half sk[CH * LD];
-    __shared__ __align__(16) half sv[CH * LD];
+    __shared__ __align__(16) half sk2[2][CH * LD];
+    __shared__ __align__(16) half sv2[2][CH * LD];
     __shared__ float sst[4][4][PL];  // per warp, per query head: weighted values, max (log2 units), sum
     __shared__ int s_last;
     const int b = blockIdx.x, h = blockIdx.y, z = blockIdx.z, S = a.splits;
@@ -904,19 +911,18 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnDecodeAr
     }
     for (int i = tid; i < (16 - G) * HD; i += 128) sq[(G + i / HD) * LD + i % HD] = __float2half_rn(0.0f);
 
-    // 2. chunks of 64 positions; the next chunk's pages are loaded into registers meanwhile
-    uint4 kr[V4], vr[V4];
-    auto load_chunk = [&](int t0) {
+    // 2. chunks of 64 positions, double-buffered: positions past the range are zero-filled
+    auto load_chunk = [&](int t0, int buf) {
+        const uint32_t ku = (uint32_t) __cvta_generic_to_shared(sk2[buf]), vu = (uint32_t) __cvta_generic_to_shared(sv2[buf]);
 #pragma unroll
         for (int i = 0; i < V4; i++) {
             const int vi = tid + 128 * i, j = vi / (HD / 8), c8 = vi % (HD / 8), pos = t0 + j;
-            kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
-            if (pos < p1) {
-                const size_t off = paged_off(a.kv, page_row, pos, 0, h, a.n_kv, HD) + 8 * c8;
-                const size_t vstride = (size_t) a.n_kv * 16 * HD;
-                kr[i] = *reinterpret_cast<const uint4 *>(a.kv.pool + off);
-                vr[i] = *reinterpret_cast<const uint4 *>(a.kv.pool + off + vstride);
-            }
+            const bool valid = pos < p1;
+            const size_t off = valid ? paged_off(a.kv, page_row, pos, 0, h, a.n_kv, HD) + 8 * c8 : 0;
+            const size_t vstride = valid ? (size_t) a.n_kv * 16 * HD : 0;
+            const uint32_t so = (uint32_t) (j * LD + 8 * c8) * 2;
+            cp_async16(ku + so, a.kv.pool + off, valid);
+            cp_async16(vu + so, a.kv.pool + off + vstride, valid);
         }
     };
     __syncthreads();  // the appended key/value (global) and the query rows (shared) are visible
@@ -925,18 +931,15 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnDecodeAr
 #pragma unroll
     for (int n = 0; n < HD / 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
-    const uint32_t sq_u = (uint32_t) __cvta_generic_to_shared(sq), sk_u = (uint32_t) __cvta_generic_to_shared(sk),
-                   sv_u = (uint32_t) __cvta_generic_to_shared(sv);
-    if (p0 < p1) load_chunk(p0);
-    for (int t0 = p0; t0 < p1; t0 += CH) {
-#pragma unroll
-        for (int i = 0; i < V4; i++) {
-            const int vi = tid + 128 * i, j = vi / (HD / 8), c8 = vi % (HD / 8);
-            *reinterpret_cast<uint4 *>(sk + j * LD + 8 * c8) = kr[i];
-            *reinterpret_cast<uint4 *>(sv + j * LD + 8 * c8) = vr[i];
-        }
-        __syncthreads();
-        if (t0 + CH < p1) load_chunk(t0 + CH);
+    const uint32_t sq_u = (uint32_t) __cvta_generic_to_shared(sq);
+    if (p0 < p1) load_chunk(p0, 0);
+    cp_async_commit();
+    for (int t0 = p0, it = 0; t0 < p1; t0 += CH, it++) {
+        if (t0 + CH < p1) load_chunk(t0 + CH, (it + 1) & 1);
+        cp_async_commit();  // possibly empty: the wait below always leaves exactly the newest group
+        cp_async_wait1();
+        __syncthreads();    // every thread's copies of this chunk have landed
+        const uint32_t sk_u = (uint32_t) __cvta_generic_to_shared(sk2[it & 1]), sv_u = (uint32_t) __cvta_generic_to_shared(sv2[it & 1]);
         const int w0 = t0 + 16 * warp;  // this warp's page
         if (w0 < p1) {
             float sc[2][4];
@@ -1003,7 +1006,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnDecodeAr
                 mma16816(o[2 * n2 + 1], pf, b2, b3);
             }
         }
-        __syncthreads();  // every warp is done with this chunk before the next one is stored
+        __syncthreads();  // every warp is done with this buffer before the copies after next refill it
     }
 #pragma unroll
     for (int off = 1; off <= 2; off <<= 1) l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
