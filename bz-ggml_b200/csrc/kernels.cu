@@ -1427,6 +1427,81 @@ __device__ int pick_from_sorted(const unsigned long long * keys, int V, float te
     return pick;
 }
 
+// The `keep` largest of the block's keys (each thread holds kv[0..3], unique keys, padding 0),
+// sorted descending into sel[0..64) (the rest 0): a radix select finds the keep-th largest key
+// one byte at a time from the top (8 histogram passes over the candidates still matching the
+// bytes found), the keys at or above it are gathered, and one warp sorts those <= 64 keys.
+// The result equals the first `keep` entries of sort_keys_desc over the same keys.
+__device__ void select_top_keys(const unsigned long long (&kv)[4], int keep, unsigned long long * sel, int * hist,
+                                unsigned long long * s_prefix, int * s_rem) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    unsigned long long prefix = 0ull;
+    int rem = keep;
+    for (int d = 7; d >= 0; d--) {
+        if (tid < 256) hist[tid] = 0;
+        __syncthreads();
+        const unsigned long long hi = d == 7 ? 0ull : (~0ull << (8 * (d + 1)));
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if ((kv[q] & hi) == (prefix & hi)) atomicAdd(&hist[(kv[q] >> (8 * d)) & 255], 1);
+        __syncthreads();
+        if (tid < 32) {
+            // lane l scans bins 255 - 8 l down to 248 - 8 l: lanes in order visit the bins from the top
+            int c = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) c += hist[255 - 8 * lane - j];
+            int incl = c;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += t;
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, incl >= rem);
+            const int L = __ffs(m) - 1;
+            if (lane == L) {
+                int acc = incl - c;
+                int b = 255 - 8 * lane - 7;
+                for (int j = 0; j < 8; j++) {
+                    const int h = hist[255 - 8 * lane - j];
+                    if (acc + h >= rem) { b = 255 - 8 * lane - j; break; }
+                    acc += h;
+                }
+                *s_prefix = prefix | ((unsigned long long) b << (8 * d));
+                *s_rem = rem - acc;
+            }
+        }
+        __syncthreads();
+        prefix = *s_prefix;
+        rem = *s_rem;
+    }
+    // prefix is now the keep-th largest key: exactly `keep` keys are >= it
+    __syncthreads();  // every thread has read the last pass's shared results
+    if (tid < 64) sel[tid] = 0ull;
+    if (tid == 0) *s_rem = 0;
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        if (kv[q] >= prefix) sel[atomicAdd(s_rem, 1)] = kv[q];
+    __syncthreads();
+    if (tid < 32) {
+        for (int kk = 2; kk <= 64; kk <<= 1) {
+            for (int j = kk >> 1; j > 0; j >>= 1) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int i = lane + 32 * h, ixj = i ^ j;
+                    if (ixj > i) {
+                        const unsigned long long x = sel[i], y = sel[ixj];
+                        const bool desc = (i & kk) == 0;
+                        if (desc ? (x < y) : (x > y)) { sel[i] = y; sel[ixj] = x; }
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    }
+    __syncthreads();
+}
+
 __device__ __forceinline__ float philox_unit(uint32_t key, uint32_t draw, uint32_t hi) {
     return (float) (philox_word0(key, draw, hi) >> 8) * (1.0f / 16777216.0f);
 }
@@ -1447,7 +1522,10 @@ __global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
     const float * lu = pr >= 0 ? a.logits + (size_t) pr * a.ld : nullptr;
     const float cfg = s.cfg, rep = s.rep;
     const uint16_t * hr = a.hist + (size_t) slot * a.hist_ld;
-    for (int i = threadIdx.x; i < kSortN; i += blockDim.x) {
+    unsigned long long kv[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int i = threadIdx.x + q * blockDim.x;
         unsigned long long key = 0ull;
         if (i < a.V) {
             float l = lr[i];
@@ -1455,18 +1533,31 @@ __global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
             if (i >= a.sup_lo && i < a.sup_hi) l = -INFINITY;
             if (rep != 1.0f && i < a.hist_ld) {
                 const int c = hr[i];
-                for (int q = 0; q < c; q++) l = l > 0.0f ? l / rep : l * rep;
+                for (int q2 = 0; q2 < c; q2++) l = l > 0.0f ? l / rep : l * rep;
             }
             key = sort_key(l, i);
         }
-        keys[i] = key;
+        kv[q] = key;
     }
-    __syncthreads();
-    sort_keys_desc(keys);
+    // top-k of at most 64 (the reference's 50): select instead of sorting every key
+    const int keep = (s.top_k > 0 && s.top_k < a.V) ? s.top_k : a.V;
+    __shared__ int s_hist[256];
+    __shared__ unsigned long long s_sel[64], s_prefix;
+    __shared__ int s_rem;
+    const unsigned long long * sorted = keys;
+    if (keep <= 64) {
+        select_top_keys(kv, keep, s_sel, s_hist, &s_prefix, &s_rem);
+        sorted = s_sel;
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) keys[threadIdx.x + q * blockDim.x] = kv[q];
+        __syncthreads();
+        sort_keys_desc(keys);
+    }
     if (threadIdx.x != 0) return;
     uint32_t key = s.key, draw = s.draw;
     if (a.seeds) { key = a.seeds[r] + (uint32_t) (a.step_ctr ? *a.step_ctr : 0); draw = 0; }
-    const int pick = pick_from_sorted(keys, a.V, s.temp, s.top_k, s.top_p, philox_unit(key, draw, 0u));
+    const int pick = pick_from_sorted(sorted, a.V, s.temp, s.top_k, s.top_p, philox_unit(key, draw, 0u));
     s.key = key;
     s.draw = draw + 1;
     SessState * u = pr >= 0 ? &a.st[a.row_slot[pr]] : nullptr;  // the unconditional branch's state
@@ -1852,6 +1943,7 @@ void launch_argmax_gather(const StepArgs & a, const float * logits, int ld, int 
 
 void launch_sample(const SampleArgs & a, cudaStream_t s) {
     if (a.V > kSortN) throw std::runtime_error("sampler: vocabulary larger than 4096");
+    static_assert(kSortN == 4 * 1024, "the sampler's threads hold four keys each");
     launch_k(sample_kernel, a.R, 1024, 0, s, a);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
