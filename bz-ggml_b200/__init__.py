@@ -104,6 +104,10 @@ SIGNATURES = {
                                                  _c_int_p, _c_float_p]),
     "bzb_generator_debug_gemv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                 _c_float_p, _c_float_p]),
+    "bzb_generator_debug_gemm": (ctypes.c_longlong, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, _c_float_p,
+                                                     _c_float_p, ctypes.c_int]),
+    "bzb_generator_debug_grid_spin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
+    "bzb_debug_mbar_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong]),
     "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_int]),
     "bzb_generator_depth_trace": (ctypes.c_int, [ctypes.c_void_p, _c_double_p, ctypes.c_int]),
@@ -261,6 +265,20 @@ class GeneratorHandle:
 
     def active_session_count(self) -> int:
         return self.lib.lib.breeze_generator_session_count(self.handle)
+
+    def sessions_step_round(self, session_ids: Sequence[int], seed: int = 42) -> Tuple[List[int], List[List[int]]]:
+        """One session_step per listed session with seed + i (reference bindings.py:307-319): returns
+        (next cb0 per session, -1 at EOS, budget or unknown session; frames [n][16], rows of sessions
+        that did not step left zero)."""
+        n = len(session_ids)
+        if n == 0:
+            return [], []
+        ids = np.asarray(session_ids, np.int32)
+        fr = np.zeros((n, 16), np.int32)
+        nx = np.zeros(n, np.int32)
+        self.last_round_completed = self.lib.lib.breeze_generator_sessions_step_round(
+            self.handle, _ip(ids), n, ctypes.c_uint(seed & 0xFFFFFFFF), _ip(fr), _ip(nx))
+        return nx.tolist(), fr.tolist()
 
     def sessions_step_batched(self, session_ids: Sequence[int], seeds: Optional[Sequence[int]] = None):
         n = len(session_ids)
@@ -427,6 +445,21 @@ class GeneratorHandle:
     def session_set_q4(self, session_id: int, use_q4: bool = True) -> bool:
         return self.lib.lib.breeze_generator_session_set_q4(self.handle, session_id, 1 if use_q4 else 0) == 0
 
+    def debug_gemm(self, name: str, x: np.ndarray, out_dim: int, repeats: int = 0) -> Tuple[np.ndarray, int]:
+        """One launch of a resident (step-layout) matrix on x [rows][K]: returns (y [rows][out_dim],
+        32-bit words that differed over `repeats` captured re-launches)."""
+        xx = np.ascontiguousarray(x, np.float32)
+        y = np.zeros((xx.shape[0], out_dim), np.float32)
+        n = self.lib.lib.bzb_generator_debug_gemm(self.handle, name.encode(), xx.shape[0], _fp(xx), _fp(y), repeats)
+        if n < 0:
+            raise RuntimeError(self.lib.last_error())
+        return y, int(n)
+
+    def set_debug_grid_spin(self, polls: int) -> None:
+        """Grid-barrier poll limit of the persistent depth launches debug_depth makes (0: default)."""
+        if self.lib.lib.bzb_generator_debug_grid_spin(self.handle, int(polls)) != 0:
+            raise RuntimeError(self.lib.last_error())
+
     def debug_gemv(self, tensor: str, x: np.ndarray, out_dim: int, sub: int = -1) -> np.ndarray:
         xx = np.ascontiguousarray(x, np.float32)
         y = np.zeros((xx.shape[0], out_dim), np.float32)
@@ -563,6 +596,15 @@ class ContextHandle:
 
     def __del__(self):
         self.close()
+
+
+def mbar_timeout_probe(polls: int, device: int = 0) -> int:
+    """Error code recorded by the tcgen05 pipelines' bounded mbarrier wait when it runs out on a
+    barrier nothing arrives on (bzb_debug_mbar_timeout)."""
+    code = lib().lib.bzb_debug_mbar_timeout(device, int(polls))
+    if code < 0:
+        raise RuntimeError(lib().last_error())
+    return code
 
 
 def split_text(text: str, budget: int, first_budget: int = 0) -> List[str]:

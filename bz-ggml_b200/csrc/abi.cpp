@@ -708,6 +708,40 @@ int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int su
     }
 }
 
+int bzb_generator_debug_grid_spin(breeze_generator * gen, long long polls) {
+    if (!gen) return -1;
+    gen->eng->set_debug_grid_spin(polls);
+    return 0;
+}
+
+int bzb_debug_mbar_timeout(int device, long long polls) {
+    if (polls <= 0) {
+        set_error("mbar_timeout: the poll limit must be positive");
+        return -1;
+    }
+    try {
+        if (cudaSetDevice(device) != cudaSuccess) throw std::runtime_error("no such CUDA device");
+        return bzb::probe_mbar_timeout(polls);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+long long bzb_generator_debug_gemm(breeze_generator * gen, const char * name, int rows, const float * x, float * y,
+                                   int repeats) {
+    if (!gen || !name || rows <= 0 || !x || !y || repeats < 0) {
+        set_error("debug_gemm: bad arguments");
+        return -1;
+    }
+    try {
+        return gen->eng->debug_gemm(name, rows, x, y, repeats);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * tensor, int rows, const void * x16, int ldx,
                                float * y, int ldy, void * stream) {
     if (!gen || !tensor) {

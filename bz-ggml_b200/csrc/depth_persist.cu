@@ -95,10 +95,25 @@ __device__ __forceinline__ bool dwait(uint64_t * bar, uint32_t parity, int * err
 }
 constexpr unsigned kBackoff = 64;
 
+// the wait for copies and MMAs a role has issued, after a failure: unlike dwait it does not
+// return early because an error is recorded, so the CTA releases its shared and tensor memory
+// only after they have landed (error code 5 if even they time out)
+__device__ __forceinline__ bool ddrain(uint64_t * bar, uint32_t parity, int * err) {
+    const uint32_t a = smem_u32(bar);
+    for (long long i = 0; i < kSpinLimit * 16; i++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    atomicCAS(err, 0, 5);
+    return false;
+}
+
 // wait until `target` phase arrivals have been counted (every phase before the current one
 // complete on every CTA)
-__device__ __forceinline__ bool grid_wait(const unsigned * bar, unsigned target, int * err) {
-    for (long long i = 0; i < kGridSpin; i++) {
+__device__ __forceinline__ bool grid_wait(const unsigned * bar, unsigned target, int * err, long long limit) {
+    for (long long i = 0; i < limit; i++) {
         unsigned v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
         if (v >= target) return true;
@@ -488,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     int * err = p.err;
+    const long long grid_spin = p.grid_spin > 0 ? p.grid_spin : kGridSpin;
 
     if (warp == kMmaWarp) tmem_alloc(&tmem_slot, kTmemCols);
     if (tid == 0) {
@@ -525,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
         for (int i = 0; i < p.n_phases; i++) {
             const DpPhase ph = load_phase(p.phases + i);
             if (tid == 0) {
-                s_stop = (s_abort || !grid_wait(p.bar, (unsigned) i * G, err)) ? 1 : 0;
+                s_stop = (s_abort || !grid_wait(p.bar, (unsigned) i * G, err, grid_spin)) ? 1 : 0;
                 if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots] = gtimer();
             }
             epi_sync();
@@ -727,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
             }
             // every MMA issued above has completed before TMEM is released
             umma_commit(&drain_bar);
-            dwait(&drain_bar, 0, err);
+            ddrain(&drain_bar, 0, err);
             if (!ok) s_abort = 1;
         }
     } else if (warp == kWeightWarp) {
@@ -755,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
             }
             // copies still in flight land before the CTA exits
             for (uint32_t k = rg > (uint32_t) kRawGroups ? rg - kRawGroups : 0; k < rg; k++)
-                dwait(&raw_full[k % kRawGroups], (k / kRawGroups) & 1u, err);
+                ddrain(&raw_full[k % kRawGroups], (k / kRawGroups) & 1u, err);
             if (!ok) s_abort = 1;
         }
     } else {
@@ -768,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                 if (ph.type != DP_GEMM) continue;
                 const int v0 = unit_of(i, cta, G);
                 if (v0 >= ph.n_units) continue;
-                ok = grid_wait(p.bar, (unsigned) i * G, err);
+                ok = grid_wait(p.bar, (unsigned) i * G, err, grid_spin);
                 if (!ok) break;
                 fence_proxy_async_global();
                 if (p.trace) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 2] = gtimer();
@@ -786,7 +802,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                 }
             }
             for (uint32_t k = bg > (uint32_t) kBGroups ? bg - kBGroups : 0; k < bg; k++)
-                dwait(&b_full[k % kBGroups], (k / kBGroups) & 1u, err);
+                ddrain(&b_full[k % kBGroups], (k / kBGroups) & 1u, err);
             if (!ok) s_abort = 1;
         }
     }

@@ -82,6 +82,9 @@ struct DpParams {
     float * logits_out = nullptr;       // [R][nc-1][vs] or null
     unsigned * bar = nullptr;           // phase-arrival counter, zero at launch
     int * err = nullptr;
+    // polls of a grid phase barrier before the CTA gives up (error code 3); 0 keeps the default
+    // (about a second). A shorter limit lets a test make the barrier run out on purpose.
+    long long grid_spin = 0;
     // optional timeline [n_phases][grid][kDpTraceSlots] of %globaltimer (ns) per CTA and phase:
     // 0 epilogue start, 1 epilogue end, 2 activation loads start, 3 first activation chunk
     // landed, 4 first weight tile dequantised, 5 last MMA issued, 6 accumulator ready,

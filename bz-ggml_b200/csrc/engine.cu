@@ -753,8 +753,15 @@ int Engine::depth_trace(double * out, int max_phases) {
     return (int) total;
 }
 
+void Engine::raise_device_error(int code, const std::string & what) {
+    // the failure is reported once: clear the word so that the next launches start clean
+    CK(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
+    CK(cudaStreamSynchronize(stream_));
+    throw std::runtime_error(what + " (device error code " + std::to_string(code) + ")");
+}
+
 void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace,
-                           const int * row_set) {
+                           const int * row_set, long long grid_spin) {
     const DpPlan * pl = depth_plan(R);
     if (!pl) throw std::runtime_error("persistent depth decoder: unsupported batch");
     const DdConfig & dd = cfg.dd;
@@ -775,6 +782,7 @@ void Engine::enqueue_depth(int R, const int * forced_dev, float * logits_dev, un
     p.row_set = row_set; p.set_id = cur_set_;
     p.forced = forced_dev; p.logits_out = logits_dev;
     p.bar = dp_bar_; p.err = err_; p.trace = trace;
+    p.grid_spin = grid_spin;
     if (prof_) {
         CK(cudaEventCreate(&dprof_a_));
         CK(cudaEventCreate(&dprof_b_));
@@ -1012,9 +1020,7 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     int errv = 0;
     CK(cudaMemcpyAsync(&errv, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
-    if (errv)
-        throw std::runtime_error("a bounded wait timed out inside the frame step (device error code " +
-                                 std::to_string(errv) + ")");
+    if (errv) raise_device_error(errv, "a bounded wait timed out inside the frame step");
     for (int k = 0; k < K; k++) res.steps_executed += aa[k] ? 1 : 0;
     const int wcopy = std::min(width, nc);
     for (int k = 0; k < K; k++) {
@@ -1651,7 +1657,7 @@ void Engine::debug_depth(int n, const float * hidden, const int * cb0, const int
             CK(cudaMemcpyAsync(fd, f.data(), f.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
         }
         depth_plan(R);
-        enqueue_depth(R, fd, ld);
+        enqueue_depth(R, fd, ld, nullptr, nullptr, dbg_grid_spin_);
         std::vector<float> all((size_t) R * (nc - 1) * vs);
         int errv = 0;
         CK(cudaMemcpyAsync(all.data(), ld, all.size() * sizeof(float), cudaMemcpyDeviceToHost, stream_));
@@ -1660,7 +1666,7 @@ void Engine::debug_depth(int n, const float * hidden, const int * cb0, const int
         CK(cudaStreamSynchronize(stream_));
         cudaFree(ld);
         if (fd) cudaFree(fd);
-        if (errv) throw std::runtime_error("persistent depth decoder: a bounded wait timed out (device error code " + std::to_string(errv) + ")");
+        if (errv) raise_device_error(errv, "persistent depth decoder: a bounded wait timed out");
         std::memcpy(logits_out, all.data(), (size_t) n * (nc - 1) * vs * sizeof(float));
         for (int i = 0; i < n; i++)
             for (int j = 1; j < nc; j++) codes_out[(size_t) i * (nc - 1) + (j - 1)] = fr[(size_t) i * nc + j];
@@ -1799,6 +1805,105 @@ double Engine::bench_gemv(const char * tensor, int sub, int rows, int iters, int
     cudaFree(xd);
     cudaFree(yd);
     return ms * 1000.0 / iters;
+}
+
+const QMat * Engine::resident_any(const char * name, int * epi) const {
+    *epi = EPI_STORE;
+    if (const QMat * m = resident_matrix(name)) return m;
+    int l = -1, n = 0;
+    char part[32] = { 0 };
+    if (std::sscanf(name, "dd.head.%d%n", &l, &n) == 1 && name[n] == 0)
+        return l >= 0 && l < (int) dd_head_.size() ? &dd_head_[l] : nullptr;
+    if (std::strcmp(name, "te.proj.weight") == 0) return has_te_ ? &te_proj_ : nullptr;
+    const std::vector<LayerW> * layers = nullptr;
+    int gated = EPI_SWIGLU;
+    if (std::sscanf(name, "bb.blk.%d.%31[a-z_]%n", &l, part, &n) == 2 && name[n] == 0) layers = &bb_;
+    else if (std::sscanf(name, "dd.blk.%d.%31[a-z_]%n", &l, part, &n) == 2 && name[n] == 0) layers = &dd_;
+    else if (std::sscanf(name, "te.blk.%d.%31[a-z_]%n", &l, part, &n) == 2 && name[n] == 0) {
+        layers = &te_;
+        gated = EPI_GEGLU;
+    }
+    if (!layers || l < 0 || l >= (int) layers->size()) return nullptr;
+    if (std::strcmp(part, "attn_qkv") == 0) return &(*layers)[l].qkv;
+    if (std::strcmp(part, "attn_output") == 0) return &(*layers)[l].o;
+    if (std::strcmp(part, "ffn_down") == 0) return &(*layers)[l].down;
+    if (std::strcmp(part, "ffn_gate_up") == 0) {
+        *epi = gated;
+        return &(*layers)[l].gu;
+    }
+    return nullptr;
+}
+
+long long Engine::debug_gemm(const char * name, int rows, const float * x, float * y, int repeats) {
+    int epi = EPI_STORE;
+    const QMat * wp = resident_any(name, &epi);
+    if (!wp) throw std::runtime_error(std::string("debug_gemm: no resident matrix named ") + name);
+    if (rows <= 0 || repeats < 0) throw std::runtime_error("debug_gemm: bad row or repeat count");
+    const QMat & w = *wp;
+    const bool gated = epi >= EPI_SWIGLU;
+    const int K = w.K, ld = gated ? w.M / 2 : w.M;
+    const size_t out_bytes = (size_t) rows * ld * (gated ? sizeof(half) : sizeof(float));
+    std::vector<half> xh((size_t) rows * K);
+    for (size_t i = 0; i < xh.size(); i++) xh[i] = __float2half_rn(x[i]);
+    half * xd = nullptr;
+    void * y0 = nullptr, * y1 = nullptr;
+    int * cnt = nullptr;
+    CK(cudaMalloc(&xd, xh.size() * sizeof(half)));
+    CK(cudaMalloc(&y0, out_bytes));
+    CK(cudaMalloc(&y1, out_bytes));
+    CK(cudaMalloc(&cnt, sizeof(int)));
+    long long mismatches = 0;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    auto out_of = [&](void * p) {
+        return gated ? GemvOut{ epi, nullptr, static_cast<half *>(p), ld } : GemvOut{ epi, static_cast<float *>(p), nullptr, ld };
+    };
+    try {
+        CK(cudaMemcpyAsync(xd, xh.data(), xh.size() * sizeof(half), cudaMemcpyHostToDevice, stream_));
+        CK(cudaMemsetAsync(cnt, 0, sizeof(int), stream_));
+        launch_gemm(w, xd, K, rows, out_of(y0));
+        if (repeats > 0) {
+            // the frame step's conditions: captured launches with programmatic dependent launch
+            CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+            set_pdl_scope(true);
+            try {
+                for (int r = 0; r < repeats; r++) {
+                    launch_gemm(w, xd, K, rows, out_of(y1));
+                    launch_bits_diff(y0, y1, out_bytes / 4, cnt, stream_);
+                }
+            } catch (...) {
+                set_pdl_scope(false);
+                cudaStreamEndCapture(stream_, &g);
+                throw;
+            }
+            set_pdl_scope(false);
+            CK(cudaStreamEndCapture(stream_, &g));
+            CK(cudaGraphInstantiate(&ge, g, 0));
+            CK(cudaGraphLaunch(ge, stream_));
+        }
+        std::vector<uint8_t> hb(out_bytes);
+        int c = 0, errv = 0;
+        CK(cudaMemcpyAsync(hb.data(), y0, out_bytes, cudaMemcpyDeviceToHost, stream_));
+        CK(cudaMemcpyAsync(&c, cnt, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaMemcpyAsync(&errv, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+        if (errv) raise_device_error(errv, "debug_gemm: a bounded wait timed out in the tcgen05 GEMM");
+        mismatches = c;
+        const size_t n = (size_t) rows * ld;
+        if (gated)
+            for (size_t i = 0; i < n; i++) y[i] = __half2float(reinterpret_cast<const half *>(hb.data())[i]);
+        else
+            std::memcpy(y, hb.data(), out_bytes);
+    } catch (...) {
+        if (ge) cudaGraphExecDestroy(ge);
+        if (g) cudaGraphDestroy(g);
+        cudaFree(xd); cudaFree(y0); cudaFree(y1); cudaFree(cnt);
+        throw;
+    }
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    cudaFree(xd); cudaFree(y0); cudaFree(y1); cudaFree(cnt);
+    return mismatches;
 }
 
 const QMat * Engine::resident_matrix(const char * tensor) const {

@@ -132,6 +132,18 @@ public:
     size_t depth_bytes_per_step() const;
     // average microseconds of `iters` back-to-back launches of one dequant-GEMM (epilogue kind)
     double bench_gemv(const char * tensor, int sub, int rows, int iters, int epi);
+    // one launch of a matrix as the frame step holds it (fused q/k/v, gate/up interleaved with
+    // its SwiGLU or GeGLU epilogue, a depth head) on x [rows][K] (f32, rounded to f16); y is
+    // [rows][M] for store epilogues, [rows][M/2] for the gated ones. With repeats > 0 the same
+    // launch is captured `repeats` more times in one graph (programmatic dependent launch on, as
+    // in the frame step), each result bit-compared on the device with the first; returns the
+    // number of differing 32-bit words
+    long long debug_gemm(const char * name, int rows, const float * x, float * y, int repeats);
+    // test hook: the grid-barrier poll limit of the persistent depth launches debug_depth makes
+    // (0 restores the default); frame-step graphs never use it
+    void set_debug_grid_spin(long long polls) { dbg_grid_spin_ = polls > 0 ? polls : 0; }
+    // the resident matrix a name refers to and the epilogue the frame step uses with it, or null
+    const QMat * resident_any(const char * name, int * epi) const;
     // one eager persistent depth launch for the current batch with its timeline recorded:
     // out = {n_phases, grid, slots, type[n_phases], timeline[n_phases][grid][slots]} (microseconds
     // from the first CTA's start, -1 where a slot was not reached); returns the doubles written
@@ -195,7 +207,10 @@ private:
     };
     const DpPlan * depth_plan(int R);
     void enqueue_depth(int R, const int * forced_dev, float * logits_dev, unsigned long long * trace = nullptr,
-                       const int * row_set = nullptr);
+                       const int * row_set = nullptr, long long grid_spin = 0);
+    // clears the device error word, then throws `what` with the code
+    [[noreturn]] void raise_device_error(int code, const std::string & what);
+    long long dbg_grid_spin_ = 0;  // grid-barrier poll limit of debug_depth launches (0: default)
     bool dp_supported(int R) const;
     int acquire_slot(int sid, int n_pages, bool register_sid = true);
     void release_slot(int slot);

@@ -1726,6 +1726,17 @@ __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ct
     if (threadIdx.x == 0) *ctr = k + 1;
 }
 
+// counts the 32-bit words of b that differ bitwise from a (repeat-launch determinism probe)
+__global__ void bits_diff_kernel(const uint32_t * a, const uint32_t * b, size_t n, int * count) {
+    pdl_trigger();
+    pdl_wait();
+    int local = 0;
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x)
+        local += a[i] != b[i];
+    for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+    if ((threadIdx.x & 31) == 0 && local) atomicAdd(count, local);
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------ launchers
@@ -2014,6 +2025,13 @@ void launch_advance(const int * row_slot, const int * row_active, const int * ro
 
 void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s) {
     launch_k(frames_commit_kernel, 1, 256, 0, s, cur, frames_all, n, step_ctr);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_bits_diff(const void * a, const void * b, size_t n_words, int * count, cudaStream_t s) {
+    const unsigned grid = (unsigned) std::max<size_t>(1, std::min<size_t>((n_words + 255) / 256, 148 * 4));
+    launch_k(bits_diff_kernel, grid, 256, 0, s, static_cast<const uint32_t *>(a), static_cast<const uint32_t *>(b),
+             n_words, count);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -117,6 +117,9 @@ void repack_umma_q4k(const uint8_t * raw_dev, int M, int K, uint8_t * blk, cudaS
 void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const GemvOut & out, int * err,
                       cudaStream_t s, bool pdl);
 bool pdl_scope();
+// runs the tcgen05 pipelines' bounded mbarrier wait (limit polls) on a barrier nothing arrives on,
+// in a one-thread kernel on the current device; returns the error code the wait recorded
+int probe_mbar_timeout(long long limit);
 void split_q8_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, cudaStream_t s);
 // Q4_K rows into 4-bit values (one per byte), sub-block scales and mins
 void split_q4k_rows(const uint8_t * raw_dev, int rows, int K, int8_t * qs, half * ds, half * ms, cudaStream_t s);
@@ -278,6 +281,8 @@ void launch_advance(const int * row_slot, const int * row_active, const int * ro
                     int * next_out, cudaStream_t s);
 // copies the current frame into frames_all[step] and advances the burst step counter
 void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s);
+// adds to *count the number of 32-bit words of b that differ bitwise from a (n_words each)
+void launch_bits_diff(const void * a, const void * b, size_t n_words, int * count, cudaStream_t s);
 
 // Philox4x32-10 uniform in [0, 1): top 24 bits of the first output word for (key, draw)
 __host__ __device__ inline uint32_t philox_word0(uint32_t key, uint32_t draw_lo, uint32_t draw_hi) {

@@ -308,8 +308,10 @@ int main(int argc, char ** argv) {
         s.te_hidden = 256; s.te_layers = 1; s.te_heads = 2; s.te_kv = 1; s.te_hd = 128; s.te_ffn = 512; s.te_window = 8;
     } else if (preset != "full") return usage();
     if (nc_override > 0) s.nc = nc_override;
-    if (s.qtype == G_Q4_K && (s.hidden % 256 || s.dd_hidden % 256 || s.bb_ffn % 256 || s.dd_ffn % 256 || s.te_hidden % 256)) {
-        std::fprintf(stderr, "Q4_K needs every row length to be a multiple of 256\n");
+    // the backbone and depth linears must be whole Q4_K super-blocks; text-encoder and vocoder
+    // tensors whose rows are not keep Q8_0 (lin() below)
+    if (s.qtype == G_Q4_K && (s.hidden % 256 || s.dd_hidden % 256 || s.bb_ffn % 256 || s.dd_ffn % 256)) {
+        std::fprintf(stderr, "Q4_K needs backbone and depth row lengths that are multiples of 256\n");
         return 2;
     }
 

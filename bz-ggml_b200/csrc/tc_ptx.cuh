@@ -25,17 +25,34 @@ __device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
 }
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(a), "r"(parity) : "memory");
+    return done != 0;
+}
+
 // bounded wait for the completion of the mbarrier phase with the given parity; returns false
-// (and records the failure) when the limit is reached instead of spinning forever
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int * err) {
+// when `limit` polls pass (recording error code 1) or as soon as another thread has recorded an
+// error, instead of spinning forever
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int * err, long long limit = kSpinLimit) {
     const uint32_t a = smem_u32(bar);
-    for (long long i = 0; i < kSpinLimit; i++) {
-        uint32_t done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
-        if (done) return true;
+    for (long long i = 0; i < limit; i++) {
+        if (mbar_try(a, parity)) return true;
+        if ((i & 1023) == 1023 && err && *reinterpret_cast<volatile int *>(err)) return false;
     }
-    if (err) atomicExch(err, 1);
+    if (err) atomicCAS(err, 0, 1);
+    return false;
+}
+
+// the wait a role uses after a failure to let the copies or MMAs it issued land before the
+// CTA releases its shared memory or tensor memory: it does not give up when an error is already
+// recorded, only after `limit` polls (recording error code 5)
+__device__ __forceinline__ bool mbar_drain(uint64_t * bar, uint32_t parity, int * err, long long limit = kSpinLimit) {
+    const uint32_t a = smem_u32(bar);
+    for (long long i = 0; i < limit; i++)
+        if (mbar_try(a, parity)) return true;
+    if (err) atomicCAS(err, 0, 5);
     return false;
 }
 

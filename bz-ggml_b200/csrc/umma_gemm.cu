@@ -191,19 +191,24 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     if (p.splits > 1) cluster_arrive_relaxed();
     bool ok = true;
 
+    // A role stops at its first failed (bounded) wait; then the loaders wait for the copies they
+    // issued and the MMA thread for its MMAs, so that no copy lands in shared memory and no MMA
+    // touches tensor memory after the CTA has released them.
     const int cb = umat_chunk_bytes(p.q4);
     if (warp < 8) {
         // producer: weight row r, Q8_0 block hb of every chunk
         const int r = tid & (kTileM - 1), hb = tid >> 7;
-        for (int s = 0; s < nst; s++) {
+        for (int s = 0; s < nst && ok; s++) {
             const int rs = s % kRawStages, ab = s % kAStages, nsub = min(kSC, nch - s * kSC);
-            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (s / kRawStages) & 1u, p.err);
+            ok = mbar_wait(&raw_full[rs], (uint32_t) (s / kRawStages) & 1u, p.err);
+            if (!ok) break;
             RawPiece pc[kSC];
 #pragma unroll
             for (int j = 0; j < kSC; j++)
                 if (j < nsub) pc[j] = read_piece(sR + rs * kSC * kRawBytes + j * cb, p.q4, r, hb);
             mbar_arrive(&raw_empty[rs]);
-            if (s >= kAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((s / kAStages) - 1) & 1u, p.err);
+            if (s >= kAStages) ok = mbar_wait(&a_empty[ab], (uint32_t) ((s / kAStages) - 1) & 1u, p.err);
+            if (!ok) break;
 #pragma unroll
             for (int j = 0; j < kSC; j++)
                 if (j < nsub) write_piece(pc[j], p.q4, r, hb, sA + (ab * kSC + j) * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
@@ -212,10 +217,11 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
         }
     } else if (warp == 8) {
         if (lane == 0) {
-            for (int s = 0; s < nst; s++) {
+            for (int s = 0; s < nst && ok; s++) {
                 const int ab = s % kAStages, bb = s % kBStages, nsub = min(kSC, nch - s * kSC);
-                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (s / kBStages) & 1u, p.err);
+                ok = mbar_wait(&b_full[bb], (uint32_t) (s / kBStages) & 1u, p.err);
                 if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (s / kAStages) & 1u, p.err);
+                if (!ok) break;
                 tc_fence_after();
 #pragma unroll
                 for (int j = 0; j < kSC; j++) {
@@ -230,29 +236,42 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
                 umma_commit(&b_empty[bb]);
             }
             umma_commit(&done_bar);  // arrives once every MMA above has completed
+            // tensor memory is released after the block barrier below: the MMAs must be done first
+            if (!mbar_drain(&done_bar, 0u, p.err)) ok = false;
         }
     } else if (warp == 9) {
         if (lane == 0) {
             // weights and scales are constant: stream them before the predecessor finishes;
             // one bulk copy per stage: a tile's chunks are contiguous in the repacked layout
             const uint8_t * base = p.blk + (size_t) (mt * p.KC + c_beg) * cb;
+            int issued = 0;
             for (int s = 0; s < nst; s++) {
                 const int rs = s % kRawStages, nsub = min(kSC, nch - s * kSC);
-                if (s >= kRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((s / kRawStages) - 1) & 1u, p.err);
+                if (s >= kRawStages) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((s / kRawStages) - 1) & 1u, p.err);
+                if (!ok) break;
                 mbar_expect_tx(&raw_full[rs], (uint32_t) (nsub * cb));
                 bulk_g2s(sR + rs * kSC * kRawBytes, base + (size_t) s * kSC * cb, (uint32_t) (nsub * cb), &raw_full[rs]);
+                issued = s + 1;
             }
+            // the copies still in flight land before the CTA can exit
+            for (int s = max(0, issued - kRawStages); s < issued; s++)
+                mbar_drain(&raw_full[s % kRawStages], (uint32_t) (s / kRawStages) & 1u, p.err);
         }
     } else {
         if (lane == 0) {
             pdl_wait();  // activations come from the previous kernel
+            int issued = 0;
             for (int s = 0; s < nst; s++) {
                 const int bb = s % kBStages, nsub = min(kSC, nch - s * kSC);
-                if (s >= kBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((s / kBStages) - 1) & 1u, p.err);
+                if (s >= kBStages) ok = mbar_wait(&b_empty[bb], (uint32_t) ((s / kBStages) - 1) & 1u, p.err);
+                if (!ok) break;
                 mbar_expect_tx(&b_full[bb], (uint32_t) (nsub * kBBytes));
                 for (int j = 0; j < nsub; j++)
                     tma_2d(sB + (bb * kSC + j) * kBBytes, &xmap, (c_beg + s * kSC + j) * kChunkK, row0, &b_full[bb]);
+                issued = s + 1;
             }
+            for (int s = max(0, issued - kBStages); s < issued; s++)
+                mbar_drain(&b_full[s % kBStages], (uint32_t) (s / kBStages) & 1u, p.err);
         }
     }
     pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed
@@ -260,7 +279,7 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
     // accumulator rows 32w..32w+31 (warps 0-3), all N columns
     float v[N];
     if (warp < 4) {
-        if (ok) ok = mbar_wait(&done_bar, 0u, p.err);
+        if (!mbar_wait(&done_bar, 0u, p.err)) ok = false;
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t) (32 * warp) << 16);
 #pragma unroll
@@ -442,14 +461,18 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
     pdl_trigger();
     bool ok = true;
 
+    // failure handling as in the decode kernel: stop at the first failed wait, then let the
+    // issued copies and MMAs land before shared and tensor memory are released
     if (warp < 8) {
         const int r = tid & (kTileM - 1), hb = tid >> 7;
         for (int c = 0; c < nch; c++) {
             const int rs = c % kPRawStages, ab = c % kPAStages;
-            if (ok) ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kPRawStages) & 1u, p.err);
+            ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kPRawStages) & 1u, p.err);
+            if (!ok) break;
             const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
             mbar_arrive(&raw_empty[rs]);
-            if (c >= kPAStages && ok) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kPAStages) - 1) & 1u, p.err);
+            if (c >= kPAStages) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kPAStages) - 1) & 1u, p.err);
+            if (!ok) break;
             write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
             fence_proxy_async();
             mbar_arrive(&a_full[ab]);
@@ -458,8 +481,9 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
         if (lane == 0) {
             for (int c = 0; c < nch; c++) {
                 const int ab = c % kPAStages, bb = c % kPBStages;
-                if (ok) ok = mbar_wait(&b_full[bb], (uint32_t) (c / kPBStages) & 1u, p.err);
+                ok = mbar_wait(&b_full[bb], (uint32_t) (c / kPBStages) & 1u, p.err);
                 if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kPAStages) & 1u, p.err);
+                if (!ok) break;
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kPBBytes);
 #pragma unroll
@@ -469,33 +493,44 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
                 umma_commit(&b_empty[bb]);
             }
             umma_commit(&done_bar);
+            if (!mbar_drain(&done_bar, 0u, p.err)) ok = false;
         }
     } else if (warp == 9) {
         if (lane == 0) {
             const int cb = umat_chunk_bytes(p.q4);
             const uint8_t * base = p.blk + (size_t) mt * p.KC * cb;
+            int issued = 0;
             for (int c = 0; c < nch; c++) {
                 const int rs = c % kPRawStages;
-                if (c >= kPRawStages && ok) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kPRawStages) - 1) & 1u, p.err);
+                if (c >= kPRawStages) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kPRawStages) - 1) & 1u, p.err);
+                if (!ok) break;
                 mbar_expect_tx(&raw_full[rs], (uint32_t) cb);
                 bulk_g2s(sR + rs * kRawBytes, base + (size_t) c * cb, (uint32_t) cb, &raw_full[rs]);
+                issued = c + 1;
             }
+            for (int c = max(0, issued - kPRawStages); c < issued; c++)
+                mbar_drain(&raw_full[c % kPRawStages], (uint32_t) (c / kPRawStages) & 1u, p.err);
         }
     } else {
         if (lane == 0) {
             pdl_wait();  // activations come from the previous kernel
+            int issued = 0;
             for (int c = 0; c < nch; c++) {
                 const int bb = c % kPBStages;
-                if (c >= kPBStages && ok) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kPBStages) - 1) & 1u, p.err);
+                if (c >= kPBStages) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kPBStages) - 1) & 1u, p.err);
+                if (!ok) break;
                 mbar_expect_tx(&b_full[bb], kPBBytes);
                 tma_2d(sB + bb * kPBBytes, &xmap, c * kChunkK, row0, &b_full[bb]);
+                issued = c + 1;
             }
+            for (int c = max(0, issued - kPBStages); c < issued; c++)
+                mbar_drain(&b_full[c % kPBStages], (uint32_t) (c / kPBStages) & 1u, p.err);
         }
     }
     pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed
 
     if (warp < 8) {
-        if (ok) ok = mbar_wait(&done_bar, 0u, p.err);
+        if (!mbar_wait(&done_bar, 0u, p.err)) ok = false;
         tc_fence_after();
         const int q = warp & 3, h = warp >> 2;
         const uint32_t taddr = tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (128 * h);
@@ -713,6 +748,36 @@ CUtensorMap make_x_group_map(const half * x, int K, int ldx, int rows, int box_r
     return m;
 }
 
+
+namespace {
+// one thread waits, with the GEMM pipelines' bounded wait, on a barrier that nothing arrives on
+__global__ void mbar_timeout_probe_kernel(int * err, long long limit) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && mbar_wait(&bar, 0u, err, limit)) atomicExch(err, -1);  // must not complete
+}
+}  // namespace
+
+int probe_mbar_timeout(long long limit) {
+    int * err = nullptr;
+    UCHECK(cudaMalloc(&err, sizeof(int)));
+    int code = 0;
+    try {
+        UCHECK(cudaMemset(err, 0, sizeof(int)));
+        mbar_timeout_probe_kernel<<<1, 32>>>(err, limit);
+        UCHECK(cudaGetLastError());
+        UCHECK(cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost));
+    } catch (...) {
+        cudaFree(err);
+        throw;
+    }
+    cudaFree(err);
+    return code;
+}
 
 void init_umma_attributes() {
     for (const void * f : { (const void *) umma_prefill_kernel<EPI_STORE>, (const void *) umma_prefill_kernel<EPI_RESID>,

@@ -54,6 +54,31 @@ BREEZE_API int bzb_generator_debug_depth(breeze_generator * gen, int n, const fl
 BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int sub, int rows,
                                         const float * x, float * y);
 
+/* parity probe of a matrix exactly as the frame step holds it: `name` is a resident matrix --
+   {bb,dd,te}.blk.N.{attn_qkv, attn_output, ffn_gate_up, ffn_down} (attn_qkv: q, k and v rows
+   fused; ffn_gate_up: gate and up interleaved, run with the step's SwiGLU or GeGLU epilogue),
+   bb.lm_head.weight, dd.in_proj.weight, te.proj.weight or dd.head.J (depth head J) -- on x
+   [rows][K] (f32, rounded to f16 as the step's activations are). y receives [rows][M], or
+   [rows][M/2] of gated outputs (f16 values widened to f32). With repeats > 0 the launch is
+   captured `repeats` more times in one CUDA graph under programmatic dependent launch, and each
+   result is compared bit for bit on the device with the first. Returns the number of 32-bit
+   words that differed (0 for a deterministic kernel), or -1 with breeze_last_error(). */
+BREEZE_API long long bzb_generator_debug_gemm(breeze_generator * gen, const char * name, int rows, const float * x,
+                                              float * y, int repeats);
+
+/* Tests of the bounded device waits (no reference counterpart). Every spin-wait in the kernels
+   gives up after a poll limit, records an error code, lets the copies and MMAs it issued land,
+   frees its tensor memory and returns; the host then reports the code and clears it.
+   bzb_generator_debug_grid_spin sets the poll limit of the persistent depth decoder's grid
+   barriers for the launches bzb_generator_debug_depth makes (0 restores the default; frame-step
+   graphs never use it): a limit of a few polls makes a barrier run out, and that call then returns
+   -1 with breeze_last_error() naming the timeout while the generator stays usable.
+   bzb_debug_mbar_timeout runs the tcgen05 pipelines' mbarrier wait with `polls` polls on a
+   barrier that nothing arrives on, on `device`, and returns the error code it recorded (1 for a
+   wait that gave up), or -1 with breeze_last_error(). */
+BREEZE_API int bzb_generator_debug_grid_spin(breeze_generator * gen, long long polls);
+BREEZE_API int bzb_debug_mbar_timeout(int device, long long polls);
+
 /* average microseconds of back-to-back launches of one dequant-GEMM of a named Q8_0 tensor on
    `rows` activation rows (epilogue 0 store, 1 residual add, 2 SwiGLU, 3 GeGLU), or -1 */
 BREEZE_API double bzb_generator_bench_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, int iters,

@@ -895,6 +895,8 @@ class Generator:
         self.m = model
         self.sessions = {}
         self.q4 = None
+        # per session: (penalised logits, Philox key, draw index) of its latest cb0 draw
+        self.last_cb0_logits = {}
 
     def load_q4_depth(self, path: str):
         self.q4 = self.m.with_depth_override(path)
@@ -956,7 +958,10 @@ class Generator:
             sess.st_u = BBState.new(self.m, embeds_u.shape[0] + est + 8)
             sess.last_hidden_u, lu = self.m.backbone_run(sess.st_u, embeds_u)
             alloc += embeds_u.shape[0] + est + 8
-        cb0 = self._sample_cb0(sess, combine_logits(lg, lu, sess.cfg))
+        first = combine_logits(lg, lu, sess.cfg)
+        self.last_cb0_logits[sid] = (apply_penalties(first, sess.sp.rep, sess.hist, self.m.cfg.cb_size, self.m.cfg.vs),
+                                     sess.rng.key, sess.rng.draw)
+        cb0 = self._sample_cb0(sess, first)
         sess.hist[cb0] = sess.hist.get(cb0, 0) + 1
         sess.last_cb0 = cb0
         self.sessions[sid] = sess

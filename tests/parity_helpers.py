@@ -74,3 +74,21 @@ def snr_db(ref, got):
     ref = np.asarray(ref, np.float64)
     err = np.asarray(got, np.float64) - ref
     return 10.0 * np.log10((ref @ ref + 1e-30) / (err @ err + 1e-30))
+
+
+def kernel_weights_q4k(raw: np.ndarray, rows: int, K: int) -> np.ndarray:
+    """The f16 weights the kernel feeds the tensor cores: per sub-block a = d * scale and
+    b = dmin * min (exact), w = a q - b by one f32 fused multiply-add, then rounded to f16."""
+    blocks = raw[: rows * K // 256 * 144].reshape(-1, 144)
+    d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dmin = blocks[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    sc, mn = bo.q4k_scale_min(blocks[:, 4:16])
+    a = d[:, None].astype(np.float64) * sc.astype(np.float64)
+    b = dmin[:, None].astype(np.float64) * mn.astype(np.float64)
+    qs = blocks[:, 16:]
+    q = np.empty((blocks.shape[0], 8, 32), np.float64)
+    for s in range(8):
+        byte = qs[:, 32 * (s // 2): 32 * (s // 2) + 32]
+        q[:, s] = (byte >> (4 * (s % 2))) & 0xF
+    w = (a[:, :, None] * q - b[:, :, None]).astype(np.float32).astype(np.float16)
+    return w.reshape(rows, K).astype(np.float64)

@@ -125,3 +125,48 @@ def test_cfg_burst_retires_both_branches(pkg, gen, tiny_oracle):
         assert list(nxt) == [-1, -1]
         assert gen.session_free(61) == 0 and gen.session_free(62) == 0
     assert gen.active_session_count() == 0
+
+
+def test_sessions_step_round_matches_oracle(pkg, gen, tiny_oracle):
+    """breeze_generator_sessions_step_round (src/c_api.cpp:584-599): session_step for each listed
+    session in order with seed + i; the return value counts the sessions still going; an unknown
+    or finished session gets -1 and its frame row is not written."""
+    cfg = tiny_oracle.cfg
+    ref = bo.Generator(tiny_oracle)
+    scales = {71: 1.0, 72: 2.0, 73: 1.0}
+    budgets = {71: 6, 72: 6, 73: 2}
+    try:
+        for sid, s in scales.items():
+            text = pkg.ids_to_text([sid * 5, 3000 + sid, 40000 + sid]) + " round"
+            cb0, alloc = gen.session_create_ext(sid, text, seed=sid, max_new_tokens=budgets[sid], cfg_scale=s)
+            rcb0, ralloc = ref.session_create(sid, text, seed=sid, max_new_tokens=budgets[sid], cfg_scale=s)
+            assert (cb0, alloc) == (rcb0, ralloc)
+        ids = [71, 4242, 72, 73]
+        flips = 0
+        for rnd in range(3):
+            seed = 500 + 10 * rnd
+            live = {sid: ref.sessions[sid].active for sid in scales}
+            nxt, frames = gen.sessions_step_round(ids, seed)
+            frames = np.asarray(frames)
+            going = 0
+            for i, sid in enumerate(ids):
+                if sid not in scales or not live[sid]:
+                    assert nxt[i] == -1 and (frames[i] == 0).all(), (rnd, sid)
+                    continue
+                dl = {}
+                rf, rn = ref.step_batched([sid], forced_depth=frames[i][None, 1:cfg.nc], depth_logits_out=dl,
+                                          sampled_depth=True, depth_seeds=[seed + i])
+                assert frames[i][0] == rf[0][0], (rnd, sid)
+                flips += _check(ref, cfg.nc, sid, frames[i][1:cfg.nc], dl, scales[sid], (rnd, sid))
+                if rn[0] >= 0 and nxt[i] >= 0:
+                    flips += reconcile_cb0(ref, sid, int(nxt[i]), int(rn[0]), scales[sid], (rnd, sid))
+                else:
+                    assert nxt[i] == rn[0] == -1, (rnd, sid, nxt[i], rn[0])
+                going += int(nxt[i] >= 0)
+            assert gen.last_round_completed == going
+        # session 73's budget of 2 ran out in the second round
+        assert not ref.sessions[73].active
+        assert flips <= flip_budget(3 * 3 * cfg.nc), flips
+    finally:
+        for sid in scales:
+            gen.session_free(sid)

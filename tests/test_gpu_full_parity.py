@@ -1,0 +1,239 @@
+"""Parity at the benchmarked configuration (needs a B200).
+
+The model is the full-size synthetic Breeze-TTS-2 the benchmark runs: a 16-layer d 2048
+backbone (32 query / 8 kv heads of 64, FFN 8192), a 4-layer d 1024 depth decoder over 32
+codebooks, the 26-layer text encoder and the full codec decoder, with Q8_0 and with Q4_K
+backbone and depth weights. The checks run the kernels the frame step runs, at its shapes:
+
+- every kind of resident matrix (fused q/k/v, interleaved gate/up with its SwiGLU epilogue,
+  the K = 8192 down projection, the LM head, depth layers and heads) on 1, 16, 64 and 100
+  activation rows, and the 256-row prefill shape: within 1e-5 (relative to sum |x| |w|) of the
+  f16-operand product the kernel computes, and within the logit tolerance of the oracle's f32;
+- the same launches repeated hundreds of times inside a CUDA graph under programmatic dependent
+  launch, each result compared bit for bit with the first (the kernels are deterministic);
+- the persistent depth decoder on 64 rows at nc 32 under teacher forcing: logits within max-abs
+  2e-2 and cosine 0.9995 of the oracle at every sub-step, codes equal to the oracle's argmax
+  except at counted near-ties;
+- sessions with prompts at the ends of the benchmark's ranges (16 and 512 text tokens, 0 and
+  125 voice frames) prefilled and stepped teacher-forced: first cb0 and allocation equal, hidden
+  states after prefill and after every step within the same tolerance, cb0 draws equal or
+  reachable by the same Philox uniform within the tolerance.
+
+Near-ties: f16 activations against the oracle's f32 move a logit by up to a few 1e-3 here, so
+an argmax may differ where the oracle's own top two are that close. A differing code is accepted
+only when the oracle's logit for it is within TIE_FULL of the oracle's maximum, and the number
+of such codes is bounded.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import breeze_oracle as bo
+from parity_helpers import LOGIT_ATOL, flip_budget, kernel_weights_q4k, reconcile_cb0
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9995
+TIE_FULL = 5e-3      # largest oracle top-1 minus engine-pick logit gap accepted as a near-tie
+REPEATS = 500        # captured re-launches per GEMM shape in the determinism check
+
+
+def cosine(a, b):
+    a = a.reshape(-1).astype(np.float64)
+    b = b.reshape(-1).astype(np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30))
+
+
+def model_dir():
+    d = os.environ.get("BZB_MODEL_DIR", "/tmp/bzb_models")
+    os.makedirs(d, exist_ok=True)
+    return d
+
+
+@pytest.fixture(scope="module", params=["q8_0", "q4_k"])
+def full(request, pkg):
+    """(generator, oracle model) for the full-size model with the given backbone/depth weights
+    (the same file the benchmark writes)."""
+    quant = request.param
+    path = os.path.join(model_dir(), f"breeze_full_nc32_{quant}_seed0_eosoff.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        pkg.synth_model(tmp, preset="full", nc=32, quant=quant, seed=0, eos_off=True)
+        os.replace(tmp, path)
+    gen = pkg.GeneratorHandle(path, 0)
+    m = bo.Model(path)
+    yield gen, m, quant
+    gen.close()
+
+
+def kernel_w16(m, name):
+    """The f16 weights [M][K] the kernel multiplies for a tensor (Q8_0: f16(q d); Q4_K: f16(a q - b))."""
+    t = m.g.tensors[name]
+    w = m.w(name)
+    w2 = w.reshape(-1, w.shape[-1])
+    if t.type == bo.Q4_K:
+        return kernel_weights_q4k(t.raw, w2.shape[0], w2.shape[1]), w2
+    return w2.astype(np.float16).astype(np.float64), w2
+
+
+def resident(m, name):
+    """(f16 kernel weights, f32 oracle weights, gated) for a resident matrix name; gated
+    matrices return (gate, up) pairs."""
+    if name.startswith("dd.head."):
+        j = int(name.split(".")[2])
+        w16, w = kernel_w16(m, "dd.codebooks_head.weight")
+        vs = m.cfg.vs
+        return w16[j * vs:(j + 1) * vs], w[j * vs:(j + 1) * vs], False
+    if name.endswith(".attn_qkv"):
+        parts = [kernel_w16(m, name.replace("attn_qkv", p + ".weight")) for p in ("attn_q", "attn_k", "attn_v")]
+        return np.concatenate([p[0] for p in parts]), np.concatenate([p[1] for p in parts]), False
+    if name.endswith(".ffn_gate_up"):
+        g = kernel_w16(m, name.replace("ffn_gate_up", "ffn_gate.weight"))
+        u = kernel_w16(m, name.replace("ffn_gate_up", "ffn_up.weight"))
+        return (g[0], u[0]), (g[1], u[1]), True
+    w16, w = kernel_w16(m, name)
+    return w16, w, False
+
+
+GEMM_NAMES = ["bb.blk.3.attn_qkv", "bb.blk.3.attn_output", "bb.blk.5.ffn_gate_up", "bb.blk.5.ffn_down",
+              "bb.lm_head.weight", "dd.blk.1.attn_qkv", "dd.blk.1.ffn_gate_up", "dd.blk.2.ffn_down", "dd.head.30",
+              "dd.in_proj.weight"]
+
+
+@pytest.mark.parametrize("name", GEMM_NAMES)
+@pytest.mark.parametrize("rows,prefill", [(1, "auto"), (16, "auto"), (64, "auto"), (100, "auto"), (300, "1")])
+def test_full_gemm_matches_f16_reference(full, name, rows, prefill, monkeypatch):
+    gen, m, quant = full
+    if prefill != "auto":
+        monkeypatch.setenv("BZB_PREFILL_GEMM", prefill)
+    w16, w, gated = resident(m, name)
+    K = (w16[0] if gated else w16).shape[1]
+    out_dim = (w16[0] if gated else w16).shape[0]
+    x = np.random.default_rng(rows * 31 + len(name)).standard_normal((rows, K)).astype(np.float32)
+    y, _ = gen.debug_gemm(name, x, out_dim)
+    x16 = x.astype(np.float16).astype(np.float64)
+    if gated:
+        g16, u16 = x16 @ w16[0].T, x16 @ w16[1].T
+        ref16 = g16 / (1.0 + np.exp(-g16)) * u16
+        # f16 output: half an ulp of the value plus the f32-accumulation error of g and u
+        tol = np.abs(ref16) * 2.0 ** -10 + 1e-5 * (np.abs(x16) @ np.abs(w16[0]).T) * (1.0 + np.abs(u16))
+        assert np.all(np.abs(y - ref16) <= tol + 1e-6), np.max(np.abs(y - ref16) - tol)
+        g, u = bo.linear(x, w[0]), bo.linear(x, w[1])
+        ref = g / (1.0 + np.exp(-g)) * u
+    else:
+        ref16 = x16 @ w16.T
+        scale = np.abs(x16) @ np.abs(w16).T + 1e-6
+        assert np.max(np.abs(y - ref16) / scale) < 1e-5
+        ref = bo.linear(x, w)
+    assert np.abs(y - ref).max() < LOGIT_ATOL, np.abs(y - ref).max()
+    assert cosine(y, ref) > COS_MIN
+
+
+@pytest.mark.parametrize("name,rows,prefill", [
+    ("bb.blk.5.ffn_gate_up", 64, "auto"), ("bb.blk.5.ffn_down", 64, "auto"), ("bb.blk.3.attn_qkv", 64, "auto"),
+    ("bb.blk.3.attn_output", 64, "auto"), ("bb.lm_head.weight", 64, "auto"), ("bb.blk.5.ffn_gate_up", 100, "auto"),
+    ("bb.blk.5.ffn_down", 16, "auto"), ("bb.blk.5.ffn_down", 1, "auto"), ("dd.blk.1.ffn_gate_up", 64, "auto"),
+    ("dd.head.7", 64, "auto"), ("bb.blk.5.ffn_gate_up", 300, "1"), ("bb.blk.5.ffn_down", 300, "1")])
+def test_full_gemm_repeats_bit_identical(full, name, rows, prefill, monkeypatch):
+    """Hundreds of captured launches of one shape (two 64-wide chunks per pipeline stage, the
+    cluster split-K reduction, partial activation tiles) give the first launch's bits every time."""
+    gen, m, quant = full
+    if prefill != "auto":
+        monkeypatch.setenv("BZB_PREFILL_GEMM", prefill)
+    w16, _, gated = resident(m, name)
+    K = (w16[0] if gated else w16).shape[1]
+    out_dim = (w16[0] if gated else w16).shape[0]
+    x = np.random.default_rng(rows).standard_normal((rows, K)).astype(np.float32)
+    _, diff = gen.debug_gemm(name, x, out_dim, repeats=REPEATS)
+    assert diff == 0, f"{diff} words differed over {REPEATS} launches"
+
+
+def check_depth_logits(codes, logits, ref_logits, tag):
+    """Per (row, sub-step): logits within tolerance; a code differing from the oracle's argmax
+    must be a near-tie. Returns the number of near-tie codes."""
+    ties = 0
+    worst = 0.0
+    n, steps, _ = logits.shape
+    for i in range(n):
+        for j in range(steps):
+            a, b = logits[i, j], ref_logits[i, j]
+            err = float(np.abs(a - b).max())
+            worst = max(worst, err)
+            assert err < LOGIT_ATOL, (tag, i, j, err)
+            assert cosine(a, b) > COS_MIN, (tag, i, j)
+            c = int(codes[i, j])
+            if c != int(np.argmax(b)):
+                gap = float(b.max() - b[c])
+                assert gap < TIE_FULL, (tag, i, j, c, int(np.argmax(b)), gap)
+                ties += 1
+    return ties, worst
+
+
+def test_full_depth_decoder_64_rows_teacher_forced(full):
+    """The persistent depth decoder as the 64-session frame step runs it (nc 32, d 1024)."""
+    gen, m, quant = full
+    cfg = m.cfg
+    rng = np.random.default_rng(64)
+    n = 64
+    hidden = rng.standard_normal((n, cfg.hidden)).astype(np.float32)
+    cb0 = rng.integers(0, 2048, n)
+    codes, logits = gen.debug_depth(hidden, cb0, cfg.vs)
+    _, ref_logits = m.depth_logits_chain(hidden, cb0, forced=codes)
+    ties, worst = check_depth_logits(codes, logits, ref_logits, quant)
+    assert ties <= flip_budget(n * (cfg.nc - 1)) // 3, (ties, worst)
+    # the same inputs again: the same codes and bit-identical logits
+    codes2, logits2 = gen.debug_depth(hidden, cb0, cfg.vs, forced=codes)
+    assert np.array_equal(codes2, codes) and np.array_equal(logits2, logits)
+
+
+# prompts at the ends of the benchmark workload's ranges: text tokens U[16,512], voice 0-125 frames
+SESSIONS = {"q8_0": [(512, 125), (16, 0), (137, 63)], "q4_k": [(300, 63), (40, 0)]}
+
+
+def test_full_sessions_prefill_and_steps_match_oracle(pkg, full):
+    gen, m, quant = full
+    cfg = m.cfg
+    ref = bo.Generator(m)
+    rng = np.random.default_rng(512)
+    ids = []
+    try:
+        for k, (n_text, n_voice) in enumerate(SESSIONS[quant]):
+            sid = 700 + k
+            text = pkg.ids_to_text(rng.integers(264, 128000, n_text))
+            kw = dict(seed=sid, max_new_tokens=64)
+            if n_voice:
+                kw.update(ref_text=pkg.ids_to_text(rng.integers(264, 128000, 8)),
+                          ref_codes=rng.integers(0, 2048, (n_voice, cfg.nc)).astype(np.int32))
+            cb0, alloc = gen.session_create_ext(sid, text, ref_frames=n_voice, **kw)
+            rcb0, ralloc = ref.session_create(sid, text, **kw)
+            ids.append(sid)
+            assert alloc == ralloc
+            h = gen.debug_hidden(sid, cfg.hidden)
+            rh = ref.sessions[sid].last_hidden
+            assert np.abs(h - rh).max() < LOGIT_ATOL and cosine(h, rh) > COS_MIN, (sid, np.abs(h - rh).max())
+            reconcile_cb0(ref, sid, cb0, rcb0, 1.0, "create")
+        ties = flips = 0
+        for step in range(2):
+            seeds = [13 * step + s for s in ids]
+            n_exec, frames, nxt = gen.step_frames(ids, 1, seeds)
+            assert n_exec == 1
+            dl = {}
+            rf, rn = ref.step_batched(ids, seeds=seeds, forced_depth=frames[0][:, 1:], depth_logits_out=dl)
+            assert np.array_equal(frames[0][:, 0], rf[:, 0])
+            for i, sid in enumerate(ids):
+                for j in range(cfg.nc - 1):
+                    lg = dl[sid][j]
+                    c = int(frames[0][i, j + 1])
+                    if c != int(np.argmax(lg)):
+                        assert float(lg.max() - lg[c]) < TIE_FULL, (step, sid, j, float(lg.max() - lg[c]))
+                        ties += 1
+                flips += reconcile_cb0(ref, sid, int(nxt[i]), int(rn[i]), 1.0, step)
+                h = gen.debug_hidden(sid, cfg.hidden)
+                rh = ref.sessions[sid].last_hidden
+                assert np.abs(h - rh).max() < LOGIT_ATOL and cosine(h, rh) > COS_MIN, (step, sid, np.abs(h - rh).max())
+        assert ties <= flip_budget(2 * len(ids) * (cfg.nc - 1)) // 3
+        assert flips <= flip_budget(2 * len(ids))
+    finally:
+        for sid in ids:
+            gen.session_free(sid)

@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 
 import breeze_oracle as bo
-from parity_helpers import LOGIT_ATOL, TIE_GAP, check_depth, flip_budget, reconcile_cb0, snr_db
+from parity_helpers import LOGIT_ATOL, TIE_GAP, check_depth, flip_budget, kernel_weights_q4k, reconcile_cb0, snr_db
 
 pytestmark = pytest.mark.gpu
 
@@ -44,24 +44,6 @@ def q4_gen(pkg, q4_model):
     g = pkg.GeneratorHandle(q4_model, 0)
     yield g
     g.close()
-
-
-def kernel_weights_q4k(raw: np.ndarray, rows: int, K: int) -> np.ndarray:
-    """The f16 weights the kernel feeds the tensor cores: per sub-block a = d * scale and
-    b = dmin * min (exact), w = a q - b by one f32 fused multiply-add, then rounded to f16."""
-    blocks = raw[: rows * K // 256 * 144].reshape(-1, 144)
-    d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
-    dmin = blocks[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
-    sc, mn = bo.q4k_scale_min(blocks[:, 4:16])
-    a = d[:, None].astype(np.float64) * sc.astype(np.float64)
-    b = dmin[:, None].astype(np.float64) * mn.astype(np.float64)
-    qs = blocks[:, 16:]
-    q = np.empty((blocks.shape[0], 8, 32), np.float64)
-    for s in range(8):
-        byte = qs[:, 32 * (s // 2): 32 * (s // 2) + 32]
-        q[:, s] = (byte >> (4 * (s % 2))) & 0xF
-    w = (a[:, :, None] * q - b[:, :, None]).astype(np.float32).astype(np.float16)
-    return w.reshape(rows, K).astype(np.float64)
 
 
 @pytest.mark.parametrize("tensor,sub", [("bb.blk.0.attn_q.weight", -1), ("bb.blk.1.ffn_down.weight", -1),
