@@ -105,7 +105,7 @@ SIGNATURES = {
     "bzb_generator_debug_gemv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                 _c_float_p, _c_float_p]),
     "bzb_generator_debug_gemm": (ctypes.c_longlong, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, _c_float_p,
-                                                     _c_float_p, ctypes.c_int]),
+                                                     _c_float_p, ctypes.c_int, ctypes.c_int, _c_int_p, ctypes.c_int]),
     "bzb_generator_debug_grid_spin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
     "bzb_debug_mbar_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong]),
     "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
@@ -445,14 +445,20 @@ class GeneratorHandle:
     def session_set_q4(self, session_id: int, use_q4: bool = True) -> bool:
         return self.lib.lib.breeze_generator_session_set_q4(self.handle, session_id, 1 if use_q4 else 0) == 0
 
-    def debug_gemm(self, name: str, x: np.ndarray, out_dim: int, repeats: int = 0) -> Tuple[np.ndarray, int]:
+    def debug_gemm(self, name: str, x: np.ndarray, out_dim: int, repeats: int = 0, pdl: bool = True,
+                   where_cap: int = 0):
         """One launch of a resident (step-layout) matrix on x [rows][K]: returns (y [rows][out_dim],
-        32-bit words that differed over `repeats` captured re-launches)."""
+        32-bit words that differed over `repeats` captured re-launches); with where_cap > 0 also the
+        first differences as an array of (word index, repeat index) rows."""
         xx = np.ascontiguousarray(x, np.float32)
         y = np.zeros((xx.shape[0], out_dim), np.float32)
-        n = self.lib.lib.bzb_generator_debug_gemm(self.handle, name.encode(), xx.shape[0], _fp(xx), _fp(y), repeats)
+        where = np.zeros((max(where_cap, 1), 2), np.int32)
+        n = self.lib.lib.bzb_generator_debug_gemm(self.handle, name.encode(), xx.shape[0], _fp(xx), _fp(y), repeats,
+                                                  0 if pdl else 1, _ip(where) if where_cap else None, where_cap)
         if n < 0:
             raise RuntimeError(self.lib.last_error())
+        if where_cap:
+            return y, int(n), where[:min(int(n), where_cap)]
         return y, int(n)
 
     def set_debug_grid_spin(self, polls: int) -> None:

@@ -729,13 +729,13 @@ int bzb_debug_mbar_timeout(int device, long long polls) {
 }
 
 long long bzb_generator_debug_gemm(breeze_generator * gen, const char * name, int rows, const float * x, float * y,
-                                   int repeats) {
-    if (!gen || !name || rows <= 0 || !x || !y || repeats < 0) {
+                                   int repeats, int flags, int * out_where, int where_cap) {
+    if (!gen || !name || rows <= 0 || !x || !y || repeats < 0 || where_cap < 0) {
         set_error("debug_gemm: bad arguments");
         return -1;
     }
     try {
-        return gen->eng->debug_gemm(name, rows, x, y, repeats);
+        return gen->eng->debug_gemm(name, rows, x, y, repeats, flags, out_where, where_cap);
     } catch (const std::exception & e) {
         set_error(e.what());
         return -1;

@@ -763,6 +763,9 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                         const int rs = rg % kRawGroups;
                         if (rg >= kRawGroups) ok = dwait(&raw_empty[rs], ((rg / kRawGroups) - 1) & 1u, err, kBackoff);
                         if (!ok) break;
+                        // the producers read this slot with generic loads: order those reads before
+                        // the bulk copy's async-proxy writes into it
+                        fence_proxy_async();
                         if (p.trace && g0 == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 7] = gtimer();
                         mbar_expect_tx(&raw_full[rs], (uint32_t) (gs * cb));
                         bulk_g2s(sR + rs * kRawGroupBytes, base + (size_t) g0 * cb, (uint32_t) (gs * cb), &raw_full[rs]);

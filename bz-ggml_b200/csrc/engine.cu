@@ -1834,7 +1834,8 @@ const QMat * Engine::resident_any(const char * name, int * epi) const {
     return nullptr;
 }
 
-long long Engine::debug_gemm(const char * name, int rows, const float * x, float * y, int repeats) {
+long long Engine::debug_gemm(const char * name, int rows, const float * x, float * y, int repeats, int flags,
+                             int * where, int cap) {
     int epi = EPI_STORE;
     const QMat * wp = resident_any(name, &epi);
     if (!wp) throw std::runtime_error(std::string("debug_gemm: no resident matrix named ") + name);
@@ -1847,11 +1848,13 @@ long long Engine::debug_gemm(const char * name, int rows, const float * x, float
     for (size_t i = 0; i < xh.size(); i++) xh[i] = __float2half_rn(x[i]);
     half * xd = nullptr;
     void * y0 = nullptr, * y1 = nullptr;
-    int * cnt = nullptr;
+    int * cnt = nullptr, * wd = nullptr;
+    cap = where ? std::max(cap, 0) : 0;
     CK(cudaMalloc(&xd, xh.size() * sizeof(half)));
     CK(cudaMalloc(&y0, out_bytes));
     CK(cudaMalloc(&y1, out_bytes));
     CK(cudaMalloc(&cnt, sizeof(int)));
+    CK(cudaMalloc(&wd, (size_t) std::max(cap, 1) * 2 * sizeof(int)));
     long long mismatches = 0;
     cudaGraph_t g = nullptr;
     cudaGraphExec_t ge = nullptr;
@@ -1865,11 +1868,11 @@ long long Engine::debug_gemm(const char * name, int rows, const float * x, float
         if (repeats > 0) {
             // the frame step's conditions: captured launches with programmatic dependent launch
             CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
-            set_pdl_scope(true);
+            set_pdl_scope((flags & 1) == 0);
             try {
                 for (int r = 0; r < repeats; r++) {
                     launch_gemm(w, xd, K, rows, out_of(y1));
-                    launch_bits_diff(y0, y1, out_bytes / 4, cnt, stream_);
+                    launch_bits_diff(y0, y1, out_bytes / 4, cnt, stream_, cap ? wd : nullptr, cap, r);
                 }
             } catch (...) {
                 set_pdl_scope(false);
@@ -1889,6 +1892,7 @@ long long Engine::debug_gemm(const char * name, int rows, const float * x, float
         CK(cudaStreamSynchronize(stream_));
         if (errv) raise_device_error(errv, "debug_gemm: a bounded wait timed out in the tcgen05 GEMM");
         mismatches = c;
+        if (cap > 0) CK(cudaMemcpy(where, wd, (size_t) std::min(c, cap) * 2 * sizeof(int), cudaMemcpyDeviceToHost));
         const size_t n = (size_t) rows * ld;
         if (gated)
             for (size_t i = 0; i < n; i++) y[i] = __half2float(reinterpret_cast<const half *>(hb.data())[i]);
@@ -1897,12 +1901,12 @@ long long Engine::debug_gemm(const char * name, int rows, const float * x, float
     } catch (...) {
         if (ge) cudaGraphExecDestroy(ge);
         if (g) cudaGraphDestroy(g);
-        cudaFree(xd); cudaFree(y0); cudaFree(y1); cudaFree(cnt);
+        cudaFree(xd); cudaFree(y0); cudaFree(y1); cudaFree(cnt); cudaFree(wd);
         throw;
     }
     if (ge) cudaGraphExecDestroy(ge);
     if (g) cudaGraphDestroy(g);
-    cudaFree(xd); cudaFree(y0); cudaFree(y1); cudaFree(cnt);
+    cudaFree(xd); cudaFree(y0); cudaFree(y1); cudaFree(cnt); cudaFree(wd);
     return mismatches;
 }
 

@@ -137,8 +137,11 @@ public:
     // [rows][M] for store epilogues, [rows][M/2] for the gated ones. With repeats > 0 the same
     // launch is captured `repeats` more times in one graph (programmatic dependent launch on, as
     // in the frame step), each result bit-compared on the device with the first; returns the
-    // number of differing 32-bit words
-    long long debug_gemm(const char * name, int rows, const float * x, float * y, int repeats);
+    // number of differing 32-bit words. flags bit 0 captures the repeats without programmatic
+    // dependent launch; `where` (optional) receives the first `cap` differences as (word index,
+    // repeat) pairs
+    long long debug_gemm(const char * name, int rows, const float * x, float * y, int repeats, int flags = 0,
+                         int * where = nullptr, int cap = 0);
     // test hook: the grid-barrier poll limit of the persistent depth launches debug_depth makes
     // (0 restores the default); frame-step graphs never use it
     void set_debug_grid_spin(long long polls) { dbg_grid_spin_ = polls > 0 ? polls : 0; }

@@ -1726,15 +1726,21 @@ __global__ void frames_commit_kernel(const int * cur, int * all, int n, int * ct
     if (threadIdx.x == 0) *ctr = k + 1;
 }
 
-// counts the 32-bit words of b that differ bitwise from a (repeat-launch determinism probe)
-__global__ void bits_diff_kernel(const uint32_t * a, const uint32_t * b, size_t n, int * count) {
+// counts the 32-bit words of b that differ bitwise from a (repeat-launch determinism probe);
+// with `where` non-null the first `cap` differences are recorded as (word index, tag) pairs
+__global__ void bits_diff_kernel(const uint32_t * a, const uint32_t * b, size_t n, int * count, int * where, int cap,
+                                 int tag) {
     pdl_trigger();
     pdl_wait();
-    int local = 0;
-    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x)
-        local += a[i] != b[i];
-    for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-    if ((threadIdx.x & 31) == 0 && local) atomicAdd(count, local);
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        if (a[i] != b[i]) {
+            const int k = atomicAdd(count, 1);
+            if (where && k < cap) {
+                where[2 * k] = (int) i;
+                where[2 * k + 1] = tag;
+            }
+        }
+    }
 }
 
 }  // namespace
@@ -2028,10 +2034,11 @@ void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_c
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_bits_diff(const void * a, const void * b, size_t n_words, int * count, cudaStream_t s) {
+void launch_bits_diff(const void * a, const void * b, size_t n_words, int * count, cudaStream_t s, int * where, int cap,
+                      int tag) {
     const unsigned grid = (unsigned) std::max<size_t>(1, std::min<size_t>((n_words + 255) / 256, 148 * 4));
     launch_k(bits_diff_kernel, grid, 256, 0, s, static_cast<const uint32_t *>(a), static_cast<const uint32_t *>(b),
-             n_words, count);
+             n_words, count, where, cap, tag);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -281,8 +281,10 @@ void launch_advance(const int * row_slot, const int * row_active, const int * ro
                     int * next_out, cudaStream_t s);
 // copies the current frame into frames_all[step] and advances the burst step counter
 void launch_frames_commit(const int * cur, int * frames_all, int n, int * step_ctr, cudaStream_t s);
-// adds to *count the number of 32-bit words of b that differ bitwise from a (n_words each)
-void launch_bits_diff(const void * a, const void * b, size_t n_words, int * count, cudaStream_t s);
+// adds to *count the number of 32-bit words of b that differ bitwise from a (n_words each); with
+// `where` the first `cap` differences overall are recorded as (word index, tag) int pairs
+void launch_bits_diff(const void * a, const void * b, size_t n_words, int * count, cudaStream_t s,
+                      int * where = nullptr, int cap = 0, int tag = 0);
 
 // Philox4x32-10 uniform in [0, 1): top 24 bits of the first output word for (key, draw)
 __host__ __device__ inline uint32_t philox_word0(uint32_t key, uint32_t draw_lo, uint32_t draw_hi) {

@@ -11,7 +11,13 @@
 //     into the swizzled f16 A stage;
 //   * one MMA warp issues four tcgen05.mma.cta_group::1.kind::f16 (128 x N x 16) per chunk into
 //     a TMEM accumulator and commits each stage's MMAs to its "empty" barriers.
-// Every hand-over is an mbarrier; no thread holds global loads in flight across a fence.
+// Every hand-over is an mbarrier; no thread holds global loads in flight across a fence. The raw
+// weight ring is read by the producers with generic shared-memory loads and refilled by bulk
+// copies, which write through the async proxy: the loader issues fence.proxy.async after it has
+// acquired an empty slot, or a copy can land before the last reads of the slot are performed
+// (measured: without the fence 5-20 % of back-to-back launches of a 256-CTA grid returned a few
+// wrong weight rows in one CTA; with it none in thousands).
+
 // Split-K partials of one tile are reduced on chip: the splits form a thread-block cluster, each
 // CTA pushes the rows another split owns into that split's receive buffer (distributed shared
 // memory stores) and sums the slices of its own rows in rank order.
@@ -249,6 +255,9 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
                 const int rs = s % kRawStages, nsub = min(kSC, nch - s * kSC);
                 if (s >= kRawStages) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((s / kRawStages) - 1) & 1u, p.err);
                 if (!ok) break;
+                // the producers read this slot with generic loads; without a proxy fence the bulk
+                // copy (async proxy) may overwrite it before those reads are performed
+                fence_proxy_async();
                 mbar_expect_tx(&raw_full[rs], (uint32_t) (nsub * cb));
                 bulk_g2s(sR + rs * kSC * kRawBytes, base + (size_t) s * kSC * cb, (uint32_t) (nsub * cb), &raw_full[rs]);
                 issued = s + 1;
@@ -504,6 +513,7 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
                 const int rs = c % kPRawStages;
                 if (c >= kPRawStages) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kPRawStages) - 1) & 1u, p.err);
                 if (!ok) break;
+                fence_proxy_async();  // generic reads of the slot before the async-proxy overwrite
                 mbar_expect_tx(&raw_full[rs], (uint32_t) cb);
                 bulk_g2s(sR + rs * kRawBytes, base + (size_t) c * cb, (uint32_t) cb, &raw_full[rs]);
                 issued = c + 1;

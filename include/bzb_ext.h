@@ -61,10 +61,12 @@ BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * ten
    [rows][K] (f32, rounded to f16 as the step's activations are). y receives [rows][M], or
    [rows][M/2] of gated outputs (f16 values widened to f32). With repeats > 0 the launch is
    captured `repeats` more times in one CUDA graph under programmatic dependent launch, and each
-   result is compared bit for bit on the device with the first. Returns the number of 32-bit
-   words that differed (0 for a deterministic kernel), or -1 with breeze_last_error(). */
+   result is compared bit for bit on the device with the first (flags bit 0: capture without
+   programmatic dependent launch). Returns the number of 32-bit words that differed (0 for a
+   deterministic kernel), or -1 with breeze_last_error(); out_where, when non-null, receives the
+   first where_cap differences as (word index into y's rows, repeat index) int pairs. */
 BREEZE_API long long bzb_generator_debug_gemm(breeze_generator * gen, const char * name, int rows, const float * x,
-                                              float * y, int repeats);
+                                              float * y, int repeats, int flags, int * out_where, int where_cap);
 
 /* Tests of the bounded device waits (no reference counterpart). Every spin-wait in the kernels
    gives up after a poll limit, records an error code, lets the copies and MMAs it issued land,

@@ -96,8 +96,8 @@ def resident(m, name):
     return w16, w, False
 
 
-GEMM_NAMES = ["bb.blk.3.attn_qkv", "bb.blk.3.attn_output", "bb.blk.5.ffn_gate_up", "bb.blk.5.ffn_down",
-              "bb.lm_head.weight", "dd.blk.1.attn_qkv", "dd.blk.1.ffn_gate_up", "dd.blk.2.ffn_down", "dd.head.30",
+GEMM_NAMES = ["bb.blk.3.attn_qkv", "bb.blk.3.attn_output.weight", "bb.blk.5.ffn_gate_up", "bb.blk.5.ffn_down.weight",
+              "bb.lm_head.weight", "dd.blk.1.attn_qkv", "dd.blk.1.ffn_gate_up", "dd.blk.2.ffn_down.weight", "dd.head.30",
               "dd.in_proj.weight"]
 
 
@@ -131,10 +131,10 @@ def test_full_gemm_matches_f16_reference(full, name, rows, prefill, monkeypatch)
 
 
 @pytest.mark.parametrize("name,rows,prefill", [
-    ("bb.blk.5.ffn_gate_up", 64, "auto"), ("bb.blk.5.ffn_down", 64, "auto"), ("bb.blk.3.attn_qkv", 64, "auto"),
-    ("bb.blk.3.attn_output", 64, "auto"), ("bb.lm_head.weight", 64, "auto"), ("bb.blk.5.ffn_gate_up", 100, "auto"),
-    ("bb.blk.5.ffn_down", 16, "auto"), ("bb.blk.5.ffn_down", 1, "auto"), ("dd.blk.1.ffn_gate_up", 64, "auto"),
-    ("dd.head.7", 64, "auto"), ("bb.blk.5.ffn_gate_up", 300, "1"), ("bb.blk.5.ffn_down", 300, "1")])
+    ("bb.blk.5.ffn_gate_up", 64, "auto"), ("bb.blk.5.ffn_down.weight", 64, "auto"), ("bb.blk.3.attn_qkv", 64, "auto"),
+    ("bb.blk.3.attn_output.weight", 64, "auto"), ("bb.lm_head.weight", 64, "auto"), ("bb.blk.5.ffn_gate_up", 100, "auto"),
+    ("bb.blk.5.ffn_down.weight", 16, "auto"), ("bb.blk.5.ffn_down.weight", 1, "auto"), ("dd.blk.1.ffn_gate_up", 64, "auto"),
+    ("dd.head.7", 64, "auto"), ("bb.blk.5.ffn_gate_up", 300, "1"), ("bb.blk.5.ffn_down.weight", 300, "1")])
 def test_full_gemm_repeats_bit_identical(full, name, rows, prefill, monkeypatch):
     """Hundreds of captured launches of one shape (two 64-wide chunks per pipeline stage, the
     cluster split-K reduction, partial activation tiles) give the first launch's bits every time."""
