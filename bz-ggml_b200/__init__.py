@@ -106,6 +106,15 @@ SIGNATURES = {
                                                 _c_float_p, _c_float_p]),
     "bzb_generator_debug_gemm": (ctypes.c_longlong, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, _c_float_p,
                                                      _c_float_p, ctypes.c_int, ctypes.c_int, _c_int_p, ctypes.c_int]),
+    "bzb_vocoder_stream_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "bzb_vocoder_stream_close": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "bzb_vocoder_streams_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_int_p, _c_int_p, ctypes.c_int,
+                                                  _c_float_p]),
+    "bzb_vocoder_last_pcm": (ctypes.c_int, [ctypes.c_void_p, _c_float_p, ctypes.c_int]),
+    "bzb_generator_sessions_step_pcm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _c_int_p, ctypes.c_int,
+                                                       _c_uint_p, _c_int_p, _c_int_p, _c_float_p]),
+    "bzb_generator_step_pcm_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _c_int_p, ctypes.c_int,
+                                                     _c_uint_p, ctypes.c_int]),
     "bzb_generator_debug_grid_spin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
     "bzb_debug_mbar_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong]),
     "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
@@ -316,6 +325,33 @@ class GeneratorHandle:
             raise RuntimeError(f"step_frames failed: {self.lib.last_error()}")
         return rc, fr, nx
 
+    def step_pcm(self, voc: "VocoderHandle", session_ids: Sequence[int], seeds: Optional[Sequence[int]] = None,
+                 want_frames: bool = True, want_pcm: bool = True):
+        """One frame step of the listed sessions plus the PCM of every new frame, decoded on each
+        session's vocoder stream (bzb_generator_sessions_step_pcm). Returns (still active, frames
+        [n][nc] or None, next cb0 [n], pcm [n][1920] or None)."""
+        n = len(session_ids)
+        ids = np.ascontiguousarray(np.asarray(session_ids, np.int32))
+        fr = np.zeros((n, self.nc), np.int32) if want_frames else None
+        nx = np.zeros(n, np.int32)
+        pcm = np.zeros((n, VocoderHandle.SAMPLES_PER_FRAME), np.float32) if want_pcm else None
+        sd = None if seeds is None else np.ascontiguousarray(np.asarray(seeds, np.uint32))
+        rc = self.lib.lib.bzb_generator_sessions_step_pcm(self.handle, voc.handle, _ip(ids), n, _up(sd),
+                                                          None if fr is None else _ip(fr), _ip(nx),
+                                                          None if pcm is None else _fp(pcm))
+        if rc < 0:
+            raise RuntimeError(f"sessions_step_pcm failed: {self.lib.last_error()}")
+        return rc, fr, nx, pcm
+
+    def step_pcm_device(self, voc: "VocoderHandle", session_ids: Sequence[int], seeds: Optional[Sequence[int]] = None,
+                        burst_steps: int = 1) -> None:
+        """burst_steps device-resident frame steps, each followed by the streaming decode of its frames
+        (bzb_generator_step_pcm_device); asynchronous on the generator's stream."""
+        ids = np.ascontiguousarray(np.asarray(session_ids, np.int32))
+        sd = None if seeds is None else np.ascontiguousarray(np.asarray(seeds, np.uint32))
+        if self.lib.lib.bzb_generator_step_pcm_device(self.handle, voc.handle, _ip(ids), len(ids), _up(sd), burst_steps) != 0:
+            raise RuntimeError(self.lib.last_error())
+
     def step_device(self, burst_steps: int) -> None:
         if self.lib.lib.bzb_generator_step_device(self.handle, burst_steps) != 0:
             raise RuntimeError(self.lib.last_error())
@@ -518,6 +554,31 @@ class VocoderHandle:
 
     def session_free(self, session_id: int) -> int:
         return self.lib.lib.breeze_vocoder_session_free(self.handle, session_id)
+
+    def stream_open(self, stream_id: int) -> None:
+        if self.lib.lib.bzb_vocoder_stream_open(self.handle, stream_id) != 0:
+            raise RuntimeError(self.lib.last_error())
+
+    def stream_close(self, stream_id: int) -> bool:
+        return self.lib.lib.bzb_vocoder_stream_close(self.handle, stream_id) == 0
+
+    def streams_decode(self, stream_ids: Sequence[int], codes: np.ndarray) -> np.ndarray:
+        """codes [n][T][nc] new frames of n distinct streams -> PCM [n][T * 1920], each stream
+        continuing its carried decoder state (bzb_vocoder_streams_decode)."""
+        c = np.ascontiguousarray(codes, np.int32)
+        n, T = c.shape[0], c.shape[1]
+        ids = np.ascontiguousarray(np.asarray(stream_ids, np.int32))
+        out = np.zeros((n, T * self.SAMPLES_PER_FRAME), np.float32)
+        if self.lib.lib.bzb_vocoder_streams_decode(self.handle, n, _ip(ids), _ip(c), T, _fp(out)) != n:
+            raise RuntimeError(f"streams_decode failed: {self.lib.last_error()}")
+        return out
+
+    def last_pcm(self, n_samples: int) -> np.ndarray:
+        """The PCM the last device-resident step left in the vocoder (synchronises)."""
+        out = np.zeros(n_samples, np.float32)
+        if self.lib.lib.bzb_vocoder_last_pcm(self.handle, _fp(out), n_samples) != n_samples:
+            raise RuntimeError(self.lib.last_error())
+        return out
 
     def stream_decode(self, frames: np.ndarray) -> np.ndarray:
         f = np.ascontiguousarray(frames, np.int32)

@@ -478,7 +478,9 @@ breeze_vocoder * breeze_vocoder_create_from_generator(breeze_generator * gen) {
     try {
         auto v = std::make_unique<breeze_vocoder>();
         v->device = gen->device;
-        v->voc = std::make_unique<bzb::Vocoder>(gen->eng->gguf(), gen->eng->cfg, gen->device);
+        // the generator's stream: decodes are ordered after its frame steps and may read their
+        // frames on the device (bzb_generator_step_pcm_device)
+        v->voc = std::make_unique<bzb::Vocoder>(gen->eng->gguf(), gen->eng->cfg, gen->device, gen->eng->stream());
         return v.release();
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -701,6 +703,120 @@ int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int su
     if (!gen || !tensor || rows <= 0 || !x || !y) return -1;
     try {
         gen->eng->debug_gemv(tensor, sub, rows, x, y);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+// ------------------------------------------------------------------------------------ streams
+int bzb_vocoder_stream_open(breeze_vocoder * voc, int stream_id) {
+    if (!voc) return -1;
+    try {
+        voc->voc->stream_open(stream_id);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_vocoder_stream_close(breeze_vocoder * voc, int stream_id) {
+    if (!voc) return -1;
+    return voc->voc->stream_close(stream_id) ? 0 : -1;
+}
+
+int bzb_vocoder_streams_decode(breeze_vocoder * voc, int n, const int * stream_ids, const int * codes, int n_frames,
+                               float * out_pcm) {
+    if (!voc || n <= 0 || !stream_ids || !codes || n_frames <= 0 || !out_pcm) {
+        set_error("streams_decode: bad arguments");
+        return -1;
+    }
+    try {
+        voc->voc->streams_decode(n, stream_ids, nullptr, codes, n_frames, out_pcm);
+        return n;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_vocoder_last_pcm(breeze_vocoder * voc, float * out, int n_samples) {
+    if (!voc || !out || n_samples < 0) return -1;
+    try {
+        voc->voc->check_device_error();
+        if (cudaMemcpy(out, voc->voc->last_pcm(), (size_t) n_samples * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+            throw std::runtime_error("last_pcm: copy failed");
+        return n_samples;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+static bool same_device_stream(breeze_generator * gen, breeze_vocoder * voc) {
+    if (voc->voc->stream() != gen->eng->stream()) {
+        set_error("the vocoder must come from breeze_vocoder_create_from_generator of this generator");
+        return false;
+    }
+    return true;
+}
+
+int bzb_generator_sessions_step_pcm(breeze_generator * gen, breeze_vocoder * voc, const int * session_ids, int n,
+                                    const unsigned int * seeds, int * out_frames, int * out_next_cb0, float * out_pcm) {
+    if (!gen || !voc || !session_ids || n <= 0 || !out_next_cb0) {
+        set_error("sessions_step_pcm: bad arguments");
+        return -1;
+    }
+    try {
+        if (!same_device_stream(gen, voc)) return -1;
+        bzb::Engine & eng = *gen->eng;
+        const int nc = eng.nc();
+        std::vector<int> frames((size_t) n * nc);
+        const bzb::StepResult r = eng.step(session_ids, n, 1, seeds, true, frames.data(), nc, out_next_cb0, true);
+        if (out_frames) std::memcpy(out_frames, frames.data(), frames.size() * sizeof(int));
+        // every session that produced a frame decodes it on its stream (keyed by session id,
+        // restarted when the id's session was created again)
+        std::vector<int> ids, rows, codes;
+        std::vector<unsigned long long> epochs;
+        for (int i = 0; i < n; i++) {
+            if (frames[(size_t) i * nc] < 0) continue;
+            ids.push_back(session_ids[i]);
+            rows.push_back(i);
+            epochs.push_back(eng.session_epoch(session_ids[i]));
+            codes.insert(codes.end(), frames.begin() + (size_t) i * nc, frames.begin() + (size_t) (i + 1) * nc);
+        }
+        if (out_pcm) std::fill_n(out_pcm, (size_t) n * bzb::Vocoder::kSamplesPerFrame, 0.0f);
+        if (!ids.empty()) {
+            std::vector<float> pcm(ids.size() * bzb::Vocoder::kSamplesPerFrame);
+            voc->voc->streams_decode((int) ids.size(), ids.data(), epochs.data(), codes.data(), 1, pcm.data());
+            if (out_pcm)
+                for (size_t j = 0; j < ids.size(); j++)
+                    std::memcpy(out_pcm + (size_t) rows[j] * bzb::Vocoder::kSamplesPerFrame,
+                                pcm.data() + j * bzb::Vocoder::kSamplesPerFrame, bzb::Vocoder::kSamplesPerFrame * sizeof(float));
+        }
+        return r.steps_executed == 0 ? 0 : r.still_active;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int bzb_generator_step_pcm_device(breeze_generator * gen, breeze_vocoder * voc, const int * session_ids, int n,
+                                  const unsigned int * seeds, int burst_steps) {
+    if (!gen || !voc || !session_ids || n <= 0 || burst_steps <= 0) {
+        set_error("step_pcm_device: bad arguments");
+        return -1;
+    }
+    try {
+        if (!same_device_stream(gen, voc)) return -1;
+        bzb::Engine & eng = *gen->eng;
+        std::vector<unsigned long long> epochs(n);
+        for (int i = 0; i < n; i++) epochs[i] = eng.session_epoch(session_ids[i]);
+        eng.step_launch_device(session_ids, n, seeds, burst_steps, [&](int k) {
+            voc->voc->streams_decode_device(n, session_ids, epochs.data(), eng.device_frames(k), eng.nc(), 1, nullptr);
+        });
         return 0;
     } catch (const std::exception & e) {
         set_error(e.what());

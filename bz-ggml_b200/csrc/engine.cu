@@ -922,14 +922,12 @@ cudaGraphExec_t Engine::graph_for(int R, int flags) {
     return exec;
 }
 
-StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
-                        int width, int * next_out, bool fill_inactive, bool sampled_depth,
-                        const uint32_t * depth_seeds, const StepForce * force) {
-    StepResult res;
+int Engine::setup_step(const int * sids, int n, int K, const uint32_t * seeds, bool sampled_depth,
+                       const uint32_t * depth_seeds, const StepForce * force, std::vector<int> & rs, cudaGraphExec_t * g_out) {
     const int nc = cfg.nc;
     if (n > rmax_) throw std::runtime_error("batch of " + std::to_string(n) + " sessions exceeds the engine's " + std::to_string(rmax_) + " rows (BZB_MAX_BATCH)");
     if (K > kmax_) throw std::runtime_error("burst longer than 64 steps");
-    std::vector<int> rs(n, -1);
+    rs.assign(n, -1);
     std::vector<char> used(max_slots_, 0);
     bool any = false;
     int n_pairs = 0;
@@ -943,9 +941,7 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
         any = true;
         if (slots_[s].partner >= 0) n_pairs++;
     }
-    for (int i = 0; i < n; i++) next_out[i] = -1;
-    if (burst && fill_inactive) std::fill_n(frames_out, (size_t) K * n * width, -1);
-    if (!any) return res;
+    if (!any) return 0;
     // rows: the listed sessions in order, then the unconditional branches of two-branch sessions
     if (n + n_pairs > rmax_) throw std::runtime_error("batch of " + std::to_string(n + n_pairs) + " branches exceeds the engine's " + std::to_string(rmax_) + " rows (BZB_MAX_BATCH)");
     const int R = std::max(8, round_up(n + n_pairs, 8));
@@ -1012,6 +1008,21 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     CK(cudaMemsetAsync(step_ctr_, 0, sizeof(int), stream_));
     CK(cudaMemsetAsync(any_active_, 0, kmax_ * sizeof(int), stream_));
     CK(cudaMemsetAsync(next_, 0xFF, R * sizeof(int), stream_));
+    *g_out = g;
+    return R;
+}
+
+StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
+                        int width, int * next_out, bool fill_inactive, bool sampled_depth,
+                        const uint32_t * depth_seeds, const StepForce * force) {
+    StepResult res;
+    const int nc = cfg.nc;
+    for (int i = 0; i < n; i++) next_out[i] = -1;
+    if (burst && fill_inactive) std::fill_n(frames_out, (size_t) K * n * width, -1);
+    std::vector<int> rs;
+    cudaGraphExec_t g = nullptr;
+    const int R = setup_step(sids, n, K, seeds, sampled_depth, depth_seeds, force, rs, &g);
+    if (R == 0) return res;
     for (int k = 0; k < K; k++) CK(cudaGraphLaunch(g, stream_));
     std::vector<int> fr((size_t) K * R * nc), nx(R), aa(K);
     CK(cudaMemcpyAsync(fr.data(), frames_all_, fr.size() * sizeof(int), cudaMemcpyDeviceToHost, stream_));
@@ -1051,6 +1062,22 @@ void Engine::step_device_only(int K) {
     for (int k = 0; k < K; k++) CK(cudaGraphLaunch(g, stream_));
 }
 
+void Engine::step_launch_device(const int * sids, int n, const uint32_t * seeds, int K,
+                                const std::function<void(int)> & after_step) {
+    for (int i = 0; i < n; i++) {
+        auto it = sid_to_slot_.find(sids[i]);
+        if (it == sid_to_slot_.end() || !slots_[it->second].active)
+            throw std::runtime_error("device step: session " + std::to_string(sids[i]) + " is not active");
+    }
+    std::vector<int> rs;
+    cudaGraphExec_t g = nullptr;
+    if (setup_step(sids, n, K, seeds, false, nullptr, nullptr, rs, &g) == 0) return;
+    for (int k = 0; k < K; k++) {
+        CK(cudaGraphLaunch(g, stream_));
+        if (after_step) after_step(k);
+    }
+}
+
 void Engine::sync() { CK(cudaStreamSynchronize(stream_)); }
 
 bool Engine::session_active(int sid) const {
@@ -1076,7 +1103,10 @@ int Engine::acquire_slot(int sid, int n_pages, bool register_sid) {
     CK(cudaMemcpyAsync(page_table_ + (size_t) slot * max_pages_, row.data(), max_pages_ * sizeof(int),
                        cudaMemcpyHostToDevice, stream_));
     CK(cudaStreamSynchronize(stream_));
-    if (register_sid) sid_to_slot_[sid] = slot;
+    if (register_sid) {
+        sid_to_slot_[sid] = slot;
+        sid_epoch_[sid] = ++epoch_ctr_;
+    }
     else s.follower = true;
     return slot;
 }

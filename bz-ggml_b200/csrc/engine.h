@@ -6,6 +6,7 @@
 #include "host.h"
 #include "kernels.cuh"
 
+#include <functional>
 #include <map>
 #include <memory>
 #include <string>
@@ -117,6 +118,16 @@ public:
 
     // device-resident run of K steps for the current batch (no host copies): timing entry
     void step_device_only(int K);
+    // K frame steps of the listed sessions (every one active) without host copies or a host
+    // synchronisation; after each step's graph, after_step(k) may enqueue more work on the
+    // engine's stream that reads that step's frames (device_frames(k), row i = session i)
+    void step_launch_device(const int * sids, int n, const uint32_t * seeds, int K, const std::function<void(int)> & after_step);
+    const int * device_frames(int k) const { return frames_all_ + (size_t) k * cur_R_ * cfg.nc; }
+    // a counter that changes every time a session with this id is created (0: no such session)
+    unsigned long long session_epoch(int sid) const {
+        auto it = sid_epoch_.find(sid);
+        return it == sid_epoch_.end() ? 0ull : it->second;
+    }
     void sync();
     cudaStream_t stream() const { return stream_; }
 
@@ -186,6 +197,11 @@ private:
     void swap_depth_sets();
     const GgufFile & src() const { return src_ ? *src_ : gg_; }
     void enqueue_step(int R, int flags);
+    // the part of step() before its graph launches: rows (the listed sessions, then the partners
+    // of two-branch sessions), flags, device uploads, the graph; returns R, 0 when no listed
+    // session is active (rs: row -> slot)
+    int setup_step(const int * sids, int n, int K, const uint32_t * seeds, bool sampled_depth, const uint32_t * depth_seeds,
+                   const StepForce * force, std::vector<int> & rs, cudaGraphExec_t * g_out);
     void prefill_prompt(int slot, const std::vector<std::vector<int>> & segs, const int * ref_codes, int ref_frames,
                         float * logits);
     void depth_layer(int l, int rows, int R, int n_new, int start);
@@ -257,6 +273,8 @@ private:
     std::vector<SlotHost> slots_;
     std::vector<int> free_slots_;
     std::unordered_map<int, int> sid_to_slot_;
+    std::unordered_map<int, unsigned long long> sid_epoch_;
+    unsigned long long epoch_ctr_ = 0;
 
     // step buffers
     int rmax_ = 0, kmax_ = 0;

@@ -101,7 +101,22 @@ struct ConvArgs {
     int splits = 1, ci_per_split = 0;
     float * part = nullptr;
     int lxp = 0;                        // staged window row stride (floats)
+    // Segments: the L steps are S = L / seg_len independent sequences of seg_len steps each (one
+    // per decoded stream; seg_len 0: one sequence of L steps). Each segment's first
+    // P = (taps - 1) dil inputs come from its state -- the last P inputs of the stream's previous
+    // call -- instead of zeros, so consecutive calls continue one causal sequence. A stream slot
+    // keeps two copies of this layer's state, [2][cin][P] floats at st + slot * st_stride; segment
+    // b reads copy seg_par[b] (-1: a new stream, zero state) of slot seg_slot[b], and the tile that
+    // holds a segment's last step writes its new state (the last P inputs of [state | data]) to
+    // copy voc_state_next(seg_par[b]). st null: zero state, nothing written.
+    int seg_len = 0;
+    float * st = nullptr;
+    size_t st_stride = 0;
+    const int * seg_slot = nullptr, * seg_par = nullptr;
 };
+
+// the state copy a segment writes: the other one, or copy 0 after a zero (new-stream) state
+__host__ __device__ inline int voc_state_next(int par) { return par < 0 ? 0 : 1 - par; }
 
 __device__ __forceinline__ uint32_t to_tf32(float f) {
     uint32_t r;
@@ -137,6 +152,8 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
     constexpr int kAld = kCCI + 4;
     float * As = csm;                                   // [2][kCBM][kAld]: weight tile of one tap
     float * xs = csm + 2 * kCBM * kAld;                 // [kCCI][lxp]: input window of one chunk
+    int * wseg = reinterpret_cast<int *>(xs + kCCI * a.lxp);  // [lxp]: segment of each window entry
+    int * wtau = wseg + a.lxp;                          // [lxp]: its step in the segment (< 0: state)
     const int phases = a.ostride;
     const int phase = blockIdx.z % phases, split = blockIdx.z / phases;
     const int ci_beg = split * a.ci_per_split, ci_end = min(a.cin, ci_beg + a.ci_per_split);
@@ -145,7 +162,27 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
     const int g = lane >> 2, t4 = lane & 3;
-    const int halo = (a.taps - 1) * a.dil, lx = kCBN + halo;
+    const int halo = (a.taps - 1) * a.dil;
+    // The window holds the tile's steps in the padded sequence where every segment is preceded
+    // by its P = halo state inputs: step n (segment n / seg) sits at padded index
+    // n + P (n / seg) + P, and the window starts P entries before the tile's first step.
+    const int seg = a.seg_len > 0 ? a.seg_len : a.L;
+    const int n_last = min(t0 + kCBN, a.L) - 1;
+    const int b_first = t0 / seg;
+    const int wbeg = t0 + halo * b_first;
+    const int lx = n_last + halo * (n_last / seg) + halo - wbeg + 1;
+    for (int u = tid; u < lx; u += kCThreads) {
+        const int v = wbeg + u, b = v / (halo + seg);
+        wseg[u] = b;
+        wtau[u] = v - b * (halo + seg) - halo;
+    }
+    // window column of this thread's output steps for tap taps-1 (the unshifted one)
+    int cbase[4];
+#pragma unroll
+    for (int ni = 0; ni < 4; ni++) {
+        const int n = min(t0 + wn + ni * 8 + g, a.L - 1);
+        cbase[ni] = n + halo * (n / seg) - wbeg;
+    }
     float acc[2][4][4];
 #pragma unroll
     for (int mi = 0; mi < 2; mi++)
@@ -193,24 +230,48 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
     for (int it = 0; it < n_iter; it++) {
         const int k = it % a.taps, cur = it & 1;
         if (k == 0) {
-            // a new channel chunk: stage its input window (zero before t = 0 and past the chunk)
+            // a new channel chunk: stage its input window (a segment's state before its first
+            // step: zero without a state; zero past the chunk and past the last step)
             __syncthreads();  // every warp is done with the previous window
             const int c0 = ci_beg + (it / a.taps) * kCCI;
             for (int e = tid; e < kCCI * lx; e += kCThreads) {
                 const int i = e / lx, u = e - i * lx;
-                const int ci = c0 + i, t = t0 - halo + u;
+                const int ci = c0 + i, b = wseg[u], tau = wtau[u];
                 float v = 0.0f;
-                if (ci < ci_end && t >= 0 && t < a.L) {
-                    const int src = ci / a.istride, ph = ci - src * a.istride;
-                    v = a.x[(size_t) src * a.Lin + (size_t) t * a.istride + ph];
+                if (ci < ci_end) {
+                    if (tau < 0) {
+                        const int par = a.st && b * seg < a.L ? a.seg_par[b] : -1;
+                        if (par >= 0)
+                            v = a.st[(size_t) a.seg_slot[b] * a.st_stride + ((size_t) par * a.cin + ci) * halo + (tau + halo)];
+                    } else {
+                        const int t = b * seg + tau;
+                        if (t < a.L) {
+                            const int src = ci / a.istride, ph = ci - src * a.istride;
+                            v = a.x[(size_t) src * a.Lin + (size_t) t * a.istride + ph];
+                        }
+                    }
                 }
                 xs[i * a.lxp + u] = v;
             }
         }
         __syncthreads();  // weight tile `cur` and the window are in place
+        if (k == 0 && a.st && halo > 0 && blockIdx.y == 0 && phase == 0) {
+            // segments whose last step is in this tile: their new state is the last `halo`
+            // entries of [state | data], at padded indices b (halo + seg) + seg + r
+            const int c0 = ci_beg + (it / a.taps) * kCCI;
+            for (int b = b_first; b * seg + seg - 1 <= n_last; b++) {
+                if ((b + 1) * seg - 1 < t0) continue;
+                float * dst = a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) voc_state_next(a.seg_par[b]) * a.cin * halo;
+                const int u0 = b * (halo + seg) + seg - wbeg;
+                for (int e = tid; e < kCCI * halo; e += kCThreads) {
+                    const int i = e / halo, r = e - i * halo;
+                    if (c0 + i < ci_end) dst[(size_t) (c0 + i) * halo + r] = xs[i * a.lxp + u0 + r];
+                }
+            }
+        }
         if (it + 1 < n_iter) load_a(it + 1);  // next tile's global loads overlap these MMAs
         const float * At = As + (size_t) cur * kCBM * kAld;
-        const int shift = halo - (a.taps - 1 - k) * a.dil;  // window column of output t0 for tap k
+        const int shift = halo - (a.taps - 1 - k) * a.dil;  // tap k reads (taps-1-k) dil steps back
 #pragma unroll
         for (int kk = 0; kk < kCCI; kk += 8) {
             uint32_t af[2][4], bf[4][2];
@@ -224,7 +285,7 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
             }
 #pragma unroll
             for (int ni = 0; ni < 4; ni++) {
-                const int col = wn + ni * 8 + g + shift;
+                const int col = cbase[ni] + shift;
                 bf[ni][0] = to_tf32(xs[(kk + t4) * a.lxp + col]);
                 bf[ni][1] = to_tf32(xs[(kk + t4 + 4) * a.lxp + col]);
             }
@@ -262,19 +323,97 @@ __global__ void voc_conv_reduce_kernel(const ConvArgs a) {
     }
 }
 
-// causal depthwise conv (src/codec_conv.cpp:42-59), w [K][C]: y[c][t] = b[c] + sum_k w[k][c]
-// x[c][t - (K-1) + k]
-__global__ void voc_depthwise_kernel(const float * x, int C, int L, const float * w, const float * b, int K, float * y) {
-    const size_t n = (size_t) C * L;
-    for (size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (size_t) gridDim.x * blockDim.x) {
-        const int c = (int) (idx / L), t = (int) (idx % L);
-        float acc = 0.0f;
-        for (int k = 0; k < K; k++) {
-            const int tt = t - (K - 1) + k;
-            if (tt >= 0) acc += w[(size_t) k * C + c] * x[(size_t) c * L + tt];
+// causal depthwise conv (src/codec_conv.cpp:42-59), w [K][C], y[c][t] = b[c] + sum_k w[k][c]
+// x[c][t - (K-1) + k], over S segments of seg steps each (x [C][S seg]); a segment's first
+// K-1 inputs come from copy seg_par of its slot's state ([2][C][K-1] at st + slot st_stride;
+// -1 or st null: zero). Threads past the outputs write each segment's new state (the last K-1
+// inputs of [state | data]) to copy voc_state_next(seg_par).
+__global__ void voc_depthwise_seg_kernel(const float * x, int C, int S, int seg, const float * w, const float * b, int K,
+                                         float * y, float * st, size_t st_stride, const int * seg_slot, const int * seg_par) {
+    const int P = K - 1, L = S * seg;
+    const size_t n_out = (size_t) C * L, n_st = st ? (size_t) S * C * P : 0;
+    for (size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x; idx < n_out + n_st; idx += (size_t) gridDim.x * blockDim.x) {
+        if (idx < n_out) {
+            const int c = (int) (idx / L), n = (int) (idx % L), sg = n / seg, tau = n - sg * seg;
+            const int par = st ? seg_par[sg] : -1;
+            const float * sin_ = par >= 0 ? st + (size_t) seg_slot[sg] * st_stride + ((size_t) par * C + c) * P : nullptr;
+            float acc = 0.0f;
+            for (int k = 0; k < K; k++) {
+                const int tt = tau - P + k;
+                const float v = tt >= 0 ? x[(size_t) c * L + (size_t) sg * seg + tt] : (sin_ ? sin_[P + tt] : 0.0f);
+                acc += w[(size_t) k * C + c] * v;
+            }
+            y[idx] = acc + (b ? b[c] : 0.0f);
+        } else {
+            const size_t j = idx - n_out;
+            const int r = (int) (j % P), c = (int) ((j / P) % C), sg = (int) (j / ((size_t) P * C));
+            const int par = seg_par[sg];
+            float * slot = st + (size_t) seg_slot[sg] * st_stride;
+            const int q = r + seg;  // index into [state (P) | data (seg)]
+            const float v = q < P ? (par >= 0 ? slot[((size_t) par * C + c) * P + q] : 0.0f)
+                                  : x[(size_t) c * L + (size_t) sg * seg + (q - P)];
+            slot[((size_t) voc_state_next(par) * C + c) * P + r] = v;
         }
-        y[idx] = acc + (b ? b[c] : 0.0f);
     }
+}
+
+// K and V of T new frames of S streams into their rings: row s T + t is position pos0[s] + t of
+// ring slot[s] (k rotated by NEOX RoPE at that position). Ring layout per slot:
+// [R positions][2 (k, v)][nkv hd] floats, position p at p mod R.
+__global__ void voc_kv_ring_append_kernel(const float * k, const float * v, int S, int T, int nkv, int hd,
+                                          const float2 * rope, float * ring, size_t slot_stride, int R,
+                                          const int * slots, const int * pos0) {
+    const int kvd = nkv * hd, half_d = hd / 2;
+    const size_t n = (size_t) S * T * kvd;
+    for (size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (size_t) gridDim.x * blockDim.x) {
+        const int e = (int) (idx % kvd), row = (int) (idx / kvd), sgm = row / T, t = row - sgm * T;
+        const int d = e % hd;
+        const int pos = pos0[sgm] + t;
+        const int dp = d < half_d ? d + half_d : d - half_d;
+        const float x0 = k[(size_t) row * kvd + e], x1 = k[(size_t) row * kvd + e - d + dp];
+        const float2 cs = rope[(size_t) pos * half_d + (d < half_d ? d : d - half_d)];
+        const float kr = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
+        float * dst = ring + (size_t) slots[sgm] * slot_stride + (size_t) (pos % R) * 2 * kvd;
+        dst[e] = kr;
+        dst[kvd + e] = v[(size_t) row * kvd + e];
+    }
+}
+
+// causal sliding-window attention of T new frames per stream over its ring (keys already
+// rotated): one warp per (row s T + t, head h), query at position pos0[s] + t, keys
+// pos - window < j <= pos; hd <= 128
+__global__ void voc_attn_ring_kernel(const float * q, int S, int T, int nh, int nkv, int hd, int window,
+                                     const float2 * rope, float scale, const float * ring, size_t slot_stride, int R,
+                                     const int * slots, const int * pos0, half * out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= S * T * nh) return;
+    const int row = warp / nh, h = warp % nh, sgm = row / T, t = row - sgm * T, g = h / (nh / nkv);
+    const int E = hd / 32, half_d = hd / 2, kvd = nkv * hd;
+    const int pos = pos0[sgm] + t;
+    const float * base = ring + (size_t) slots[sgm] * slot_stride;
+    float qv[4];
+    for (int e = 0; e < E; e++) {
+        const int d = lane + 32 * e;
+        const int dp = d < half_d ? d + half_d : d - half_d;
+        const float x0 = q[((size_t) row * nh + h) * hd + d], x1 = q[((size_t) row * nh + h) * hd + dp];
+        const float2 cs = rope[(size_t) pos * half_d + (d < half_d ? d : d - half_d)];
+        qv[e] = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
+    }
+    const int j0 = max(0, window > 0 ? pos - window + 1 : 0);
+    float m = -INFINITY, l = 0.0f, acc[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+    for (int j = j0; j <= pos; j++) {
+        const float * kr = base + (size_t) (j % R) * 2 * kvd + (size_t) g * hd;
+        float dot = 0.0f;
+        for (int e = 0; e < E; e++) dot += qv[e] * kr[lane + 32 * e];
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float sc = dot * scale;
+        const float mn = fmaxf(m, sc);
+        const float corr = expf(m - mn), p = expf(sc - mn);
+        l = l * corr + p;
+        for (int e = 0; e < E; e++) acc[e] = acc[e] * corr + p * kr[kvd + lane + 32 * e];
+        m = mn;
+    }
+    for (int e = 0; e < E; e++) out[((size_t) row * nh + h) * hd + lane + 32 * e] = __float2half_rn(acc[e] / l);
 }
 
 // layer norm over each row of [R][C] (mean and variance in double, src/common.cpp:131-134) -> f16
@@ -387,11 +526,17 @@ __global__ void voc_attn_kernel(const float * q, const float * k, const float * 
 
 unsigned grid_for(size_t n) { return (unsigned) std::min<size_t>((n + 255) / 256, 148 * 16); }
 
-size_t conv_smem_bytes(int lxp) { return ((size_t) 2 * kCBM * (kCCI + 4) + (size_t) kCCI * lxp) * sizeof(float); }
-int conv_lxp(int taps, int dil) {
-    // window row stride: at least 64 + halo, and 8 mod 32 so that the 4 x 8 B-fragment reads
-    // of a warp fall in distinct banks
-    const int lx = kCBN + (taps - 1) * dil;
+size_t conv_smem_bytes(int lxp) {
+    return ((size_t) 2 * kCBM * (kCCI + 4) + (size_t) kCCI * lxp) * sizeof(float) + (size_t) 2 * lxp * sizeof(int);
+}
+// window row stride: at least the widest window a tile stages -- 64 steps plus `halo` state
+// entries for every segment the tile touches (a 64-step tile touches at most
+// ceil(63 / seg_len) + 1 segments) -- and 8 mod 32 so that the 4 x 8 B-fragment reads of a warp
+// fall in distinct banks. seg_len 0: one segment.
+int conv_lxp(int taps, int dil, int seg_len = 0, int n_seg = 1) {
+    const int halo = (taps - 1) * dil;
+    const int touched = seg_len > 0 ? std::min(n_seg, (kCBN - 1 + seg_len - 1) / seg_len + 1) : 1;
+    const int lx = kCBN + halo * touched;
     return (lx + 23) / 32 * 32 + 8;
 }
 
@@ -423,7 +568,8 @@ void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats,
     a.splits = splits;
     a.ci_per_split = ((chunks + splits - 1) / splits) * kCCI;
     a.part = scratch;
-    a.lxp = conv_lxp(a.taps, a.dil);
+    a.lxp = conv_lxp(a.taps, a.dil, a.seg_len, a.seg_len > 0 ? a.L / a.seg_len : 1);
+    raise_conv_smem_limit(conv_smem_bytes(a.lxp));
     const dim3 grid((unsigned) ((a.L + kCBN - 1) / kCBN), (unsigned) ((a.cout + kCBM - 1) / kCBM), (unsigned) (phases * splits));
     voc_conv_mma_kernel<<<grid, kCThreads, conv_smem_bytes(a.lxp), s>>>(a);
     if (splits > 1) {
@@ -543,9 +689,15 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
     return c;
 }
 
-Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_(gg), cfg_(cfg), vc_(cfg.voc), device_(device) {
+Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaStream_t stream)
+    : gg_(gg), cfg_(cfg), vc_(cfg.voc), device_(device) {
     VCHECK(cudaSetDevice(device));
-    VCHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (stream) {
+        stream_ = stream;
+        own_stream_ = false;
+    } else {
+        VCHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    }
     const GgufTensor & e0 = need("codec.dq.first.0.embed");
     dq_ = (int) e0.ne[0];
     if (e0.ne[1] < cfg_.vs) throw std::runtime_error("vocoder: codebook tables need at least audio_vocab_size rows");
@@ -657,6 +809,30 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device) : gg_
         }
         raise_conv_smem_limit(conv_smem_bytes(lxp));
     }
+    // the carried state of a stream, in decode order: dpre; per ConvNeXt stage its transposed
+    // conv and depthwise conv; dhead; per SEANet block its transposed conv and each residual
+    // unit's two convs; dfin (a transposed conv carries taps - 1 inputs, a conv (taps - 1) dil)
+    {
+        auto add = [&](int cin, int P) {
+            st_off_.push_back(st_floats_);
+            st_floats_ += (size_t) 2 * cin * P;
+        };
+        add(cbdim_, dpre_.taps - 1);
+        for (const Up & u : ups_) {
+            add(latent_, u.up.taps - 1);
+            add(latent_, u.dw.K - 1);
+        }
+        add(latent_, dhead_.taps - 1);
+        const int dil[3] = { 1, 3, 9 };
+        for (const Blk & b : blks_) {
+            add(b.up.cin, b.up.taps - 1);
+            for (int j = 0; j < 3; j++) {
+                add(b.res[j].c1.cin, (b.res[j].c1.taps - 1) * dil[j]);
+                add(b.res[j].c2.cin, b.res[j].c2.taps - 1);
+            }
+        }
+        add(dfin_.cin, dfin_.taps - 1);
+    }
     err_ = dalloc<int>(1);
     VCHECK(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
     scr_.ws_elems = (size_t) 1 << 20;
@@ -673,8 +849,9 @@ Vocoder::~Vocoder() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
     for (void * p : scratch_allocs_) cudaFree(p);
+    for (void * p : stream_allocs_) cudaFree(p);
     for (void * p : allocs_) cudaFree(p);
-    if (stream_) cudaStreamDestroy(stream_);
+    if (stream_ && own_stream_) cudaStreamDestroy(stream_);
 }
 
 void Vocoder::ensure(int T) {
@@ -716,6 +893,7 @@ void Vocoder::ensure(int T) {
     g_ = fa(Tc * vc_.ffn);
     pcm_ = fa(Tc * kSamplesPerFrame);
     u_ = fa(Tc * vc_.ffn);
+    fring_ = fa(Tc * 2 * vc_.n_kv * vc_.hd);
     t16_ = ha(up_rows * wide);
     att16_ = ha(Tc * vc_.n_head * vc_.hd);
     f16_ = ha(std::max(up_rows * wide, Tc * (size_t) dq_ * 2));
@@ -738,90 +916,173 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
     if (T <= 0) return;
     VCHECK(cudaSetDevice(device_));
     ensure(T);
+    VCHECK(cudaMemcpyAsync(codes_, codes, (size_t) T * cfg_.nc * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    decode_segments(codes_, cfg_.nc, 1, T, nullptr, pcm_);
+    VCHECK(cudaMemcpyAsync(pcm, pcm_, (size_t) T * kSamplesPerFrame * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    check_device_error();
+}
+
+void Vocoder::check_device_error() {
+    int err = 0;
+    VCHECK(cudaMemcpyAsync(&err, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    VCHECK(cudaStreamSynchronize(stream_));
+    if (err) {
+        VCHECK(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
+        VCHECK(cudaStreamSynchronize(stream_));
+        throw std::runtime_error("vocoder: a bounded wait timed out in the tcgen05 GEMM (device error code " +
+                                 std::to_string(err) + ")");
+    }
+}
+
+void Vocoder::ensure_segments(int S) {
+    if (S <= seg_cap_) return;
+    VCHECK(cudaStreamSynchronize(stream_));
+    const int cap = std::max(S, 256);
+    int * d = nullptr;
+    VCHECK(cudaMalloc(&d, (size_t) 5 * cap * sizeof(int)));
+    std::vector<int> h((size_t) 2 * cap, 0);
+    for (int i = 0; i < cap; i++) h[i] = i;
+    VCHECK(cudaMemcpyAsync(d + (size_t) 3 * cap, h.data(), h.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    VCHECK(cudaStreamSynchronize(stream_));
+    if (seg_dev_) cudaFree(seg_dev_);
+    seg_dev_ = d;
+    seg_ident_ = d + (size_t) 3 * cap;
+    seg_cap_ = cap;
+}
+
+void Vocoder::decode_segments(const int * codes_dev, int ld_codes, int S, int T, const Segment * segs, float * pcm_dev) {
+    if (S <= 0 || T <= 0) return;
+    VCHECK(cudaSetDevice(device_));
+    const int NF = S * T;  // frames of the whole batch
+    ensure(NF);
+    ensure_segments(S);
     cudaStream_t s = stream_;
     const int nc = cfg_.nc, H = vc_.hidden, nh = vc_.n_head, nkv = vc_.n_kv, hd = vc_.hd, F = vc_.ffn;
     if (hd > 128 || hd % 32 || nh % nkv) throw std::runtime_error("vocoder: head_dim must be 32..128 (multiple of 32), heads a multiple of kv heads");
-    VCHECK(cudaMemcpyAsync(codes_, codes, (size_t) T * nc * sizeof(int), cudaMemcpyHostToDevice, s));
+    const bool streaming = segs != nullptr;
+    const int kvd = nkv * hd;
+    // per segment: stream slot, state copy, first position (whole decodes: 0, 1, ... / -1 / 0)
+    const int * d_slot = seg_ident_, * d_par = nullptr, * d_pos = seg_ident_ + seg_cap_;
+    if (streaming) {
+        if (!st_pool_) throw std::runtime_error("vocoder: stream state is not allocated");
+        if (T > ring_R_ - vc_.window + 1)
+            throw std::runtime_error("vocoder: at most " + std::to_string(ring_R_ - vc_.window + 1) + " new frames per stream and call");
+        std::vector<int> h((size_t) 3 * S);
+        for (int b = 0; b < S; b++) {
+            if (segs[b].pos + T > kMaxStreamFrames) throw std::runtime_error("vocoder: a stream passed " + std::to_string(kMaxStreamFrames) + " frames");
+            h[b] = segs[b].slot;
+            h[S + b] = segs[b].par;
+            h[2 * S + b] = segs[b].pos;
+        }
+        VCHECK(cudaMemcpyAsync(seg_dev_, h.data(), h.size() * sizeof(int), cudaMemcpyHostToDevice, s));
+        d_slot = seg_dev_;
+        d_par = seg_dev_ + S;
+        d_pos = seg_dev_ + 2 * S;
+    }
+    int li = 0;  // state layer of the next causal convolution (decode order, see the constructor)
 
-    // quantiser decode -> [T][cbdim] -> [cbdim][T]
-    half * e_first = f16_, * e_rest = f16_ + (size_t) T * dq_;
-    voc_embed_kernel<<<T, 128, 0, s>>>(emb_first_, emb_rest_[0], codes_, nc, nc, dq_, cfg_.vs, e_first, e_rest);
-    linear(dq_first_out_, e_first, dq_, T, GemvOut{ EPI_STORE, t32_, nullptr, cbdim_ }, s);
-    if (nc > 1) linear(dq_rest_out_, e_rest, dq_, T, GemvOut{ EPI_RESID, t32_, nullptr, cbdim_ }, s);
+    // quantiser decode -> [NF][cbdim] -> [cbdim][NF]
+    half * e_first = f16_, * e_rest = f16_ + (size_t) NF * dq_;
+    voc_embed_kernel<<<NF, 128, 0, s>>>(emb_first_, emb_rest_[0], codes_dev, ld_codes, nc, dq_, cfg_.vs, e_first, e_rest);
+    linear(dq_first_out_, e_first, dq_, NF, GemvOut{ EPI_STORE, t32_, nullptr, cbdim_ }, s);
+    if (nc > 1) linear(dq_rest_out_, e_rest, dq_, NF, GemvOut{ EPI_RESID, t32_, nullptr, cbdim_ }, s);
     auto transpose = [&](const float * in, int R, int C, float * out, const float * add) {
         voc_transpose_kernel<<<dim3((C + 31) / 32, (R + 31) / 32), dim3(32, 8), 0, s>>>(in, R, C, out, add);
     };
-    // one causal conv (or the phases of a transposed conv) over x [cin][L]; the output
-    // [cout][L * phases] holds v = conv + bias (+ res), or SnakeBeta(v) with (sa, sb); y2, when
+    // one causal conv (or the phases of a transposed conv) over x [cin][S seg]: S segments of
+    // `seg` steps, each continuing its stream's state of layer li when streaming. The output
+    // [cout][S seg phases] holds v = conv + bias (+ res), or SnakeBeta(v) with (sa, sb); y2, when
     // given, receives SnakeBeta(v) with (s2a, s2b)
     struct Act { const float * a = nullptr, * b = nullptr; };
-    auto conv = [&](const Conv & c, const float * x, int L, int dil, float * y, Act act = {}, const float * res = nullptr,
+    auto conv = [&](const Conv & c, const float * x, int seg, int dil, float * y, Act act = {}, const float * res = nullptr,
                     float * y2 = nullptr, Act act2 = {}, bool clamp = false) {
         ConvArgs ca;
-        ca.x = x; ca.cin = c.cin; ca.L = L;
+        ca.x = x; ca.cin = c.cin; ca.L = S * seg;
         ca.w = c.w; ca.taps = c.taps; ca.dil = dil;
         ca.bias = c.b; ca.cout = c.cout;
-        ca.y = y; ca.ldy = L * c.phases; ca.ostride = c.phases;
+        ca.y = y; ca.ldy = S * seg * c.phases; ca.ostride = c.phases;
         ca.res = res; ca.sa = act.a; ca.sb = act.b;
         ca.y2 = y2; ca.s2a = act2.a; ca.s2b = act2.b;
         ca.clamp = clamp ? 1 : 0;
+        ca.seg_len = seg;
+        if (streaming && (c.taps - 1) * dil > 0) {
+            ca.st = st_pool_ + st_off_[li];
+            ca.st_stride = st_floats_;
+            ca.seg_slot = d_slot;
+            ca.seg_par = d_par;
+        }
+        li++;
         launch_conv(ca, c.phases, part_, 2 * act_elems_, s);
     };
-    transpose(t32_, T, cbdim_, a_, nullptr);
-    conv(dpre_, a_, T, 1, b_);                                       // [latent][T]
+    transpose(t32_, NF, cbdim_, a_, nullptr);
+    conv(dpre_, a_, T, 1, b_);                                       // [latent][NF]
 
-    // transformer on [T][latent] rows
-    transpose(b_, latent_, T, a_, nullptr);                          // a_ = [T][latent]
-    voc_to_f16_kernel<<<grid_for((size_t) T * latent_), 256, 0, s>>>(a_, (size_t) T * latent_, t16_);
-    float * h = c_;                                                  // [T][H]
-    linear(in_proj_, t16_, latent_, T, GemvOut{ EPI_STORE, h, nullptr, H }, s);
-    voc_bias_scale_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, (size_t) T * H, H, in_proj_b_, nullptr);
+    // transformer on [NF][latent] rows; keys and values go to each segment's ring (a stream's
+    // own ring, or for whole decodes one of T positions per segment)
+    transpose(b_, latent_, NF, a_, nullptr);                         // a_ = [NF][latent]
+    voc_to_f16_kernel<<<grid_for((size_t) NF * latent_), 256, 0, s>>>(a_, (size_t) NF * latent_, t16_);
+    float * h = c_;                                                  // [NF][H]
+    linear(in_proj_, t16_, latent_, NF, GemvOut{ EPI_STORE, h, nullptr, H }, s);
+    voc_bias_scale_kernel<<<grid_for((size_t) NF * H), 256, 0, s>>>(h, (size_t) NF * H, H, in_proj_b_, nullptr);
     const float scale = 1.0f / std::sqrt((float) hd);
-    for (const Layer & Ly : layers_) {
-        launch_rmsnorm(h, H, Ly.attn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
-        linear(Ly.q, t16_, H, T, GemvOut{ EPI_STORE, q_, nullptr, nh * hd }, s);
-        linear(Ly.k, t16_, H, T, GemvOut{ EPI_STORE, k_, nullptr, nkv * hd }, s);
-        linear(Ly.v, t16_, H, T, GemvOut{ EPI_STORE, v_, nullptr, nkv * hd }, s);
-        const int warps = T * nh;
-        voc_attn_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, k_, v_, T, nh, nkv, hd, vc_.window, rope_, scale, att16_);
-        linear(Ly.o, att16_, nh * hd, T, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
-        voc_scaled_add_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, o_, (size_t) T * H, H, Ly.attn_scale);
-        launch_rmsnorm(h, H, Ly.ffn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
-        linear(Ly.gate, t16_, H, T, GemvOut{ EPI_STORE, g_, nullptr, F }, s);
-        linear(Ly.up, t16_, H, T, GemvOut{ EPI_STORE, u_, nullptr, F }, s);
-        voc_silu_mul_kernel<<<grid_for((size_t) T * F), 256, 0, s>>>(g_, u_, (size_t) T * F, t16_);
-        linear(Ly.down, t16_, F, T, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
-        voc_scaled_add_kernel<<<grid_for((size_t) T * H), 256, 0, s>>>(h, o_, (size_t) T * H, H, Ly.ffn_scale);
+    const float2 * rope = streaming ? srope_ : rope_;
+    const int R = streaming ? ring_R_ : T;
+    const size_t slot_stride = streaming ? (size_t) vc_.n_layer * ring_R_ * 2 * kvd : (size_t) T * 2 * kvd;
+    for (size_t l = 0; l < layers_.size(); l++) {
+        const Layer & Ly = layers_[l];
+        float * ring = streaming ? ring_ + l * (size_t) ring_R_ * 2 * kvd : fring_;
+        launch_rmsnorm(h, H, Ly.attn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
+        linear(Ly.q, t16_, H, NF, GemvOut{ EPI_STORE, q_, nullptr, nh * hd }, s);
+        linear(Ly.k, t16_, H, NF, GemvOut{ EPI_STORE, k_, nullptr, kvd }, s);
+        linear(Ly.v, t16_, H, NF, GemvOut{ EPI_STORE, v_, nullptr, kvd }, s);
+        voc_kv_ring_append_kernel<<<grid_for((size_t) NF * kvd), 256, 0, s>>>(k_, v_, S, T, nkv, hd, rope, ring, slot_stride,
+                                                                              R, d_slot, d_pos);
+        const int warps = NF * nh;
+        voc_attn_ring_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, S, T, nh, nkv, hd, vc_.window, rope, scale, ring,
+                                                                        slot_stride, R, d_slot, d_pos, att16_);
+        linear(Ly.o, att16_, nh * hd, NF, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
+        voc_scaled_add_kernel<<<grid_for((size_t) NF * H), 256, 0, s>>>(h, o_, (size_t) NF * H, H, Ly.attn_scale);
+        launch_rmsnorm(h, H, Ly.ffn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
+        linear(Ly.gate, t16_, H, NF, GemvOut{ EPI_STORE, g_, nullptr, F }, s);
+        linear(Ly.up, t16_, H, NF, GemvOut{ EPI_STORE, u_, nullptr, F }, s);
+        voc_silu_mul_kernel<<<grid_for((size_t) NF * F), 256, 0, s>>>(g_, u_, (size_t) NF * F, t16_);
+        linear(Ly.down, t16_, F, NF, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
+        voc_scaled_add_kernel<<<grid_for((size_t) NF * H), 256, 0, s>>>(h, o_, (size_t) NF * H, H, Ly.ffn_scale);
     }
-    launch_rmsnorm(h, H, out_norm_, H, vc_.eps, t16_, H, nullptr, 0, 0, T, nullptr, s);
-    linear(out_proj_, t16_, H, T, GemvOut{ EPI_STORE, o_, nullptr, latent_ }, s);
-    voc_bias_scale_kernel<<<grid_for((size_t) T * latent_), 256, 0, s>>>(o_, (size_t) T * latent_, latent_, out_proj_b_, nullptr);
-    transpose(o_, T, latent_, a_, nullptr);                          // a_ = [latent][T]
+    launch_rmsnorm(h, H, out_norm_, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
+    linear(out_proj_, t16_, H, NF, GemvOut{ EPI_STORE, o_, nullptr, latent_ }, s);
+    voc_bias_scale_kernel<<<grid_for((size_t) NF * latent_), 256, 0, s>>>(o_, (size_t) NF * latent_, latent_, out_proj_b_, nullptr);
+    transpose(o_, NF, latent_, a_, nullptr);                         // a_ = [latent][NF]
 
-    // ConvNeXt upsampling stages
+    // ConvNeXt upsampling stages (L: steps per segment, NL = S L rows in all)
     int L = T;
     float * x = a_;
     float * y = b_;
     for (const Up & u : ups_) {
         conv(u.up, x, L, 1, y);
         L *= u.ratio;
-        std::swap(x, y);                                             // x = [latent][L]
-        const size_t n = (size_t) L * latent_;
-        voc_depthwise_kernel<<<grid_for(n), 256, 0, s>>>(x, latent_, L, u.dw.w, u.dw.b, u.dw.K, y);
-        transpose(y, latent_, L, t32_, nullptr);                     // [L][latent]
-        voc_layernorm_kernel<<<L, 256, 0, s>>>(t32_, latent_, u.norm_w, u.norm_b, 1e-6f, t16_);
+        std::swap(x, y);                                             // x = [latent][S L]
+        const int NL = S * L;
+        const size_t n = (size_t) NL * latent_;
+        const bool dw_state = streaming && u.dw.K > 1;
+        voc_depthwise_seg_kernel<<<grid_for(n + (dw_state ? (size_t) S * latent_ * (u.dw.K - 1) : 0)), 256, 0, s>>>(
+            x, latent_, S, L, u.dw.w, u.dw.b, u.dw.K, y, dw_state ? st_pool_ + st_off_[li] : nullptr, st_floats_, d_slot, d_par);
+        li++;
+        transpose(y, latent_, NL, t32_, nullptr);                    // [S L][latent]
+        voc_layernorm_kernel<<<NL, 256, 0, s>>>(t32_, latent_, u.norm_w, u.norm_b, 1e-6f, t16_);
         const int F4 = u.pw1.M;
-        linear(u.pw1, t16_, latent_, L, GemvOut{ EPI_STORE, o_, nullptr, F4 }, s);
-        voc_bias_gelu_kernel<<<grid_for((size_t) L * F4), 256, 0, s>>>(o_, (size_t) L * F4, F4, u.pw1_b, f16_);
-        linear(u.pw2, f16_, F4, L, GemvOut{ EPI_STORE, t32_, nullptr, latent_ }, s);
+        linear(u.pw1, t16_, latent_, NL, GemvOut{ EPI_STORE, o_, nullptr, F4 }, s);
+        voc_bias_gelu_kernel<<<grid_for((size_t) NL * F4), 256, 0, s>>>(o_, (size_t) NL * F4, F4, u.pw1_b, f16_);
+        linear(u.pw2, f16_, F4, NL, GemvOut{ EPI_STORE, t32_, nullptr, latent_ }, s);
         voc_bias_scale_kernel<<<grid_for(n), 256, 0, s>>>(t32_, n, latent_, u.pw2_b, u.gamma);
-        transpose(t32_, L, latent_, y, x);                           // y = x + branch^T
+        transpose(t32_, NL, latent_, y, x);                          // y = x + branch^T
         std::swap(x, y);
     }
     // SEANet decoder (src/codec_decoder.cpp:80-97). Every SnakeBeta is applied by the conv that
     // produces its input: Xb holds a block's residual stream, Sb the SnakeBeta of it that the
     // next conv reads, Hb the first conv of a residual unit (already SnakeBeta'd for the second).
     // The second conv of a unit adds Xb in place and also writes the next activation into Sb.
+    // A stream's carried state of each conv is its own (already activated) input.
     float * Xb = c_, * Sb = y, * Hb = x;
     auto next_act = [&](size_t bi, int j) -> Act {
         if (j + 1 < 3) return { blks_[bi].res[j + 1].a1, blks_[bi].res[j + 1].b1 };
@@ -843,13 +1104,9 @@ void Vocoder::decode(const int * codes, int T, float * pcm) {
         }
     }
     if (L != T * kSamplesPerFrame) throw std::runtime_error("vocoder: unexpected output length");
-    conv(dfin_, Sb, L, 1, pcm_, {}, nullptr, nullptr, {}, true);
+    conv(dfin_, Sb, L, 1, pcm_dev, {}, nullptr, nullptr, {}, true);
+    if (li != (int) st_off_.size()) throw std::runtime_error("vocoder: state layers out of step with the decode");
     VCHECK(cudaGetLastError());
-    VCHECK(cudaMemcpyAsync(pcm, pcm_, (size_t) L * sizeof(float), cudaMemcpyDeviceToHost, s));
-    int err = 0;
-    VCHECK(cudaMemcpyAsync(&err, err_, sizeof(int), cudaMemcpyDeviceToHost, s));
-    VCHECK(cudaStreamSynchronize(s));
-    if (err) throw std::runtime_error("vocoder: a bounded wait timed out in the tcgen05 GEMM");
 }
 
 // ---------------------------------------------------------------------------------- sessions
@@ -879,20 +1136,167 @@ int Vocoder::session_decode(int sid, const int * frames, int n_frames, float * o
     return n_frames * spf;
 }
 
+// Every entry's history is taken before any is decoded and the histories are extended in batch
+// order afterwards, as in src/c_api.cpp:1066-1162. Entries of equal total length (history + new
+// frames) are decoded together as the segments of one batched decode.
 int Vocoder::session_decode_batch(int batch, const int * sids, const int * flat_tokens, const int * token_offsets,
                                   const int * n_frames, float * flat_pcm, const int * pcm_offsets, int * out_n_samples) {
-    int running_tok = 0, running_pcm = 0;
+    std::lock_guard<std::mutex> lk(mu_);
     const int nc = cfg_.nc, spf = kSamplesPerFrame;
+    std::vector<std::vector<int>> codes(batch);
+    std::vector<int> past(batch, 0), nfs(batch, 0), poffs(batch, 0);
+    std::map<int, std::vector<int>> groups;  // total frames -> entries
+    int running_tok = 0, running_pcm = 0;
     for (int b = 0; b < batch; b++) {
-        const int nf = n_frames[b];
+        const int nf = std::max(0, n_frames[b]);
         const int off = token_offsets ? token_offsets[b] : running_tok;
-        const int poff = pcm_offsets ? pcm_offsets[b] : running_pcm;
-        if (nf > 0) session_decode(sids[b], flat_tokens + off, nf, flat_pcm + poff);
-        if (out_n_samples) out_n_samples[b] = nf * spf;
+        poffs[b] = pcm_offsets ? pcm_offsets[b] : running_pcm;
+        const std::vector<int> & hist = history_[sids[b]];  // an unknown session is created (src/c_api.cpp:1085-1093)
+        past[b] = (int) hist.size() / nc;
+        nfs[b] = nf;
+        if (nf > 0) {
+            codes[b] = hist;
+            codes[b].insert(codes[b].end(), flat_tokens + off, flat_tokens + off + (size_t) nf * nc);
+            groups[past[b] + nf].push_back(b);
+        }
         running_tok += nf * nc;
         running_pcm += nf * spf;
     }
+    std::vector<int> hc;
+    std::vector<float> audio;
+    for (const auto & kv : groups) {
+        const int T = kv.first, S = (int) kv.second.size();
+        hc.resize((size_t) S * T * nc);
+        for (int i = 0; i < S; i++) std::copy(codes[kv.second[i]].begin(), codes[kv.second[i]].end(), hc.begin() + (size_t) i * T * nc);
+        ensure(S * T);
+        VCHECK(cudaMemcpyAsync(codes_, hc.data(), hc.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        decode_segments(codes_, nc, S, T, nullptr, pcm_);
+        audio.resize((size_t) S * T * spf);
+        VCHECK(cudaMemcpyAsync(audio.data(), pcm_, audio.size() * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        check_device_error();
+        for (int i = 0; i < S; i++) {
+            const int b = kv.second[i];
+            std::memcpy(flat_pcm + poffs[b], audio.data() + ((size_t) i * T + past[b]) * spf, (size_t) nfs[b] * spf * sizeof(float));
+        }
+    }
+    for (int b = 0; b < batch; b++) {
+        if (out_n_samples) out_n_samples[b] = nfs[b] * spf;
+        if (nfs[b] == 0) continue;
+        std::vector<int> & hist = history_[sids[b]];
+        hist.insert(hist.end(), codes[b].begin() + (size_t) past[b] * nc, codes[b].end());
+        const int cur = (int) hist.size() / nc;
+        if (cur > kMaxHistory) hist.erase(hist.begin(), hist.begin() + (size_t) (cur - kMaxHistory) * nc);
+    }
     return batch;
+}
+
+// ----------------------------------------------------------------------------------- streams
+void Vocoder::ensure_streams() {
+    if (st_pool_) return;
+    VCHECK(cudaSetDevice(device_));
+    const char * e = std::getenv("BZB_VOC_STREAMS");
+    stream_cap_ = e ? std::max(1, std::atoi(e)) : 256;
+    // a stream's ring keeps the attention window plus one call's new frames (at most 56)
+    ring_R_ = (vc_.window + 56 + 7) / 8 * 8;
+    const size_t kvd = (size_t) vc_.n_kv * vc_.hd;
+    auto alloc = [&](size_t bytes) {
+        void * p = nullptr;
+        VCHECK(cudaMalloc(&p, std::max<size_t>(bytes, 16)));
+        stream_allocs_.push_back(p);
+        return p;
+    };
+    st_pool_ = (float *) alloc((size_t) stream_cap_ * st_floats_ * sizeof(float));
+    ring_ = (float *) alloc((size_t) stream_cap_ * vc_.n_layer * ring_R_ * 2 * kvd * sizeof(float));
+    const std::vector<float2> tab = rope_table(kMaxStreamFrames, vc_.hd, vc_.theta, 1.0f, nullptr);
+    srope_ = (float2 *) alloc(tab.size() * sizeof(float2));
+    VCHECK(cudaMemcpyAsync(srope_, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream_));
+    VCHECK(cudaStreamSynchronize(stream_));
+    for (int i = stream_cap_ - 1; i >= 0; i--) free_slots_.push_back(i);
+}
+
+void Vocoder::stream_open(int id) {
+    std::lock_guard<std::mutex> lk(mu_);
+    ensure_streams();
+    auto it = streams_.find(id);
+    if (it != streams_.end()) {
+        it->second.pos = 0;
+        it->second.par = -1;
+        return;
+    }
+    if (free_slots_.empty()) throw std::runtime_error("vocoder: all " + std::to_string(stream_cap_) + " stream slots are in use (BZB_VOC_STREAMS)");
+    StreamInfo si;
+    si.slot = free_slots_.back();
+    free_slots_.pop_back();
+    streams_[id] = si;
+}
+
+bool Vocoder::stream_close(int id) {
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = streams_.find(id);
+    if (it == streams_.end()) return false;
+    free_slots_.push_back(it->second.slot);
+    streams_.erase(it);
+    return true;
+}
+
+std::vector<Vocoder::Segment> Vocoder::stream_segments(int n, const int * ids, const unsigned long long * epochs, int T) {
+    ensure_streams();
+    std::vector<Segment> segs(n);
+    std::map<int, int> seen;
+    for (int i = 0; i < n; i++) {
+        if (!seen.emplace(ids[i], i).second) throw std::runtime_error("vocoder: stream " + std::to_string(ids[i]) + " listed twice in one call");
+        auto it = streams_.find(ids[i]);
+        if (it == streams_.end()) {
+            if (free_slots_.empty()) throw std::runtime_error("vocoder: all " + std::to_string(stream_cap_) + " stream slots are in use (BZB_VOC_STREAMS)");
+            StreamInfo si;
+            si.slot = free_slots_.back();
+            free_slots_.pop_back();
+            if (epochs) si.epoch = epochs[i];
+            it = streams_.emplace(ids[i], si).first;
+        } else if (epochs && it->second.epoch != epochs[i]) {
+            it->second.pos = 0;
+            it->second.par = -1;
+            it->second.epoch = epochs[i];
+        }
+        if (it->second.pos + T > kMaxStreamFrames)
+            throw std::runtime_error("vocoder: stream " + std::to_string(ids[i]) + " would pass " + std::to_string(kMaxStreamFrames) + " frames");
+        segs[i].slot = it->second.slot;
+        segs[i].par = it->second.par;
+        segs[i].pos = it->second.pos;
+    }
+    return segs;
+}
+
+void Vocoder::advance(int n, const int * ids, int T) {
+    for (int i = 0; i < n; i++) {
+        StreamInfo & si = streams_[ids[i]];
+        si.pos += T;
+        si.par = voc_state_next(si.par);
+    }
+}
+
+void Vocoder::streams_decode(int n, const int * ids, const unsigned long long * epochs, const int * codes, int T,
+                             float * pcm) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (n <= 0 || T <= 0) return;
+    VCHECK(cudaSetDevice(device_));
+    const std::vector<Segment> segs = stream_segments(n, ids, epochs, T);
+    ensure(n * T);
+    VCHECK(cudaMemcpyAsync(codes_, codes, (size_t) n * T * cfg_.nc * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    decode_segments(codes_, cfg_.nc, n, T, segs.data(), pcm_);
+    advance(n, ids, T);
+    VCHECK(cudaMemcpyAsync(pcm, pcm_, (size_t) n * T * kSamplesPerFrame * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    check_device_error();
+}
+
+void Vocoder::streams_decode_device(int n, const int * ids, const unsigned long long * epochs, const int * codes_dev,
+                                   int ld_codes, int T, float * pcm_dev) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (n <= 0 || T <= 0) return;
+    const std::vector<Segment> segs = stream_segments(n, ids, epochs, T);
+    ensure(n * T);
+    decode_segments(codes_dev, ld_codes, n, T, segs.data(), pcm_dev ? pcm_dev : pcm_);
+    advance(n, ids, T);
 }
 
 int Vocoder::stream_decode(const int * frames, int n_frames, float * out_pcm) {
@@ -904,16 +1308,34 @@ int Vocoder::stream_decode(const int * frames, int n_frames, float * out_pcm) {
 int Vocoder::stream_decode_batch(int batch, const int * flat_tokens, const int * token_offsets, const int * n_frames,
                                  float * flat_pcm, const int * pcm_offsets, int * out_n_samples) {
     std::lock_guard<std::mutex> lk(mu_);
-    int running_tok = 0, running_pcm = 0;
     const int nc = cfg_.nc, spf = kSamplesPerFrame;
+    std::map<int, std::vector<int>> groups;  // frames -> entries, decoded as segments of one batch
+    std::vector<int> toks(batch), poffs(batch), nfs(batch);
+    int running_tok = 0, running_pcm = 0;
     for (int b = 0; b < batch; b++) {
-        const int nf = n_frames[b];
-        const int off = token_offsets ? token_offsets[b] : running_tok;
-        const int poff = pcm_offsets ? pcm_offsets[b] : running_pcm;
-        if (nf > 0) decode(flat_tokens + off, nf, flat_pcm + poff);
-        if (out_n_samples) out_n_samples[b] = nf * spf;
-        running_tok += nf * nc;
-        running_pcm += nf * spf;
+        nfs[b] = std::max(0, n_frames[b]);
+        toks[b] = token_offsets ? token_offsets[b] : running_tok;
+        poffs[b] = pcm_offsets ? pcm_offsets[b] : running_pcm;
+        if (nfs[b] > 0) groups[nfs[b]].push_back(b);
+        if (out_n_samples) out_n_samples[b] = nfs[b] * spf;
+        running_tok += nfs[b] * nc;
+        running_pcm += nfs[b] * spf;
+    }
+    std::vector<int> hc;
+    std::vector<float> audio;
+    for (const auto & kv : groups) {
+        const int T = kv.first, S = (int) kv.second.size();
+        hc.resize((size_t) S * T * nc);
+        for (int i = 0; i < S; i++)
+            std::memcpy(hc.data() + (size_t) i * T * nc, flat_tokens + toks[kv.second[i]], (size_t) T * nc * sizeof(int));
+        ensure(S * T);
+        VCHECK(cudaMemcpyAsync(codes_, hc.data(), hc.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        decode_segments(codes_, nc, S, T, nullptr, pcm_);
+        audio.resize((size_t) S * T * spf);
+        VCHECK(cudaMemcpyAsync(audio.data(), pcm_, audio.size() * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        check_device_error();
+        for (int i = 0; i < S; i++)
+            std::memcpy(flat_pcm + poffs[kv.second[i]], audio.data() + (size_t) i * T * spf, (size_t) T * spf * sizeof(float));
     }
     return batch;
 }

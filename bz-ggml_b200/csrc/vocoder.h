@@ -15,15 +15,50 @@ namespace bzb {
 
 class Vocoder {
 public:
-    // loads the `codec.*` tensors of an open GGUF onto `device`
-    Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device);
+    // loads the `codec.*` tensors of an open GGUF onto `device`; with `stream` every kernel runs on
+    // that stream (a generator's, so that decodes are ordered after its frame steps), otherwise on
+    // a stream of its own
+    Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaStream_t stream = nullptr);
     ~Vocoder();
 
     static constexpr int kSamplesPerFrame = 1920;  // a constant of the reference C API
     static constexpr int kMaxHistory = 32;          // frames kept per session for the causal lookback
+    static constexpr int kMaxStreamFrames = 8192;   // positions a stream can reach (its RoPE table)
 
     // codes frame-major [T][nc] (host) -> PCM [T * 1920] (host), clamped to [-1, 1]
     void decode(const int * codes, int T, float * pcm);
+
+    // One segment of a batched decode: the stream slot whose carried state continues, the copy of
+    // its state to read (-1: a new stream, zero state) and its first frame's position.
+    struct Segment { int slot = 0, par = -1, pos = 0; };
+    // S segments of T frames each decoded as one batch on the device (every linear one GEMM over
+    // all S T frames, every convolution one launch), asynchronously on the vocoder's stream:
+    // codes_dev rows [S T][ld_codes] ints, segment-major; pcm_dev [S][T 1920]. segs null: each
+    // segment is a whole decode (zero left context, positions 0..T-1); otherwise segs[b] continues
+    // that stream, whose state for the next call is then written to copy voc-state-next(par).
+    void decode_segments(const int * codes_dev, int ld_codes, int S, int T, const Segment * segs, float * pcm_dev);
+
+    // Streams (no counterpart in the reference): per-stream carried state -- every causal
+    // convolution's last inputs and the transformer's keys and values of the last `window`
+    // positions -- so that each call decodes only its new frames and the PCM equals that of one
+    // decode of the stream's whole history. Opening an id resets its stream.
+    void stream_open(int id);
+    bool stream_close(int id);
+    int stream_count() const { return (int) streams_.size(); }
+    // T new frames for each of n distinct streams: codes [n][T][nc] (host) -> pcm [n][T 1920]
+    // (host); unknown ids are opened; epochs (optional) as for streams_decode_device
+    void streams_decode(int n, const int * ids, const unsigned long long * epochs, const int * codes, int T, float * pcm);
+    // the same on device buffers without a host synchronisation: stream i's frames are rows
+    // i T .. i T + T - 1 of codes_dev (row stride ld_codes ints); pcm_dev null: the vocoder's own
+    // buffer (last_pcm()); when epochs is given, a stream whose stored epoch differs from
+    // epochs[i] starts over (its session was created again)
+    void streams_decode_device(int n, const int * ids, const unsigned long long * epochs, const int * codes_dev,
+                              int ld_codes, int T, float * pcm_dev);
+    const float * last_pcm() const { return pcm_; }
+    // reads the device error word after the calls so far (a bounded wait timed out when it is
+    // nonzero: it is cleared and the failure thrown)
+    void check_device_error();
+    cudaStream_t stream() const { return stream_; }
 
     // reference session API (breeze_vocoder_session_*); every call serialised on one mutex
     void session_create(int sid);
@@ -39,6 +74,16 @@ public:
     int device() const { return device_; }
 
 private:
+    struct StreamInfo {
+        int slot = 0, par = -1, pos = 0;
+        unsigned long long epoch = 0;
+    };
+    void ensure_streams();
+    void ensure_segments(int S);
+    // the segments of n stream ids for T new frames (opening unknown ids; with epochs, restarting
+    // streams whose epoch changed); advance() moves them past the decoded frames
+    std::vector<Segment> stream_segments(int n, const int * ids, const unsigned long long * epochs, int T);
+    void advance(int n, const int * ids, int T);
     struct Conv {
         // [phases][Cout][taps][Cin] (tap-major): a conv has one phase of K taps; a stride-s
         // transposed conv has s phases of ceil(K / s) taps (depthwise: [K][C])
@@ -82,6 +127,7 @@ private:
     VocConfig vc_;
     int device_ = 0;
     cudaStream_t stream_ = nullptr;
+    bool own_stream_ = true;
     std::vector<void *> allocs_;
     std::vector<void *> scratch_allocs_;
 
@@ -110,6 +156,22 @@ private:
     float * part_ = nullptr;  // channel-split partial sums of the convolutions
     half * t16_ = nullptr, * att16_ = nullptr, * f16_ = nullptr;
     int * codes_ = nullptr;
+    float * fring_ = nullptr;  // keys and values of whole-decode segments [S][T][2][kv dim]
+
+    // streams: carried convolution states [slot][st_floats_] (every state layer's [2][cin][P] at
+    // st_off_[layer], in decode order), key/value rings [slot][layer][ring_R_][2][kv dim]
+    std::map<int, StreamInfo> streams_;
+    std::vector<int> free_slots_;
+    int stream_cap_ = 0;
+    std::vector<size_t> st_off_;
+    size_t st_floats_ = 0;
+    float * st_pool_ = nullptr, * ring_ = nullptr;
+    int ring_R_ = 0;
+    float2 * srope_ = nullptr;  // RoPE table for kMaxStreamFrames positions
+    int * seg_dev_ = nullptr;   // [3][seg_cap_]: slot, copy, first position of each segment
+    int * seg_ident_ = nullptr; // [2][seg_cap_]: 0, 1, 2, ... and zeros (whole-decode segments)
+    int seg_cap_ = 0;
+    std::vector<void *> stream_allocs_;
 
     std::mutex mu_;
     std::map<int, std::vector<int>> history_;

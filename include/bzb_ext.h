@@ -68,6 +68,42 @@ BREEZE_API int bzb_generator_debug_gemv(breeze_generator * gen, const char * ten
 BREEZE_API long long bzb_generator_debug_gemm(breeze_generator * gen, const char * name, int rows, const float * x,
                                               float * y, int repeats, int flags, int * out_where, int where_cap);
 
+/* Streaming PCM (no counterpart in the reference, whose vocoder sessions re-decode up to 32
+   frames of history with every call, src/c_api.cpp:1004-1162). A stream carries the codec
+   decoder's causal state from call to call -- the last inputs of every causal convolution and
+   the transformer's keys and values over its attention window -- so each call decodes only its
+   new frames, and the PCM of a stream equals that of one decode of all its frames at once. Calls
+   for many streams run as one batch: every linear is one GEMM and every convolution one launch
+   over all of them. A vocoder holds up to BZB_VOC_STREAMS streams (default 256; about 5 MB of
+   device memory each, allocated with the first stream) of at most 8192 frames, and takes at
+   most 56 new frames per stream and call.
+   bzb_vocoder_stream_open starts (or restarts) a stream; bzb_vocoder_stream_close releases it
+   (-1 when unknown). bzb_vocoder_streams_decode decodes n_frames new frames of each of n
+   distinct streams: codes [n][n_frames][num_codebooks], out_pcm [n][n_frames * 1920] (host
+   buffers); unknown ids are opened. Returns n, or -1 with breeze_last_error(). */
+BREEZE_API int bzb_vocoder_stream_open(breeze_vocoder * voc, int stream_id);
+BREEZE_API int bzb_vocoder_stream_close(breeze_vocoder * voc, int stream_id);
+BREEZE_API int bzb_vocoder_streams_decode(breeze_vocoder * voc, int n, const int * stream_ids, const int * codes,
+                                          int n_frames, float * out_pcm);
+
+/* One serving step: breeze_generator_sessions_step_burst for one frame (full-width frames) and
+   the PCM of every new frame, decoded on the stream of its session id (restarted whenever a
+   session with that id is created). voc must come from breeze_vocoder_create_from_generator of
+   this generator. out_frames [n][num_codebooks] (optional; -1 rows for sessions that did not
+   step), out_next_cb0 [n], out_pcm [n][1920] (optional; zero rows for sessions that did not
+   step). Returns the number of sessions still active, or -1 with breeze_last_error(). */
+BREEZE_API int bzb_generator_sessions_step_pcm(breeze_generator * gen, breeze_vocoder * voc, const int * session_ids,
+                                               int n, const unsigned int * seeds, int * out_frames, int * out_next_cb0,
+                                               float * out_pcm);
+/* The same steps resident on the device (timing and serving loops that keep PCM on the GPU):
+   burst_steps frame steps of the listed sessions, each followed by the streaming decode of the
+   new frames, with no host copies and no synchronisation. Every listed session must be active.
+   The last step's PCM stays in the vocoder ([n][1920]; bzb_vocoder_last_pcm copies it out after
+   synchronising). Returns 0, or -1 with breeze_last_error(). */
+BREEZE_API int bzb_generator_step_pcm_device(breeze_generator * gen, breeze_vocoder * voc, const int * session_ids,
+                                             int n, const unsigned int * seeds, int burst_steps);
+BREEZE_API int bzb_vocoder_last_pcm(breeze_vocoder * voc, float * out, int n_samples);
+
 /* Tests of the bounded device waits (no reference counterpart). Every spin-wait in the kernels
    gives up after a poll limit, records an error code, lets the copies and MMAs it issued land,
    frees its tensor memory and returns; the host then reports the code and clears it.
