@@ -111,6 +111,7 @@ SIGNATURES = {
     "bzb_vocoder_streams_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _c_int_p, _c_int_p, ctypes.c_int,
                                                   _c_float_p]),
     "bzb_vocoder_last_pcm": (ctypes.c_int, [ctypes.c_void_p, _c_float_p, ctypes.c_int]),
+    "bzb_vocoder_kernels_per_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
     "bzb_generator_sessions_step_pcm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _c_int_p, ctypes.c_int,
                                                        _c_uint_p, _c_int_p, _c_int_p, _c_float_p]),
     "bzb_generator_step_pcm_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _c_int_p, ctypes.c_int,
@@ -572,6 +573,12 @@ class VocoderHandle:
         if self.lib.lib.bzb_vocoder_streams_decode(self.handle, n, _ip(ids), _ip(c), T, _fp(out)) != n:
             raise RuntimeError(f"streams_decode failed: {self.lib.last_error()}")
         return out
+
+    def kernels_per_decode(self, n_streams: int, n_frames: int) -> int:
+        n = self.lib.lib.bzb_vocoder_kernels_per_decode(self.handle, n_streams, n_frames)
+        if n < 0:
+            raise RuntimeError(self.lib.last_error())
+        return n
 
     def last_pcm(self, n_samples: int) -> np.ndarray:
         """The PCM the last device-resident step left in the vocoder (synchronises)."""

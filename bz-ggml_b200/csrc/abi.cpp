@@ -742,6 +742,16 @@ int bzb_vocoder_streams_decode(breeze_vocoder * voc, int n, const int * stream_i
     }
 }
 
+int bzb_vocoder_kernels_per_decode(breeze_vocoder * voc, int n_streams, int n_frames) {
+    if (!voc || n_streams <= 0 || n_frames <= 0) return -1;
+    try {
+        return voc->voc->kernels_per_decode(n_streams, n_frames);
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 int bzb_vocoder_last_pcm(breeze_vocoder * voc, float * out, int n_samples) {
     if (!voc || !out || n_samples < 0) return -1;
     try {

@@ -1190,6 +1190,37 @@ int Vocoder::session_decode_batch(int batch, const int * sids, const int * flat_
     return batch;
 }
 
+int Vocoder::kernels_per_decode(int S, int T) {
+    std::lock_guard<std::mutex> lk(mu_);
+    VCHECK(cudaSetDevice(device_));
+    ensure(S * T);
+    ensure_segments(S);
+    for (int i = 0; i < 2; i++) decode_segments(codes_, cfg_.nc, S, T, nullptr, pcm_);  // attributes and capacity settled
+    VCHECK(cudaStreamSynchronize(stream_));
+    cudaGraph_t g = nullptr;
+    VCHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+        decode_segments(codes_, cfg_.nc, S, T, nullptr, pcm_);
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    VCHECK(cudaStreamEndCapture(stream_, &g));
+    size_t n = 0;
+    VCHECK(cudaGraphGetNodes(g, nullptr, &n));
+    std::vector<cudaGraphNode_t> nodes(n);
+    VCHECK(cudaGraphGetNodes(g, nodes.data(), &n));
+    int kernels = 0;
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        VCHECK(cudaGraphNodeGetType(nd, &t));
+        kernels += t == cudaGraphNodeTypeKernel;
+    }
+    cudaGraphDestroy(g);
+    return kernels;
+}
+
 // ----------------------------------------------------------------------------------- streams
 void Vocoder::ensure_streams() {
     if (st_pool_) return;

@@ -55,6 +55,9 @@ public:
     void streams_decode_device(int n, const int * ids, const unsigned long long * epochs, const int * codes_dev,
                               int ld_codes, int T, float * pcm_dev);
     const float * last_pcm() const { return pcm_; }
+    // kernels one batched decode of S segments of T frames launches (counted from a captured,
+    // never launched graph of a whole-decode call; a streaming call launches the same ones)
+    int kernels_per_decode(int S, int T);
     // reads the device error word after the calls so far (a bounded wait timed out when it is
     // nonzero: it is cleared and the failure thrown)
     void check_device_error();

@@ -103,6 +103,8 @@ BREEZE_API int bzb_generator_sessions_step_pcm(breeze_generator * gen, breeze_vo
 BREEZE_API int bzb_generator_step_pcm_device(breeze_generator * gen, breeze_vocoder * voc, const int * session_ids,
                                              int n, const unsigned int * seeds, int burst_steps);
 BREEZE_API int bzb_vocoder_last_pcm(breeze_vocoder * voc, float * out, int n_samples);
+/* kernels one batched decode of n_streams streams x n_frames frames launches, or -1 */
+BREEZE_API int bzb_vocoder_kernels_per_decode(breeze_vocoder * voc, int n_streams, int n_frames);
 
 /* Tests of the bounded device waits (no reference counterpart). Every spin-wait in the kernels
    gives up after a poll limit, records an error code, lets the copies and MMAs it issued land,
