@@ -1964,8 +1964,17 @@ void Engine::gemm_noalloc(const char * tensor, int rows, const half * x16, int l
     if (!w->qs) throw std::runtime_error("gemm_noalloc: the allocation-free GEMV serves Q8_0 matrices only");
     if (ldx < w->K || (ldx & 1) || (reinterpret_cast<uintptr_t>(x16) & 3) || (reinterpret_cast<uintptr_t>(y) & 3))
         throw std::runtime_error("gemm_noalloc: x must be 4-byte aligned with an even stride >= K, y 4-byte aligned");
+    // the caller's current device is restored on return
+    int prev = 0;
+    CK(cudaGetDevice(&prev));
     CK(cudaSetDevice(device));
-    launch_gemv_static_scratch(*w, x16, ldx, rows, y, ldy, s ? s : stream_);
+    try {
+        launch_gemv_static_scratch(*w, x16, ldx, rows, y, ldy, s ? s : stream_);
+    } catch (...) {
+        cudaSetDevice(prev);
+        throw;
+    }
+    CK(cudaSetDevice(prev));
 }
 
 size_t Engine::weight_bytes_per_step() const {

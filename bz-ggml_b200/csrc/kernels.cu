@@ -1757,7 +1757,7 @@ void init_kernel_attributes() {
 }
 
 void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out,
-                 const GemvScratch & scr, cudaStream_t s) {
+                 const GemvScratch & scr, cudaStream_t s, bool fit_scratch) {
     if (rows <= 0) return;
     if (ldx % 2 != 0 || w.K % 32 != 0) throw std::runtime_error("gemv: activation stride or K not aligned");
     const int chunks = (rows + 63) / 64;
@@ -1768,9 +1768,16 @@ void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const Gemv
     const int wave = 2 * 148;
     int splits = std::max(1, wave / (MG * chunks));
     splits = std::min(splits, std::min(kMaxSplits, std::max(1, w.KB / kSub)));
-    if (const char * e = std::getenv("BZB_GEMV_SPLITS")) splits = std::max(1, std::min(kMaxSplits, std::atoi(e)));
+    const char * e = fit_scratch ? nullptr : std::getenv("BZB_GEMV_SPLITS");
+    if (e) splits = std::max(1, std::min(kMaxSplits, std::atoi(e)));
     int kper = (w.KB + splits - 1) / splits;
     splits = (w.KB + kper - 1) / kper;
+    // a fixed scratch: fewer splits until the partials and the tile counters fit
+    while (fit_scratch && splits > 1 && ((size_t) chunks * splits * w.MT * NT * 32 > scr.ws_elems ||
+                                         (size_t) chunks * MG > (size_t) scr.n_counters)) {
+        kper = (w.KB + splits - 2) / (splits - 1);
+        splits = (w.KB + kper - 1) / kper;
+    }
     if (splits > 1 && (size_t) chunks * splits * w.MT * NT * 32 > scr.ws_elems) throw std::runtime_error("gemv: split-K scratch too small");
     if (splits > 1 && (size_t) chunks * MG > (size_t) scr.n_counters) throw std::runtime_error("gemv: counter scratch too small");
     GemvParams p;
@@ -1836,8 +1843,9 @@ void launch_gemv_static_scratch(const QMat & w, const half * x16, int ldx, int r
     // tile counters must start at zero; a launch that did not finish could have left them set
     const size_t n_ctr = std::min((size_t) kStaticGemvCounters, (size_t) ((rows + 63) / 64) * ((w.MT + 7) / 8));
     BZB_CUDA_CHECK(cudaMemsetAsync(scr.counters, 0, n_ctr * sizeof(int), s));
-    // launch_gemv rejects a split plan that does not fit the scratch before launching anything
-    launch_gemv(w, x16, ldx, rows, GemvOut{ EPI_STORE, y, nullptr, ldy }, scr, s);
+    // the split plan is reduced to what the fixed scratch holds (BZB_GEMV_SPLITS does not apply);
+    // a plan that still cannot fit is rejected before anything is launched
+    launch_gemv(w, x16, ldx, rows, GemvOut{ EPI_STORE, y, nullptr, ldy }, scr, s, true);
 }
 
 void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s) {

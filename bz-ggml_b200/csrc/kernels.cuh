@@ -90,8 +90,10 @@ void init_kernel_attributes();
 void set_pdl_scope(bool on);
 
 // y[rows, M] = x16[rows, K] . W^T with the chosen epilogue; rows may exceed 64 (column chunks)
+// fit_scratch: choose at most the split-K plan `scr` holds (the allocation-free entry point's
+// fixed scratch) and ignore the BZB_GEMV_SPLITS override
 void launch_gemv(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out,
-                 const GemvScratch & scr, cudaStream_t s);
+                 const GemvScratch & scr, cudaStream_t s, bool fit_scratch = false);
 
 void repack_q8(const uint8_t * raw_dev, int M, int K, uint4 * qs, half2 * ds, cudaStream_t s);
 

@@ -8,6 +8,7 @@
 // shared memory.
 #include "vocoder.h"
 #include "rope.h"
+#include "tc_ptx.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -313,6 +314,223 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
     }
 }
 
+// The decoder's convolutions on the 5th-generation tensor cores (tcgen05): an implicit GEMM with
+// the time steps as M (128 per CTA), the output channels as N (a tile of nt <= 256) and
+// (64-channel chunk, tap) pairs as K steps of 64. Per chunk, the 8 producer warps stage the
+// chunk's input window time-major as f16 (128-byte rows of 64 channels, the 16-byte pieces of
+// row u XOR-swizzled by u mod 8), with each segment's state in front of its steps exactly as the
+// TF32 kernel stages it; for every tap they then copy the 128 rows that tap reads -- a row shift
+// of (taps-1-k) dil -- into a 128-byte-swizzled K-major A stage. One thread streams the f16 weight
+// tiles (pre-tiled at load, one bulk copy of nt x 128 bytes per K step) into the B ring, one
+// issues four tcgen05.mma kind::f16 (128 x nt x 16) per K step into a TMEM accumulator, and the
+// producers finally read the accumulator back and apply the same epilogue (bias, residual,
+// SnakeBeta of the stored value and of a second copy, PCM clamp). Every wait is bounded; after a
+// failed wait a role stops, the loader lets its copies land and the MMA thread its MMAs before
+// shared and tensor memory are released.
+constexpr int kTM = 128;             // time steps per CTA (MMA M)
+constexpr int kTThreads = 320;       // warps 0-7 producers and epilogue, 8 MMA, 9 weight loader
+constexpr int kTAB = kTM * 128;      // one A stage: 128 rows x 64 f16
+constexpr int kTSmemMax = 226 * 1024;  // the 227 KB opt-in limit covers static shared memory too
+
+struct TcConv {
+    ConvArgs a;                      // geometry, epilogue, segments and states (istride 1)
+    const half * w16 = nullptr;      // [phases][otiles][kchunks][taps] tiles of nt x 64 f16
+    int nt = 0, otiles = 0, kchunks = 0;
+    int win_rows = 0;                // window capacity (rows of 64 f16)
+    int a_stages = 3, b_stages = 3;  // at most 4 each
+    int * err = nullptr;
+};
+
+__device__ __forceinline__ void bar_producers() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_constant__ TcConv p) {
+    using namespace tc;
+    const ConvArgs & a = p.a;
+    extern __shared__ uint8_t tsm_raw[];
+    __shared__ uint64_t a_full[4], a_empty[4], b_full[4], b_empty[4], done_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int s_abort;
+    uint8_t * sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t) 1023);
+    uint8_t * sA = sm;
+    uint8_t * sB = sA + p.a_stages * kTAB;
+    const uint32_t tb = (uint32_t) p.nt * 128;
+    uint8_t * sW = sB + p.b_stages * tb;
+    int * wseg = reinterpret_cast<int *>(sW + (size_t) p.win_rows * 128);
+    int * wtau = wseg + p.win_rows;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int phase = blockIdx.z, ot = blockIdx.y;
+    const int t0 = blockIdx.x * kTM;
+    const int halo = (a.taps - 1) * a.dil;
+    const int seg = a.seg_len > 0 ? a.seg_len : a.L;
+    const int n_last = min(t0 + kTM, a.L) - 1;
+    const int b_first = t0 / seg;
+    const int wbeg = t0 + halo * b_first;
+    const int lx = n_last + halo * (n_last / seg) + halo - wbeg + 1;
+    const int AS = p.a_stages, BS = p.b_stages;
+    const int n_it = p.kchunks * a.taps;
+    const uint32_t cols = p.nt <= 32 ? 32u : p.nt <= 64 ? 64u : p.nt <= 128 ? 128u : 256u;
+    const uint32_t idesc = (1u << 4) | ((uint32_t) (p.nt >> 3) << 17) | ((uint32_t) (kTM >> 4) << 24);
+
+    if (warp == 8) tmem_alloc(&tmem_slot, cols);
+    if (tid == 0) {
+        for (int i = 0; i < AS; i++) {
+            mbar_init(&a_full[i], 256);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < BS; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        mbar_init(&done_bar, 1);
+        fence_mbar_init();
+        s_abort = 0;
+    }
+    for (int u = tid; u < lx; u += kTThreads) {
+        const int v = wbeg + u, b = v / (halo + seg);
+        wseg[u] = b;
+        wtau[u] = v - b * (halo + seg) - halo;
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+
+    if (warp < 8) {
+        // copies per tap: rows r = tid / 8 + 32 m (m < 4), 16-byte piece j = tid mod 8
+        const int j = tid & 7;
+        int cb[4];
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const int n = min(t0 + (tid >> 3) + 32 * m, a.L - 1);
+            cb[m] = n + halo * (n / seg) - wbeg;
+        }
+        int it = 0;
+        for (int c = 0; c < p.kchunks; c++) {
+            bar_producers();  // every producer is done with the previous window
+            if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+            // the chunk's window: piece jj (8 channels) of row u; a warp's lanes take consecutive rows
+            for (int e = tid; e < 8 * lx; e += 256) {
+                const int jj = e / lx, u = e - jj * lx;
+                const int b = wseg[u], tau = wtau[u];
+                const int par = tau < 0 && a.st && b * seg < a.L ? a.seg_par[b] : -1;
+                const float * stp = par >= 0 ? a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) par * a.cin * halo : nullptr;
+                const int t = b * seg + tau;
+                uint32_t w[4];
+#pragma unroll
+                for (int q = 0; q < 8; q += 2) {
+                    float f0 = 0.0f, f1 = 0.0f;
+                    const int ci = c * 64 + jj * 8 + q;
+                    if (tau < 0) {
+                        if (stp) {
+                            if (ci < a.cin) f0 = stp[(size_t) ci * halo + tau + halo];
+                            if (ci + 1 < a.cin) f1 = stp[(size_t) (ci + 1) * halo + tau + halo];
+                        }
+                    } else if (t < a.L) {
+                        if (ci < a.cin) f0 = a.x[(size_t) ci * a.L + t];
+                        if (ci + 1 < a.cin) f1 = a.x[(size_t) (ci + 1) * a.L + t];
+                    }
+                    const half2 h2 = __floats2half2_rn(f0, f1);
+                    w[q / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+                }
+                *reinterpret_cast<uint4 *>(sW + (size_t) u * 128 + ((jj ^ (u & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            bar_producers();  // the window is complete
+            if (a.st && halo > 0 && ot == 0 && phase == 0) {
+                // segments whose last step is in this tile: the new state of this chunk's channels
+                for (int b = b_first; b * seg + seg - 1 <= n_last; b++) {
+                    float * dst = a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) voc_state_next(a.seg_par[b]) * a.cin * halo;
+                    const int u0 = b * (halo + seg) + seg - wbeg;
+                    for (int e = tid; e < 64 * halo; e += 256) {
+                        const int i = e / halo, r = e - i * halo, ci = c * 64 + i, u = u0 + r;
+                        if (ci < a.cin) {
+                            const half hv = *reinterpret_cast<const half *>(sW + (size_t) u * 128 + (((i >> 3) ^ (u & 7)) << 4) + (i & 7) * 2);
+                            dst[(size_t) ci * halo + r] = __half2float(hv);
+                        }
+                    }
+                }
+            }
+            for (int k = 0; k < a.taps; k++, it++) {
+                const int st = it % AS;
+                if (ok && it >= AS) ok = mbar_wait(&a_empty[st], (uint32_t) ((it / AS) - 1) & 1u, p.err);
+                if (!ok) {
+                    s_abort = 1;
+                    continue;
+                }
+                const int shift = halo - (a.taps - 1 - k) * a.dil;
+                uint8_t * A = sA + st * kTAB;
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                    const int r = (tid >> 3) + 32 * m, u = cb[m] + shift;
+                    const uint4 v = *reinterpret_cast<const uint4 *>(sW + (size_t) u * 128 + ((j ^ (u & 7)) << 4));
+                    *reinterpret_cast<uint4 *>(A + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4)) = v;
+                }
+                fence_proxy_async();
+                mbar_arrive(&a_full[st]);
+            }
+        }
+    } else if (warp == 8) {
+        if (lane == 0) {
+            for (int it = 0; it < n_it; it++) {
+                const int st = it % AS, sb = it % BS;
+                ok = mbar_wait(&b_full[sb], (uint32_t) (it / BS) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[st], (uint32_t) (it / AS) & 1u, p.err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + st * kTAB), b0 = smem_u32(sB + sb * tb);
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&a_empty[st]);
+                umma_commit(&b_empty[sb]);
+            }
+            umma_commit(&done_bar);
+            if (!mbar_drain(&done_bar, 0u, p.err)) ok = false;
+        }
+    } else {
+        if (lane == 0) {
+            const uint8_t * base = reinterpret_cast<const uint8_t *>(p.w16) +
+                                   (((size_t) phase * p.otiles + ot) * p.kchunks) * a.taps * (size_t) tb;
+            int issued = 0;
+            for (int it = 0; it < n_it; it++) {
+                const int sb = it % BS;
+                if (it >= BS) ok = mbar_wait(&b_empty[sb], (uint32_t) ((it / BS) - 1) & 1u, p.err);
+                if (!ok) break;
+                mbar_expect_tx(&b_full[sb], tb);
+                bulk_g2s(sB + sb * tb, base + (size_t) it * tb, tb, &b_full[sb]);
+                issued = it + 1;
+            }
+            for (int it = max(0, issued - BS); it < issued; it++)
+                mbar_drain(&b_full[it % BS], (uint32_t) (it / BS) & 1u, p.err);
+        }
+    }
+
+    if (warp < 8) {
+        if (!mbar_wait(&done_bar, 0u, p.err)) ok = false;
+        tc_fence_after();
+        const int q = warp & 3, hh = warp >> 2, half_cols = p.nt / 2;
+        const int t = t0 + 32 * q + lane;
+        const bool live = ok && t < a.L;
+        for (int c0 = hh * half_cols; c0 < (hh + 1) * half_cols; c0 += 16) {  // warp-uniform: every lane loads
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
+            if (live) {
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const int o = ot * p.nt + c0 + e;
+                    if (o < a.cout) conv_epilogue(a, o, (size_t) o * a.ldy + (size_t) t * a.ostride + phase, v[e]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) tmem_dealloc(tmem, cols);
+}
+
 // sums the channel-split partials in split order and applies the epilogue
 __global__ void voc_conv_reduce_kernel(const ConvArgs a) {
     const size_t n = (size_t) a.cout * a.ldy;
@@ -578,6 +796,49 @@ void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats,
     }
 }
 
+// the tcgen05 convolution of `a` (istride 1) with weights tiled as `c` describes
+void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunks, int phases, int * err, cudaStream_t s) {
+    if (a.L <= 0) return;
+    if (a.istride != 1) throw std::runtime_error("tcgen05 conv: strided input is not supported");
+    a.Lin = a.L;
+    a.splits = 1;
+    TcConv p;
+    p.a = a;
+    p.w16 = w16;
+    p.nt = nt;
+    p.otiles = otiles;
+    p.kchunks = kchunks;
+    p.err = err;
+    const int halo = (a.taps - 1) * a.dil;
+    const int seg = a.seg_len > 0 ? a.seg_len : a.L;
+    const int n_seg = a.L / seg;
+    const int touched = std::min(n_seg, (kTM - 1 + seg - 1) / seg + 1);
+    p.win_rows = (kTM + halo * touched + 7) / 8 * 8;
+    auto smem = [&](int as, int bs) {
+        return (size_t) 1024 + (size_t) as * kTAB + (size_t) bs * nt * 128 + (size_t) p.win_rows * (128 + 8);
+    };
+    p.a_stages = 3;
+    p.b_stages = 3;
+    while (smem(p.a_stages, p.b_stages) > (size_t) kTSmemMax) {
+        if (p.b_stages > 2) p.b_stages--;
+        else if (p.a_stages > 2) p.a_stages--;
+        else throw std::runtime_error("tcgen05 conv: the input window does not fit in shared memory");
+    }
+    static std::mutex mu;
+    static std::map<int, bool> attr_set;
+    int dev = 0;
+    VCHECK(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[dev]) {
+            VCHECK(cudaFuncSetAttribute(voc_conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemMax));
+            attr_set[dev] = true;
+        }
+    }
+    const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) phases);
+    voc_conv_tc_kernel<<<grid, kTThreads, smem(p.a_stages, p.b_stages), s>>>(p);
+}
+
 }  // namespace
 
 template <class T> T * Vocoder::dalloc(size_t n) {
@@ -667,6 +928,7 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
         float * d = dalloc<float>(h.size());
         VCHECK(cudaMemcpyAsync(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice, stream_));
         c.w = d;
+        tile_conv_f16(c, h);
         return c;
     }
     // [cin][cout][K] -> per output phase p: tap-major [cout][taps][cin]; the input step t - m
@@ -686,7 +948,37 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
     float * d = dalloc<float>(h.size());
     VCHECK(cudaMemcpyAsync(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice, stream_));
     c.w = d;
+    tile_conv_f16(c, h);
     return c;
+}
+
+void Vocoder::tile_conv_f16(Conv & c, const std::vector<float> & h) {
+    c.otiles = (c.cout + 255) / 256;
+    c.nt = ((c.cout + c.otiles - 1) / c.otiles + 31) / 32 * 32;
+    c.kchunks = (c.cin + 63) / 64;
+    const size_t tile = (size_t) c.nt * 64;  // halves
+    std::vector<half> t((size_t) c.phases * c.otiles * c.kchunks * c.taps * tile, __float2half(0.0f));
+    for (int ph = 0; ph < c.phases; ph++)
+        for (int ot = 0; ot < c.otiles; ot++)
+            for (int ch = 0; ch < c.kchunks; ch++)
+                for (int k = 0; k < c.taps; k++) {
+                    half * dst = t.data() + ((((size_t) ph * c.otiles + ot) * c.kchunks + ch) * c.taps + k) * tile;
+                    for (int n = 0; n < c.nt; n++) {
+                        const int o = ot * c.nt + n;
+                        if (o >= c.cout) continue;
+                        for (int i = 0; i < 64; i++) {
+                            const int ci = ch * 64 + i;
+                            if (ci >= c.cin) continue;
+                            // row n: 8-row atoms of 1024 B, 16-byte piece i/8 swizzled by n mod 8
+                            const size_t byte = (size_t) (n / 8) * 1024 + (n % 8) * 128 + (size_t) (((i / 8) ^ (n % 8)) * 16) + (i % 8) * 2;
+                            dst[byte / 2] = __float2half_rn(h[(((size_t) ph * c.cout + o) * c.taps + k) * c.cin + ci]);
+                        }
+                    }
+                }
+    c.w16 = dalloc<half>(t.size());
+    VCHECK(cudaMemcpyAsync(c.w16, t.data(), t.size() * sizeof(half), cudaMemcpyHostToDevice, stream_));
+    // the host vector goes out of scope: the upload must complete first
+    VCHECK(cudaStreamSynchronize(stream_));
 }
 
 Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaStream_t stream)
@@ -1012,7 +1304,7 @@ void Vocoder::decode_segments(const int * codes_dev, int ld_codes, int S, int T,
             ca.seg_par = d_par;
         }
         li++;
-        launch_conv(ca, c.phases, part_, 2 * act_elems_, s);
+        launch_conv_tc(ca, c.w16, c.nt, c.otiles, c.kchunks, c.phases, err_, s);
     };
     transpose(t32_, NF, cbdim_, a_, nullptr);
     conv(dpre_, a_, T, 1, b_);                                       // [latent][NF]

@@ -94,6 +94,11 @@ private:
         float * b = nullptr;
         int cin = 0, cout = 0, K = 0;
         int taps = 0, phases = 1, stride = 0;
+        // the tcgen05 convolution's weights: f16 tiles [phases][otiles][kchunks][taps] of nt output
+        // channels x 64 input channels, each the 128-byte-swizzled K-major image one bulk copy
+        // brings into shared memory (rows and channels past cout / cin are zero)
+        half * w16 = nullptr;
+        int nt = 0, otiles = 0, kchunks = 0;
     };
     struct Layer {
         QMat q, k, v, o, gate, up, down;
@@ -122,6 +127,8 @@ private:
     void linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s);
     // stride 0: a causal conv; stride s > 0: a transposed conv, split into s phase convs
     Conv load_conv(const std::string & name, int K, int cin, int cout, int stride);
+    // the f16 tiles of a conv from its tap-major f32 weights [phases][cout][taps][cin]
+    void tile_conv_f16(Conv & c, const std::vector<float> & tapmajor);
     void ensure(int T);
     template <class T> T * dalloc(size_t n);
 

@@ -13,7 +13,7 @@ reference checkout is present; the fixtures are committed so that the tests need
                    python/bz_ggml/cluster.py: estimate_speech_profile, select_burst_steps and
                    a TieredSlotPool acquire/release trace
 
-usage: python tests/golden/make_golden.py [reference checkout, default /root/reference]
+usage: python tests/golden/make_golden.py <reference checkout>
 """
 import ctypes
 import importlib.util
@@ -173,4 +173,6 @@ def cluster_cases(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(__doc__)
+    main(sys.argv[1])

@@ -59,7 +59,7 @@ def full(request, pkg):
     path = os.path.join(model_dir(), f"breeze_full_nc32_{quant}_seed0_eosoff.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        pkg.synth_model(tmp, preset="full", nc=32, quant=quant, seed=0, eos_off=True)
+        pkg.synth_model(tmp, preset="full", nc=32, quant=quant, seed=0, eos_off=True, depth_top_k=1)
         os.replace(tmp, path)
     gen = pkg.GeneratorHandle(path, 0)
     m = bo.Model(path)
