@@ -338,6 +338,9 @@ struct TcConv {
     int nt = 0, otiles = 0, kchunks = 0;
     int win_rows = 0;                // window capacity (rows of 64 f16)
     int a_stages = 3, b_stages = 3;  // at most 4 each
+    // input-channel split across CTAs (blockIdx.z / phases): chunks [split cps, (split + 1) cps);
+    // with splits > 1 the raw sums go to a.part[split][...] and voc_conv_reduce_kernel finishes
+    int splits = 1, cps = 0;
     int * err = nullptr;
 };
 
@@ -359,7 +362,8 @@ __global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_
     int * wtau = wseg + p.win_rows;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int phase = blockIdx.z, ot = blockIdx.y;
+    const int phases = a.ostride, phase = blockIdx.z % phases, split = blockIdx.z / phases, ot = blockIdx.y;
+    const int c_beg = split * p.cps, c_end = min(p.kchunks, c_beg + p.cps);
     const int t0 = blockIdx.x * kTM;
     const int halo = (a.taps - 1) * a.dil;
     const int seg = a.seg_len > 0 ? a.seg_len : a.L;
@@ -368,7 +372,7 @@ __global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_
     const int wbeg = t0 + halo * b_first;
     const int lx = n_last + halo * (n_last / seg) + halo - wbeg + 1;
     const int AS = p.a_stages, BS = p.b_stages;
-    const int n_it = p.kchunks * a.taps;
+    const int n_it = max(0, c_end - c_beg) * a.taps;
     const uint32_t cols = p.nt <= 32 ? 32u : p.nt <= 64 ? 64u : p.nt <= 128 ? 128u : 256u;
     const uint32_t idesc = (1u << 4) | ((uint32_t) (p.nt >> 3) << 17) | ((uint32_t) (kTM >> 4) << 24);
 
@@ -406,34 +410,53 @@ __global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_
             cb[m] = n + halo * (n / seg) - wbeg;
         }
         int it = 0;
-        for (int c = 0; c < p.kchunks; c++) {
+        for (int c = c_beg; c < c_end; c++) {
             bar_producers();  // every producer is done with the previous window
             if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-            // the chunk's window: piece jj (8 channels) of row u; a warp's lanes take consecutive rows
-            for (int e = tid; e < 8 * lx; e += 256) {
-                const int jj = e / lx, u = e - jj * lx;
-                const int b = wseg[u], tau = wtau[u];
-                const int par = tau < 0 && a.st && b * seg < a.L ? a.seg_par[b] : -1;
-                const float * stp = par >= 0 ? a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) par * a.cin * halo : nullptr;
-                const int t = b * seg + tau;
-                uint32_t w[4];
+            // the chunk's window: piece jj (8 channels) of row u; a warp's lanes take consecutive
+            // rows, and each thread loads 4 items before converting any, so that 32 loads are in
+            // flight per thread instead of 8
+            for (int e0 = tid; e0 < 8 * lx; e0 += 4 * 256) {
+                float f[4][8];
 #pragma unroll
-                for (int q = 0; q < 8; q += 2) {
-                    float f0 = 0.0f, f1 = 0.0f;
-                    const int ci = c * 64 + jj * 8 + q;
+                for (int m = 0; m < 4; m++) {
+                    const int e = e0 + 256 * m;
+#pragma unroll
+                    for (int q = 0; q < 8; q++) f[m][q] = 0.0f;
+                    if (e >= 8 * lx) continue;
+                    const int jj = e / lx, u = e - jj * lx;
+                    const int b = wseg[u], tau = wtau[u];
+                    const int ci0 = c * 64 + jj * 8;
                     if (tau < 0) {
-                        if (stp) {
-                            if (ci < a.cin) f0 = stp[(size_t) ci * halo + tau + halo];
-                            if (ci + 1 < a.cin) f1 = stp[(size_t) (ci + 1) * halo + tau + halo];
+                        const int par = a.st && b * seg < a.L ? a.seg_par[b] : -1;
+                        if (par >= 0) {
+                            const float * stp = a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) par * a.cin * halo;
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                if (ci0 + q < a.cin) f[m][q] = stp[(size_t) (ci0 + q) * halo + tau + halo];
                         }
-                    } else if (t < a.L) {
-                        if (ci < a.cin) f0 = a.x[(size_t) ci * a.L + t];
-                        if (ci + 1 < a.cin) f1 = a.x[(size_t) (ci + 1) * a.L + t];
+                    } else {
+                        const int t = b * seg + tau;
+                        if (t < a.L) {
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                if (ci0 + q < a.cin) f[m][q] = a.x[(size_t) (ci0 + q) * a.L + t];
+                        }
                     }
-                    const half2 h2 = __floats2half2_rn(f0, f1);
-                    w[q / 2] = *reinterpret_cast<const uint32_t *>(&h2);
                 }
-                *reinterpret_cast<uint4 *>(sW + (size_t) u * 128 + ((jj ^ (u & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                    const int e = e0 + 256 * m;
+                    if (e >= 8 * lx) continue;
+                    const int jj = e / lx, u = e - jj * lx;
+                    uint32_t w[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const half2 h2 = __floats2half2_rn(f[m][2 * q], f[m][2 * q + 1]);
+                        w[q] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    *reinterpret_cast<uint4 *>(sW + (size_t) u * 128 + ((jj ^ (u & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
             }
             bar_producers();  // the window is complete
             if (a.st && halo > 0 && ot == 0 && phase == 0) {
@@ -490,7 +513,7 @@ __global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_
     } else {
         if (lane == 0) {
             const uint8_t * base = reinterpret_cast<const uint8_t *>(p.w16) +
-                                   (((size_t) phase * p.otiles + ot) * p.kchunks) * a.taps * (size_t) tb;
+                                   (((size_t) phase * p.otiles + ot) * p.kchunks + c_beg) * a.taps * (size_t) tb;
             int issued = 0;
             for (int it = 0; it < n_it; it++) {
                 const int sb = it % BS;
@@ -521,7 +544,10 @@ __global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
                     const int o = ot * p.nt + c0 + e;
-                    if (o < a.cout) conv_epilogue(a, o, (size_t) o * a.ldy + (size_t) t * a.ostride + phase, v[e]);
+                    if (o >= a.cout) continue;
+                    const size_t idx = (size_t) o * a.ldy + (size_t) t * a.ostride + phase;
+                    if (p.splits > 1) a.part[(size_t) split * a.cout * a.ldy + idx] = n_it > 0 ? v[e] : 0.0f;
+                    else conv_epilogue(a, o, idx, v[e]);
                 }
             }
         }
@@ -797,12 +823,22 @@ void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats,
 }
 
 // the tcgen05 convolution of `a` (istride 1) with weights tiled as `c` describes
-void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunks, int phases, int * err, cudaStream_t s) {
+void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunks, int phases, int * err,
+                    float * scratch, size_t scratch_floats, cudaStream_t s) {
     if (a.L <= 0) return;
     if (a.istride != 1) throw std::runtime_error("tcgen05 conv: strided input is not supported");
     a.Lin = a.L;
-    a.splits = 1;
+    // small grids: split the input-channel chunks across CTAs until about two waves are in flight
+    const int tiles = ((a.L + kTM - 1) / kTM) * otiles * phases;
+    int splits = 1;
+    while (tiles * splits * 2 <= 2 * 148 && splits * 2 <= kchunks && splits < 16 &&
+           (size_t) splits * 2 * a.cout * a.ldy <= scratch_floats)
+        splits *= 2;
+    a.splits = splits;
+    a.part = scratch;
     TcConv p;
+    p.splits = splits;
+    p.cps = (kchunks + splits - 1) / splits;
     p.a = a;
     p.w16 = w16;
     p.nt = nt;
@@ -835,8 +871,12 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
             attr_set[dev] = true;
         }
     }
-    const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) phases);
+    const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) (phases * splits));
     voc_conv_tc_kernel<<<grid, kTThreads, smem(p.a_stages, p.b_stages), s>>>(p);
+    if (splits > 1) {
+        const size_t n = (size_t) a.cout * a.ldy;
+        voc_conv_reduce_kernel<<<(unsigned) std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(a);
+    }
 }
 
 }  // namespace
@@ -1304,7 +1344,7 @@ void Vocoder::decode_segments(const int * codes_dev, int ld_codes, int S, int T,
             ca.seg_par = d_par;
         }
         li++;
-        launch_conv_tc(ca, c.w16, c.nt, c.otiles, c.kchunks, c.phases, err_, s);
+        launch_conv_tc(ca, c.w16, c.nt, c.otiles, c.kchunks, c.phases, err_, part_, 2 * act_elems_, s);
     };
     transpose(t32_, NF, cbdim_, a_, nullptr);
     conv(dpre_, a_, T, 1, b_);                                       // [latent][NF]
