@@ -346,7 +346,7 @@ struct TcConv {
 
 __device__ __forceinline__ void bar_producers() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kTThreads, 1) voc_conv_tc_kernel(const __grid_constant__ TcConv p) {
+__global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_constant__ TcConv p) {
     using namespace tc;
     const ConvArgs & a = p.a;
     extern __shared__ uint8_t tsm_raw[];
@@ -855,6 +855,15 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     };
     p.a_stages = 3;
     p.b_stages = 3;
+    // grids of more than one wave: two CTAs per SM (one's staging and epilogue latency hidden
+    // behind the other's work) when two-stage rings make room for them
+    const long long ctas = (long long) ((a.L + kTM - 1) / kTM) * otiles * phases * splits;
+    const size_t two_per_sm = (size_t) 113 * 1024;
+    if (ctas > 148 && smem(2, 2) <= two_per_sm)
+        while (smem(p.a_stages, p.b_stages) > two_per_sm) {
+            if (p.b_stages > 2) p.b_stages--;
+            else p.a_stages--;
+        }
     while (smem(p.a_stages, p.b_stages) > (size_t) kTSmemMax) {
         if (p.b_stages > 2) p.b_stages--;
         else if (p.a_stages > 2) p.a_stages--;
