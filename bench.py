@@ -82,6 +82,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="after the ramp, run one device-resident serving step between cudaProfilerStart/Stop and exit (ncu)")
+    ap.add_argument("--profile-admit", action="store_true",
+                    help="after the ramp, run one admission (a retired session replaced: batched create of one "
+                         "arrival) between cudaProfilerStart/Stop and exit (ncu)")
     ap.add_argument("--model-preset", default="full", choices=["full", "depth"],
                     help="'depth': the full-size depth decoder behind a one-layer backbone (small profiling captures)")
     return ap.parse_args()
@@ -529,6 +532,18 @@ def main():
         srv.step_device()
     gen.sync()
     t_ramp = time.perf_counter() - t_ramp
+    if args.profile_admit:
+        srv.left[srv.live[0]] = 0
+        gen.sync()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        n = srv.admit()
+        gen.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled_admissions": n}))
+        voc.close()
+        gen.close()
+        return
     if args.profile:
         srv.admit()
         torch.cuda.synchronize()

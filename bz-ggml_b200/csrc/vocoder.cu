@@ -943,6 +943,15 @@ QMat Vocoder::load_q8(const std::string & name) {
         repack_q8(raw, M, K, qs, ds, stream_);
         q.qs = qs;
         q.ds = ds;
+        if (K % 64 == 0) {
+            // the tcgen05 dequant-GEMM's layout as well: the batched decodes' linears run on it
+            UMat u;
+            u.M = M; u.MT = (M + 127) / 128; u.K = K; u.KC = K / 64; u.q4 = 0;
+            uint8_t * ub = dalloc<uint8_t>((size_t) u.MT * u.KC * kUChunkBytes);
+            repack_umma(raw, M, K, ub, stream_);
+            u.blk = ub;
+            q.u = u;
+        }
     }
     VCHECK(cudaStreamSynchronize(stream_));
     cudaFree(raw);
@@ -950,8 +959,10 @@ QMat Vocoder::load_q8(const std::string & name) {
 }
 
 void Vocoder::linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s) {
-    if (w.qs) launch_gemv(w, x16, ldx, rows, out, scr_, s);
-    else launch_umma_gemm(w.u, x16, ldx, rows, out, err_, s, false);
+    if (w.u.blk && ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(x16) & 15) == 0)
+        launch_umma_gemm(w.u, x16, ldx, rows, out, err_, s, false);
+    else if (w.qs) launch_gemv(w, x16, ldx, rows, out, scr_, s);
+    else throw std::runtime_error("vocoder: a Q4_K linear needs 16-byte aligned activations with a stride multiple of 8");
 }
 
 Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int cout, int stride) {
