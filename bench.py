@@ -436,6 +436,44 @@ def abi_path(pkg, gen, srv, nc, burst=8):
                      "breeze_vocoder_session_decode_batch with 32 frames of kept history, the last of 5 timed"}
 
 
+def cluster_config(pkg, args, per_gpu=40):
+    """The N-island harness (bz-ggml_b200/cluster.py) over every GPU this process sees, one island
+    per GPU on one shared job queue: configuration 4's burst (Q4_K model, `per_gpu` requests per
+    GPU at t = 0, prompts U[32,256] tokens, 63-frame voice contexts, U[100,300] frames, PCM made on
+    the server). Aggregate RTF = all audio / wall; per-island request counts show the balance."""
+    import importlib
+    import torch
+    cl = importlib.import_module(pkg.__name__ + ".cluster")
+    n_gpu = torch.cuda.device_count()
+    path = model_path(args, 0, quant="q4_k")
+    arr = Arrivals(pkg, args.nc, 44, prompt=(32, 256), voice=(63, 63), gen=(100, 300), first_id=6_000_000)
+    tasks = []
+    for i in range(per_gpu * n_gpu):
+        sp = arr.take()
+        tasks.append(cl.UserTask(id=sp["session_id"], text=sp["text"], seed=sp["seed"], max_steps=sp["max_new_tokens"],
+                                 ref_text=sp.get("ref_text"), ref_codes=sp["ref_codes"].reshape(-1).tolist(),
+                                 ref_frames=sp["ref_frames"]))
+    with cl.IslandCluster(path, devices=tuple(range(n_gpu)), max_slots=per_gpu, chunk_size=8, max_burst=16) as cluster:
+        warm = [cl.UserTask(id=7_000_000 + i, text=tasks[i].text, max_steps=4) for i in range(n_gpu)]
+        cluster.run_workload(warm)
+        t0 = time.perf_counter()
+        results = cluster.run_workload(tasks)
+        wall = time.perf_counter() - t0
+    per_island, audio = {}, 0.0
+    for r in results:
+        gpu = int(r.worker.split("GPU ")[1].split(" ")[0])
+        d = per_island.setdefault(gpu, {"requests": 0, "audio_s": 0.0})
+        d["requests"] += 1
+        d["audio_s"] += r.audio_s
+        audio += r.audio_s
+    ttfa = [r.ttfa_s * 1e3 for r in results]
+    return {"islands": n_gpu, "requests": len(results), "audio_s": audio, "wall_s": wall,
+            "aggregate_rtf": audio / wall, "ttfa_p50_ms": statistics.median(ttfa),
+            "ttfa_p90_ms": float(np.percentile(ttfa, 90)), "per_island": per_island,
+            "route": "IslandCluster.run_workload: one process, one island (generator + vocoder) per GPU, shared "
+                     "job queue, tiered slot pool, batched creation, burst steps, server-side PCM"}
+
+
 def cpu_reference_rtf(path, n_sessions, bursts, warm_bursts, burst=8, seed=7):
     """The reference's serving loop on the host cores, with the oracle for the path: n sessions of
     the workload (prefill untimed), then bursts of `burst` batched frame steps, each followed by the
@@ -652,6 +690,8 @@ def main():
     gen.close()
     if "1" in want:
         configs["c1_single_session_generate"] = config1(pkg, path)
+    if "cluster" in want and world == 1:
+        configs["cluster_islands"] = cluster_config(pkg, args)
     if "4" in want:
         if barrier:
             barrier()

@@ -71,3 +71,31 @@ def test_islands_serve_tokens_and_audio(pkg, tiny_model):
             assert r.turnaround_s >= r.compute_wall_s >= 0 and r.ttfa_s <= r.turnaround_s + 1e-3
     finally:
         voc.close()
+
+
+def test_islands_on_every_gpu(pkg, tiny_model):
+    """One island per visible GPU on one shared job queue (the reference's DualInstanceCluster
+    generalised, python/bz_ggml/cluster.py:402-414, 744-750): every request is served once, by
+    some island, and every island takes part. Runs where the process sees two or more GPUs."""
+    import torch
+    n_gpu = torch.cuda.device_count()
+    if n_gpu < 2:
+        pytest.skip("needs two or more GPUs in the process")
+    cl = importlib.import_module(pkg.__name__ + ".cluster")
+    tasks = [cl.UserTask(id=500 + i, text=pkg.ids_to_text([600 + i, 700 + 3 * i, 800 + i]) + " spread", seed=i,
+                         max_steps=12 + (i % 5), client_has_vocoder=(i % 3 == 0))
+             for i in range(6 * n_gpu)]
+    with cl.IslandCluster(tiny_model, devices=tuple(range(n_gpu)), max_slots=4, chunk_size=4, slot_tiers=(2, 1, 1),
+                          keep_tokens=True, keep_pcm=True) as cluster:
+        results = cluster.run_workload(tasks)
+        assert all(g.active_session_count() == 0 for g in cluster.gens)
+    assert sorted(r.id for r in results) == sorted(t.id for t in tasks)
+    islands = {}
+    for t, r in zip(tasks, results):
+        n = r.frames.shape[0]
+        assert 0 < n <= t.max_steps
+        if not t.client_has_vocoder:
+            assert r.pcm.size == n * 1920
+        gpu = int(r.worker.split("GPU ")[1].split(" ")[0])
+        islands[gpu] = islands.get(gpu, 0) + 1
+    assert set(islands) == set(range(n_gpu)), islands
