@@ -92,13 +92,13 @@ struct ConvArgs {
     float * y = nullptr;                // y[o * ldy + t * ostride + phase]
     int ldy = 0, ostride = 1;
     const float * res = nullptr;        // residual added before the activations (same indexing), or null
-    const float * sa = nullptr, * sb = nullptr;     // SnakeBeta (alpha, beta) of the stored value, or null
-    float * y2 = nullptr;               // second output: SnakeBeta(value) with (s2a, s2b), or ELU(value), or null
+    const float * sa = nullptr, * sb = nullptr;     // SnakeBeta (alpha, 1 / beta) of the stored value, or null
+    float * y2 = nullptr;               // second output: SnakeBeta(value) with (s2a, 1 / s2b), or ELU(value), or null
     const float * s2a = nullptr, * s2b = nullptr;
     int elu1 = 0, elu2 = 0;             // ELU instead of SnakeBeta for the stored value / the second output
     int clamp = 0;
     // split of the input channels over blockIdx.z / phases (1: no split); partial sums go to
-    // part[split][o * ldy + t * ostride + phase]
+    // part[conv_part_index(split, o, t, phase)]
     int splits = 1, ci_per_split = 0;
     float * part = nullptr;
     int lxp = 0;                        // staged window row stride (floats)
@@ -131,21 +131,34 @@ __device__ __forceinline__ void mma_tf32(float c[4], const uint32_t a[4], const 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-__device__ __forceinline__ float snake_beta(float v, float alpha, float beta) {
-    const float s = sinf(v * alpha);
-    return v + (s * s) / beta;
+// SnakeBeta x + sin(alpha x)^2 / beta with the reciprocal of beta stored at load: one fused
+// multiply-add after the hardware sine (absolute error ~2^-21 |alpha x|, far below the PCM bar)
+__device__ __forceinline__ float snake_beta(float v, float alpha, float inv_beta) {
+    const float s = __sinf(v * alpha);
+    return fmaf(s * s, inv_beta, v);
 }
 
 // ELU as ggml_elu: x for x > 0, exp(x) - 1 otherwise
 __device__ __forceinline__ float elu_f(float v) { return v > 0.0f ? v : expm1f(v); }
 
-__device__ __forceinline__ void conv_epilogue(const ConvArgs & a, int o, size_t idx, float v) {
-    v += a.bias ? __ldg(a.bias + o) : 0.0f;
-    if (a.res) v += a.res[idx];
+// stores v = conv + bias (+ residual) of output channel o at idx, with its activations
+__device__ __forceinline__ void conv_store(const ConvArgs & a, int o, size_t idx, float v) {
     float out = a.elu1 ? elu_f(v) : a.sa ? snake_beta(v, __ldg(a.sa + o), __ldg(a.sb + o)) : v;
     if (a.clamp) out = fminf(1.0f, fmaxf(-1.0f, out));
     a.y[idx] = out;
     if (a.y2) a.y2[idx] = a.elu2 ? elu_f(v) : snake_beta(v, __ldg(a.s2a + o), __ldg(a.s2b + o));
+}
+
+__device__ __forceinline__ void conv_epilogue(const ConvArgs & a, int o, size_t idx, float v) {
+    v += a.bias ? __ldg(a.bias + o) : 0.0f;
+    if (a.res) v += a.res[idx];
+    conv_store(a, o, idx, v);
+}
+
+// the partial sum of input-channel split sp for output (o, step t, phase ph): phase-major planes
+// [split][phase][cout][L], so that a warp's consecutive steps store to consecutive addresses
+__device__ __forceinline__ size_t conv_part_index(const ConvArgs & a, int sp, int o, int t, int ph) {
+    return (((size_t) sp * a.ostride + ph) * a.cout + o) * (size_t) a.L + t;
 }
 
 __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs a) {
@@ -307,7 +320,7 @@ __global__ void __launch_bounds__(kCThreads) voc_conv_mma_kernel(const ConvArgs 
                 const int t = t0 + wn + ni * 8 + 2 * t4 + (e & 1);
                 if (o >= a.cout || t >= a.L) continue;
                 const size_t idx = (size_t) o * a.ldy + (size_t) t * a.ostride + phase;
-                if (a.splits > 1) a.part[(size_t) split * a.cout * a.ldy + idx] = acc[mi][ni][e];
+                if (a.splits > 1) a.part[conv_part_index(a, split, o, t, phase)] = acc[mi][ni][e];
                 else conv_epilogue(a, o, idx, acc[mi][ni][e]);
             }
         }
@@ -413,49 +426,51 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
         for (int c = c_beg; c < c_end; c++) {
             bar_producers();  // every producer is done with the previous window
             if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-            // the chunk's window: piece jj (8 channels) of row u; a warp's lanes take consecutive
-            // rows, and each thread loads 4 items before converting any, so that 32 loads are in
-            // flight per thread instead of 8
-            for (int e0 = tid; e0 < 8 * lx; e0 += 4 * 256) {
-                float f[4][8];
+            // the chunk's window: warp w stages piece w (channels c 64 + 8 w ...) of every row,
+            // its lanes taking consecutive rows (coalesced loads of consecutive steps); each lane
+            // loads 4 rows before converting any, so that 32 loads are in flight
+            {
+                const int ci0 = c * 64 + warp * 8, nq = min(8, a.cin - ci0);
+                for (int ub = 0; ub < lx; ub += 128) {
+                    float f[4][8];
 #pragma unroll
-                for (int m = 0; m < 4; m++) {
-                    const int e = e0 + 256 * m;
+                    for (int m = 0; m < 4; m++) {
 #pragma unroll
-                    for (int q = 0; q < 8; q++) f[m][q] = 0.0f;
-                    if (e >= 8 * lx) continue;
-                    const int jj = e / lx, u = e - jj * lx;
-                    const int b = wseg[u], tau = wtau[u];
-                    const int ci0 = c * 64 + jj * 8;
-                    if (tau < 0) {
-                        const int par = a.st && b * seg < a.L ? a.seg_par[b] : -1;
-                        if (par >= 0) {
-                            const float * stp = a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) par * a.cin * halo;
+                        for (int q = 0; q < 8; q++) f[m][q] = 0.0f;
+                        const int u = ub + 32 * m + lane;
+                        if (u >= lx || nq <= 0) continue;
+                        const int b = wseg[u], tau = wtau[u];
+                        if (tau < 0) {
+                            const int par = a.st && b * seg < a.L ? a.seg_par[b] : -1;
+                            if (par >= 0) {
+                                const float * stp = a.st + (size_t) a.seg_slot[b] * a.st_stride +
+                                                    ((size_t) par * a.cin + ci0) * halo + tau + halo;
 #pragma unroll
-                            for (int q = 0; q < 8; q++)
-                                if (ci0 + q < a.cin) f[m][q] = stp[(size_t) (ci0 + q) * halo + tau + halo];
-                        }
-                    } else {
-                        const int t = b * seg + tau;
-                        if (t < a.L) {
+                                for (int q = 0; q < 8; q++)
+                                    if (q < nq) f[m][q] = stp[(size_t) q * halo];
+                            }
+                        } else {
+                            const int t = b * seg + tau;
+                            if (t < a.L) {
+                                const float * xp = a.x + (size_t) ci0 * a.L + t;
 #pragma unroll
-                            for (int q = 0; q < 8; q++)
-                                if (ci0 + q < a.cin) f[m][q] = a.x[(size_t) (ci0 + q) * a.L + t];
+                                for (int q = 0; q < 8; q++)
+                                    if (q < nq) f[m][q] = xp[(size_t) q * a.L];
+                            }
                         }
                     }
-                }
 #pragma unroll
-                for (int m = 0; m < 4; m++) {
-                    const int e = e0 + 256 * m;
-                    if (e >= 8 * lx) continue;
-                    const int jj = e / lx, u = e - jj * lx;
-                    uint32_t w[4];
+                    for (int m = 0; m < 4; m++) {
+                        const int u = ub + 32 * m + lane;
+                        if (u >= lx) continue;
+                        uint32_t w[4];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const half2 h2 = __floats2half2_rn(f[m][2 * q], f[m][2 * q + 1]);
-                        w[q] = *reinterpret_cast<const uint32_t *>(&h2);
+                        for (int q = 0; q < 4; q++) {
+                            const half2 h2 = __floats2half2_rn(f[m][2 * q], f[m][2 * q + 1]);
+                            w[q] = *reinterpret_cast<const uint32_t *>(&h2);
+                        }
+                        *reinterpret_cast<uint4 *>(sW + (size_t) u * 128 + ((warp ^ (u & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
-                    *reinterpret_cast<uint4 *>(sW + (size_t) u * 128 + ((jj ^ (u & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
             bar_producers();  // the window is complete
@@ -534,21 +549,33 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
         const int q = warp & 3, hh = warp >> 2, half_cols = p.nt / 2;
         const int t = t0 + 32 * q + lane;
         const bool live = ok && t < a.L;
+        const size_t tcol = (size_t) t * a.ostride + phase;
         for (int c0 = hh * half_cols; c0 < (hh + 1) * half_cols; c0 += 16) {  // warp-uniform: every lane loads
             float v[16];
             tmem_ld16(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
-            if (live) {
+            const int ob = ot * p.nt + c0, ne = min(16, a.cout - ob);
+            if (live && p.splits > 1) {
+#pragma unroll
+                for (int e = 0; e < 16; e++)
+                    if (e < ne) a.part[conv_part_index(a, split, ob + e, t, phase)] = n_it > 0 ? v[e] : 0.0f;
+            } else if (live) {
+                // every load of the 16 outputs before the first store: y may be the residual
+                // itself (updated in place), which would otherwise serialise load after store
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    const int o = ot * p.nt + c0 + e;
-                    if (o >= a.cout) continue;
-                    const size_t idx = (size_t) o * a.ldy + (size_t) t * a.ostride + phase;
-                    if (p.splits > 1) a.part[(size_t) split * a.cout * a.ldy + idx] = n_it > 0 ? v[e] : 0.0f;
-                    else conv_epilogue(a, o, idx, v[e]);
+                    float add = 0.0f;
+                    if (e < ne) {
+                        if (a.bias) add = __ldg(a.bias + ob + e);
+                        if (a.res) add += a.res[(size_t) (ob + e) * a.ldy + tcol];
+                    }
+                    v[e] += add;
                 }
+#pragma unroll
+                for (int e = 0; e < 16; e++)
+                    if (e < ne) conv_store(a, ob + e, (size_t) (ob + e) * a.ldy + tcol, v[e]);
             }
         }
     }
@@ -557,14 +584,22 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     if (warp == 8) tmem_dealloc(tmem, cols);
 }
 
-// sums the channel-split partials in split order and applies the epilogue
+// sums the channel-split partials in split order and applies the epilogue: blockIdx.y is the
+// output channel, threads take consecutive outputs i = t ostride + phase of its row
 __global__ void voc_conv_reduce_kernel(const ConvArgs a) {
-    const size_t n = (size_t) a.cout * a.ldy;
-    for (size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (size_t) gridDim.x * blockDim.x) {
-        float v = 0.0f;
-        for (int sp = 0; sp < a.splits; sp++) v += a.part[(size_t) sp * n + idx];
-        conv_epilogue(a, (int) (idx / a.ldy), idx, v);
-    }
+    const int P = a.ostride, n_row = a.L * P;
+    for (int o = blockIdx.y; o < a.cout; o += gridDim.y)
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_row; i += gridDim.x * blockDim.x) {
+            const int t = i / P, ph = i - t * P;
+            float v = 0.0f;
+            for (int sp = 0; sp < a.splits; sp++) v += a.part[conv_part_index(a, sp, o, t, ph)];
+            conv_epilogue(a, o, (size_t) o * a.ldy + i, v);
+        }
+}
+
+void launch_conv_reduce(const ConvArgs & a, cudaStream_t s) {
+    const dim3 grid((unsigned) std::min((a.L * a.ostride + 255) / 256, 65535), (unsigned) std::min(a.cout, 65535));
+    voc_conv_reduce_kernel<<<grid, 256, 0, s>>>(a);
 }
 
 // causal depthwise conv (src/codec_conv.cpp:42-59), w [K][C], y[c][t] = b[c] + sum_k w[k][c]
@@ -816,10 +851,7 @@ void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats,
     raise_conv_smem_limit(conv_smem_bytes(a.lxp));
     const dim3 grid((unsigned) ((a.L + kCBN - 1) / kCBN), (unsigned) ((a.cout + kCBM - 1) / kCBM), (unsigned) (phases * splits));
     voc_conv_mma_kernel<<<grid, kCThreads, conv_smem_bytes(a.lxp), s>>>(a);
-    if (splits > 1) {
-        const size_t n = (size_t) a.cout * a.ldy;
-        voc_conv_reduce_kernel<<<(unsigned) std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(a);
-    }
+    if (splits > 1) launch_conv_reduce(a, s);
 }
 
 // the tcgen05 convolution of `a` (istride 1) with weights tiled as `c` describes
@@ -882,10 +914,7 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     }
     const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) (phases * splits));
     voc_conv_tc_kernel<<<grid, kTThreads, smem(p.a_stages, p.b_stages), s>>>(p);
-    if (splits > 1) {
-        const size_t n = (size_t) a.cout * a.ldy;
-        voc_conv_reduce_kernel<<<(unsigned) std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(a);
-    }
+    if (splits > 1) launch_conv_reduce(a, s);
 }
 
 }  // namespace
@@ -903,7 +932,7 @@ const GgufTensor & Vocoder::need(const std::string & name) const {
     throw std::runtime_error("vocoder: tensor " + name + " missing from the GGUF");
 }
 
-float * Vocoder::load_f32(const std::string & name, int64_t expect, bool exp_of) {
+float * Vocoder::load_f32(const std::string & name, int64_t expect, bool exp_of, bool recip) {
     const GgufTensor & t = need(name);
     if (t.type != 0 || (expect >= 0 && t.nelem() != expect))
         throw std::runtime_error("vocoder: " + name + " must be F32 with " + std::to_string(expect) + " elements");
@@ -911,6 +940,8 @@ float * Vocoder::load_f32(const std::string & name, int64_t expect, bool exp_of)
     std::memcpy(h.data(), gg_.data(t), h.size() * 4);
     if (exp_of)
         for (float & v : h) v = expf(v);  // SnakeBeta parameters are stored as logarithms
+    if (recip)
+        for (float & v : h) v = 1.0f / v;  // SnakeBeta's beta: the kernels multiply by 1 / beta
     float * d = dalloc<float>(h.size());
     VCHECK(cudaMemcpyAsync(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice, stream_));
     return d;
@@ -1120,7 +1151,7 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaS
         Blk b;
         b.rate = vc_.rates[i];
         b.alpha = load_f32(p + ".alpha", ch, true);
-        b.beta = load_f32(p + ".beta", ch, true);
+        b.beta = load_f32(p + ".beta", ch, true, true);
         const GgufTensor & ut = need(p + ".up.conv.weight");
         const int co = (int) ut.ne[1];
         b.up = load_conv(p + ".up.conv", (int) ut.ne[0], ch, co, b.rate);
@@ -1129,17 +1160,17 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaS
             const std::string q = p + ".res." + std::to_string(j);
             Res r;
             r.a1 = load_f32(q + ".a1", ch, true);
-            r.b1 = load_f32(q + ".b1", ch, true);
+            r.b1 = load_f32(q + ".b1", ch, true, true);
             r.c1 = load_conv(q + ".conv1.conv", (int) need(q + ".conv1.conv.weight").ne[0], ch, ch, 0);
             r.a2 = load_f32(q + ".a2", ch, true);
-            r.b2 = load_f32(q + ".b2", ch, true);
+            r.b2 = load_f32(q + ".b2", ch, true, true);
             r.c2 = load_conv(q + ".conv2.conv", (int) need(q + ".conv2.conv.weight").ne[0], ch, ch, 0);
             b.res[j] = r;
         }
         blks_.push_back(b);
     }
     fin_alpha_ = load_f32("codec.dfin.alpha", ch, true);
-    fin_beta_ = load_f32("codec.dfin.beta", ch, true);
+    fin_beta_ = load_f32("codec.dfin.beta", ch, true, true);
     dfin_ = load_conv("codec.dfin.conv", (int) need("codec.dfin.conv.weight").ne[0], ch, 1, 0);
     int up_total = 1;
     for (int r : vc_.ratios) up_total *= r;

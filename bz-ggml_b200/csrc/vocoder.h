@@ -122,7 +122,7 @@ private:
     };
 
     const GgufTensor & need(const std::string & name) const;
-    float * load_f32(const std::string & name, int64_t expect, bool exp_of = false);
+    float * load_f32(const std::string & name, int64_t expect, bool exp_of = false, bool recip = false);
     QMat load_q8(const std::string & name);  // Q8_0 (mma.sync layout) or Q4_K (tcgen05 layout)
     void linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s);
     // stride 0: a causal conv; stride s > 0: a transposed conv, split into s phase convs
