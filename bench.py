@@ -30,9 +30,11 @@ Prints one JSON line (rank 0):
 - `ttfa`: time to first audio of the sessions admitted in the timed loop (prefill + first step
   with its PCM), and an open-loop run with Poisson arrivals at 4/s (configuration 3 as stated);
 - `configs`: configuration 1 (one session through breeze_generate, greedy, 100 frames),
-  configuration 2 (16 equal sessions, 200 frames, 63-frame voice prompts) and configuration 4
-  (Q4_K model, 40 sessions arriving at once), each with PCM, and the reference ABI's own calls
-  (sessions_step_burst, windowed session_decode_batch) on the same batch.
+  configuration 2 (16 equal sessions, 200 frames, 63-frame voice prompts), configuration 4
+  (Q4_K model, 40 sessions arriving at once) and configuration 5 (this GPU's share of elastic
+  waves of streaming sessions, generation U[200,1500] frames; and 64 sessions at contexts near the
+  2040-position clamp), each with PCM, and the reference ABI's own calls (sessions_step_burst,
+  windowed session_decode_batch) on the same batch.
 The per-step working set (~5 GB of weights and KV) exceeds the 126 MB L2: no flush is needed.
 
 `--impl reference` times the reference's algorithm for the same path on the host cores: the
@@ -78,13 +80,18 @@ def parse():
     ap.add_argument("--model-dir", default=os.environ.get("BZB_MODEL_DIR", "/tmp/bzb_models"))
     ap.add_argument("--cpu-sample-sessions", type=int, default=2)
     ap.add_argument("--poisson-s", type=float, default=6.0, help="seconds of the open-loop Poisson run (0: skip)")
-    ap.add_argument("--configs", default="1,2,4,abi", help="other configurations to measure (comma list, or none)")
+    ap.add_argument("--configs", default="1,2,4,5,abi", help="other configurations to measure (comma list, or none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="after the ramp, run one device-resident serving step between cudaProfilerStart/Stop and exit (ncu)")
     ap.add_argument("--profile-admit", action="store_true",
                     help="after the ramp, run one admission (a retired session replaced: batched create of one "
                          "arrival) between cudaProfilerStart/Stop and exit (ncu)")
+    ap.add_argument("--profile-create", action="store_true",
+                    help="after the ramp, run one batched creation of --sessions new arrivals between "
+                         "cudaProfilerStart/Stop and exit (ncu)")
+    ap.add_argument("--prompt-cap", type=int, default=512,
+                    help="upper end of the text prompt lengths (tokens); smaller values make small profiling captures")
     ap.add_argument("--model-preset", default="full", choices=["full", "depth"],
                     help="'depth': the full-size depth decoder behind a one-layer backbone (small profiling captures)")
     return ap.parse_args()
@@ -353,6 +360,109 @@ def config2(pkg, gen, voc, nc):
             "route": "bzb_generator_sessions_create_batch + 200 x bzb_generator_sessions_step_pcm"}
 
 
+def config5(pkg, gen, voc, nc, seed, elastic_s=10.0, n_gpus_share=8, long_steps=30):
+    """Configuration 5, streaming PCM with elastic load, on this GPU's share of it. Two parts:
+    - elastic: waves of 20 sessions every 2 s spread over 8 GPUs (this GPU takes waves of 2 and 3
+      alternately), generation lengths U[200,1500] frames, prompts and voices as configuration 3;
+      arrivals join the running batch at the next step (one batched create), every live session
+      makes one frame and its 1920 PCM samples per step through the C ABI; aggregate RTF, time to
+      first audio (first PCM returned minus arrival) and concurrency, host wall clock;
+    - long_context: 64 sessions whose contexts start at 1300-1850 positions (text prompts
+      U[1300,1700] tokens plus 0-125 voice frames) and grow towards the 2040-position clamp:
+      `long_steps` device-resident serving steps with PCM timed by CUDA events, then as many
+      through the C ABI (the paged decode attention over its longest spans)."""
+    import torch
+    out = {}
+    # elastic waves
+    arr = Arrivals(pkg, nc, seed, gen=(200, 1500), first_id=8_000_000)
+    live, left, arrived, first = [], {}, {}, {}
+    ttfa, conc, frames, steps = [], [], 0, 0
+    wave, next_wave = 0, 0.0
+    t0 = time.perf_counter()
+    while True:
+        now = time.perf_counter() - t0
+        if now >= elastic_s:
+            break
+        specs = []
+        while next_wave <= now:
+            k = 20 // n_gpus_share + (1 if wave % 2 and 20 % n_gpus_share else 0)
+            for _ in range(k):
+                sp = arr.take()
+                arrived[sp["session_id"]] = t0 + next_wave
+                specs.append(sp)
+            wave += 1
+            next_wave += 2.0
+        if specs:
+            gen.sessions_create_batch(specs)
+            for sp in specs:
+                live.append(sp["session_id"])
+                left[sp["session_id"]] = sp["max_new_tokens"]
+        if not live:
+            time.sleep(0.005)
+            continue
+        gen.step_pcm(voc, live, [(s * 13 + left[s]) & 0xFFFFFFFF for s in live], want_frames=False)
+        t = time.perf_counter()
+        for sid in live:
+            if sid not in first:
+                first[sid] = t
+                ttfa.append((t - arrived[sid]) * 1e3)
+            left[sid] -= 1
+        frames += len(live)
+        steps += 1
+        conc.append(len(live))
+        for sid in [x for x in live if left[x] == 0]:
+            gen.session_free(sid)
+            voc.stream_close(sid)
+            live.remove(sid)
+    wall = time.perf_counter() - t0
+    for sid in live:
+        gen.session_free(sid)
+        voc.stream_close(sid)
+    out["elastic"] = {
+        "seconds": wall, "waves": wave, "arrivals": len(arrived), "steps": steps,
+        "ms_per_step": wall / max(steps, 1) * 1e3, "aggregate_rtf": frames * FRAME_S / wall,
+        "ttfa_p50_ms": statistics.median(ttfa) if ttfa else None,
+        "ttfa_p90_ms": float(np.percentile(ttfa, 90)) if ttfa else None,
+        "mean_concurrency": float(np.mean(conc)) if conc else 0.0, "peak_concurrency": max(conc) if conc else 0,
+        "method": f"this GPU's share of 20 arrivals per 2 s over {n_gpus_share} GPUs, generation U[200,1500] frames; "
+                  "bzb_generator_sessions_create_batch per step with arrivals, bzb_generator_sessions_step_pcm "
+                  "per step; host wall clock"}
+    # long contexts
+    arr = Arrivals(pkg, nc, seed + 1, prompt=(1300, 1700), gen=(100, 100), first_id=9_000_000)
+    specs = [arr.take() for _ in range(64)]
+    gen.sessions_create_batch(specs)
+    ids = [sp["session_id"] for sp in specs]
+    stream = torch.cuda.ExternalStream(gen.stream_ptr())
+    for k in range(3):
+        gen.step_pcm_device(voc, ids, [i + k for i in range(64)])
+    gen.sync()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(long_steps):
+        gen.step_pcm_device(voc, ids, [i + 3 + k for i in range(64)])
+    e1.record(stream)
+    e1.synchronize()
+    ms_dev = e0.elapsed_time(e1)
+    t1 = time.perf_counter()
+    for k in range(long_steps):
+        gen.step_pcm(voc, ids, [i + 3 + long_steps + k for i in range(64)], want_frames=False)
+    ms_abi = (time.perf_counter() - t1) * 1e3
+    for sid in ids:
+        gen.session_free(sid)
+        voc.stream_close(sid)
+    prompt = [sp["text"].count("<|t") + sp.get("ref_frames", 0) for sp in specs]
+    out["long_context"] = {
+        "sessions": 64, "prompt_positions_mean": float(np.mean(prompt)), "prompt_positions_max": int(max(prompt)),
+        "context_at_end_max": int(max(prompt)) + 3 + 2 * long_steps,
+        "ms_per_step": ms_dev / long_steps, "rtf": 64 * long_steps * FRAME_S / (ms_dev / 1e3),
+        "e2e_ms_per_step": ms_abi / long_steps, "e2e_rtf": 64 * long_steps * FRAME_S / (ms_abi / 1e3),
+        "method": "64 sessions prefilled to long contexts (text and voice prompt positions as shown, plus the "
+                  "instruction), then serving steps with PCM: bzb_generator_step_pcm_device timed by CUDA events, "
+                  "then bzb_generator_sessions_step_pcm with host buffers (host wall clock)"}
+    return out
+
+
 def config4(pkg, args, local, n_sessions=40):
     """Configuration 4: a Q4_K model (backbone and depth linears Q4_K); 40 sessions per GPU arrive
     at t = 0 (prompts U[32,256] tokens, 5 s voice contexts of 63 frames, generation U[100,300]
@@ -562,7 +672,8 @@ def main():
     voc = pkg.VocoderHandle(generator=gen)
     t_load = time.perf_counter() - t_load
     nc = gen.nc
-    srv = Server(gen, voc, Arrivals(pkg, nc, 1000 + rank), args.sessions)
+    cap = max(1, args.prompt_cap)
+    srv = Server(gen, voc, Arrivals(pkg, nc, 1000 + rank, prompt=(min(16, cap), cap)), args.sessions)
     # ramp: from a cold start to the steady state of the closed loop (ages and contexts mixed)
     t_ramp = time.perf_counter()
     for _ in range(args.ramp):
@@ -579,6 +690,18 @@ def main():
         gen.sync()
         torch.cuda.profiler.stop()
         print(json.dumps({"profiled_admissions": n}))
+        voc.close()
+        gen.close()
+        return
+    if args.profile_create:
+        specs = [srv.arr.take() for _ in range(args.sessions)]
+        gen.sync()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        gen.sessions_create_batch(specs)
+        gen.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled_creations": len(specs)}))
         voc.close()
         gen.close()
         return
@@ -682,10 +805,12 @@ def main():
         configs["abi_path"] = abi_path(pkg, gen, srv, nc)
     if "2" in want:
         configs["c2_16_equal_sessions"] = config2(pkg, gen, voc, nc)
-    # the main generator's sessions are done with: free them before other models load
+    # the main generator's sessions are done with: free them before other workloads
     for sid in list(srv.live):
         gen.session_free(sid)
         voc.stream_close(sid)
+    if "5" in want:
+        configs["c5_streaming_elastic"] = config5(pkg, gen, voc, nc, 5000 + rank)
     voc.close()
     gen.close()
     if "1" in want:

@@ -34,12 +34,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
 
 // bounded wait for the completion of the mbarrier phase with the given parity; returns false
 // when `limit` polls pass (recording error code 1) or as soon as another thread has recorded an
-// error, instead of spinning forever
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int * err, long long limit = kSpinLimit) {
+// error, instead of spinning forever. `backoff_ns` > 0 sleeps that long between polls after the
+// first few, so that a warp with a long wait ahead leaves the issue slots to the warps doing
+// the work (the MMA issuer, whose latency paces the pipeline, polls without pause)
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int * err, long long limit = kSpinLimit,
+                                          unsigned backoff_ns = 0) {
     const uint32_t a = smem_u32(bar);
     for (long long i = 0; i < limit; i++) {
         if (mbar_try(a, parity)) return true;
         if ((i & 1023) == 1023 && err && *reinterpret_cast<volatile int *>(err)) return false;
+        if (backoff_ns && i >= 4) __nanosleep(backoff_ns);
     }
     if (err) atomicCAS(err, 0, 1);
     return false;

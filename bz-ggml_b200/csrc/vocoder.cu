@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     int * wtau = wseg + p.win_rows;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int phases = a.ostride, phase = blockIdx.z % phases, split = blockIdx.z / phases, ot = blockIdx.y;
+    const int P = a.ostride, split = blockIdx.z, ot = blockIdx.y;
     const int c_beg = split * p.cps, c_end = min(p.kchunks, c_beg + p.cps);
     const int t0 = blockIdx.x * kTM;
     const int halo = (a.taps - 1) * a.dil;
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     if (warp == 8) tmem_alloc(&tmem_slot, cols);
     if (tid == 0) {
         for (int i = 0; i < AS; i++) {
-            mbar_init(&a_full[i], 256);
+            mbar_init(&a_full[i], 8);   // one arrival per producer warp
             mbar_init(&a_empty[i], 1);
         }
         for (int i = 0; i < BS; i++) {
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
                 }
             }
             bar_producers();  // the window is complete
-            if (a.st && halo > 0 && ot == 0 && phase == 0) {
+            if (a.st && halo > 0 && ot == 0) {
                 // segments whose last step is in this tile: the new state of this chunk's channels
                 for (int b = b_first; b * seg + seg - 1 <= n_last; b++) {
                     float * dst = a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) voc_state_next(a.seg_par[b]) * a.cin * halo;
@@ -490,7 +490,8 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
             }
             for (int k = 0; k < a.taps; k++, it++) {
                 const int st = it % AS;
-                if (ok && it >= AS) ok = mbar_wait(&a_empty[st], (uint32_t) ((it / AS) - 1) & 1u, p.err);
+                if (ok && it >= AS) ok = mbar_wait(&a_empty[st], (uint32_t) ((it / AS) - 1) & 1u, p.err, kSpinLimit, 32);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) {
                     s_abort = 1;
                     continue;
@@ -503,8 +504,9 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
                     const uint4 v = *reinterpret_cast<const uint4 *>(sW + (size_t) u * 128 + ((j ^ (u & 7)) << 4));
                     *reinterpret_cast<uint4 *>(A + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4)) = v;
                 }
-                fence_proxy_async();
-                mbar_arrive(&a_full[st]);
+                fence_proxy_async();  // each thread's stores before the warp's arrival
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[st]);
             }
         }
     } else if (warp == 8) {
@@ -527,12 +529,11 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
         }
     } else {
         if (lane == 0) {
-            const uint8_t * base = reinterpret_cast<const uint8_t *>(p.w16) +
-                                   (((size_t) phase * p.otiles + ot) * p.kchunks + c_beg) * a.taps * (size_t) tb;
+            const uint8_t * base = reinterpret_cast<const uint8_t *>(p.w16) + ((size_t) ot * p.kchunks + c_beg) * a.taps * (size_t) tb;
             int issued = 0;
             for (int it = 0; it < n_it; it++) {
                 const int sb = it % BS;
-                if (it >= BS) ok = mbar_wait(&b_empty[sb], (uint32_t) ((it / BS) - 1) & 1u, p.err);
+                if (it >= BS) ok = mbar_wait(&b_empty[sb], (uint32_t) ((it / BS) - 1) & 1u, p.err, kSpinLimit, 64);
                 if (!ok) break;
                 mbar_expect_tx(&b_full[sb], tb);
                 bulk_g2s(sB + sb * tb, base + (size_t) it * tb, tb, &b_full[sb]);
@@ -544,38 +545,64 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     }
 
     if (warp < 8) {
-        if (!mbar_wait(&done_bar, 0u, p.err)) ok = false;
-        tc_fence_after();
         const int q = warp & 3, hh = warp >> 2, half_cols = p.nt / 2;
         const int t = t0 + 32 * q + lane;
+        const size_t tcol = (size_t) t * P;
+        const bool want_res = a.res && p.splits == 1 && t < a.L;
+        // the residual of a 16-column group (zero past the outputs), loaded one group ahead of its
+        // use and the first group before the wait for the accumulator, so that its latency hides
+        // behind the MMAs and the previous group's stores (the loads of one group never touch
+        // another group's outputs, so reading ahead of the in-place stores is safe)
+        auto load_res = [&](int c0, float * r) {
+            const int ob = ot * p.nt + c0, ne = min(16, a.cout * P - ob);
+            int o = ob / P, ph = ob - (ob / P) * P;
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                r[e] = (want_res && e < ne) ? a.res[(size_t) o * a.ldy + tcol + ph] : 0.0f;
+                if (++ph == P) {
+                    ph = 0;
+                    o++;
+                }
+            }
+        };
+        float rn[16];
+        load_res(hh * half_cols, rn);
+        if (!mbar_wait(&done_bar, 0u, p.err, kSpinLimit, 128)) ok = false;
+        tc_fence_after();
         const bool live = ok && t < a.L;
-        const size_t tcol = (size_t) t * a.ostride + phase;
         for (int c0 = hh * half_cols; c0 < (hh + 1) * half_cols; c0 += 16) {  // warp-uniform: every lane loads
+            float r[16];
+#pragma unroll
+            for (int e = 0; e < 16; e++) r[e] = rn[e];
+            if (c0 + 16 < (hh + 1) * half_cols) load_res(c0 + 16, rn);
             float v[16];
             tmem_ld16(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
-            const int ob = ot * p.nt + c0, ne = min(16, a.cout - ob);
+            // column g = ob + e is output channel g / P, phase g % P
+            const int ob = ot * p.nt + c0, ne = min(16, a.cout * P - ob);
+            const int o0 = ob / P, ph0 = ob - o0 * P;
             if (live && p.splits > 1) {
-#pragma unroll
-                for (int e = 0; e < 16; e++)
-                    if (e < ne) a.part[conv_part_index(a, split, ob + e, t, phase)] = n_it > 0 ? v[e] : 0.0f;
-            } else if (live) {
-                // every load of the 16 outputs before the first store: y may be the residual
-                // itself (updated in place), which would otherwise serialise load after store
+                int o = o0, ph = ph0;
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    float add = 0.0f;
-                    if (e < ne) {
-                        if (a.bias) add = __ldg(a.bias + ob + e);
-                        if (a.res) add += a.res[(size_t) (ob + e) * a.ldy + tcol];
+                    if (e < ne) a.part[conv_part_index(a, split, o, t, ph)] = n_it > 0 ? v[e] : 0.0f;
+                    if (++ph == P) {
+                        ph = 0;
+                        o++;
                     }
-                    v[e] += add;
                 }
+            } else if (live) {
+                int o = o0, ph = ph0;
 #pragma unroll
-                for (int e = 0; e < 16; e++)
-                    if (e < ne) conv_store(a, ob + e, (size_t) (ob + e) * a.ldy + tcol, v[e]);
+                for (int e = 0; e < 16; e++) {
+                    if (e < ne) conv_store(a, o, (size_t) o * a.ldy + tcol + ph, v[e] + r[e] + (a.bias ? __ldg(a.bias + o) : 0.0f));
+                    if (++ph == P) {
+                        ph = 0;
+                        o++;
+                    }
+                }
             }
         }
     }
@@ -660,36 +687,57 @@ __global__ void voc_kv_ring_append_kernel(const float * k, const float * v, int 
 
 // causal sliding-window attention of T new frames per stream over its ring (keys already
 // rotated): one warp per (row s T + t, head h), query at position pos0[s] + t, keys
-// pos - window < j <= pos; hd <= 128
-__global__ void voc_attn_ring_kernel(const float * q, int S, int T, int nh, int nkv, int hd, int window,
+// pos - window < j <= pos; hd <= 128, a multiple of 4. The positions go in blocks of 32, one per
+// lane: each lane forms its position's score from the whole key row (the rotated query sits in
+// shared memory), so the key loads of a block are independent of one another; the block's
+// softmax weights are then broadcast lane by lane into the value sums of the lane's dims (online
+// rescaling between blocks).
+__global__ void __launch_bounds__(128) voc_attn_ring_kernel(const float * q, int S, int T, int nh, int nkv, int hd, int window,
                                      const float2 * rope, float scale, const float * ring, size_t slot_stride, int R,
                                      const int * slots, const int * pos0, half * out) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    __shared__ float qs[4][128];
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     if (warp >= S * T * nh) return;
     const int row = warp / nh, h = warp % nh, sgm = row / T, t = row - sgm * T, g = h / (nh / nkv);
     const int E = hd / 32, half_d = hd / 2, kvd = nkv * hd;
     const int pos = pos0[sgm] + t;
-    const float * base = ring + (size_t) slots[sgm] * slot_stride;
-    float qv[4];
-    for (int e = 0; e < E; e++) {
-        const int d = lane + 32 * e;
+    const float * base = ring + (size_t) slots[sgm] * slot_stride + (size_t) g * hd;
+    for (int d = lane; d < hd; d += 32) {
         const int dp = d < half_d ? d + half_d : d - half_d;
         const float x0 = q[((size_t) row * nh + h) * hd + d], x1 = q[((size_t) row * nh + h) * hd + dp];
         const float2 cs = rope[(size_t) pos * half_d + (d < half_d ? d : d - half_d)];
-        qv[e] = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
+        qs[wib][d] = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
     }
+    __syncwarp();
     const int j0 = max(0, window > 0 ? pos - window + 1 : 0);
     float m = -INFINITY, l = 0.0f, acc[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
-    for (int j = j0; j <= pos; j++) {
-        const float * kr = base + (size_t) (j % R) * 2 * kvd + (size_t) g * hd;
-        float dot = 0.0f;
-        for (int e = 0; e < E; e++) dot += qv[e] * kr[lane + 32 * e];
-        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        const float sc = dot * scale;
-        const float mn = fmaxf(m, sc);
-        const float corr = expf(m - mn), p = expf(sc - mn);
-        l = l * corr + p;
-        for (int e = 0; e < E; e++) acc[e] = acc[e] * corr + p * kr[kvd + lane + 32 * e];
+    for (int jb = j0; jb <= pos; jb += 32) {
+        const int j = jb + lane;
+        float sc = -INFINITY;
+        if (j <= pos) {
+            const float4 * kr = reinterpret_cast<const float4 *>(base + (size_t) (j % R) * 2 * kvd);
+            float dot = 0.0f;
+            for (int i = 0; i < hd / 4; i++) {
+                const float4 kk = kr[i];
+                dot += qs[wib][4 * i] * kk.x + qs[wib][4 * i + 1] * kk.y + qs[wib][4 * i + 2] * kk.z + qs[wib][4 * i + 3] * kk.w;
+            }
+            sc = dot * scale;
+        }
+        float mb = sc;
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float mn = fmaxf(m, mb);
+        const float corr = expf(m - mn);
+        const float p = j <= pos ? expf(sc - mn) : 0.0f;
+        float ps = p;
+        for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        l = l * corr + ps;
+        for (int e = 0; e < E; e++) acc[e] *= corr;
+        const int nb = min(32, pos - jb + 1);
+        for (int jj = 0; jj < nb; jj++) {
+            const float pj = __shfl_sync(0xffffffffu, p, jj);
+            const float * vr = base + (size_t) ((jb + jj) % R) * 2 * kvd + kvd;
+            for (int e = 0; e < E; e++) acc[e] += pj * vr[lane + 32 * e];
+        }
         m = mn;
     }
     for (int e = 0; e < E; e++) out[((size_t) row * nh + h) * hd + lane + 32 * e] = __float2half_rn(acc[e] / l);
@@ -855,13 +903,13 @@ void launch_conv(ConvArgs a, int phases, float * scratch, size_t scratch_floats,
 }
 
 // the tcgen05 convolution of `a` (istride 1) with weights tiled as `c` describes
-void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunks, int phases, int * err,
+void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunks, int * err,
                     float * scratch, size_t scratch_floats, cudaStream_t s) {
     if (a.L <= 0) return;
     if (a.istride != 1) throw std::runtime_error("tcgen05 conv: strided input is not supported");
     a.Lin = a.L;
     // small grids: split the input-channel chunks across CTAs until about two waves are in flight
-    const int tiles = ((a.L + kTM - 1) / kTM) * otiles * phases;
+    const int tiles = ((a.L + kTM - 1) / kTM) * otiles;  // otiles cover the phases too
     int splits = 1;
     while (tiles * splits * 2 <= 2 * 148 && splits * 2 <= kchunks && splits < 16 &&
            (size_t) splits * 2 * a.cout * a.ldy <= scratch_floats)
@@ -889,7 +937,7 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     p.b_stages = 3;
     // grids of more than one wave: two CTAs per SM (one's staging and epilogue latency hidden
     // behind the other's work) when two-stage rings make room for them
-    const long long ctas = (long long) ((a.L + kTM - 1) / kTM) * otiles * phases * splits;
+    const long long ctas = (long long) tiles * splits;
     const size_t two_per_sm = (size_t) 113 * 1024;
     if (ctas > 148 && smem(2, 2) <= two_per_sm)
         while (smem(p.a_stages, p.b_stages) > two_per_sm) {
@@ -912,7 +960,7 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
             attr_set[dev] = true;
         }
     }
-    const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) (phases * splits));
+    const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) splits);
     voc_conv_tc_kernel<<<grid, kTThreads, smem(p.a_stages, p.b_stages), s>>>(p);
     if (splits > 1) launch_conv_reduce(a, s);
 }
@@ -1044,19 +1092,20 @@ Vocoder::Conv Vocoder::load_conv(const std::string & name, int K, int cin, int c
 }
 
 void Vocoder::tile_conv_f16(Conv & c, const std::vector<float> & h) {
-    c.otiles = (c.cout + 255) / 256;
-    c.nt = ((c.cout + c.otiles - 1) / c.otiles + 31) / 32 * 32;
+    const int ncol = c.cout * c.phases;
+    c.otiles = (ncol + 255) / 256;
+    c.nt = ((ncol + c.otiles - 1) / c.otiles + 31) / 32 * 32;
     c.kchunks = (c.cin + 63) / 64;
     const size_t tile = (size_t) c.nt * 64;  // halves
-    std::vector<half> t((size_t) c.phases * c.otiles * c.kchunks * c.taps * tile, __float2half(0.0f));
-    for (int ph = 0; ph < c.phases; ph++)
-        for (int ot = 0; ot < c.otiles; ot++)
-            for (int ch = 0; ch < c.kchunks; ch++)
-                for (int k = 0; k < c.taps; k++) {
-                    half * dst = t.data() + ((((size_t) ph * c.otiles + ot) * c.kchunks + ch) * c.taps + k) * tile;
-                    for (int n = 0; n < c.nt; n++) {
-                        const int o = ot * c.nt + n;
-                        if (o >= c.cout) continue;
+    std::vector<half> t((size_t) c.otiles * c.kchunks * c.taps * tile, __float2half(0.0f));
+    for (int ot = 0; ot < c.otiles; ot++)
+        for (int ch = 0; ch < c.kchunks; ch++)
+            for (int k = 0; k < c.taps; k++) {
+                half * dst = t.data() + (((size_t) ot * c.kchunks + ch) * c.taps + k) * tile;
+                for (int n = 0; n < c.nt; n++) {
+                        const int g = ot * c.nt + n;
+                        if (g >= ncol) continue;
+                        const int o = g / c.phases, ph = g % c.phases;
                         for (int i = 0; i < 64; i++) {
                             const int ci = ch * 64 + i;
                             if (ci >= c.cin) continue;
@@ -1064,8 +1113,8 @@ void Vocoder::tile_conv_f16(Conv & c, const std::vector<float> & h) {
                             const size_t byte = (size_t) (n / 8) * 1024 + (n % 8) * 128 + (size_t) (((i / 8) ^ (n % 8)) * 16) + (i % 8) * 2;
                             dst[byte / 2] = __float2half_rn(h[(((size_t) ph * c.cout + o) * c.taps + k) * c.cin + ci]);
                         }
-                    }
                 }
+            }
     c.w16 = dalloc<half>(t.size());
     VCHECK(cudaMemcpyAsync(c.w16, t.data(), t.size() * sizeof(half), cudaMemcpyHostToDevice, stream_));
     // the host vector goes out of scope: the upload must complete first
@@ -1395,7 +1444,7 @@ void Vocoder::decode_segments(const int * codes_dev, int ld_codes, int S, int T,
             ca.seg_par = d_par;
         }
         li++;
-        launch_conv_tc(ca, c.w16, c.nt, c.otiles, c.kchunks, c.phases, err_, part_, 2 * act_elems_, s);
+        launch_conv_tc(ca, c.w16, c.nt, c.otiles, c.kchunks, err_, part_, 2 * act_elems_, s);
     };
     transpose(t32_, NF, cbdim_, a_, nullptr);
     conv(dpre_, a_, T, 1, b_);                                       // [latent][NF]

@@ -94,9 +94,11 @@ private:
         float * b = nullptr;
         int cin = 0, cout = 0, K = 0;
         int taps = 0, phases = 1, stride = 0;
-        // the tcgen05 convolution's weights: f16 tiles [phases][otiles][kchunks][taps] of nt output
-        // channels x 64 input channels, each the 128-byte-swizzled K-major image one bulk copy
-        // brings into shared memory (rows and channels past cout / cin are zero)
+        // the tcgen05 convolution's weights: f16 tiles [otiles][kchunks][taps] of nt output
+        // columns x 64 input channels, each the 128-byte-swizzled K-major image one bulk copy
+        // brings into shared memory. Column g is output channel g / phases of phase g % phases:
+        // every phase of a transposed conv reads the same input window, so the phases are more
+        // output columns of one GEMM (rows past cout x phases and channels past cin are zero)
         half * w16 = nullptr;
         int nt = 0, otiles = 0, kchunks = 0;
     };
