@@ -1100,9 +1100,9 @@ int Engine::acquire_slot(int sid, int n_pages, bool register_sid) {
     }
     std::vector<int> row(max_pages_, s.pages.empty() ? 0 : s.pages[0]);
     for (int i = 0; i < n_pages; i++) row[i] = s.pages[i];
+    // a copy from pageable host memory is staged before the call returns: `row` may go
     CK(cudaMemcpyAsync(page_table_ + (size_t) slot * max_pages_, row.data(), max_pages_ * sizeof(int),
                        cudaMemcpyHostToDevice, stream_));
-    CK(cudaStreamSynchronize(stream_));
     if (register_sid) {
         sid_to_slot_[sid] = slot;
         sid_epoch_[sid] = ++epoch_ctr_;
@@ -1121,10 +1121,11 @@ void Engine::release_slot(int slot) {
     if (partner >= 0) release_slot(partner);  // the session's unconditional branch
 }
 
+// the slot and its pages go back to the free lists at once: whatever reuses them is enqueued on
+// the same stream, after the work that still reads them
 bool Engine::session_free(int sid) {
     auto it = sid_to_slot_.find(sid);
     if (it == sid_to_slot_.end()) return false;
-    CK(cudaStreamSynchronize(stream_));
     release_slot(it->second);
     return true;
 }
@@ -1521,8 +1522,9 @@ void Engine::sessions_create_batch(const std::vector<CreateSpec> & specs, int * 
             nseg += prep[g1].total_u ? 2 : 1;
             g1++;
         }
-        CK(cudaStreamSynchronize(stream_));
-        // slots (a reused id frees its old slot first, src/c_api.cpp:333-337)
+        // slots (a reused id frees its old slot first, src/c_api.cpp:333-337); the work still
+        // queued on the stream is ordered before everything enqueued here
+
         std::vector<int> slot_c(g1 - g0, -1), slot_u(g1 - g0, -1);
         try {
             for (int i = g0; i < g1; i++) {
@@ -1577,8 +1579,7 @@ void Engine::sessions_create_batch(const std::vector<CreateSpec> & specs, int * 
                 CK(cudaMemcpyAsync(pidx_, fdst.data(), F * sizeof(int), cudaMemcpyHostToDevice, stream_));
                 launch_copy_rows(pstage_, H, nullptr, px_, H, pidx_, F, H, stream_);
             }
-            CK(cudaStreamSynchronize(stream_));  // host vectors feeding the copies go out of scope
-            bb_prefill_packed(segs, plogs_);
+            bb_prefill_packed(segs, plogs_);  // (copies from pageable host vectors are staged at the call)
             // session states, histories, and the first cb0 of every session (guidance-combined)
             const int nb = (int) segs.size();
             std::vector<int> rslot(nb), rpair(nb, -1), lead_of_spec(g1 - g0, -1);
