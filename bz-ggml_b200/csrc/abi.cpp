@@ -48,6 +48,29 @@ struct breeze_context {
 };
 
 namespace {
+// Every call that reaches a handle's GPU runs with the handle's device current and gives the
+// calling thread its previous device back: one process may serve islands on several GPUs from
+// several threads, each thread with whatever device it last used.
+class OnDevice {
+public:
+    explicit OnDevice(int device) {
+        if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+        // never throws (some callers are outside a try block): a device that cannot be selected
+        // makes the call's first CUDA operation fail, and that failure is reported
+        if (prev_ != device) cudaSetDevice(device);
+        restore_ = prev_ >= 0 && prev_ != device;
+    }
+    ~OnDevice() {
+        if (restore_) cudaSetDevice(prev_);
+    }
+    OnDevice(const OnDevice &) = delete;
+    OnDevice & operator=(const OnDevice &) = delete;
+
+private:
+    int prev_ = -1;
+    bool restore_ = false;
+};
+
 // per-thread last error: the reference keeps one unsynchronised global (src/c_api.cpp:28);
 // each calling thread reads the message of its own last failing call here
 thread_local std::string g_error;
@@ -91,6 +114,7 @@ int generate_impl(breeze_context * ctx, const breeze_request * req, const int * 
                   double * out_timings) {
     if (!ctx || !req) { set_error("null context or request"); return 1; }
     try {
+        OnDevice on_device_(ctx->gen->device);
         bzb::GenRequest g = to_gen_request(req);
         const int nc = ctx->gen->eng->cfg.nc;
         if (ref_codes && ref_frames > 0) g.ref_codes.assign(ref_codes, ref_codes + (size_t) ref_frames * nc), g.ref_frames = ref_frames;
@@ -161,6 +185,7 @@ breeze_context * breeze_init(const char * gguf_path, int use_gpu) {
 
 void breeze_free(breeze_context * ctx) {
     if (!ctx) return;
+    OnDevice on_device_(ctx->gen ? ctx->gen->device : 0);
     ctx->voc.reset();
     breeze_generator_free(ctx->gen);
     delete ctx;
@@ -177,6 +202,7 @@ int breeze_generate(breeze_context * ctx, const breeze_request * req, breeze_aud
 int breeze_generate_wav(breeze_context * ctx, const breeze_request * req, const char * out_path) {
     if (!ctx || !req || !out_path) { set_error("null argument"); return 1; }
     try {
+        OnDevice on_device_(ctx->gen->device);
         std::vector<float> audio;
         bzb::GenRequest g = to_gen_request(req);
         encode_ref_audio(ctx, g);
@@ -214,6 +240,7 @@ breeze_generator * breeze_generator_init(const char * gguf_path, int cuda_device
 
 void breeze_generator_free(breeze_generator * gen) {
     if (!gen) return;
+    OnDevice on_device_(gen->device);
     delete gen;
 }
 
@@ -221,6 +248,7 @@ int breeze_generator_prefill(breeze_generator * gen, const char * text, const ch
                              int * out_cb0) {
     if (!gen || !text || !out_cb0) return -1;
     try {
+        OnDevice on_device_(gen->device);
         int alloc = 0;
         gen->eng->session_create(kLegacySession, text, instruction, nullptr, nullptr, 0, 1.0f, seed,
                                  gen->eng->cfg.max_new_tokens > 0 ? gen->eng->cfg.max_new_tokens : 2048, out_cb0, &alloc);
@@ -235,6 +263,7 @@ int breeze_generator_step_frame(breeze_generator * gen, int cb0, unsigned int se
     (void) cb0;  // the session's own last cb0 is the one the reference's caller passes back
     if (!gen || !out_frame_16 || !gen->eng->session_active(kLegacySession)) return -1;
     try {
+        OnDevice on_device_(gen->device);
         const int sid = kLegacySession;
         int next = -1;
         // depth codes from the GGUF's depth sampler with the call's seed (src/c_api.cpp:297-299)
@@ -252,6 +281,7 @@ int breeze_generator_session_create_ext(breeze_generator * gen, int session_id, 
                                         int * out_cb0, int * out_allocated_tokens) {
     if (!gen || !text || !out_cb0) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->session_create(session_id, text, instruction, ref_text, ref_codes, ref_frames, cfg_scale, seed,
                                  max_new_tokens, out_cb0, out_allocated_tokens);
         return 0;
@@ -271,6 +301,7 @@ int breeze_generator_session_step(breeze_generator * gen, int session_id, unsign
     if (!gen || !out_frame_16) return -1;
     if (!gen->eng->session_active(session_id)) return -1;
     try {
+        OnDevice on_device_(gen->device);
         int next = -1;
         // depth codes from the GGUF's depth sampler with the call's seed (src/c_api.cpp:468-479)
         gen->eng->step(&session_id, 1, 1, nullptr, false, out_frame_16, kAbiFrameWidth, &next, false, true, &seed);
@@ -284,6 +315,7 @@ int breeze_generator_session_step(breeze_generator * gen, int session_id, unsign
 int breeze_generator_session_free(breeze_generator * gen, int session_id) {
     if (!gen) return -1;
     try {
+        OnDevice on_device_(gen->device);
         return gen->eng->session_free(session_id) ? 0 : -1;
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -294,6 +326,7 @@ int breeze_generator_session_free(breeze_generator * gen, int session_id) {
 int breeze_generator_load_q4_depth(breeze_generator * gen, const char * q4_gguf_path) {
     if (!gen || !q4_gguf_path) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->load_q4_depth(q4_gguf_path);
         return 0;
     } catch (const std::exception & e) {
@@ -304,6 +337,7 @@ int breeze_generator_load_q4_depth(breeze_generator * gen, const char * q4_gguf_
 
 int breeze_generator_session_set_q4(breeze_generator * gen, int session_id, int use_q4) {
     if (!gen) return -1;
+    OnDevice on_device_(gen->device);
     // without a loaded Q4 depth piece the flag resolves to off (src/c_api.cpp:576)
     return gen->eng->session_set_q4(session_id, use_q4 != 0) ? 0 : -1;
 }
@@ -326,6 +360,7 @@ int breeze_generator_sessions_step_batched(breeze_generator * gen, const int * s
                                            const unsigned int * seeds, int * out_frames_16, int * out_next_cb0) {
     if (!gen || !session_ids || num_sessions <= 0 || !out_frames_16 || !out_next_cb0) return 0;
     try {
+        OnDevice on_device_(gen->device);
         const bzb::StepResult r = gen->eng->step(session_ids, num_sessions, 1, seeds, false, out_frames_16,
                                                  kAbiFrameWidth, out_next_cb0, false);
         return r.steps_executed == 0 ? 0 : r.still_active;
@@ -340,6 +375,7 @@ int breeze_generator_sessions_step_burst(breeze_generator * gen, const int * ses
                                          int * out_next_cb0) {
     if (!gen || !session_ids || num_sessions <= 0 || burst_steps <= 0 || !out_frames_burst || !out_next_cb0) return 0;
     try {
+        OnDevice on_device_(gen->device);
         return burst_impl(gen, session_ids, num_sessions, burst_steps, seeds, out_frames_burst, kAbiFrameWidth, out_next_cb0);
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -353,6 +389,7 @@ int breeze_generator_convert_voice(breeze_generator * gen, const int * src_codes
                                    unsigned int seed, int * out_codes, float * out_pcm, int max_out_pcm) {
     if (!gen || !src_codes || src_T <= 0) return -1;
     try {
+        OnDevice on_device_(gen->device);
         bzb::Engine & eng = *gen->eng;
         const int nc = eng.cfg.nc, spf = bzb::Vocoder::kSamplesPerFrame;
         // frames are num_codebooks codes apart (the reference indexes them so, src/generation.cpp:346-364);
@@ -436,6 +473,7 @@ int breeze_generator_encode_audio(breeze_generator * gen, const float * pcm, int
                                   int * out_n_frames) {
     if (!gen || !pcm || n_samples <= 0 || !out_codes || !out_n_frames) return -1;
     try {
+        OnDevice on_device_(gen->device);
         // frames of min(num_codebooks, 16) codes: the ABI's frame width (the bindings size the
         // buffer at 16 codes per frame, python/bz_ggml/bindings.py:444-446)
         std::vector<int> codes;
@@ -471,11 +509,16 @@ breeze_vocoder * breeze_vocoder_init(const char * gguf_path, int cuda_device) {
     }
 }
 
-void breeze_vocoder_free(breeze_vocoder * voc) { delete voc; }
+void breeze_vocoder_free(breeze_vocoder * voc) {
+    if (!voc) return;
+    OnDevice on_device_(voc->device);
+    delete voc;
+}
 
 breeze_vocoder * breeze_vocoder_create_from_generator(breeze_generator * gen) {
     if (!gen) return nullptr;
     try {
+        OnDevice on_device_(gen->device);
         auto v = std::make_unique<breeze_vocoder>();
         v->device = gen->device;
         // the generator's stream: decodes are ordered after its frame steps and may read their
@@ -490,6 +533,7 @@ breeze_vocoder * breeze_vocoder_create_from_generator(breeze_generator * gen) {
 
 int breeze_vocoder_session_create(breeze_vocoder * voc, int session_id) {
     if (!voc || !voc->voc) return -1;
+    OnDevice on_device_(voc->device);
     voc->voc->session_create(session_id);
     return 0;
 }
@@ -498,6 +542,7 @@ int breeze_vocoder_session_decode(breeze_vocoder * voc, int session_id, const in
                                   float * out_pcm) {
     if (!voc || !voc->voc || !frames || n_frames <= 0 || !out_pcm) return 0;
     try {
+        OnDevice on_device_(voc->device);
         return voc->voc->session_decode(session_id, frames, n_frames, out_pcm);
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -511,6 +556,7 @@ int breeze_vocoder_session_decode_batch(breeze_vocoder * voc, int batch_size, co
                                         int * out_n_samples) {
     if (!voc || !voc->voc || batch_size <= 0 || !session_ids || !flat_tokens || !n_frames_per_stream || !flat_pcm) return 0;
     try {
+        OnDevice on_device_(voc->device);
         return voc->voc->session_decode_batch(batch_size, session_ids, flat_tokens, token_offsets, n_frames_per_stream,
                                               flat_pcm, pcm_offsets, out_n_samples);
     } catch (const std::exception & e) {
@@ -521,12 +567,14 @@ int breeze_vocoder_session_decode_batch(breeze_vocoder * voc, int batch_size, co
 
 int breeze_vocoder_session_free(breeze_vocoder * voc, int session_id) {
     if (!voc || !voc->voc) return -1;
+    OnDevice on_device_(voc->device);
     return voc->voc->session_free(session_id) ? 0 : -1;
 }
 
 int breeze_vocoder_stream_decode(breeze_vocoder * voc, const int * frames, int n_frames, float * out_pcm) {
     if (!voc || !voc->voc || !frames || n_frames <= 0 || !out_pcm) return 0;
     try {
+        OnDevice on_device_(voc->device);
         return voc->voc->stream_decode(frames, n_frames, out_pcm);
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -539,6 +587,7 @@ int breeze_vocoder_stream_decode_batch(breeze_vocoder * voc, int batch_size, con
                                        const int * pcm_offsets, int * out_n_samples) {
     if (!voc || !voc->voc || batch_size <= 0 || !flat_tokens || !n_frames_per_stream || !flat_pcm) return 0;
     try {
+        OnDevice on_device_(voc->device);
         return voc->voc->stream_decode_batch(batch_size, flat_tokens, token_offsets, n_frames_per_stream, flat_pcm,
                                              pcm_offsets, out_n_samples);
     } catch (const std::exception & e) {
@@ -624,6 +673,7 @@ int bzb_generator_sessions_step_frames(breeze_generator * gen, const int * sessi
                                        int * out_next_cb0) {
     if (!gen || !session_ids || num_sessions <= 0 || burst_steps <= 0 || !out_frames || !out_next_cb0) return 0;
     try {
+        OnDevice on_device_(gen->device);
         return burst_impl(gen, session_ids, num_sessions, burst_steps, seeds, out_frames, gen->eng->nc(), out_next_cb0);
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -634,6 +684,7 @@ int bzb_generator_sessions_step_frames(breeze_generator * gen, const int * sessi
 int bzb_generator_step_device(breeze_generator * gen, int burst_steps) {
     if (!gen || burst_steps <= 0) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->step_device_only(burst_steps);
         return 0;
     } catch (const std::exception & e) {
@@ -645,6 +696,7 @@ int bzb_generator_step_device(breeze_generator * gen, int burst_steps) {
 int bzb_generator_sync(breeze_generator * gen) {
     if (!gen) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->sync();
         return 0;
     } catch (const std::exception & e) {
@@ -668,6 +720,7 @@ int bzb_generator_launches_per_step(breeze_generator * gen) { return gen ? gen->
 int bzb_generator_profile_step(breeze_generator * gen, double * out7) {
     if (!gen || !out7) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->profile_step(out7);
         return 0;
     } catch (const std::exception & e) {
@@ -679,6 +732,7 @@ int bzb_generator_profile_step(breeze_generator * gen, double * out7) {
 int bzb_generator_debug_hidden(breeze_generator * gen, int session_id, float * out) {
     if (!gen || !out) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->debug_hidden(session_id, out);
         return 0;
     } catch (const std::exception & e) {
@@ -691,6 +745,7 @@ int bzb_generator_debug_depth(breeze_generator * gen, int n, const float * hidde
                               int * out_codes, float * out_logits) {
     if (!gen || !hidden || !cb0 || !out_codes || !out_logits) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->debug_depth(n, hidden, cb0, forced, out_codes, out_logits);
         return 0;
     } catch (const std::exception & e) {
@@ -702,6 +757,7 @@ int bzb_generator_debug_depth(breeze_generator * gen, int n, const float * hidde
 int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int sub, int rows, const float * x, float * y) {
     if (!gen || !tensor || rows <= 0 || !x || !y) return -1;
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->debug_gemv(tensor, sub, rows, x, y);
         return 0;
     } catch (const std::exception & e) {
@@ -714,6 +770,7 @@ int bzb_generator_debug_gemv(breeze_generator * gen, const char * tensor, int su
 int bzb_vocoder_stream_open(breeze_vocoder * voc, int stream_id) {
     if (!voc) return -1;
     try {
+        OnDevice on_device_(voc->device);
         voc->voc->stream_open(stream_id);
         return 0;
     } catch (const std::exception & e) {
@@ -724,6 +781,7 @@ int bzb_vocoder_stream_open(breeze_vocoder * voc, int stream_id) {
 
 int bzb_vocoder_stream_close(breeze_vocoder * voc, int stream_id) {
     if (!voc) return -1;
+    OnDevice on_device_(voc->device);
     return voc->voc->stream_close(stream_id) ? 0 : -1;
 }
 
@@ -734,6 +792,7 @@ int bzb_vocoder_streams_decode(breeze_vocoder * voc, int n, const int * stream_i
         return -1;
     }
     try {
+        OnDevice on_device_(voc->device);
         voc->voc->streams_decode(n, stream_ids, nullptr, codes, n_frames, out_pcm);
         return n;
     } catch (const std::exception & e) {
@@ -745,6 +804,7 @@ int bzb_vocoder_streams_decode(breeze_vocoder * voc, int n, const int * stream_i
 int bzb_vocoder_kernels_per_decode(breeze_vocoder * voc, int n_streams, int n_frames) {
     if (!voc || n_streams <= 0 || n_frames <= 0) return -1;
     try {
+        OnDevice on_device_(voc->device);
         return voc->voc->kernels_per_decode(n_streams, n_frames);
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -755,6 +815,7 @@ int bzb_vocoder_kernels_per_decode(breeze_vocoder * voc, int n_streams, int n_fr
 int bzb_vocoder_last_pcm(breeze_vocoder * voc, float * out, int n_samples) {
     if (!voc || !out || n_samples < 0) return -1;
     try {
+        OnDevice on_device_(voc->device);
         voc->voc->check_device_error();
         if (cudaMemcpy(out, voc->voc->last_pcm(), (size_t) n_samples * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
             throw std::runtime_error("last_pcm: copy failed");
@@ -780,6 +841,7 @@ int bzb_generator_sessions_step_pcm(breeze_generator * gen, breeze_vocoder * voc
         return -1;
     }
     try {
+        OnDevice on_device_(gen->device);
         if (!same_device_stream(gen, voc)) return -1;
         bzb::Engine & eng = *gen->eng;
         const int nc = eng.nc();
@@ -820,6 +882,7 @@ int bzb_generator_step_pcm_device(breeze_generator * gen, breeze_vocoder * voc, 
         return -1;
     }
     try {
+        OnDevice on_device_(gen->device);
         if (!same_device_stream(gen, voc)) return -1;
         bzb::Engine & eng = *gen->eng;
         std::vector<unsigned long long> epochs(n);
@@ -875,6 +938,7 @@ int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * tensor, int 
         return -1;
     }
     try {
+        OnDevice on_device_(gen->device);
         gen->eng->gemm_noalloc(tensor, rows, static_cast<const half *>(x16), ldx, y, ldy,
                                static_cast<cudaStream_t>(stream));
         return 0;
@@ -887,6 +951,7 @@ int bzb_generator_gemm_noalloc(breeze_generator * gen, const char * tensor, int 
 int bzb_generator_depth_trace(breeze_generator * gen, double * out, int capacity) {
     if (!gen) return -1;
     try {
+        OnDevice on_device_(gen->device);
         return gen->eng->depth_trace(out, capacity);
     } catch (const std::exception & e) {
         set_error(e.what());
@@ -953,6 +1018,7 @@ int bzb_generator_sessions_create_batch(breeze_generator * gen, int n, const int
                                         const int * max_new_tokens, int * out_cb0, int * out_allocated_tokens) {
     if (!gen || n < 0 || (n > 0 && (!session_ids || !texts || !out_cb0))) return -1;
     try {
+        OnDevice on_device_(gen->device);
         std::vector<bzb::CreateSpec> specs(n);
         for (int i = 0; i < n; i++) {
             if (!texts[i]) throw std::runtime_error("null text");
@@ -979,6 +1045,7 @@ int bzb_generator_encode_audio_full(breeze_generator * gen, const float * pcm, i
                                     int max_frames, int * out_n_frames) {
     if (!gen || !pcm || n_samples <= 0 || !out_codes || max_frames < 0 || !out_n_frames) return -1;
     try {
+        OnDevice on_device_(gen->device);
         std::vector<int> codes;
         const int T = gen->encoder().encode(pcm, n_samples, codes);
         const int nc = gen->eng->cfg.nc;
