@@ -274,9 +274,11 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
                 const int bb = s % kBStages, nsub = min(kSC, nch - s * kSC);
                 if (s >= kBStages) ok = mbar_wait(&b_empty[bb], (uint32_t) ((s / kBStages) - 1) & 1u, p.err);
                 if (!ok) break;
-                mbar_expect_tx(&b_full[bb], (uint32_t) (nsub * kBBytes));
-                for (int j = 0; j < nsub; j++)
-                    tma_2d(sB + (bb * kSC + j) * kBBytes, &xmap, (c_beg + s * kSC + j) * kChunkK, row0, &b_full[bb]);
+                // one 3-D box per stage (kSC chunk tiles; every copy costs the SM about the same
+                // time whatever its size): chunks past K read as zeros and are never multiplied
+                (void) nsub;
+                mbar_expect_tx(&b_full[bb], (uint32_t) (kSC * kBBytes));
+                tma_3d(sB + bb * kSC * kBBytes, &xmap, 0, row0, c_beg + s * kSC, &b_full[bb]);
                 issued = s + 1;
             }
             for (int s = max(0, issued - kBStages); s < issued; s++)
@@ -866,7 +868,7 @@ void launch_umma_gemm(const UMat & w, const half * x16, int ldx, int rows, const
     p.kc_per_split = (w.KC + splits - 1) / splits;
     p.splits = splits;
     p.x = x16; p.ldx = ldx; p.rows = rows; p.out = out; p.err = err;
-    const CUtensorMap map = make_x_map(x16, w.K, ldx, rows, 16 * NT16);
+    const CUtensorMap map = make_x_group_map(x16, w.K, ldx, rows, 16 * NT16, kSC);
     dim3 grid(w.MT, splits, chunks);
     switch (NT16) {
         case 1: launch_nt<1>(p, map, grid, s, pdl); break;
