@@ -15,6 +15,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <functional>
 #include <vector>
 
 struct breeze_generator {
@@ -845,28 +846,38 @@ int bzb_generator_sessions_step_pcm(breeze_generator * gen, breeze_vocoder * voc
         if (!same_device_stream(gen, voc)) return -1;
         bzb::Engine & eng = *gen->eng;
         const int nc = eng.nc();
-        std::vector<int> frames((size_t) n * nc);
-        const bzb::StepResult r = eng.step(session_ids, n, 1, seeds, true, frames.data(), nc, out_next_cb0, true);
-        if (out_frames) std::memcpy(out_frames, frames.data(), frames.size() * sizeof(int));
-        // every session that produced a frame decodes it on its stream (keyed by session id,
-        // restarted when the id's session was created again)
-        std::vector<int> ids, rows, codes;
+        constexpr int spf = bzb::Vocoder::kSamplesPerFrame;
+        // every session the host knows as live decodes its new frame on its stream (keyed by
+        // session id, restarted when the id's session was created again), enqueued right after
+        // the frame step on the device frames: no host round trip between the two. A session
+        // that finished on the device in the previous step has no frame now; it is decoded once
+        // more from its -1 codes (its stream, which no later frame continues, moves on by that
+        // frame) and its PCM is returned as zeros, like that of every row without a frame.
+        std::vector<int> ids, rows;
         std::vector<unsigned long long> epochs;
-        for (int i = 0; i < n; i++) {
-            if (frames[(size_t) i * nc] < 0) continue;
-            ids.push_back(session_ids[i]);
-            rows.push_back(i);
-            epochs.push_back(eng.session_epoch(session_ids[i]));
-            codes.insert(codes.end(), frames.begin() + (size_t) i * nc, frames.begin() + (size_t) (i + 1) * nc);
-        }
-        if (out_pcm) std::fill_n(out_pcm, (size_t) n * bzb::Vocoder::kSamplesPerFrame, 0.0f);
-        if (!ids.empty()) {
-            std::vector<float> pcm(ids.size() * bzb::Vocoder::kSamplesPerFrame);
-            voc->voc->streams_decode((int) ids.size(), ids.data(), epochs.data(), codes.data(), 1, pcm.data());
-            if (out_pcm)
-                for (size_t j = 0; j < ids.size(); j++)
-                    std::memcpy(out_pcm + (size_t) rows[j] * bzb::Vocoder::kSamplesPerFrame,
-                                pcm.data() + j * bzb::Vocoder::kSamplesPerFrame, bzb::Vocoder::kSamplesPerFrame * sizeof(float));
+        for (int i = 0; i < n; i++)
+            if (eng.session_active(session_ids[i])) {
+                ids.push_back(session_ids[i]);
+                rows.push_back(i);
+                epochs.push_back(eng.session_epoch(session_ids[i]));
+            }
+        const int m = (int) ids.size();
+        const bool identity = m == n;
+        const std::function<void(int)> decode = [&](int k) {
+            if (m > 0)
+                voc->voc->streams_decode_rows_async(m, ids.data(), epochs.data(), eng.device_frames(k), nc,
+                                                    identity ? nullptr : rows.data());
+        };
+        std::vector<int> frames((size_t) n * nc);
+        const bzb::StepResult r = eng.step(session_ids, n, 1, seeds, true, frames.data(), nc, out_next_cb0, true,
+                                           false, nullptr, nullptr, &decode);
+        voc->voc->check_device_error();
+        if (out_frames) std::memcpy(out_frames, frames.data(), frames.size() * sizeof(int));
+        if (out_pcm) {
+            std::fill_n(out_pcm, (size_t) n * spf, 0.0f);
+            const float * ph = voc->voc->pinned_pcm();
+            for (int j = 0; j < m; j++)
+                if (frames[(size_t) rows[j] * nc] >= 0) std::memcpy(out_pcm + (size_t) rows[j] * spf, ph + (size_t) j * spf, spf * sizeof(float));
         }
         return r.steps_executed == 0 ? 0 : r.still_active;
     } catch (const std::exception & e) {

@@ -1014,7 +1014,8 @@ int Engine::setup_step(const int * sids, int n, int K, const uint32_t * seeds, b
 
 StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
                         int width, int * next_out, bool fill_inactive, bool sampled_depth,
-                        const uint32_t * depth_seeds, const StepForce * force) {
+                        const uint32_t * depth_seeds, const StepForce * force,
+                        const std::function<void(int)> * after_graph) {
     StepResult res;
     const int nc = cfg.nc;
     for (int i = 0; i < n; i++) next_out[i] = -1;
@@ -1023,7 +1024,10 @@ StepResult Engine::step(const int * sids, int n, int K, const uint32_t * seeds, 
     cudaGraphExec_t g = nullptr;
     const int R = setup_step(sids, n, K, seeds, sampled_depth, depth_seeds, force, rs, &g);
     if (R == 0) return res;
-    for (int k = 0; k < K; k++) CK(cudaGraphLaunch(g, stream_));
+    for (int k = 0; k < K; k++) {
+        CK(cudaGraphLaunch(g, stream_));
+        if (after_graph) (*after_graph)(k);
+    }
     std::vector<int> fr((size_t) K * R * nc), nx(R), aa(K);
     CK(cudaMemcpyAsync(fr.data(), frames_all_, fr.size() * sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaMemcpyAsync(nx.data(), next_, R * sizeof(int), cudaMemcpyDeviceToHost, stream_));

@@ -112,9 +112,13 @@ public:
     // the argmax unless the batch holds a two-branch session or `sampled_depth` is set (then
     // each session's depth sampler, src/depth_decoder.cpp:130-247); `depth_seeds` [n] reseeds the
     // depth draws per call (src/c_api.cpp:468).
+    // after_graph (optional) is called after each step's graph launch, before the host copies
+    // and the synchronisation: work it enqueues on the engine's stream reads that step's frames
+    // on the device (device_frames(k)) and completes before step() returns
     StepResult step(const int * sids, int n, int K, const uint32_t * seeds, bool burst, int * frames_out,
                     int width, int * next_out, bool fill_inactive, bool sampled_depth = false,
-                    const uint32_t * depth_seeds = nullptr, const StepForce * force = nullptr);
+                    const uint32_t * depth_seeds = nullptr, const StepForce * force = nullptr,
+                    const std::function<void(int)> * after_graph = nullptr);
 
     // device-resident run of K steps for the current batch (no host copies): timing entry
     void step_device_only(int K);

@@ -46,6 +46,14 @@ __global__ void voc_embed_kernel(const float * first, const float * rest, const 
     }
 }
 
+// dst[j][c] = src[rows[j]][c] for m rows of nc codes (src row stride ld)
+__global__ void voc_gather_rows_kernel(const int * src, int ld, const int * rows, int m, int nc, int * dst) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < m * nc; i += gridDim.x * blockDim.x) {
+        const int j = i / nc, c = i - j * nc;
+        dst[i] = src[(size_t) rows[j] * ld + c];
+    }
+}
+
 // out[c][r] = in[r][c] (+ add[c][r] when non-null)
 __global__ void voc_transpose_kernel(const float * in, int R, int C, float * out, const float * add) {
     __shared__ float tile[32][33];
@@ -1280,6 +1288,8 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaS
 Vocoder::~Vocoder() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    if (pcm_host_) cudaFreeHost(pcm_host_);
+    if (rows_dev_) cudaFree(rows_dev_);
     for (void * p : scratch_allocs_) cudaFree(p);
     for (void * p : stream_allocs_) cudaFree(p);
     for (void * p : allocs_) cudaFree(p);
@@ -1760,6 +1770,41 @@ void Vocoder::streams_decode_device(int n, const int * ids, const unsigned long 
     ensure(n * T);
     decode_segments(codes_dev, ld_codes, n, T, segs.data(), pcm_dev ? pcm_dev : pcm_);
     advance(n, ids, T);
+}
+
+void Vocoder::streams_decode_rows_async(int m, const int * ids, const unsigned long long * epochs, const int * frames_dev,
+                                        int ld, const int * rows) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (m <= 0) return;
+    const std::vector<Segment> segs = stream_segments(m, ids, epochs, 1);
+    ensure(m);
+    const int * codes = frames_dev;
+    int ldc = ld;
+    if (rows) {
+        if (m > rows_cap_) {
+            VCHECK(cudaStreamSynchronize(stream_));
+            if (rows_dev_) cudaFree(rows_dev_);
+            rows_dev_ = nullptr;
+            rows_cap_ = std::max(m, 256);
+            VCHECK(cudaMalloc(&rows_dev_, (size_t) rows_cap_ * sizeof(int)));
+        }
+        // a copy from pageable host memory is staged before the call returns
+        VCHECK(cudaMemcpyAsync(rows_dev_, rows, (size_t) m * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        voc_gather_rows_kernel<<<grid_for((size_t) m * cfg_.nc), 256, 0, stream_>>>(frames_dev, ld, rows_dev_, m, cfg_.nc, codes_);
+        codes = codes_;
+        ldc = cfg_.nc;
+    }
+    decode_segments(codes, ldc, m, 1, segs.data(), pcm_);
+    const size_t need = (size_t) m * kSamplesPerFrame;
+    if (need > pcm_host_cap_) {
+        VCHECK(cudaStreamSynchronize(stream_));
+        if (pcm_host_) cudaFreeHost(pcm_host_);
+        pcm_host_ = nullptr;
+        pcm_host_cap_ = std::max(need, (size_t) 64 * kSamplesPerFrame);
+        VCHECK(cudaMallocHost(&pcm_host_, pcm_host_cap_ * sizeof(float)));
+    }
+    VCHECK(cudaMemcpyAsync(pcm_host_, pcm_, need * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    advance(m, ids, 1);
 }
 
 int Vocoder::stream_decode(const int * frames, int n_frames, float * out_pcm) {

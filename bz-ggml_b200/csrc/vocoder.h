@@ -55,6 +55,13 @@ public:
     void streams_decode_device(int n, const int * ids, const unsigned long long * epochs, const int * codes_dev,
                               int ld_codes, int T, float * pcm_dev);
     const float * last_pcm() const { return pcm_; }
+    // the serving step's decode: one new frame for each of m streams, stream j's frame being row
+    // rows[j] of the device frames (row stride ld ints; rows null: row j), enqueued without a host
+    // synchronisation; the PCM goes on into the vocoder's pinned host buffer ([m][1920],
+    // pinned_pcm()) asynchronously and is valid once the stream has been synchronised
+    void streams_decode_rows_async(int m, const int * ids, const unsigned long long * epochs, const int * frames_dev,
+                                   int ld, const int * rows);
+    const float * pinned_pcm() const { return pcm_host_; }
     // kernels one batched decode of S segments of T frames launches (counted from a captured,
     // never launched graph of a whole-decode call; a streaming call launches the same ones)
     int kernels_per_decode(int S, int T);
@@ -169,6 +176,10 @@ private:
     half * t16_ = nullptr, * att16_ = nullptr, * f16_ = nullptr;
     int * codes_ = nullptr;
     float * fring_ = nullptr;  // keys and values of whole-decode segments [S][T][2][kv dim]
+    float * pcm_host_ = nullptr;  // pinned PCM of the serving step's decode
+    size_t pcm_host_cap_ = 0;     // floats
+    int * rows_dev_ = nullptr;    // frame rows of the serving step's streams
+    int rows_cap_ = 0;
 
     // streams: carried convolution states [slot][st_floats_] (every state layer's [2][cin][P] at
     // st_off_[layer], in decode order), key/value rings [slot][layer][ring_R_][2][kv dim]
