@@ -1238,9 +1238,20 @@ void Engine::session_create(int sid, const std::string & text, const char * inst
                           has_ref ? ref_frames : 0, seed, est, sp, true, out_cb0, out_alloc);
 }
 
+// Programmatic dependent launch for an eager run of kernels (a prompt's prefill): each kernel's
+// CTAs start while its predecessor drains and wait (griddepcontrol.wait) before reading its
+// outputs, as inside the step graphs. Host copies between the kernels keep plain stream order.
+struct EagerPdl {
+    EagerPdl() { set_pdl_scope(true); }
+    ~EagerPdl() { set_pdl_scope(false); }
+    EagerPdl(const EagerPdl &) = delete;
+    EagerPdl & operator=(const EagerPdl &) = delete;
+};
+
 void Engine::prefill_prompt(int slot, const std::vector<std::vector<int>> & segs, const int * ref_codes,
                             int ref_frames, float * logits) {
     const int H = cfg.hidden, nc = cfg.nc;
+    const EagerPdl pdl;
     int off = 0;
     auto add_text = [&](const std::vector<int> & toks) {
         te_forward(toks, px_ + (size_t) off * H);
@@ -1542,6 +1553,7 @@ void Engine::sessions_create_batch(const std::vector<CreateSpec> & specs, int * 
                 }
             }
             ensure_prefill_capacity(rows);
+            const EagerPdl pdl;
             // packed rows: branch by branch ([ref text][ref frames][EOS] tail), conditional first
             std::vector<int4> segs;                       // {first row, rows, slot, session index}
             std::vector<const std::vector<int> *> tsegs;  // text segments in encoder order

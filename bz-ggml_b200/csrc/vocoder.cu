@@ -365,6 +365,76 @@ struct TcConv {
     int * err = nullptr;
 };
 
+// The fused epilogue of one output step t (the calling thread's TMEM lane) over accumulator
+// columns [c_lo, c_hi): column g = ot nt + c is output channel g / P, phase g % P (P = ostride).
+// With input-channel splits the raw sums go to the phase-major partials; otherwise bias, the
+// residual, the activations and the stores. The residual of a 16-column group is loaded one
+// group ahead of its use (the first one by the caller before its wait for the accumulator), so
+// that its latency hides behind the MMAs and the previous group's stores; the loads of one group
+// never touch another group's outputs, so reading ahead of in-place stores is safe.
+struct TcEpi {
+    const ConvArgs & a;
+    int nt, ot, P, split, splits;
+    bool have_sum, want_res;
+    int t;
+    size_t tcol;
+    __device__ __forceinline__ TcEpi(const ConvArgs & a_, int nt_, int ot_, int split_, int splits_, bool have_sum_, int t_,
+                                     bool row_ok)
+        : a(a_), nt(nt_), ot(ot_), P(a_.ostride), split(split_), splits(splits_), have_sum(have_sum_),
+          want_res(a_.res && splits_ == 1 && row_ok), t(t_), tcol((size_t) t_ * a_.ostride) {}
+
+    __device__ __forceinline__ void load_res(int c0, float * r) const {
+        const int ob = ot * nt + c0, ne = min(16, a.cout * P - ob);
+        int o = ob / P, ph = ob - (ob / P) * P;
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            r[e] = (want_res && e < ne) ? a.res[(size_t) o * a.ldy + tcol + ph] : 0.0f;
+            if (++ph == P) {
+                ph = 0;
+                o++;
+            }
+        }
+    }
+
+    // warp-uniform loop: every lane takes part in each tensor-memory load
+    __device__ __forceinline__ void run(uint32_t taddr, int c_lo, int c_hi, bool live, float * rn) const {
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+            float r[16];
+#pragma unroll
+            for (int e = 0; e < 16; e++) r[e] = rn[e];
+            if (c0 + 16 < c_hi) load_res(c0 + 16, rn);
+            float v[16];
+            tc::tmem_ld16(taddr + (uint32_t) c0, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
+            const int ob = ot * nt + c0, ne = min(16, a.cout * P - ob);
+            const int o0 = ob / P, ph0 = ob - o0 * P;
+            if (live && splits > 1) {
+                int o = o0, ph = ph0;
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    if (e < ne) a.part[conv_part_index(a, split, o, t, ph)] = have_sum ? v[e] : 0.0f;
+                    if (++ph == P) {
+                        ph = 0;
+                        o++;
+                    }
+                }
+            } else if (live) {
+                int o = o0, ph = ph0;
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    if (e < ne) conv_store(a, o, (size_t) o * a.ldy + tcol + ph, v[e] + r[e] + (a.bias ? __ldg(a.bias + o) : 0.0f));
+                    if (++ph == P) {
+                        ph = 0;
+                        o++;
+                    }
+                }
+            }
+        }
+    }
+};
+
 __device__ __forceinline__ void bar_producers() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_constant__ TcConv p) {
@@ -383,7 +453,7 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     int * wtau = wseg + p.win_rows;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int P = a.ostride, split = blockIdx.z, ot = blockIdx.y;
+    const int split = blockIdx.z, ot = blockIdx.y;
     const int c_beg = split * p.cps, c_end = min(p.kchunks, c_beg + p.cps);
     const int t0 = blockIdx.x * kTM;
     const int halo = (a.taps - 1) * a.dil;
@@ -555,64 +625,201 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     if (warp < 8) {
         const int q = warp & 3, hh = warp >> 2, half_cols = p.nt / 2;
         const int t = t0 + 32 * q + lane;
-        const size_t tcol = (size_t) t * P;
-        const bool want_res = a.res && p.splits == 1 && t < a.L;
-        // the residual of a 16-column group (zero past the outputs), loaded one group ahead of its
-        // use and the first group before the wait for the accumulator, so that its latency hides
-        // behind the MMAs and the previous group's stores (the loads of one group never touch
-        // another group's outputs, so reading ahead of the in-place stores is safe)
-        auto load_res = [&](int c0, float * r) {
-            const int ob = ot * p.nt + c0, ne = min(16, a.cout * P - ob);
-            int o = ob / P, ph = ob - (ob / P) * P;
-#pragma unroll
-            for (int e = 0; e < 16; e++) {
-                r[e] = (want_res && e < ne) ? a.res[(size_t) o * a.ldy + tcol + ph] : 0.0f;
-                if (++ph == P) {
-                    ph = 0;
-                    o++;
-                }
-            }
-        };
+        const TcEpi ep(a, p.nt, ot, split, p.splits, n_it > 0, t, t < a.L);
         float rn[16];
-        load_res(hh * half_cols, rn);
+        ep.load_res(hh * half_cols, rn);
         if (!mbar_wait(&done_bar, 0u, p.err, kSpinLimit, 128)) ok = false;
         tc_fence_after();
-        const bool live = ok && t < a.L;
-        for (int c0 = hh * half_cols; c0 < (hh + 1) * half_cols; c0 += 16) {  // warp-uniform: every lane loads
-            float r[16];
+        ep.run(tmem + ((uint32_t) (32 * q) << 16), hh * half_cols, (hh + 1) * half_cols, ok && t < a.L, rn);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) tmem_dealloc(tmem, cols);
+}
+
+// The same convolution with the staged window itself as the A operand, for sequences of at least
+// one tile per segment: a CTA's 128 steps lie in one segment (tiles are laid out per segment, the
+// last one of a segment partly empty), so output step r of tap k reads window row r + k dil and
+// the tap's A operand is the window from row k dil on: a shared-memory descriptor that starts
+// k dil rows into the 1024-byte-aligned window, whose 16-byte pieces are stored at the XOR of the
+// row's own address bits like every 128-byte-swizzled tile (the swizzle follows the absolute
+// address, so the descriptor's matrix base offset stays 0: setting it to the start row's phase
+// fails the parity tests). The producers stage one window per
+// 64-channel chunk (two buffers) and hand each over once for all its taps; there are no per-tap
+// copies. Rows past the window's data are never stored (their outputs belong to steps past the
+// segment).
+struct TcConvW {
+    ConvArgs a;
+    const half * w16 = nullptr;
+    int nt = 0, otiles = 0, kchunks = 0;
+    int tps = 0;         // tiles per segment
+    int win_rows = 0;    // window rows per buffer (a multiple of 8: 128 + halo rounded up)
+    int b_stages = 3;    // at most 4
+    int splits = 1, cps = 0;
+    int * err = nullptr;
+};
+
+__global__ void __launch_bounds__(kTThreads, 2) voc_conv_tcw_kernel(const __grid_constant__ TcConvW p) {
+    using namespace tc;
+    const ConvArgs & a = p.a;
+    extern __shared__ uint8_t tsm_raw[];
+    __shared__ uint64_t w_full[2], w_empty[2], b_full[4], b_empty[4], done_bar;
+    __shared__ uint32_t tmem_slot;
+    uint8_t * sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t) 1023);
+    const uint32_t wbytes = (uint32_t) p.win_rows * 128;
+    uint8_t * sWin = sm;                 // [2][win_rows][128 B]
+    uint8_t * sB = sm + 2 * wbytes;      // [b_stages][nt][128 B]
+    const uint32_t tb = (uint32_t) p.nt * 128;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = blockIdx.z, ot = blockIdx.y;
+    const int c_beg = split * p.cps, c_end = min(p.kchunks, c_beg + p.cps);
+    const int seg = a.seg_len > 0 ? a.seg_len : a.L;
+    const int b = blockIdx.x / p.tps, tau0 = (blockIdx.x % p.tps) * kTM;
+    const int rows = min(kTM, seg - tau0);
+    const int halo = (a.taps - 1) * a.dil;
+    const int lx = rows + halo;
+    const int n_ch = max(0, c_end - c_beg), n_it = n_ch * a.taps;
+    const int BS = p.b_stages;
+    const uint32_t cols = p.nt <= 32 ? 32u : p.nt <= 64 ? 64u : p.nt <= 128 ? 128u : 256u;
+    const uint32_t idesc = (1u << 4) | ((uint32_t) (p.nt >> 3) << 17) | ((uint32_t) (kTM >> 4) << 24);
+
+    if (warp == 8) tmem_alloc(&tmem_slot, cols);
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&w_full[i], 8);   // one arrival per producer warp
+            mbar_init(&w_empty[i], 1);
+        }
+        for (int i = 0; i < BS; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        mbar_init(&done_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+
+    if (warp < 8) {
+        // warp w stages piece w (channels c 64 + 8 w ...) of every window row, lanes on consecutive
+        // rows (coalesced loads of consecutive steps), 4 rows per lane in flight
+        const int par = (a.st && halo > 0) ? a.seg_par[b] : -1;
+        const float * stb = par >= 0 ? a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) par * a.cin * halo : nullptr;
+        const float * xb = a.x + (size_t) b * seg;
+        for (int ci = 0; ci < n_ch; ci++) {
+            const int c = c_beg + ci, wb = ci & 1;
+            if (ok && ci >= 2) ok = mbar_wait(&w_empty[wb], (uint32_t) ((ci / 2) - 1) & 1u, p.err, kSpinLimit, 32);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            uint8_t * W = sWin + wb * wbytes;
+            const int ci0 = c * 64 + warp * 8, nq = min(8, a.cin - ci0);
+            for (int ub = 0; ub < lx; ub += 128) {
+                float f[4][8];
 #pragma unroll
-            for (int e = 0; e < 16; e++) r[e] = rn[e];
-            if (c0 + 16 < (hh + 1) * half_cols) load_res(c0 + 16, rn);
-            float v[16];
-            tmem_ld16(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) c0, v);
-            tmem_wait_ld();
+                for (int m = 0; m < 4; m++) {
 #pragma unroll
-            for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
-            // column g = ob + e is output channel g / P, phase g % P
-            const int ob = ot * p.nt + c0, ne = min(16, a.cout * P - ob);
-            const int o0 = ob / P, ph0 = ob - o0 * P;
-            if (live && p.splits > 1) {
-                int o = o0, ph = ph0;
+                    for (int q = 0; q < 8; q++) f[m][q] = 0.0f;
+                    const int u = ub + 32 * m + lane;
+                    if (u >= lx || nq <= 0) continue;
+                    const int tau = tau0 + u - halo;
+                    if (tau < 0) {
+                        if (stb) {
 #pragma unroll
-                for (int e = 0; e < 16; e++) {
-                    if (e < ne) a.part[conv_part_index(a, split, o, t, ph)] = n_it > 0 ? v[e] : 0.0f;
-                    if (++ph == P) {
-                        ph = 0;
-                        o++;
+                            for (int q = 0; q < 8; q++)
+                                if (q < nq) f[m][q] = stb[(size_t) (ci0 + q) * halo + tau + halo];
+                        }
+                    } else {
+                        const float * xp = xb + (size_t) ci0 * a.L + tau;
+#pragma unroll
+                        for (int q = 0; q < 8; q++)
+                            if (q < nq) f[m][q] = xp[(size_t) q * a.L];
                     }
                 }
-            } else if (live) {
-                int o = o0, ph = ph0;
 #pragma unroll
-                for (int e = 0; e < 16; e++) {
-                    if (e < ne) conv_store(a, o, (size_t) o * a.ldy + tcol + ph, v[e] + r[e] + (a.bias ? __ldg(a.bias + o) : 0.0f));
-                    if (++ph == P) {
-                        ph = 0;
-                        o++;
+                for (int m = 0; m < 4; m++) {
+                    const int u = ub + 32 * m + lane;
+                    if (u >= lx) continue;
+                    uint32_t w[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const half2 h2 = __floats2half2_rn(f[m][2 * q], f[m][2 * q + 1]);
+                        w[q] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    *reinterpret_cast<uint4 *>(W + (size_t) u * 128 + ((warp ^ (u & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            __syncwarp();
+            // the tile holding the segment's last step writes the segment's new state for this
+            // warp's channels: the last halo rows of [state | data] (from the f16 window, as read)
+            if (a.st && halo > 0 && ot == 0 && tau0 + rows == seg && nq > 0) {
+                float * dst = a.st + (size_t) a.seg_slot[b] * a.st_stride + (size_t) voc_state_next(a.seg_par[b]) * a.cin * halo;
+                for (int e = lane; e < 8 * halo; e += 32) {
+                    const int i = e / halo, r = e - i * halo, u = lx - halo + r;
+                    if (i < nq) {
+                        const half hv = *reinterpret_cast<const half *>(W + (size_t) u * 128 + ((warp ^ (u & 7)) << 4) + i * 2);
+                        dst[(size_t) (ci0 + i) * halo + r] = __half2float(hv);
                     }
                 }
             }
+            fence_proxy_async();  // each thread's window stores before the warp's arrival
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&w_full[wb]);
         }
+    } else if (warp == 8) {
+        if (lane == 0) {
+            int it = 0;
+            for (int ci = 0; ci < n_ch && ok; ci++) {
+                const int wb = ci & 1;
+                ok = mbar_wait(&w_full[wb], (uint32_t) (ci / 2) & 1u, p.err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t wa = smem_u32(sWin + wb * wbytes);
+                for (int k = 0; k < a.taps; k++, it++) {
+                    const int sb = it % BS;
+                    ok = mbar_wait(&b_full[sb], (uint32_t) (it / BS) & 1u, p.err);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = wa + (uint32_t) (k * a.dil) * 128, b0 = smem_u32(sB + sb * tb);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&b_empty[sb]);
+                }
+                if (!ok) break;
+                umma_commit(&w_empty[wb]);
+            }
+            umma_commit(&done_bar);
+            if (!mbar_drain(&done_bar, 0u, p.err)) ok = false;
+        }
+    } else {
+        if (lane == 0) {
+            const uint8_t * base = reinterpret_cast<const uint8_t *>(p.w16) + ((size_t) ot * p.kchunks + c_beg) * a.taps * (size_t) tb;
+            int issued = 0;
+            for (int it = 0; it < n_it; it++) {
+                const int sb = it % BS;
+                if (it >= BS) ok = mbar_wait(&b_empty[sb], (uint32_t) ((it / BS) - 1) & 1u, p.err, kSpinLimit, 64);
+                if (!ok) break;
+                mbar_expect_tx(&b_full[sb], tb);
+                bulk_g2s(sB + sb * tb, base + (size_t) it * tb, tb, &b_full[sb]);
+                issued = it + 1;
+            }
+            for (int it = max(0, issued - BS); it < issued; it++)
+                mbar_drain(&b_full[it % BS], (uint32_t) (it / BS) & 1u, p.err);
+        }
+    }
+
+    if (warp < 8) {
+        const int q = warp & 3, hh = warp >> 2, half_cols = p.nt / 2;
+        const int r = 32 * q + lane;
+        const int t = b * seg + tau0 + r;
+        const TcEpi ep(a, p.nt, ot, split, p.splits, n_it > 0, t, r < rows);
+        float rn[16];
+        ep.load_res(hh * half_cols, rn);
+        if (!mbar_wait(&done_bar, 0u, p.err, kSpinLimit, 128)) ok = false;
+        tc_fence_after();
+        ep.run(tmem + ((uint32_t) (32 * q) << 16), hh * half_cols, (hh + 1) * half_cols, ok && r < rows, rn);
     }
     tc_fence_before();
     __syncthreads();
@@ -916,6 +1123,53 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     if (a.L <= 0) return;
     if (a.istride != 1) throw std::runtime_error("tcgen05 conv: strided input is not supported");
     a.Lin = a.L;
+    static std::mutex mu;
+    static std::map<int, bool> attr_set;
+    int dev = 0;
+    VCHECK(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[dev]) {
+            VCHECK(cudaFuncSetAttribute(voc_conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemMax));
+            VCHECK(cudaFuncSetAttribute(voc_conv_tcw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemMax));
+            attr_set[dev] = true;
+        }
+    }
+    const int halo = (a.taps - 1) * a.dil;
+    const int seg = a.seg_len > 0 ? a.seg_len : a.L;
+    const int n_seg = a.L / seg;
+    const size_t two_per_sm = (size_t) 113 * 1024;
+    // segments of at least 112 steps: tiles per segment (at most 1/8 of a tile's rows unused) and
+    // the window itself as the A operand of every tap
+    if (seg >= 112) {
+        TcConvW q;
+        q.w16 = w16;
+        q.nt = nt;
+        q.otiles = otiles;
+        q.kchunks = kchunks;
+        q.err = err;
+        q.tps = (seg + kTM - 1) / kTM;
+        q.win_rows = (kTM + halo + 7) / 8 * 8;
+        const int tiles = n_seg * q.tps * otiles;
+        int splits = 1;
+        while (tiles * splits * 2 <= 2 * 148 && splits * 2 <= kchunks && splits < 16 &&
+               (size_t) splits * 2 * a.cout * a.ldy <= scratch_floats)
+            splits *= 2;
+        a.splits = splits;
+        a.part = scratch;
+        q.a = a;
+        q.splits = splits;
+        q.cps = (kchunks + splits - 1) / splits;
+        auto smem = [&](int bs) { return (size_t) 1024 + (size_t) 2 * q.win_rows * 128 + (size_t) bs * nt * 128; };
+        q.b_stages = 4;
+        const size_t cap = (long long) tiles * splits > 148 ? two_per_sm : (size_t) kTSmemMax;
+        while (q.b_stages > 2 && smem(q.b_stages) > cap) q.b_stages--;
+        if (smem(q.b_stages) > (size_t) kTSmemMax) throw std::runtime_error("tcgen05 conv: the windows do not fit in shared memory");
+        const dim3 grid((unsigned) (n_seg * q.tps), (unsigned) otiles, (unsigned) splits);
+        voc_conv_tcw_kernel<<<grid, kTThreads, smem(q.b_stages), s>>>(q);
+        if (splits > 1) launch_conv_reduce(a, s);
+        return;
+    }
     // small grids: split the input-channel chunks across CTAs until about two waves are in flight
     const int tiles = ((a.L + kTM - 1) / kTM) * otiles;  // otiles cover the phases too
     int splits = 1;
@@ -933,9 +1187,6 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     p.otiles = otiles;
     p.kchunks = kchunks;
     p.err = err;
-    const int halo = (a.taps - 1) * a.dil;
-    const int seg = a.seg_len > 0 ? a.seg_len : a.L;
-    const int n_seg = a.L / seg;
     const int touched = std::min(n_seg, (kTM - 1 + seg - 1) / seg + 1);
     p.win_rows = (kTM + halo * touched + 7) / 8 * 8;
     auto smem = [&](int as, int bs) {
@@ -946,7 +1197,6 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     // grids of more than one wave: two CTAs per SM (one's staging and epilogue latency hidden
     // behind the other's work) when two-stage rings make room for them
     const long long ctas = (long long) tiles * splits;
-    const size_t two_per_sm = (size_t) 113 * 1024;
     if (ctas > 148 && smem(2, 2) <= two_per_sm)
         while (smem(p.a_stages, p.b_stages) > two_per_sm) {
             if (p.b_stages > 2) p.b_stages--;
@@ -956,17 +1206,6 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
         if (p.b_stages > 2) p.b_stages--;
         else if (p.a_stages > 2) p.a_stages--;
         else throw std::runtime_error("tcgen05 conv: the input window does not fit in shared memory");
-    }
-    static std::mutex mu;
-    static std::map<int, bool> attr_set;
-    int dev = 0;
-    VCHECK(cudaGetDevice(&dev));
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!attr_set[dev]) {
-            VCHECK(cudaFuncSetAttribute(voc_conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemMax));
-            attr_set[dev] = true;
-        }
     }
     const dim3 grid((unsigned) ((a.L + kTM - 1) / kTM), (unsigned) otiles, (unsigned) splits);
     voc_conv_tc_kernel<<<grid, kTThreads, smem(p.a_stages, p.b_stages), s>>>(p);
