@@ -881,7 +881,7 @@ __global__ void voc_depthwise_seg_kernel(const float * x, int C, int S, int seg,
 // K and V of T new frames of S streams into their rings: row s T + t is position pos0[s] + t of
 // ring slot[s] (k rotated by NEOX RoPE at that position). Ring layout per slot:
 // [R positions][2 (k, v)][nkv hd] floats, position p at p mod R.
-__global__ void voc_kv_ring_append_kernel(const float * k, const float * v, int S, int T, int nkv, int hd,
+__global__ void voc_kv_ring_append_kernel(const float * k, const float * v, int ld, int S, int T, int nkv, int hd,
                                           const float2 * rope, float * ring, size_t slot_stride, int R,
                                           const int * slots, const int * pos0) {
     const int kvd = nkv * hd, half_d = hd / 2;
@@ -891,12 +891,12 @@ __global__ void voc_kv_ring_append_kernel(const float * k, const float * v, int 
         const int d = e % hd;
         const int pos = pos0[sgm] + t;
         const int dp = d < half_d ? d + half_d : d - half_d;
-        const float x0 = k[(size_t) row * kvd + e], x1 = k[(size_t) row * kvd + e - d + dp];
+        const float x0 = k[(size_t) row * ld + e], x1 = k[(size_t) row * ld + e - d + dp];
         const float2 cs = rope[(size_t) pos * half_d + (d < half_d ? d : d - half_d)];
         const float kr = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
         float * dst = ring + (size_t) slots[sgm] * slot_stride + (size_t) (pos % R) * 2 * kvd;
         dst[e] = kr;
-        dst[kvd + e] = v[(size_t) row * kvd + e];
+        dst[kvd + e] = v[(size_t) row * ld + e];
     }
 }
 
@@ -907,7 +907,7 @@ __global__ void voc_kv_ring_append_kernel(const float * k, const float * v, int 
 // shared memory), so the key loads of a block are independent of one another; the block's
 // softmax weights are then broadcast lane by lane into the value sums of the lane's dims (online
 // rescaling between blocks).
-__global__ void __launch_bounds__(128) voc_attn_ring_kernel(const float * q, int S, int T, int nh, int nkv, int hd, int window,
+__global__ void __launch_bounds__(128) voc_attn_ring_kernel(const float * q, int ldq, int S, int T, int nh, int nkv, int hd, int window,
                                      const float2 * rope, float scale, const float * ring, size_t slot_stride, int R,
                                      const int * slots, const int * pos0, half * out) {
     __shared__ float qs[4][128];
@@ -919,7 +919,7 @@ __global__ void __launch_bounds__(128) voc_attn_ring_kernel(const float * q, int
     const float * base = ring + (size_t) slots[sgm] * slot_stride + (size_t) g * hd;
     for (int d = lane; d < hd; d += 32) {
         const int dp = d < half_d ? d + half_d : d - half_d;
-        const float x0 = q[((size_t) row * nh + h) * hd + d], x1 = q[((size_t) row * nh + h) * hd + dp];
+        const float x0 = q[(size_t) row * ldq + (size_t) h * hd + d], x1 = q[(size_t) row * ldq + (size_t) h * hd + dp];
         const float2 cs = rope[(size_t) pos * half_d + (d < half_d ? d : d - half_d)];
         qs[wib][d] = d < half_d ? x0 * cs.x - x1 * cs.y : x1 * cs.y + x0 * cs.x;
     }
@@ -1012,13 +1012,30 @@ __global__ void voc_scaled_add_kernel(float * h, const float * o, size_t n, int 
         h[i] += o[i] * scale[i % C];
 }
 
-// y16 = f16(silu(g) * u)
-__global__ void voc_silu_mul_kernel(const float * g, const float * u, size_t n, half * y16) {
-    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
-        const float a = g[i];
-        y16[i] = __float2half_rn((a / (1.0f + expf(-a))) * u[i]);
+// row r of h += o * scale (a branch's output and its layer scale), then y16 = RMSNorm(h) * w:
+// the residual add of one block and the norm that feeds the next (one CTA per row)
+__global__ void voc_add_rmsnorm_kernel(float * h, const float * o, const float * scale, int C, const float * w, float eps,
+                                       half * y16) {
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    float * hr = h + (size_t) r * C;
+    const float * orow = o + (size_t) r * C;
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float v = hr[c] + orow[c] * scale[c];
+        hr[c] = v;
+        ss += v * v;
     }
+    for (int k = 16; k > 0; k >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, k);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < nw; i++) tot += red[i];
+    const float inv = 1.0f / sqrtf(tot / (float) C + eps);
+    for (int c = threadIdx.x; c < C; c += blockDim.x) y16[(size_t) r * C + c] = __float2half_rn((hr[c] * inv) * w[c]);
 }
+
 
 // x16 = f16(x) for [R][C] rows
 __global__ void voc_to_f16_kernel(const float * x, size_t n, half * y) {
@@ -1284,6 +1301,55 @@ QMat Vocoder::load_q8(const std::string & name) {
     return q;
 }
 
+// several Q8_0 / Q4_K matrices of one row length as one tcgen05 matrix: rows stacked in order,
+// or (interleave_pairs) a gate and an up matrix in alternating 16-row groups, the layout of the
+// GEMM's SwiGLU epilogue (output column j = group 16 + row in group)
+QMat Vocoder::load_q8_fused(const std::vector<std::string> & names, bool interleave_pairs) {
+    std::vector<const GgufTensor *> parts;
+    for (const std::string & n : names) parts.push_back(&need(n));
+    const int K = (int) parts[0]->ne[0];
+    const bool q4 = parts[0]->type == GT_Q4_K;
+    for (const GgufTensor * t : parts) {
+        if (t->type != GT_Q8_0 && t->type != GT_Q4_K) throw std::runtime_error("vocoder: " + t->name + " must be Q8_0 or Q4_K");
+        if (t->type != parts[0]->type || t->ne[0] != K) throw std::runtime_error("vocoder: " + t->name + " differs from its fused partner");
+    }
+    if (K % 64 || (q4 && K % 256)) throw std::runtime_error("vocoder: fused matrices need rows of a multiple of 64 (256 for Q4_K)");
+    const size_t row_bytes = q4 ? (size_t) (K / 256) * 144 : (size_t) (K / 32) * 34;
+    std::vector<const uint8_t *> rows;
+    if (interleave_pairs) {
+        const int F = (int) parts[0]->rows();
+        if (parts.size() != 2 || parts[1]->rows() != F || F % 16) throw std::runtime_error("vocoder: gate/up pair shapes differ");
+        for (int p = 0; p < 2 * F; p++) {
+            const int grp = p / 32, r = p % 32;
+            rows.push_back(gg_.data(*parts[r < 16 ? 0 : 1]) + (size_t) (grp * 16 + (r & 15)) * row_bytes);
+        }
+    } else {
+        for (const GgufTensor * t : parts)
+            for (int64_t r = 0; r < t->rows(); r++) rows.push_back(gg_.data(*t) + (size_t) r * row_bytes);
+    }
+    const int M = (int) rows.size();
+    std::vector<uint8_t> raw((size_t) M * row_bytes);
+    for (int r = 0; r < M; r++) std::memcpy(raw.data() + (size_t) r * row_bytes, rows[r], row_bytes);
+    uint8_t * raw_dev = nullptr;
+    VCHECK(cudaMalloc(&raw_dev, raw.size()));
+    VCHECK(cudaMemcpyAsync(raw_dev, raw.data(), raw.size(), cudaMemcpyHostToDevice, stream_));
+    QMat q;
+    q.M = M;
+    q.K = K;
+    q.KB = K / 32;
+    q.MT = (M + 15) / 16;
+    UMat u;
+    u.M = M; u.MT = (M + 127) / 128; u.K = K; u.KC = K / 64; u.q4 = q4 ? 1 : 0;
+    uint8_t * ub = dalloc<uint8_t>((size_t) u.MT * u.KC * umat_chunk_bytes(u.q4));
+    if (q4) repack_umma_q4k(raw_dev, M, K, ub, stream_);
+    else repack_umma(raw_dev, M, K, ub, stream_);
+    u.blk = ub;
+    q.u = u;
+    VCHECK(cudaStreamSynchronize(stream_));
+    cudaFree(raw_dev);
+    return q;
+}
+
 void Vocoder::linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s) {
     if (w.u.blk && ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(x16) & 15) == 0)
         launch_umma_gemm(w.u, x16, ldx, rows, out, err_, s, false);
@@ -1403,14 +1469,11 @@ Vocoder::Vocoder(const GgufFile & gg, const ModelConfig & cfg, int device, cudaS
         const std::string p = "codec.dtf.blk." + std::to_string(l);
         Layer L;
         L.attn_norm = load_f32(p + ".attn_norm.weight", vc_.hidden);
-        L.q = load_q8(p + ".attn_q.weight");
-        L.k = load_q8(p + ".attn_k.weight");
-        L.v = load_q8(p + ".attn_v.weight");
+        L.qkv = load_q8_fused({ p + ".attn_q.weight", p + ".attn_k.weight", p + ".attn_v.weight" }, false);
         L.o = load_q8(p + ".attn_output.weight");
         L.attn_scale = load_f32(p + ".attn_scale", vc_.hidden);
         L.ffn_norm = load_f32(p + ".ffn_norm.weight", vc_.hidden);
-        L.gate = load_q8(p + ".ffn_gate.weight");
-        L.up = load_q8(p + ".ffn_up.weight");
+        L.gate_up = load_q8_fused({ p + ".ffn_gate.weight", p + ".ffn_up.weight" }, true);
         L.down = load_q8(p + ".ffn_down.weight");
         L.ffn_scale = load_f32(p + ".ffn_scale", vc_.hidden);
         layers_.push_back(L);
@@ -1567,13 +1630,9 @@ void Vocoder::ensure(int T) {
     c_ = fa(act_elems_);
     part_ = fa(2 * act_elems_);
     t32_ = fa(up_rows * wide);
-    q_ = fa(Tc * vc_.n_head * vc_.hd);
-    k_ = fa(Tc * vc_.n_kv * vc_.hd);
-    v_ = fa(Tc * vc_.n_kv * vc_.hd);
+    q_ = fa(Tc * ((size_t) vc_.n_head * vc_.hd + 2 * (size_t) vc_.n_kv * vc_.hd));  // rows of q | k | v
     o_ = fa(up_rows * wide);
-    g_ = fa(Tc * vc_.ffn);
     pcm_ = fa(Tc * kSamplesPerFrame);
-    u_ = fa(Tc * vc_.ffn);
     fring_ = fa(Tc * 2 * vc_.n_kv * vc_.hd);
     t16_ = ha(up_rows * wide);
     att16_ = ha(Tc * vc_.n_head * vc_.hd);
@@ -1709,28 +1768,27 @@ void Vocoder::decode_segments(const int * codes_dev, int ld_codes, int S, int T,
     const float2 * rope = streaming ? srope_ : rope_;
     const int R = streaming ? ring_R_ : T;
     const size_t slot_stride = streaming ? (size_t) vc_.n_layer * ring_R_ * 2 * kvd : (size_t) T * 2 * kvd;
+    // per layer: one q/k/v GEMM, the ring append and attention, the o GEMM, the residual add
+    // fused with the FFN norm, one gate/up GEMM with the SwiGLU epilogue (f16 out), the down GEMM,
+    // the residual add fused with the next norm
+    const int QKV = nh * hd + 2 * kvd;
+    launch_rmsnorm(h, H, layers_.empty() ? out_norm_ : layers_[0].attn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
     for (size_t l = 0; l < layers_.size(); l++) {
         const Layer & Ly = layers_[l];
         float * ring = streaming ? ring_ + l * (size_t) ring_R_ * 2 * kvd : fring_;
-        launch_rmsnorm(h, H, Ly.attn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
-        linear(Ly.q, t16_, H, NF, GemvOut{ EPI_STORE, q_, nullptr, nh * hd }, s);
-        linear(Ly.k, t16_, H, NF, GemvOut{ EPI_STORE, k_, nullptr, kvd }, s);
-        linear(Ly.v, t16_, H, NF, GemvOut{ EPI_STORE, v_, nullptr, kvd }, s);
-        voc_kv_ring_append_kernel<<<grid_for((size_t) NF * kvd), 256, 0, s>>>(k_, v_, S, T, nkv, hd, rope, ring, slot_stride,
-                                                                              R, d_slot, d_pos);
+        linear(Ly.qkv, t16_, H, NF, GemvOut{ EPI_STORE, q_, nullptr, QKV }, s);
+        voc_kv_ring_append_kernel<<<grid_for((size_t) NF * kvd), 256, 0, s>>>(q_ + nh * hd, q_ + nh * hd + kvd, QKV, S, T, nkv, hd,
+                                                                              rope, ring, slot_stride, R, d_slot, d_pos);
         const int warps = NF * nh;
-        voc_attn_ring_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, S, T, nh, nkv, hd, vc_.window, rope, scale, ring,
+        voc_attn_ring_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(q_, QKV, S, T, nh, nkv, hd, vc_.window, rope, scale, ring,
                                                                         slot_stride, R, d_slot, d_pos, att16_);
         linear(Ly.o, att16_, nh * hd, NF, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
-        voc_scaled_add_kernel<<<grid_for((size_t) NF * H), 256, 0, s>>>(h, o_, (size_t) NF * H, H, Ly.attn_scale);
-        launch_rmsnorm(h, H, Ly.ffn_norm, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
-        linear(Ly.gate, t16_, H, NF, GemvOut{ EPI_STORE, g_, nullptr, F }, s);
-        linear(Ly.up, t16_, H, NF, GemvOut{ EPI_STORE, u_, nullptr, F }, s);
-        voc_silu_mul_kernel<<<grid_for((size_t) NF * F), 256, 0, s>>>(g_, u_, (size_t) NF * F, t16_);
-        linear(Ly.down, t16_, F, NF, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
-        voc_scaled_add_kernel<<<grid_for((size_t) NF * H), 256, 0, s>>>(h, o_, (size_t) NF * H, H, Ly.ffn_scale);
+        voc_add_rmsnorm_kernel<<<NF, 256, 0, s>>>(h, o_, Ly.attn_scale, H, Ly.ffn_norm, vc_.eps, t16_);
+        linear(Ly.gate_up, t16_, H, NF, GemvOut{ EPI_SWIGLU, nullptr, f16_, F }, s);
+        linear(Ly.down, f16_, F, NF, GemvOut{ EPI_STORE, o_, nullptr, H }, s);
+        const float * next_norm = l + 1 < layers_.size() ? layers_[l + 1].attn_norm : out_norm_;
+        voc_add_rmsnorm_kernel<<<NF, 256, 0, s>>>(h, o_, Ly.ffn_scale, H, next_norm, vc_.eps, t16_);
     }
-    launch_rmsnorm(h, H, out_norm_, H, vc_.eps, t16_, H, nullptr, 0, 0, NF, nullptr, s);
     linear(out_proj_, t16_, H, NF, GemvOut{ EPI_STORE, o_, nullptr, latent_ }, s);
     voc_bias_scale_kernel<<<grid_for((size_t) NF * latent_), 256, 0, s>>>(o_, (size_t) NF * latent_, latent_, out_proj_b_, nullptr);
     transpose(o_, NF, latent_, a_, nullptr);                         // a_ = [latent][NF]

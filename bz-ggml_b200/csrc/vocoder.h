@@ -110,7 +110,9 @@ private:
         int nt = 0, otiles = 0, kchunks = 0;
     };
     struct Layer {
-        QMat q, k, v, o, gate, up, down;
+        // qkv: the q, k and v rows stacked (one GEMM); gate_up: gate and up rows interleaved in
+        // 16-row groups for the GEMM's SwiGLU epilogue (tcgen05 layout only)
+        QMat qkv, o, gate_up, down;
         float * attn_norm = nullptr, * ffn_norm = nullptr, * attn_scale = nullptr, * ffn_scale = nullptr;
     };
     struct Up {  // ConvNeXt upsampling stage
@@ -132,6 +134,7 @@ private:
 
     const GgufTensor & need(const std::string & name) const;
     float * load_f32(const std::string & name, int64_t expect, bool exp_of = false, bool recip = false);
+    QMat load_q8_fused(const std::vector<std::string> & names, bool interleave_pairs);
     QMat load_q8(const std::string & name);  // Q8_0 (mma.sync layout) or Q4_K (tcgen05 layout)
     void linear(const QMat & w, const half * x16, int ldx, int rows, const GemvOut & out, cudaStream_t s);
     // stride 0: a causal conv; stride s > 0: a transposed conv, split into s phase convs
@@ -170,8 +173,8 @@ private:
     int tcap_ = 0;
     size_t act_elems_ = 0;
     float * a_ = nullptr, * b_ = nullptr, * c_ = nullptr;   // conv-stack ping-pong [C][L]
-    float * t32_ = nullptr, * q_ = nullptr, * k_ = nullptr, * v_ = nullptr, * o_ = nullptr;
-    float * g_ = nullptr, * u_ = nullptr, * pcm_ = nullptr;
+    float * t32_ = nullptr, * q_ = nullptr, * o_ = nullptr;  // q_: rows of q | k | v
+    float * pcm_ = nullptr;
     float * part_ = nullptr;  // channel-split partial sums of the convolutions
     half * t16_ = nullptr, * att16_ = nullptr, * f16_ = nullptr;
     int * codes_ = nullptr;
