@@ -463,12 +463,12 @@ def config5(pkg, gen, voc, nc, seed, elastic_s=10.0, n_gpus_share=8, long_steps=
     return out
 
 
-def config4(pkg, args, local, n_sessions=40):
+def config4(pkg, args, local, barrier=None, n_sessions=40):
     """Configuration 4: a Q4_K model (backbone and depth linears Q4_K); 40 sessions per GPU arrive
     at t = 0 (prompts U[32,256] tokens, 5 s voice contexts of 63 frames, generation U[100,300]
     frames); one batched create, then serving steps (frame + PCM, C ABI) until every session has
     finished. Aggregate RTF = all audio / wall; TTFA = the first step's return (host wall clock)."""
-    path = model_path(args, 0, quant="q4_k")
+    path = model_path(args, local, barrier, quant="q4_k")  # written once per node, by local rank 0
     gen = pkg.GeneratorHandle(path, local)
     voc = pkg.VocoderHandle(generator=gen)
     try:
@@ -820,7 +820,7 @@ def main():
     if "4" in want:
         if barrier:
             barrier()
-        configs["c4_q4k_burst"] = config4(pkg, args, local)
+        configs["c4_q4k_burst"] = config4(pkg, args, local, barrier)
         if world > 1:
             t = torch.tensor([configs["c4_q4k_burst"]["wall_s"]], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

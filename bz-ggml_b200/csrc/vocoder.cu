@@ -637,8 +637,8 @@ __global__ void __launch_bounds__(kTThreads, 2) voc_conv_tc_kernel(const __grid_
     if (warp == 8) tmem_dealloc(tmem, cols);
 }
 
-// The same convolution with the staged window itself as the A operand, for sequences of at least
-// one tile per segment: a CTA's 128 steps lie in one segment (tiles are laid out per segment, the
+// The same convolution with the staged window itself as the A operand, for segments of 96 steps
+// and more: a CTA's 128 steps lie in one segment (tiles are laid out per segment, the
 // last one of a segment partly empty), so output step r of tap k reads window row r + k dil and
 // the tap's A operand is the window from row k dil on: a shared-memory descriptor that starts
 // k dil rows into the 1024-byte-aligned window, whose 16-byte pieces are stored at the XOR of the
@@ -946,16 +946,31 @@ __global__ void __launch_bounds__(128) voc_attn_ring_kernel(const float * q, int
         float ps = p;
         for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
         l = l * corr + ps;
-        for (int e = 0; e < E; e++) acc[e] *= corr;
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[e] *= corr;
+        // value rows eight at a time, every load of a group issued before its sums (the loads of
+        // consecutive positions do not wait on one another)
         const int nb = min(32, pos - jb + 1);
-        for (int jj = 0; jj < nb; jj++) {
-            const float pj = __shfl_sync(0xffffffffu, p, jj);
-            const float * vr = base + (size_t) ((jb + jj) % R) * 2 * kvd + kvd;
-            for (int e = 0; e < E; e++) acc[e] += pj * vr[lane + 32 * e];
+        for (int j8 = 0; j8 < nb; j8 += 8) {
+            float vv[8][4];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float * vr = base + (size_t) ((jb + j8 + u) % R) * 2 * kvd + kvd;
+#pragma unroll
+                for (int e = 0; e < 4; e++) vv[u][e] = (j8 + u < nb && e < E) ? vr[lane + 32 * e] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float pj = __shfl_sync(0xffffffffu, p, (j8 + u) & 31);  // zero past the last position
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[e] += pj * vv[u][e];
+            }
         }
         m = mn;
     }
-    for (int e = 0; e < E; e++) out[((size_t) row * nh + h) * hd + lane + 32 * e] = __float2half_rn(acc[e] / l);
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+        if (e < E) out[((size_t) row * nh + h) * hd + lane + 32 * e] = __float2half_rn(acc[e] / l);
 }
 
 // layer norm over each row of [R][C] (mean and variance in double, src/common.cpp:131-134) -> f16
@@ -1156,9 +1171,10 @@ void launch_conv_tc(ConvArgs a, const half * w16, int nt, int otiles, int kchunk
     const int seg = a.seg_len > 0 ? a.seg_len : a.L;
     const int n_seg = a.L / seg;
     const size_t two_per_sm = (size_t) 113 * 1024;
-    // segments of at least 112 steps: tiles per segment (at most 1/8 of a tile's rows unused) and
-    // the window itself as the A operand of every tap
-    if (seg >= 112) {
+    // segments of at least 96 steps: tiles per segment (at most a quarter of a tile's rows unused)
+    // and the window itself as the A operand of every tap (measured, 64 streams x 1 frame: 96
+    // steps and up 2.87 ms per decode, 112 and up 3.02 ms, every stage 3.02 ms)
+    if (seg >= 96) {
         TcConvW q;
         q.w16 = w16;
         q.nt = nt;
