@@ -514,8 +514,8 @@ void Engine::ensure_prefill_capacity(int T) {
         tqkv_ = (float *) pa((size_t) tmax_ * (teq + 2 * tekv) * 4);
         tatt16_ = (half *) pa((size_t) tmax_ * teq * 2);
         ttmp_ = (float *) pa((size_t) tmax_ * te.hidden * 4);
-        tk_ = (float *) pa((size_t) tmax_ * tekv * 4);
-        tv_ = (float *) pa((size_t) tmax_ * tekv * 4);
+        tk_ = (half *) pa((size_t) tmax_ * tekv * 2);
+        tv_ = (half *) pa((size_t) tmax_ * tekv * 2);
     }
 }
 
@@ -1146,7 +1146,8 @@ void Engine::te_forward(const std::vector<int> & tokens, float * out_rows) {
     for (int l = 0; l < te.n_layer; l++) {
         const LayerW & w = te_[l];
         const bool full = l < (int) te.is_full.size() && te.is_full[l] != 0;
-        launch_rmsnorm(tx_, D, w.attn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        // layer 0's attention norm; later layers receive theirs from the previous layer's last add
+        if (l == 0) launch_rmsnorm(tx_, D, w.attn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
         gemv(w.qkv, th16_, D, T, GemvOut{ EPI_STORE, tqkv_, nullptr, qkvd });
         PrefillArgs pa;
         pa.qkv = tqkv_; pa.ldq = qkvd; pa.T = T; pa.start = 0;
@@ -1161,13 +1162,14 @@ void Engine::te_forward(const std::vector<int> & tokens, float * out_rows) {
         launch_qk_prep(pa, false, stream_);
         launch_attn_prefill(pa, false, stream_);
         gemv(w.o, tatt16_, q, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
-        launch_norm_add(tx_, ttmp_, D, w.post_attn, te.eps, T, stream_);
-        launch_rmsnorm(tx_, D, w.ffn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        launch_norm_add_norm(tx_, ttmp_, D, w.post_attn, te.eps, w.ffn_norm, th16_, D, T, stream_);
         gemv(w.gu, th16_, D, T, GemvOut{ EPI_GEGLU, nullptr, tff16_, te.ffn });
         gemv(w.down, tff16_, te.ffn, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
-        launch_norm_add(tx_, ttmp_, D, w.post_ffn, te.eps, T, stream_);
+        // the next layer's attention norm, or the output norm after the last layer
+        const float * next_norm = l + 1 < te.n_layer ? te_[l + 1].attn_norm : te_out_norm_;
+        launch_norm_add_norm(tx_, ttmp_, D, w.post_ffn, te.eps, next_norm, th16_, D, T, stream_);
     }
-    launch_rmsnorm(tx_, D, te_out_norm_, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+    if (te.n_layer == 0) launch_rmsnorm(tx_, D, te_out_norm_, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
     gemv(te_proj_, th16_, D, T, GemvOut{ EPI_STORE, out_rows, nullptr, cfg.hidden });
 }
 
@@ -1406,7 +1408,8 @@ void Engine::te_forward_packed(const std::vector<const std::vector<int> *> & tse
     for (int l = 0; l < te.n_layer; l++) {
         const LayerW & w = te_[l];
         const bool full = l < (int) te.is_full.size() && te.is_full[l] != 0;
-        launch_rmsnorm(tx_, D, w.attn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        // layer 0's attention norm; later layers receive theirs from the previous layer's last add
+        if (l == 0) launch_rmsnorm(tx_, D, w.attn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
         gemv(w.qkv, th16_, D, T, GemvOut{ EPI_STORE, tqkv_, nullptr, qkvd });
         PrefillArgs pa;
         pa.qkv = tqkv_; pa.ldq = qkvd; pa.T = T; pa.start = 0;
@@ -1422,13 +1425,14 @@ void Engine::te_forward_packed(const std::vector<const std::vector<int> *> & tse
         launch_qk_prep(pa, false, stream_);
         launch_attn_prefill(pa, false, stream_);
         gemv(w.o, tatt16_, q, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
-        launch_norm_add(tx_, ttmp_, D, w.post_attn, te.eps, T, stream_);
-        launch_rmsnorm(tx_, D, w.ffn_norm, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+        launch_norm_add_norm(tx_, ttmp_, D, w.post_attn, te.eps, w.ffn_norm, th16_, D, T, stream_);
         gemv(w.gu, th16_, D, T, GemvOut{ EPI_GEGLU, nullptr, tff16_, te.ffn });
         gemv(w.down, tff16_, te.ffn, T, GemvOut{ EPI_STORE, ttmp_, nullptr, D });
-        launch_norm_add(tx_, ttmp_, D, w.post_ffn, te.eps, T, stream_);
+        // the next layer's attention norm, or the output norm after the last layer
+        const float * next_norm = l + 1 < te.n_layer ? te_[l + 1].attn_norm : te_out_norm_;
+        launch_norm_add_norm(tx_, ttmp_, D, w.post_ffn, te.eps, next_norm, th16_, D, T, stream_);
     }
-    launch_rmsnorm(tx_, D, te_out_norm_, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
+    if (te.n_layer == 0) launch_rmsnorm(tx_, D, te_out_norm_, D, te.eps, th16_, D, nullptr, 0, 0, T, nullptr, stream_);
     gemv(te_proj_, th16_, D, T, GemvOut{ EPI_STORE, out_rows, nullptr, cfg.hidden });
 }
 

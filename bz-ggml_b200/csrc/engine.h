@@ -299,7 +299,8 @@ private:
     // prefill buffers (grown on demand)
     int tmax_ = 0;
     float * px_ = nullptr, * pqkv_ = nullptr, * plog_ = nullptr, * tx_ = nullptr, * tqkv_ = nullptr;
-    float * ttmp_ = nullptr, * tk_ = nullptr, * tv_ = nullptr;
+    float * ttmp_ = nullptr;
+    half * tk_ = nullptr, * tv_ = nullptr;  // text encoder keys and values (f16, the attention's operand type)
     half * ph16_ = nullptr, * pff16_ = nullptr, * patt16_ = nullptr, * th16_ = nullptr, * tff16_ = nullptr,
          * tatt16_ = nullptr;
     int * ptok_ = nullptr, * pframes_ = nullptr;

@@ -433,6 +433,31 @@ __global__ void norm_add_kernel(float * x, const float * t, int D, const float *
     for (int d = threadIdx.x; d < D; d += blockDim.x) x[(size_t) r * D + d] += (tr[d] * scale) * w[d];
 }
 
+// x += RMSNorm(t) * w (a sub-block's post-norm and residual add), then y16 = RMSNorm(x) * w2, the
+// norm that feeds the next sub-block (each thread re-reads only the elements it wrote)
+__global__ void norm_add_norm_kernel(float * x, const float * t, int D, const float * w, float eps, const float * w2,
+                                     half * y16, int ld16) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    const float * tr = t + (size_t) r * D;
+    float * xr = x + (size_t) r * D;
+    float ss = 0.0f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) ss += tr[d] * tr[d];
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float) D + eps);
+    float ss2 = 0.0f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float v = xr[d] + (tr[d] * scale) * w[d];
+        xr[d] = v;
+        ss2 += v * v;
+    }
+    ss2 = block_sum(ss2, red);
+    const float scale2 = 1.0f / sqrtf(ss2 / (float) D + eps);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) y16[(size_t) r * ld16 + d] = __float2half_rn((xr[d] * scale2) * w2[d]);
+}
+
 // ------------------------------------------------------------------------------------ embeddings
 __global__ void embed_rows_kernel(QRows e, const int * idx, float scale, float * o32, half * o16, int ld) {
     pdl_trigger();
@@ -821,9 +846,9 @@ __global__ void qk_prep_kernel(const PrefillArgs a) {
 #pragma unroll
             for (int e = 0; e < E; e++) dst[lane + 32 * e] = __float2half_rn(x[e]);
         } else {
-            float * dst = (kind == 1 ? a.flat_k : a.flat_v) + ((size_t) r * a.n_kv + h) * HD;
+            half * dst = (kind == 1 ? a.flat_k : a.flat_v) + ((size_t) r * a.n_kv + h) * HD;
 #pragma unroll
-            for (int e = 0; e < E; e++) dst[lane + 32 * e] = x[e];
+            for (int e = 0; e < E; e++) dst[lane + 32 * e] = __float2half_rn(x[e]);
         }
     }
 }
@@ -1087,12 +1112,13 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const AttnDecodeAr
 template <int HD>
 __host__ __device__ constexpr int prefill_kb() { return HD >= 256 ? 32 : 64; }
 template <int HD>
-constexpr size_t prefill_smem() { return (size_t) (kPrefillQBlock + 2 * prefill_kb<HD>()) * (HD + 8) * sizeof(half); }
+constexpr size_t prefill_smem() { return (size_t) (kPrefillQBlock + 4 * prefill_kb<HD>()) * (HD + 8) * sizeof(half); }
 
 // Prefill attention on the tensor cores (mma.sync m16n8k16, f16 operands, f32 accumulation and
 // online softmax): one CTA per (query block of 64 rows of one sequence, query head), 4 warps of
-// 16 query rows. Q is staged once as f16; K and V tiles of KB positions are converted to f16 in
-// shared memory (rows padded by 8 halves so ldmatrix rows fall in distinct banks). S = Q K^T
+// 16 query rows. Q is staged once as f16; K and V tiles of KB f16 positions come by cp.async into
+// two shared-memory buffers, the next tile's copies in flight while the current one is used
+// (rows padded by 8 halves so ldmatrix rows fall in distinct banks). S = Q K^T
 // comes from ldmatrix fragments of Q and K, P = exp(S - max) is repacked from the accumulator
 // registers into A fragments, and V is read with the transposing ldmatrix. Causal, windowed
 // (text encoder) and full spans are per query row, as in the f32 restatement.
@@ -1103,8 +1129,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillArgs a) 
     constexpr int QB = kPrefillQBlock, KB = prefill_kb<HD>(), LD = HD + 8;
     extern __shared__ __align__(16) unsigned char psm_raw[];
     half * sq = reinterpret_cast<half *>(psm_raw);  // [QB][LD]
-    half * sk = sq + QB * LD;                        // [KB][LD]
-    half * sv = sk + KB * LD;                        // [KB][LD]
+    half * sk = sq + QB * LD;                        // [2][KB][LD]
+    half * sv = sk + 2 * KB * LD;                    // [2][KB][LD]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     // this CTA's sequence: rows [base, base + T) of the packed rows (one sequence: all of them)
     int base = 0, T = a.T, r0 = blockIdx.x * QB;
@@ -1147,28 +1173,39 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillArgs a) 
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
     const uint32_t sq_u = (uint32_t) __cvta_generic_to_shared(sq), sk_u = (uint32_t) __cvta_generic_to_shared(sk),
                    sv_u = (uint32_t) __cvta_generic_to_shared(sv);
-    for (int t0 = (lo_min / KB) * KB; t0 < hi_max; t0 += KB) {
-        __syncthreads();
+    // K and V of positions [t0, t0 + KB) into buffer b (positions past hi_max read as zeros; their
+    // copy addresses stay on a position the CTA reads anyway)
+    auto load_tile = [&](int t0, int b) {
+        const uint32_t dk = sk_u + (uint32_t) (b * KB * LD) * 2, dv = sv_u + (uint32_t) (b * KB * LD) * 2;
         for (int i = threadIdx.x; i < KB * (HD / 8); i += blockDim.x) {
             const int j = i / (HD / 8), c8 = i - j * (HD / 8);
             const int pos = t0 + j;
-            uint4 kq = make_uint4(0u, 0u, 0u, 0u), vq = kq;
-            if (pos < hi_max) {
-                if (PAGED) {
-                    kq = *reinterpret_cast<const uint4 *>(a.kv.pool + paged_off(a.kv, page_row, pos, 0, h, a.n_kv, HD) + 8 * c8);
-                    vq = *reinterpret_cast<const uint4 *>(a.kv.pool + paged_off(a.kv, page_row, pos, 1, h, a.n_kv, HD) + 8 * c8);
-                } else {
-                    const size_t off = ((size_t) (base + pos) * a.n_kv + h) * HD + 8 * c8;
-                    const float4 k0 = *reinterpret_cast<const float4 *>(a.flat_k + off), k1 = *reinterpret_cast<const float4 *>(a.flat_k + off + 4);
-                    const float4 v0 = *reinterpret_cast<const float4 *>(a.flat_v + off), v1 = *reinterpret_cast<const float4 *>(a.flat_v + off + 4);
-                    kq = make_uint4(pack_h2(k0.x, k0.y), pack_h2(k0.z, k0.w), pack_h2(k1.x, k1.y), pack_h2(k1.z, k1.w));
-                    vq = make_uint4(pack_h2(v0.x, v0.y), pack_h2(v0.z, v0.w), pack_h2(v1.x, v1.y), pack_h2(v1.z, v1.w));
-                }
+            const bool valid = pos < hi_max;
+            const int pc = valid ? pos : lo_min;
+            const half * ks, * vs;
+            if (PAGED) {
+                ks = a.kv.pool + paged_off(a.kv, page_row, pc, 0, h, a.n_kv, HD) + 8 * c8;
+                vs = a.kv.pool + paged_off(a.kv, page_row, pc, 1, h, a.n_kv, HD) + 8 * c8;
+            } else {
+                const size_t off = ((size_t) (base + pc) * a.n_kv + h) * HD + 8 * c8;
+                ks = a.flat_k + off;
+                vs = a.flat_v + off;
             }
-            *reinterpret_cast<uint4 *>(sk + j * LD + 8 * c8) = kq;
-            *reinterpret_cast<uint4 *>(sv + j * LD + 8 * c8) = vq;
+            const uint32_t so = (uint32_t) (j * LD + 8 * c8) * 2;
+            cp_async16(dk + so, ks, valid);
+            cp_async16(dv + so, vs, valid);
         }
+    };
+    const int t_first = (lo_min / KB) * KB;
+    if (t_first < hi_max) load_tile(t_first, 0);
+    cp_async_commit();
+    int buf = 0;
+    for (int t0 = t_first; t0 < hi_max; t0 += KB, buf ^= 1) {
+        if (t0 + KB < hi_max) load_tile(t0 + KB, buf ^ 1);
+        cp_async_commit();  // possibly empty: the wait leaves only the newest group in flight
+        cp_async_wait1();
         __syncthreads();
+        const uint32_t skb = sk_u + (uint32_t) (buf * KB * LD) * 2, svb = sv_u + (uint32_t) (buf * KB * LD) * 2;
         // S = Q K^T for rows 16w..16w+15 and the tile's KB positions
         float sc[KB / 8][4];
 #pragma unroll
@@ -1182,7 +1219,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillArgs a) 
             for (int n2 = 0; n2 < KB / 16; n2++) {
                 uint32_t b0, b1, b2, b3;
                 const int kr = 16 * n2 + (lane & 7) + (lane >> 4) * 8, kc = 16 * kk + ((lane >> 3) & 1) * 8;
-                ldsm_x4(sk_u + (uint32_t) (kr * LD + kc) * 2, b0, b1, b2, b3);
+                ldsm_x4(skb + (uint32_t) (kr * LD + kc) * 2, b0, b1, b2, b3);
                 mma16816(sc[2 * n2], af, b0, b1);
                 mma16816(sc[2 * n2 + 1], af, b2, b3);
             }
@@ -1241,11 +1278,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillArgs a) 
             for (int n2 = 0; n2 < HD / 16; n2++) {
                 uint32_t b0, b1, b2, b3;
                 const int vr = 16 * k2 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = 16 * n2 + (lane >> 4) * 8;
-                ldsm_x4_t(sv_u + (uint32_t) (vr * LD + vc) * 2, b0, b1, b2, b3);
+                ldsm_x4_t(svb + (uint32_t) (vr * LD + vc) * 2, b0, b1, b2, b3);
                 mma16816(o[2 * n2], pf, b0, b1);
                 mma16816(o[2 * n2 + 1], pf, b2, b3);
             }
         }
+        __syncthreads();  // every warp is done with buffer buf before the next tile's copies reuse it
     }
 #pragma unroll
     for (int off = 1; off <= 2; off <<= 1) {
@@ -1880,6 +1918,13 @@ void launch_rmsnorm(const float * x, int ldx, const float * w, int D, float eps,
 void launch_norm_add(float * x, const float * t, int D, const float * w, float eps, int rows, cudaStream_t s) {
     if (rows <= 0) return;
     launch_k(norm_add_kernel, rows, 256, 0, s, x, t, D, w, eps);
+    BZB_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_norm_add_norm(float * x, const float * t, int D, const float * w, float eps, const float * w2, half * y16,
+                          int ld16, int rows, cudaStream_t s) {
+    if (rows <= 0) return;
+    launch_k(norm_add_norm_kernel, rows, 256, 0, s, x, t, D, w, eps, w2, y16, ld16);
     BZB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -139,6 +139,9 @@ void launch_copy_rows(const float * src, int lds, const int * src_idx, float * d
                       int cols, cudaStream_t s);
 // x[r] += rmsnorm(t[r]) * w  (Gemma post-norms)
 void launch_norm_add(float * x, const float * t, int D, const float * w, float eps, int rows, cudaStream_t s);
+// x += RMSNorm(t) w, then y16 = RMSNorm(x) w2 (row stride ld16)
+void launch_norm_add_norm(float * x, const float * t, int D, const float * w, float eps, const float * w2, half * y16,
+                          int ld16, int rows, cudaStream_t s);
 
 // dst[r] = f16/f32 dequantised row idx[r] of an embedding table, scaled
 void launch_embed_rows(const QRows & e, const int * idx, int n, float scale, float * out32, half * out16,
@@ -191,10 +194,10 @@ struct PrefillArgs {
     float eps = 0;
     const float2 * rope = nullptr;
     float scale = 0;
-    // paged destination (slot's page row) or flat f32 k/v [T][n_kv][hd]
+    // paged destination (slot's page row) or flat f16 k/v [T][n_kv][hd]
     AttnKV kv;
     const int * page_row = nullptr;
-    float * flat_k = nullptr, * flat_v = nullptr;
+    half * flat_k = nullptr, * flat_v = nullptr;
     int window = 0;         // bidirectional window (0 = full) for the text encoder
     bool causal = true;
     half * out = nullptr;
