@@ -124,8 +124,18 @@ class Arrivals:
         self.rng = np.random.default_rng(seed)
         self.prompt, self.voice, self.gen = prompt, voice, gen
         self.next_id = first_id
+        self.ready = []
+
+    def prefill(self, n):
+        """Draws the next n arrivals ahead of time: producing the synthetic request (the text and
+        voice a client would send) is not the server's work, so timed loops take ready ones."""
+        while len(self.ready) < n:
+            self.ready.append(self._draw())
 
     def take(self):
+        return self.ready.pop(0) if self.ready else self._draw()
+
+    def _draw(self):
         rng = self.rng
         plen = int(rng.integers(self.prompt[0], self.prompt[1] + 1))
         vframes = int(rng.integers(self.voice[0], self.voice[1] + 1))
@@ -257,6 +267,7 @@ def poisson_run(pkg, gen, voc, nc, seed, rate, duration, max_live):
     first PCM of a session (its first step's return) minus its arrival time (python/bz_ggml/
     cluster.py:636-637, 661), host wall clock."""
     arr = Arrivals(pkg, nc, seed, first_id=2_000_000)
+    arr.prefill(int(2 * rate * duration) + 16)  # the clients' requests exist before they arrive
     rng = np.random.default_rng(seed + 1)
     live, left, arrived, first = [], {}, {}, {}
     ttfa, conc, frames = [], [], 0
@@ -375,6 +386,7 @@ def config5(pkg, gen, voc, nc, seed, elastic_s=10.0, n_gpus_share=8, long_steps=
     out = {}
     # elastic waves
     arr = Arrivals(pkg, nc, seed, gen=(200, 1500), first_id=8_000_000)
+    arr.prefill(int(elastic_s / 2 + 2) * (20 // n_gpus_share + 1))
     live, left, arrived, first = [], {}, {}, {}
     ttfa, conc, frames, steps = [], [], 0, 0
     wave, next_wave = 0, 0.0
@@ -742,7 +754,9 @@ def main():
         torch.cuda.synchronize()
         gen.sync()
 
-    # timed: device-resident serving steps, admissions included
+    # timed: device-resident serving steps, admissions included (the arrivals' synthetic requests
+    # drawn beforehand)
+    srv.arr.prefill(4 * args.steps + args.sessions)
     admits_before, frames_before = srv.admitted, srv.frames
     ttfa_ev = []
     begin()
@@ -765,6 +779,7 @@ def main():
     mean_ctx = float(np.mean(list(srv.ctx.values())))
 
     # the same loop through the C ABI with host buffers
+    srv.arr.prefill(4 * args.steps + args.sessions)
     frames_before, admit_h2d_before = srv.frames, srv.admit_h2d
     h2d = d2h = 0
     begin()
