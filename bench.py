@@ -25,7 +25,9 @@ Prints one JSON line (rank 0):
 - `value`: the serving steps resident on the device (bzb_generator_step_pcm_device: frames and PCM
   stay in HBM; admissions are host calls between steps), CUDA events on the engine's stream;
 - `e2e`: the same loop through the C ABI with host buffers (bzb_generator_sessions_step_pcm:
-  session ids and seeds up, frames, next cb0 and every session's PCM down, each step);
+  session ids and seeds up, frames, next cb0 and every session's PCM down, each step), over
+  `--long-steps` steps (100) so that it meets the closed loop's steady admission rate;
+  `steady_state`: the device-resident loop over as many steps, its like-for-like partner;
 - `decode_only`: the frame step alone on the final batch (no vocoder, no admission);
 - `ttfa`: time to first audio of the sessions admitted in the timed loop (prefill + first step
   with its PCM), and an open-loop run with Poisson arrivals at 4/s (configuration 3 as stated);
@@ -82,6 +84,9 @@ def parse():
     ap.add_argument("--poisson-s", type=float, default=6.0, help="seconds of the open-loop Poisson run (0: skip)")
     ap.add_argument("--configs", default="1,2,4,5,abi", help="other configurations to measure (comma list, or none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--long-steps", type=int, default=100,
+                    help="steps of the end-to-end (C ABI) loop and of the long device-resident loop beside it: "
+                         "enough admissions for the closed loop's steady rate (about 0.28 per step)")
     ap.add_argument("--profile", action="store_true",
                     help="after the ramp, run one device-resident serving step between cudaProfilerStart/Stop and exit (ncu)")
     ap.add_argument("--profile-admit", action="store_true",
@@ -778,13 +783,26 @@ def main():
         ttfa_closed += [ea.elapsed_time(eb)] * k
     mean_ctx = float(np.mean(list(srv.ctx.values())))
 
-    # the same loop through the C ABI with host buffers
-    srv.arr.prefill(4 * args.steps + args.sessions)
-    frames_before, admit_h2d_before = srv.frames, srv.admit_h2d
+    # long windows at the closed loop's steady admission rate: the device-resident loop, then the
+    # same loop through the C ABI with host buffers (e2e)
+    n_long = max(args.steps, args.long_steps)
+    srv.arr.prefill(n_long + args.sessions)
+    admits_before, frames_before = srv.admitted, srv.frames
+    begin()
+    e0 = ev()
+    for _ in range(n_long):
+        srv.admit()
+        srv.step_device()
+    e1 = ev()
+    e1.synchronize()
+    ms_long = max_over_ranks(e0.elapsed_time(e1))
+    frames_long, admits_long = srv.frames - frames_before, srv.admitted - admits_before
+    srv.arr.prefill(n_long + args.sessions)
+    frames_before, admit_h2d_before, admits_before = srv.frames, srv.admit_h2d, srv.admitted
     h2d = d2h = 0
     begin()
     e0 = ev()
-    for _ in range(args.steps):
+    for _ in range(n_long):
         srv.admit()
         hb, db = srv.step_abi()
         h2d += hb
@@ -792,7 +810,7 @@ def main():
     e1 = ev()
     e1.synchronize()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1))
-    frames_e2e = srv.frames - frames_before
+    frames_e2e, admits_e2e = srv.frames - frames_before, srv.admitted - admits_before
     h2d += srv.admit_h2d - admit_h2d_before
 
     # the frame step alone on the last batch, and one profiled eager step (roofline)
@@ -892,10 +910,14 @@ def main():
                        "l2": "per-step working set > 126 MB L2 (no flush needed)", "ramp_steps": args.ramp,
                        "ramp_s": t_ramp, "admissions_in_timed_steps": admits_timed, "mean_context": mean_ctx,
                        "model_load_s": t_load},
-            "e2e": {"value": e2e, "unit": "x realtime", "h2d_bytes_per_step": h2d / args.steps,
-                    "d2h_bytes_per_step": d2h / args.steps,
+            "e2e": {"value": e2e, "unit": "x realtime", "h2d_bytes_per_step": h2d / n_long,
+                    "d2h_bytes_per_step": d2h / n_long, "steps": n_long, "admissions": admits_e2e,
                     "route": "per step: admissions (bzb_generator_sessions_create_batch, prompt text and voice codes "
                              "up) and bzb_generator_sessions_step_pcm (ids and seeds up; frames, next cb0 and PCM down)"},
+            "steady_state": {"value": world * frames_long * FRAME_S / (ms_long / 1e3), "unit": "x realtime",
+                             "steps": n_long, "admissions": admits_long, "ms_per_step": ms_long / n_long,
+                             "method": "the device-resident loop over as many steps as e2e (the K-step value sees "
+                                       "fewer admissions than the steady rate of about 0.28 per step)"},
             "decode_only": {"value": world * args.sessions * args.steps * FRAME_S / (ms_decode / 1e3),
                             "ms_per_step": ms_decode / args.steps,
                             "method": "the frame step's graph alone on the last batch (no vocoder, no admission)"},
