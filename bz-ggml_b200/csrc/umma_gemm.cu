@@ -425,10 +425,9 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_gemm_kernel(const UParams
 // reads TMEM lanes 32 (w % 4) .. + 31, activation rows 128 (w / 4) .. + 127).
 constexpr int kPN = 256;
 constexpr int kPRawStages = 4;
-constexpr int kPAStages = 2;
-constexpr int kPBStages = 4;
+constexpr int kPStages = 3;   // stages of the dequantised weight tile and the activation tile together
 constexpr int kPBBytes = kPN * kChunkK * 2;
-constexpr int kPrefillSmem = 1024 + kPAStages * kABytes + kPBStages * kPBBytes + kPRawStages * kRawBytes;
+constexpr int kPrefillSmem = 1024 + kPStages * (kABytes + kPBBytes) + kPRawStages * kRawBytes;
 static_assert(kPrefillSmem <= 227 * 1024, "prefill GEMM shared memory");
 
 template <int EPI>
@@ -436,13 +435,16 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
     constexpr uint32_t kCols = kPN;
     constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t) (kPN >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t a_full[kPAStages], a_empty[kPAStages], b_full[kPBStages], b_empty[kPBStages];
+    // one ring for both MMA operands: stage s is full once the 8 producer warps have written its
+    // weight tile and its activation tile has landed, and empty once the MMAs reading it are done,
+    // so the MMA thread waits and commits once per chunk
+    __shared__ uint64_t st_full[kPStages], st_empty[kPStages];
     __shared__ uint64_t raw_full[kPRawStages], raw_empty[kPRawStages], done_bar;
     __shared__ uint32_t tmem_slot;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
-    uint8_t * sB = sA + kPAStages * kABytes;
-    uint8_t * sR = sB + kPBStages * kPBBytes;
+    uint8_t * sB = sA + kPStages * kABytes;
+    uint8_t * sR = sB + kPStages * kPBBytes;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, row0 = blockIdx.y * kPN;
@@ -451,17 +453,13 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
 
     if (warp == 8) tmem_alloc(&tmem_slot, kCols);
     if (tid == 0) {
-        for (int i = 0; i < kPAStages; i++) {
-            mbar_init(&a_full[i], kThreads);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < kPBStages; i++) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
+        for (int i = 0; i < kPStages; i++) {
+            mbar_init(&st_full[i], 8 + 1);  // producer warps + the activation copy's expect_tx
+            mbar_init(&st_empty[i], 1);
         }
         for (int i = 0; i < kPRawStages; i++) {
             mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], kThreads);
+            mbar_init(&raw_empty[i], 8);    // one arrival per producer warp
         }
         mbar_init(&done_bar, 1);
         fence_mbar_init();
@@ -477,31 +475,33 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
     if (warp < 8) {
         const int r = tid & (kTileM - 1), hb = tid >> 7;
         for (int c = 0; c < nch; c++) {
-            const int rs = c % kPRawStages, ab = c % kPAStages;
+            const int rs = c % kPRawStages, st = c % kPStages;
             ok = mbar_wait(&raw_full[rs], (uint32_t) (c / kPRawStages) & 1u, p.err);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             const RawPiece pc = read_piece(sR + rs * kRawBytes, p.q4, r, hb);
-            mbar_arrive(&raw_empty[rs]);
-            if (c >= kPAStages) ok = mbar_wait(&a_empty[ab], (uint32_t) ((c / kPAStages) - 1) & 1u, p.err);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+            if (c >= kPStages) ok = mbar_wait(&st_empty[st], (uint32_t) ((c / kPStages) - 1) & 1u, p.err, kSpinLimit, 32);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            write_piece(pc, p.q4, r, hb, sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
-            fence_proxy_async();
-            mbar_arrive(&a_full[ab]);
+            write_piece(pc, p.q4, r, hb, sA + st * kABytes + (r >> 3) * 1024 + (r & 7) * 128);
+            fence_proxy_async();  // each thread's stores before the warp's arrival
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&st_full[st]);
         }
     } else if (warp == 8) {
         if (lane == 0) {
             for (int c = 0; c < nch; c++) {
-                const int ab = c % kPAStages, bb = c % kPBStages;
-                ok = mbar_wait(&b_full[bb], (uint32_t) (c / kPBStages) & 1u, p.err);
-                if (ok) ok = mbar_wait(&a_full[ab], (uint32_t) (c / kPAStages) & 1u, p.err);
+                const int st = c % kPStages;
+                ok = mbar_wait(&st_full[st], (uint32_t) (c / kPStages) & 1u, p.err);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sA + ab * kABytes), b0 = smem_u32(sB + bb * kPBBytes);
+                const uint32_t a0 = smem_u32(sA + st * kABytes), b0 = smem_u32(sB + st * kPBBytes);
 #pragma unroll
                 for (int kk = 0; kk < kChunkK / 16; kk++)
                     umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&a_empty[ab]);
-                umma_commit(&b_empty[bb]);
+                umma_commit(&st_empty[st]);
             }
             umma_commit(&done_bar);
             if (!mbar_drain(&done_bar, 0u, p.err)) ok = false;
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
             int issued = 0;
             for (int c = 0; c < nch; c++) {
                 const int rs = c % kPRawStages;
-                if (c >= kPRawStages) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kPRawStages) - 1) & 1u, p.err);
+                if (c >= kPRawStages) ok = mbar_wait(&raw_empty[rs], (uint32_t) ((c / kPRawStages) - 1) & 1u, p.err, kSpinLimit, 32);
                 if (!ok) break;
                 fence_proxy_async();  // generic reads of the slot before the async-proxy overwrite
                 mbar_expect_tx(&raw_full[rs], (uint32_t) cb);
@@ -528,15 +528,18 @@ __global__ void __launch_bounds__(kAllThreads, 1) umma_prefill_kernel(const UPar
             pdl_wait();  // activations come from the previous kernel
             int issued = 0;
             for (int c = 0; c < nch; c++) {
-                const int bb = c % kPBStages;
-                if (c >= kPBStages) ok = mbar_wait(&b_empty[bb], (uint32_t) ((c / kPBStages) - 1) & 1u, p.err);
+                const int st = c % kPStages;
+                if (c >= kPStages) ok = mbar_wait(&st_empty[st], (uint32_t) ((c / kPStages) - 1) & 1u, p.err, kSpinLimit, 32);
                 if (!ok) break;
-                mbar_expect_tx(&b_full[bb], kPBBytes);
-                tma_2d(sB + bb * kPBBytes, &xmap, c * kChunkK, row0, &b_full[bb]);
+                mbar_expect_tx(&st_full[st], kPBBytes);
+                tma_2d(sB + st * kPBBytes, &xmap, c * kChunkK, row0, &st_full[st]);
                 issued = c + 1;
             }
-            for (int c = max(0, issued - kPBStages); c < issued; c++)
-                mbar_drain(&b_full[c % kPBStages], (uint32_t) (c / kPBStages) & 1u, p.err);
+            // the copies still in flight land before the CTA can exit. A stage's full phase also
+            // needs the producers' arrivals, which a failed run may never make: the wait is bounded
+            // (some 65,000 polls, far longer than any copy takes to land) and then gives up
+            for (int c = max(0, issued - kPStages); c < issued; c++)
+                mbar_drain(&st_full[c % kPStages], (uint32_t) (c / kPStages) & 1u, p.err, kSpinLimit / 64);
         }
     }
     pdl_wait();  // every thread: outputs are read/written below only after the predecessor completed
