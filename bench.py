@@ -765,16 +765,18 @@ def main():
     admits_before, frames_before = srv.admitted, srv.frames
     ttfa_ev = []
     begin()
-    with ClockSampler(uuid) as clk:
-        e0 = ev()
-        for _ in range(args.steps):
-            ea = ev()
-            k = srv.admit()
-            srv.step_device()
-            if k:
-                ttfa_ev.append((ea, ev(), k))
-        e1 = ev()
-        e1.synchronize()
+    # clocks sampled through the K timed steps and the long windows after them
+    clk = ClockSampler(uuid)
+    clk.__enter__()
+    e0 = ev()
+    for _ in range(args.steps):
+        ea = ev()
+        k = srv.admit()
+        srv.step_device()
+        if k:
+            ttfa_ev.append((ea, ev(), k))
+    e1 = ev()
+    e1.synchronize()
     ms_dev = max_over_ranks(e0.elapsed_time(e1))
     frames_dev = srv.frames - frames_before
     admits_timed = srv.admitted - admits_before
@@ -810,6 +812,7 @@ def main():
     e1 = ev()
     e1.synchronize()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+    clk.__exit__(None, None, None)
     frames_e2e, admits_e2e = srv.frames - frames_before, srv.admitted - admits_before
     h2d += srv.admit_h2d - admit_h2d_before
 
