@@ -45,9 +45,12 @@ constexpr int kChunkK = 64;
 constexpr int kABytes = kTileM * kChunkK * 2;            // f16 A stage
 // Every bulk or tensor copy costs the SM a roughly fixed ~0.4 us of issue time whatever its size
 // up to 32 KB, so weights and activations move in groups of kDpGroup chunks per copy.
-constexpr int kRawGroups = 3;                            // weight ring: groups of 4 chunks
+constexpr int kRawGroups = 2;                            // weight ring: groups of 4 chunks
 constexpr int kRawGroupBytes = kDpGroup * kUChunkBytes;
-constexpr int kAStages = 3;
+// dequantised A ring: stages of kASC chunks, handed to the MMA thread with one arrival and
+// released with one commit per stage (a unit's last stage may hold one chunk)
+constexpr int kASC = 2;
+constexpr int kAStages = 2;
 constexpr int kBGroups = 2;                              // activation ring: groups of 4 chunks
 constexpr int kBChunkMax = 64 * kChunkK * 2;             // one chunk of up to 64 activation rows
 constexpr int kBGroupBytes = kDpGroup * kBChunkMax;
@@ -59,7 +62,7 @@ constexpr int kTmemCols = 128;                           // two 64-column accumu
 constexpr int kQFloats = 4 * 2 * 128;                    // query heads of one attention task
 constexpr long long kGridSpin = 1ll << 23;
 
-constexpr int kSmemBytes = 1024 + kAStages * kABytes + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
+constexpr int kSmemBytes = 1024 + kAStages * kASC * kABytes + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
                            (kQFloats + 256 + 16) * 4;
 
 #define DCHECK(x)                                                                             \
@@ -494,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     __shared__ int s_abort;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
-    uint8_t * sB = sA + kAStages * kABytes;
+    uint8_t * sB = sA + kAStages * kASC * kABytes;
     uint8_t * sR = sB + kBGroups * kBGroupBytes;
     float * sQ = reinterpret_cast<float *>(sR + kRawGroups * kRawGroupBytes);
     float * sScale = sQ + kQFloats;
@@ -628,16 +631,17 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
         // ---------------------------------------------------------------- dequantising producers
         const int t = tid - kEpiThreads;
         const int r = t & (kTileM - 1), hb = t >> 7;
-        uint32_t rg = 0, ac = 0;
+        uint32_t rg = 0, as = 0;
         bool ok = true;
         for (int i = 0; i < p.n_phases && ok; i++) {
             const DpPhase ph = load_phase(p.phases + i);
             if (ph.type != DP_GEMM) continue;
             for (int u = unit_of(i, cta, G); u < ph.n_units && ok; u += G) {
                 const UnitRange ur = unit_range(ph, u);
-                for (int c = 0; c < ur.nch && ok; c++, ac++) {
+                for (int c = 0; c < ur.nch && ok; c++) {
                     const int within = c % kDpGroup, gs = min(kDpGroup, ur.nch - (c - within));
-                    const int rs = rg % kRawGroups, ab = ac % kAStages;
+                    const int rs = rg % kRawGroups, ab = as % kAStages, sub = c % kASC;
+                    const bool stage_end = sub == kASC - 1 || c == ur.nch - 1;
                     if (within == 0) ok = dwait(&raw_full[rs], (rg / kRawGroups) & 1u, err, kBackoff);
                     if (!ok) break;
                     if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
@@ -660,10 +664,10 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                         if (lane == 0) mbar_arrive(&raw_empty[rs]);
                         rg++;
                     }
-                    if (ac >= kAStages) ok = dwait(&a_empty[ab], ((ac / kAStages) - 1) & 1u, err, kBackoff);
+                    if (sub == 0 && as >= kAStages) ok = dwait(&a_empty[ab], ((as / kAStages) - 1) & 1u, err, kBackoff);
                     if (!ok) break;
                     const half2 s2 = __halves2half2(sc, sc);
-                    uint8_t * arow = sA + ab * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+                    uint8_t * arow = sA + (ab * kASC + sub) * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
                     if (ph.q4) {
                         float qa, qb;
                         q4k_chunk_scale_min(meta, hb, qa, qb);
@@ -686,9 +690,12 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                             *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
                         }
                     }
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[ab]);
+                    if (stage_end) {
+                        fence_proxy_async();  // each thread's stores of the stage before the arrival
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_full[ab]);
+                        as++;
+                    }
 
                 }
             }
@@ -697,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            uint32_t ck = 0, bg = 0, uc = 0;
+            uint32_t as = 0, bg = 0, uc = 0;
             bool ok = true;
             for (int i = 0; i < p.n_phases && ok; i++) {
                 const DpPhase ph = load_phase(p.phases + i);
@@ -710,25 +717,29 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     tc_fence_after();
                     const uint32_t idesc = (1u << 4) | ((uint32_t) (ph.nb >> 3) << 17) | ((uint32_t) (kTileM >> 4) << 24);
                     const uint32_t d = tmem + (uint32_t) (acc * 64);
-                    for (int c = 0; c < ur.nch; c++, ck++) {
+                    for (int c = 0; c < ur.nch; c++) {
                         const int within = c % kDpGroup, gs = min(kDpGroup, ur.nch - (c - within));
-                        const int ab = ck % kAStages, bs = bg % kBGroups;
+                        const int ab = as % kAStages, bs = bg % kBGroups, sub = c % kASC;
+                        const bool stage_end = sub == kASC - 1 || c == ur.nch - 1;
                         if (within == 0) ok = dwait(&b_full[bs], (bg / kBGroups) & 1u, err);
                         if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 3] = gtimer();
                         if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 9 + c] = gtimer();
-                        ok = ok && dwait(&a_full[ab], (ck / kAStages) & 1u, err);
+                        if (sub == 0) ok = ok && dwait(&a_full[ab], (as / kAStages) & 1u, err);
                         if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 4] = gtimer();
                         if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 25 + c] = gtimer();
                         if (!ok) break;
                         // no tcgen05 fence here: shared-memory operands are ordered by the stage
                         // barriers (TMA complete_tx, or the dequantisers' proxy fence + arrive); the
                         // fence after the accumulator wait above orders the TMEM reuse
-                        const uint32_t a0 = smem_u32(sA + ab * kABytes);
+                        const uint32_t a0 = smem_u32(sA + (ab * kASC + sub) * kABytes);
                         const uint32_t b0 = smem_u32(sB + bs * kBGroupBytes + within * ph.nb * kChunkK * 2);
 #pragma unroll
                         for (int kk = 0; kk < kChunkK / 16; kk++)
                             umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (c > 0 || kk > 0) ? 1u : 0u);
-                        umma_commit(&a_empty[ab]);
+                        if (stage_end) {
+                            umma_commit(&a_empty[ab]);  // the stage's MMAs release its A tiles
+                            as++;
+                        }
                         if (within == gs - 1) {
                             umma_commit(&b_empty[bs]);  // the group's last chunk releases its stage
                             bg++;
