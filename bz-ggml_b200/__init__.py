@@ -117,6 +117,9 @@ SIGNATURES = {
     "bzb_generator_step_pcm_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _c_int_p, ctypes.c_int,
                                                      _c_uint_p, ctypes.c_int]),
     "bzb_generator_debug_grid_spin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
+    "bzb_generator_debug_sample": (ctypes.c_int, [ctypes.c_void_p, _c_float_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_float, ctypes.c_float, ctypes.c_uint, ctypes.c_int,
+                                                  ctypes.c_int, _c_int_p]),
     "bzb_debug_mbar_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong]),
     "bzb_generator_bench_gemv": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_int]),
@@ -497,6 +500,17 @@ class GeneratorHandle:
         if where_cap:
             return y, int(n), where[:min(int(n), where_cap)]
         return y, int(n)
+
+    def debug_sample(self, logits: np.ndarray, top_k: int, temp: float, top_p: float = 1.0, seed: int = 0,
+                     draws: int = 1, force_sort: bool = False) -> np.ndarray:
+        """cb0 sampler picks [draws][rows] on logits [rows][V] (bzb_generator_debug_sample)."""
+        lg = np.ascontiguousarray(np.asarray(logits, np.float32))
+        rows, V = lg.shape
+        out = np.zeros((draws, rows), np.int32)
+        if self.lib.lib.bzb_generator_debug_sample(self.handle, _fp(lg), V, rows, top_k, temp, top_p, seed & 0xFFFFFFFF,
+                                                   draws, 1 if force_sort else 0, _ip(out)) != 0:
+            raise RuntimeError(self.lib.last_error())
+        return out
 
     def set_debug_grid_spin(self, polls: int) -> None:
         """Grid-barrier poll limit of the persistent depth launches debug_depth makes (0: default)."""

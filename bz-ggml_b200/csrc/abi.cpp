@@ -908,6 +908,22 @@ int bzb_generator_step_pcm_device(breeze_generator * gen, breeze_vocoder * voc, 
     }
 }
 
+int bzb_generator_debug_sample(breeze_generator * gen, const float * logits, int V, int rows, int top_k, float temp,
+                               float top_p, unsigned int seed, int draws, int force_sort, int * out_picks) {
+    if (!gen || !logits || !out_picks) {
+        set_error("debug_sample: null argument");
+        return -1;
+    }
+    try {
+        OnDevice on_device_(gen->device);
+        gen->eng->debug_sample(logits, V, rows, top_k, temp, top_p, seed, draws, force_sort, out_picks);
+        return 0;
+    } catch (const std::exception & e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 int bzb_generator_debug_grid_spin(breeze_generator * gen, long long polls) {
     if (!gen) return -1;
     gen->eng->set_debug_grid_spin(polls);

@@ -8,6 +8,8 @@
 // Session state (positions, sampler streams, penalty histories, last hidden) never leaves the
 // device between steps; the host only uploads the row->slot table and seeds.
 #include "engine.h"
+
+#include <climits>
 #include "rope.h"
 
 #include <algorithm>
@@ -1883,6 +1885,56 @@ const QMat * Engine::resident_any(const char * name, int * epi) const {
         return &(*layers)[l].gu;
     }
     return nullptr;
+}
+
+void Engine::debug_sample(const float * logits, int V, int rows, int top_k, float temp, float top_p, uint32_t seed,
+                          int draws, int force_sort, int * picks) {
+    if (V <= 0 || V > 4096 || rows <= 0 || draws <= 0) throw std::runtime_error("debug_sample: bad shape");
+    float * lg = nullptr;
+    SessState * st = nullptr;
+    uint16_t * hist = nullptr;
+    int * slot = nullptr, * nx = nullptr;
+    auto release = [&] { cudaFree(lg); cudaFree(st); cudaFree(hist); cudaFree(slot); cudaFree(nx); };
+    try {
+        CK(cudaMalloc(&lg, (size_t) rows * V * sizeof(float)));
+        CK(cudaMalloc(&st, (size_t) rows * sizeof(SessState)));
+        CK(cudaMalloc(&hist, (size_t) rows * V * sizeof(uint16_t)));
+        CK(cudaMalloc(&slot, (size_t) rows * sizeof(int)));
+        CK(cudaMalloc(&nx, (size_t) rows * draws * sizeof(int)));
+        std::vector<SessState> hs(rows);
+        std::vector<int> hslot(rows);
+        for (int r = 0; r < rows; r++) {
+            SessState x{};
+            x.active = 1;
+            x.max_tokens = INT_MAX;
+            x.last_cb0 = -1;
+            x.key = seed + (uint32_t) r;
+            x.top_k = top_k; x.temp = temp; x.top_p = top_p; x.rep = 1.0f; x.cfg = 1.0f;
+            hs[r] = x;
+            hslot[r] = r;
+        }
+        CK(cudaMemcpyAsync(lg, logits, (size_t) rows * V * sizeof(float), cudaMemcpyHostToDevice, stream_));
+        CK(cudaMemcpyAsync(st, hs.data(), hs.size() * sizeof(SessState), cudaMemcpyHostToDevice, stream_));
+        CK(cudaMemcpyAsync(slot, hslot.data(), hslot.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        CK(cudaMemsetAsync(hist, 0, (size_t) rows * V * sizeof(uint16_t), stream_));
+        SampleArgs sm;
+        sm.logits = lg; sm.ld = V; sm.V = V; sm.R = rows;
+        sm.row_slot = slot; sm.st = st; sm.hist = hist; sm.hist_ld = V;
+        sm.sup_lo = V; sm.sup_hi = V; sm.eos = -1;
+        sm.update_hist_first = 1;  // every draw returns its pick and leaves the state otherwise alone
+        sm.force_sort = force_sort;
+        for (int d = 0; d < draws; d++) {
+            sm.next_out = nx + (size_t) d * rows;
+            launch_sample(sm, stream_);
+        }
+        CK(cudaMemcpyAsync(picks, nx, (size_t) rows * draws * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        release();
+        throw;
+    }
+    release();
 }
 
 long long Engine::debug_gemm(const char * name, int rows, const float * x, float * y, int repeats, int flags,

@@ -157,6 +157,11 @@ public:
     // repeat) pairs
     long long debug_gemm(const char * name, int rows, const float * x, float * y, int repeats, int flags = 0,
                          int * where = nullptr, int cap = 0);
+    // test hook: the cb0 sampler on given logits [rows][V] (V <= 4096) with the given top-k,
+    // temperature and top-p (no suppression, no penalty), `draws` draws per row from Philox key
+    // seed + row; force_sort takes the full sort even where top-k <= 64 selects. picks [draws][rows]
+    void debug_sample(const float * logits, int V, int rows, int top_k, float temp, float top_p, uint32_t seed, int draws,
+                      int force_sort, int * picks);
     // test hook: the grid-barrier poll limit of the persistent depth launches debug_depth makes
     // (0 restores the default); frame-step graphs never use it
     void set_debug_grid_spin(long long polls) { dbg_grid_spin_ = polls > 0 ? polls : 0; }

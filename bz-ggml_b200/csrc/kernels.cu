@@ -1583,7 +1583,7 @@ __global__ void __launch_bounds__(1024) sample_kernel(const SampleArgs a) {
     __shared__ unsigned long long s_sel[64], s_prefix;
     __shared__ int s_rem;
     const unsigned long long * sorted = keys;
-    if (keep <= 64) {
+    if (keep <= 64 && !a.force_sort) {
         select_top_keys(kv, keep, s_sel, s_hist, &s_prefix, &s_rem);
         sorted = s_sel;
     } else {

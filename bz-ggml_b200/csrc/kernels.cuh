@@ -274,6 +274,7 @@ struct SampleArgs {
     int clamp_on_finish = 0;            // burst: last_cb0 = -1 on finish
     int advance_pos = 1;
     int update_hist_first = 0;          // prefill: first cb0 is always recorded
+    int force_sort = 0;                 // test hook: the full sort even for top-k <= 64
 };
 void launch_sample(const SampleArgs & a, cudaStream_t s);
 // teacher-forced steps: copies step *step_ctr's rows of force_all / feed_all ([K][n] ints) into

@@ -117,6 +117,13 @@ BREEZE_API int bzb_vocoder_kernels_per_decode(breeze_vocoder * voc, int n_stream
    barrier that nothing arrives on, on `device`, and returns the error code it recorded (1 for a
    wait that gave up), or -1 with breeze_last_error(). */
 BREEZE_API int bzb_generator_debug_grid_spin(breeze_generator * gen, long long polls);
+/* Test of the cb0 sampler's two top-k paths (no reference counterpart): draws `draws` picks per
+   row from logits [rows][V] (V <= 4096) with the given top-k, temperature and top-p (no
+   suppression or penalty; Philox key seed + row), into out_picks [draws][rows]; force_sort != 0
+   takes the full sort where top-k <= 64 would select. 0, or -1 with breeze_last_error(). */
+BREEZE_API int bzb_generator_debug_sample(breeze_generator * gen, const float * logits, int V, int rows, int top_k,
+                                          float temp, float top_p, unsigned int seed, int draws, int force_sort,
+                                          int * out_picks);
 BREEZE_API int bzb_debug_mbar_timeout(int device, long long polls);
 
 /* average microseconds of back-to-back launches of one dequant-GEMM of a named Q8_0 tensor on
