@@ -62,8 +62,9 @@ constexpr int kTmemCols = 128;                           // two 64-column accumu
 constexpr int kQFloats = 4 * 2 * 128;                    // query heads of one attention task
 constexpr long long kGridSpin = 1ll << 23;
 
+constexpr int kStageFloats = 32 * kTileM;                // epilogue stage: 32 activation rows x 128 f32
 constexpr int kSmemBytes = 1024 + kAStages * kASC * kABytes + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
-                           (kQFloats + 256 + 16) * 4;
+                           (kQFloats + 256 + 16 + kStageFloats) * 4;
 
 #define DCHECK(x)                                                                             \
     do {                                                                                      \
@@ -134,6 +135,13 @@ __device__ __forceinline__ void grid_arrive(unsigned * bar) {
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// true on every thread of the epilogue group when `v` is true on all of them
+__device__ __forceinline__ bool epi_all(bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"((uint32_t) v) : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
@@ -392,7 +400,7 @@ __device__ void phase_argmax(const DpParams & p, const DpPhase ph, int cta, int 
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
                     const int v = v0 + k * kEpiThreads;
-                    part[s][k] = (s < ph.S && v < V) ? __ldcg(p.P + ((size_t) s * R + b) * V + v) : 0.0f;
+                    part[s][k] = (s < ph.S && v < V) ? __ldcg(p.P + ((size_t) s * R + b) * ph.out_ld + v) : 0.0f;
                 }
 #pragma unroll
             for (int k = 0; k < 8; k++) {
@@ -502,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     float * sQ = reinterpret_cast<float *>(sR + kRawGroups * kRawGroupBytes);
     float * sScale = sQ + kQFloats;
     float * sMisc = sScale + 256;
+    float * sStage = sMisc + 16;  // 16-byte aligned: every region before it is a multiple of 16 bytes
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -560,12 +569,61 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     const UnitRange ur = unit_range(ph, u);
                     const int acc = uc & 1;
                     bool ok = dwait(&acc_full[acc], (uc >> 1) & 1, err, kBackoff);
-                    ok = __all_sync(0xffffffffu, ok);
+                    // one outcome for the whole group: the body below has group barriers
+                    ok = epi_all(ok);
                     if (p.trace && tid == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 6] = gtimer();
                     tc_fence_after();
                     const uint32_t taddr = tmem + (uint32_t) (acc * 64) + ((uint32_t) (32 * warp) << 16);
                     const int m_loc = 32 * warp + lane;
-                    if (ok) {
+                    if (!ok) {
+                        if (tid == 0) s_abort = 1;
+                    } else if (ph.epi == DPE_PARTIAL) {
+                        // The accumulator goes to global memory through shared memory, 32 activation
+                        // rows at a time: TMEM -> stage [32][128] f32, then 16-byte stores of 4
+                        // consecutive matrix rows (a warp instruction writes 512 contiguous bytes;
+                        // scalar stores of one matrix row per lane take four times the instructions
+                        // and are what limits this epilogue).
+                        const int ld = ph.out_ld;  // partial row pitch, a multiple of 4
+                        float * dst0 = p.P + (size_t) ur.split * ph.rows * ld;
+                        for (int h = 0; h < ph.nb; h += 32) {
+                            for (int n0 = h; n0 < h + 32 && n0 < ph.nb; n0 += 16) {
+                                float v[16];
+                                tmem_ld16(taddr + n0, v);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
+#pragma unroll
+                                for (int e = 0; e < 16; e++) sStage[(n0 - h + e) * kTileM + m_loc] = v[e];
+                            }
+                            if (h + 32 >= ph.nb) {
+                                // every TMEM read of the unit is done: the MMA may reuse the accumulator
+                                tc_fence_before();
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                            }
+                            epi_sync();
+                            const int nr = min(32, ph.nb - h);
+                            for (int idx = tid; idx < nr * (kTileM / 4); idx += kEpiThreads) {
+                                const int r = idx / (kTileM / 4), c4 = idx % (kTileM / 4);
+                                const int n = ur.row0 + h + r, m = ur.tile * kTileM + 4 * c4;
+                                if (n < ph.rows && m < ph.M)
+                                    __stcg(reinterpret_cast<float4 *>(dst0 + (size_t) n * ld + m),
+                                           *reinterpret_cast<const float4 *>(sStage + r * kTileM + 4 * c4));
+                            }
+                            epi_sync();  // the stage is refilled next
+                        }
+                    } else {
+                        // 16-row gate/up interleave: lanes 0-15 hold gate rows, lanes 16-31 the
+                        // matching up rows. Partners swap values so that every lane finishes half of
+                        // the columns: lane l < 16 the even ones, lane l + 16 the odd. The row scales
+                        // are read into registers first (a shared-memory read between global stores
+                        // would wait for each of them and chain the rows), and the products go to a
+                        // shared stage [rows][64 + 16] f16 (the pad puts the even and odd rows of one
+                        // store in different banks), written out with 16-byte stores.
+                        const int pr = lane & 15;
+                        const bool gate_lane = lane < 16;
+                        half * stage = reinterpret_cast<half *>(sStage);
+                        constexpr int kGp = kTileM / 2 + 16;
                         for (int n0 = 0; n0 < ph.nb; n0 += 16) {
                             float v[16];
                             tmem_ld16(taddr + n0, v);
@@ -573,41 +631,38 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
 #pragma unroll
                             for (int e = 0; e < 16; e++) asm volatile("" : "+f"(v[e]));
                             const int nbase = ur.row0 + n0;  // activation row of v[0]
-                            if (ph.epi == DPE_PARTIAL) {
-                                const int m = ur.tile * kTileM + m_loc;
-                                if (m < ph.M) {
-                                    float * dst = p.P + (size_t) ur.split * ph.rows * ph.M + m;
+                            float scv[8];
 #pragma unroll
-                                    for (int e = 0; e < 16; e++)
-                                        if (nbase + e < ph.rows) __stcg(dst + (size_t) (nbase + e) * ph.M, v[e]);
-                                }
-                            } else {
-                                // 16-row gate/up interleave: lanes 0-15 hold gate rows, lanes 16-31 the
-                                // matching up rows. Partners swap values so that every lane finishes
-                                // half of the columns: lane l < 16 the even ones, lane l + 16 the odd.
-                                const int pr = lane & 15;
-                                const int jc = ur.tile * (kTileM / 2) + 16 * warp + pr;
-                                const bool gate_lane = lane < 16;
+                            for (int e2 = 0; e2 < 8; e2++) scv[e2] = sScale[min(nbase + 2 * e2 + (gate_lane ? 0 : 1), 255)];
 #pragma unroll
-                                for (int e = 0; e < 16; e++) {
-                                    const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
-                                    const int n = nbase + e;
-                                    if ((e & 1) == (gate_lane ? 0 : 1) && n < ph.rows && jc < ph.out_ld) {
-                                        const float sc = sScale[n];
-                                        const float gt = (gate_lane ? v[e] : other) * sc;
-                                        const float up = (gate_lane ? other : v[e]) * sc;
-                                        const float act = __fdividef(gt, 1.0f + __expf(-gt));
-                                        p.g16[(size_t) n * p.ffn + jc] = __float2half_rn(act * up);
-                                    }
-                                }
+                            for (int e2 = 0; e2 < 8; e2++) {
+                                // lanes < 16 finish row n0 + 2 e2, lanes >= 16 row n0 + 2 e2 + 1
+                                const float oe = __shfl_xor_sync(0xffffffffu, v[2 * e2], 16);
+                                const float oo = __shfl_xor_sync(0xffffffffu, v[2 * e2 + 1], 16);
+                                const float gt = (gate_lane ? v[2 * e2] : oo) * scv[e2];
+                                const float up = (gate_lane ? oe : v[2 * e2 + 1]) * scv[e2];
+                                const float act = __fdividef(gt, 1.0f + __expf(-gt));
+                                stage[(n0 + 2 * e2 + (gate_lane ? 0 : 1)) * kGp + 16 * warp + pr] = __float2half_rn(act * up);
                             }
                         }
-                    } else if (tid == 0) {
-                        s_abort = 1;
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                        epi_sync();
+                        for (int idx = tid; idx < ph.nb * 8; idx += kEpiThreads) {
+                            const int r = idx >> 3, c8 = idx & 7;
+                            const int n = ur.row0 + r, jc = ur.tile * (kTileM / 2) + 8 * c8;
+                            if (n < ph.rows && jc < ph.out_ld)
+                                *reinterpret_cast<uint4 *>(p.g16 + (size_t) n * p.ffn + jc) =
+                                    *reinterpret_cast<const uint4 *>(stage + r * kGp + 8 * c8);
+                        }
+                        epi_sync();  // the stage is refilled by the next unit
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    if (!ok) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    }
                     uc++;
                 }
             } else if (ph.type == DP_REDUCE) {

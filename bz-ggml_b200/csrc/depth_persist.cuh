@@ -28,7 +28,7 @@ struct alignas(16) DpPhase {
     int nb = 0;         // MMA N: activation rows per unit, a multiple of 16, at most 64
     int rows = 0;       // activation rows whose results are kept
     int epi = DPE_PARTIAL;
-    int out_ld = 0;     // partial: the matrix rows M; SwiGLU: the FFN width
+    int out_ld = 0;     // partial (and arg-max): row pitch of the partials, M rounded up to 4; SwiGLU: the FFN width
     int ss_row0 = 0;    // rows whose RMS scale applies (SwiGLU, arg-max) start here in `ss`
     // consumers of partials
     int S = 1;          // splits of the GEMM that produced the partials

@@ -474,7 +474,7 @@ void Engine::alloc_buffers() {
     // persistent depth decoder: split-K partials for up to 16 splits of the widest depth
     // matrix at 2 x 64 rows (or of the head at 64 rows), row norm sums, phase counter
     dp_grid_ = depth_persist_grid();
-    dp_P_floats_ = std::max((size_t) 16 * 128 * std::max(dd.hidden, ddq + 2 * ddkv), (size_t) 16 * 64 * cfg.vs);
+    dp_P_floats_ = std::max((size_t) 16 * 128 * std::max(dd.hidden, ddq + 2 * ddkv), (size_t) 16 * 64 * round_up(cfg.vs, 4));
     dp_P_ = dalloc<float>(dp_P_floats_);
     dp_P2_ = dalloc<float>((size_t) rmax_ * (ddq + 2 * ddkv));
     dp_ss_ = dalloc<float>((size_t) 256 * std::max(1, dd.hidden / 64));
@@ -666,7 +666,10 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
         int S = epi == DPE_PARTIAL ? std::max(1, std::min(max_splits, std::min(w.KC, G / (w.MT * q.row_chunks)))) : 1;
         q.kc_per = (w.KC + S - 1) / S;
         S = (w.KC + q.kc_per - 1) / q.kc_per;
-        if (epi == DPE_PARTIAL && (size_t) S * rows * w.M > dp_P_floats_)
+        // partial rows are written 4 floats at a time: the pitch is a multiple of 4
+        if (epi == DPE_PARTIAL && (out_ld % 4 != 0 || out_ld < w.M))
+            throw std::runtime_error("persistent depth decoder: partial row pitch");
+        if (epi == DPE_PARTIAL && (size_t) S * rows * out_ld > dp_P_floats_)
             throw std::runtime_error("persistent depth decoder: partial buffer too small");
         q.splits = S; q.n_units = w.MT * S * q.row_chunks;
         q.map = map; q.b_row0 = b_row0; q.rows = rows; q.epi = epi; q.out_ld = out_ld;
@@ -703,9 +706,9 @@ const Engine::DpPlan * Engine::depth_plan(int R) {
             reduce(S, rows, 1, l + 1 < dd.n_layer ? dd_[l + 1].attn_norm : dd_out_norm_);
         }
         // the head reads the position-1 rows in the first sub-step
-        S = gemm(dd_head_[j - 1].u, 3, first ? R : 0, R, DPE_PARTIAL, vs, 8);  // arg-max sums <= 8 splits
+        S = gemm(dd_head_[j - 1].u, 3, first ? R : 0, R, DPE_PARTIAL, round_up(vs, 4), 8);  // arg-max sums <= 8 splits
         DpPhase am;
-        am.type = DP_ARGMAX; am.S = S; am.j = j; am.ss_row0 = first ? R : 0;
+        am.type = DP_ARGMAX; am.S = S; am.j = j; am.ss_row0 = first ? R : 0; am.out_ld = round_up(vs, 4);
         ph.push_back(am);
     }
     DpPlan plan;
