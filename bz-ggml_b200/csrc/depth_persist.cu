@@ -10,8 +10,11 @@
 //   warps 0-3   epilogue group: drains the TMEM accumulators of GEMM units, and runs the
 //               element-wise phases (split-K reduction + residual + norm preparation, attention,
 //               arg-max + next embedding);
-//   warps 4-11  dequantise raw Q8_0 chunks into the 128-byte-swizzled f16 A tile;
-//   warp 12     issues tcgen05.mma (128 x N x 16) and owns the TMEM columns;
+//   warps 4-11  dequantise raw Q8_0 chunks into the f16 A tile, written straight to tensor
+//               memory (tcgen05.st): the MMA reads A from TMEM, so the weight tile never passes
+//               through shared memory as f16 (half of the shared-memory traffic per chunk);
+//   warp 12     issues tcgen05.mma (128 x N x 16, A from TMEM, B from shared memory) and owns
+//               the TMEM columns;
 //   warp 13     streams weight chunks with bulk async copies;
 //   warp 14     loads activation chunks with 2-D TMA after the phase's input is complete.
 // Weights never depend on activations, so warps 4-13 run ahead across phase boundaries and
@@ -42,15 +45,15 @@ using namespace tc;
 
 constexpr int kTileM = 128;
 constexpr int kChunkK = 64;
-constexpr int kABytes = kTileM * kChunkK * 2;            // f16 A stage
 // Every bulk or tensor copy costs the SM a roughly fixed ~0.4 us of issue time whatever its size
 // up to 32 KB, so weights and activations move in groups of kDpGroup chunks per copy.
 constexpr int kRawGroups = 2;                            // weight ring: groups of 4 chunks
 constexpr int kRawGroupBytes = kDpGroup * kUChunkBytes;
-// dequantised A ring: stages of kASC chunks, handed to the MMA thread with one arrival and
-// released with one commit per stage (a unit's last stage may hold one chunk)
+// dequantised A ring in TMEM: stages of kASC chunks (32 columns each), handed to the MMA thread
+// with one arrival and released with one commit per stage (a unit's last stage may hold one chunk)
 constexpr int kASC = 2;
 constexpr int kAStages = 2;
+constexpr int kACols = kChunkK / 2;                      // a 128 x 64 f16 chunk: 32 columns
 constexpr int kBGroups = 2;                              // activation ring: groups of 4 chunks
 constexpr int kBChunkMax = 64 * kChunkK * 2;             // one chunk of up to 64 activation rows
 constexpr int kBGroupBytes = kDpGroup * kBChunkMax;
@@ -58,12 +61,14 @@ constexpr int kEpiThreads = 128;
 constexpr int kDqThreads = 256;
 constexpr int kMmaWarp = 12, kWeightWarp = 13, kActWarp = 14;
 constexpr int kThreads = 480;
-constexpr int kTmemCols = 128;                           // two 64-column accumulators
+constexpr int kAccCols = 128;                            // two 64-column accumulators
+constexpr int kTmemCols = 256;                           // accumulators, then the A ring
+static_assert(kAccCols + kAStages * kASC * kACols <= kTmemCols, "TMEM columns");
 constexpr int kQFloats = 4 * 2 * 128;                    // query heads of one attention task
 constexpr long long kGridSpin = 1ll << 23;
 
 constexpr int kStageFloats = 32 * kTileM;                // epilogue stage: 32 activation rows x 128 f32
-constexpr int kSmemBytes = 1024 + kAStages * kASC * kABytes + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
+constexpr int kSmemBytes = 1024 + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
                            (kQFloats + 256 + 16 + kStageFloats) * 4;
 
 #define DCHECK(x)                                                                             \
@@ -504,8 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     __shared__ uint32_t tmem_slot;
     __shared__ int s_abort;
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
-    uint8_t * sA = smem;
-    uint8_t * sB = sA + kAStages * kASC * kABytes;
+    uint8_t * sB = smem;
     uint8_t * sR = sB + kBGroups * kBGroupBytes;
     float * sQ = reinterpret_cast<float *>(sR + kRawGroups * kRawGroupBytes);
     float * sScale = sQ + kQFloats;
@@ -697,7 +701,8 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     const int within = c % kDpGroup, gs = min(kDpGroup, ur.nch - (c - within));
                     const int rs = rg % kRawGroups, ab = as % kAStages, sub = c % kASC;
                     const bool stage_end = sub == kASC - 1 || c == ur.nch - 1;
-                    if (within == 0) ok = dwait(&raw_full[rs], (rg / kRawGroups) & 1u, err, kBackoff);
+                    // every wait's outcome is made warp-uniform: the TMEM stores below are warp-collective
+                    if (within == 0) ok = __all_sync(0xffffffffu, dwait(&raw_full[rs], (rg / kRawGroups) & 1u, err, kBackoff));
                     if (!ok) break;
                     if (p.trace && t == 0 && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 8] = gtimer();
                     const uint8_t * raw = sR + rs * kRawGroupBytes + within * umat_chunk_bytes(ph.q4);
@@ -719,10 +724,14 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                         if (lane == 0) mbar_arrive(&raw_empty[rs]);
                         rg++;
                     }
-                    if (sub == 0 && as >= kAStages) ok = dwait(&a_empty[ab], ((as / kAStages) - 1) & 1u, err, kBackoff);
+                    if (sub == 0 && as >= kAStages)
+                        ok = __all_sync(0xffffffffu, dwait(&a_empty[ab], ((as / kAStages) - 1) & 1u, err, kBackoff));
                     if (!ok) break;
                     const half2 s2 = __halves2half2(sc, sc);
-                    uint8_t * arow = sA + (ab * kASC + sub) * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+                    // this thread's 32 K values (half hb of the chunk) of A row r, as 16 columns of
+                    // its TMEM lane; the stage's MMAs were complete (a_empty) before the first write
+                    if (sub == 0) tc_fence_after();
+                    uint32_t o16[16];
                     if (ph.q4) {
                         float qa, qb;
                         q4k_chunk_scale_min(meta, hb, qa, qb);
@@ -731,22 +740,22 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                         for (int q = 0; q < 4; q++) {
                             uint32_t o[4];
                             dq8_nib_f32(w4[q], qa, qb, o);
-                            const int jj = hb * 4 + q;
-                            *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+                            for (int k = 0; k < 4; k++) o16[4 * q + k] = o[k];
                         }
                     } else {
                         const uint32_t w8[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
 #pragma unroll
                         for (int q = 0; q < 4; q++) {
-                            uint4 o;
-                            dq4(w8[2 * q], s2, o.x, o.y);
-                            dq4(w8[2 * q + 1], s2, o.z, o.w);
-                            const int jj = hb * 4 + q;
-                            *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = o;
+                            dq4(w8[2 * q], s2, o16[4 * q], o16[4 * q + 1]);
+                            dq4(w8[2 * q + 1], s2, o16[4 * q + 2], o16[4 * q + 3]);
                         }
                     }
+                    tmem_st16(tmem + ((uint32_t) (32 * (warp & 3)) << 16) + (uint32_t) (kAccCols + (ab * kASC + sub) * kACols + hb * 16),
+                              o16);
                     if (stage_end) {
-                        fence_proxy_async();  // each thread's stores of the stage before the arrival
+                        tmem_wait_st();  // this thread's TMEM stores of the stage complete
+                        tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&a_full[ab]);
                         as++;
@@ -755,6 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                 }
             }
         }
+        tmem_wait_st();
         if (!ok) s_abort = 1;
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
@@ -783,14 +793,14 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                         if (p.trace && c == 0) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 4] = gtimer();
                         if (p.trace && c < 16) p.trace[((size_t) i * G + cta) * kDpTraceSlots + 25 + c] = gtimer();
                         if (!ok) break;
-                        // no tcgen05 fence here: shared-memory operands are ordered by the stage
-                        // barriers (TMA complete_tx, or the dequantisers' proxy fence + arrive); the
-                        // fence after the accumulator wait above orders the TMEM reuse
-                        const uint32_t a0 = smem_u32(sA + (ab * kASC + sub) * kABytes);
+                        // the A stage was written to TMEM by the dequantisers (tcgen05.st, wait,
+                        // fence before their arrival): order this thread's MMAs after that wait
+                        if (sub == 0) tc_fence_after();
+                        const uint32_t a0 = tmem + (uint32_t) (kAccCols + (ab * kASC + sub) * kACols);
                         const uint32_t b0 = smem_u32(sB + bs * kBGroupBytes + within * ph.nb * kChunkK * 2);
 #pragma unroll
                         for (int kk = 0; kk < kChunkK / 16; kk++)
-                            umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (c > 0 || kk > 0) ? 1u : 0u);
+                            umma_f16_tmem_a(d, a0 + kk * 8, sw128_desc(b0 + kk * 32), idesc, (c > 0 || kk > 0) ? 1u : 0u);
                         if (stage_end) {
                             umma_commit(&a_empty[ab]);  // the stage's MMAs release its A tiles
                             as++;
