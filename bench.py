@@ -876,8 +876,8 @@ def main():
         dom_gbs = prof["depth_bytes"] / (prof["depth_ms"] / 1e3) / 1e9
         if nc == 32 and args.sessions == 64:
             # dram__bytes_read.sum + dram__bytes_write.sum of one launch, from an ncu capture of the
-            # same depth decode (64 sessions, nc 32) on the depth-sized model: 3.862 GB + 34.7 MB
-            traffic = 3.862190e9 + 34.703104e6
+            # same depth decode (64 sessions, nc 32) on the depth-sized model: 3.868 GB + 34.3 MB
+            traffic = 3.868159e9 + 34.275840e6
         dom_name = "depth_persist_kernel (persistent tcgen05 depth decoder, 31 sub-steps)"
         dom_share = prof["depth_ms"] / prof["step_ms"]
     else:
