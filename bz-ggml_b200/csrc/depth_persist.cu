@@ -66,10 +66,12 @@ constexpr int kTmemCols = 256;                           // accumulators, then t
 static_assert(kAccCols + kAStages * kASC * kACols <= kTmemCols, "TMEM columns");
 constexpr int kQFloats = 4 * 2 * 128;                    // query heads of one attention task
 constexpr long long kGridSpin = 1ll << 23;
+constexpr int kMaxSplitsK = 16;                          // the split-K partials a reduction sums at most
 
 constexpr int kStageFloats = 32 * kTileM;                // epilogue stage: 32 activation rows x 128 f32
+constexpr int kRedFloats = 4 * kMaxSplitsK * 32 * 4;     // reduction landing areas: 4 warps x 16 splits x 32 float4
 constexpr int kSmemBytes = 1024 + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
-                           (kQFloats + 256 + 16 + kStageFloats) * 4;
+                           (kQFloats + 256 + 16 + kStageFloats + kRedFloats) * 4;
 
 #define DCHECK(x)                                                                             \
     do {                                                                                      \
@@ -197,7 +199,7 @@ __device__ __forceinline__ UnitRange unit_range(const DpPhase ph, int u) {
     return r;
 }
 
-constexpr int kMaxSplits = 16;
+constexpr int kMaxSplits = kMaxSplitsK;
 constexpr int kArgSplits = 8;   // the head's split-K is capped at this
 
 // x[e] = sum over s < S of P[s * split_stride + off + 32 e], e < 4, with all loads in flight
@@ -249,32 +251,51 @@ __device__ __forceinline__ void row_scales(const DpParams & p, int row0, int row
 }
 
 // ---- element-wise phases (epilogue group: 128 threads, warps 0-3) -------------------------
-__device__ void phase_reduce(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane) {
+__device__ __forceinline__ void cp_async16(void * dst_smem, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// sRed: this warp's [kMaxSplits][32] float4 landing area
+__device__ void phase_reduce(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane, float4 * sRed) {
     const int D = p.D, nch = D / kChunkK, rows = ph.rows;
-    const int W = G * 4;
-    for (int t = cta * 4 + warp; t < rows * nch; t += W) {
-        const int n = t / nch, c = t % nch;
-        const int col = c * kChunkK + 2 * lane;
-        // every partial load is issued before the first add, so the S loads overlap
-        float2 v[kMaxSplits];
-#pragma unroll
-        for (int s = 0; s < kMaxSplits; s++)
-            if (s < ph.S) v[s] = __ldcg(reinterpret_cast<const float2 *>(p.P + ((size_t) s * rows + n) * D + col));
-        const float2 xo = ph.resid ? __ldcg(reinterpret_cast<const float2 *>(p.x + (size_t) n * D + col)) : make_float2(0.0f, 0.0f);
-        float2 acc = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int s = 0; s < kMaxSplits; s++)
-            if (s < ph.S) {
-                acc.x += v[s].x;
-                acc.y += v[s].y;
+    const int W = G * 4, nt2 = (nch + 1) / 2;
+    // A warp task is 128 columns, two 64-column chunks, 4 per lane (lanes 0-15 the first chunk):
+    // 64 rows of 1,024 columns are 512 tasks, one round on 592 warps, so no warp waits for two L2
+    // round trips in a row. The S partials of a lane land in shared memory by cp.async, all in
+    // flight at once without holding registers.
+    for (int t = cta * 4 + warp; t < rows * nt2; t += W) {
+        const int n = t / nt2, c = (t % nt2) * 2 + (lane >> 4);
+        const bool valid = c < nch;
+        const int col = c * kChunkK + 4 * (lane & 15);
+        if (valid)
+            for (int s = 0; s < ph.S; s++) cp_async16(sRed + s * 32 + lane, p.P + ((size_t) s * rows + n) * D + col);
+        const float4 xo = ph.resid && valid ? __ldcg(reinterpret_cast<const float4 *>(p.x + (size_t) n * D + col))
+                                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        cp_async_wait_all();
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (valid)
+            for (int s = 0; s < ph.S; s++) {
+                const float4 v = sRed[s * 32 + lane];
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
             }
-        const float2 xn = ph.resid ? make_float2(xo.x + acc.x, xo.y + acc.y) : acc;
-        __stcg(reinterpret_cast<float2 *>(p.x + (size_t) n * D + col), xn);
-        const float2 w = *reinterpret_cast<const float2 *>(ph.norm_w + col);
-        half2 h = __floats2half2_rn(xn.x * w.x, xn.y * w.y);
-        __stcg(reinterpret_cast<unsigned *>(p.h16 + (size_t) n * D + col), *reinterpret_cast<unsigned *>(&h));
-        const float sq = wsum(xn.x * xn.x + xn.y * xn.y);
-        if (lane == 0) __stcg(p.ss + (size_t) n * nch + c, sq);
+        const float4 xn = ph.resid ? make_float4(xo.x + acc.x, xo.y + acc.y, xo.z + acc.z, xo.w + acc.w) : acc;
+        float sq = 0.0f;
+        if (valid) {
+            __stcg(reinterpret_cast<float4 *>(p.x + (size_t) n * D + col), xn);
+            const float4 w = *reinterpret_cast<const float4 *>(ph.norm_w + col);
+            half2 h[2] = { __floats2half2_rn(xn.x * w.x, xn.y * w.y), __floats2half2_rn(xn.z * w.z, xn.w * w.w) };
+            __stcg(reinterpret_cast<uint2 *>(p.h16 + (size_t) n * D + col), *reinterpret_cast<uint2 *>(h));
+            sq = xn.x * xn.x + xn.y * xn.y + xn.z * xn.z + xn.w * xn.w;
+        }
+        // the chunk's sum of squares over its 16 lanes
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if ((lane & 15) == 0 && valid) __stcg(p.ss + (size_t) n * nch + c, sq);
+        __syncwarp();  // every lane has read its landing slots before the next task refills them
     }
 }
 
@@ -515,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
     float * sScale = sQ + kQFloats;
     float * sMisc = sScale + 256;
     float * sStage = sMisc + 16;  // 16-byte aligned: every region before it is a multiple of 16 bytes
+    float4 * sRed = reinterpret_cast<float4 *>(sStage + kStageFloats);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -670,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
                     uc++;
                 }
             } else if (ph.type == DP_REDUCE) {
-                phase_reduce(p, ph, cta, G, warp, lane);
+                phase_reduce(p, ph, cta, G, warp, lane, sRed + warp * (kMaxSplits * 32));
             } else if (ph.type == DP_ATTN) {
                 phase_attn(p, ph, cta, G, warp, lane, sQ);
             } else {
