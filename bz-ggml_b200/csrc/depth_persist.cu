@@ -70,6 +70,7 @@ constexpr int kMaxSplitsK = 16;                          // the split-K partials
 
 constexpr int kStageFloats = 32 * kTileM;                // epilogue stage: 32 activation rows x 128 f32
 constexpr int kRedFloats = 4 * kMaxSplitsK * 32 * 4;     // reduction landing areas: 4 warps x 16 splits x 32 float4
+static_assert(kRedFloats >= 32 * 2 * 128, "attention reuses the reduction landing area for 32 positions of keys and values");
 constexpr int kSmemBytes = 1024 + kBGroups * kBGroupBytes + kRawGroups * kRawGroupBytes +
                            (kQFloats + 256 + 16 + kStageFloats + kRedFloats) * 4;
 
@@ -299,7 +300,9 @@ __device__ void phase_reduce(const DpParams & p, const DpPhase ph, int cta, int 
     }
 }
 
-__device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane, float * sQ) {
+// sKV: [32 positions][2][128] f32 landing area (the reductions' area, unused during attention)
+__device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G, int warp, int lane, float * sQ,
+                           float * sKV) {
     const int R = p.R, hd = 128, nkv = p.n_kv, nh = p.n_head, D = p.D;
     const int M = nh * hd + 2 * nkv * hd;
     const int rows = ph.rows, S = ph.alt ? 1 : ph.S, n_new = ph.n_new;
@@ -347,6 +350,21 @@ __device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G,
         epi_sync();  // appended keys/values and the queries visible to the group
         const float * kb = kvl + (size_t) b * p.nc * 2 * nkv * hd + (size_t) g * hd;
         const size_t pstride = (size_t) 2 * nkv * hd;  // floats between consecutive positions
+        // The task's key and value rows (positions 0 .. start + n_new - 1, at most 32) land in
+        // shared memory once for the query warps by cp.async, all in flight together: sKV
+        // [position][key, value][hd] f32. Reading them row block by row block from L2 cost each
+        // warp one round trip per 8 positions.
+        {
+            const int lim_all = ph.start + n_new;
+            const int tid = warp * 32 + lane;
+            for (int q = tid; q < lim_all * 2 * (hd / 4); q += kEpiThreads) {
+                const int pp = q / (2 * (hd / 4)), rem = q % (2 * (hd / 4));
+                const int isv = rem / (hd / 4), c4 = rem % (hd / 4);
+                cp_async16(sKV + (pp * 2 + isv) * hd + 4 * c4, kb + (size_t) pp * pstride + isv * nkv * hd + 4 * c4);
+            }
+            cp_async_wait_all();
+        }
+        epi_sync();
         for (int i = 0; i < n_new && qwarp; i++) {
             const int lim = ph.start + i + 1;
             // scores: the warp reads one key row per position (lane = 4 dims), 8 rows in flight;
@@ -357,7 +375,7 @@ __device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G,
                 float4 k4[8];
 #pragma unroll
                 for (int k = 0; k < 8; k++)
-                    k4[k] = pp0 + k < lim ? __ldcg(reinterpret_cast<const float4 *>(kb + (size_t) (pp0 + k) * pstride) + lane)
+                    k4[k] = pp0 + k < lim ? *(reinterpret_cast<const float4 *>(sKV + (pp0 + k) * 2 * hd) + lane)
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
@@ -378,7 +396,7 @@ __device__ void phase_attn(const DpParams & p, const DpPhase ph, int cta, int G,
                 for (int k = 0; k < 8; k++)
 #pragma unroll
                     for (int e = 0; e < 4; e++)
-                        vv[k][e] = pp0 + k < lim ? __ldcg(kb + (size_t) (pp0 + k) * pstride + nkv * hd + lane + 32 * e) : 0.0f;
+                        vv[k][e] = pp0 + k < lim ? sKV[((pp0 + k) * 2 + 1) * hd + lane + 32 * e] : 0.0f;
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
                     const int pp = pp0 + k;
@@ -694,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1) depth_persist_kernel(const DpPara
             } else if (ph.type == DP_REDUCE) {
                 phase_reduce(p, ph, cta, G, warp, lane, sRed + warp * (kMaxSplits * 32));
             } else if (ph.type == DP_ATTN) {
-                phase_attn(p, ph, cta, G, warp, lane, sQ);
+                phase_attn(p, ph, cta, G, warp, lane, sQ, reinterpret_cast<float *>(sRed));
             } else {
                 phase_argmax(p, ph, cta, G, tid, warp, lane, sMisc);
             }

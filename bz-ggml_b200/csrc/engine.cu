@@ -596,6 +596,7 @@ bool Engine::dp_supported(int R) const {
     if (dd.hd != 128 || dd.n_kv <= 0 || dd.n_head % dd.n_kv || dd.n_head > 4 * dd.n_kv || dd.n_head * dd.hd != dd.hidden)
         return false;
     if (dd.hidden % 64 || cfg.hidden % 64 || dd.ffn % 64 || dd.hidden / 64 > 32) return false;
+    if (cfg.nc > 32) return false;  // the attention phase holds at most 32 positions of keys and values
     if (!dd_in_.u.blk) return false;
     for (const LayerW & w : dd_)
         if (!w.qkv.u.blk || !w.o.u.blk || !w.gu.u.blk || !w.down.u.blk) return false;
